@@ -1,0 +1,163 @@
+"""Generate the golden fixtures of tests/golden/*.npz by running the reference implementation on the CPU.
+
+Run from the repository root in a container that has the reference checkout (read-only is fine):
+    python tests/golden/make_golden.py /path/to/reference
+
+Each fixture stores seeded inputs, the layer's parameters (state_dict names of asrn.estable.CapaASRNEstable) and the
+reference's own intermediates and outputs, captured by calling the reference's methods:
+  _contexto -> Qc, Kc, beta, log_alfa (asrn/estable.py:153-194); Bt = beta.cumsum(1) (asrn/estable.py:418)
+  _phi_y_valores -> phi, V (asrn/nucleo.py:644-659); _ids (asrn/nucleo.py:661-664)
+  stable argsort of the per-table ids (asrn/estable.py:220-221)
+  _acumular -> salida and the per-table signals (hay, max, peak) (asrn/estable.py:204-300)
+  _claves_vistos / _ordenar_claves / _repeticion (asrn/nucleo.py:688-701, asrn/estable.py:304-321)
+  forward -> h' (asrn/estable.py:407-421)
+The model fixture adds create_model + forward + generate (asrn/__init__.py:60-64, asrn/nucleo.py:1088-1103, 1965-2043).
+The fixtures are read by the tests on any machine; this script is the only place that imports the reference.
+"""
+import os
+import sys
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+from asrn_b200 import synthetic  # noqa: E402
+
+
+def _move(capa, seed=1, gamma=(0.5, 3.0)):
+    """Push the parameters that start neutral (zero) off zero so every term of the layer is exercised
+    (the recipe of the reference's own tests: tests/test_estable.py:44-53)."""
+    import asrn.nucleo as v89
+    g = torch.Generator().manual_seed(seed)
+    with torch.no_grad():
+        for n, p in capa.named_parameters():
+            if n in v89._NUEVOS_V87 or n in ('cq.weight', 'w_sufijo', 'w_vistos', 'g_conf.weight', 'g_conf.bias'):
+                p.add_(torch.randn(p.shape, generator=g) * 0.5)
+        if gamma is not None:
+            capa.gamma.copy_(torch.linspace(gamma[0], gamma[1], capa.n_tablas))
+
+
+def _np(x):
+    x = x.detach()
+    if x.dtype == torch.bfloat16:
+        x = x.float()
+    return x.cpu().numpy()
+
+
+def layer_case(name, d, B, L, V, bf16, opts, seed=0, tokens=None, keep_values=True):
+    import asrn
+    torch.manual_seed(seed)
+    capa = asrn.ASRNLayer(d, **opts)
+    _move(capa, seed=seed + 1)
+    capa.eval()
+    if tokens is None:
+        x = synthetic.zipf_tokens(B, L, V, 1.1, seed)
+        x = synthetic.plant_repeats(x, 0.25, 4, max(4, L // 4), seed=seed + 1)
+    else:
+        x = tokens
+    x = torch.from_numpy(x)
+    g = torch.Generator().manual_seed(seed + 7)
+    table = torch.randn(V, d, generator=g)
+    E = table[x]
+    h = torch.randn(B, L, d, generator=g)
+    out = {}
+    captured = {}
+    orig = capa._senales
+
+    def grab(salida, senal):
+        captured['senal'] = senal.detach().clone()
+        return orig(salida, senal)
+
+    capa._senales = grab
+    with torch.no_grad(), torch.autocast('cpu', dtype=torch.bfloat16, enabled=bf16):
+        sig = asrn.firmas_de_piezas(x)
+        Qc, Kc, beta, log_alfa = capa._contexto(h)
+        Bt = beta.cumsum(1)
+        phi, Vv = capa._phi_y_valores(E)
+        ids = capa._ids(phi)
+        T = capa.n_tablas
+        ids_rows = ids.transpose(1, 2).reshape(B * T, L)
+        orden = ids_rows.argsort(dim=-1, stable=True)
+        acc = capa._acumular(E, Qc, Kc, Bt, log_alfa, sig)
+        claves = capa._claves_vistos(sig)
+        orden_ng, repetido = capa._ordenar_claves(claves)
+        rep = capa._repeticion(sig, beta, Bt, log_alfa)
+        y = capa(E, h, x)
+    capa._senales = orig
+    out.update(tokens=x.numpy(), E=_np(E), h=_np(h), sig=_np(sig), Qc=_np(Qc), Kc=_np(Kc), beta=_np(beta),
+               log_alfa=_np(log_alfa), Bt=_np(Bt), phi=_np(phi), V=_np(Vv), ids=_np(ids),
+               orden=orden.numpy().astype(np.int32), salida=_np(acc['salida']),
+               peso_total=_np(acc['peso_total']), mejor=_np(acc['mejor']), pico=_np(acc['pico']),
+               peso_ctx=_np(acc['peso_ctx']), senal=_np(captured['senal']), claves=_np(claves),
+               orden_ng=orden_ng.numpy().astype(np.int32), repetido=repetido.numpy(), vistos=_np(rep['vistos']),
+               hawkes=_np(rep['hawkes']), racha=_np(rep['racha']), out=_np(y))
+    if not keep_values:
+        del out['V']
+    for k, v in capa.state_dict().items():
+        out['param.' + k] = _np(v)
+    meta = dict(d=d, B=B, L=L, V=V, bf16=int(bf16), **{k: v for k, v in opts.items()})
+    for k, v in meta.items():
+        out['meta.' + k] = np.array(v)
+    path = os.path.join(HERE, name + '.npz')
+    np.savez_compressed(path, **out)
+    print(f'{name}: {os.path.getsize(path) / 1024:.0f} KB')
+
+
+def model_case(name, V, d, n_capas, B, L, L0, n_new, seed=0):
+    import asrn
+    m = asrn.create_model(V=V, d=d, n_capas=n_capas, semilla=seed)
+    for c in m.largos:
+        _move(c, seed=seed + 3)
+    m.eval()
+    x = torch.from_numpy(synthetic.uniform_bytes_with_repeats(B, L, seed) % V)
+    with torch.no_grad():
+        logits = m(x)
+    out = dict(tokens=x.numpy(), logits=logits.numpy())
+    for ajeno in (True, False):
+        seqs, steps = asrn.generate(m, x[:, :L0], n_nuevos=n_new, top_k=1, memoria_de_lo_ajeno=ajeno)
+        tag = 'ajeno' if ajeno else 'propia'
+        out[f'gen_{tag}_seqs'] = seqs.numpy()
+        out[f'gen_{tag}_logits'] = steps.numpy()
+    for k, v in m.state_dict().items():
+        out['param.' + k] = _np(v)
+    meta = dict(V=V, d=d, n_capas=n_capas, B=B, L=L, L0=L0, n_new=n_new, seed=seed)
+    for k, v in meta.items():
+        out['meta.' + k] = np.array(v)
+    path = os.path.join(HERE, name + '.npz')
+    np.savez_compressed(path, **out)
+    print(f'{name}: {os.path.getsize(path) / 1024:.0f} KB')
+
+
+def init_case(name, V, d, n_capas, seed):
+    """Checksums of create_model's freshly initialised weights (same seed -> same weights in the build)."""
+    import asrn
+    m = asrn.create_model(V=V, d=d, n_capas=n_capas, semilla=seed)
+    out = {}
+    for k, v in m.state_dict().items():
+        t = v.detach().double()
+        out['sum.' + k] = np.array(float(t.sum()))
+        out['sumsq.' + k] = np.array(float((t * t).sum()))
+        out['first.' + k] = t.reshape(-1)[:8].numpy()
+    path = os.path.join(HERE, name + '.npz')
+    np.savez_compressed(path, **out)
+    print(f'{name}: {os.path.getsize(path) / 1024:.0f} KB')
+
+
+def main(ref):
+    sys.path.insert(0, ref)
+    torch.set_num_threads(8)
+    layer_case('layer_f32', 64, 2, 256, 64, False, {})
+    layer_case('layer_bf16', 64, 2, 256, 64, True, {})
+    layer_case('layer_f32_opts', 48, 2, 200, 24, False, dict(chunk=8, n_bits=6, confirmar=20, sufijo=6, vistos=3))
+    layer_case('layer_f32_d96', 96, 2, 150, 40, False, dict(chunk=16, n_bits=4))
+    layer_case('layer_f32_short', 32, 1, 5, 12, False, dict(chunk=16, n_bits=4))
+    layer_case('layer_f32_one', 32, 1, 1, 12, False, dict(chunk=16, n_bits=4))
+    layer_case('layer_bf16_d256', 256, 1, 512, 256, True, {}, keep_values=False)
+    layer_case('layer_f32_d256', 256, 1, 512, 256, False, {}, keep_values=False)
+    model_case('model_small', V=256, d=64, n_capas=4, B=2, L=192, L0=96, n_new=24)
+    init_case('init_cfg1', V=256, d=64, n_capas=4, seed=0)
+
+
+if __name__ == '__main__':
+    main(sys.argv[1] if len(sys.argv) > 1 else '/root/reference')
