@@ -1,0 +1,331 @@
+// extern "C" entry points of libasrn_b200.so (declared in include/asrn_b200.h).
+#include "common.cuh"
+#include "layout.h"
+
+using namespace asrn;
+
+namespace {
+
+cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+int check_config(const asrn_layer_config* c) {
+  if (!c) return ASRN_ERR_ARG;
+  if (c->B < 0 || c->L < 0 || c->d < 1 || c->d > 1024) return ASRN_ERR_ARG;
+  if (c->n_tablas < 2 || c->n_tablas > kMaxTables) return ASRN_ERR_ARG;
+  if (c->n_bits < 1 || c->n_bits > kMaxBits) return ASRN_ERR_ARG;
+  if ((int64_t)c->n_tablas * c->n_bits > kMaxPhi) return ASRN_ERR_UNSUPPORTED;
+  if (c->chunk < 1 || c->chunk > 32) return ASRN_ERR_UNSUPPORTED;
+  if (c->tablas_contexto < 1 || c->tablas_contexto >= c->n_tablas) return ASRN_ERR_ARG;
+  if (c->confirmar < 1 || c->confirmar > kMaxConfirm) return ASRN_ERR_UNSUPPORTED;
+  if (c->sufijo < 1 || c->sufijo > kMaxSuffix) return ASRN_ERR_UNSUPPORTED;
+  if (c->vistos < 1 || c->vistos > kMaxSeen) return ASRN_ERR_UNSUPPORTED;
+  if (c->nodos_racha < 2) return ASRN_ERR_ARG;
+  if (c->hidden < 1 || c->hidden > kMaxHidden) return ASRN_ERR_UNSUPPORTED;
+  if (c->half != 0 && c->half != 1) return ASRN_ERR_ARG;
+  if (c->L > (int64_t)1 << 30) return ASRN_ERR_UNSUPPORTED;
+  return ASRN_OK;
+}
+
+int check_weights(const asrn_layer_weights* w) {
+  if (!w) return ASRN_ERR_ARG;
+  const void* ps[] = {w->ln_w, w->ln_b, w->cq, w->ck, w->w_reloj, w->b_reloj, w->pal0_w, w->pal0_b, w->pal2_w,
+                      w->pal2_b, w->ctx0_w, w->ctx0_b, w->ctx2_w, w->ctx2_b, w->v_w, w->o_w, w->g_w, w->g_b,
+                      w->g_conf_w, w->g_conf_b, w->w_vistos, w->u_hawkes, w->log_kappa, w->log_kappa_racha,
+                      w->w_sufijo, w->gamma, w->d_racha, w->c_vistos, w->r_firma};
+  for (const void* p : ps)
+    if (!p) return ASRN_ERR_ARG;
+  return ASRN_OK;
+}
+
+// Workspace of one layer forward, in order of use.
+struct Workspace {
+  size_t sig, qc, kc, beta, bt, la, glogit, ea, phi, ids_rows, orden, ids_o, acc, hay, mx, pk, vistos, hawkes,
+      racha, sort, total;
+  size_t sort_bytes;
+};
+
+Workspace workspace_layout(const asrn_layer_config& c) {
+  const size_t M = (size_t)c.B * c.L, es = c.half ? 2 : 4, d = c.d, T = c.n_tablas, n = c.vistos;
+  const size_t P = T * c.n_bits;
+  Workspace w;
+  size_t o = 0;
+  auto take = [&](size_t bytes) { size_t at = o; o = align_up(o + bytes); return at; };
+  w.sig = take(M * 4);
+  w.qc = take(M * c.confirmar * es);
+  w.kc = take(M * c.confirmar * es);
+  w.beta = take(M * 8);
+  w.bt = take(M * 8);
+  w.la = take(M * 4);
+  w.glogit = take(M * 4);
+  w.ea = take(c.half ? M * d * es : 0);
+  w.phi = take(M * P * es);
+  w.ids_rows = take(M * T * 2);
+  w.orden = take(M * T * 4);
+  w.ids_o = take(M * T * 2);
+  w.acc = take(M * d * 4);
+  w.hay = take(M * T);
+  w.mx = take(M * T * 4);
+  w.pk = take(M * T * 4);
+  w.vistos = take(M * n);
+  w.hawkes = take(M * n * 4);
+  w.racha = take(M * 4);
+  w.sort_bytes = bucket_sort_workspace((int64_t)c.B * T, c.L, c.n_bits);
+  w.sort = take(w.sort_bytes);
+  w.total = o;
+  return w;
+}
+
+ContextArgs context_args(const asrn_layer_config& c, const asrn_layer_weights& w, const char* prep, const float* h,
+                         const float* E, const int64_t* tokens) {
+  const PreparedLayout pl = prepared_layout(c);
+  ContextArgs a{};
+  a.B = c.B; a.L = c.L; a.d = (int)c.d; a.cf = c.confirmar;
+  a.h = h; a.E = E; a.tokens = tokens;
+  a.ln_w = w.ln_w; a.ln_b = w.ln_b; a.w_reloj = w.w_reloj; a.b_reloj = w.b_reloj;
+  a.g_w = w.g_w; a.g_b = w.g_b; a.r_firma = w.r_firma;
+  a.wctx = prep + pl.wctx;
+  a.beta_max = c.beta_max; a.log_alfa_min = c.log_alfa_min;
+  return a;
+}
+
+HashArgs hash_args(const asrn_layer_config& c, const char* prep, const float* E, void* Ea, void* phi,
+                   uint16_t* ids_rows) {
+  const PreparedLayout pl = prepared_layout(c);
+  HashArgs a{};
+  a.B = c.B; a.L = c.L; a.d = (int)c.d; a.m = c.hidden; a.T = c.n_tablas; a.Tw = c.n_tablas - c.tablas_contexto;
+  a.nb = c.n_bits; a.P = c.n_tablas * c.n_bits;
+  a.E = E; a.Ea = Ea;
+  a.w1 = prep + pl.w1; a.b1 = reinterpret_cast<const float*>(prep + pl.b1);
+  a.w2 = prep + pl.w2; a.b2 = reinterpret_cast<const float*>(prep + pl.b2);
+  a.phi = phi; a.ids_rows = ids_rows;
+  return a;
+}
+
+ScoreArgs score_args(const asrn_layer_config& c, const asrn_layer_weights& w, const char* prep) {
+  const PreparedLayout pl = prepared_layout(c);
+  ScoreArgs a{};
+  a.B = c.B; a.L = c.L; a.d = (int)c.d; a.T = c.n_tablas; a.nb = c.n_bits; a.P = c.n_tablas * c.n_bits;
+  a.C = c.chunk; a.cf = c.confirmar; a.K = c.sufijo;
+  a.inv_temp_div = (float)sqrt((double)a.P);
+  a.esc_c = (float)pow((double)c.confirmar, -0.5);
+  a.w_suf = w.w_sufijo;
+  a.tasa = reinterpret_cast<const float*>(prep + pl.tasa);
+  return a;
+}
+
+RepetitionArgs repetition_args(const asrn_layer_config& c, const asrn_layer_weights& w, const char* prep) {
+  const PreparedLayout pl = prepared_layout(c);
+  RepetitionArgs a{};
+  a.B = c.B; a.L = c.L; a.n = c.vistos;
+  a.c = w.c_vistos;
+  a.kappa = reinterpret_cast<const float*>(prep + pl.kappa);
+  return a;
+}
+
+GateArgs gate_args(const asrn_layer_config& c, const asrn_layer_weights& w, const char* prep) {
+  const PreparedLayout pl = prepared_layout(c);
+  GateArgs a{};
+  a.B = c.B; a.L = c.L; a.d = (int)c.d; a.T = c.n_tablas; a.Tc = c.tablas_contexto; a.n = c.vistos;
+  a.nodes = c.nodos_racha;
+  a.mejor_max = c.mejor_max; a.tope = c.tope_puerta; a.racha_paso = (float)c.racha_paso;
+  a.wov = prep + pl.wov;
+  a.gconf = reinterpret_cast<const float*>(prep + pl.gconf);
+  a.w_vistos = w.w_vistos; a.u_hawkes = w.u_hawkes; a.d_racha = w.d_racha;
+  a.u_racha = reinterpret_cast<const float*>(prep + pl.u_racha);
+  return a;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* asrn_status_string(int status) {
+  switch (status) {
+    case ASRN_OK: return "ok";
+    case ASRN_ERR_ARG: return "invalid argument (shape, null pointer or option out of range)";
+    case ASRN_ERR_UNSUPPORTED: return "option combination not supported by this build";
+    case ASRN_ERR_WORKSPACE: return "workspace or prepared buffer too small";
+    case ASRN_ERR_CUDA: return "CUDA kernel launch failed";
+    case ASRN_ERR_TIMEOUT: return "bounded device wait timed out";
+    default: return "unknown status";
+  }
+}
+
+int asrn_abi_version(void) { return 1; }
+
+size_t asrn_layer_prepared_bytes(const asrn_layer_config* cfg) {
+  if (check_config(cfg) != ASRN_OK) return 0;
+  return prepared_layout(*cfg).total;
+}
+
+int asrn_layer_prepare(const asrn_layer_config* cfg, const asrn_layer_weights* w, void* prepared, size_t bytes,
+                       void* stream) {
+  int st = check_config(cfg);
+  if (st) return st;
+  if ((st = check_weights(w))) return st;
+  if (!prepared || bytes < prepared_layout(*cfg).total) return ASRN_ERR_WORKSPACE;
+  return launch_prepare(*cfg, *w, prepared, as_stream(stream));
+}
+
+size_t asrn_layer_workspace_bytes(const asrn_layer_config* cfg) {
+  if (check_config(cfg) != ASRN_OK) return 0;
+  return workspace_layout(*cfg).total;
+}
+
+int asrn_layer_forward(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared,
+                       const float* E, const float* h, const int64_t* tokens, float* h_out, void* workspace,
+                       size_t workspace_bytes, void* stream) {
+  int st = check_config(cfg);
+  if (st) return st;
+  if ((st = check_weights(w))) return st;
+  const asrn_layer_config& c = *cfg;
+  if ((int64_t)c.B * c.L == 0) return ASRN_OK;
+  if (!E || !h || !h_out || !prepared) return ASRN_ERR_ARG;
+  const Workspace ws = workspace_layout(c);
+  if (!workspace || workspace_bytes < ws.total) return ASRN_ERR_WORKSPACE;
+  cudaStream_t s = as_stream(stream);
+  char* base = reinterpret_cast<char*>(workspace);
+  const char* prep = reinterpret_cast<const char*>(prepared);
+  const int64_t M = c.B * c.L;
+  float* sig = reinterpret_cast<float*>(base + ws.sig);
+  double* beta = reinterpret_cast<double*>(base + ws.beta);
+  double* Bt = reinterpret_cast<double*>(base + ws.bt);
+  float* la = reinterpret_cast<float*>(base + ws.la);
+  float* glogit = reinterpret_cast<float*>(base + ws.glogit);
+  void* Ea = c.half ? (void*)(base + ws.ea) : (void*)E;
+  void* phi = base + ws.phi;
+  uint16_t* ids_rows = reinterpret_cast<uint16_t*>(base + ws.ids_rows);
+  int32_t* orden = reinterpret_cast<int32_t*>(base + ws.orden);
+  uint16_t* ids_o = reinterpret_cast<uint16_t*>(base + ws.ids_o);
+  float* acc = reinterpret_cast<float*>(base + ws.acc);
+  uint8_t* hay = reinterpret_cast<uint8_t*>(base + ws.hay);
+  float* mx = reinterpret_cast<float*>(base + ws.mx);
+  float* pk = reinterpret_cast<float*>(base + ws.pk);
+  uint8_t* vistos = reinterpret_cast<uint8_t*>(base + ws.vistos);
+  float* hawkes = reinterpret_cast<float*>(base + ws.hawkes);
+  float* racha = reinterpret_cast<float*>(base + ws.racha);
+
+  ContextArgs ca = context_args(c, *w, prep, h, E, tokens);
+  ca.Qc = base + ws.qc; ca.Kc = base + ws.kc; ca.beta = beta; ca.log_alfa = la; ca.glogit = glogit; ca.sig = sig;
+  if ((st = launch_context(ca, c.half, s))) return st;
+  if ((st = launch_clock(beta, Bt, c.B, c.L, s))) return st;
+  HashArgs ha = hash_args(c, prep, E, Ea, phi, ids_rows);
+  if ((st = launch_hash(ha, c.half, s))) return st;
+  if ((st = launch_bucket_sort(c.B * c.n_tablas, c.L, c.n_bits, ids_rows, orden, ids_o, base + ws.sort,
+                               ws.sort_bytes, s)))
+    return st;
+  if (cudaMemsetAsync(acc, 0, (size_t)M * c.d * 4, s) != cudaSuccess) return ASRN_ERR_CUDA;
+  ScoreArgs sa = score_args(c, *w, prep);
+  sa.orden = orden; sa.ids_o = ids_o; sa.phi = phi; sa.Qc = base + ws.qc; sa.Kc = base + ws.kc; sa.sig = sig;
+  sa.Bt = Bt; sa.log_alfa = la; sa.Ea = Ea; sa.acc = acc; sa.sen_hay = hay; sa.sen_mx = mx; sa.sen_pk = pk;
+  if ((st = launch_score(sa, c.half, s))) return st;
+  RepetitionArgs ra = repetition_args(c, *w, prep);
+  ra.sig = sig; ra.beta = beta; ra.Bt = Bt; ra.log_alfa = la; ra.vistos = vistos; ra.hawkes = hawkes;
+  ra.racha = racha;
+  if ((st = launch_repetition(ra, nullptr, 0, s))) return st;
+  GateArgs ga = gate_args(c, *w, prep);
+  ga.h = h; ga.glogit = glogit; ga.acc = acc; ga.sen_hay = hay; ga.sen_mx = mx; ga.sen_pk = pk;
+  ga.vistos = vistos; ga.hawkes = hawkes; ga.racha = racha; ga.out = h_out;
+  return launch_gate(ga, c.half, s);
+}
+
+int asrn_context(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared, const float* h,
+                 const float* E, const int64_t* tokens, void* Qc, void* Kc, double* beta, float* log_alfa,
+                 float* glogit, float* sig, void* stream) {
+  int st = check_config(cfg);
+  if (st) return st;
+  if ((st = check_weights(w))) return st;
+  if (!h || !prepared || !Qc || !Kc || !beta || !log_alfa || !glogit || !sig || (!tokens && !E)) return ASRN_ERR_ARG;
+  ContextArgs a = context_args(*cfg, *w, reinterpret_cast<const char*>(prepared), h, E, tokens);
+  a.Qc = Qc; a.Kc = Kc; a.beta = beta; a.log_alfa = log_alfa; a.glogit = glogit; a.sig = sig;
+  return launch_context(a, cfg->half, as_stream(stream));
+}
+
+int asrn_clock(int64_t B, int64_t L, const double* beta, double* Bt, void* stream) {
+  if (B < 0 || L < 0 || (B * L > 0 && (!beta || !Bt))) return ASRN_ERR_ARG;
+  return launch_clock(beta, Bt, B, L, as_stream(stream));
+}
+
+int asrn_hash(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared, const float* E,
+              void* Ea, void* phi, uint16_t* ids_rows, void* stream) {
+  int st = check_config(cfg);
+  if (st) return st;
+  if (!prepared || !E || !phi || !ids_rows || (cfg->half && !Ea)) return ASRN_ERR_ARG;
+  (void)w;
+  HashArgs a = hash_args(*cfg, reinterpret_cast<const char*>(prepared), E, Ea, phi, ids_rows);
+  return launch_hash(a, cfg->half, as_stream(stream));
+}
+
+int asrn_ids_from_phi(int64_t B, int64_t L, int32_t T, int32_t nb, const float* phi, uint16_t* ids_rows,
+                      void* stream) {
+  if (B < 0 || L < 0 || T < 1 || nb < 1 || nb > 16 || (B * L > 0 && (!phi || !ids_rows))) return ASRN_ERR_ARG;
+  return launch_ids_from_phi(B, L, T, nb, phi, ids_rows, as_stream(stream));
+}
+
+size_t asrn_bucket_sort_workspace_bytes(int64_t rows, int64_t L, int32_t nb) {
+  return bucket_sort_workspace(rows, L, nb);
+}
+
+int asrn_bucket_sort(int64_t rows, int64_t L, int32_t nb, const uint16_t* ids_rows, int32_t* orden,
+                     uint16_t* ids_o, void* workspace, size_t workspace_bytes, void* stream) {
+  if (rows < 0 || L < 0 || (rows * L > 0 && (!ids_rows || !orden || !ids_o))) return ASRN_ERR_ARG;
+  return launch_bucket_sort(rows, L, nb, ids_rows, orden, ids_o, workspace, workspace_bytes, as_stream(stream));
+}
+
+int asrn_score(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared,
+               const int32_t* orden, const uint16_t* ids_o, const void* phi, const void* Qc, const void* Kc,
+               const float* sig, const double* Bt, const float* log_alfa, const void* Ea, float* acc,
+               uint8_t* sen_hay, float* sen_mx, float* sen_pk, void* stream) {
+  int st = check_config(cfg);
+  if (st) return st;
+  if ((st = check_weights(w))) return st;
+  if (!prepared || !orden || !ids_o || !phi || !Qc || !Kc || !sig || !Bt || !log_alfa || !Ea || !acc || !sen_hay ||
+      !sen_mx || !sen_pk)
+    return ASRN_ERR_ARG;
+  ScoreArgs a = score_args(*cfg, *w, reinterpret_cast<const char*>(prepared));
+  a.orden = orden; a.ids_o = ids_o; a.phi = phi; a.Qc = Qc; a.Kc = Kc; a.sig = sig; a.Bt = Bt; a.log_alfa = log_alfa;
+  a.Ea = Ea; a.acc = acc; a.sen_hay = sen_hay; a.sen_mx = sen_mx; a.sen_pk = sen_pk;
+  return launch_score(a, cfg->half, as_stream(stream));
+}
+
+int asrn_candidates(int64_t B, int64_t L, int32_t T, int32_t C, int32_t K, const int32_t* orden,
+                    const uint16_t* ids_o, const float* sig, int32_t* cand, uint8_t* suffix, void* stream) {
+  if (B < 0 || L < 0 || T < 1 || (B * L > 0 && (!orden || !ids_o || !sig || !cand || !suffix))) return ASRN_ERR_ARG;
+  return launch_candidates(B, L, T, C, K, orden, ids_o, sig, cand, suffix, as_stream(stream));
+}
+
+size_t asrn_repetition_workspace_bytes(const asrn_layer_config* cfg) {
+  if (check_config(cfg) != ASRN_OK) return 0;
+  return repetition_workspace(cfg->B, cfg->L, cfg->vistos);
+}
+
+int asrn_repetition(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared,
+                    const float* sig, const double* beta, const double* Bt, const float* log_alfa, uint8_t* vistos,
+                    float* hawkes, float* racha, double* keys, int32_t* orden_ng, uint8_t* repetido,
+                    void* workspace, size_t workspace_bytes, void* stream) {
+  int st = check_config(cfg);
+  if (st) return st;
+  if ((st = check_weights(w))) return st;
+  if (!prepared || !sig || !beta || !Bt || !log_alfa || !vistos || !hawkes || !racha) return ASRN_ERR_ARG;
+  RepetitionArgs a = repetition_args(*cfg, *w, reinterpret_cast<const char*>(prepared));
+  a.sig = sig; a.beta = beta; a.Bt = Bt; a.log_alfa = log_alfa; a.vistos = vistos; a.hawkes = hawkes; a.racha = racha;
+  a.keys = keys; a.orden_ng = orden_ng; a.repetido = repetido;
+  return launch_repetition(a, workspace, workspace_bytes, as_stream(stream));
+}
+
+int asrn_gate(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared, const float* h,
+              const float* glogit, const float* acc, const uint8_t* sen_hay, const float* sen_mx,
+              const float* sen_pk, const uint8_t* vistos, const float* hawkes, const float* racha, float* h_out,
+              void* stream) {
+  int st = check_config(cfg);
+  if (st) return st;
+  if ((st = check_weights(w))) return st;
+  if (!prepared || !h || !glogit || !acc || !sen_hay || !sen_mx || !sen_pk || !vistos || !hawkes || !racha || !h_out)
+    return ASRN_ERR_ARG;
+  GateArgs a = gate_args(*cfg, *w, reinterpret_cast<const char*>(prepared));
+  a.h = h; a.glogit = glogit; a.acc = acc; a.sen_hay = sen_hay; a.sen_mx = sen_mx; a.sen_pk = sen_pk;
+  a.vistos = vistos; a.hawkes = hawkes; a.racha = racha; a.out = h_out;
+  return launch_gate(a, cfg->half, as_stream(stream));
+}
+
+}  // extern "C"

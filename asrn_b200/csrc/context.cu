@@ -1,0 +1,169 @@
+// Context stage: LN(h) -> Qc, Kc, beta, log_alfa; g(h); token signatures; and the fp64 clock Bt = cumsum(beta).
+// Reference: CapaASRNEstable._contexto (asrn/estable.py:153-194), firmas_de_piezas (asrn/nucleo.py:161-164),
+// CapaASRN._firma (asrn/nucleo.py:634-637), the clock Bt = beta.cumsum(1) (asrn/estable.py:418) and the gate's
+// g(h) term computed in the precision of h (asrn/estable.py:393-394).
+#include "common.cuh"
+#include "layout.h"
+
+namespace asrn {
+
+// One warp per token. Each lane owns the elements j = lane + 32 i of the row (coalesced across the warp).
+template <bool Half>
+__global__ void __launch_bounds__(256) k_context(ContextArgs a) {
+  using A = Act<Half>;
+  const int64_t M = a.B * a.L;
+  const int d = a.d, cf = a.cf;
+  const int lane = threadIdx.x & 31;
+  const int64_t tok = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (tok >= M) return;
+  const float* hrow = a.h + tok * d;
+  constexpr int kMaxPer = 32;  // d <= 1024
+  float x[kMaxPer];
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxPer; ++i) {
+    int j = lane + 32 * i;
+    x[i] = (j < d) ? hrow[j] : 0.f;
+    s += x[i];
+  }
+  const float mean = warp_sum(s) / (float)d;
+  float v = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxPer; ++i) {
+    int j = lane + 32 * i;
+    float c = (j < d) ? x[i] - mean : 0.f;
+    v += c * c;
+  }
+  const float rstd = 1.f / sqrtf(warp_sum(v) / (float)d + 1e-5f);
+  // g(h): raw h, fp32 (asrn/estable.py:393-394)
+  float gl = 0.f;
+  float hn[kMaxPer];
+#pragma unroll
+  for (int i = 0; i < kMaxPer; ++i) {
+    int j = lane + 32 * i;
+    if (j < d) {
+      gl += x[i] * a.g_w[j];
+      hn[i] = (x[i] - mean) * rstd * a.ln_w[j] + a.ln_b[j];
+    } else {
+      hn[i] = 0.f;
+    }
+  }
+  gl = warp_sum(gl);
+  // clock projection u = LN(h) . w_reloj + b_reloj in true fp32 (asrn/estable.py:171-185)
+  float u0 = 0.f, u1 = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxPer; ++i) {
+    int j = lane + 32 * i;
+    if (j < d) {
+      u0 += hn[i] * a.w_reloj[j];
+      u1 += hn[i] * a.w_reloj[d + j];
+    }
+  }
+  u0 = warp_sum(u0) + a.b_reloj[0];
+  u1 = warp_sum(u1) + a.b_reloj[1];
+  // Qc, Kc = LN(h)_act . [cq; ck]^T (act: bf16 inputs and output under autocast)
+  const typename A::T* W = reinterpret_cast<const typename A::T*>(a.wctx);
+  for (int o = 0; o < 2 * cf; ++o) {
+    float acc = 0.f;
+#pragma unroll
+    for (int i = 0; i < kMaxPer; ++i) {
+      int j = lane + 32 * i;
+      if (j < d) acc += act<Half>(hn[i]) * A::load(W + (int64_t)o * d + j);
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) {
+      typename A::T* dst = reinterpret_cast<typename A::T*>(o < cf ? a.Qc : a.Kc);
+      A::store(dst + tok * cf + (o < cf ? o : o - cf), acc);
+    }
+  }
+  // signature: token id as fp32, or E . r_firma (fp32) when no ids are given
+  float sig;
+  if (a.tokens) {
+    sig = (float)a.tokens[tok];
+  } else {
+    float e = 0.f;
+    const float* erow = a.E + tok * d;
+    for (int j = lane; j < d; j += 32) e += erow[j] * a.r_firma[j];
+    sig = warp_sum(e);
+  }
+  if (lane == 0) {
+    float beta = fminf(softplus_t(u0), a.beta_max);
+    float la = fmaxf(logsigmoid_t(u1) + 0.693147180559945309f, a.log_alfa_min);
+    a.beta[tok] = (double)beta;
+    a.log_alfa[tok] = la;
+    a.glogit[tok] = gl + a.g_b[0];
+    a.sig[tok] = sig;
+  }
+}
+
+// Inclusive fp64 prefix sum along L, one block per batch row, chunks of 1024 * 4 with a running carry.
+__global__ void __launch_bounds__(1024) k_clock(const double* __restrict__ beta, double* __restrict__ Bt, int64_t L) {
+  const int64_t b = blockIdx.x;
+  const double* src = beta + b * L;
+  double* dst = Bt + b * L;
+  __shared__ double warp_tot[32];
+  __shared__ double carry_s;
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  if (tid == 0) carry_s = 0.0;
+  __syncthreads();
+  constexpr int kItems = 4;
+  for (int64_t base = 0; base < L; base += 1024 * kItems) {
+    double v[kItems];
+    double run = 0.0;
+#pragma unroll
+    for (int k = 0; k < kItems; ++k) {
+      int64_t i = base + (int64_t)tid * kItems + k;
+      run += (i < L) ? src[i] : 0.0;
+      v[k] = run;
+    }
+    // warp inclusive scan of the thread totals
+    double t = run;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      double y = __shfl_up_sync(0xffffffffu, t, o);
+      if (lane >= o) t += y;
+    }
+    if (lane == 31) warp_tot[wid] = t;
+    __syncthreads();
+    if (wid == 0) {
+      double w = warp_tot[lane];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        double y = __shfl_up_sync(0xffffffffu, w, o);
+        if (lane >= o) w += y;
+      }
+      warp_tot[lane] = w;
+    }
+    __syncthreads();
+    const double carry = carry_s;
+    const double excl = carry + (wid > 0 ? warp_tot[wid - 1] : 0.0) + (t - run);
+#pragma unroll
+    for (int k = 0; k < kItems; ++k) {
+      int64_t i = base + (int64_t)tid * kItems + k;
+      if (i < L) dst[i] = excl + v[k];
+    }
+    __syncthreads();
+    if (tid == 0) carry_s = carry + warp_tot[31];
+    __syncthreads();
+  }
+}
+
+int launch_context(const ContextArgs& a, bool half, cudaStream_t s) {
+  const int64_t M = a.B * a.L;
+  if (M == 0) return ASRN_OK;
+  const int warps = 8;
+  dim3 grid((unsigned)((M + warps - 1) / warps));
+  if (half)
+    k_context<true><<<grid, warps * 32, 0, s>>>(a);
+  else
+    k_context<false><<<grid, warps * 32, 0, s>>>(a);
+  return cudaGetLastError() == cudaSuccess ? ASRN_OK : ASRN_ERR_CUDA;
+}
+
+int launch_clock(const double* beta, double* Bt, int64_t B, int64_t L, cudaStream_t s) {
+  if (B == 0 || L == 0) return ASRN_OK;
+  k_clock<<<(unsigned)B, 1024, 0, s>>>(beta, Bt, L);
+  return cudaGetLastError() == cudaSuccess ? ASRN_OK : ASRN_ERR_CUDA;
+}
+
+}  // namespace asrn

@@ -1,0 +1,140 @@
+// Kernel argument structs and the byte layout of the prepared-weights and workspace buffers.
+#pragma once
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "../../include/asrn_b200.h"
+
+namespace asrn {
+
+inline size_t align_up(size_t x, size_t a = 256) { return (x + a - 1) / a * a; }
+
+// Derived weights, computed on the device by asrn_layer_prepare. "act" = bf16 when half, fp32 otherwise.
+struct PreparedLayout {
+  size_t wctx;    // (2cf, d) act: [cq; ck]
+  size_t w1;      // (3m, d) act: [pal0; ctx0[:, :d]; ctx0[:, d:]]
+  size_t b1;      // (2m) f32: pal0.bias, ctx0.bias (bf16-rounded when half: autocast rounds biases)
+  size_t w2;      // (P, m) act: [pal2; ctx2]
+  size_t b2;      // (P) f32 (rounded when half)
+  size_t wov;     // (d, d) act: W_o @ W_v
+  size_t gconf;   // (8) f32: g_conf weight (4), bias, (rounded when half)
+  size_t tasa;    // (T) f32: gamma / C
+  size_t kappa;   // (n + 1) f32: exp(log_kappa) (n), exp(log_kappa_racha), floored by kappa_min
+  size_t u_racha; // (nodes) f32: cumsum(d_racha)
+  size_t total;
+};
+
+inline PreparedLayout prepared_layout(const asrn_layer_config& c) {
+  const size_t es = c.half ? 2 : 4;
+  const size_t d = (size_t)c.d, m = (size_t)c.hidden, cf = (size_t)c.confirmar;
+  const size_t P = (size_t)c.n_tablas * c.n_bits;
+  PreparedLayout p;
+  size_t o = 0;
+  p.wctx = o; o = align_up(o + 2 * cf * d * es);
+  p.w1 = o; o = align_up(o + 3 * m * d * es);
+  p.b1 = o; o = align_up(o + 2 * m * 4);
+  p.w2 = o; o = align_up(o + P * m * es);
+  p.b2 = o; o = align_up(o + P * 4);
+  p.wov = o; o = align_up(o + d * d * es);
+  p.gconf = o; o = align_up(o + 8 * 4);
+  p.tasa = o; o = align_up(o + (size_t)c.n_tablas * 4);
+  p.kappa = o; o = align_up(o + ((size_t)c.vistos + 1) * 4);
+  p.u_racha = o; o = align_up(o + (size_t)c.nodos_racha * 4);
+  p.total = o;
+  return p;
+}
+
+struct ContextArgs {
+  int64_t B, L;
+  int d, cf;
+  const float* h;
+  const float* E;         // only for signatures without token ids
+  const int64_t* tokens;  // may be null
+  const float *ln_w, *ln_b, *w_reloj, *b_reloj, *g_w, *g_b, *r_firma;
+  const void* wctx;       // act (2cf, d)
+  float beta_max, log_alfa_min;
+  void *Qc, *Kc;
+  double* beta;
+  float *log_alfa, *glogit, *sig;
+};
+
+struct HashArgs {
+  int64_t B, L;
+  int d, m, T, Tw, nb, P;
+  const float* E;
+  void* Ea;                // act copy of E (written when half)
+  const void* w1;          // act (3m, d)
+  const float* b1;         // (2m)
+  const void* w2;          // act (P, m)
+  const float* b2;         // (P)
+  void* phi;               // act (B, L, P)
+  uint16_t* ids_rows;      // (B*T, L)
+};
+
+struct ScoreArgs {
+  int64_t B, L;
+  int d, T, nb, P, C, cf, K;
+  float inv_temp_div;      // temperature (scores are divided by it)
+  float esc_c;             // cf^-1/2
+  const int32_t* orden;
+  const uint16_t* ids_o;
+  const void *phi, *Qc, *Kc, *Ea;
+  const float* sig;
+  const double* Bt;
+  const float* log_alfa;
+  const float* w_suf;      // (K + 1)
+  const float* tasa;       // (T)
+  float* acc;
+  uint8_t* sen_hay;
+  float *sen_mx, *sen_pk;
+};
+
+struct RepetitionArgs {
+  int64_t B, L;
+  int n;
+  const float* sig;
+  const double* c;         // c_vistos (n)
+  const double* beta;
+  const double* Bt;
+  const float* log_alfa;
+  const float* kappa;      // (n + 1): the last one is the streak rate
+  uint8_t* vistos;
+  float *hawkes, *racha;
+  double* keys;            // optional
+  int32_t* orden_ng;       // optional
+  uint8_t* repetido;       // optional
+};
+
+struct GateArgs {
+  int64_t B, L;
+  int d, T, Tc, n, nodes;
+  float mejor_max, tope;
+  float racha_paso;
+  const float *h, *glogit, *acc;
+  const uint8_t* sen_hay;
+  const float *sen_mx, *sen_pk;
+  const uint8_t* vistos;
+  const float *hawkes, *racha;
+  const void* wov;         // act (d, d)
+  const float* gconf;      // (5)
+  const float *w_vistos, *u_hawkes, *u_racha, *d_racha;
+  float* out;
+};
+
+int launch_context(const ContextArgs& a, bool half, cudaStream_t s);
+int launch_clock(const double* beta, double* Bt, int64_t B, int64_t L, cudaStream_t s);
+int launch_hash(const HashArgs& a, bool half, cudaStream_t s);
+int launch_ids_from_phi(int64_t B, int64_t L, int T, int nb, const float* phi, uint16_t* ids_rows, cudaStream_t s);
+size_t bucket_sort_workspace(int64_t rows, int64_t L, int nb);
+int launch_bucket_sort(int64_t rows, int64_t L, int nb, const uint16_t* ids_rows, int32_t* orden, uint16_t* ids_o,
+                       void* ws, size_t ws_bytes, cudaStream_t s);
+int launch_score(const ScoreArgs& a, bool half, cudaStream_t s);
+int launch_candidates(int64_t B, int64_t L, int T, int C, int K, const int32_t* orden, const uint16_t* ids_o,
+                      const float* sig, int32_t* cand, uint8_t* suffix, cudaStream_t s);
+size_t repetition_workspace(int64_t B, int64_t L, int n);
+int launch_repetition(const RepetitionArgs& a, void* ws, size_t ws_bytes, cudaStream_t s);
+int launch_gate(const GateArgs& a, bool half, cudaStream_t s);
+int launch_prepare(const asrn_layer_config& c, const asrn_layer_weights& w, void* prepared, cudaStream_t s);
+
+}  // namespace asrn

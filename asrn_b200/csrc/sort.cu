@@ -1,0 +1,189 @@
+// Per-table stable bucket sort: for every row r = b * T + tau, the text positions ordered by bucket id, ties by
+// position. Reference: ids.transpose(1, 2).reshape(B*T, L).argsort(dim=-1, stable=True) (asrn/estable.py:220-221).
+//
+// Design: a row is cut into tiles of at most kTile positions. Each tile sorts composite 32-bit keys
+// (id << 13 | local position) in shared memory (bitonic network; the keys are unique, so any sort is stable).
+// A single-tile row is written out directly. Longer rows add a per-tile histogram of the 2^nb buckets, a column
+// scan over tiles plus a scan over buckets (the global slot where each tile's run of a bucket starts), and a
+// scatter of every tile's runs to their slots.
+#include "common.cuh"
+#include "layout.h"
+
+namespace asrn {
+
+constexpr int kTile = 8192;
+constexpr int kPosBits = 13;
+constexpr uint32_t kPosMask = (1u << kPosBits) - 1;
+
+__device__ __forceinline__ void bitonic_sort_u32(uint32_t* keys, int n2) {
+  for (int k = 2; k <= n2; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      for (int i = threadIdx.x; i < n2; i += blockDim.x) {
+        const int ixj = i ^ j;
+        if (ixj > i) {
+          const uint32_t a = keys[i], b = keys[ixj];
+          const bool up = (i & k) == 0;
+          if ((a > b) == up) {
+            keys[i] = b;
+            keys[ixj] = a;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+}
+
+// first index in keys[0, n) whose key >= v (keys ascending)
+__device__ __forceinline__ int lower_bound_u32(const uint32_t* keys, int n, uint32_t v) {
+  int lo = 0, hi = n;
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    if (keys[mid] < v) lo = mid + 1; else hi = mid;
+  }
+  return lo;
+}
+
+__global__ void __launch_bounds__(1024) k_bsort_tile(const uint16_t* __restrict__ ids_rows, int64_t L, int ntiles,
+                                                     int n2, int nb, int32_t* __restrict__ orden,
+                                                     uint16_t* __restrict__ ids_o, uint32_t* __restrict__ tmp,
+                                                     int32_t* __restrict__ hist) {
+  extern __shared__ uint32_t keys[];
+  const int tile = blockIdx.x;
+  const int64_t row = blockIdx.y;
+  const int64_t base = (int64_t)tile * kTile;
+  const int n = (int)min((int64_t)kTile, L - base);
+  const uint16_t* src = ids_rows + row * L + base;
+  for (int i = threadIdx.x; i < n2; i += blockDim.x)
+    keys[i] = (i < n) ? (((uint32_t)src[i] << kPosBits) | (uint32_t)i) : 0xFFFFFFFFu;
+  __syncthreads();
+  bitonic_sort_u32(keys, n2);
+  if (ntiles == 1) {
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      const uint32_t k = keys[i];
+      orden[row * L + i] = (int32_t)(k & kPosMask);
+      ids_o[row * L + i] = (uint16_t)(k >> kPosBits);
+    }
+    return;
+  }
+  uint32_t* t = tmp + row * L + base;
+  int32_t* hrow = hist + (row * ntiles + tile) * ((int64_t)1 << nb);
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const uint32_t k = keys[i];
+    t[i] = k;
+    const uint32_t id = k >> kPosBits;
+    if (i == n - 1 || (keys[i + 1] >> kPosBits) != id) {
+      const int first = lower_bound_u32(keys, n, id << kPosBits);
+      hrow[id] = i - first + 1;
+    }
+  }
+}
+
+// Per row: hist[row][tile][bin] (counts) -> the global slot where the tile's run of bin starts.
+__global__ void __launch_bounds__(1024) k_bsort_offsets(int32_t* __restrict__ hist, int ntiles, int nb) {
+  const int64_t row = blockIdx.x;
+  const int nbins = 1 << nb;
+  const int per = (nbins + blockDim.x - 1) / blockDim.x;
+  const int b0 = threadIdx.x * per;
+  int32_t* h = hist + row * (int64_t)ntiles * nbins;
+  int local = 0;
+  for (int k = 0; k < per; ++k) {
+    const int bin = b0 + k;
+    if (bin >= nbins) break;
+    int run = 0;
+    for (int tl = 0; tl < ntiles; ++tl) run += h[(int64_t)tl * nbins + bin];
+    local += run;
+  }
+  // block exclusive scan of the per-thread totals
+  __shared__ int wsum[32];
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  int incl = local;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  if (lane == 31) wsum[wid] = incl;
+  __syncthreads();
+  if (wid == 0) {
+    int w = (lane < (int)(blockDim.x >> 5)) ? wsum[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
+    }
+    wsum[lane] = w;
+  }
+  __syncthreads();
+  int run_base = (wid > 0 ? wsum[wid - 1] : 0) + incl - local;
+  for (int k = 0; k < per; ++k) {
+    const int bin = b0 + k;
+    if (bin >= nbins) break;
+    int off = run_base;
+    for (int tl = 0; tl < ntiles; ++tl) {
+      const int c = h[(int64_t)tl * nbins + bin];
+      h[(int64_t)tl * nbins + bin] = off;
+      off += c;
+    }
+    run_base = off;
+  }
+}
+
+__global__ void __launch_bounds__(1024) k_bsort_scatter(const uint32_t* __restrict__ tmp,
+                                                        const int32_t* __restrict__ hist, int64_t L, int ntiles,
+                                                        int nb, int32_t* __restrict__ orden,
+                                                        uint16_t* __restrict__ ids_o) {
+  extern __shared__ uint32_t keys[];
+  const int tile = blockIdx.x;
+  const int64_t row = blockIdx.y;
+  const int64_t base = (int64_t)tile * kTile;
+  const int n = (int)min((int64_t)kTile, L - base);
+  const uint32_t* t = tmp + row * L + base;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) keys[i] = t[i];
+  __syncthreads();
+  const int32_t* hrow = hist + (row * ntiles + tile) * ((int64_t)1 << nb);
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const uint32_t k = keys[i];
+    const uint32_t id = k >> kPosBits;
+    const int first = lower_bound_u32(keys, n, id << kPosBits);
+    const int64_t dst = row * L + hrow[id] + (i - first);
+    orden[dst] = (int32_t)(base + (k & kPosMask));
+    ids_o[dst] = (uint16_t)id;
+  }
+}
+
+static int ntiles_of(int64_t L) { return (int)((L + kTile - 1) / kTile); }
+
+size_t bucket_sort_workspace(int64_t rows, int64_t L, int nb) {
+  const int nt = ntiles_of(L);
+  if (nt <= 1) return 0;
+  return align_up((size_t)rows * L * 4) + align_up((size_t)rows * nt * ((size_t)1 << nb) * 4);
+}
+
+int launch_bucket_sort(int64_t rows, int64_t L, int nb, const uint16_t* ids_rows, int32_t* orden, uint16_t* ids_o,
+                       void* ws, size_t ws_bytes, cudaStream_t s) {
+  if (rows == 0 || L == 0) return ASRN_OK;
+  if (nb < 1 || nb > 16 || L > ((int64_t)1 << 31) - 1) return ASRN_ERR_ARG;
+  const int nt = ntiles_of(L);
+  int n2 = 1;
+  const int64_t tile_len = L < kTile ? L : (int64_t)kTile;
+  while (n2 < tile_len) n2 <<= 1;
+  const size_t smem = (size_t)n2 * 4;
+  cudaFuncSetAttribute(k_bsort_tile, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(smem < 4 ? 4 : smem));
+  if (nt == 1) {
+    k_bsort_tile<<<dim3(1, (unsigned)rows), 1024, smem, s>>>(ids_rows, L, 1, n2, nb, orden, ids_o, nullptr, nullptr);
+    return cudaGetLastError() == cudaSuccess ? ASRN_OK : ASRN_ERR_CUDA;
+  }
+  if (ws_bytes < bucket_sort_workspace(rows, L, nb) || ws == nullptr) return ASRN_ERR_WORKSPACE;
+  uint32_t* tmp = reinterpret_cast<uint32_t*>(ws);
+  int32_t* hist = reinterpret_cast<int32_t*>(reinterpret_cast<char*>(ws) + align_up((size_t)rows * L * 4));
+  const size_t hist_bytes = (size_t)rows * nt * ((size_t)1 << nb) * 4;
+  if (cudaMemsetAsync(hist, 0, hist_bytes, s) != cudaSuccess) return ASRN_ERR_CUDA;
+  k_bsort_tile<<<dim3(nt, (unsigned)rows), 1024, smem, s>>>(ids_rows, L, nt, n2, nb, orden, ids_o, tmp, hist);
+  k_bsort_offsets<<<(unsigned)rows, 1024, 0, s>>>(hist, nt, nb);
+  cudaFuncSetAttribute(k_bsort_scatter, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  k_bsort_scatter<<<dim3(nt, (unsigned)rows), 1024, smem, s>>>(tmp, hist, L, nt, nb, orden, ids_o);
+  return cudaGetLastError() == cudaSuccess ? ASRN_OK : ASRN_ERR_CUDA;
+}
+
+}  // namespace asrn

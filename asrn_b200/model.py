@@ -1,0 +1,114 @@
+"""The ASRN language model around the layer: embedding -> local blocks with an ASRN layer after every `largo_cada`
+blocks -> ln_f -> tied head. Mirror of asrn.nucleo.ModeloASRN / BloqueLocal / crear_modelo
+(asrn/nucleo.py:969-1119) with the same module names (state_dict compatible) and initialisation order.
+
+The local blocks, embedding and head are plain PyTorch (cuDNN / cuBLAS): they are outside the ASRN hot path. The
+ASRN layers are asrn_b200.ASRNLayer (CUDA kernels of libasrn_b200.so).
+"""
+import math
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from .layer import ASRNLayer
+
+
+def firmas_de_piezas(piezas):
+    """Token id -> fp32 signature (asrn/nucleo.py:161-164)."""
+    return piezas.to(torch.float32)
+
+
+class BloqueLocal(nn.Module):
+    """Causal local context: dense convolution over the k-1 previous tokens and the current one, then an MLP
+    (asrn/nucleo.py:969-1014, the default mezcla='conv')."""
+
+    def __init__(self, d, k=4, ff=128, dropout=0.0, mezcla='conv', memoria_max=1024):
+        super().__init__()
+        if mezcla != 'conv':
+            raise NotImplementedError("asrn_b200 builds the default local block (mezcla='conv')")
+        self.k, self.mezcla = k, mezcla
+        self.ln1 = nn.LayerNorm(d)
+        self.conv = nn.Conv1d(d, d, k)
+        self.ln2 = nn.LayerNorm(d)
+        self.ff = nn.Sequential(nn.Linear(d, ff), nn.GELU(), nn.Linear(ff, d))
+        self.drop = nn.Dropout(dropout)
+
+    def forward(self, h):
+        z = self.ln1(h)
+        c = F.gelu(self.conv(F.pad(z.transpose(1, 2), (self.k - 1, 0))).transpose(1, 2))
+        h = h + self.drop(c)
+        return h + self.drop(self.ff(self.ln2(h)))
+
+
+LocalBlock = BloqueLocal
+
+
+def _escalar_profundo(modulo, n_capas):
+    """Deep-model start (asrn/nucleo.py:1035-1044): outputs added to the state shrink by 1/sqrt(2 n_capas)."""
+    f = 1.0 / (2 * n_capas) ** 0.5
+    if isinstance(modulo, BloqueLocal):
+        modulo.conv.weight.mul_(f)
+        modulo.ff[2].weight.mul_(f)
+    else:
+        modulo.o.weight.mul_(f)
+
+
+class ModeloASRN(nn.Module):
+    """Same arguments and module names as the reference model (asrn/nucleo.py:1054-1078)."""
+
+    def __init__(self, V, d=64, n_capas=2, largo_cada=2, ff=None, k=4, init_profundo=None, checkpoint=False,
+                 dropout=0.0, mezcla='conv', memoria_max=1024, protecciones=None, **opciones_capa):
+        super().__init__()
+        assert n_capas >= 2 and largo_cada >= 1
+        assert V <= 2 ** 24, 'token signatures are exact up to 2**24 tokens'
+        self.config = dict(V=V, d=d, n_capas=n_capas, largo_cada=largo_cada, ff=ff or 2 * d, k=k, dropout=dropout,
+                           mezcla=mezcla, memoria_max=memoria_max, opciones_capa=dict(opciones_capa))
+        self.n_capas, self.checkpoint = n_capas, checkpoint
+        self.init_profundo = n_capas >= 8 if init_profundo is None else bool(init_profundo)
+        self.pos_largo = [i for i in range(n_capas - 1) if i % largo_cada == 0]
+        self.emb = nn.Embedding(V, d)
+        nn.init.normal_(self.emb.weight, std=0.02)
+        self.ln_f = nn.LayerNorm(d)
+        self.head = nn.Linear(d, V, bias=False)
+        self.head.weight = self.emb.weight
+        self.bloques = nn.ModuleList([BloqueLocal(d, k, ff or 2 * d, dropout, mezcla, memoria_max)
+                                      for _ in range(n_capas)])
+        self.largos = nn.ModuleList([ASRNLayer(d, protecciones, dropout=dropout, **opciones_capa)
+                                     for _ in self.pos_largo])
+        if self.init_profundo:
+            with torch.no_grad():
+                for b in self.bloques:
+                    _escalar_profundo(b, n_capas)
+                for c in self.largos:
+                    _escalar_profundo(c, n_capas)
+
+    def forward(self, x):
+        if self.emb.weight.dtype in (torch.float16, torch.bfloat16):
+            raise ValueError(f'the model has {self.emb.weight.dtype} weights: ASRN needs float32 weights; use '
+                             'torch.autocast for bf16 (asrn/nucleo.py:1025-1032)')
+        E = self.emb(x)
+        h, j = E, 0
+        for i, blq in enumerate(self.bloques):
+            h = blq(h)
+            if i in self.pos_largo:
+                h = self.largos[j](E, h, x)
+                j += 1
+        return self.head(self.ln_f(h))
+
+    def num_parametros(self):
+        return sum(p.numel() for p in self.parameters())
+
+
+ASRNModel = ModeloASRN
+
+
+def crear_modelo(V, d=64, n_capas=2, largo_cada=2, semilla=None, protecciones=None, **kw):
+    """asrn.create_model (asrn/__init__.py:60-64 -> asrn/nucleo.py:1114-1119): the model with the stable layer;
+    semilla fixes torch's RNG right before construction, so the weights equal the reference's for that seed."""
+    if semilla is not None:
+        torch.manual_seed(semilla)
+    return ModeloASRN(V, d, n_capas, largo_cada, protecciones=protecciones, **kw)
+
+
+create_model = crear_modelo

@@ -1,0 +1,373 @@
+"""Benchmark of the ASRN layer forward on B200 (the metric of BASELINE.json):
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 --master-port P bench.py --gpus N ...
+
+Workload (configuration 3 of the benchmark, the layer metric): one ASRNLayer(768) forward with default options on
+32 sequences x 8192 tokens per GPU, fp32 E/h as the model passes them, bf16 autocast; tokens Zipf(1.1) over 50,304
+with 20 % of positions in planted repeats of length 16-256 (seeded synthetic data, asrn_b200/synthetic.py), E rows from
+a random embedding table, random-init weights with the neutral parameters moved off zero. A step is one layer forward
+over the GPU's batch. Batches shard across GPUs with no collective, so per-GPU work is fixed (weak scaling).
+
+Printed (rank 0, one JSON line): value = tokens/s of the whole job (all ranks' tokens / max-over-ranks device time of
+K steps, inputs resident in HBM; the 805 MB E and h per GPU exceed the 126 MB L2, so no flush is needed), e2e = the
+same through ASRNLayer.forward with pinned host buffers and H2D/D2H copies in the timed region, roofline of the
+dominant kernel (candidate scoring, HBM-bound), the CPU baseline (the oracle port on the host cores), clocks.
+--impl reference: times the CPU implementation of the path (oracle port) on the host cores instead.
+"""
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, HERE)
+
+D, L_SEQ, B_PER_GPU, V = 768, 8192, 32, 50304
+METRIC = 'asrn_layer_fwd_tokens_per_s'
+UNIT = 'tokens/s'
+# Algorithmic HBM bytes per token of the candidate-scoring kernel at this config (bf16 features, fp32 accumulator):
+# per table, a key's phi + Kc + query phi + Qc (2 * 128 * 2 B), its value row (768 * 2 B) and 72 B of ids / clock /
+# log_alfa / signature; plus the output row (768 * 2 B): T * (512 + 1536 + 72) + 1536 = 18,496 B.
+SCORE_BYTES_PER_TOKEN = 8 * (2 * 128 * 2 + D * 2 + 72) + D * 2
+LAYER_BYTES_PER_TOKEN = 34696
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument('--gpus', type=int, default=1)
+    p.add_argument('--steps', type=int, default=10)
+    p.add_argument('--warmup', type=int, default=3)
+    p.add_argument('--impl', default='ours', choices=['ours', 'reference'])
+    p.add_argument('--batch', type=int, default=B_PER_GPU, help='sequences per GPU')
+    p.add_argument('--seq', type=int, default=L_SEQ)
+    p.add_argument('--no-cpu-baseline', action='store_true')
+    return p.parse_args()
+
+
+def config(args, n):
+    return {'workload': 'cfg3 layer: ASRNLayer(768) forward, %d x %d tokens per GPU, bf16 autocast, fp32 E/h'
+                        % (args.batch, args.seq),
+            'global_batch': args.batch * n, 'seq_len': args.seq, 'd': D, 'vocab': V,
+            'parallelism': 'dp%d (batch sharded, no collective)' % n,
+            'l2': 'inputs larger than L2 (E and h are %.0f MB each per GPU; L2 is 126 MB), no flush'
+                  % (args.batch * args.seq * D * 4 / 1e6)}
+
+
+# ---------------------------------------------------------------------------------------------------------------------
+# inputs
+# ---------------------------------------------------------------------------------------------------------------------
+
+def make_layer_params(seed=0):
+    """Random-init ASRNLayer(768) weights with the neutral (zero-init) parameters moved off zero (the reference tests'
+    recipe), as a state_dict of CPU tensors."""
+    import torch
+    import asrn_b200
+    torch.manual_seed(seed)
+    layer = asrn_b200.ASRNLayer(D)
+    g = torch.Generator().manual_seed(seed + 1)
+    with torch.no_grad():
+        for n, p in layer.named_parameters():
+            if n in ('w_reloj', 'b_reloj', 'gamma', 'log_kappa', 'log_kappa_racha', 'u_hawkes', 'd_racha', 'cq.weight',
+                     'w_sufijo', 'w_vistos', 'g_conf.weight', 'g_conf.bias'):
+                p.add_(torch.randn(p.shape, generator=g) * 0.5)
+        layer.gamma.copy_(torch.linspace(0.5, 3.0, layer.n_tablas))
+    return layer
+
+
+def make_inputs(batch, seq, rank, seed=0):
+    """(tokens int64 (B, L), E float32 (B, L, d), h float32 (B, L, d)) as numpy; rank-dependent seeds."""
+    import numpy as np
+    from asrn_b200 import synthetic
+    x = synthetic.config_tokens('cfg3', B=batch, L=seq, seed=seed + 1000 * rank)
+    g = np.random.default_rng(seed + 7)
+    table = (g.standard_normal((V, D)) * 0.02).astype(np.float32)      # emb init std 0.02 (asrn/nucleo.py:1066)
+    E = table[x]
+    h = (E + g.standard_normal(E.shape).astype(np.float32) * 0.5).astype(np.float32)
+    return x, E, h, table
+
+
+# ---------------------------------------------------------------------------------------------------------------------
+# clocks during the timed region
+# ---------------------------------------------------------------------------------------------------------------------
+
+class ClockSampler:
+    FIELDS = ('index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,'
+              'clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,'
+              'clocks_event_reasons.sw_power_cap')
+
+    def __init__(self, gpu_index):
+        self.idx = gpu_index
+        self.proc = None
+        self.f = None
+
+    def start(self):
+        try:
+            self.f = tempfile.NamedTemporaryFile('w+', suffix='.csv', delete=False)
+            self.proc = subprocess.Popen(['nvidia-smi', '-i', str(self.idx), '--query-gpu=' + self.FIELDS,
+                                          '--format=csv,noheader,nounits', '-lms', '100'], stdout=self.f,
+                                         stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {'sm_mhz': None, 'sm_max_mhz': None, 'reasons': ['nvidia-smi unavailable']}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.f.flush()
+        self.f.seek(0)
+        rows = [r.split(',') for r in self.f.read().strip().splitlines() if r.strip()]
+        os.unlink(self.f.name)
+        sm, mx, reasons = [], [], set()
+        names = ('hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap')
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                mx.append(float(r[2]))
+                for nm, v in zip(names, r[5:9]):
+                    if v.strip().lower() in ('active', '1'):
+                        reasons.add(nm)
+            except (ValueError, IndexError):
+                continue
+        return {'sm_mhz': statistics.median(sm) if sm else None, 'sm_max_mhz': max(mx) if mx else None,
+                'reasons': sorted(reasons), 'samples': len(sm)}
+
+
+# ---------------------------------------------------------------------------------------------------------------------
+# CPU baseline: the oracle port (the reference's algorithm restated in numpy) on the host cores
+# ---------------------------------------------------------------------------------------------------------------------
+
+def _oracle_one(payload):
+    """One sequence through the oracle's vectorised layer forward; returns seconds. Runs in a spawned worker."""
+    os.environ.setdefault('OMP_NUM_THREADS', '1')
+    os.environ.setdefault('OPENBLAS_NUM_THREADS', '1')
+    import numpy as np
+    sys.path.insert(0, HERE)
+    from oracle import asrn_oracle as O
+    params, x, E, h = payload
+    lay = O.Layer(params, D)
+    t0 = time.perf_counter()
+    O.layer_forward_fast(lay, E, h, x, half=True)
+    return time.perf_counter() - t0
+
+
+def cpu_baseline(layer_params, x, E, h, seq, workers=None, budget_s=20.0):
+    """Tokens/s of the oracle port on `workers` host processes (one sequence each, spawn pool)."""
+    import multiprocessing as mp
+    workers = workers or max(1, min(os.cpu_count() or 1, x.shape[0], 16))
+    ctx = mp.get_context('spawn')
+    n = min(workers, x.shape[0])
+    payloads = [(layer_params, x[i:i + 1, :seq], E[i:i + 1, :seq], h[i:i + 1, :seq]) for i in range(n)]
+    with ctx.Pool(n) as pool:
+        t0 = time.perf_counter()
+        secs = pool.map(_oracle_one, payloads)
+        wall = time.perf_counter() - t0
+    tok = n * seq
+    return {'value': tok / wall, 'unit': UNIT, 'cores': n, 'kind': 'port',
+            'sample': '%d sequence(s) x %d tokens of the same workload, one per host process (numpy oracle port of '
+                      'the reference CPU path, bf16 autocast emulated); wall %.1f s, per-sequence %.1f s'
+                      % (n, seq, wall, statistics.median(secs))}
+
+
+# ---------------------------------------------------------------------------------------------------------------------
+# main
+# ---------------------------------------------------------------------------------------------------------------------
+
+def dist_env():
+    rank = int(os.environ.get('RANK', 0))
+    world = int(os.environ.get('WORLD_SIZE', 1))
+    local = int(os.environ.get('LOCAL_RANK', 0))
+    return rank, world, local
+
+
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return 0
+    import numpy as np
+    import torch
+    layer = make_layer_params()
+    params = {k: v.detach().numpy() for k, v in layer.state_dict().items()}
+    seq = min(args.seq, 2048)
+    x, E, h, _ = make_inputs(max(1, min(16, os.cpu_count() or 1)), seq, 0)
+    vals = []
+    for _ in range(args.warmup if args.warmup < 1 else 1):
+        pass
+    info = None
+    for _ in range(max(1, args.steps)):
+        info = cpu_baseline(params, x, E, h, seq)
+        vals.append(info['value'])
+    v = statistics.median(vals)
+    info['value'] = v
+    out = {'metric': METRIC, 'value': v, 'unit': UNIT, 'n_gpus': world, 'steps': args.steps, 'warmup': args.warmup,
+           'ms_per_step': None, 'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'bf16',
+           'data': 'synthetic', 'impl': 'reference', 'config': config(args, world), 'cpu_baseline': info,
+           'e2e': {'value': v, 'unit': UNIT, 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}}
+    print(json.dumps(out), flush=True)
+    return 0
+
+
+def load_profile_traffic():
+    """Per-launch DRAM bytes of the scoring kernel from the committed ncu summary (profiles/), or None."""
+    p = os.path.join(HERE, 'profiles', 'traffic.json')
+    try:
+        with open(p) as f:
+            t = json.load(f)
+        return t.get('score_bytes_per_token')
+    except (OSError, ValueError):
+        return None
+
+
+def run_ours(args):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    rank, world, local = dist_env()
+    if world > 1:
+        import datetime
+        dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=120))
+    torch.cuda.set_device(local)
+    dev = torch.device('cuda', local)
+    import asrn_b200
+    from asrn_b200 import stages
+
+    layer = make_layer_params().to(dev).eval()
+    x_np, E_np, h_np, _table = make_inputs(args.batch, args.seq, rank)
+    cpu_info = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        params = {k: v.detach().cpu().numpy() for k, v in layer.state_dict().items()}
+        cpu_info = cpu_baseline(params, x_np, E_np, h_np, min(args.seq, 2048))
+    x = torch.from_numpy(x_np).to(dev)
+    E = torch.from_numpy(E_np).to(dev)
+    h = torch.from_numpy(h_np).to(dev)
+    tokens = args.batch * args.seq
+
+    def step():
+        with torch.no_grad(), torch.autocast('cuda', dtype=torch.bfloat16):
+            return layer(E, h, x)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(args.steps):
+        y = step()
+    t1.record()
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1)
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    # launches of our kernels per forward: context, clock, hash, bucket sort (1, or 3 when rows span tiles),
+    # scoring, n-gram rows, streak, gate
+    launches_per_step = 7 + (1 if args.seq <= 8192 else 3)
+
+    # dominant kernel (candidate scoring), timed on its launching stream with the forward's own intermediates
+    with torch.no_grad():
+        ctx = stages.context(layer, h, x, half=True)
+        Bt = stages.clock(ctx['beta'])
+        hs = stages.hash(layer, E, half=True)
+        orden, ids_o = stages.bucket_sort(hs['ids_rows'], layer.n_bits)
+        call = lambda: stages.score(layer, orden, ids_o, hs['phi'], ctx['Qc'], ctx['Kc'], ctx['sig'], Bt,
+                                    ctx['log_alfa'], hs['Ea'], half=True)
+        for _ in range(2):
+            call()
+        torch.cuda.synchronize()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        for _ in range(args.steps):
+            call()
+        s1.record()
+        torch.cuda.synchronize()
+        score_ms = s0.elapsed_time(s1) / args.steps
+        del ctx, Bt, hs, orden, ids_o
+
+    # end to end through the public API with pinned host buffers
+    Eh = torch.from_numpy(E_np).pin_memory()
+    hh = torch.from_numpy(h_np).pin_memory()
+    xh = torch.from_numpy(x_np).pin_memory()
+    out_h = torch.empty_like(hh).pin_memory()
+
+    def e2e_step():
+        Ed, hd, xd = Eh.to(dev, non_blocking=True), hh.to(dev, non_blocking=True), xh.to(dev, non_blocking=True)
+        with torch.no_grad(), torch.autocast('cuda', dtype=torch.bfloat16):
+            yd = layer(Ed, hd, xd)
+        out_h.copy_(yd, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_steps = max(2, min(args.steps, 5))
+    e0.record()
+    for _ in range(e_steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / e_steps
+
+    times = torch.tensor([ms, e2e_ms, score_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    ms, e2e_ms, score_ms = times.tolist()
+    if rank == 0:
+        import json as _json
+        peaks = {}
+        try:
+            with open(os.path.join(HERE, 'MEASURED_PEAKS.json')) as f:
+                peaks = _json.load(f)
+        except (OSError, ValueError):
+            pass
+        hbm = peaks.get('hbm_gbs', 6650.0)
+        peak_src = 'measured' if 'hbm_gbs' in peaks else 'fallback'
+        achieved = SCORE_BYTES_PER_TOKEN * tokens / (score_ms * 1e-3) / 1e9
+        traffic_pt = load_profile_traffic()
+        value = world * tokens * args.steps / (ms * 1e-3)
+        out = {'metric': METRIC, 'value': value, 'unit': UNIT, 'n_gpus': world, 'steps': args.steps,
+               'warmup': max(3, args.warmup), 'ms_per_step': ms / args.steps, 'higher_is_better': True,
+               'scaling': 'weak', 'vs_baseline': None, 'dtype': 'bf16', 'data': 'synthetic',
+               'config': config(args, world),
+               'e2e': {'value': world * tokens / (e2e_ms * 1e-3), 'unit': UNIT,
+                       'h2d_bytes_per_step': int(E_np.nbytes + h_np.nbytes + x_np.nbytes),
+                       'd2h_bytes_per_step': int(h_np.nbytes)},
+               'roofline': {'bound': 'hbm', 'kernel': 'k_score (candidate scoring)', 'achieved': achieved,
+                            'peak': hbm, 'peak_source': peak_src, 'unit': 'GB/s', 'frac': achieved / hbm,
+                            'algorithmic_bytes_per_token': SCORE_BYTES_PER_TOKEN,
+                            'traffic': None if traffic_pt is None else traffic_pt * tokens,
+                            'kernel_ms': score_ms,
+                            'layer_frac': LAYER_BYTES_PER_TOKEN * tokens / (ms / args.steps * 1e-3) / 1e9 / hbm},
+               'gpu_launches': launches_per_step * args.steps,
+               'clocks': clk}
+        if cpu_info is not None:
+            out['cpu_baseline'] = cpu_info
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    args = parse()
+    if args.impl == 'reference':
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == '__main__':
+    sys.exit(main())

@@ -1,0 +1,166 @@
+/*
+ * asrn_b200.h -- C ABI of libasrn_b200.so: the ASRN layer forward and its O(1) generation step on B200 (sm_100a).
+ *
+ * Conventions
+ *   - Every entry point takes plain device pointers, sizes and a CUDA stream (passed as void*, a cudaStream_t).
+ *     The caller allocates every buffer; entry points never allocate, free or synchronise, and are stream-ordered.
+ *   - Return value: ASRN_OK (0) or an ASRN_ERR_* status; asrn_status_string() names it. No exception crosses the ABI.
+ *   - "act" buffers hold activations in the layer's compute type: bfloat16 when cfg->half (the reference under
+ *     torch.autocast(dtype=bfloat16)), float32 otherwise.
+ *   - Layouts are row-major: (B, L, d) means index (b * L + t) * d + j. A "row" of a per-table tensor is r = b * T + tau.
+ *
+ * Reference interfaces replaced (KIROKOWA/ASRN, paths inside that project):
+ *   asrn_layer_forward      CapaASRNEstable.forward            asrn/estable.py:407-421
+ *   asrn_context            CapaASRNEstable._contexto          asrn/estable.py:153-194 (+ firmas_de_piezas,
+ *                                                              asrn/nucleo.py:161-164, and _firma, :634-637)
+ *   asrn_clock              Bt = beta.cumsum(1)                asrn/estable.py:418
+ *   asrn_hash               CapaASRN._phi_y_valores + _ids     asrn/nucleo.py:644-664
+ *   asrn_ids_from_phi       CapaASRN._ids                      asrn/nucleo.py:661-664
+ *   asrn_bucket_sort        ids.argsort(dim=-1, stable=True)   asrn/estable.py:220-221
+ *   asrn_candidates         the candidate window + _largo_seguido asrn/estable.py:232-265, asrn/nucleo.py:98-108
+ *   asrn_score              _acumular after the projection     asrn/estable.py:204-300 (the seam the reference
+ *                           (_CasillerosTriton.apply)          fills with asrn/nucleo.py:461-488)
+ *   asrn_repetition         CapaASRNEstable._repeticion        asrn/estable.py:304-321 (+ _claves_vistos,
+ *                                                              _ordenar_claves, escaneo: asrn/nucleo.py:175-257,
+ *                                                              688-701)
+ *   asrn_gate               CapaASRNEstable._combinar          asrn/estable.py:376-403
+ */
+#ifndef ASRN_B200_H
+#define ASRN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  ASRN_OK = 0,
+  ASRN_ERR_ARG = 1,          /* bad shape, null pointer or option out of range */
+  ASRN_ERR_UNSUPPORTED = 2,  /* option combination this build does not implement */
+  ASRN_ERR_WORKSPACE = 3,    /* workspace / prepared buffer too small or misaligned */
+  ASRN_ERR_CUDA = 4,         /* a kernel launch failed (cudaGetLastError) */
+  ASRN_ERR_TIMEOUT = 5       /* a bounded device wait gave up */
+};
+
+/* Layer options (asrn/nucleo.py:585-630) and protections (asrn/estable.py:57-77). */
+typedef struct asrn_layer_config {
+  int64_t B, L, d;           /* batch, length, width */
+  int32_t n_tablas;          /* T, <= 16 */
+  int32_t n_bits;            /* bits per table, <= 16 */
+  int32_t chunk;             /* C: candidates per table and query, <= 32 */
+  int32_t tablas_contexto;   /* context tables (the last ones) */
+  int32_t confirmar;         /* cf, <= 32 */
+  int32_t sufijo;            /* K, <= 8 */
+  int32_t vistos;            /* n-gram orders 1..n, <= 8 */
+  int32_t nodos_racha;       /* streak response nodes */
+  int32_t hidden;            /* max(8, afin_oculto // 2), <= 128 */
+  int32_t half;              /* 1: bfloat16 autocast semantics, 0: float32 */
+  float beta_max;            /* +inf: no cap */
+  float log_alfa_min;        /* -inf: no floor */
+  float mejor_max;           /* +inf: no clamp */
+  float tope_puerta;         /* 0: no gate cap */
+  float kappa_min;           /* 0: no floor */
+  double racha_paso;         /* log1p(racha_max) / (nodos_racha - 1) */
+} asrn_layer_config;
+
+/* The layer's parameters as stored by the reference (state_dict names in comments), float32 device pointers. */
+typedef struct asrn_layer_weights {
+  const float *ln_w, *ln_b;            /* ln_ctx.weight, ln_ctx.bias (d) */
+  const float *cq, *ck;                /* cq.weight, ck.weight (cf, d) */
+  const float *w_reloj, *b_reloj;      /* w_reloj (2, d), b_reloj (2) */
+  const float *pal0_w, *pal0_b;        /* afin_palabra.0.weight (m, d), .bias (m) */
+  const float *pal2_w, *pal2_b;        /* afin_palabra.2.weight ((T - Tc) * nb, m), .bias */
+  const float *ctx0_w, *ctx0_b;        /* afin_contexto.0.weight (m, 2d), .bias (m) */
+  const float *ctx2_w, *ctx2_b;        /* afin_contexto.2.weight (Tc * nb, m), .bias */
+  const float *v_w, *o_w;              /* v.weight, o.weight (d, d) */
+  const float *g_w, *g_b;              /* g.weight (1, d), g.bias (1) */
+  const float *g_conf_w, *g_conf_b;    /* g_conf.weight (1, 4), g_conf.bias (1) */
+  const float *w_vistos, *u_hawkes;    /* (n) */
+  const float *log_kappa;              /* (n) */
+  const float *log_kappa_racha;        /* (1) */
+  const float *w_sufijo;               /* (K + 1) */
+  const float *gamma;                  /* (T) */
+  const float *d_racha;                /* (nodos_racha) */
+  const double *c_vistos;              /* buffer c_vistos (n), float64 */
+  const float *r_firma;                /* buffer r_firma (d): signatures when no token ids are given */
+} asrn_layer_weights;
+
+const char* asrn_status_string(int status);
+int asrn_abi_version(void);
+
+/* ---- whole layer ------------------------------------------------------------------------------------------------ */
+
+/* Derived weights (concatenated / rounded projections, W_o @ W_v, decay rates) for a config, computed on the device.
+ * Recompute after the parameters change. */
+size_t asrn_layer_prepared_bytes(const asrn_layer_config* cfg);
+int asrn_layer_prepare(const asrn_layer_config* cfg, const asrn_layer_weights* w, void* prepared, size_t bytes,
+                       void* stream);
+
+size_t asrn_layer_workspace_bytes(const asrn_layer_config* cfg);
+/* h_out = layer(E, h, tokens). E, h, h_out: (B, L, d) float32. tokens: (B, L) int64 token ids, or NULL to use the
+ * reference's vector signature E . r_firma. h_out may not alias E or h. */
+int asrn_layer_forward(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared,
+                       const float* E, const float* h, const int64_t* tokens, float* h_out, void* workspace,
+                       size_t workspace_bytes, void* stream);
+
+/* ---- stages (each one seam of the reference; the layer forward runs them in this order) -------------------------- */
+
+/* LN(h) -> Qc, Kc (act, (B, L, cf)), beta (float64), log_alfa (float32); glogit = g(h) (float32); sig (float32). */
+int asrn_context(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared, const float* h,
+                 const float* E, const int64_t* tokens, void* Qc, void* Kc, double* beta, float* log_alfa,
+                 float* glogit, float* sig, void* stream);
+
+/* Bt = inclusive prefix sum of beta along L, float64, per batch row. */
+int asrn_clock(int64_t B, int64_t L, const double* beta, double* Bt, void* stream);
+
+/* E -> Ea (act copy of E, (B, L, d); may equal E when !half), phi (act, (B, L, T * nb)) and the bucket ids per
+ * table row, ids_rows (B * T, L) uint16. */
+int asrn_hash(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared, const float* E,
+              void* Ea, void* phi, uint16_t* ids_rows, void* stream);
+
+/* Sign-pack only: phi (B, L, T * nb) float32 -> ids_rows (B * T, L) uint16, bit j = (phi[tau * nb + j] > 0). */
+int asrn_ids_from_phi(int64_t B, int64_t L, int32_t T, int32_t nb, const float* phi, uint16_t* ids_rows,
+                      void* stream);
+
+/* Stable sort of every row of ids_rows by bucket id (ties by position): orden[r][s] = text position of sorted slot
+ * s, ids_o[r][s] = its bucket id. */
+size_t asrn_bucket_sort_workspace_bytes(int64_t rows, int64_t L, int32_t nb);
+int asrn_bucket_sort(int64_t rows, int64_t L, int32_t nb, const uint16_t* ids_rows, int32_t* orden,
+                     uint16_t* ids_o, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Candidate scoring of every (row, sorted slot) against its <= C bucket mates, exact-mask softmax, copy of the next
+ * token's value row: acc (B, L, d) float32 += sum over tables and candidates of att * Ea[k + 1] (acc must be zeroed
+ * by the caller; apply W_v to acc to get the reference's `salida`). Per-table gate signals in text order, (B, L, T):
+ * hay (uint8), mx (float32, -1e9 when no candidate), pk (float32). */
+int asrn_score(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared,
+               const int32_t* orden, const uint16_t* ids_o, const void* phi, const void* Qc, const void* Kc,
+               const float* sig, const double* Bt, const float* log_alfa, const void* Ea, float* acc,
+               uint8_t* sen_hay, float* sen_mx, float* sen_pk, void* stream);
+
+/* Candidate windows as the scoring kernel selects them (for verification): cand (B*T, L, C) int32 = text position
+ * of the j-th most recent bucket mate of sorted slot s (slot s-1-j), -1 if none; suffix (B*T, L, C) uint8 = its
+ * suffix-match length with the query, 0..K (asrn/estable.py:232-236, 251, 262-265; asrn/nucleo.py:98-108). */
+int asrn_candidates(int64_t B, int64_t L, int32_t T, int32_t C, int32_t K, const int32_t* orden,
+                    const uint16_t* ids_o, const float* sig, int32_t* cand, uint8_t* suffix, void* stream);
+
+/* n-gram repetition memory: vistos (B, L, n) uint8, hawkes (B, L, n) float32, racha (B, L) float32.
+ * Optional debug outputs (NULL to skip): keys (B, L, n) float64, orden_ng (B, n, L) int32 (stable argsort of the
+ * keys, NaN last), repetido (B, n, L) uint8. */
+size_t asrn_repetition_workspace_bytes(const asrn_layer_config* cfg);
+int asrn_repetition(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared,
+                    const float* sig, const double* beta, const double* Bt, const float* log_alfa, uint8_t* vistos,
+                    float* hawkes, float* racha, double* keys, int32_t* orden_ng, uint8_t* repetido,
+                    void* workspace, size_t workspace_bytes, void* stream);
+
+/* Gate and output projection: h_out = h + sigmoid(logit) * (W_o W_v)(acc / max(1, tables with candidates)). */
+int asrn_gate(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared, const float* h,
+              const float* glogit, const float* acc, const uint8_t* sen_hay, const float* sen_mx,
+              const float* sen_pk, const uint8_t* vistos, const float* hawkes, const float* racha, float* h_out,
+              void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* ASRN_B200_H */

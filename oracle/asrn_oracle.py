@@ -213,7 +213,7 @@ def candidatos_filas(ids_o_row, C):
     return lo
 
 
-def acumular(lay, E, Qc, Kc, Bt, log_alfa, sig, half, want_detail=False):
+def acumular(lay, E, Qc, Kc, Bt, log_alfa, sig, half, want_detail=False, ids_override=None):
     """asrn/estable.py:204-300 restated per query: each (row, sorted slot) scores its candidates with
       s = <phi_q, phi_k>/sqrt(P) + <Qc_q, Kc_k> cf^-1/2 + w_suf[suffix length] + log_alfa_k + (gamma_tau / C)(B_k - B_q)
     (clock difference in fp64, then fp32), exact-mask softmax (asrn/estable.py:121-138), copies the next token's value
@@ -221,7 +221,7 @@ def acumular(lay, E, Qc, Kc, Bt, log_alfa, sig, half, want_detail=False):
     B, L, d = E.shape
     T, C, K = lay.T, lay.C, lay.K
     phi, V = phi_y_valores(lay, E, half)
-    ids = ids_de(phi, T, lay.nb)
+    ids = ids_de(phi, T, lay.nb) if ids_override is None else np.asarray(ids_override, np.int32)
     orden, ids_o = bucket_sort(ids)
     Pf = anteriores(sig, K)
     tasa = (lay['gamma'].astype(np.float32) / np.float32(C)).astype(np.float32)
@@ -375,12 +375,13 @@ def combinar(lay, acc, h, half):
     return (h + gate * aporte).astype(np.float32)
 
 
-def layer_forward(lay, E, h, tokens, half=False, return_parts=False):
-    """asrn/estable.py:407-421: h' = layer(E, h, tokens)."""
+def layer_forward(lay, E, h, tokens, half=False, return_parts=False, ids_override=None):
+    """asrn/estable.py:407-421: h' = layer(E, h, tokens). ids_override (B, L, T): bucket ids to use instead of the
+    ones of this restatement's own phi (to compare a pipeline conditioned on its own bucket ids)."""
     sig = firmas_de_piezas(tokens)
     Qc, Kc, beta, log_alfa = contexto(lay, h, half)
     Bt = np.cumsum(beta, axis=1)
-    acc = acumular(lay, E, Qc, Kc, Bt, log_alfa, sig, half)
+    acc = acumular(lay, E, Qc, Kc, Bt, log_alfa, sig, half, ids_override=ids_override)
     rep = repeticion(lay, sig, beta, Bt, log_alfa)
     acc.update(rep)
     out = combinar(lay, acc, h, half)
@@ -388,3 +389,97 @@ def layer_forward(lay, E, h, tokens, half=False, return_parts=False):
         acc.update(Qc=Qc, Kc=Kc, beta=beta, log_alfa=log_alfa, Bt=Bt, sig=sig, out=out)
         return acc
     return out
+
+
+# --------------------------------------------------------------------------------------------------------------------
+# Vectorised restatement (the reference's window formulation), for timing the CPU path on realistic sizes
+# --------------------------------------------------------------------------------------------------------------------
+
+def acumular_fast(lay, E, Qc, Kc, Bt, log_alfa, sig, half):
+    """asrn/estable.py:204-272 as the reference computes it on the CPU: every row sorted by bucket, cut into blocks of
+    C with a zero block in front, windows (W, C, 2C) of the previous + current block, batched products, exact-mask
+    softmax, copy of the next token's value, back to text order and summed over the tables."""
+    B, L, d = E.shape
+    T, C, K = lay.T, lay.C, lay.K
+    n_pad = (-L) % C
+    R = (L + n_pad) // C + 1
+    BT = B * T
+    phi, V = phi_y_valores(lay, E, half)
+    ids = ids_de(phi, T, lay.nb)
+    rows = ids.transpose(0, 2, 1).reshape(BT, L)
+    orden = np.argsort(rows, axis=-1, kind='stable')
+    nulo = B * L
+    fuente = np.full((BT, R * C), nulo, np.int64)
+    fuente[:, C:C + L] = orden + np.repeat(np.arange(0, nulo, L), T)[:, None]
+    real = fuente != nulo
+    ids_o = np.full((BT, R * C), -1, np.int64)
+    ids_o[:, C:C + L] = np.take_along_axis(rows, orden, -1)
+
+    def ordenar(x):
+        k = x.shape[-1]
+        return np.concatenate([x.reshape(nulo, k), np.zeros((1, k), x.dtype)])[fuente.reshape(-1)].reshape(BT, -1, k)
+
+    def preguntas(x):
+        return x.reshape(BT * R, C, *x.shape[2:])[1:]
+
+    def llaves(x):
+        flat = x.reshape(BT * R * C, *x.shape[2:])
+        w = np.lib.stride_tricks.sliding_window_view(flat, 2 * C, axis=0)[::C]
+        return np.moveaxis(w, -1, 1)
+
+    phi_o, V_o = ordenar(phi), ordenar(V)
+    Qc_o, Kc_o, Pf_o = ordenar(Qc), ordenar(Kc), ordenar(anteriores(sig, K))
+    s1 = np.matmul(preguntas(phi_o), llaves(phi_o).transpose(0, 2, 1))
+    s2 = np.matmul(preguntas(Qc_o), llaves(Kc_o).transpose(0, 2, 1))
+    if half:
+        sc = bf16(bf16(bf16(s1) / np.float32(lay.temperatura)) + bf16(bf16(s2) * np.float32(lay.cf ** -0.5)))
+    else:
+        sc = (s1 / np.float32(lay.temperatura) + s2 * np.float32(lay.cf ** -0.5)).astype(np.float32)
+    ln = largo_seguido(preguntas(Pf_o)[:, :, None, :], llaves(Pf_o)[:, None, :, :])
+    sc = (sc + lay['w_sufijo'].astype(np.float32)[ln]).astype(np.float32)
+    tasa = np.tile(lay['gamma'].astype(np.float32) / np.float32(C), B)
+    B_o = ordenar(Bt[..., None])[..., 0]
+    la_o = ordenar(log_alfa[..., None])[..., 0]
+    tasa_w = preguntas(np.broadcast_to(tasa[:, None], (BT, R * C)).copy())[:, 0]
+    dt = (llaves(B_o)[:, None, :] - preguntas(B_o)[:, :, None]).astype(np.float32)
+    sc = (sc + llaves(la_o)[:, None, :]).astype(np.float32)
+    sc = (sc + dt * tasa_w[:, None, None]).astype(np.float32)
+    i = np.arange(C)[:, None]
+    j = np.arange(2 * C)
+    ant = (j >= i) & (j < C + i)
+    valido = (preguntas(ids_o)[:, :, None] == llaves(ids_o)[:, None, :]) & llaves(real)[:, None, :] & ant
+    hay = valido.any(-1, keepdims=True)
+    mx = np.where(valido, sc, -np.inf).max(-1, keepdims=True)
+    ref = np.where(hay, mx, 0).astype(np.float32)
+    with np.errstate(invalid='ignore', over='ignore'):
+        e = np.where(valido, np.exp((sc - ref).astype(np.float32)), 0).astype(np.float32)
+    att = (e / np.where(hay, e.sum(-1, keepdims=True, dtype=np.float32), 1)).astype(np.float32)
+    Vk = llaves(V_o)
+    if half:
+        out = bf16(np.matmul(bf16(att), Vk))
+    else:
+        out = np.matmul(att, Vk).astype(np.float32)
+    en_orden = np.empty_like(orden)
+    np.put_along_axis(en_orden, orden, np.arange(L)[None, :].repeat(BT, 0), 1)
+    fila = (en_orden + np.arange(0, BT * R * C, R * C)[:, None]).reshape(-1)
+    salida = out.reshape(-1, d)[fila].reshape(B, T, L, d).sum(1, dtype=np.float32)
+    if half:
+        salida = bf16(salida)
+    mxs = np.where(hay, mx, PROHIBIDO).astype(np.float32)
+    pk = att.max(-1, keepdims=True)
+    sen = np.concatenate([hay.astype(np.float32), mxs, pk], -1).reshape(-1, 3)[fila].reshape(B, T, L, 3)
+    hay_t = sen[..., 0:1]
+    mejor = np.maximum(np.where(hay_t > 0, sen[..., 1:2], PROHIBIDO).max(1), PROHIBIDO).astype(np.float32)
+    return {'salida': salida, 'peso_total': hay_t.sum(1), 'mejor': mejor, 'pico': (sen[..., 2:3] * hay_t).sum(1),
+            'peso_ctx': hay_t[:, T - lay.Tc:].sum(1), 'senal': sen, 'phi': phi, 'ids': ids,
+            'orden': orden.astype(np.int32)}
+
+
+def layer_forward_fast(lay, E, h, tokens, half=False):
+    """layer_forward with the vectorised scoring (same results up to fp32 summation order)."""
+    sig = firmas_de_piezas(tokens)
+    Qc, Kc, beta, log_alfa = contexto(lay, h, half)
+    Bt = np.cumsum(beta, axis=1)
+    acc = acumular_fast(lay, E, Qc, Kc, Bt, log_alfa, sig, half)
+    acc.update(repeticion(lay, sig, beta, Bt, log_alfa))
+    return combinar(lay, acc, h, half)

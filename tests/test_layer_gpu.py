@@ -1,0 +1,289 @@
+"""GPU parity of the CUDA path (libasrn_b200.so through the C ABI) against the reference's own outputs
+(tests/golden/*.npz) and the CPU oracle (oracle/asrn_oracle.py).
+
+Bars: bucket ids from the reference's phi, sort permutations, candidate indices and
+suffix-match lengths bit-exact; fp32 outputs within 1e-4 max-norm relative error; bf16 outputs within 2e-2.
+End-to-end bucket ids from our own phi may differ from the reference only where |phi_ref| is within rounding of 0.
+"""
+import numpy as np
+import pytest
+import torch
+
+from conftest import LAYER_FIXTURES, layer_options, load_fixture, rel_err
+from oracle import asrn_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+TOL_F32 = 1e-4
+TOL_BF16 = 2e-2
+
+
+def _layer(params, meta, dev):
+    import asrn_b200
+    layer = asrn_b200.ASRNLayer(meta['d'], **layer_options(meta))
+    layer.load_state_dict({k: torch.from_numpy(np.asarray(v)) for k, v in params.items()})
+    return layer.to(dev).eval()
+
+
+def _t(x, dev, dtype=None):
+    t = torch.from_numpy(np.ascontiguousarray(x)).to(dev)
+    return t if dtype is None else t.to(dtype)
+
+
+def _ids_rows(ids_btl, dev):
+    B, L, T = ids_btl.shape
+    return _t(ids_btl.transpose(0, 2, 1).reshape(B * T, L).astype(np.int16), dev)
+
+
+@pytest.mark.parametrize('name', LAYER_FIXTURES)
+def test_signpack_of_reference_phi_is_bit_exact(name, cuda):
+    from asrn_b200 import stages
+    z, params, meta = load_fixture(name)
+    B, L = z['tokens'].shape
+    T, nb = z['ids'].shape[-1], layer_options(meta).get('n_bits', 14)
+    rows = stages.ids_from_phi(_t(z['phi'], cuda), T, nb)
+    got = stages.ids_rows_to_btl(rows, B, T).cpu().numpy()
+    assert np.array_equal(got, z['ids'])
+
+
+@pytest.mark.parametrize('name', LAYER_FIXTURES)
+def test_bucket_sort_of_reference_ids_is_bit_exact(name, cuda):
+    from asrn_b200 import stages
+    z, params, meta = load_fixture(name)
+    nb = layer_options(meta).get('n_bits', 14)
+    orden, ids_o = stages.bucket_sort(_ids_rows(z['ids'], cuda), nb)
+    assert np.array_equal(orden.cpu().numpy(), z['orden'])
+    B, L, T = z['ids'].shape
+    rows = z['ids'].transpose(0, 2, 1).reshape(B * T, L)
+    assert np.array_equal(ids_o.cpu().numpy().astype(np.int32) & 0xFFFF, np.take_along_axis(rows, z['orden'], -1))
+
+
+@pytest.mark.parametrize('L,nb,rows', [(20000, 14, 3), (8193, 4, 2), (30000, 2, 2), (65536, 16, 1), (8192, 14, 2),
+                                       (1, 14, 1), (37, 3, 4)])
+def test_bucket_sort_long_rows_match_stable_argsort(L, nb, rows, cuda):
+    """Rows longer than one tile (the per-tile histogram merge), many ties, and tiny rows."""
+    from asrn_b200 import stages
+    g = np.random.default_rng(L + nb)
+    ids = g.integers(0, 1 << nb, (rows, L)).astype(np.int64)
+    ids[:, L // 3:L // 2] = ids[:, :L // 2 - L // 3]                       # repeated runs
+    orden, ids_o = stages.bucket_sort(_t(ids.astype(np.uint16).view(np.int16), cuda), nb)
+    ref = np.argsort(ids, axis=-1, kind='stable')
+    assert np.array_equal(orden.cpu().numpy(), ref)
+    assert np.array_equal(ids_o.cpu().numpy().view(np.uint16).astype(np.int64), np.take_along_axis(ids, ref, -1))
+
+
+@pytest.mark.parametrize('name', LAYER_FIXTURES)
+def test_candidates_and_suffix_lengths_are_bit_exact(name, cuda):
+    """Candidate indices (the <= C most recent bucket mates) and suffix-match lengths vs the window definition."""
+    from asrn_b200 import stages
+    z, params, meta = load_fixture(name)
+    opts = layer_options(meta)
+    C, K = opts.get('chunk', 32), opts.get('sufijo', 4)
+    B, L, T = z['ids'].shape
+    rows = z['ids'].transpose(0, 2, 1).reshape(B * T, L)
+    ids_o = np.take_along_axis(rows, z['orden'], -1)
+    cand, suf = stages.candidates(_t(z['orden'], cuda), _t(ids_o.astype(np.int16), cuda), _t(z['sig'], cuda), T, C, K)
+    cand, suf = cand.cpu().numpy(), suf.cpu().numpy()
+    Pf = O.anteriores(z['sig'], K)
+    for r in range(B * T):
+        b = r // T
+        lo = O.candidatos_filas(ids_o[r], C)
+        for s in range(L):
+            ks = z['orden'][r, lo[s]:s][::-1]                                  # most recent first
+            want = np.full(C, -1)
+            want[:ks.size] = ks
+            assert np.array_equal(cand[r, s], want), (r, s)
+            q = z['orden'][r, s]
+            ln = O.largo_seguido(np.broadcast_to(Pf[b, q], (ks.size, K)), Pf[b, ks]) if ks.size else np.zeros(0)
+            assert np.array_equal(suf[r, s, :ks.size], ln), (r, s)
+
+
+@pytest.mark.parametrize('name', LAYER_FIXTURES)
+def test_repetition_memory_matches_reference(name, cuda):
+    """n-gram keys, their stable sort and repeated flags bit-exact; Hawkes intensity and streak within 1e-5."""
+    from asrn_b200 import stages
+    z, params, meta = load_fixture(name)
+    layer = _layer(params, meta, cuda)
+    out = stages.repetition(layer, _t(z['sig'], cuda), _t(z['beta'], cuda), _t(z['Bt'], cuda),
+                            _t(z['log_alfa'], cuda), debug=True)
+    assert np.array_equal(out['keys'].cpu().numpy(), z['claves'], equal_nan=True)
+    assert np.array_equal(out['orden_ng'].cpu().numpy(), z['orden_ng'])
+    assert np.array_equal(out['repetido'].cpu().numpy().astype(bool), z['repetido'])
+    assert np.array_equal(out['vistos'].cpu().numpy().astype(np.float32), z['vistos'])
+    assert rel_err(out['hawkes'].cpu().numpy(), z['hawkes']) <= 1e-5
+    assert rel_err(out['racha'].cpu().numpy(), z['racha']) <= 1e-5
+
+
+@pytest.mark.parametrize('name', LAYER_FIXTURES)
+def test_context_matches_reference(name, cuda):
+    from asrn_b200 import stages
+    z, params, meta = load_fixture(name)
+    half = bool(meta['bf16'])
+    layer = _layer(params, meta, cuda)
+    out = stages.context(layer, _t(z['h'], cuda), _t(z['tokens'], cuda), half=half)
+    tol = TOL_BF16 if half else 1e-5
+    assert rel_err(out['Qc'].float().cpu().numpy(), z['Qc']) <= tol
+    assert rel_err(out['Kc'].float().cpu().numpy(), z['Kc']) <= tol
+    assert rel_err(out['beta'].cpu().numpy(), z['beta']) <= 1e-5
+    assert rel_err(out['log_alfa'].cpu().numpy(), z['log_alfa']) <= 1e-5
+    assert np.array_equal(out['sig'].cpu().numpy(), z['sig'])
+    Bt = stages.clock(out['beta'])
+    assert rel_err(Bt.cpu().numpy(), z['Bt']) <= 1e-6
+
+
+def _check_ids_agree(ids_got, ids_ref, phi_ref, nb):
+    """Our end-to-end bucket ids differ from the reference only on bits whose phi is within rounding of zero."""
+    if np.array_equal(ids_got, ids_ref):
+        return 1.0
+    B, L, T = ids_ref.shape
+    diff = ids_got ^ ids_ref
+    bits = (diff[..., None] >> np.arange(nb)) & 1                           # (B, L, T, nb)
+    ph = np.abs(phi_ref.reshape(B, L, T, nb))
+    scale = np.abs(phi_ref).max()
+    assert (ph[bits.astype(bool)] <= 2e-2 * scale).all(), 'a bucket bit flipped on a phi far from zero'
+    return float((ids_got == ids_ref).mean())
+
+
+@pytest.mark.parametrize('name', LAYER_FIXTURES)
+def test_hash_projection_matches_reference(name, cuda):
+    from asrn_b200 import stages
+    z, params, meta = load_fixture(name)
+    half = bool(meta['bf16'])
+    layer = _layer(params, meta, cuda)
+    out = stages.hash(layer, _t(z['E'], cuda), half=half)
+    assert rel_err(out['phi'].float().cpu().numpy(), z['phi']) <= (TOL_BF16 if half else 1e-5)
+    B, L, T = z['ids'].shape
+    ids = stages.ids_rows_to_btl(out['ids_rows'], B, T).cpu().numpy()
+    agree = _check_ids_agree(ids, z['ids'], z['phi'], layer.n_bits)
+    assert agree >= 0.99
+    if half:
+        assert np.array_equal(out['Ea'].float().cpu().numpy(), O.bf16(z['E']))
+
+
+@pytest.mark.parametrize('name', LAYER_FIXTURES)
+def test_scoring_of_reference_intermediates_matches_reference(name, cuda):
+    """_acumular fed with the reference's own phi / Qc / Kc / clock / sort: signals and the copied output."""
+    from asrn_b200 import stages
+    z, params, meta = load_fixture(name)
+    half = bool(meta['bf16'])
+    layer = _layer(params, meta, cuda)
+    B, L, T = z['ids'].shape
+    rows = z['ids'].transpose(0, 2, 1).reshape(B * T, L)
+    ids_o = np.take_along_axis(rows, z['orden'], -1).astype(np.int16)
+    Ea = O.bf16(z['E']) if half else z['E']
+    out = stages.score(layer, _t(z['orden'], cuda), _t(ids_o, cuda), _t(z['phi'], cuda), _t(z['Qc'], cuda),
+                       _t(z['Kc'], cuda), _t(z['sig'], cuda), _t(z['Bt'], cuda), _t(z['log_alfa'], cuda),
+                       _t(Ea, cuda), half=half)
+    senal = z['senal'].transpose(0, 2, 1, 3)                                     # (B, L, T, 3)
+    assert np.array_equal(out['hay'].cpu().numpy(), senal[..., 0].astype(np.uint8))
+    hay = senal[..., 0] > 0
+    assert rel_err(out['mx'].cpu().numpy()[hay], senal[..., 1][hay]) <= (1e-3 if half else 1e-5)
+    assert np.all(out['mx'].cpu().numpy()[~hay] == -1e9)
+    assert rel_err(out['pk'].cpu().numpy(), senal[..., 2]) <= (1e-3 if half else 1e-5)
+    Wv = torch.from_numpy(params['v.weight']).to(cuda).double()
+    salida = (out['acc'].double() @ Wv.T).cpu().numpy()
+    assert rel_err(salida, z['salida']) <= (TOL_BF16 if half else TOL_F32)
+
+
+@pytest.mark.parametrize('name', LAYER_FIXTURES)
+def test_layer_forward_matches_reference(name, cuda):
+    """End to end through ASRNLayer.forward (the drop-in API): h' and h' - h against the reference."""
+    import asrn_b200
+    from asrn_b200 import stages
+    z, params, meta = load_fixture(name)
+    half = bool(meta['bf16'])
+    layer = _layer(params, meta, cuda)
+    E, h, x = _t(z['E'], cuda), _t(z['h'], cuda), _t(z['tokens'], cuda)
+    with torch.no_grad(), torch.autocast('cuda', dtype=torch.bfloat16, enabled=half):
+        y = layer(E, h, x)
+    assert y.dtype == torch.float32 and y.shape == h.shape
+    y = y.cpu().numpy()
+    B, L, T = z['ids'].shape
+    ids = stages.ids_rows_to_btl(stages.hash(layer, E, half=half)['ids_rows'], B, T).cpu().numpy()
+    _check_ids_agree(ids, z['ids'], z['phi'], layer.n_bits)
+    if np.array_equal(ids, z['ids']):
+        ref = z['out']
+    else:                                                  # compare with the oracle conditioned on our bucket ids
+        lay = O.Layer(params, meta['d'], **layer_options(meta))
+        ref = O.layer_forward(lay, z['E'], z['h'], z['tokens'], half=half, ids_override=ids)
+    tol = TOL_BF16 if half else TOL_F32
+    assert rel_err(y, ref) <= tol
+    assert rel_err(y - z['h'], ref - z['h']) <= tol
+
+
+@pytest.mark.parametrize('d,B,L,half,opts', [
+    (256, 2, 1024, False, {}),
+    (768, 1, 640, True, {}),
+    (64, 3, 700, False, dict(chunk=8, n_bits=5, confirmar=20, sufijo=6, vistos=3)),
+    (48, 2, 333, True, dict(chunk=16, n_bits=4)),
+])
+def test_layer_forward_matches_oracle_on_seeded_inputs(d, B, L, half, opts, cuda):
+    """Seeded Zipf + planted-repeat inputs (the benchmark distribution), moved parameters, vs the CPU oracle."""
+    import asrn_b200
+    from asrn_b200 import stages, synthetic
+    torch.manual_seed(0)
+    layer = asrn_b200.ASRNLayer(d, **opts)
+    g = torch.Generator().manual_seed(1)
+    with torch.no_grad():
+        for n, p in layer.named_parameters():
+            if n in ('w_reloj', 'b_reloj', 'gamma', 'log_kappa', 'log_kappa_racha', 'u_hawkes', 'd_racha', 'cq.weight',
+                     'w_sufijo', 'w_vistos', 'g_conf.weight', 'g_conf.bias'):
+                p.add_(torch.randn(p.shape, generator=g) * 0.5)
+        layer.gamma.copy_(torch.linspace(0.5, 3.0, layer.n_tablas))
+    V = 512
+    x = synthetic.zipf_tokens(B, L, V, 1.1, seed=3)
+    x = synthetic.plant_repeats(x, 0.25, 8, 64, seed=4)
+    table = np.random.default_rng(5).standard_normal((V, d)).astype(np.float32)
+    E = table[x]
+    h = np.random.default_rng(6).standard_normal((B, L, d)).astype(np.float32)
+    layer = layer.to(cuda).eval()
+    with torch.no_grad(), torch.autocast('cuda', dtype=torch.bfloat16, enabled=half):
+        y = layer(_t(E, cuda), _t(h, cuda), _t(x, cuda)).cpu().numpy()
+    ids = stages.ids_rows_to_btl(stages.hash(layer, _t(E, cuda), half=half)['ids_rows'], B, layer.n_tablas)
+    ids = ids.cpu().numpy()
+    params = {k: v.detach().cpu().numpy() for k, v in layer.state_dict().items()}
+    lay = O.Layer(params, d, **opts)
+    parts = O.layer_forward(lay, E, h, x, half=half, return_parts=True, ids_override=ids)
+    ids_oracle = O.ids_de(O.phi_y_valores(lay, E, half)[0], layer.n_tablas, layer.n_bits)
+    _check_ids_agree(ids, ids_oracle, O.phi_y_valores(lay, E, half)[0], layer.n_bits)
+    tol = TOL_BF16 if half else TOL_F32
+    assert rel_err(y, parts['out']) <= tol
+    assert rel_err(y - h, parts['out'] - h) <= tol
+
+
+def test_causality_future_does_not_change_past(cuda):
+    """Changing tokens after t0 leaves h' before t0 unchanged (tests/test_nucleo.py:1201-1217)."""
+    import asrn_b200
+    torch.manual_seed(0)
+    layer = asrn_b200.ASRNLayer(64).to(cuda).eval()
+    with torch.no_grad():
+        layer.gamma.copy_(torch.linspace(0.5, 3.0, 8))
+        layer.w_sufijo.normal_(std=0.5)
+    B, L, t0 = 2, 600, 300
+    g = torch.Generator().manual_seed(2)
+    x = torch.randint(0, 20, (B, L), generator=g)
+    table = torch.randn(20, 64, generator=g)
+    h = torch.randn(B, L, 64, generator=g)
+    x2 = x.clone()
+    x2[:, t0:] = torch.randint(0, 20, (B, L - t0), generator=g)
+    h2 = h.clone()
+    h2[:, t0:] = torch.randn(B, L - t0, 64, generator=g)
+    with torch.no_grad():
+        y1 = layer(table[x].to(cuda), h.to(cuda), x.to(cuda))
+        y2 = layer(table[x2].to(cuda), h2.to(cuda), x2.to(cuda))
+    d = (y1[:, :t0] - y2[:, :t0]).abs().max().item()
+    assert d <= 1e-5 * y1[:, :t0].abs().max().item()
+
+
+def test_signatures_from_vectors_when_no_token_ids(cuda):
+    """piezas=None: the signature is E . r_firma (asrn/nucleo.py:634-637)."""
+    from asrn_b200 import stages
+    z, params, meta = load_fixture('layer_f32')
+    layer = _layer(params, meta, cuda)
+    E = _t(z['E'], cuda)
+    out = stages.context(layer, _t(z['h'], cuda), None, E=E)
+    want = z['E'] @ params['r_firma']
+    assert rel_err(out['sig'].cpu().numpy(), want) <= 1e-5
+    with torch.no_grad():
+        y = layer(E, _t(z['h'], cuda), None)
+    assert torch.isfinite(y).all()
