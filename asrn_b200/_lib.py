@@ -52,6 +52,7 @@ _SIGS = {
     'asrn_abi_version': (ctypes.c_int, []),
     'asrn_layer_prepared_bytes': (ctypes.c_size_t, [_P]),
     'asrn_layer_prepare': (ctypes.c_int, [_P, _P, _P, ctypes.c_size_t, _P]),
+    'asrn_layer_status': (ctypes.c_int, [_P, _P, ctypes.c_int, _P]),
     'asrn_layer_workspace_bytes': (ctypes.c_size_t, [_P]),
     'asrn_layer_forward': (ctypes.c_int, [_P, _P, _P, _P, _P, _P, _P, _P, ctypes.c_size_t, _P]),
     'asrn_context': (ctypes.c_int, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P]),

@@ -97,6 +97,8 @@ HashArgs hash_args(const asrn_layer_config& c, const char* prep, const float* E,
   a.E = E; a.Ea = Ea;
   a.w1 = prep + pl.w1; a.b1 = reinterpret_cast<const float*>(prep + pl.b1);
   a.w2 = prep + pl.w2; a.b2 = reinterpret_cast<const float*>(prep + pl.b2);
+  a.w2bd = prep + pl.w2bd;
+  a.status = reinterpret_cast<int*>(const_cast<char*>(prep) + pl.status);
   a.phi = phi; a.ids_rows = ids_rows;
   return a;
 }
@@ -132,6 +134,7 @@ GateArgs gate_args(const asrn_layer_config& c, const asrn_layer_weights& w, cons
   a.gconf = reinterpret_cast<const float*>(prep + pl.gconf);
   a.w_vistos = w.w_vistos; a.u_hawkes = w.u_hawkes; a.d_racha = w.d_racha;
   a.u_racha = reinterpret_cast<const float*>(prep + pl.u_racha);
+  a.status = reinterpret_cast<int*>(const_cast<char*>(prep) + pl.status);
   return a;
 }
 
@@ -165,6 +168,20 @@ int asrn_layer_prepare(const asrn_layer_config* cfg, const asrn_layer_weights* w
   if ((st = check_weights(w))) return st;
   if (!prepared || bytes < prepared_layout(*cfg).total) return ASRN_ERR_WORKSPACE;
   return launch_prepare(*cfg, *w, prepared, as_stream(stream));
+}
+
+int asrn_layer_status(const asrn_layer_config* cfg, const void* prepared, int reset, void* stream) {
+  int st = check_config(cfg);
+  if (st) return -st;
+  if (!prepared) return -ASRN_ERR_ARG;
+  const PreparedLayout pl = prepared_layout(*cfg);
+  int* dev = reinterpret_cast<int*>(const_cast<char*>(reinterpret_cast<const char*>(prepared)) + pl.status);
+  int host = 0;
+  cudaStream_t s = as_stream(stream);
+  if (cudaMemcpyAsync(&host, dev, sizeof(int), cudaMemcpyDeviceToHost, s) != cudaSuccess) return -ASRN_ERR_CUDA;
+  if (reset && cudaMemsetAsync(dev, 0, sizeof(int), s) != cudaSuccess) return -ASRN_ERR_CUDA;
+  if (cudaStreamSynchronize(s) != cudaSuccess) return -ASRN_ERR_CUDA;
+  return host;
 }
 
 size_t asrn_layer_workspace_bytes(const asrn_layer_config* cfg) {

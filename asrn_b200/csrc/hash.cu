@@ -7,6 +7,8 @@
 // (E in the compute type) and the gate applies W_o W_v to their weighted sum.
 // The context projection is split as c0(t) = E_t . ctx0[:, :d]^T + E_{t-1} . ctx0[:, d:]^T + b, both halves
 // accumulated in fp32 before the (bf16) rounding, so the rounding chain matches the reference's single product.
+#include <cuda.h>
+
 #include "common.cuh"
 #include "layout.h"
 
@@ -135,9 +137,20 @@ __global__ void k_ids_from_phi(int64_t B, int64_t L, int T, int nb, const float*
   ids_rows[(b * T + tau) * L + t] = (uint16_t)id;
 }
 
+bool hash_tc_supported(const HashArgs& a);
+int launch_hash_tc(const HashArgs& a, const CUtensorMap& w1, const CUtensorMap& w2, cudaStream_t s);
+
 int launch_hash(const HashArgs& a, bool half, cudaStream_t s) {
   const int64_t M = a.B * a.L;
   if (M == 0) return ASRN_OK;
+  if (half && tensor_cores_enabled() && hash_tc_supported(a)) {
+    CUtensorMap w1, w2;
+    const int Np = (a.P + 15) / 16 * 16;
+    if (!make_tmap_bf16(&w1, a.w1, (uint64_t)a.d, (uint64_t)(3 * a.m), (uint64_t)a.d * 2, 64, (uint32_t)(3 * a.m)) ||
+        !make_tmap_bf16(&w2, a.w2bd, (uint64_t)(2 * a.m), (uint64_t)Np, (uint64_t)(2 * a.m) * 2, 64, (uint32_t)Np))
+      return ASRN_ERR_CUDA;
+    return launch_hash_tc(a, w1, w2, s);
+  }
   if (3 * a.m > 384) return ASRN_ERR_UNSUPPORTED;
   const size_t smem = sizeof(float) * ((size_t)kHashKC * (kHashTM + 1) + (size_t)kHashKC * 3 * a.m +
                                        8 * (size_t)(2 * a.m + a.P));

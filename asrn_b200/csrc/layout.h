@@ -22,6 +22,8 @@ struct PreparedLayout {
   size_t tasa;    // (T) f32: gamma / C
   size_t kappa;   // (n + 1) f32: exp(log_kappa) (n), exp(log_kappa_racha), floored by kappa_min
   size_t u_racha; // (nodes) f32: cumsum(d_racha)
+  size_t w2bd;    // (Np, 2m) bf16: block-diagonal [pal2 | 0 ; 0 | ctx2], Np = P rounded up to 16 (tensor-core path)
+  size_t status;  // int: device status word (ASRN_OK or the first error a kernel recorded)
   size_t total;
 };
 
@@ -41,6 +43,8 @@ inline PreparedLayout prepared_layout(const asrn_layer_config& c) {
   p.tasa = o; o = align_up(o + (size_t)c.n_tablas * 4);
   p.kappa = o; o = align_up(o + ((size_t)c.vistos + 1) * 4);
   p.u_racha = o; o = align_up(o + (size_t)c.nodos_racha * 4);
+  p.w2bd = o; o = align_up(o + ((P + 15) / 16 * 16) * 2 * m * 2);
+  p.status = o; o = align_up(o + 4);
   p.total = o;
   return p;
 }
@@ -68,8 +72,10 @@ struct HashArgs {
   const float* b1;         // (2m)
   const void* w2;          // act (P, m)
   const float* b2;         // (P)
+  const void* w2bd;        // bf16 (Np, 2m) block-diagonal second layer (tensor-core path)
   void* phi;               // act (B, L, P)
   uint16_t* ids_rows;      // (B*T, L)
+  int* status;             // device status word
 };
 
 struct ScoreArgs {
@@ -120,6 +126,7 @@ struct GateArgs {
   const float* gconf;      // (5)
   const float *w_vistos, *u_hawkes, *u_racha, *d_racha;
   float* out;
+  int* status;             // device status word
 };
 
 int launch_context(const ContextArgs& a, bool half, cudaStream_t s);
@@ -136,5 +143,10 @@ size_t repetition_workspace(int64_t B, int64_t L, int n);
 int launch_repetition(const RepetitionArgs& a, void* ws, size_t ws_bytes, cudaStream_t s);
 int launch_gate(const GateArgs& a, bool half, cudaStream_t s);
 int launch_prepare(const asrn_layer_config& c, const asrn_layer_weights& w, void* prepared, cudaStream_t s);
+// 2-D bf16 TMA tensor map, 128-byte swizzle: rows of `inner` elements (row stride in bytes), box inner x outer.
+bool make_tmap_bf16(void* map /* CUtensorMap */, const void* base, uint64_t inner, uint64_t outer,
+                    uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer);
+// GEMM implementation choice: false when ASRN_B200_GEMM=simt forces the CUDA-core kernels (for cross-checks).
+bool tensor_cores_enabled();
 
 }  // namespace asrn

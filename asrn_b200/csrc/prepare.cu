@@ -65,6 +65,19 @@ __global__ void k_scalars(asrn_layer_config c, const float* gamma, const float* 
   gconf[4] = c.half ? round_bf16(gconf_b[0]) : gconf_b[0];
 }
 
+// Block-diagonal second hash layer in bf16: row o < Pw holds pal2[o] in K [0, m); row Pw <= o < P holds
+// ctx2[o - Pw] in K [m, 2m); everything else is 0 (products with 0 add exact zeros to the fp32 accumulator).
+__global__ void k_w2bd(const float* __restrict__ pal2, const float* __restrict__ ctx2, int Pw, int P, int Np, int m,
+                       __nv_bfloat16* __restrict__ dst) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= Np * 2 * m) return;
+  const int o = i / (2 * m), k = i % (2 * m);
+  float v = 0.f;
+  if (o < Pw && k < m) v = pal2[o * m + k];
+  else if (o >= Pw && o < P && k >= m) v = ctx2[(o - Pw) * m + (k - m)];
+  dst[i] = __float2bfloat16_rn(v);
+}
+
 template <bool Half>
 static void copy_rows(const float* src, int64_t stride, int64_t col0, int64_t rows, int64_t cols, void* dst,
                       int64_t row0, cudaStream_t s) {
@@ -91,6 +104,10 @@ static void prepare_t(const asrn_layer_config& c, const asrn_layer_weights& w, c
   k_round_vec<<<(unsigned)((m + 255) / 256), 256, 0, s>>>(w.ctx0_b, b1 + m, (int)m, Half);
   k_round_vec<<<(unsigned)((Pw + 255) / 256), 256, 0, s>>>(w.pal2_b, b2, (int)Pw, Half);
   k_round_vec<<<(unsigned)((Pc + 255) / 256), 256, 0, s>>>(w.ctx2_b, b2 + Pw, (int)Pc, Half);
+  const int P = (int)(Pw + Pc), Np = (P + 15) / 16 * 16;
+  k_w2bd<<<(unsigned)((Np * 2 * m + 255) / 256), 256, 0, s>>>(w.pal2_w, w.ctx2_w, (int)Pw, P, Np, (int)m,
+                                                             reinterpret_cast<__nv_bfloat16*>(base + L.w2bd));
+  cudaMemsetAsync(base + L.status, 0, 4, s);
   dim3 g((unsigned)((d + 31) / 32), (unsigned)((d + 31) / 32));
   k_wov<Half><<<g, dim3(32, 32), 0, s>>>(w.o_w, w.v_w, (int)d, base + L.wov);
   k_scalars<<<1, 32, 0, s>>>(c, w.gamma, w.log_kappa, w.log_kappa_racha, w.d_racha, w.g_conf_w, w.g_conf_b,

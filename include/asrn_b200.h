@@ -98,6 +98,11 @@ size_t asrn_layer_prepared_bytes(const asrn_layer_config* cfg);
 int asrn_layer_prepare(const asrn_layer_config* cfg, const asrn_layer_weights* w, void* prepared, size_t bytes,
                        void* stream);
 
+/* The device status word kept in the prepared buffer: ASRN_OK, or the first error a kernel recorded (for example
+ * ASRN_ERR_TIMEOUT from a bounded wait). Synchronises `stream`; reset != 0 clears the word. Returns the status
+ * (>= 0), or -ASRN_ERR_* if it could not be read. */
+int asrn_layer_status(const asrn_layer_config* cfg, const void* prepared, int reset, void* stream);
+
 size_t asrn_layer_workspace_bytes(const asrn_layer_config* cfg);
 /* h_out = layer(E, h, tokens). E, h, h_out: (B, L, d) float32. tokens: (B, L) int64 token ids, or NULL to use the
  * reference's vector signature E . r_firma. h_out may not alias E or h. */

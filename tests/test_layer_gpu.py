@@ -287,3 +287,47 @@ def test_signatures_from_vectors_when_no_token_ids(cuda):
     with torch.no_grad():
         y = layer(E, _t(z['h'], cuda), None)
     assert torch.isfinite(y).all()
+
+
+@pytest.mark.parametrize('d,B,L', [(768, 2, 1000), (64, 3, 300), (256, 1, 4096)])
+def test_tensor_core_gemms_match_cuda_core_kernels(d, B, L, cuda, monkeypatch):
+    """The tcgen05 hash projection and gate GEMM (bf16) against the CUDA-core kernels on the same inputs: bf16 E copy
+    bit-exact, phi within bf16 rounding, bucket ids equal except on bits whose phi is within rounding of 0, h' within
+    the bf16 tolerance, and the device status word clean (no bounded wait timed out)."""
+    import asrn_b200
+    from asrn_b200 import _lib, stages
+    torch.manual_seed(0)
+    layer = asrn_b200.ASRNLayer(d).to(cuda).eval()
+    with torch.no_grad():
+        layer.gamma.copy_(torch.linspace(0.5, 3.0, 8))
+        layer.cq.weight.normal_(std=0.3)
+    g = torch.Generator().manual_seed(4)
+    x = torch.randint(0, 300, (B, L), generator=g)
+    x[:, L // 2:L // 2 + L // 4] = x[:, :L // 4]
+    E = (torch.randn(300, d, generator=g)[x]).to(cuda)
+    h = torch.randn(B, L, d, generator=g).to(cuda)
+    outs = {}
+    for mode in ('tc', 'simt'):
+        if mode == 'simt':
+            monkeypatch.setenv('ASRN_B200_GEMM', 'simt')
+        else:
+            monkeypatch.delenv('ASRN_B200_GEMM', raising=False)
+        hs = stages.hash(layer, E, half=True)
+        with torch.no_grad(), torch.autocast('cuda', dtype=torch.bfloat16):
+            y = layer(E, h, x.to(cuda))
+        outs[mode] = (hs, y)
+    monkeypatch.delenv('ASRN_B200_GEMM', raising=False)
+    (h_tc, y_tc), (h_si, y_si) = outs['tc'], outs['simt']
+    assert torch.equal(h_tc['Ea'], h_si['Ea'])
+    phi_tc, phi_si = h_tc['phi'].float().cpu().numpy(), h_si['phi'].float().cpu().numpy()
+    assert rel_err(phi_tc, phi_si) <= 2e-2
+    ids_tc = stages.ids_rows_to_btl(h_tc['ids_rows'], B, 8).cpu().numpy()
+    ids_si = stages.ids_rows_to_btl(h_si['ids_rows'], B, 8).cpu().numpy()
+    _check_ids_agree(ids_tc, ids_si, phi_si, layer.n_bits)
+    if np.array_equal(ids_tc, ids_si):
+        assert rel_err(y_tc.cpu().numpy(), y_si.cpu().numpy()) <= TOL_BF16
+        assert rel_err((y_tc - h).cpu().numpy(), (y_si - h).cpu().numpy()) <= TOL_BF16
+    w, _keep, prep = layer.prepared(cuda, True)
+    cfg = _lib.make_config(layer, B, L, True)
+    import ctypes
+    assert _lib.lib().asrn_layer_status(ctypes.byref(cfg), _lib.ptr(prep), 0, _lib.stream_ptr(cuda)) == 0
