@@ -85,6 +85,7 @@ ContextArgs context_args(const asrn_layer_config& c, const asrn_layer_weights& w
   a.g_w = w.g_w; a.g_b = w.g_b; a.r_firma = w.r_firma;
   a.wctx = prep + pl.wctx;
   a.beta_max = c.beta_max; a.log_alfa_min = c.log_alfa_min;
+  a.status = reinterpret_cast<int*>(const_cast<char*>(prep) + pl.status);
   return a;
 }
 

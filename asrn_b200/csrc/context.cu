@@ -148,9 +148,13 @@ __global__ void __launch_bounds__(1024) k_clock(const double* __restrict__ beta,
   }
 }
 
+bool context_tc_supported(const ContextArgs& a);
+int launch_context_tc(const ContextArgs& a, int* status, cudaStream_t s);
+
 int launch_context(const ContextArgs& a, bool half, cudaStream_t s) {
   const int64_t M = a.B * a.L;
   if (M == 0) return ASRN_OK;
+  if (half && tensor_cores_enabled() && context_tc_supported(a)) return launch_context_tc(a, a.status, s);
   const int warps = 8;
   dim3 grid((unsigned)((M + warps - 1) / warps));
   if (half)

@@ -61,6 +61,7 @@ struct ContextArgs {
   void *Qc, *Kc;
   double* beta;
   float *log_alfa, *glogit, *sig;
+  int* status;            // device status word
 };
 
 struct HashArgs {

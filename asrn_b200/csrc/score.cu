@@ -267,10 +267,14 @@ static void launch_score_t(const ScoreArgs& a, cudaStream_t s, size_t smem) {
   k_score_simt<Half, Vec><<<grid, 256, smem, s>>>(a);
 }
 
+bool score_tc_supported(const ScoreArgs& a);
+int launch_score_tc(const ScoreArgs& a, cudaStream_t s);
+
 int launch_score(const ScoreArgs& a, bool half, cudaStream_t s) {
   if (a.B == 0 || a.L == 0) return ASRN_OK;
   if (a.C < 1 || a.C > 32 || a.d > 1024 || a.P > kMaxPhi || a.cf > kMaxConfirm || a.K > kMaxSuffix)
     return ASRN_ERR_UNSUPPORTED;
+  if (half && tensor_cores_enabled() && score_tc_supported(a)) return launch_score_tc(a, s);
   const size_t smem = score_smem_bytes(a.P, a.cf, a.K);
   const bool vec = (a.d % 4) == 0;
   if (half) {

@@ -160,17 +160,42 @@ def _oracle_one(payload):
     return time.perf_counter() - t0
 
 
-def cpu_baseline(layer_params, x, E, h, seq, workers=None, budget_s=20.0):
+def host_cores():
+    """Host cores this process may use: the affinity mask, capped by a cgroup CPU quota if one is set."""
+    n = len(os.sched_getaffinity(0)) if hasattr(os, 'sched_getaffinity') else (os.cpu_count() or 1)
+    try:
+        with open('/sys/fs/cgroup/cpu.max') as f:
+            quota, period = f.read().split()
+        if quota != 'max':
+            n = min(n, max(1, int(int(quota) / int(period))))
+    except (OSError, ValueError):
+        pass
+    return max(1, n)
+
+
+def cpu_baseline(layer_params, x, E, h, seq, workers=None):
     """Tokens/s of the oracle port on `workers` host processes (one sequence each, spawn pool)."""
     import multiprocessing as mp
-    workers = workers or max(1, min(os.cpu_count() or 1, x.shape[0], 16))
+    workers = workers or max(1, min(host_cores(), x.shape[0], 32))
     ctx = mp.get_context('spawn')
     n = min(workers, x.shape[0])
     payloads = [(layer_params, x[i:i + 1, :seq], E[i:i + 1, :seq], h[i:i + 1, :seq]) for i in range(n)]
-    with ctx.Pool(n) as pool:
-        t0 = time.perf_counter()
-        secs = pool.map(_oracle_one, payloads)
-        wall = time.perf_counter() - t0
+    # one BLAS thread per worker process: the workers import numpy while unpickling their task, so the limit has to be
+    # in the environment they inherit (16 workers x 16 BLAS threads each oversubscribe the cores 16 times)
+    saved = {k: os.environ.get(k) for k in ('OMP_NUM_THREADS', 'OPENBLAS_NUM_THREADS', 'MKL_NUM_THREADS')}
+    os.environ.update({k: '1' for k in saved})
+    try:
+        with ctx.Pool(n) as pool:
+            pool.map(_oracle_one, payloads[:n])          # warm-up: imports, first-touch of the arrays
+            t0 = time.perf_counter()
+            secs = pool.map(_oracle_one, payloads)
+            wall = time.perf_counter() - t0
+    finally:
+        for k, v in saved.items():
+            if v is None:
+                os.environ.pop(k, None)
+            else:
+                os.environ[k] = v
     tok = n * seq
     return {'value': tok / wall, 'unit': UNIT, 'cores': n, 'kind': 'port',
             'sample': '%d sequence(s) x %d tokens of the same workload, one per host process (numpy oracle port of '
@@ -197,13 +222,11 @@ def run_reference(args):
     import torch
     layer = make_layer_params()
     params = {k: v.detach().numpy() for k, v in layer.state_dict().items()}
-    seq = min(args.seq, 2048)
-    x, E, h, _ = make_inputs(max(1, min(16, os.cpu_count() or 1)), seq, 0)
+    seq = args.seq
+    x, E, h, _ = make_inputs(max(1, min(32, host_cores())), seq, 0)
     vals = []
-    for _ in range(args.warmup if args.warmup < 1 else 1):
-        pass
     info = None
-    for _ in range(max(1, args.steps)):
+    for _ in range(max(1, min(args.steps, 3))):
         info = cpu_baseline(params, x, E, h, seq)
         vals.append(info['value'])
     v = statistics.median(vals)
@@ -245,7 +268,7 @@ def run_ours(args):
     cpu_info = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         params = {k: v.detach().cpu().numpy() for k, v in layer.state_dict().items()}
-        cpu_info = cpu_baseline(params, x_np, E_np, h_np, min(args.seq, 2048))
+        cpu_info = cpu_baseline(params, x_np, E_np, h_np, args.seq)
     x = torch.from_numpy(x_np).to(dev)
     E = torch.from_numpy(E_np).to(dev)
     h = torch.from_numpy(h_np).to(dev)

@@ -33,10 +33,15 @@ PROHIBIDO = -1e9                                      # asrn/nucleo.py:86
 def bf16(x):
     """Round to the nearest bfloat16 (ties to even), returned as float32 (the rounding torch's .to(bfloat16) does)."""
     x = np.ascontiguousarray(x, dtype=np.float32)
-    u = x.view(np.uint32).astype(np.uint64)
-    r = (u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000
-    out = r.astype(np.uint32).view(np.float32)
-    return np.where(np.isnan(x), x, out).astype(np.float32)
+    u = x.view(np.uint32)
+    r = u + np.uint32(0x7FFF)
+    r += (u >> np.uint32(16)) & np.uint32(1)
+    r &= np.uint32(0xFFFF0000)
+    out = r.view(np.float32)
+    nan = np.isnan(x)
+    if nan.any():
+        out = np.where(nan, x, out)
+    return out
 
 
 def _f32(x):
