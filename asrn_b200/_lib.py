@@ -63,6 +63,7 @@ _SIGS = {
     'asrn_bucket_sort': (ctypes.c_int, [ctypes.c_int64, ctypes.c_int64, ctypes.c_int32, _P, _P, _P, _P,
                                         ctypes.c_size_t, _P]),
     'asrn_score': (ctypes.c_int, [_P] * 17),
+    'asrn_bucket_sort_noalloc': (ctypes.c_int, [ctypes.c_int64, ctypes.c_int64, ctypes.c_int32, _P, _P, _P, _P]),
     'asrn_candidates': (ctypes.c_int, [ctypes.c_int64, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                        _P, _P, _P, _P, _P, _P]),
     'asrn_repetition_workspace_bytes': (ctypes.c_size_t, [_P]),

@@ -306,6 +306,12 @@ int asrn_score(const asrn_layer_config* cfg, const asrn_layer_weights* w, const 
   return launch_score(a, cfg->half, as_stream(stream));
 }
 
+int asrn_bucket_sort_noalloc(int64_t rows, int64_t L, int32_t nb, const uint16_t* ids_rows, int32_t* orden,
+                             uint16_t* ids_o, void* stream) {
+  if (rows < 0 || L < 0 || (rows * L > 0 && (!ids_rows || !orden || !ids_o))) return ASRN_ERR_ARG;
+  return launch_bucket_sort_noalloc(rows, L, nb, ids_rows, orden, ids_o, as_stream(stream));
+}
+
 int asrn_candidates(int64_t B, int64_t L, int32_t T, int32_t C, int32_t K, const int32_t* orden,
                     const uint16_t* ids_o, const float* sig, int32_t* cand, uint8_t* suffix, void* stream) {
   if (B < 0 || L < 0 || T < 1 || (B * L > 0 && (!orden || !ids_o || !sig || !cand || !suffix))) return ASRN_ERR_ARG;

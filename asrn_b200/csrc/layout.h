@@ -137,6 +137,8 @@ int launch_ids_from_phi(int64_t B, int64_t L, int T, int nb, const float* phi, u
 size_t bucket_sort_workspace(int64_t rows, int64_t L, int nb);
 int launch_bucket_sort(int64_t rows, int64_t L, int nb, const uint16_t* ids_rows, int32_t* orden, uint16_t* ids_o,
                        void* ws, size_t ws_bytes, cudaStream_t s);
+int launch_bucket_sort_noalloc(int64_t rows, int64_t L, int nb, const uint16_t* ids_rows, int32_t* orden,
+                               uint16_t* ids_o, cudaStream_t s);
 int launch_score(const ScoreArgs& a, bool half, cudaStream_t s);
 int launch_candidates(int64_t B, int64_t L, int T, int C, int K, const int32_t* orden, const uint16_t* ids_o,
                       const float* sig, int32_t* cand, uint8_t* suffix, cudaStream_t s);

@@ -6,6 +6,8 @@
 // A single-tile row is written out directly. Longer rows add a per-tile histogram of the 2^nb buckets, a column
 // scan over tiles plus a scan over buckets (the global slot where each tile's run of a bucket starts), and a
 // scatter of every tile's runs to their slots.
+#include <mutex>
+
 #include "common.cuh"
 #include "layout.h"
 
@@ -184,6 +186,47 @@ int launch_bucket_sort(int64_t rows, int64_t L, int nb, const uint16_t* ids_rows
   cudaFuncSetAttribute(k_bsort_scatter, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   k_bsort_scatter<<<dim3(nt, (unsigned)rows), 1024, smem, s>>>(tmp, hist, L, nt, nb, orden, ids_o);
   return cudaGetLastError() == cudaSuccess ? ASRN_OK : ASRN_ERR_CUDA;
+}
+
+// ---- allocation-free variant -----------------------------------------------------------------------------------
+// For callers that cannot allocate device memory at the time they sort: a plug-in that runs inside a host process
+// whose allocator it does not own, a serving loop that must keep a fixed memory footprint after start-up, or code that
+// runs while other work holds the allocator. The scratch of rows longer than one tile (the tiles' sorted keys and their
+// bucket histograms) lives in a fixed device array of this library instead of a caller-provided workspace.
+// Every GPU that loads the library keeps this array until the process exits. All calls share it and it keeps the last
+// call's contents: the histogram part is cleared on the stream before each use, and calls that overlap on the GPU (two
+// streams, or two host threads) race on it -- order them on one stream.
+constexpr size_t kNoAllocScratchBytes = (size_t)32 << 20;   // 32 MiB
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+// Device address of the scratch array for the current device, looked up once per device (with that device current).
+// In host code the array's name only stands for the symbol; kernels must be given this address.
+static int noalloc_scratch(void** out) {
+  static std::mutex mu;
+  static void* addr[128] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) return ASRN_ERR_CUDA;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) return ASRN_ERR_CUDA;
+    addr[dev] = p;
+  }
+  *out = addr[dev];
+  return ASRN_OK;
+}
+
+int launch_bucket_sort_noalloc(int64_t rows, int64_t L, int nb, const uint16_t* ids_rows, int32_t* orden,
+                               uint16_t* ids_o, cudaStream_t s) {
+  if (rows < 0 || L < 0 || nb < 1 || nb > 16) return ASRN_ERR_ARG;
+  const size_t need = bucket_sort_workspace(rows, L, nb);
+  if (need > kNoAllocScratchBytes) return ASRN_ERR_WORKSPACE;
+  void* ws = nullptr;
+  if (need > 0) {
+    const int st = noalloc_scratch(&ws);
+    if (st != ASRN_OK) return st;
+  }
+  return launch_bucket_sort(rows, L, nb, ids_rows, orden, ids_o, ws, need, s);
 }
 
 }  // namespace asrn

@@ -144,6 +144,17 @@ int asrn_score(const asrn_layer_config* cfg, const asrn_layer_weights* w, const 
                const float* sig, const double* Bt, const float* log_alfa, const void* Ea, float* acc,
                uint8_t* sen_hay, float* sen_mx, float* sen_pk, void* stream);
 
+/* The same bucket sort for callers that cannot allocate device memory when they sort (a plug-in inside a host process
+ * whose allocator it does not own, a serving loop that keeps a fixed memory footprint after start-up): no workspace
+ * argument; rows longer than one tile (8192 positions) use a fixed 32 MiB scratch array inside this library, which
+ * every GPU that loads the library keeps until the process exits. Requests whose scratch would exceed 32 MiB
+ * (rows * L * 4 + rows * ceil(L / 8192) * 2^nb * 4 bytes, each rounded up to 256) return ASRN_ERR_WORKSPACE.
+ * The first call on a device looks up the array's device address (once per device, with that device current): make
+ * it before any stream capture. Calls share the array: calls that overlap on the GPU race, so order them on one stream.
+ * No counterpart in the reference (its sort is torch.argsort, which allocates through PyTorch). */
+int asrn_bucket_sort_noalloc(int64_t rows, int64_t L, int32_t nb, const uint16_t* ids_rows, int32_t* orden,
+                             uint16_t* ids_o, void* stream);
+
 /* Candidate windows as the scoring kernel selects them (for verification): cand (B*T, L, C) int32 = text position
  * of the j-th most recent bucket mate of sorted slot s (slot s-1-j), -1 if none; suffix (B*T, L, C) uint8 = its
  * suffix-match length with the query, 0..K (asrn/estable.py:232-236, 251, 262-265; asrn/nucleo.py:98-108). */
