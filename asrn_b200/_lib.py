@@ -68,7 +68,8 @@ _SIGS = {
                                        _P, _P, _P, _P, _P, _P]),
     'asrn_repetition_workspace_bytes': (ctypes.c_size_t, [_P]),
     'asrn_repetition': (ctypes.c_int, [_P] * 14 + [ctypes.c_size_t, _P]),
-    'asrn_gate': (ctypes.c_int, [_P] * 14),
+    'asrn_gate_workspace_bytes': (ctypes.c_size_t, [_P]),
+    'asrn_gate': (ctypes.c_int, [_P] * 14 + [ctypes.c_size_t, _P]),
 }
 
 

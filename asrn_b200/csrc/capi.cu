@@ -40,7 +40,7 @@ int check_weights(const asrn_layer_weights* w) {
 // Workspace of one layer forward, in order of use.
 struct Workspace {
   size_t sig, qc, kc, beta, bt, la, glogit, ea, phi, ids_rows, orden, ids_o, acc, hay, mx, pk, vistos, hawkes,
-      racha, sort, total;
+      racha, sort, sigma, total;
   size_t sort_bytes;
 };
 
@@ -71,6 +71,7 @@ Workspace workspace_layout(const asrn_layer_config& c) {
   w.racha = take(M * 4);
   w.sort_bytes = bucket_sort_workspace((int64_t)c.B * T, c.L, c.n_bits);
   w.sort = take(w.sort_bytes);
+  w.sigma = take(M * 4);
   w.total = o;
   return w;
 }
@@ -244,6 +245,10 @@ int asrn_layer_forward(const asrn_layer_config* cfg, const asrn_layer_weights* w
   GateArgs ga = gate_args(c, *w, prep);
   ga.h = h; ga.glogit = glogit; ga.acc = acc; ga.sen_hay = hay; ga.sen_mx = mx; ga.sen_pk = pk;
   ga.vistos = vistos; ga.hawkes = hawkes; ga.racha = racha; ga.out = h_out;
+  if (c.half) {   // the bf16 copy of E is dead after scoring: it holds the gate's GEMM operand
+    ga.cbuf = reinterpret_cast<__nv_bfloat16*>(base + ws.ea);
+    ga.sigma = reinterpret_cast<float*>(base + ws.sigma);
+  }
   return launch_gate(ga, c.half, s);
 }
 
@@ -337,10 +342,15 @@ int asrn_repetition(const asrn_layer_config* cfg, const asrn_layer_weights* w, c
   return launch_repetition(a, workspace, workspace_bytes, as_stream(stream));
 }
 
+size_t asrn_gate_workspace_bytes(const asrn_layer_config* cfg) {
+  if (check_config(cfg) != ASRN_OK) return 0;
+  return gate_workspace(cfg->B * cfg->L, (int)cfg->d, cfg->half != 0);
+}
+
 int asrn_gate(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared, const float* h,
               const float* glogit, const float* acc, const uint8_t* sen_hay, const float* sen_mx,
               const float* sen_pk, const uint8_t* vistos, const float* hawkes, const float* racha, float* h_out,
-              void* stream) {
+              void* workspace, size_t workspace_bytes, void* stream) {
   int st = check_config(cfg);
   if (st) return st;
   if ((st = check_weights(w))) return st;
@@ -349,6 +359,13 @@ int asrn_gate(const asrn_layer_config* cfg, const asrn_layer_weights* w, const v
   GateArgs a = gate_args(*cfg, *w, reinterpret_cast<const char*>(prepared));
   a.h = h; a.glogit = glogit; a.acc = acc; a.sen_hay = sen_hay; a.sen_mx = sen_mx; a.sen_pk = sen_pk;
   a.vistos = vistos; a.hawkes = hawkes; a.racha = racha; a.out = h_out;
+  const size_t need = gate_workspace(cfg->B * cfg->L, (int)cfg->d, cfg->half != 0);
+  if (need > 0) {
+    if (!workspace || workspace_bytes < need) return ASRN_ERR_WORKSPACE;
+    a.cbuf = reinterpret_cast<__nv_bfloat16*>(workspace);
+    a.sigma = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) +
+                                       align_up((size_t)cfg->B * cfg->L * cfg->d * 2));
+  }
   return launch_gate(a, cfg->half, as_stream(stream));
 }
 

@@ -118,17 +118,39 @@ __global__ void __launch_bounds__(256) k_gate_simt(GateArgs a) {
 }
 
 // ---- tensor-core version (bf16 autocast mode) -------------------------------------------------------------------
-// Tile: 128 tokens (TMEM lanes) x NT output columns (TMEM columns), K = d in chunks of 64. A = bf16(acc / max(1,pt))
-// built by the threads in the 128-byte-swizzled K-major layout; B = rows [n0, n0 + NT) of W_ov by TMA; the fp32
-// accumulator in TMEM; the epilogue transposes 32 x 32 blocks through shared memory so that h is read and h'
-// written in coalesced rows.
+// k_gate_prep: one warp per token computes the gate sigmoid(logit) (rounded to bf16) and the GEMM operand
+//   c = bf16(acc / max(1, pt)) (asrn/estable.py:387, the autocast rounding of o's input); memory-bound.
+// k_gate_tc: h' = h + bf16(sigma * bf16(c . W_ov^T)). Tile 128 tokens (TMEM lanes) x NT columns (TMEM columns),
+//   K = d in chunks of 64; both operands by TMA (128-byte swizzle), one producer thread and one MMA thread
+//   (tcgen05.commit frees each stage), the fp32 accumulator in TMEM; the epilogue transposes 32 x 32 blocks
+//   through shared memory so that h is read and h' written in coalesced rows.
+__global__ void __launch_bounds__(256) k_gate_prep(GateArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int64_t g = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int64_t M = a.B * a.L;
+  if (g >= M) return;
+  float sg = 0.f, pt = 1.f;
+  if (lane == 0) gate_of_token<true>(a, g, &sg, &pt);
+  sg = __shfl_sync(0xffffffffu, sg, 0);
+  pt = __shfl_sync(0xffffffffu, pt, 0);
+  if (lane == 0) a.sigma[g] = sg;
+  const float4* src = reinterpret_cast<const float4*>(a.acc + g * a.d);
+  uint2* dst = reinterpret_cast<uint2*>(a.cbuf + g * a.d);
+  for (int c = lane; c < a.d / 4; c += 32) {
+    const float4 x = src[c];
+    dst[c] = make_uint2(umma::pack_bf16x2(__fdiv_rn(x.x, pt), __fdiv_rn(x.y, pt)),
+                        umma::pack_bf16x2(__fdiv_rn(x.z, pt), __fdiv_rn(x.w, pt)));
+  }
+}
+
 namespace {
 constexpr int kGTM = 128, kGBK = 64, kGThreads = 256;
 constexpr int kGStageA = kGTM * 128;
 }  // namespace
 
 template <int NT>
-__global__ void __launch_bounds__(kGThreads, 2) k_gate_tc(const __grid_constant__ CUtensorMap tmap_wov, GateArgs a) {
+__global__ void __launch_bounds__(kGThreads, 2)
+k_gate_tc(const __grid_constant__ CUtensorMap tmap_c, const __grid_constant__ CUtensorMap tmap_wov, GateArgs a) {
   using namespace umma;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -137,13 +159,12 @@ __global__ void __launch_bounds__(kGThreads, 2) k_gate_tc(const __grid_constant_
   uint8_t* sA = sm;
   uint8_t* sB = sm + 2 * kGStageA;
   uint8_t* tail = sB + 2 * kStageB;
-  uint64_t* full_b = reinterpret_cast<uint64_t*>(tail);
-  uint64_t* mma_done = full_b + 2;
-  uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(full_b + 4);
+  uint64_t* full = reinterpret_cast<uint64_t*>(tail);          // [2]
+  uint64_t* empty = full + 2;                                   // [2]
+  uint64_t* acc_full = full + 4;
+  uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(full + 5);
   int* abort_s = reinterpret_cast<int*>(tmem_base_s + 1);
-  float* s_sigma = reinterpret_cast<float*>(tmem_base_s + 4);
-  float* s_pt = s_sigma + kGTM;
-  float* tr = reinterpret_cast<float*>(sm);          // epilogue: [8 warps][32][33], reuses the stage buffers
+  float* tr = reinterpret_cast<float*>(sm);                    // epilogue: [8 warps][32][33], reuses the stages
 
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
   const int d = a.d;
@@ -152,81 +173,52 @@ __global__ void __launch_bounds__(kGThreads, 2) k_gate_tc(const __grid_constant_
   const int64_t M = a.B * a.L;
   const int64_t m0 = (int64_t)blockIdx.y * kGTM;
   if (tid == 0) {
-    for (int i = 0; i < 4; ++i) mbar_init(full_b + i, 1);
+    for (int i = 0; i < 5; ++i) mbar_init(full + i, 1);
     *abort_s = 0;
     fence_mbar_init();
+    prefetch_tensormap(&tmap_c);
     prefetch_tensormap(&tmap_wov);
   }
   if (wid == 0) {
     tmem_alloc(tmem_base_s, NT < 32 ? 32 : NT);
     tmem_relinquish();
   }
-  if (tid < kGTM) {
-    float sg = 0.f, pt = 1.f;
-    if (m0 + tid < M) gate_of_token<true>(a, m0 + tid, &sg, &pt);
-    s_sigma[tid] = sg;
-    s_pt[tid] = pt;
-  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_base_s;
+  constexpr uint32_t kTx = (uint32_t)(kGStageA + kStageB);
 
-  const int ar = tid >> 1, ah = tid & 1;
-  const int64_t ag = m0 + ar;
-  const bool arow_ok = ag < M;
-  const float* arow = a.acc + (arow_ok ? ag : 0) * (int64_t)d + ah * 32;
-  const float pt_r = s_pt[ar];
-  float4 pre[8];
-  auto load_chunk = [&](int k) {
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-      pre[i] = arow_ok ? __ldg(reinterpret_cast<const float4*>(arow + k * kGBK) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-  };
-  load_chunk(0);
-  const uint32_t idesc = idesc_bf16(kGTM, NT);
-  bool ok = true;
-  for (int k = 0; k < nk; ++k) {
-    const int s = k & 1;
-    if (k >= 2) ok = mbar_wait(mma_done + s, ((k - 2) >> 1) & 1, a.status) && ok;
-    if (tid == 0 && ok) {
-      mbar_expect_tx(full_b + s, (uint32_t)kStageB);
-      tma_load_2d(sB + s * kStageB, &tmap_wov, k * kGBK, n0, full_b + s);
+  if (tid == 0) {                         // producer
+    for (int k = 0; k < nk; ++k) {
+      const int s = k & 1;
+      if (k >= 2 && !mbar_wait(empty + s, ((k - 2) >> 1) & 1, a.status)) { *abort_s = 1; break; }
+      mbar_expect_tx(full + s, kTx);
+      tma_load_2d(sA + s * kGStageA, &tmap_c, k * kGBK, (int)m0, full + s);
+      tma_load_2d(sB + s * kStageB, &tmap_wov, k * kGBK, n0, full + s);
     }
-    uint8_t* dstA = sA + s * kGStageA;
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      const float4 x0 = pre[2 * c], x1 = pre[2 * c + 1];
-      const uint4 q = make_uint4(pack_bf16x2(__fdiv_rn(x0.x, pt_r), __fdiv_rn(x0.y, pt_r)),
-                                 pack_bf16x2(__fdiv_rn(x0.z, pt_r), __fdiv_rn(x0.w, pt_r)),
-                                 pack_bf16x2(__fdiv_rn(x1.x, pt_r), __fdiv_rn(x1.y, pt_r)),
-                                 pack_bf16x2(__fdiv_rn(x1.z, pt_r), __fdiv_rn(x1.w, pt_r)));
-      *reinterpret_cast<uint4*>(dstA + umma::sw128_offset(ar, ah * 4 + c)) = q;
-    }
-    if (k + 1 < nk) load_chunk(k + 1);
-    fence_proxy_async();
-    tc_fence_before();
-    __syncthreads();
-    if (tid == 0) {
+  } else if (tid == 32) {                 // MMA issuer
+    const uint32_t idesc = idesc_bf16(kGTM, NT);
+    bool ok = true;
+    for (int k = 0; k < nk && ok; ++k) {
+      const int s = k & 1;
+      ok = mbar_wait(full + s, (k >> 1) & 1, a.status);
+      if (!ok) break;
       tc_fence_after();
-      if (ok) ok = mbar_wait(full_b + s, (k >> 1) & 1, a.status);
-      if (ok) {
-        const uint32_t a0 = smem_u32(dstA), b0 = smem_u32(sB + s * kStageB);
+      const uint32_t a0 = smem_u32(sA + s * kGStageA), b0 = smem_u32(sB + s * kStageB);
 #pragma unroll
-        for (int j = 0; j < kGBK / 16; ++j)
-          mma_bf16(tmem, desc_sw128(a0 + j * 32), desc_sw128(b0 + j * 32), idesc, (k > 0 || j > 0) ? 1u : 0u);
-      }
-      mma_commit(mma_done + s);
-      if (!ok) *abort_s = 1;
+      for (int j = 0; j < kGBK / 16; ++j)
+        mma_bf16(tmem, desc_sw128(a0 + j * 32), desc_sw128(b0 + j * 32), idesc, (k > 0 || j > 0) ? 1u : 0u);
+      mma_commit(empty + s);
     }
+    if (!ok) *abort_s = 1;
+    mma_commit(acc_full);
   }
-  ok = mbar_wait(mma_done + ((nk - 1) & 1), ((nk - 1) >> 1) & 1, a.status) && ok;
-  if (nk >= 2) ok = mbar_wait(mma_done + ((nk - 2) & 1), ((nk - 2) >> 1) & 1, a.status) && ok;
+  __syncwarp();
+  const bool ok = mbar_wait(acc_full, 0, a.status);
   tc_fence_after();
   __syncthreads();
-  if (!ok) *abort_s = 1;
-  __syncthreads();
-  if (*abort_s == 0) {
+  if (ok && *abort_s == 0) {
     const int q4 = wid & 3, grp = wid >> 2;
     const uint32_t trow = tmem + ((uint32_t)(q4 * 32) << 16);
     float* T = tr + wid * (32 * 33);
@@ -242,7 +234,7 @@ __global__ void __launch_bounds__(kGThreads, 2) k_gate_tc(const __grid_constant_
         const int64_t g = m0 + row;
         if (g >= M) break;
         const float o = round_bf16(T[rr * 33 + lane]);
-        const float add = round_bf16(__fmul_rn(s_sigma[row], o));
+        const float add = round_bf16(__fmul_rn(a.sigma[g], o));
         a.out[g * d + col] = __fadd_rn(a.h[g * d + col], add);
       }
       __syncwarp();
@@ -260,7 +252,7 @@ template <int NT>
 static size_t gate_tc_smem() {
   const size_t stages = 2 * (size_t)kGStageA + 2 * (size_t)NT * 128;
   const size_t tr = 8 * 32 * 33 * 4;
-  return 1024 + (stages > tr ? stages : tr) + 64 + 2 * kGTM * 4;
+  return 1024 + (stages > tr ? stages : tr) + 64;
 }
 
 int gate_tc_tile(int d) {
@@ -271,22 +263,34 @@ int gate_tc_tile(int d) {
 }
 
 template <int NT>
-static int launch_gate_tc_t(const GateArgs& a, const CUtensorMap& map, cudaStream_t s) {
+static int launch_gate_tc_t(const GateArgs& a, const CUtensorMap& mc, const CUtensorMap& mw, cudaStream_t s) {
   const size_t smem = gate_tc_smem<NT>();
   cudaFuncSetAttribute(k_gate_tc<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   const int64_t M = a.B * a.L;
   dim3 grid((unsigned)(a.d / NT), (unsigned)((M + kGTM - 1) / kGTM));
-  k_gate_tc<NT><<<grid, kGThreads, smem, s>>>(map, a);
+  k_gate_tc<NT><<<grid, kGThreads, smem, s>>>(mc, mw, a);
   return cudaGetLastError() == cudaSuccess ? ASRN_OK : ASRN_ERR_CUDA;
 }
 
-int launch_gate_tc(const GateArgs& a, const CUtensorMap& map, int nt, cudaStream_t s) {
+int launch_gate_tc(const GateArgs& a, int nt, cudaStream_t s) {
+  const int64_t M = a.B * a.L;
+  k_gate_prep<<<(unsigned)((M + 7) / 8), 256, 0, s>>>(a);
+  if (cudaGetLastError() != cudaSuccess) return ASRN_ERR_CUDA;
+  CUtensorMap mc, mw;
+  if (!make_tmap_bf16(&mc, a.cbuf, (uint64_t)a.d, (uint64_t)M, (uint64_t)a.d * 2, 64, 128) ||
+      !make_tmap_bf16(&mw, a.wov, (uint64_t)a.d, (uint64_t)a.d, (uint64_t)a.d * 2, 64, (uint32_t)nt))
+    return ASRN_ERR_CUDA;
   switch (nt) {
-    case 256: return launch_gate_tc_t<256>(a, map, s);
-    case 128: return launch_gate_tc_t<128>(a, map, s);
-    case 64: return launch_gate_tc_t<64>(a, map, s);
+    case 256: return launch_gate_tc_t<256>(a, mc, mw, s);
+    case 128: return launch_gate_tc_t<128>(a, mc, mw, s);
+    case 64: return launch_gate_tc_t<64>(a, mc, mw, s);
     default: return ASRN_ERR_UNSUPPORTED;
   }
+}
+
+size_t gate_workspace(int64_t M, int d, bool half) {
+  if (!half || gate_tc_tile(d) == 0) return 0;
+  return align_up((size_t)M * d * 2) + align_up((size_t)M * 4);
 }
 
 int launch_gate(const GateArgs& a, bool half, cudaStream_t s) {
@@ -294,10 +298,8 @@ int launch_gate(const GateArgs& a, bool half, cudaStream_t s) {
   if (M == 0) return ASRN_OK;
   const int nt = gate_tc_tile(a.d);
   if (half && tensor_cores_enabled() && nt > 0) {
-    CUtensorMap map;
-    if (!make_tmap_bf16(&map, a.wov, (uint64_t)a.d, (uint64_t)a.d, (uint64_t)a.d * 2, 64, (uint32_t)nt))
-      return ASRN_ERR_CUDA;
-    return launch_gate_tc(a, map, nt, s);
+    if (!a.cbuf || !a.sigma) return ASRN_ERR_WORKSPACE;
+    return launch_gate_tc(a, nt, s);
   }
   dim3 grid((unsigned)((a.d + kGateTN - 1) / kGateTN), (unsigned)((M + kGateTM - 1) / kGateTM));
   if (half)

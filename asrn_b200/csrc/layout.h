@@ -1,6 +1,7 @@
 // Kernel argument structs and the byte layout of the prepared-weights and workspace buffers.
 #pragma once
 #include <cuda_runtime.h>
+#include <cuda_bf16.h>
 #include <stddef.h>
 #include <stdint.h>
 
@@ -128,6 +129,8 @@ struct GateArgs {
   const float *w_vistos, *u_hawkes, *u_racha, *d_racha;
   float* out;
   int* status;             // device status word
+  __nv_bfloat16* cbuf;     // tensor-core path: (M, d) bf16 GEMM operand bf16(acc / max(1, pt)) (workspace)
+  float* sigma;            // tensor-core path: (M) gate values (workspace)
 };
 
 int launch_context(const ContextArgs& a, bool half, cudaStream_t s);
@@ -145,6 +148,7 @@ int launch_candidates(int64_t B, int64_t L, int T, int C, int K, const int32_t* 
 size_t repetition_workspace(int64_t B, int64_t L, int n);
 int launch_repetition(const RepetitionArgs& a, void* ws, size_t ws_bytes, cudaStream_t s);
 int launch_gate(const GateArgs& a, bool half, cudaStream_t s);
+size_t gate_workspace(int64_t M, int d, bool half);
 int launch_prepare(const asrn_layer_config& c, const asrn_layer_weights& w, void* prepared, cudaStream_t s);
 // 2-D bf16 TMA tensor map, 128-byte swizzle: rows of `inner` elements (row stride in bytes), box inner x outer.
 bool make_tmap_bf16(void* map /* CUtensorMap */, const void* base, uint64_t inner, uint64_t outer,

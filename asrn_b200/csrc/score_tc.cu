@@ -7,7 +7,8 @@
 //   S = phi_q . phi_k and Qc . Kc (32 x 64 each) on mma.sync (fp32 accumulate), then the reference's rounding chain,
 //   suffix weight, log_alfa_k and the fp64 time difference, the exact-mask softmax per query, and
 //   out (32 x d_part) = att (32 x 64, bf16) . V (64 x d_part) on mma.sync, added into acc with vector reductions.
-// d is split over ceil(d / 384) blocks per span so that a block's value ring stays small enough for two blocks per SM.
+// One block of 16 warps per (row, span of 512 slots); the ring holds 96 slots so the next sub-tile's rows arrive by
+// cp.async while the current one computes. d is split over two blocks only when d > 768.
 #include "common.cuh"
 #include "layout.h"
 
@@ -15,9 +16,10 @@ namespace asrn {
 
 namespace {
 constexpr int kQ = 32;          // queries per sub-tile
-constexpr int kW = 64;          // window slots
+constexpr int kW = 64;          // window slots [q0 - 32, q0 + 32)
+constexpr int kR = 96;          // ring slots: the window plus the next sub-tile's 32 slots (prefetched)
 constexpr int kSpanTc = 512;    // sorted slots per block
-constexpr int kThreadsTc = 256;
+constexpr int kThreadsTc = 512; // 16 warps
 
 struct TcSmem {
   int* pos;
@@ -26,10 +28,10 @@ struct TcSmem {
   double* bt;
   float* la;
   float* pf;
-  __nv_bfloat16* phi;   // [64][Pp]
-  __nv_bfloat16* qc;    // [64][Cp]
-  __nv_bfloat16* kc;    // [64][Cp]
-  __nv_bfloat16* v;     // [64][Dp]
+  __nv_bfloat16* phi;   // [kR][Pp]
+  __nv_bfloat16* qc;    // [kR][Cp]
+  __nv_bfloat16* kc;    // [kR][Cp]
+  __nv_bfloat16* v;     // [kR][Dp]
   float* sc;            // [32][65]
   __nv_bfloat16* att;   // [32][72]
   int* qhay;            // [32]
@@ -41,12 +43,12 @@ __host__ __device__ inline int pad16(int x) { return (x + 15) / 16 * 16; }
 __host__ __device__ inline size_t tc_smem_bytes(int P, int cf, int K, int dpart) {
   const int Pp = pad16(P) + 8, Cp = pad16(cf) + 8, Dp = dpart + 8;
   size_t b = 0;
-  b += kW * 8;                    // bt
-  b += kW * 4 * 3;                // pos, id, used
-  b += kW * 4;                    // la
-  b += kW * 4 * (size_t)K;        // pf
+  b += kR * 8;                    // bt
+  b += kR * 4 * 3;                // pos, id, used
+  b += kR * 4;                    // la
+  b += kR * 4 * (size_t)K;        // pf
   b = (b + 15) / 16 * 16;
-  b += (size_t)kW * Pp * 2 + 2 * (size_t)kW * Cp * 2 + (size_t)kW * Dp * 2;
+  b += (size_t)kR * Pp * 2 + 2 * (size_t)kR * Cp * 2 + (size_t)kR * Dp * 2;
   b += (size_t)kQ * 65 * 4;
   b += (size_t)kQ * 72 * 2;
   b += kQ * 4;
@@ -60,22 +62,24 @@ __device__ inline TcSmem carve_tc(char* base, int P, int cf, int K, int dpart) {
   s.Dp = dpart + 8;
   s.K = K;
   char* p = base;
-  s.bt = reinterpret_cast<double*>(p); p += kW * 8;
-  s.pos = reinterpret_cast<int*>(p); p += kW * 4;
-  s.id = reinterpret_cast<int*>(p); p += kW * 4;
-  s.used = reinterpret_cast<int*>(p); p += kW * 4;
-  s.la = reinterpret_cast<float*>(p); p += kW * 4;
-  s.pf = reinterpret_cast<float*>(p); p += kW * 4 * K;
+  s.bt = reinterpret_cast<double*>(p); p += kR * 8;
+  s.pos = reinterpret_cast<int*>(p); p += kR * 4;
+  s.id = reinterpret_cast<int*>(p); p += kR * 4;
+  s.used = reinterpret_cast<int*>(p); p += kR * 4;
+  s.la = reinterpret_cast<float*>(p); p += kR * 4;
+  s.pf = reinterpret_cast<float*>(p); p += kR * 4 * K;
   p = base + ((p - base) + 15) / 16 * 16;
-  s.phi = reinterpret_cast<__nv_bfloat16*>(p); p += (size_t)kW * s.Pp * 2;
-  s.qc = reinterpret_cast<__nv_bfloat16*>(p); p += (size_t)kW * s.Cp * 2;
-  s.kc = reinterpret_cast<__nv_bfloat16*>(p); p += (size_t)kW * s.Cp * 2;
-  s.v = reinterpret_cast<__nv_bfloat16*>(p); p += (size_t)kW * s.Dp * 2;
+  s.phi = reinterpret_cast<__nv_bfloat16*>(p); p += (size_t)kR * s.Pp * 2;
+  s.qc = reinterpret_cast<__nv_bfloat16*>(p); p += (size_t)kR * s.Cp * 2;
+  s.kc = reinterpret_cast<__nv_bfloat16*>(p); p += (size_t)kR * s.Cp * 2;
+  s.v = reinterpret_cast<__nv_bfloat16*>(p); p += (size_t)kR * s.Dp * 2;
   s.sc = reinterpret_cast<float*>(p); p += kQ * 65 * 4;
   s.att = reinterpret_cast<__nv_bfloat16*>(p); p += kQ * 72 * 2;
   s.qhay = reinterpret_cast<int*>(p);
   return s;
 }
+
+__device__ __forceinline__ int ring(int64_t slot) { return (int)((slot + kR) % kR); }   // slot >= -kR
 
 __device__ __forceinline__ uint32_t su32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -110,20 +114,13 @@ __device__ __forceinline__ void red_add_v2(float* addr, float a, float b) {
 }
 }  // namespace
 
-// Gather slots [s_begin, s_end) of row r into the ring (features by plain and asynchronous copies, value rows by
-// asynchronous copies with zero fill for rows no query uses).
-__device__ __forceinline__ void tc_load_slots(const ScoreArgs& a, const TcSmem& S, int64_t r, int64_t b,
-                                              int64_t s_begin, int64_t s_end, int dp0, int dpart, int Ppad,
-                                              int Cpad) {
-  const __nv_bfloat16* phi = reinterpret_cast<const __nv_bfloat16*>(a.phi);
-  const __nv_bfloat16* Qc = reinterpret_cast<const __nv_bfloat16*>(a.Qc);
-  const __nv_bfloat16* Kc = reinterpret_cast<const __nv_bfloat16*>(a.Kc);
-  const __nv_bfloat16* Ea = reinterpret_cast<const __nv_bfloat16*>(a.Ea);
+// Slot scalars of slots [s_begin, s_end) of row r (one thread per slot) into their ring rows.
+__device__ __forceinline__ void tc_load_scalars(const ScoreArgs& a, const TcSmem& S, int64_t r, int64_t b,
+                                                int64_t s_begin, int64_t s_end) {
   const int n = (int)(s_end - s_begin);
-  // scalars: one thread per slot
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
     const int64_t s = s_begin + i;
-    const int ri = (int)(s & (kW - 1));
+    const int ri = ring(s);
     const bool real = s >= 0 && s < a.L;
     const int pos = real ? a.orden[r * a.L + s] : 0;
     const int id = real ? (int)a.ids_o[r * a.L + s] : -1;
@@ -139,39 +136,48 @@ __device__ __forceinline__ void tc_load_slots(const ScoreArgs& a, const TcSmem& 
       S.pf[ri * a.K + c] = (real && t >= 0) ? a.sig[b * a.L + t] : __int_as_float(0x7fc00000);
     }
   }
-  // vector rows: 16-byte chunks
-  const int cph = Ppad / 8, cpc = Cpad / 8, cpv = dpart / 8;
-  const int per_slot = cph + 2 * cpc + cpv;
-  for (int e = threadIdx.x; e < n * per_slot; e += blockDim.x) {
-    const int i = e / per_slot, c = e % per_slot;
-    const int64_t s = s_begin + i;
-    const int ri = (int)(s & (kW - 1));
-    const bool real = s >= 0 && s < a.L;
-    const int pos = real ? a.orden[r * a.L + s] : 0;
-    const int64_t g = b * a.L + pos;
-    if (c < cph) {
-      const int col = c * 8;
-      const bool ok = real && col < a.P;
-      cp_async16(S.phi + ri * S.Pp + col, phi + g * a.P + (ok ? col : 0), ok);
-    } else if (c < cph + cpc) {
-      const int col = (c - cph) * 8;
-      const bool ok = real && col < a.cf;
-      cp_async16(S.qc + ri * S.Cp + col, Qc + g * a.cf + (ok ? col : 0), ok);
-    } else if (c < cph + 2 * cpc) {
-      const int col = (c - cph - cpc) * 8;
-      const bool ok = real && col < a.cf;
-      cp_async16(S.kc + ri * S.Cp + col, Kc + g * a.cf + (ok ? col : 0), ok);
-    } else {
-      const int col = (c - cph - 2 * cpc) * 8;
-      bool ok = real && s + 1 < a.L && pos + 1 < a.L;
-      if (ok) ok = (int)a.ids_o[r * a.L + s + 1] == (int)a.ids_o[r * a.L + s];
-      cp_async16(S.v + ri * S.Dp + col, Ea + (b * a.L + (ok ? pos + 1 : 0)) * (int64_t)a.d + dp0 + col, ok);
-    }
-  }
-  cp_async_commit();
 }
 
-__global__ void __launch_bounds__(kThreadsTc, 2) k_score_tc(ScoreArgs a, int nds, int dpart) {
+// Vector rows (phi, Qc, Kc and the value row when used) of slots [s_begin, s_end): 16-byte asynchronous copies,
+// zero-filled where a slot is not real or its value row is not needed. Reads the slot scalars from shared memory.
+__device__ __forceinline__ void tc_load_vectors(const ScoreArgs& a, const TcSmem& S, int64_t b, int64_t s_begin,
+                                                int64_t s_end, int dp0, int dpart, int Ppad, int Cpad) {
+  const __nv_bfloat16* phi = reinterpret_cast<const __nv_bfloat16*>(a.phi);
+  const __nv_bfloat16* Qc = reinterpret_cast<const __nv_bfloat16*>(a.Qc);
+  const __nv_bfloat16* Kc = reinterpret_cast<const __nv_bfloat16*>(a.Kc);
+  const __nv_bfloat16* Ea = reinterpret_cast<const __nv_bfloat16*>(a.Ea);
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const int cph = Ppad / 8, cpc = Cpad / 8, cpv = dpart / 8;
+  const int per_slot = cph + 2 * cpc + cpv;
+  for (int64_t s = s_begin + wid; s < s_end; s += nw) {     // one warp per slot, lanes over its 16-byte chunks
+    const int ri = ring(s);
+    const bool real = S.id[ri] >= 0;
+    const int pos = S.pos[ri];
+    const bool used = S.used[ri] != 0;
+    const int64_t g = b * a.L + pos;
+    const __nv_bfloat16* vsrc = Ea + (b * a.L + (used ? pos + 1 : 0)) * (int64_t)a.d + dp0;
+    for (int c = lane; c < per_slot; c += 32) {
+      if (c < cph) {
+        const int col = c * 8;
+        const bool ok = real && col < a.P;
+        cp_async16(S.phi + ri * S.Pp + col, phi + g * a.P + (ok ? col : 0), ok);
+      } else if (c < cph + cpc) {
+        const int col = (c - cph) * 8;
+        const bool ok = real && col < a.cf;
+        cp_async16(S.qc + ri * S.Cp + col, Qc + g * a.cf + (ok ? col : 0), ok);
+      } else if (c < cph + 2 * cpc) {
+        const int col = (c - cph - cpc) * 8;
+        const bool ok = real && col < a.cf;
+        cp_async16(S.kc + ri * S.Cp + col, Kc + g * a.cf + (ok ? col : 0), ok);
+      } else {
+        const int col = (c - cph - 2 * cpc) * 8;
+        cp_async16(S.v + ri * S.Dp + col, vsrc + (used ? col : 0), used);
+      }
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kThreadsTc, 1) k_score_tc(ScoreArgs a, int nds, int dpart) {
   extern __shared__ __align__(16) char smem_raw[];
   const TcSmem S = carve_tc(smem_raw, a.P, a.cf, a.K, dpart);
   const int64_t r = blockIdx.y;
@@ -187,58 +193,66 @@ __global__ void __launch_bounds__(kThreadsTc, 2) k_score_tc(ScoreArgs a, int nds
   const int C = a.C;
   const bool write_signals = part == 0;
 
+  // first window: slots [S0 - 32, S0 + 32)
+  tc_load_scalars(a, S, r, b, S0 - kQ, S0 + kQ);
+  __syncthreads();
+  tc_load_vectors(a, S, b, S0 - kQ, S0 + kQ, dp0, dpart, Ppad, Cpad);
+  cp_async_commit();
+
   for (int64_t q0 = S0; q0 < S1; q0 += kQ) {
-    tc_load_slots(a, S, r, b, q0 == S0 ? q0 - kQ : q0, q0 + kQ, dp0, dpart, Ppad, Cpad);
+    // ring rows: window key j (slot q0 - 32 + j) -> wrow(j); query i (slot q0 + i) -> wrow(32 + i)
+    const int rbase = ring(q0 - kQ);
+    auto wrow = [rbase](int j) { const int x = rbase + j; return x >= kR ? x - kR : x; };
     cp_async_wait_all();
     __syncthreads();
+    // prefetch the next sub-tile's slots into the free third of the ring while this one computes
+    const bool more = q0 + kQ < S1;
+    if (more) {
+      tc_load_scalars(a, S, r, b, q0 + kQ, q0 + 2 * kQ);
+    }
+    __syncthreads();
+    if (more) tc_load_vectors(a, S, b, q0 + kQ, q0 + 2 * kQ, dp0, dpart, Ppad, Cpad);
+    cp_async_commit();
 
-    // ---- scores: warp w -> m-tile (w >> 2), n-tiles 2 (w & 3), 2 (w & 3) + 1 ------------------------------------
+    // ---- scores: warp w -> m-tile (w >> 3), n-tile (w & 7) --------------------------------------------------------
     {
-      const int mt = wid >> 2;
-      const int nt0 = (wid & 3) * 2;
-      float cphi[2][4] = {}, cqk[2][4] = {};
-      // A rows: queries mt*16 + (lane & 15), k offset (lane >> 4) * 8
-      const int qa = mt * 16 + (lane & 15);
-      const int ra = (int)((q0 + qa) & (kW - 1));
-      const int ka = (lane >> 4) * 8;
-      for (int k0 = 0; k0 < Ppad; k0 += 16) {
-        uint32_t a0, a1, a2, a3;
-        ldsm_x4(su32(S.phi + ra * S.Pp + k0 + ka), a0, a1, a2, a3);
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          const int key = (nt0 + j) * 8 + (lane & 7);
-          const int rk = (int)((q0 - kQ + key) & (kW - 1));
-          uint32_t b0, b1;
-          ldsm_x2(su32(S.phi + rk * S.Pp + k0 + ((lane >> 3) & 1) * 8), b0, b1);
-          mma16816(cphi[j], a0, a1, a2, a3, b0, b1);
+      const int mt = wid >> 3;
+      const int nt = wid & 7;
+      float cphi[4] = {0.f, 0.f, 0.f, 0.f}, cqk[4] = {0.f, 0.f, 0.f, 0.f};
+      // band: this tile's keys [8 nt, 8 nt + 8) meet queries [16 mt, 16 mt + 16) only if some key is within C before
+      const int key_lo = nt * 8, q_lo = mt * 16;
+      const bool band = key_lo + 7 >= q_lo + 32 - C && key_lo < q_lo + 16 + 32;
+      if (band) {
+        const int qa = mt * 16 + (lane & 15);
+        const int ra = wrow(kQ + qa);
+        const int ka = (lane >> 4) * 8;
+        const int key = nt * 8 + (lane & 7);
+        const int rk = wrow(key);
+        const int kb = ((lane >> 3) & 1) * 8;
+        for (int k0 = 0; k0 < Ppad; k0 += 16) {
+          uint32_t a0, a1, a2, a3, b0, b1;
+          ldsm_x4(su32(S.phi + ra * S.Pp + k0 + ka), a0, a1, a2, a3);
+          ldsm_x2(su32(S.phi + rk * S.Pp + k0 + kb), b0, b1);
+          mma16816(cphi, a0, a1, a2, a3, b0, b1);
+        }
+        for (int k0 = 0; k0 < Cpad; k0 += 16) {
+          uint32_t a0, a1, a2, a3, b0, b1;
+          ldsm_x4(su32(S.qc + ra * S.Cp + k0 + ka), a0, a1, a2, a3);
+          ldsm_x2(su32(S.kc + rk * S.Cp + k0 + kb), b0, b1);
+          mma16816(cqk, a0, a1, a2, a3, b0, b1);
         }
       }
-      for (int k0 = 0; k0 < Cpad; k0 += 16) {
-        uint32_t a0, a1, a2, a3;
-        ldsm_x4(su32(S.qc + ra * S.Cp + k0 + ka), a0, a1, a2, a3);
 #pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          const int key = (nt0 + j) * 8 + (lane & 7);
-          const int rk = (int)((q0 - kQ + key) & (kW - 1));
-          uint32_t b0, b1;
-          ldsm_x2(su32(S.kc + rk * S.Cp + k0 + ((lane >> 3) & 1) * 8), b0, b1);
-          mma16816(cqk[j], a0, a1, a2, a3, b0, b1);
-        }
-      }
-      // finish each element: rounding chain, suffix, log_alfa_k, time; invalid -> -inf
-#pragma unroll
-      for (int j = 0; j < 2; ++j)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int qi = mt * 16 + (lane >> 2) + (e >> 1) * 8;
-          const int kj = (nt0 + j) * 8 + (lane & 3) * 2 + (e & 1);
-          const int64_t sq = q0 + qi, sk = q0 - kQ + kj;
-          const int rq = (int)(sq & (kW - 1)), rk = (int)(sk & (kW - 1));
-          float val = -INFINITY;
-          const bool valid = sq < a.L && sk >= 0 && sk < sq && sk >= sq - C && S.id[rk] == S.id[rq];
-          if (valid) {
-            const float s1 = round_bf16(__fdiv_rn(round_bf16(cphi[j][e]), a.inv_temp_div));
-            const float s2 = round_bf16(__fmul_rn(round_bf16(cqk[j][e]), a.esc_c));
+      for (int e = 0; e < 4; ++e) {
+        const int qi = mt * 16 + (lane >> 2) + (e >> 1) * 8;
+        const int kj = nt * 8 + (lane & 3) * 2 + (e & 1);
+        const int64_t sq = q0 + qi, sk = q0 - kQ + kj;
+        float val = -INFINITY;
+        if (band && kj < qi + 32 && kj >= qi + 32 - C && sq < a.L && sk >= 0) {
+          const int rq = wrow(kQ + qi), rk = wrow(kj);
+          if (S.id[rk] == S.id[rq]) {
+            const float s1 = round_bf16(__fdiv_rn(round_bf16(cphi[e]), a.inv_temp_div));
+            const float s2 = round_bf16(__fmul_rn(round_bf16(cqk[e]), a.esc_c));
             float t1 = round_bf16(__fadd_rn(s1, s2));
             int ln = 0;
             for (int c = 0; c < a.K; ++c) {
@@ -249,19 +263,21 @@ __global__ void __launch_bounds__(kThreadsTc, 2) k_score_tc(ScoreArgs a, int nds
             const float dt = __double2float_rn(S.bt[rk] - S.bt[rq]);
             val = __fadd_rn(t1, __fmul_rn(dt, tasa));
           }
-          S.sc[qi * 65 + kj] = val;
         }
+        S.sc[qi * 65 + kj] = val;
+      }
     }
     __syncthreads();
 
-    // ---- softmax per query (warp w: queries 4w .. 4w+3; lane -> keys lane, lane + 32) -------------------------------
-    for (int qi = wid * 4; qi < wid * 4 + 4; ++qi) {
+    // ---- softmax per query (warp w: queries 2w, 2w + 1; lane -> keys lane, lane + 32) --------------------------------
+    for (int qi = wid * 2; qi < wid * 2 + 2; ++qi) {
       const int64_t sq = q0 + qi;
       const float x0 = S.sc[qi * 65 + lane], x1 = S.sc[qi * 65 + lane + 32];
       const bool v0 = x0 != -INFINITY, v1 = x1 != -INFINITY;
-      const int nv = __popc(__ballot_sync(0xffffffffu, v0)) + __popc(__ballot_sync(0xffffffffu, v1));
+      const bool anyv = __any_sync(0xffffffffu, v0 || v1);
       float w0 = 0.f, w1 = 0.f;
-      if (nv > 0) {
+      const bool mine = sq < S1;
+      if (anyv) {
         const float mx = warp_max(fmaxf(x0, x1));
         const float e0 = v0 ? expf(__fsub_rn(x0, mx)) : 0.f;
         const float e1 = v1 ? expf(__fsub_rn(x1, mx)) : 0.f;
@@ -269,33 +285,32 @@ __global__ void __launch_bounds__(kThreadsTc, 2) k_score_tc(ScoreArgs a, int nds
         w0 = __fdiv_rn(e0, sum);
         w1 = __fdiv_rn(e1, sum);
         const float peak = warp_max(fmaxf(w0, w1));
-        if (lane == 0 && write_signals && sq < S1) {
-          const int64_t gq = b * a.L + S.pos[(int)(sq & (kW - 1))];
+        if (lane == 0 && write_signals && mine) {
+          const int64_t gq = b * a.L + S.pos[wrow(kQ + qi)];
           a.sen_hay[gq * a.T + tau] = 1;
           a.sen_mx[gq * a.T + tau] = mx;
           a.sen_pk[gq * a.T + tau] = peak;
         }
-      } else if (lane == 0 && write_signals && sq < S1) {
-        const int64_t gq = b * a.L + S.pos[(int)(sq & (kW - 1))];
+      } else if (lane == 0 && write_signals && mine) {
+        const int64_t gq = b * a.L + S.pos[wrow(kQ + qi)];
         a.sen_hay[gq * a.T + tau] = 0;
         a.sen_mx[gq * a.T + tau] = kProhibido;
         a.sen_pk[gq * a.T + tau] = 0.f;
       }
       S.att[qi * 72 + lane] = __float2bfloat16_rn(w0);
       S.att[qi * 72 + lane + 32] = __float2bfloat16_rn(w1);
-      if (lane == 0) S.qhay[qi] = (nv > 0 && sq < S1) ? 1 : 0;
+      if (lane == 0) S.qhay[qi] = (anyv && mine) ? 1 : 0;
     }
     __syncthreads();
 
-    // ---- out = att . V on tensor cores; warp w owns columns [w * dpart / 8, (w + 1) * dpart / 8) -----------------
+    // ---- out = att . V on tensor cores; warp w owns n8 tiles w, w + 16, ... of the d_part columns -----------------
     {
-      const int cols = dpart / 8;           // multiple of 8
-      const int c0w = wid * cols;
-      const int nn = cols / 8;              // n8 tiles of this warp (<= 6)
+      const int ntiles = dpart / 8;
       for (int mt = 0; mt < 2; ++mt) {
         const int qbase = mt * 16;
         const bool any = S.qhay[qbase + (lane & 15)] != 0;
         if (!__any_sync(0xffffffffu, any)) continue;
+        if (wid >= ntiles) continue;
         float acc[6][4];
 #pragma unroll
         for (int j = 0; j < 6; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
@@ -303,45 +318,53 @@ __global__ void __launch_bounds__(kThreadsTc, 2) k_score_tc(ScoreArgs a, int nds
         for (int ks = mt; ks < mt + 3; ++ks) {
           uint32_t a0, a1, a2, a3;
           ldsm_x4(su32(S.att + (qbase + (lane & 15)) * 72 + ks * 16 + (lane >> 4) * 8), a0, a1, a2, a3);
-          const int key = ks * 16 + (lane & 15);
-          const int rk = (int)((q0 - kQ + key) & (kW - 1));
+          const int rk = wrow(ks * 16 + (lane & 15));
 #pragma unroll
           for (int j = 0; j < 6; ++j) {
-            if (j < nn) {
+            const int tile = wid + 16 * j;
+            if (tile < ntiles) {
               uint32_t b0, b1;
-              ldsm_x2_t(su32(S.v + rk * S.Dp + c0w + j * 8), b0, b1);
+              ldsm_x2_t(su32(S.v + rk * S.Dp + tile * 8), b0, b1);
               mma16816(acc[j], a0, a1, a2, a3, b0, b1);
             }
           }
         }
-        // reductions into acc rows of the queries that have candidates
+        // one 16-byte reduction per lane and tile: lanes q and q ^ 1 of a quad swap halves so that the even lane
+        // holds columns 4 (q >> 1) .. + 3 of row r and the odd lane the same columns of row r + 8
+        const int qd = lane & 3;
+        const int rowq = qbase + (lane >> 2) + ((qd & 1) ? 8 : 0);
+        const bool hasq = S.qhay[rowq] != 0;
+        const int64_t gq = b * a.L + S.pos[wrow(kQ + rowq)];
+        float* dst = a.acc + gq * a.d + dp0 + (qd >> 1) * 4;
 #pragma unroll
-        for (int hrow = 0; hrow < 2; ++hrow) {
-          const int qi = qbase + (lane >> 2) + hrow * 8;
-          if (!S.qhay[qi]) continue;
-          const int64_t gq = b * a.L + S.pos[(int)((q0 + qi) & (kW - 1))];
-          float* dst = a.acc + gq * a.d + dp0 + c0w + (lane & 3) * 2;
-#pragma unroll
-          for (int j = 0; j < 6; ++j)
-            if (j < nn) red_add_v2(dst + j * 8, acc[j][hrow * 2], acc[j][hrow * 2 + 1]);
+        for (int j = 0; j < 6; ++j) {
+          const int tile = wid + 16 * j;
+          if (tile < ntiles) {
+            const bool odd = qd & 1;
+            const float s0 = odd ? acc[j][0] : acc[j][2], s1 = odd ? acc[j][1] : acc[j][3];
+            const float r0 = __shfl_xor_sync(0xffffffffu, s0, 1), r1 = __shfl_xor_sync(0xffffffffu, s1, 1);
+            const float v0 = odd ? r0 : acc[j][0], v1 = odd ? r1 : acc[j][1];
+            const float v2 = odd ? acc[j][2] : r0, v3 = odd ? acc[j][3] : r1;
+            if (hasq) red_add_v4(dst + tile * 8, v0, v1, v2, v3);
+          }
         }
       }
     }
-    __syncthreads();
   }
+  cp_async_wait_all();
 }
 
-// cp.async moves 16-byte chunks: phi, Qc, Kc and Ea rows must be multiples of 8 bf16 (rows stay 16-byte aligned).
 bool score_tc_supported(const ScoreArgs& a) {
   return a.d % 64 == 0 && a.d <= 1024 && a.C <= 32 && a.P <= kMaxPhi && a.P % 8 == 0 && a.cf <= kMaxConfirm &&
          a.cf % 8 == 0 && a.K <= kMaxSuffix;
 }
 
 int launch_score_tc(const ScoreArgs& a, cudaStream_t s) {
-  int nds = (a.d + 383) / 384;
+  // the whole width in one block when its 96-row value ring fits next to the features (d <= 768), else halves
+  int nds = (a.d + 767) / 768;
   while (a.d % (nds * 64) != 0) ++nds;
   const int dpart = a.d / nds;
-  if (dpart / 8 / 8 > 6) return ASRN_ERR_UNSUPPORTED;
+  if (dpart / 8 > 16 * 6) return ASRN_ERR_UNSUPPORTED;
   const size_t smem = tc_smem_bytes(a.P, a.cf, a.K, dpart);
   cudaFuncSetAttribute(k_score_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   dim3 grid((unsigned)(((a.L + kSpanTc - 1) / kSpanTc) * nds), (unsigned)(a.B * a.T));

@@ -173,6 +173,8 @@ def gate(layer, h, glogit, acc, hay, mx, pk, vistos, hawkes, racha, half=False):
     h = h.float().contiguous()
     out = torch.empty_like(h)
     args = [x.contiguous() for x in (glogit, acc, hay, mx, pk, vistos, hawkes, racha)]
+    nbytes = _L().asrn_gate_workspace_bytes(ctypes_ref(cfg))
+    ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=dev)
     _lib.check(_L().asrn_gate(ctypes_ref(cfg), ctypes_ref(w), _p(prep), _p(h), *[_p(x) for x in args], _p(out),
-                              _s(dev)), 'asrn_gate')
+                              _p(ws), nbytes, _s(dev)), 'asrn_gate')
     return out

@@ -170,11 +170,13 @@ int asrn_repetition(const asrn_layer_config* cfg, const asrn_layer_weights* w, c
                     float* hawkes, float* racha, double* keys, int32_t* orden_ng, uint8_t* repetido,
                     void* workspace, size_t workspace_bytes, void* stream);
 
-/* Gate and output projection: h_out = h + sigmoid(logit) * (W_o W_v)(acc / max(1, tables with candidates)). */
+/* Gate and output projection: h_out = h + sigmoid(logit) * (W_o W_v)(acc / max(1, tables with candidates)).
+ * The bf16 tensor-core path needs a workspace of asrn_gate_workspace_bytes(cfg) (0 when it is not used). */
+size_t asrn_gate_workspace_bytes(const asrn_layer_config* cfg);
 int asrn_gate(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared, const float* h,
               const float* glogit, const float* acc, const uint8_t* sen_hay, const float* sen_mx,
               const float* sen_pk, const uint8_t* vistos, const float* hawkes, const float* racha, float* h_out,
-              void* stream);
+              void* workspace, size_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }
