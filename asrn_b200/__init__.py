@@ -8,8 +8,10 @@ Drop-in for the reference package's public API on this path (KIROKOWA/ASRN, asrn
 """
 from .layer import ASRNLayer, CapaASRNEstable, Protecciones, Protections
 from .model import ASRNModel, BloqueLocal, LocalBlock, ModeloASRN, create_model, crear_modelo, firmas_de_piezas
+from .writer import Escritor, Writer, escribir, generate
 
 __all__ = ['ASRNLayer', 'CapaASRNEstable', 'Protecciones', 'Protections', 'ASRNModel', 'ModeloASRN', 'LocalBlock',
-           'BloqueLocal', 'create_model', 'crear_modelo', 'firmas_de_piezas']
+           'BloqueLocal', 'create_model', 'crear_modelo', 'firmas_de_piezas', 'generate', 'escribir', 'Writer',
+           'Escritor']
 
 __version__ = '0.1'

@@ -68,6 +68,16 @@ _SIGS = {
                                        _P, _P, _P, _P, _P, _P]),
     'asrn_repetition_workspace_bytes': (ctypes.c_size_t, [_P]),
     'asrn_repetition': (ctypes.c_int, [_P] * 14 + [ctypes.c_size_t, _P]),
+    'asrn_gen_ring_build': (ctypes.c_int, [ctypes.c_int64, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32,
+                                           ctypes.c_int32, ctypes.c_int64, _P, _P, _P, _P, _P]),
+    'asrn_gen_hawkes_table_bytes': (ctypes.c_size_t, [ctypes.c_int64, ctypes.c_int32, ctypes.c_int64]),
+    'asrn_gen_hawkes_build': (ctypes.c_int, [_P, _P, _P, ctypes.c_int64, ctypes.c_int64, _P, _P, _P, _P, _P,
+                                             ctypes.c_int64, _P]),
+    'asrn_gen_attend': (ctypes.c_int, [_P, _P, _P, ctypes.c_int64, ctypes.c_int64] + [_P] * 15),
+    'asrn_gen_memory': (ctypes.c_int, [_P, _P, _P, ctypes.c_int64, ctypes.c_int64, _P, _P, _P, _P, _P,
+                                       ctypes.c_int64, _P, _P, _P, _P, _P]),
+    'asrn_gen_ring_insert': (ctypes.c_int, [ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                            ctypes.c_int64, _P, _P, _P, _P]),
     'asrn_gate_workspace_bytes': (ctypes.c_size_t, [_P]),
     'asrn_gate': (ctypes.c_int, [_P] * 14 + [ctypes.c_size_t, _P]),
 }

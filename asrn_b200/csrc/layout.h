@@ -133,7 +133,40 @@ struct GateArgs {
   float* sigma;            // tensor-core path: (M) gate values (workspace)
 };
 
+// One generation step of one layer: B sequences, the new token at position t of caches of `cap` positions.
+struct GenArgs {
+  int64_t B, t, cap;
+  int d, T, nb, P, C, cf, K, n;
+  float inv_temp_div, esc_c;
+  const uint16_t* ids_t;     // (B, T) bucket ids of the new token
+  const void* phi_t;         // (B, P) act
+  const void* qc_t;          // (B, cf) act
+  const int32_t* ring;       // (B, T, 2^nb, C)
+  const float* sig_cache;    // (B, cap) signatures
+  const double* bt_cache;    // (B, cap) clock
+  const float* la_cache;     // (B, cap) log alfa
+  const void* phi_cache;     // (B, cap, P) act
+  const void* kc_cache;      // (B, cap, cf) act
+  const void* ea_cache;      // (B, cap, d) act rows of E (the value of position k is row k + 1)
+  const float* w_suf;        // (K + 1)
+  const float* tasa;         // (T)
+  float* acc;                // (B, d), zeroed by the caller
+  uint8_t* sen_hay;          // (B, T)
+  float *sen_mx, *sen_pk;    // (B, T)
+};
+
 int launch_context(const ContextArgs& a, bool half, cudaStream_t s);
+size_t hawkes_table_bytes(int64_t B, int n, int64_t cap);
+int launch_ring_build(int64_t B, int64_t L, int T, int nb, int C, int64_t n_valid, const int32_t* orden,
+                      const uint16_t* ids_o, int32_t* ring, int32_t* count, cudaStream_t s);
+int launch_hawkes_build(int64_t B, int64_t L, int64_t ld, int n, const float* sig, const double* cv, const double* Bt,
+                        const float* la, const float* hawkes, void* table, int64_t cap, int* status, cudaStream_t s);
+int launch_gen_attend(const GenArgs& a, bool half, cudaStream_t s);
+int launch_gen_memory(const GenArgs& a, void* table, int64_t hcap, const double* cv, const float* kappa,
+                      const double* beta_t, const float* la_t, float* racha_state, uint8_t* vistos, float* hawkes,
+                      float* racha, int* status, cudaStream_t s);
+int launch_ring_insert(int64_t B, int T, int nb, int C, int64_t t, const uint16_t* ids_t, int32_t* ring,
+                       int32_t* count, cudaStream_t s);
 int launch_clock(const double* beta, double* Bt, int64_t B, int64_t L, cudaStream_t s);
 int launch_hash(const HashArgs& a, bool half, cudaStream_t s);
 int launch_ids_from_phi(int64_t B, int64_t L, int T, int nb, const float* phi, uint16_t* ids_rows, cudaStream_t s);

@@ -24,6 +24,11 @@
  *                                                              _ordenar_claves, escaneo: asrn/nucleo.py:175-257,
  *                                                              688-701)
  *   asrn_gate               CapaASRNEstable._combinar          asrn/estable.py:376-403
+ *   asrn_gen_ring_build     _anillo_desde                      asrn/nucleo.py:1585-1607
+ *   asrn_gen_hawkes_build   _MemoriaHawkes.cargar              asrn/nucleo.py:1656-1681
+ *   asrn_gen_attend         _candidatos + _atender_cand        asrn/nucleo.py:1621-1631, asrn/estable.py:359-372
+ *   asrn_gen_memory         _MemoriaHawkes.paso + _repeticion_o1  asrn/nucleo.py:1683-1714, 953-960
+ *   asrn_gen_ring_insert    _anillo_meter                      asrn/nucleo.py:1610-1618
  */
 #ifndef ASRN_B200_H
 #define ASRN_B200_H
@@ -177,6 +182,44 @@ int asrn_gate(const asrn_layer_config* cfg, const asrn_layer_weights* w, const v
               const float* glogit, const float* acc, const uint8_t* sen_hay, const float* sen_mx,
               const float* sen_pk, const uint8_t* vistos, const float* hawkes, const float* racha, float* h_out,
               void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- O(1) generation step (the writer's per-token work of one ASRN layer) ------------------------------------------
+ * Per layer the caller keeps: rings (B, T, 2^nb, C) int32 and counts (B, T, 2^nb) int32; a Hawkes table of
+ * asrn_gen_hawkes_table_bytes(B, n, hcap) bytes (hcap a power of two, at least twice the positions a sequence will
+ * hold); per sequence caches of `cap` positions: signatures f32, clock f64, log_alfa f32, phi (P) and Kc (cf) in the
+ * compute type; and, shared by every layer, the rows of E in the compute type (the value of position k is row k+1). */
+
+/* Rings of the prompt from its bucket sort (asrn_bucket_sort of the (B*T, L) ids): positions < n_valid, the C most
+ * recent of each bucket in slot rank % C, -1 for empty slots; count = positions per bucket. */
+int asrn_gen_ring_build(int64_t B, int64_t L, int32_t T, int32_t nb, int32_t C, int64_t n_valid, const int32_t* orden,
+                        const uint16_t* ids_o, int32_t* ring, int32_t* count, void* stream);
+
+size_t asrn_gen_hawkes_table_bytes(int64_t B, int32_t n, int64_t cap);
+/* Hawkes table at the end of the prompt (cfg->B sequences of L positions; caches with leading dimension ld): for each
+ * n-gram key its last occurrence p gives (B_u, A) = (Bt[p], hawkes[p] + exp(log_alfa[p])). hawkes: (B, L, n). */
+int asrn_gen_hawkes_build(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared, int64_t L,
+                          int64_t ld, const float* sig, const double* Bt, const float* log_alfa, const float* hawkes,
+                          void* table, int64_t cap, void* stream);
+
+/* The new token at position t (its phi_t, Qc_t, ids_t and its clock / log_alfa / signature already in the caches)
+ * against the C candidates of each table from the rings: acc (B, d) += sum over tables of att * E[k + 1] (zero it
+ * first); per-table signals (B, T). */
+int asrn_gen_attend(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared, int64_t t,
+                    int64_t cap, const uint16_t* ids_t, const void* phi_t, const void* qc_t, const int32_t* ring,
+                    const float* sig_cache, const double* bt_cache, const float* la_cache, const void* phi_cache,
+                    const void* kc_cache, const void* ea_cache, float* acc, uint8_t* sen_hay, float* sen_mx,
+                    float* sen_pk, void* stream);
+
+/* n-gram memory of the new token: vistos (B, n), hawkes (B, n) from the Hawkes table (updated in place), and the
+ * streak racha (B) from racha_state (updated in place). */
+int asrn_gen_memory(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared, int64_t t,
+                    int64_t cap, const float* sig_cache, const double* bt_cache, const double* beta_t,
+                    const float* log_alfa_t, void* table, int64_t hcap, float* racha_state, uint8_t* vistos,
+                    float* hawkes, float* racha, void* stream);
+
+/* Put position t into the ring of its bucket in every table. */
+int asrn_gen_ring_insert(int64_t B, int32_t T, int32_t nb, int32_t C, int64_t t, const uint16_t* ids_t, int32_t* ring,
+                         int32_t* count, void* stream);
 
 #ifdef __cplusplus
 }

@@ -1,0 +1,94 @@
+"""GPU parity of the O(1) generation step (asrn_gen_* entry points through asrn_b200.generate) and of the model
+forward, against the reference's own outputs (tests/golden/model_small.npz) and against the whole-text forward.
+
+Bars: greedy sequences identical; logits within 1e-4 max-norm relative (fp32)."""
+import numpy as np
+import pytest
+import torch
+
+from conftest import load_fixture, rel_err
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(autouse=True)
+def _exact_fp32_torch_ops():
+    """The local blocks and the head are PyTorch ops: compare them in true fp32 (cuDNN defaults to TF32 for
+    convolutions), as the reference's golden outputs were made on the CPU."""
+    old = (torch.backends.cudnn.allow_tf32, torch.backends.cuda.matmul.allow_tf32)
+    torch.backends.cudnn.allow_tf32 = False
+    torch.backends.cuda.matmul.allow_tf32 = False
+    yield
+    torch.backends.cudnn.allow_tf32, torch.backends.cuda.matmul.allow_tf32 = old
+
+
+def _model_from_fixture(dev):
+    import asrn_b200
+    z, params, meta = load_fixture('model_small')
+    m = asrn_b200.create_model(V=meta['V'], d=meta['d'], n_capas=meta['n_capas'])
+    m.load_state_dict({k: torch.from_numpy(np.asarray(v)) for k, v in params.items()})
+    return m.to(dev).eval(), z, meta
+
+
+def test_model_forward_matches_reference(cuda):
+    m, z, meta = _model_from_fixture(cuda)
+    with torch.no_grad():
+        lg = m(torch.from_numpy(z['tokens']).to(cuda)).cpu().numpy()
+    assert rel_err(lg, z['logits']) <= 1e-4
+
+
+@pytest.mark.parametrize('ajeno', [True, False])
+def test_generate_greedy_matches_reference(ajeno, cuda):
+    import asrn_b200
+    m, z, meta = _model_from_fixture(cuda)
+    tag = 'ajeno' if ajeno else 'propia'
+    x0 = torch.from_numpy(z['tokens'][:, :meta['L0']])
+    seqs, steps = asrn_b200.generate(m, x0.to(cuda), n_nuevos=meta['n_new'], top_k=1, memoria_de_lo_ajeno=ajeno)
+    assert np.array_equal(seqs.numpy(), z[f'gen_{tag}_seqs'])
+    assert rel_err(steps.numpy(), z[f'gen_{tag}_logits']) <= 1e-4
+
+
+@pytest.mark.parametrize('B,L0,n', [(2, 40, 50), (1, 2, 30), (3, 1, 20)])
+def test_writer_steps_equal_whole_text(B, L0, n, cuda):
+    """Step by step == the model on the whole text (tests/test_nucleo.py:118-140), with buckets that overflow their
+    rings (chunk 4, 2 bits: 4 buckets per table) and moved parameters; memory of its own writing (ajeno off)."""
+    import asrn_b200
+    torch.manual_seed(1)
+    m = asrn_b200.create_model(V=60, d=32, n_capas=3, largo_cada=1, chunk=4, n_bits=2)
+    g = torch.Generator().manual_seed(0)
+    with torch.no_grad():
+        for c in m.largos:
+            for name, p in c.named_parameters():
+                if name in ('w_reloj', 'b_reloj', 'gamma', 'log_kappa', 'log_kappa_racha', 'u_hawkes', 'd_racha',
+                            'cq.weight', 'w_sufijo', 'w_vistos', 'g_conf.weight'):
+                    p.add_(torch.randn(p.shape, generator=g) * 0.5)
+    m = m.to(cuda).eval()
+    gx = torch.Generator().manual_seed(2)
+    x = torch.randint(0, 60, (B, L0 + n), generator=gx)
+    x[:, (L0 + n) // 2:(L0 + n) // 2 + (L0 + n) // 4] = x[:, :(L0 + n) // 4]
+    x = x.to(cuda)
+    w = asrn_b200.Writer(m, memoria_de_lo_ajeno=False)
+    lgs = [w.inicio(x[:, :L0], capacidad=L0 + n)]
+    lgs += [w.paso(x[:, t]) for t in range(L0, L0 + n - 1)]
+    steps = torch.stack(lgs, 1)
+    with torch.no_grad():
+        whole = m(x[:, :L0 + n - 1])[:, L0 - 1:]
+    assert rel_err(steps.cpu().numpy(), whole.cpu().numpy()) <= 1e-4
+    assert all(s == 0 for s in w.status())
+
+
+def test_generate_sampling_is_seeded(cuda):
+    """Non-greedy sampling with temperature / top-k / top-p / repetition penalty / no-repeat n-grams is deterministic
+    for a seed and respects the stop token."""
+    import asrn_b200
+    m, z, meta = _model_from_fixture(cuda)
+    x0 = torch.from_numpy(z['tokens'][:1, :32]).to(cuda)
+    a = asrn_b200.generate(m, x0, n_nuevos=12, temperatura=0.9, top_k=20, top_p=0.9, semilla=5, pena_repeticion=1.3,
+                           no_repetir_ngramas=3)[0]
+    b = asrn_b200.generate(m, x0, n_nuevos=12, temperatura=0.9, top_k=20, top_p=0.9, semilla=5, pena_repeticion=1.3,
+                           no_repetir_ngramas=3)[0]
+    assert torch.equal(a, b) and a.shape == (1, 44)
+    stop = int(a[0, 33])
+    c, lg = asrn_b200.generate(m, x0, n_nuevos=12, temperatura=0.9, top_k=20, top_p=0.9, semilla=5,
+                               pena_repeticion=1.3, no_repetir_ngramas=3, parar_en=stop, devolver_logits=False)
+    assert lg is None and int(c[0, -1]) == stop
