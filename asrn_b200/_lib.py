@@ -9,7 +9,7 @@ import os
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, 'libasrn_b200.so')
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 ASRN_OK, ASRN_ERR_ARG, ASRN_ERR_UNSUPPORTED, ASRN_ERR_WORKSPACE, ASRN_ERR_CUDA, ASRN_ERR_TIMEOUT = range(6)
 
@@ -73,11 +73,10 @@ _SIGS = {
     'asrn_gen_hawkes_table_bytes': (ctypes.c_size_t, [ctypes.c_int64, ctypes.c_int32, ctypes.c_int64]),
     'asrn_gen_hawkes_build': (ctypes.c_int, [_P, _P, _P, ctypes.c_int64, ctypes.c_int64, _P, _P, _P, _P, _P,
                                              ctypes.c_int64, _P]),
-    'asrn_gen_attend': (ctypes.c_int, [_P, _P, _P, ctypes.c_int64, ctypes.c_int64] + [_P] * 15),
-    'asrn_gen_memory': (ctypes.c_int, [_P, _P, _P, ctypes.c_int64, ctypes.c_int64, _P, _P, _P, _P, _P,
-                                       ctypes.c_int64, _P, _P, _P, _P, _P]),
+    'asrn_gen_attend': (ctypes.c_int, [_P, _P, _P, _P, ctypes.c_int64] + [_P] * 16),
+    'asrn_gen_memory': (ctypes.c_int, [_P] * 4 + [ctypes.c_int64] + [_P] * 6 + [ctypes.c_int64] + [_P] * 5),
     'asrn_gen_ring_insert': (ctypes.c_int, [ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
-                                            ctypes.c_int64, _P, _P, _P, _P]),
+                                            _P, _P, _P, _P, _P]),
     'asrn_gate_workspace_bytes': (ctypes.c_size_t, [_P]),
     'asrn_gate': (ctypes.c_int, [_P] * 14 + [ctypes.c_size_t, _P]),
 }

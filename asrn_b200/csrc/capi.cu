@@ -156,7 +156,7 @@ const char* asrn_status_string(int status) {
   }
 }
 
-int asrn_abi_version(void) { return 1; }
+int asrn_abi_version(void) { return 2; }
 
 size_t asrn_layer_prepared_bytes(const asrn_layer_config* cfg) {
   if (check_config(cfg) != ASRN_OK) return 0;
@@ -394,62 +394,63 @@ int asrn_gen_hawkes_build(const asrn_layer_config* cfg, const asrn_layer_weights
                              as_stream(stream));
 }
 
-static GenArgs gen_args(const asrn_layer_config& c, const asrn_layer_weights& w, const char* prep, int64_t t,
-                        int64_t cap) {
+static GenArgs gen_args(const asrn_layer_config& c, const asrn_layer_weights& w, const char* prep,
+                        const int64_t* t_pos, int64_t cap) {
   const PreparedLayout pl = prepared_layout(c);
   GenArgs a{};
-  a.B = c.B; a.t = t; a.cap = cap;
+  a.B = c.B; a.t_pos = t_pos; a.cap = cap;
   a.d = (int)c.d; a.T = c.n_tablas; a.nb = c.n_bits; a.P = c.n_tablas * c.n_bits; a.C = c.chunk; a.cf = c.confirmar;
   a.K = c.sufijo; a.n = c.vistos;
   a.inv_temp_div = (float)sqrt((double)a.P);
   a.esc_c = (float)pow((double)c.confirmar, -0.5);
   a.w_suf = w.w_sufijo;
   a.tasa = reinterpret_cast<const float*>(prep + pl.tasa);
+  a.status = reinterpret_cast<int*>(const_cast<char*>(prep) + pl.status);
   return a;
 }
 
-int asrn_gen_attend(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared, int64_t t,
-                    int64_t cap, const uint16_t* ids_t, const void* phi_t, const void* qc_t, const int32_t* ring,
-                    const float* sig_cache, const double* bt_cache, const float* la_cache, const void* phi_cache,
-                    const void* kc_cache, const void* ea_cache, float* acc, uint8_t* sen_hay, float* sen_mx,
-                    float* sen_pk, void* stream) {
+int asrn_gen_attend(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared,
+                    const int64_t* t_pos, int64_t cap, const uint16_t* ids_t, const void* phi_t, const void* qc_t,
+                    const void* kc_t, const int32_t* ring, const float* sig_cache, const double* bt_cache,
+                    const float* la_cache, void* phi_cache, void* kc_cache, const void* ea_cache, float* acc,
+                    uint8_t* sen_hay, float* sen_mx, float* sen_pk, void* stream) {
   int st = check_config(cfg);
   if (st) return st;
   if ((st = check_weights(w))) return st;
-  if (!prepared || !ids_t || !phi_t || !qc_t || !ring || !sig_cache || !bt_cache || !la_cache || !phi_cache ||
-      !kc_cache || !ea_cache || !acc || !sen_hay || !sen_mx || !sen_pk || t < 0 || t >= cap)
+  if (!prepared || !t_pos || !ids_t || !phi_t || !qc_t || !kc_t || !ring || !sig_cache || !bt_cache || !la_cache ||
+      !phi_cache || !kc_cache || !ea_cache || !acc || !sen_hay || !sen_mx || !sen_pk || cap < 2)
     return ASRN_ERR_ARG;
-  GenArgs a = gen_args(*cfg, *w, reinterpret_cast<const char*>(prepared), t, cap);
-  a.ids_t = ids_t; a.phi_t = phi_t; a.qc_t = qc_t; a.ring = ring; a.sig_cache = sig_cache; a.bt_cache = bt_cache;
-  a.la_cache = la_cache; a.phi_cache = phi_cache; a.kc_cache = kc_cache; a.ea_cache = ea_cache; a.acc = acc;
+  GenArgs a = gen_args(*cfg, *w, reinterpret_cast<const char*>(prepared), t_pos, cap);
+  a.ids_t = ids_t; a.phi_t = phi_t; a.qc_t = qc_t; a.kc_t = kc_t; a.ring = ring; a.sig_cache = sig_cache;
+  a.bt_cache = bt_cache; a.la_cache = la_cache; a.phi_cache = phi_cache; a.kc_cache = kc_cache;
+  a.phi_cache_w = phi_cache; a.kc_cache_w = kc_cache; a.ea_cache = ea_cache; a.acc = acc;
   a.sen_hay = sen_hay; a.sen_mx = sen_mx; a.sen_pk = sen_pk;
   return launch_gen_attend(a, cfg->half != 0, as_stream(stream));
 }
 
-int asrn_gen_memory(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared, int64_t t,
-                    int64_t cap, const float* sig_cache, const double* bt_cache, const double* beta_t,
-                    const float* log_alfa_t, void* table, int64_t hcap, float* racha_state, uint8_t* vistos,
-                    float* hawkes, float* racha, void* stream) {
+int asrn_gen_memory(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared,
+                    const int64_t* t_pos, int64_t cap, const float* sig_cache, double* bt_cache, float* la_cache,
+                    const double* beta_t, const float* log_alfa_t, void* table, int64_t hcap, float* racha_state,
+                    uint8_t* vistos, float* hawkes, float* racha, void* stream) {
   int st = check_config(cfg);
   if (st) return st;
   if ((st = check_weights(w))) return st;
-  if (!prepared || !sig_cache || !bt_cache || !beta_t || !log_alfa_t || !table || !racha_state || !vistos || !hawkes ||
-      !racha || t < 0 || t >= cap)
+  if (!prepared || !t_pos || !sig_cache || !bt_cache || !la_cache || !beta_t || !log_alfa_t || !table ||
+      !racha_state || !vistos || !hawkes || !racha || cap < 2)
     return ASRN_ERR_ARG;
   const char* prep = reinterpret_cast<const char*>(prepared);
   const PreparedLayout pl = prepared_layout(*cfg);
-  GenArgs a = gen_args(*cfg, *w, prep, t, cap);
-  a.sig_cache = sig_cache; a.bt_cache = bt_cache;
-  int* status = reinterpret_cast<int*>(const_cast<char*>(prep) + pl.status);
+  GenArgs a = gen_args(*cfg, *w, prep, t_pos, cap);
+  a.sig_cache = sig_cache; a.bt_cache = bt_cache; a.bt_w = bt_cache; a.la_cache = la_cache; a.la_w = la_cache;
   return launch_gen_memory(a, table, hcap, w->c_vistos, reinterpret_cast<const float*>(prep + pl.kappa), beta_t,
-                           log_alfa_t, racha_state, vistos, hawkes, racha, status, as_stream(stream));
+                           log_alfa_t, racha_state, vistos, hawkes, racha, a.status, as_stream(stream));
 }
 
-int asrn_gen_ring_insert(int64_t B, int32_t T, int32_t nb, int32_t C, int64_t t, const uint16_t* ids_t, int32_t* ring,
-                         int32_t* count, void* stream) {
-  if (B < 0 || T < 1 || nb < 1 || nb > 16 || C < 1 || C > 32 || (B > 0 && (!ids_t || !ring || !count)))
+int asrn_gen_ring_insert(int64_t B, int32_t T, int32_t nb, int32_t C, const int64_t* t_pos, const uint16_t* ids_t,
+                         int32_t* ring, int32_t* count, void* stream) {
+  if (B < 0 || T < 1 || nb < 1 || nb > 16 || C < 1 || C > 32 || (B > 0 && (!t_pos || !ids_t || !ring || !count)))
     return ASRN_ERR_ARG;
-  return launch_ring_insert(B, T, nb, C, t, ids_t, ring, count, as_stream(stream));
+  return launch_ring_insert(B, T, nb, C, t_pos, ids_t, ring, count, as_stream(stream));
 }
 
 }  // extern "C"

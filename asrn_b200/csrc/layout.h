@@ -135,12 +135,19 @@ struct GateArgs {
 
 // One generation step of one layer: B sequences, the new token at position t of caches of `cap` positions.
 struct GenArgs {
-  int64_t B, t, cap;
+  int64_t B, cap;
+  const int64_t* t_pos;      // device: position of the new token
   int d, T, nb, P, C, cf, K, n;
   float inv_temp_div, esc_c;
+  int* status;               // device status word
   const uint16_t* ids_t;     // (B, T) bucket ids of the new token
   const void* phi_t;         // (B, P) act
   const void* qc_t;          // (B, cf) act
+  const void* kc_t;          // (B, cf) act
+  void* phi_cache_w;         // phi_cache, written at t
+  void* kc_cache_w;          // kc_cache, written at t
+  double* bt_w;              // bt_cache, written at t
+  float* la_w;               // la_cache, written at t
   const int32_t* ring;       // (B, T, 2^nb, C)
   const float* sig_cache;    // (B, cap) signatures
   const double* bt_cache;    // (B, cap) clock
@@ -165,7 +172,7 @@ int launch_gen_attend(const GenArgs& a, bool half, cudaStream_t s);
 int launch_gen_memory(const GenArgs& a, void* table, int64_t hcap, const double* cv, const float* kappa,
                       const double* beta_t, const float* la_t, float* racha_state, uint8_t* vistos, float* hawkes,
                       float* racha, int* status, cudaStream_t s);
-int launch_ring_insert(int64_t B, int T, int nb, int C, int64_t t, const uint16_t* ids_t, int32_t* ring,
+int launch_ring_insert(int64_t B, int T, int nb, int C, const int64_t* t_pos, const uint16_t* ids_t, int32_t* ring,
                        int32_t* count, cudaStream_t s);
 int launch_clock(const double* beta, double* Bt, int64_t B, int64_t L, cudaStream_t s);
 int launch_hash(const HashArgs& a, bool half, cudaStream_t s);

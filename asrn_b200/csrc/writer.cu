@@ -10,6 +10,11 @@
 //     table keyed by the fp64 n-gram key (-0.0 stored as +0.0), linear probing, cap a power of two
 // Caches per sequence (caller-allocated, position-major): sig (cap_t) f32, Bt f64, log_alfa f32, phi (P) act,
 // Kc (cf) act, and the bf16 rows of E (shared by every layer; the value of position k is E[k + 1]).
+//
+// The position t of the new token is read from device memory (t_pos), so a step is a fixed sequence of launches
+// that a CUDA graph can replay; the step kernels append the new token's clock / log_alfa (k_gen_hawkes) and
+// phi / Kc (k_gen_attend) to the caches. A t outside [1, cap) sets ASRN_ERR_ARG in the status word and writes
+// nothing.
 #include "common.cuh"
 #include "layout.h"
 
@@ -31,7 +36,7 @@ struct HawkesEntry {
   uint64_t key;
   double bu;
   float a;
-  float pad;
+  int32_t last;   // while the prompt's table is built: the key's last position; -1 afterwards
 };
 
 // Slot of `key` in a table of `cap` entries (power of two); inserts it if absent. found = it was present.
@@ -45,6 +50,18 @@ __device__ __forceinline__ int64_t hawkes_slot(HawkesEntry* tab, int64_t cap, ui
     i = (i + 1) & (cap - 1);
   }
   *found = false;
+  return -1;
+}
+
+// Lock-free variant for the parallel build: claims an empty slot with a 64-bit CAS (bounded: at most cap probes).
+__device__ __forceinline__ int64_t hawkes_slot_atomic(HawkesEntry* tab, int64_t cap, uint64_t key) {
+  int64_t i = (int64_t)(mix64(key) & (uint64_t)(cap - 1));
+  for (int64_t p = 0; p < cap; ++p) {
+    const unsigned long long prev = atomicCAS(reinterpret_cast<unsigned long long*>(&tab[i].key),
+                                              (unsigned long long)kEmptyKey, (unsigned long long)key);
+    if (prev == kEmptyKey || prev == key) return i;
+    i = (i + 1) & (cap - 1);
+  }
   return -1;
 }
 
@@ -86,48 +103,82 @@ __global__ void k_ring_build(int64_t L, int T, int nb, int C, int64_t n_valid, c
 }
 
 // Hawkes state at the end of the prompt: for every n-gram key of (b, order) its last occurrence p gives
-// Bu = Bt[p], A = hawkes[p] + exp(log_alfa[p]) (asrn/nucleo.py:1656-1681). One thread per (b, order), in position
-// order, so the last occurrence wins.
-__global__ void k_hawkes_build(int64_t B, int64_t L, int64_t ld, int n, const float* __restrict__ sig,
-                               const double* __restrict__ cv, const double* __restrict__ Bt,
-                               const float* __restrict__ la, const float* __restrict__ hawkes, HawkesEntry* tab,
-                               int64_t cap, int* status) {
-  const int64_t row = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;   // b * n + ni
-  if (row >= B * n) return;
+// Bu = Bt[p], A = hawkes[p] + exp(log_alfa[p]) (asrn/nucleo.py:1656-1681). Two passes: every position inserts its
+// key and raises the entry's last position (atomicMax, so the result does not depend on thread order); then every
+// entry reads the state of its last position.
+__global__ void k_hawkes_insert(int64_t B, int64_t L, int64_t ld, int n, const float* __restrict__ sig,
+                                const double* __restrict__ cv, HawkesEntry* tab, int64_t cap, int* status) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;   // (b * n + ni) * L + p
+  if (i >= B * n * L) return;
+  const int64_t row = i / L, p = i % L;
   const int64_t b = row / n;
   const int ni = (int)(row % n);
+  const double key = ngram_key(sig + b * ld, p, ni, cv);
+  if (key != key) return;
   HawkesEntry* t = tab + row * cap;
-  for (int64_t p = 0; p < L; ++p) {
-    const double key = ngram_key(sig + b * ld, p, ni, cv);
-    if (key != key) continue;
-    bool found;
-    const int64_t i = hawkes_slot(t, cap, key_bits(key), &found);
-    if (i < 0) { atomicCAS(status, ASRN_OK, ASRN_ERR_WORKSPACE); return; }
-    t[i].bu = Bt[b * ld + p];
-    t[i].a = hawkes[(b * L + p) * n + ni] + expf(la[b * ld + p]);
-  }
+  const int64_t e = hawkes_slot_atomic(t, cap, key_bits(key));
+  if (e < 0) { atomicCAS(status, ASRN_OK, ASRN_ERR_WORKSPACE); return; }
+  atomicMax(&t[e].last, (int32_t)p);
 }
 
-// One new token per sequence against its candidates in table tau (asrn/estable.py:359-372, asrn/nucleo.py:1621-1631).
-// Block (b, tau), one warp: lane j scores ring slot j; the weighted value rows E[k + 1] are added into acc (B, d).
+__global__ void k_hawkes_fill(int64_t B, int64_t L, int64_t ld, int n, const double* __restrict__ Bt,
+                              const float* __restrict__ la, const float* __restrict__ hawkes, HawkesEntry* tab,
+                              int64_t cap) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;   // (b * n + ni) * cap + slot
+  if (i >= B * n * cap) return;
+  HawkesEntry& e = tab[i];
+  const int32_t p = e.last;
+  if (p < 0) return;
+  const int64_t row = i / cap;
+  const int64_t b = row / n;
+  const int ni = (int)(row % n);
+  e.bu = Bt[b * ld + p];
+  e.a = hawkes[(b * L + p) * n + ni] + expf(la[b * ld + p]);
+  e.last = -1;
+}
+
+// One new token per sequence against its candidates (asrn/estable.py:359-372, asrn/nucleo.py:1621-1631).
+// Block (b, column slice of kGenCols): warp w scores the C ring slots of tables w, w + 8, ... (lane j = slot j; every
+// column block recomputes these few dot products), then the block sums att * E[k + 1] over all tables for its
+// columns: four thread groups take tables g, g + 4, ... in order and their partial sums are added in a fixed order,
+// so acc (B, d) is written once, deterministically, with no atomics.
+constexpr int kGenCols = 128;
+constexpr int kGenThreads = 256;
+
 template <bool Half>
-__global__ void __launch_bounds__(128) k_gen_attend(GenArgs a) {
+__global__ void __launch_bounds__(kGenThreads) k_gen_attend(GenArgs a) {
   using A = Act<Half>;
   const int64_t b = blockIdx.x;
-  const int tau = blockIdx.y;
+  const int col0 = blockIdx.y * kGenCols;
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const int T = a.T, C = a.C, P = a.P, cf = a.cf, K = a.K;
-  const int64_t t = a.t;
-  __shared__ float s_att[32];
-  __shared__ int s_pos[32];
+  const int64_t t = *a.t_pos;
+  if (t < 1 || t >= a.cap) {
+    if (threadIdx.x == 0 && b == 0 && blockIdx.y == 0) atomicCAS(a.status, ASRN_OK, ASRN_ERR_ARG);
+    return;
+  }
   __shared__ float s_q[kMaxPhi + kMaxConfirm];
+  __shared__ float s_att[kMaxTables][32];
+  __shared__ int s_pos[kMaxTables][32];
+  __shared__ float s_part[4][kGenCols];
   const typename A::T* phi_q = reinterpret_cast<const typename A::T*>(a.phi_t) + b * P;
   const typename A::T* qc_q = reinterpret_cast<const typename A::T*>(a.qc_t) + b * cf;
   for (int i = threadIdx.x; i < P + cf; i += blockDim.x) s_q[i] = i < P ? A::load(phi_q + i) : A::load(qc_q + i - P);
-  const uint16_t id = a.ids_t[b * T + tau];
-  const int32_t* slots = a.ring + ((b * T + tau) * ((int64_t)1 << a.nb) + id) * C;
+  if (blockIdx.y == 0) {   // append the new token's phi and Kc (no candidate of this step is position t)
+    typename A::T* pc = reinterpret_cast<typename A::T*>(a.phi_cache_w) + (b * a.cap + t) * P;
+    typename A::T* kc = reinterpret_cast<typename A::T*>(a.kc_cache_w) + (b * a.cap + t) * cf;
+    const typename A::T* kt = reinterpret_cast<const typename A::T*>(a.kc_t) + b * cf;
+    for (int i = threadIdx.x; i < P + cf; i += blockDim.x) {
+      if (i < P) pc[i] = phi_q[i];
+      else kc[i - P] = kt[i - P];
+    }
+  }
   __syncthreads();
-  if (wid == 0) {
+  const float* sg = a.sig_cache + b * a.cap;
+  const double Bq = a.bt_cache[b * a.cap + t];
+  for (int tau = wid; tau < T; tau += kGenThreads / 32) {
+    const uint16_t id = a.ids_t[b * T + tau];
+    const int32_t* slots = a.ring + ((b * T + tau) * ((int64_t)1 << a.nb) + id) * C;
     const int pos = lane < C ? slots[lane] : -1;
     const bool valid = pos >= 0;
     float sc = -INFINITY;
@@ -145,7 +196,6 @@ __global__ void __launch_bounds__(128) k_gen_attend(GenArgs a) {
       } else {
         t1 = __fadd_rn(__fdiv_rn(dphi, a.inv_temp_div), __fmul_rn(dqk, a.esc_c));
       }
-      const float* sg = a.sig_cache + b * a.cap;
       int ln = 0;
       for (int c = 0; c < K; ++c) {
         const int64_t tq = t - 1 - c, tk = (int64_t)pos - 1 - c;
@@ -153,7 +203,7 @@ __global__ void __launch_bounds__(128) k_gen_attend(GenArgs a) {
       }
       t1 = __fadd_rn(t1, a.w_suf[ln]);
       // _atender_cand: nucleo = log_alfa_k - (gamma / C) * float(B_q - B_k), added after the suffix weight
-      const float dB = __double2float_rn(a.bt_cache[b * a.cap + t] - a.bt_cache[b * a.cap + pos]);
+      const float dB = __double2float_rn(Bq - a.bt_cache[b * a.cap + pos]);
       const float nuc = __fsub_rn(a.la_cache[b * a.cap + pos], __fmul_rn(a.tasa[tau], dB));
       sc = __fadd_rn(t1, nuc);
     }
@@ -165,32 +215,45 @@ __global__ void __launch_bounds__(128) k_gen_attend(GenArgs a) {
       const float sum = warp_sum(e);
       att = __fdiv_rn(e, sum);
       const float peak = warp_max(att);
-      if (lane == 0) {
+      if (lane == 0 && blockIdx.y == 0) {
         a.sen_hay[b * T + tau] = 1;
         a.sen_mx[b * T + tau] = mx;
         a.sen_pk[b * T + tau] = peak;
       }
-    } else if (lane == 0) {
+    } else if (lane == 0 && blockIdx.y == 0) {
       a.sen_hay[b * T + tau] = 0;
       a.sen_mx[b * T + tau] = kProhibido;
       a.sen_pk[b * T + tau] = 0.f;
     }
-    s_att[lane] = Half ? round_bf16(att) : att;
-    s_pos[lane] = valid ? pos : -1;
+    s_att[tau][lane] = Half ? round_bf16(att) : att;
+    s_pos[tau][lane] = valid ? pos : -1;
   }
   __syncthreads();
-  // out[j] = sum_slots att * E[pos + 1][j]
+  // acc[b, j] = sum over tables and slots of att * E[pos + 1][j], j in this block's columns
   const typename A::T* Ea = reinterpret_cast<const typename A::T*>(a.ea_cache) + b * a.cap * (int64_t)a.d;
-  for (int j = threadIdx.x; j < a.d; j += blockDim.x) {
-    float o = 0.f;
-    bool any = false;
+  const int g = threadIdx.x / (kGenThreads / 4);              // 4 groups of 64 threads
+  const int cl = threadIdx.x % (kGenThreads / 4);             // columns col0 + cl and col0 + cl + 64
+  const int j0 = col0 + cl, j1 = col0 + cl + kGenThreads / 4;
+  float o0 = 0.f, o1 = 0.f;
+  for (int tau = g; tau < T; tau += 4) {
     for (int c = 0; c < C; ++c) {
-      const int pos = s_pos[c];
+      const int pos = s_pos[tau][c];
       if (pos < 0) continue;
-      any = true;
-      o = fmaf(s_att[c], A::load(Ea + (int64_t)(pos + 1) * a.d + j), o);
+      const float w = s_att[tau][c];
+      const typename A::T* row = Ea + (int64_t)(pos + 1) * a.d;
+      if (j0 < a.d) o0 = fmaf(w, A::load(row + j0), o0);
+      if (j1 < a.d) o1 = fmaf(w, A::load(row + j1), o1);
     }
-    if (any) red_add_f32(a.acc + b * a.d + j, o);
+  }
+  s_part[g][cl] = o0;
+  s_part[g][cl + kGenThreads / 4] = o1;
+  __syncthreads();
+  if (threadIdx.x < kGenCols) {
+    const int j = col0 + threadIdx.x;
+    if (j < a.d) {
+      const float* q = &s_part[0][threadIdx.x];
+      a.acc[b * a.d + j] = __fadd_rn(__fadd_rn(__fadd_rn(q[0], q[kGenCols]), q[2 * kGenCols]), q[3 * kGenCols]);
+    }
   }
 }
 
@@ -202,8 +265,15 @@ __global__ void k_gen_hawkes(GenArgs a, HawkesEntry* tab, int64_t hcap, const do
   const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= a.B) return;
   const int n = a.n;
-  const int64_t t = a.t;
-  const double Bq = a.bt_cache[b * a.cap + t];
+  const int64_t t = *a.t_pos;
+  if (t < 1 || t >= a.cap) {
+    if (b == 0) atomicCAS(status, ASRN_OK, ASRN_ERR_ARG);
+    return;
+  }
+  // append the new token's clock (the inclusive fp64 sum, one more term) and log_alfa
+  const double Bq = a.bt_w[b * a.cap + t - 1] + beta_t[b];
+  a.bt_w[b * a.cap + t] = Bq;
+  a.la_w[b * a.cap + t] = la_t[b];
   const float alpha = expf(la_t[b]);
   float r = 0.f;
   for (int ni = 0; ni < n; ++ni) {
@@ -238,10 +308,12 @@ __global__ void k_gen_hawkes(GenArgs a, HawkesEntry* tab, int64_t hcap, const do
 }
 
 // Ring insert of position t for every (sequence, table) (asrn/nucleo.py:1610-1618).
-__global__ void k_ring_insert(int64_t B, int T, int nb, int C, int64_t t, const uint16_t* __restrict__ ids_t,
-                              int32_t* __restrict__ ring, int32_t* __restrict__ count) {
+__global__ void k_ring_insert(int64_t B, int T, int nb, int C, const int64_t* __restrict__ t_pos,
+                              const uint16_t* __restrict__ ids_t, int32_t* __restrict__ ring,
+                              int32_t* __restrict__ count) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= B * T) return;
+  const int64_t t = *t_pos;
   const int64_t cell = i * ((int64_t)1 << nb) + ids_t[i];
   const int32_t c = count[cell];
   ring[cell * C + (c % C)] = (int32_t)t;
@@ -269,7 +341,7 @@ __global__ void k_hawkes_clear(HawkesEntry* tab, int64_t entries) {
     tab[i].key = kEmptyKey;
     tab[i].bu = 0.0;
     tab[i].a = 0.f;
-    tab[i].pad = 0.f;
+    tab[i].last = -1;
   }
 }
 
@@ -279,18 +351,20 @@ int launch_hawkes_build(int64_t B, int64_t L, int64_t ld, int n, const float* si
   const int64_t entries = B * n * cap;
   HawkesEntry* tab = reinterpret_cast<HawkesEntry*>(table);
   if (entries > 0) k_hawkes_clear<<<(unsigned)((entries + 255) / 256), 256, 0, s>>>(tab, entries);
-  const int64_t rows = B * n;
-  if (rows > 0 && L > 0)
-    k_hawkes_build<<<(unsigned)((rows + 63) / 64), 64, 0, s>>>(B, L, ld, n, sig, cv, Bt, la, hawkes, tab, cap, status);
+  const int64_t pts = B * n * L;
+  if (pts > 0) {
+    k_hawkes_insert<<<(unsigned)((pts + 255) / 256), 256, 0, s>>>(B, L, ld, n, sig, cv, tab, cap, status);
+    k_hawkes_fill<<<(unsigned)((entries + 255) / 256), 256, 0, s>>>(B, L, ld, n, Bt, la, hawkes, tab, cap);
+  }
   return cudaGetLastError() == cudaSuccess ? ASRN_OK : ASRN_ERR_CUDA;
 }
 
 int launch_gen_attend(const GenArgs& a, bool half, cudaStream_t s) {
   if (a.B == 0) return ASRN_OK;
-  if (a.C > 32 || a.P > kMaxPhi || a.cf > kMaxConfirm) return ASRN_ERR_UNSUPPORTED;
-  dim3 grid((unsigned)a.B, (unsigned)a.T);
-  if (half) k_gen_attend<true><<<grid, 128, 0, s>>>(a);
-  else k_gen_attend<false><<<grid, 128, 0, s>>>(a);
+  if (a.C > 32 || a.P > kMaxPhi || a.cf > kMaxConfirm || a.T > kMaxTables) return ASRN_ERR_UNSUPPORTED;
+  dim3 grid((unsigned)a.B, (unsigned)((a.d + kGenCols - 1) / kGenCols));
+  if (half) k_gen_attend<true><<<grid, kGenThreads, 0, s>>>(a);
+  else k_gen_attend<false><<<grid, kGenThreads, 0, s>>>(a);
   return cudaGetLastError() == cudaSuccess ? ASRN_OK : ASRN_ERR_CUDA;
 }
 
@@ -304,11 +378,11 @@ int launch_gen_memory(const GenArgs& a, void* table, int64_t hcap, const double*
   return cudaGetLastError() == cudaSuccess ? ASRN_OK : ASRN_ERR_CUDA;
 }
 
-int launch_ring_insert(int64_t B, int T, int nb, int C, int64_t t, const uint16_t* ids_t, int32_t* ring,
+int launch_ring_insert(int64_t B, int T, int nb, int C, const int64_t* t_pos, const uint16_t* ids_t, int32_t* ring,
                        int32_t* count, cudaStream_t s) {
   const int64_t n = B * T;
   if (n == 0) return ASRN_OK;
-  k_ring_insert<<<(unsigned)((n + 127) / 128), 128, 0, s>>>(B, T, nb, C, t, ids_t, ring, count);
+  k_ring_insert<<<(unsigned)((n + 127) / 128), 128, 0, s>>>(B, T, nb, C, t_pos, ids_t, ring, count);
   return cudaGetLastError() == cudaSuccess ? ASRN_OK : ASRN_ERR_CUDA;
 }
 

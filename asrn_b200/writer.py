@@ -7,6 +7,11 @@ per layer. The ASRN work of a step runs in the kernels of libasrn_b200.so (asrn_
 new token); the local blocks, embedding and head are PyTorch ops. The rows of E (the values) are cached once, shared
 by every layer.
 
+The step is a fixed sequence of launches: the new token's position lives in device memory (the kernels read it and the
+step increments it), every buffer is allocated at the prompt for the capacity asked, and the local blocks and head
+run in explicit dtypes with weight copies made once (under bf16 autocast: the bf16 copies autocast would make, the
+conv as a (d, k*d) matrix), so after one eager step the writer captures the step in a CUDA graph and replays it.
+
 generate() keeps the reference's sampling semantics (temperature, top_k, top_p, repetition penalty, no-repeat
 n-grams, stop token, conserving the probability of continuing a quote), sampling on the host with the same seeded
 generator, so greedy decoding (top_k=1) and seeded sampling give the reference's tokens.
@@ -31,14 +36,38 @@ class _LayerState:
     pass
 
 
-class Writer:
-    """O(1) writer over an ASRNModel (asrn/nucleo.py:1717-1854)."""
+class _StepWeights:
+    """Local-block and head weights in the step's compute type: under bf16 autocast the bf16 copies autocast casts
+    them to (round to nearest even), else the fp32 parameters; the conv weight (d, d, k) as a (d, k*d) matrix over the
+    window [u_{t-k+1}, ..., u_t] (asrn/nucleo.py:1816-1822)."""
 
-    def __init__(self, modelo, memoria_de_lo_ajeno=True):
+    def __init__(self, m, act):
+        self.blocks = []
+        for blq in m.bloques:
+            d, k = blq.conv.out_channels, blq.k
+            wc = blq.conv.weight.detach().permute(0, 2, 1).reshape(d, k * d).to(act).contiguous()
+            self.blocks.append((wc, blq.conv.bias.detach().to(act),
+                                blq.ff[0].weight.detach().to(act), blq.ff[0].bias.detach().to(act),
+                                blq.ff[2].weight.detach().to(act), blq.ff[2].bias.detach().to(act)))
+        self.head = m.head.weight.detach().to(act)
+
+
+def _ln(mod, x):
+    return F.layer_norm(x, mod.normalized_shape, mod.weight, mod.bias, mod.eps)
+
+
+class Writer:
+    """O(1) writer over an ASRNModel (asrn/nucleo.py:1717-1854).
+
+    inicio(x0, capacidad) runs the prompt and returns the last position's logits; paso(tokens) appends one token per
+    sequence and returns the next logits. grafo=True (default) replays the step as a CUDA graph after its first eager
+    run; the graph's logits buffer is overwritten by the next step (paso copies it unless copiar=False)."""
+
+    def __init__(self, modelo, memoria_de_lo_ajeno=True, grafo=True):
         self.m = modelo
         self.ajeno = memoria_de_lo_ajeno
-
-    # ---- helpers --------------------------------------------------------------------------------------------------
+        self.grafo = grafo
+        self.graph = None
 
     def _act(self):
         return torch.bfloat16 if self.half else torch.float32
@@ -46,61 +75,77 @@ class Writer:
     def _cfg(self, capa, B, L):
         return _lib.make_config(capa, B, L, self.half)
 
-    @staticmethod
-    def _grow(x, cap):
-        y = x.new_zeros((x.shape[0], cap) + tuple(x.shape[2:]))
-        y[:, :x.shape[1]] = x
-        return y
-
-    def _grow_all(self):
-        cap = 2 * self.cap
-        self.sig = self._grow(self.sig, cap)
-        self.ea = self._grow(self.ea, cap)
-        for st in self.layers:
-            for name in ('phi', 'kc', 'bt', 'la'):
-                setattr(st, name, self._grow(getattr(st, name), cap))
-            if 2 * cap > st.hcap:
-                raise NotImplementedError('the n-gram table was sized for the capacity given to inicio(); '
-                                          'pass capacidad >= prompt + new tokens')
-        self.cap = cap
-
     # ---- prompt ---------------------------------------------------------------------------------------------------
 
     @torch.no_grad()
-    def inicio(self, x0, capacidad=0):
-        """Prompt pass (asrn/nucleo.py:1750-1794). x0 (B, L0) int64 on the model's device. Returns the logits of the
-        last position (B, V)."""
+    def inicio(self, x0, capacidad=0, lote=None):
+        """Prompt pass (asrn/nucleo.py:1750-1794). x0 (B, L0) int64 on the model's CUDA device; capacidad = positions
+        to hold (prompt + new tokens); lote = sequences per chunk of the prompt pass (default: about 2^20 tokens per
+        chunk). Returns the logits of the last position (B, V)."""
+        if not x0.is_cuda:
+            raise RuntimeError('asrn_b200 runs on CUDA devices only')
         m = self.m
-        self.half = compute_half(x0.device.type) if x0.is_cuda else False
+        self.half = compute_half('cuda')
         act = self._act()
         B, L0 = x0.shape
         dev = x0.device
+        d = m.emb.embedding_dim
         self.B, self.L0, self.t = B, L0, L0
         self.cap = max(L0 + 1, capacidad)
-        E = m.emb(x0)
-        d = E.shape[-1]
+        self.graph = None
         self.sig = torch.zeros(B, self.cap, dtype=torch.float32, device=dev)
-        self.sig[:, :L0] = x0.to(torch.float32)
         self.ea = torch.zeros(B, self.cap, d, dtype=act, device=dev)
-        self.ea[:, :L0] = E.to(act)
-        self.e_last = E[:, -1].clone()
-        self.buf, self.layers = [], []
+        self.e_last = torch.zeros(B, d, dtype=torch.float32, device=dev)
+        self.buf = [torch.zeros(B, blq.k - 1, d, dtype=act, device=dev) for blq in m.bloques]
+        self.layers = [self._new_state(capa, B, dev) for capa in m.largos]
+        lote = lote or max(1, min(B, (1 << 20) // max(L0, 1)))
+        logits = [self._prompt(x0[b0:b0 + lote], b0) for b0 in range(0, B, lote)]
+        self.t_dev = torch.full((1,), L0, dtype=torch.int64, device=dev)
+        self.tok = torch.zeros(B, dtype=torch.int64, device=dev)
+        self.sw = _StepWeights(m, act)
+        return torch.cat(logits, 0)
+
+    def _new_state(self, capa, B, dev):
+        act, cap = self._act(), self.cap
+        T, nb, C = capa.n_tablas, capa.n_bits, capa.chunk
+        st = _LayerState()
+        st.capa = capa
+        st.phi = torch.zeros(B, cap, T * nb, dtype=act, device=dev)
+        st.kc = torch.zeros(B, cap, capa.confirmar, dtype=act, device=dev)
+        st.bt = torch.zeros(B, cap, dtype=torch.float64, device=dev)
+        st.la = torch.zeros(B, cap, dtype=torch.float32, device=dev)
+        st.racha = torch.zeros(B, dtype=torch.float32, device=dev)
+        st.ring = torch.empty(B, T, 1 << nb, C, dtype=torch.int32, device=dev)
+        st.count = torch.empty(B, T, 1 << nb, dtype=torch.int32, device=dev)
+        st.hcap = max(64, _next_pow2(2 * cap))
+        st.table = torch.empty(B, _lib.lib().asrn_gen_hawkes_table_bytes(1, capa.vistos, st.hcap), dtype=torch.uint8,
+                               device=dev)
+        return st
+
+    def _prompt(self, xc, b0):
+        m, act = self.m, self._act()
+        Bc, L0 = xc.shape
+        b1 = b0 + Bc
+        E = m.emb(xc)
+        self.sig[b0:b1, :L0] = xc.to(torch.float32)
+        self.ea[b0:b1, :L0] = E.to(act)
+        self.e_last[b0:b1] = E[:, -1]
         h, j = E, 0
         for i, blq in enumerate(m.bloques):
             u = blq.ln1(h)
-            self.buf.append(F.pad(u, (0, 0, blq.k - 1, 0))[:, u.shape[1]:])
+            self.buf[i][b0:b1] = F.pad(u, (0, 0, blq.k - 1, 0))[:, L0:].to(act)
             h = blq(h)
             if i in m.pos_largo:
-                h = self._prompt_layer(m.largos[j], E, h, x0)
+                h = self._prompt_layer(self.layers[j], E, h, xc, b0)
                 j += 1
         return m.head(m.ln_f(h[:, -1:]))[:, -1]
 
-    def _prompt_layer(self, capa, E, h, x0):
-        B, L0 = x0.shape
-        dev = x0.device
-        half, act = self.half, self._act()
-        T, nb, C, P = capa.n_tablas, capa.n_bits, capa.chunk, capa.n_tablas * capa.n_bits
-        ctx = stages.context(capa, h, x0, half=half)
+    def _prompt_layer(self, st, E, h, xc, b0):
+        capa, half = st.capa, self.half
+        Bc, L0 = xc.shape
+        b1 = b0 + Bc
+        T, nb, C = capa.n_tablas, capa.n_bits, capa.chunk
+        ctx = stages.context(capa, h, xc, half=half)
         Bt = stages.clock(ctx['beta'])
         hs = stages.hash(capa, E, half=half)
         orden, ids_o = stages.bucket_sort(hs['ids_rows'], nb)
@@ -109,109 +154,109 @@ class Writer:
         rep = stages.repetition(capa, ctx['sig'], ctx['beta'], Bt, ctx['log_alfa'])
         h_new = stages.gate(capa, h, ctx['glogit'], sc['acc'], sc['hay'], sc['mx'], sc['pk'], rep['vistos'],
                             rep['hawkes'], rep['racha'], half=half)
-        st = _LayerState()
-        st.capa = capa
-        st.phi = torch.zeros(B, self.cap, P, dtype=act, device=dev)
-        st.phi[:, :L0] = hs['phi']
-        st.kc = torch.zeros(B, self.cap, capa.confirmar, dtype=act, device=dev)
-        st.kc[:, :L0] = ctx['Kc']
-        st.bt = torch.zeros(B, self.cap, dtype=torch.float64, device=dev)
-        st.bt[:, :L0] = Bt
-        st.la = torch.zeros(B, self.cap, dtype=torch.float32, device=dev)
-        st.la[:, :L0] = ctx['log_alfa']
-        st.racha = rep['racha'][:, -1].contiguous().clone()
+        st.phi[b0:b1, :L0] = hs['phi']
+        st.kc[b0:b1, :L0] = ctx['Kc']
+        st.bt[b0:b1, :L0] = Bt
+        st.la[b0:b1, :L0] = ctx['log_alfa']
+        st.racha[b0:b1] = rep['racha'][:, -1]
         lib = _lib.lib()
-        s = _lib.stream_ptr(dev)
-        st.ring = torch.empty(B, T, 1 << nb, C, dtype=torch.int32, device=dev)
-        st.count = torch.empty(B, T, 1 << nb, dtype=torch.int32, device=dev)
+        s = _lib.stream_ptr(xc.device)
         n_valid = L0 - 1 if self.ajeno else L0
-        _lib.check(lib.asrn_gen_ring_build(B, L0, T, nb, C, n_valid, _lib.ptr(orden), _lib.ptr(ids_o),
-                                           _lib.ptr(st.ring), _lib.ptr(st.count), s), 'asrn_gen_ring_build')
-        st.hcap = max(64, _next_pow2(2 * self.cap))
-        st.table = torch.empty(lib.asrn_gen_hawkes_table_bytes(B, capa.vistos, st.hcap), dtype=torch.uint8,
-                               device=dev)
-        w, _keep, prep = capa.prepared(dev, half)
-        cfg = self._cfg(capa, B, L0)
+        _lib.check(lib.asrn_gen_ring_build(Bc, L0, T, nb, C, n_valid, _lib.ptr(orden), _lib.ptr(ids_o),
+                                           _lib.ptr(st.ring[b0:b1]), _lib.ptr(st.count[b0:b1]), s),
+                   'asrn_gen_ring_build')
+        w, _keep, prep = capa.prepared(xc.device, half)
+        cfg = self._cfg(capa, Bc, L0)
         _lib.check(lib.asrn_gen_hawkes_build(ctypes_ref(cfg), ctypes_ref(w), _lib.ptr(prep), L0, self.cap,
-                                             _lib.ptr(self.sig), _lib.ptr(st.bt), _lib.ptr(st.la),
-                                             _lib.ptr(rep['hawkes'].contiguous()), _lib.ptr(st.table), st.hcap, s),
-                   'asrn_gen_hawkes_build')
-        self.layers.append(st)
+                                             _lib.ptr(self.sig[b0:b1]), _lib.ptr(st.bt[b0:b1]),
+                                             _lib.ptr(st.la[b0:b1]), _lib.ptr(rep['hawkes'].contiguous()),
+                                             _lib.ptr(st.table[b0:b1]), st.hcap, s), 'asrn_gen_hawkes_build')
         return h_new
 
     # ---- one token --------------------------------------------------------------------------------------------------
 
     @torch.no_grad()
-    def paso(self, pieza):
-        """One new token per sequence, pieza (B,) (asrn/nucleo.py:1796-1854). Returns the logits (B, V)."""
-        m = self.m
+    def paso(self, pieza, copiar=True):
+        """One new token per sequence, pieza (B,) (asrn/nucleo.py:1796-1854). Returns the logits (B, V): a copy, or
+        with copiar=False the step's own buffer, valid until the next step."""
         if self.t >= self.cap:
-            self._grow_all()
-        t = self.t
-        dev = self.sig.device
-        act = self._act()
-        pieza = pieza.view(-1).to(dev)
-        B = pieza.shape[0]
-        e_t = m.emb(pieza.view(-1, 1))                                       # (B, 1, d)
-        self.sig[:, t] = pieza.to(torch.float32)
-        self.ea[:, t] = e_t[:, 0].to(act)
-        tok = pieza.view(B, 1)
-        h, j = e_t, 0
-        for i, blq in enumerate(m.bloques):
-            ventana = torch.cat([self.buf[i], blq.ln1(h)], 1)
-            z = blq.conv(ventana.transpose(1, 2)).transpose(1, 2)
-            self.buf[i] = ventana[:, 1:]
-            h = h + F.gelu(z)
-            h = h + blq.ff(blq.ln2(h))
-            if i in m.pos_largo:
-                h = self._step_layer(self.layers[j], e_t, h, tok, t)
-                j += 1
-        self.e_last = e_t[:, 0]
+            raise ValueError(f'the writer holds {self.cap} positions; pass capacidad >= prompt + new tokens to '
+                             'inicio()')
+        self.tok.copy_(pieza.reshape(-1), non_blocking=True)
+        if self.graph is not None:
+            self.graph.replay()
+            lg = self.logits
+        else:
+            lg = self._step()
+            if self.grafo and self.t + 1 < self.cap:
+                self._capture()
         self.t += 1
-        return m.head(m.ln_f(h))[:, -1]
+        return lg.clone() if copiar else lg
 
-    def _step_layer(self, st, e_t, h, tok, t):
-        capa = st.capa
-        half = self.half
-        B = tok.shape[0]
+    def _capture(self):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self.logits = self._step()
+        self.graph = g
+
+    def _step(self):
+        """The step's launches: position t is self.t_dev on the device, incremented at the end."""
+        m, sw, act, B = self.m, self.sw, self._act(), self.B
+        with torch.autocast('cuda', enabled=False):
+            tok = self.tok
+            e_t = F.embedding(tok, m.emb.weight)
+            self.sig.index_copy_(1, self.t_dev, tok.to(torch.float32).view(B, 1))
+            self.ea.index_copy_(1, self.t_dev, e_t.to(act).view(B, 1, -1))
+            h, j = e_t, 0
+            for i, blq in enumerate(m.bloques):
+                wc, bc, w1, b1, w2, b2 = sw.blocks[i]
+                win = torch.cat([self.buf[i], _ln(blq.ln1, h).to(act).unsqueeze(1)], 1)
+                self.buf[i].copy_(win[:, 1:])
+                h = h + F.gelu(F.linear(win.reshape(B, -1), wc, bc))
+                h = h + F.linear(F.gelu(F.linear(_ln(blq.ln2, h).to(act), w1, b1)), w2, b2)
+                if i in m.pos_largo:
+                    h = self._step_layer(self.layers[j], e_t, h, tok)
+                    j += 1
+            lg = F.linear(_ln(m.ln_f, h).to(act), sw.head)
+            self.e_last.copy_(e_t)
+            self.t_dev += 1
+        return lg
+
+    def _step_layer(self, st, e_t, h, tok):
+        capa, half, B = st.capa, self.half, self.B
         dev = tok.device
         T, nb, C, n = capa.n_tablas, capa.n_bits, capa.chunk, capa.vistos
         lib = _lib.lib()
         s = _lib.stream_ptr(dev)
-        ctx = stages.context(capa, h, tok, half=half)
-        st.bt[:, t] = st.bt[:, t - 1] + ctx['beta'][:, 0]
-        st.la[:, t] = ctx['log_alfa'][:, 0]
-        hs = stages.hash(capa, torch.stack([self.e_last, e_t[:, 0]], 1), half=half)
+        hin = h.view(B, 1, -1)
+        ctx = stages.context(capa, hin, tok.view(B, 1), half=half)
+        hs = stages.hash(capa, torch.stack([self.e_last, e_t], 1), half=half)
         phi_t = hs['phi'][:, 1].contiguous()
         ids_t = hs['ids_rows'].view(B, T, 2)[:, :, 1].contiguous()
-        qc_t = ctx['Qc'][:, 0].contiguous()
-        acc = torch.zeros(B, 1, capa.d, dtype=torch.float32, device=dev)
-        hay = torch.empty(B, 1, T, dtype=torch.uint8, device=dev)
-        mx = torch.empty(B, 1, T, dtype=torch.float32, device=dev)
-        pk = torch.empty(B, 1, T, dtype=torch.float32, device=dev)
         w, _keep, prep = capa.prepared(dev, half)
         cfg = self._cfg(capa, B, 1)
-        _lib.check(lib.asrn_gen_attend(ctypes_ref(cfg), ctypes_ref(w), _lib.ptr(prep), t, self.cap, _lib.ptr(ids_t),
-                                       _lib.ptr(phi_t), _lib.ptr(qc_t), _lib.ptr(st.ring), _lib.ptr(self.sig),
-                                       _lib.ptr(st.bt), _lib.ptr(st.la), _lib.ptr(st.phi), _lib.ptr(st.kc),
-                                       _lib.ptr(self.ea), _lib.ptr(acc), _lib.ptr(hay), _lib.ptr(mx), _lib.ptr(pk), s),
-                   'asrn_gen_attend')
+        tp = _lib.ptr(self.t_dev)
         vistos = torch.empty(B, 1, n, dtype=torch.uint8, device=dev)
         hawkes = torch.empty(B, 1, n, dtype=torch.float32, device=dev)
         racha = torch.empty(B, 1, dtype=torch.float32, device=dev)
-        beta_t = ctx['beta'][:, 0].contiguous()
-        la_t = ctx['log_alfa'][:, 0].contiguous()
-        _lib.check(lib.asrn_gen_memory(ctypes_ref(cfg), ctypes_ref(w), _lib.ptr(prep), t, self.cap, _lib.ptr(self.sig),
-                                       _lib.ptr(st.bt), _lib.ptr(beta_t), _lib.ptr(la_t), _lib.ptr(st.table), st.hcap,
-                                       _lib.ptr(st.racha), _lib.ptr(vistos), _lib.ptr(hawkes), _lib.ptr(racha), s),
-                   'asrn_gen_memory')
-        h = stages.gate(capa, h, ctx['glogit'], acc, hay, mx, pk, vistos, hawkes, racha, half=half)
-        st.phi[:, t] = phi_t
-        st.kc[:, t] = ctx['Kc'][:, 0]
+        _lib.check(lib.asrn_gen_memory(ctypes_ref(cfg), ctypes_ref(w), _lib.ptr(prep), tp, self.cap,
+                                       _lib.ptr(self.sig), _lib.ptr(st.bt), _lib.ptr(st.la), _lib.ptr(ctx['beta']),
+                                       _lib.ptr(ctx['log_alfa']), _lib.ptr(st.table), st.hcap, _lib.ptr(st.racha),
+                                       _lib.ptr(vistos), _lib.ptr(hawkes), _lib.ptr(racha), s), 'asrn_gen_memory')
+        acc = torch.empty(B, 1, capa.d, dtype=torch.float32, device=dev)
+        hay = torch.empty(B, 1, T, dtype=torch.uint8, device=dev)
+        mx = torch.empty(B, 1, T, dtype=torch.float32, device=dev)
+        pk = torch.empty(B, 1, T, dtype=torch.float32, device=dev)
+        _lib.check(lib.asrn_gen_attend(ctypes_ref(cfg), ctypes_ref(w), _lib.ptr(prep), tp, self.cap, _lib.ptr(ids_t),
+                                       _lib.ptr(phi_t), _lib.ptr(ctx['Qc']), _lib.ptr(ctx['Kc']), _lib.ptr(st.ring),
+                                       _lib.ptr(self.sig), _lib.ptr(st.bt), _lib.ptr(st.la), _lib.ptr(st.phi),
+                                       _lib.ptr(st.kc), _lib.ptr(self.ea), _lib.ptr(acc), _lib.ptr(hay), _lib.ptr(mx),
+                                       _lib.ptr(pk), s), 'asrn_gen_attend')
+        h = stages.gate(capa, hin, ctx['glogit'], acc, hay, mx, pk, vistos, hawkes, racha, half=half)
         if not self.ajeno:
-            _lib.check(lib.asrn_gen_ring_insert(B, T, nb, C, t, _lib.ptr(ids_t), _lib.ptr(st.ring),
+            _lib.check(lib.asrn_gen_ring_insert(B, T, nb, C, tp, _lib.ptr(ids_t), _lib.ptr(st.ring),
                                                 _lib.ptr(st.count), s), 'asrn_gen_ring_insert')
-        return h
+        return h.view(B, -1)
 
     def status(self):
         """Device status words of the layers (0 = ok; synchronises)."""
@@ -222,6 +267,12 @@ class Writer:
             out.append(_lib.lib().asrn_layer_status(ctypes_ref(cfg), _lib.ptr(prep), 0,
                                                     _lib.stream_ptr(self.sig.device)))
         return out
+
+    def cerrar(self):
+        """Release the step's CUDA graph and the state."""
+        self.graph = None
+        self.logits = None
+        self.layers = []
 
 
 Escritor = Writer
@@ -348,7 +399,8 @@ def escribir(modelo, inicio, n_nuevos=200, temperatura=0.8, top_k=40, semilla=0,
             if parar_en is not None and bool(done.all()):
                 break
             if k < n_nuevos - 1:
-                lg = w.paso(nxt_cpu)
+                lg = w.paso(nxt[:, 0])
+        w.cerrar()
         x = text[:, :length]
         if not devolver_logits:
             return x.cpu(), None

@@ -187,7 +187,10 @@ int asrn_gate(const asrn_layer_config* cfg, const asrn_layer_weights* w, const v
  * Per layer the caller keeps: rings (B, T, 2^nb, C) int32 and counts (B, T, 2^nb) int32; a Hawkes table of
  * asrn_gen_hawkes_table_bytes(B, n, hcap) bytes (hcap a power of two, at least twice the positions a sequence will
  * hold); per sequence caches of `cap` positions: signatures f32, clock f64, log_alfa f32, phi (P) and Kc (cf) in the
- * compute type; and, shared by every layer, the rows of E in the compute type (the value of position k is row k+1). */
+ * compute type; and, shared by every layer, the rows of E in the compute type (the value of position k is row k+1).
+ * The step entry points read the new token's position from device memory (t_pos, one int64), so a step is a fixed
+ * sequence of launches that a CUDA graph can capture and replay; a position outside [1, cap) makes the kernels write
+ * nothing and set ASRN_ERR_ARG in the layer's status word (asrn_layer_status). */
 
 /* Rings of the prompt from its bucket sort (asrn_bucket_sort of the (B*T, L) ids): positions < n_valid, the C most
  * recent of each bucket in slot rank % C, -1 for empty slots; count = positions per bucket. */
@@ -201,25 +204,27 @@ int asrn_gen_hawkes_build(const asrn_layer_config* cfg, const asrn_layer_weights
                           int64_t ld, const float* sig, const double* Bt, const float* log_alfa, const float* hawkes,
                           void* table, int64_t cap, void* stream);
 
-/* The new token at position t (its phi_t, Qc_t, ids_t and its clock / log_alfa / signature already in the caches)
- * against the C candidates of each table from the rings: acc (B, d) += sum over tables of att * E[k + 1] (zero it
- * first); per-table signals (B, T). */
-int asrn_gen_attend(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared, int64_t t,
-                    int64_t cap, const uint16_t* ids_t, const void* phi_t, const void* qc_t, const int32_t* ring,
-                    const float* sig_cache, const double* bt_cache, const float* la_cache, const void* phi_cache,
-                    const void* kc_cache, const void* ea_cache, float* acc, uint8_t* sen_hay, float* sen_mx,
-                    float* sen_pk, void* stream);
+/* n-gram memory of the new token at position *t_pos (its signature already in sig_cache): appends its clock
+ * Bt[t] = Bt[t-1] + beta_t and log_alfa_t to the caches, then vistos (B, n), hawkes (B, n) from the Hawkes table
+ * (updated in place), and the streak racha (B) from racha_state (updated in place). Runs before asrn_gen_attend. */
+int asrn_gen_memory(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared,
+                    const int64_t* t_pos, int64_t cap, const float* sig_cache, double* bt_cache, float* la_cache,
+                    const double* beta_t, const float* log_alfa_t, void* table, int64_t hcap, float* racha_state,
+                    uint8_t* vistos, float* hawkes, float* racha, void* stream);
 
-/* n-gram memory of the new token: vistos (B, n), hawkes (B, n) from the Hawkes table (updated in place), and the
- * streak racha (B) from racha_state (updated in place). */
-int asrn_gen_memory(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared, int64_t t,
-                    int64_t cap, const float* sig_cache, const double* bt_cache, const double* beta_t,
-                    const float* log_alfa_t, void* table, int64_t hcap, float* racha_state, uint8_t* vistos,
-                    float* hawkes, float* racha, void* stream);
+/* The new token at position *t_pos (phi_t, Qc_t, Kc_t, ids_t; its clock / log_alfa already appended by
+ * asrn_gen_memory) against the C candidates of each table from the rings: acc (B, d) = sum over tables of
+ * att * E[k + 1] (summed in a fixed order: deterministic); per-table signals (B, T). Appends phi_t and Kc_t to the
+ * caches. */
+int asrn_gen_attend(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared,
+                    const int64_t* t_pos, int64_t cap, const uint16_t* ids_t, const void* phi_t, const void* qc_t,
+                    const void* kc_t, const int32_t* ring, const float* sig_cache, const double* bt_cache,
+                    const float* la_cache, void* phi_cache, void* kc_cache, const void* ea_cache, float* acc,
+                    uint8_t* sen_hay, float* sen_mx, float* sen_pk, void* stream);
 
-/* Put position t into the ring of its bucket in every table. */
-int asrn_gen_ring_insert(int64_t B, int32_t T, int32_t nb, int32_t C, int64_t t, const uint16_t* ids_t, int32_t* ring,
-                         int32_t* count, void* stream);
+/* Put position *t_pos into the ring of its bucket in every table. */
+int asrn_gen_ring_insert(int64_t B, int32_t T, int32_t nb, int32_t C, const int64_t* t_pos, const uint16_t* ids_t,
+                         int32_t* ring, int32_t* count, void* stream);
 
 #ifdef __cplusplus
 }
