@@ -40,7 +40,7 @@ int check_weights(const asrn_layer_weights* w) {
 // Workspace of one layer forward, in order of use.
 struct Workspace {
   size_t sig, qc, kc, beta, bt, la, glogit, ea, phi, ids_rows, orden, ids_o, acc, hay, mx, pk, vistos, hawkes,
-      racha, sort, sigma, total;
+      racha, sort, sigma, rep, total;
   size_t sort_bytes;
 };
 
@@ -72,6 +72,7 @@ Workspace workspace_layout(const asrn_layer_config& c) {
   w.sort_bytes = bucket_sort_workspace((int64_t)c.B * T, c.L, c.n_bits);
   w.sort = take(w.sort_bytes);
   w.sigma = take(M * 4);
+  w.rep = take(repetition_workspace(c.B, c.L, c.vistos));
   w.total = o;
   return w;
 }
@@ -241,7 +242,7 @@ int asrn_layer_forward(const asrn_layer_config* cfg, const asrn_layer_weights* w
   RepetitionArgs ra = repetition_args(c, *w, prep);
   ra.sig = sig; ra.beta = beta; ra.Bt = Bt; ra.log_alfa = la; ra.vistos = vistos; ra.hawkes = hawkes;
   ra.racha = racha;
-  if ((st = launch_repetition(ra, nullptr, 0, s))) return st;
+  if ((st = launch_repetition(ra, base + ws.rep, repetition_workspace(c.B, c.L, c.vistos), s))) return st;
   GateArgs ga = gate_args(c, *w, prep);
   ga.h = h; ga.glogit = glogit; ga.acc = acc; ga.sen_hay = hay; ga.sen_mx = mx; ga.sen_pk = pk;
   ga.vistos = vistos; ga.hawkes = hawkes; ga.racha = racha; ga.out = h_out;
@@ -451,6 +452,45 @@ int asrn_gen_ring_insert(int64_t B, int32_t T, int32_t nb, int32_t C, const int6
   if (B < 0 || T < 1 || nb < 1 || nb > 16 || C < 1 || C > 32 || (B > 0 && (!t_pos || !ids_t || !ring || !count)))
     return ASRN_ERR_ARG;
   return launch_ring_insert(B, T, nb, C, t_pos, ids_t, ring, count, as_stream(stream));
+}
+
+int asrn_gen_front(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared, const float* h,
+                   const float* e_t, const float* e_prev, const int64_t* tokens, void* Qc, void* Kc, double* beta,
+                   float* log_alfa, float* glogit, float* sig, void* phi, uint16_t* ids, void* stream) {
+  int st = check_config(cfg);
+  if (st) return st;
+  if ((st = check_weights(w))) return st;
+  if (cfg->B > 0 && (!prepared || !h || !e_t || !e_prev || !tokens || !Qc || !Kc || !beta || !log_alfa || !glogit ||
+                     !sig || !phi || !ids))
+    return ASRN_ERR_ARG;
+  const char* prep = reinterpret_cast<const char*>(prepared);
+  const PreparedLayout pl = prepared_layout(*cfg);
+  GenFrontArgs a{};
+  a.B = cfg->B; a.d = (int)cfg->d; a.cf = cfg->confirmar; a.m = cfg->hidden; a.T = cfg->n_tablas;
+  a.Tw = cfg->n_tablas - cfg->tablas_contexto; a.nb = cfg->n_bits; a.P = cfg->n_tablas * cfg->n_bits;
+  a.h = h; a.e_t = e_t; a.e_prev = e_prev; a.tokens = tokens;
+  a.ln_w = w->ln_w; a.ln_b = w->ln_b; a.w_reloj = w->w_reloj; a.b_reloj = w->b_reloj; a.g_w = w->g_w; a.g_b = w->g_b;
+  a.wctx = prep + pl.wctx; a.w1 = prep + pl.w1; a.b1 = reinterpret_cast<const float*>(prep + pl.b1);
+  a.w2 = prep + pl.w2; a.b2 = reinterpret_cast<const float*>(prep + pl.b2);
+  a.beta_max = cfg->beta_max; a.log_alfa_min = cfg->log_alfa_min;
+  a.Qc = Qc; a.Kc = Kc; a.beta = beta; a.log_alfa = log_alfa; a.glogit = glogit; a.sig = sig; a.phi = phi; a.ids = ids;
+  return launch_gen_front(a, cfg->half != 0, as_stream(stream));
+}
+
+int asrn_gen_gate(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared, const float* h,
+                  const float* glogit, const float* acc, const uint8_t* sen_hay, const float* sen_mx,
+                  const float* sen_pk, const uint8_t* vistos, const float* hawkes, const float* racha, float* h_out,
+                  void* stream) {
+  int st = check_config(cfg);
+  if (st) return st;
+  if ((st = check_weights(w))) return st;
+  if (cfg->B * cfg->L > 0 && (!prepared || !h || !glogit || !acc || !sen_hay || !sen_mx || !sen_pk || !vistos ||
+                              !hawkes || !racha || !h_out))
+    return ASRN_ERR_ARG;
+  GateArgs a = gate_args(*cfg, *w, reinterpret_cast<const char*>(prepared));
+  a.h = h; a.glogit = glogit; a.acc = acc; a.sen_hay = sen_hay; a.sen_mx = sen_mx; a.sen_pk = sen_pk;
+  a.vistos = vistos; a.hawkes = hawkes; a.racha = racha; a.out = h_out;
+  return launch_gen_gate(a, cfg->half != 0, as_stream(stream));
 }
 
 }  // extern "C"

@@ -309,4 +309,119 @@ int launch_gate(const GateArgs& a, bool half, cudaStream_t s) {
   return cudaGetLastError() == cudaSuccess ? ASRN_OK : ASRN_ERR_CUDA;
 }
 
+// ---- gate of the new tokens of a generation step (B rows) ----------------------------------------------------------
+// k_gen_gate_tc (bf16 autocast): one block per 32 output columns, so W_ov is spread over d / 32 CTAs; the gate scalars
+// of every row (gate_of_token), then h' = h + bf16(sigma * bf16(c . W_ov^T)) with c = bf16(acc / max(1, pt)) on
+// mma.sync. fp32 mode uses k_gate_simt.
+
+namespace {
+constexpr int kGGCols = 32, kGGRows = 64, kGGThreads = 128;
+
+__device__ __forceinline__ void mma_16816_bf16(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};\n"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+}  // namespace
+
+// Block: kGGCols output columns for all rows, row tiles of 64 (warp w: rows 16w .. 16w + 15). Shared memory: the
+// block's W_ov rows (kGGCols x d) and the tile's operand c (64 x d), both bf16 with rows padded by 8 elements.
+__global__ void __launch_bounds__(kGGThreads) k_gen_gate_tc(GateArgs a) {
+  extern __shared__ __align__(16) uint8_t smem_gg[];
+  const int d = a.d, ld = d + 8;
+  const int64_t M = a.B * a.L;
+  const int n0 = blockIdx.x * kGGCols;
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  const int g = lane >> 2, t4 = lane & 3;
+  __nv_bfloat16* s_w = reinterpret_cast<__nv_bfloat16*>(smem_gg);
+  __nv_bfloat16* s_c = s_w + kGGCols * ld;
+  float* s_sigma = reinterpret_cast<float*>(s_c + kGGRows * ld);
+  float* s_pt = s_sigma + kGGRows;
+  const __nv_bfloat16* W = reinterpret_cast<const __nv_bfloat16*>(a.wov);
+  // W_ov rows n0 .. n0 + 31 (16-byte chunks; rows past d are zero)
+  const int cpr = d / 8;
+  for (int e = tid; e < kGGCols * cpr; e += kGGThreads) {
+    const int r = e / cpr, c8 = e % cpr;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (n0 + r < d) v = __ldg(reinterpret_cast<const uint4*>(W + (int64_t)(n0 + r) * d) + c8);
+    *reinterpret_cast<uint4*>(s_w + r * ld + c8 * 8) = v;
+  }
+  for (int64_t r0 = 0; r0 < M; r0 += kGGRows) {
+    if (tid < kGGRows) {
+      float sg = 0.f, pt = 1.f;
+      if (r0 + tid < M) gate_of_token<true>(a, r0 + tid, &sg, &pt);
+      s_sigma[tid] = sg;
+      s_pt[tid] = pt;
+    }
+    __syncthreads();
+    const int cq = d / 4;
+    for (int e = tid; e < kGGRows * cq; e += kGGThreads) {
+      const int r = e / cq, c4 = e % cq;
+      float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (r0 + r < M) x = *reinterpret_cast<const float4*>(a.acc + (r0 + r) * d + c4 * 4);
+      const float p = s_pt[r];
+      __nv_bfloat162 lo = __floats2bfloat162_rn(__fdiv_rn(x.x, p), __fdiv_rn(x.y, p));
+      __nv_bfloat162 hi = __floats2bfloat162_rn(__fdiv_rn(x.z, p), __fdiv_rn(x.w, p));
+      *reinterpret_cast<__nv_bfloat162*>(s_c + r * ld + c4 * 4) = lo;
+      *reinterpret_cast<__nv_bfloat162*>(s_c + r * ld + c4 * 4 + 2) = hi;
+    }
+    __syncthreads();
+    float c[4][4] = {};
+    const __nv_bfloat16* ar0 = s_c + (wid * 16 + g) * ld + 2 * t4;
+    const __nv_bfloat16* ar1 = ar0 + 8 * ld;
+    for (int k0 = 0; k0 < d; k0 += 16) {
+      uint32_t af[4];
+      af[0] = *reinterpret_cast<const uint32_t*>(ar0 + k0);
+      af[1] = *reinterpret_cast<const uint32_t*>(ar1 + k0);
+      af[2] = *reinterpret_cast<const uint32_t*>(ar0 + k0 + 8);
+      af[3] = *reinterpret_cast<const uint32_t*>(ar1 + k0 + 8);
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) {
+        const __nv_bfloat16* br = s_w + (nt * 8 + g) * ld + k0 + 2 * t4;
+        mma_16816_bf16(c[nt], af, *reinterpret_cast<const uint32_t*>(br),
+                       *reinterpret_cast<const uint32_t*>(br + 8));
+      }
+    }
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) {
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const int r = wid * 16 + g + 8 * half;
+        const int64_t row = r0 + r;
+        if (row >= M) continue;
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int col = n0 + nt * 8 + 2 * t4 + e;
+          if (col >= d) continue;
+          const float o = round_bf16(c[nt][2 * half + e]);
+          const float add = round_bf16(__fmul_rn(s_sigma[r], o));
+          a.out[row * d + col] = __fadd_rn(a.h[row * d + col], add);
+        }
+      }
+    }
+    __syncthreads();
+  }
+}
+
+int launch_gen_gate(const GateArgs& a, bool half, cudaStream_t s) {
+  const int64_t M = a.B * a.L;
+  if (M == 0) return ASRN_OK;
+  if (half && a.d % 16 == 0) {
+    const int ld = a.d + 8;
+    const size_t smem = (size_t)(kGGCols + kGGRows) * ld * 2 + 2 * kGGRows * sizeof(float);
+    if (smem <= 220 * 1024) {
+      cudaFuncSetAttribute(k_gen_gate_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      k_gen_gate_tc<<<(unsigned)((a.d + kGGCols - 1) / kGGCols), kGGThreads, smem, s>>>(a);
+      return cudaGetLastError() == cudaSuccess ? ASRN_OK : ASRN_ERR_CUDA;
+    }
+  }
+  constexpr int kTM = 64, kTN = 64;
+  dim3 grid((unsigned)((a.d + kTN - 1) / kTN), (unsigned)((M + kTM - 1) / kTM));
+  if (half) k_gate_simt<true><<<grid, 256, 0, s>>>(a);
+  else k_gate_simt<false><<<grid, 256, 0, s>>>(a);
+  return cudaGetLastError() == cudaSuccess ? ASRN_OK : ASRN_ERR_CUDA;
+}
+
 }  // namespace asrn

@@ -133,6 +133,28 @@ struct GateArgs {
   float* sigma;            // tensor-core path: (M) gate values (workspace)
 };
 
+// Context + sign-hash projection of one new token per sequence (generation step).
+struct GenFrontArgs {
+  int64_t B;
+  int d, cf, m, T, Tw, nb, P;
+  const float* h;          // (B, d)
+  const float* e_t;        // (B, d) E of the new token
+  const float* e_prev;     // (B, d) E of the previous token
+  const int64_t* tokens;   // (B)
+  const float *ln_w, *ln_b, *w_reloj, *b_reloj, *g_w, *g_b;
+  const void* wctx;        // act (2cf, d)
+  const void* w1;          // act (3m, d)
+  const float* b1;         // (2m)
+  const void* w2;          // act (P, m)
+  const float* b2;         // (P)
+  float beta_max, log_alfa_min;
+  void *Qc, *Kc;           // act (B, cf)
+  double* beta;            // (B)
+  float *log_alfa, *glogit, *sig;  // (B)
+  void* phi;               // act (B, P)
+  uint16_t* ids;           // (B, T)
+};
+
 // One generation step of one layer: B sequences, the new token at position t of caches of `cap` positions.
 struct GenArgs {
   int64_t B, cap;
@@ -163,6 +185,8 @@ struct GenArgs {
 };
 
 int launch_context(const ContextArgs& a, bool half, cudaStream_t s);
+int launch_gen_front(const GenFrontArgs& a, bool half, cudaStream_t s);
+int launch_gen_gate(const GateArgs& a, bool half, cudaStream_t s);
 size_t hawkes_table_bytes(int64_t B, int n, int64_t cap);
 int launch_ring_build(int64_t B, int64_t L, int T, int nb, int C, int64_t n_valid, const int32_t* orden,
                       const uint16_t* ids_o, int32_t* ring, int32_t* count, cudaStream_t s);

@@ -6,8 +6,12 @@
 //   a_i = repetido_i * exp(-kappa_n * float(max(0, B_i - B_{i-1}))),  lambda_i = a_i (lambda_{i-1} + alfa_{i-1})
 //   hawkes / vistos scattered back to text order; streak S_t = r_t exp(-kappa_r beta_t) S_{t-1} + r_t with
 //   r_t = vistos of the longest order.
-// One block per (b, n) row sorts (key, position) pairs in shared memory with a bitonic network, then runs a
-// block-wide scan of affine maps over the sorted row.
+// Rows of at most 16384 positions: one block per (b, n) row sorts (key, position) pairs in shared memory with a
+// bitonic network, then runs a block-wide scan of affine maps over the sorted row.
+// Longer rows (workspace from repetition_workspace): tiles of 16384 are sorted the same way and written out, runs are
+// merged pairwise (merge path, log2(tiles) passes), then a tiled scan writes each tile's local inclusive maps and its
+// aggregate, and a last pass composes the aggregates of the earlier tiles into each element and scatters to text
+// order. Keys are unique as (key, position) pairs, so every correct sort gives the stable argsort of the reference.
 #include "common.cuh"
 #include "layout.h"
 
@@ -177,12 +181,234 @@ __global__ void __launch_bounds__(1024) k_racha(RepetitionArgs a) {
   }
 }
 
-size_t repetition_workspace(int64_t, int64_t, int) { return 0; }
+// ---- rows longer than kRepMaxL ---------------------------------------------------------------------------------------
 
-int launch_repetition(const RepetitionArgs& a, void*, size_t, cudaStream_t s) {
+constexpr int kRepTile = kRepMaxL;
+constexpr int kMergeItems = 8;
+
+struct RepLong {
+  uint64_t *k0, *k1;   // (rows, L) sortable keys, ping-pong
+  uint32_t *p0, *p1;   // (rows, L) positions, ping-pong
+  float2* vloc;        // (rows, L) tile-local inclusive maps (a, b)
+  float2* agg;         // (rows, tiles) tile aggregates
+};
+
+__device__ __forceinline__ double ngram_key_at(const float* sig, int64_t i, int ni, const double* c) {
+  double key = 0.0;
+  for (int j = 0; j <= ni; ++j) {
+    const int64_t t = i - j;
+    const double s = (t >= 0) ? (double)sig[t] : __longlong_as_double(0x7ff8000000000000ll);
+    key = __dadd_rn(key, __dmul_rn(s, c[j]));
+  }
+  return key;
+}
+
+__global__ void __launch_bounds__(1024) k_ngram_tile_sort(RepetitionArgs a, int64_t tiles, uint64_t* K, uint32_t* Pp) {
+  extern __shared__ __align__(16) char smem_raw[];
+  uint64_t* sk = reinterpret_cast<uint64_t*>(smem_raw);
+  uint32_t* sp = reinterpret_cast<uint32_t*>(sk + kRepTile);
+  const int64_t row = blockIdx.x / tiles, tile = blockIdx.x % tiles;
+  const int64_t b = row / a.n;
+  const int ni = (int)(row % a.n);
+  const int64_t L = a.L, base = tile * kRepTile;
+  const float* sig = a.sig + b * L;
+  for (int i = threadIdx.x; i < kRepTile; i += blockDim.x) {
+    const int64_t p = base + i;
+    if (p < L) {
+      const double key = ngram_key_at(sig, p, ni, a.c);
+      if (a.keys) a.keys[(b * L + p) * a.n + ni] = key;
+      sk[i] = sortable_key(key);
+      sp[i] = (uint32_t)p;
+    } else {
+      sk[i] = 0xFFFFFFFFFFFFFFFFull;
+      sp[i] = 0xFFFFFFFFu;
+    }
+  }
+  __syncthreads();
+  for (int k = 2; k <= kRepTile; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      for (int i = threadIdx.x; i < kRepTile; i += blockDim.x) {
+        const int ixj = i ^ j;
+        if (ixj > i) {
+          const uint64_t ka = sk[i], kb = sk[ixj];
+          const uint32_t pa = sp[i], pb = sp[ixj];
+          const bool up = (i & k) == 0;
+          if (pair_less(kb, pb, ka, pa) == up) {
+            sk[i] = kb; sk[ixj] = ka;
+            sp[i] = pb; sp[ixj] = pa;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+  const int64_t cnt = L - base < kRepTile ? L - base : kRepTile;
+  for (int i = threadIdx.x; i < cnt; i += blockDim.x) {
+    K[row * L + base + i] = sk[i];
+    Pp[row * L + base + i] = sp[i];
+  }
+}
+
+// Merge sorted runs of width w pairwise; each thread writes kMergeItems consecutive outputs of one pair, starting from
+// its merge-path diagonal (binary search).
+__global__ void __launch_bounds__(256) k_ngram_merge(const uint64_t* __restrict__ Kin, const uint32_t* __restrict__ Pin,
+                                                     uint64_t* __restrict__ Kout, uint32_t* __restrict__ Pout,
+                                                     int64_t rows, int64_t L, int64_t w) {
+  const int64_t per_row = (L + kMergeItems - 1) / kMergeItems;
+  const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (gid >= rows * per_row) return;
+  const int64_t row = gid / per_row;
+  const int64_t o0 = (gid % per_row) * kMergeItems;
+  const int64_t s = (o0 / (2 * w)) * (2 * w);
+  const int64_t la = L - s < w ? L - s : w;
+  const int64_t lb = L - s - la < w ? L - s - la : w;
+  const uint64_t* KA = Kin + row * L + s;
+  const uint32_t* PA = Pin + row * L + s;
+  const uint64_t* KB = KA + la;
+  const uint32_t* PB = PA + la;
+  const int64_t k = o0 - s;
+  const int64_t kend = (k + kMergeItems < la + lb) ? k + kMergeItems : la + lb;
+  int64_t lo = k - lb > 0 ? k - lb : 0, hi = k < la ? k : la;
+  while (lo < hi) {          // first i with A[i] > B[k - 1 - i]
+    const int64_t mid = (lo + hi) >> 1;
+    if (pair_less(KA[mid], PA[mid], KB[k - 1 - mid], PB[k - 1 - mid])) lo = mid + 1;
+    else hi = mid;
+  }
+  int64_t i = lo, j = k - lo;
+  uint64_t* ko = Kout + row * L + s;
+  uint32_t* po = Pout + row * L + s;
+  for (int64_t o = k; o < kend; ++o) {
+    const bool take_a = j >= lb || (i < la && pair_less(KA[i], PA[i], KB[j], PB[j]));
+    if (take_a) { ko[o] = KA[i]; po[o] = PA[i]; ++i; }
+    else { ko[o] = KB[j]; po[o] = PB[j]; ++j; }
+  }
+}
+
+// Affine element of sorted index i (asrn/estable.py:304-321).
+__device__ __forceinline__ Affine ngram_elem(const RepetitionArgs& a, const uint64_t* K, const uint32_t* Pp, int64_t b,
+                                             int64_t i, float kappa, bool* rep) {
+  const int64_t L = a.L;
+  *rep = i > 0 && K[i] == K[i - 1] && K[i] != 0xFFFFFFFFFFFFFFFFull;
+  if (!*rep) return Affine{0.f, 0.f};
+  const int64_t pc = Pp[i], pp = Pp[i - 1];
+  const double dB = fmax(a.Bt[b * L + pc] - a.Bt[b * L + pp], 0.0);
+  const float av = expf(__fmul_rn(-kappa, __double2float_rn(dB)));
+  return Affine{av, __fmul_rn(av, expf(a.log_alfa[b * L + pp]))};
+}
+
+constexpr int kScanItems = kRepTile / 1024;
+
+__global__ void __launch_bounds__(1024) k_ngram_scan_tile(RepetitionArgs a, int64_t tiles, const uint64_t* K,
+                                                          const uint32_t* Pp, float2* vloc, float2* agg) {
+  __shared__ Affine warp_agg[32];
+  const int64_t row = blockIdx.x / tiles, tile = blockIdx.x % tiles;
+  const int64_t b = row / a.n;
+  const int ni = (int)(row % a.n);
+  const int64_t L = a.L;
+  const float kappa = a.kappa[ni];
+  const uint64_t* Kr = K + row * L;
+  const uint32_t* Pr = Pp + row * L;
+  Affine v[kScanItems];
+  const int64_t i0 = tile * kRepTile + (int64_t)threadIdx.x * kScanItems;
+#pragma unroll
+  for (int k = 0; k < kScanItems; ++k) {
+    const int64_t i = i0 + k;
+    bool rep;
+    v[k] = (i < L) ? ngram_elem(a, Kr, Pr, b, i, kappa, &rep) : Affine{1.f, 0.f};
+  }
+  block_scan_affine<kScanItems>(v, warp_agg);
+#pragma unroll
+  for (int k = 0; k < kScanItems; ++k) {
+    const int64_t i = i0 + k;
+    if (i < L) vloc[row * L + i] = make_float2(v[k].a, v[k].b);
+  }
+  if (threadIdx.x == blockDim.x - 1) agg[row * tiles + tile] = make_float2(v[kScanItems - 1].a, v[kScanItems - 1].b);
+}
+
+__global__ void __launch_bounds__(1024) k_ngram_apply(RepetitionArgs a, int64_t tiles, const uint64_t* K,
+                                                      const uint32_t* Pp, const float2* vloc, const float2* agg) {
+  __shared__ Affine carry_s;
+  const int64_t row = blockIdx.x / tiles, tile = blockIdx.x % tiles;
+  const int64_t b = row / a.n;
+  const int ni = (int)(row % a.n);
+  const int64_t L = a.L;
+  if (threadIdx.x == 0) {
+    Affine c{1.f, 0.f};
+    for (int64_t q = 0; q < tile; ++q) {
+      const float2 g = agg[row * tiles + q];
+      c = compose(c, Affine{g.x, g.y});
+    }
+    carry_s = c;
+  }
+  __syncthreads();
+  const Affine carry = carry_s;
+  const uint64_t* Kr = K + row * L;
+  const uint32_t* Pr = Pp + row * L;
+  const int64_t end = (tile + 1) * kRepTile < L ? (tile + 1) * kRepTile : L;
+  for (int64_t i = tile * kRepTile + threadIdx.x; i < end; i += blockDim.x) {
+    const float2 lv = vloc[row * L + i];
+    const Affine s = compose(carry, Affine{lv.x, lv.y});
+    const bool rep = i > 0 && Kr[i] == Kr[i - 1] && Kr[i] != 0xFFFFFFFFFFFFFFFFull;
+    const int64_t pc = Pr[i];
+    a.hawkes[(b * L + pc) * a.n + ni] = s.b;
+    a.vistos[(b * L + pc) * a.n + ni] = rep ? 1 : 0;
+    if (a.orden_ng) a.orden_ng[(b * a.n + ni) * L + i] = (int32_t)pc;
+    if (a.repetido) a.repetido[(b * a.n + ni) * L + i] = rep ? 1 : 0;
+  }
+}
+
+static RepLong rep_long_layout(void* ws, int64_t rows, int64_t L) {
+  char* p = reinterpret_cast<char*>(ws);
+  const size_t E = (size_t)rows * L;
+  RepLong r;
+  size_t o = 0;
+  r.k0 = reinterpret_cast<uint64_t*>(p + o); o = align_up(o + E * 8);
+  r.k1 = reinterpret_cast<uint64_t*>(p + o); o = align_up(o + E * 8);
+  r.p0 = reinterpret_cast<uint32_t*>(p + o); o = align_up(o + E * 4);
+  r.p1 = reinterpret_cast<uint32_t*>(p + o); o = align_up(o + E * 4);
+  r.vloc = reinterpret_cast<float2*>(p + o); o = align_up(o + E * 8);
+  r.agg = reinterpret_cast<float2*>(p + o);
+  return r;
+}
+
+size_t repetition_workspace(int64_t B, int64_t L, int n) {
+  if (L <= kRepMaxL) return 0;
+  const size_t rows = (size_t)B * n, E = rows * (size_t)L;
+  const size_t tiles = (size_t)((L + kRepTile - 1) / kRepTile);
+  return align_up(E * 8) * 2 + align_up(E * 4) * 2 + align_up(E * 8) + align_up(rows * tiles * 8);
+}
+
+static int launch_repetition_long(const RepetitionArgs& a, void* ws, size_t ws_bytes, cudaStream_t s) {
+  if (a.L >= ((int64_t)1 << 31)) return ASRN_ERR_UNSUPPORTED;
+  if (!ws || ws_bytes < repetition_workspace(a.B, a.L, a.n)) return ASRN_ERR_WORKSPACE;
+  const int64_t rows = a.B * a.n, L = a.L;
+  const int64_t tiles = (L + kRepTile - 1) / kRepTile;
+  RepLong r = rep_long_layout(ws, rows, L);
+  const size_t smem = (size_t)kRepTile * 12;
+  cudaFuncSetAttribute(k_ngram_tile_sort, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  k_ngram_tile_sort<<<(unsigned)(rows * tiles), 1024, smem, s>>>(a, tiles, r.k0, r.p0);
+  uint64_t *kin = r.k0, *kout = r.k1;
+  uint32_t *pin = r.p0, *pout = r.p1;
+  const int64_t per_row = (L + kMergeItems - 1) / kMergeItems;
+  for (int64_t w = kRepTile; w < L; w <<= 1) {
+    k_ngram_merge<<<(unsigned)((rows * per_row + 255) / 256), 256, 0, s>>>(kin, pin, kout, pout, rows, L, w);
+    uint64_t* tk = kin; kin = kout; kout = tk;
+    uint32_t* tp = pin; pin = pout; pout = tp;
+  }
+  k_ngram_scan_tile<<<(unsigned)(rows * tiles), 1024, 0, s>>>(a, tiles, kin, pin, r.vloc, r.agg);
+  k_ngram_apply<<<(unsigned)(rows * tiles), 1024, 0, s>>>(a, tiles, kin, pin, r.vloc, r.agg);
+  return cudaGetLastError() == cudaSuccess ? ASRN_OK : ASRN_ERR_CUDA;
+}
+
+int launch_repetition(const RepetitionArgs& a, void* ws, size_t ws_bytes, cudaStream_t s) {
   if (a.B == 0 || a.L == 0) return ASRN_OK;
   if (a.n < 1 || a.n > kMaxSeen) return ASRN_ERR_ARG;
-  if (a.L > kRepMaxL) return ASRN_ERR_UNSUPPORTED;
+  if (a.L > kRepMaxL) {
+    const int st = launch_repetition_long(a, ws, ws_bytes, s);
+    if (st) return st;
+    k_racha<<<(unsigned)a.B, 1024, 0, s>>>(a);
+    return cudaGetLastError() == cudaSuccess ? ASRN_OK : ASRN_ERR_CUDA;
+  }
   int n2 = 1;
   while (n2 < a.L) n2 <<= 1;
   const size_t smem = (size_t)n2 * 12;

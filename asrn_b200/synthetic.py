@@ -68,6 +68,9 @@ def config_tokens(name, B=None, L=None, seed=0):
     if name == 'cfg3':
         x = zipf_tokens(B or 32, L or 8192, 50304, 1.1, seed)
         return plant_repeats(x, 0.20, 16, 256, seed=seed + 1)
+    if name == 'cfg5':
+        x = zipf_tokens(B or 64, L or 65536, 50304, 1.1, seed)
+        return plant_repeats(x, 0.20, 16, 256, seed=seed + 1)
     if name == 'cfg4':
         x = zipf_tokens(B or 1, L or 262144, 50304, 1.1, seed)
         return plant_repeats(x, 0.20, 32, 512, max_dist=200000, seed=seed + 1)

@@ -215,7 +215,7 @@ class Writer:
                 h = h + F.gelu(F.linear(win.reshape(B, -1), wc, bc))
                 h = h + F.linear(F.gelu(F.linear(_ln(blq.ln2, h).to(act), w1, b1)), w2, b2)
                 if i in m.pos_largo:
-                    h = self._step_layer(self.layers[j], e_t, h, tok)
+                    h = self._step_layer(self.layers[j], e_t, h.contiguous(), tok)
                     j += 1
             lg = F.linear(_ln(m.ln_f, h).to(act), sw.head)
             self.e_last.copy_(e_t)
@@ -223,40 +223,49 @@ class Writer:
         return lg
 
     def _step_layer(self, st, e_t, h, tok):
+        """One ASRN layer for the new tokens: front (context + hash), n-gram memory, candidate attention, gate."""
         capa, half, B = st.capa, self.half, self.B
         dev = tok.device
-        T, nb, C, n = capa.n_tablas, capa.n_bits, capa.chunk, capa.vistos
+        T, nb, C, n, cf, d = capa.n_tablas, capa.n_bits, capa.chunk, capa.vistos, capa.confirmar, capa.d
+        act = self._act()
         lib = _lib.lib()
         s = _lib.stream_ptr(dev)
-        hin = h.view(B, 1, -1)
-        ctx = stages.context(capa, hin, tok.view(B, 1), half=half)
-        hs = stages.hash(capa, torch.stack([self.e_last, e_t], 1), half=half)
-        phi_t = hs['phi'][:, 1].contiguous()
-        ids_t = hs['ids_rows'].view(B, T, 2)[:, :, 1].contiguous()
         w, _keep, prep = capa.prepared(dev, half)
         cfg = self._cfg(capa, B, 1)
-        tp = _lib.ptr(self.t_dev)
-        vistos = torch.empty(B, 1, n, dtype=torch.uint8, device=dev)
-        hawkes = torch.empty(B, 1, n, dtype=torch.float32, device=dev)
-        racha = torch.empty(B, 1, dtype=torch.float32, device=dev)
-        _lib.check(lib.asrn_gen_memory(ctypes_ref(cfg), ctypes_ref(w), _lib.ptr(prep), tp, self.cap,
-                                       _lib.ptr(self.sig), _lib.ptr(st.bt), _lib.ptr(st.la), _lib.ptr(ctx['beta']),
-                                       _lib.ptr(ctx['log_alfa']), _lib.ptr(st.table), st.hcap, _lib.ptr(st.racha),
+        cr, wr, pr, tp = ctypes_ref(cfg), ctypes_ref(w), _lib.ptr(prep), _lib.ptr(self.t_dev)
+        qc = torch.empty(B, cf, dtype=act, device=dev)
+        kc = torch.empty(B, cf, dtype=act, device=dev)
+        beta = torch.empty(B, dtype=torch.float64, device=dev)
+        la = torch.empty(B, dtype=torch.float32, device=dev)
+        glogit = torch.empty(B, dtype=torch.float32, device=dev)
+        sig = torch.empty(B, dtype=torch.float32, device=dev)
+        phi = torch.empty(B, T * nb, dtype=act, device=dev)
+        ids = torch.empty(B, T, dtype=torch.int16, device=dev)
+        _lib.check(lib.asrn_gen_front(cr, wr, pr, _lib.ptr(h), _lib.ptr(e_t), _lib.ptr(self.e_last), _lib.ptr(tok),
+                                      _lib.ptr(qc), _lib.ptr(kc), _lib.ptr(beta), _lib.ptr(la), _lib.ptr(glogit),
+                                      _lib.ptr(sig), _lib.ptr(phi), _lib.ptr(ids), s), 'asrn_gen_front')
+        vistos = torch.empty(B, n, dtype=torch.uint8, device=dev)
+        hawkes = torch.empty(B, n, dtype=torch.float32, device=dev)
+        racha = torch.empty(B, dtype=torch.float32, device=dev)
+        _lib.check(lib.asrn_gen_memory(cr, wr, pr, tp, self.cap, _lib.ptr(self.sig), _lib.ptr(st.bt), _lib.ptr(st.la),
+                                       _lib.ptr(beta), _lib.ptr(la), _lib.ptr(st.table), st.hcap, _lib.ptr(st.racha),
                                        _lib.ptr(vistos), _lib.ptr(hawkes), _lib.ptr(racha), s), 'asrn_gen_memory')
-        acc = torch.empty(B, 1, capa.d, dtype=torch.float32, device=dev)
-        hay = torch.empty(B, 1, T, dtype=torch.uint8, device=dev)
-        mx = torch.empty(B, 1, T, dtype=torch.float32, device=dev)
-        pk = torch.empty(B, 1, T, dtype=torch.float32, device=dev)
-        _lib.check(lib.asrn_gen_attend(ctypes_ref(cfg), ctypes_ref(w), _lib.ptr(prep), tp, self.cap, _lib.ptr(ids_t),
-                                       _lib.ptr(phi_t), _lib.ptr(ctx['Qc']), _lib.ptr(ctx['Kc']), _lib.ptr(st.ring),
-                                       _lib.ptr(self.sig), _lib.ptr(st.bt), _lib.ptr(st.la), _lib.ptr(st.phi),
-                                       _lib.ptr(st.kc), _lib.ptr(self.ea), _lib.ptr(acc), _lib.ptr(hay), _lib.ptr(mx),
-                                       _lib.ptr(pk), s), 'asrn_gen_attend')
-        h = stages.gate(capa, hin, ctx['glogit'], acc, hay, mx, pk, vistos, hawkes, racha, half=half)
+        acc = torch.empty(B, d, dtype=torch.float32, device=dev)
+        hay = torch.empty(B, T, dtype=torch.uint8, device=dev)
+        mx = torch.empty(B, T, dtype=torch.float32, device=dev)
+        pk = torch.empty(B, T, dtype=torch.float32, device=dev)
+        _lib.check(lib.asrn_gen_attend(cr, wr, pr, tp, self.cap, _lib.ptr(ids), _lib.ptr(phi), _lib.ptr(qc),
+                                       _lib.ptr(kc), _lib.ptr(st.ring), _lib.ptr(self.sig), _lib.ptr(st.bt),
+                                       _lib.ptr(st.la), _lib.ptr(st.phi), _lib.ptr(st.kc), _lib.ptr(self.ea),
+                                       _lib.ptr(acc), _lib.ptr(hay), _lib.ptr(mx), _lib.ptr(pk), s), 'asrn_gen_attend')
+        h_out = torch.empty(B, d, dtype=torch.float32, device=dev)
+        _lib.check(lib.asrn_gen_gate(cr, wr, pr, _lib.ptr(h), _lib.ptr(glogit), _lib.ptr(acc), _lib.ptr(hay),
+                                     _lib.ptr(mx), _lib.ptr(pk), _lib.ptr(vistos), _lib.ptr(hawkes), _lib.ptr(racha),
+                                     _lib.ptr(h_out), s), 'asrn_gen_gate')
         if not self.ajeno:
-            _lib.check(lib.asrn_gen_ring_insert(B, T, nb, C, tp, _lib.ptr(ids_t), _lib.ptr(st.ring),
+            _lib.check(lib.asrn_gen_ring_insert(B, T, nb, C, tp, _lib.ptr(ids), _lib.ptr(st.ring),
                                                 _lib.ptr(st.count), s), 'asrn_gen_ring_insert')
-        return h.view(B, -1)
+        return h_out
 
     def status(self):
         """Device status words of the layers (0 = ok; synchronises)."""
@@ -300,13 +309,17 @@ class _NgramIndex:
                 mp.setdefault(tuple(t[len(t) - self.n:-1]), set()).add(p)
 
     def next_mask(self, V, dev):
-        mask = torch.zeros(len(self.texts), V, dtype=torch.bool)
+        """(B, V) bool on dev: the tokens that followed each sequence's last n-1 tokens (built from index lists)."""
+        rows, cols = [], []
         for b, (t, mp) in enumerate(zip(self.texts, self.maps)):
             if len(t) >= self.n:
                 follow = mp.get(tuple(t[len(t) - self.n + 1:]), ())
-                if follow:
-                    mask[b, list(follow)] = True
-        return mask.to(dev)
+                rows += [b] * len(follow)
+                cols += list(follow)
+        mask = torch.zeros(len(self.texts), V, dtype=torch.bool, device=dev)
+        if rows:
+            mask[torch.tensor(rows, device=dev), torch.tensor(cols, device=dev)] = True
+        return mask
 
 
 def _brake(lg, recent, penalty, forbidden):
@@ -326,6 +339,16 @@ def _keep_quote_mass(q, p, quote):
     ok = (mq > 0) & (mq < 1)
     scale = torch.where(quote, mp / mq.clamp(min=1e-30), (1 - mp) / (1 - mq).clamp(min=1e-30))
     return torch.where(ok, q * scale, q)
+
+
+def _advance(gen, pending, shape):
+    """Advance the CPU generator by `pending` multinomial draws over `shape`: torch.multinomial(p, 1) draws one Exp(1)
+    per entry of p (argmax of p / q, q ~ Exp(1)), so skipping a draw and replaying it later leaves the generator where
+    the reference's is."""
+    if pending:
+        buf = torch.empty(shape)
+        for _ in range(pending):
+            buf.exponential_(1, generator=gen)
 
 
 def _sample(lg, temperature, top_k, gen, top_p=1.0, quote=None):
@@ -370,23 +393,41 @@ def escribir(modelo, inicio, n_nuevos=200, temperatura=0.8, top_k=40, semilla=0,
         if int(x.min()) < 0 or int(x.max()) >= V:
             raise ValueError(f'inicio: tokens outside [0, {V}) (min {int(x.min())}, max {int(x.max())})')
         lg = w.inicio(x, capacidad=L0 + n_nuevos)
-        text = x.new_empty(x.shape[0], L0 + n_nuevos)
+        B = x.shape[0]
+        text = x.new_empty(B, L0 + n_nuevos)
         text[:, :L0] = x
         length = L0
         quote_ng = _NgramIndex(x.cpu().tolist(), modelo.largos[0].vistos) if conservar_cita else None
-        written = _NgramIndex([[] for _ in range(x.shape[0])], no_repetir_ngramas) if no_repetir_ngramas else None
+        written = _NgramIndex([[] for _ in range(B)], no_repetir_ngramas) if no_repetir_ngramas else None
         steps = []
-        done = torch.zeros(x.shape[0], dtype=torch.bool, device=dev)
+        done = torch.zeros(B, dtype=torch.bool, device=dev)
+        # Greedy decoding (top_k = 1): the distribution is one-hot unless a row's maximum is tied, and then the
+        # multinomial draw returns the argmax whatever its random numbers; such steps take the argmax on the device
+        # and only count the skipped draw, replayed before the next real draw (ties, sampling).
+        greedy = top_k == 1
+        pending = 0
         for k in range(n_nuevos):
-            lg = lg.float().clone()
+            lg = lg.float()
             if devolver_logits:
-                steps.append(lg.cpu().clone())
+                steps.append(lg.cpu())
             braked = _brake(lg, text[:, max(0, length - ventana_pena):length], pena_repeticion,
                             written.next_mask(V, dev) if written else None)
             all_out = torch.isneginf(braked).all(-1, keepdim=True)
             lg = torch.where(all_out, lg, braked)
-            quote = quote_ng.next_mask(V, dev) if conservar_cita else None
-            nxt = _sample(lg, temperatura, top_k, gen, top_p, quote)
+            nxt = None
+            if greedy:
+                lt = lg / max(temperatura, 1e-6)
+                top = lt.max(-1, keepdim=True).values
+                tied = ((lt == top).sum(-1) > 1).any()
+                cand = lt.argmax(-1, keepdim=True)
+                if not bool(tied):
+                    nxt = cand
+                    pending += 1
+            if nxt is None:
+                _advance(gen, pending, tuple(lg.shape))
+                pending = 0
+                quote = quote_ng.next_mask(V, dev) if conservar_cita else None
+                nxt = _sample(lg, temperatura, top_k, gen, top_p, quote)
             if parar_en is not None:
                 nxt = torch.where(done.unsqueeze(1), torch.full_like(nxt, parar_en), nxt)
                 done = done | (nxt[:, 0] == parar_en)

@@ -13,6 +13,10 @@ Printed (rank 0, one JSON line): value = tokens/s of the whole job (all ranks' t
 K steps, inputs resident in HBM; the 805 MB E and h per GPU exceed the 126 MB L2, so no flush is needed), e2e = the
 same through ASRNLayer.forward with pinned host buffers and H2D/D2H copies in the timed region, roofline of the
 dominant kernel (candidate scoring, HBM-bound), the CPU baseline (the oracle port on the host cores), clocks.
+Generation leg (configuration 5, key "generation"): the configuration-3 model (random init), 64 sequences split over
+the GPUs with 65,536-token Zipf+repeat prompts, then greedy steps of the O(1) writer; value = device time per step
+(us per generated token of every sequence), with the same figure at 4,096 and 16,384-token prompts (flatness), the
+prefill rate, and the public generate() API end to end.
 --impl reference: times the CPU implementation of the path (oracle port) on the host cores instead.
 """
 import argparse
@@ -36,17 +40,23 @@ UNIT = 'tokens/s'
 # log_alfa / signature; plus the output row (768 * 2 B): T * (512 + 1536 + 72) + 1536 = 18,496 B.
 SCORE_BYTES_PER_TOKEN = 8 * (2 * 128 * 2 + D * 2 + 72) + D * 2
 LAYER_BYTES_PER_TOKEN = 34696
+# generation leg (configuration 5): the configuration-3 model, 64 sequences split over the GPUs, 65,536-token prompts,
+# greedy steps; flatness is checked at shorter prompts too
+GEN_B, GEN_L0, GEN_NEW, GEN_FLAT = 64, 65536, 1024, (4096, 16384)
 
 
 def parse():
     p = argparse.ArgumentParser()
     p.add_argument('--gpus', type=int, default=1)
-    p.add_argument('--steps', type=int, default=10)
+    p.add_argument('--steps', type=int, default=20)
     p.add_argument('--warmup', type=int, default=3)
     p.add_argument('--impl', default='ours', choices=['ours', 'reference'])
     p.add_argument('--batch', type=int, default=B_PER_GPU, help='sequences per GPU')
     p.add_argument('--seq', type=int, default=L_SEQ)
     p.add_argument('--no-cpu-baseline', action='store_true')
+    p.add_argument('--no-gen', action='store_true', help='skip the generation leg')
+    p.add_argument('--gen-prompt', type=int, default=GEN_L0, help='prompt length of the generation leg')
+    p.add_argument('--gen-steps', type=int, default=GEN_NEW, help='timed generation steps')
     return p.parse_args()
 
 
@@ -250,6 +260,66 @@ def load_profile_traffic():
         return None
 
 
+def run_generation(args, dev, rank, world):
+    """Generation leg: per prompt length, the prompt pass (prefill) then args.gen_steps greedy steps of the O(1)
+    writer, each step the CUDA-graph replay of the model's step plus a device argmax feeding the next token (no host
+    sync), timed with CUDA events; then the public API (generate, top_k=1) end to end at the shortest prompt."""
+    import torch
+    import asrn_b200
+    from asrn_b200 import synthetic
+    B = max(1, GEN_B // world)
+    torch.manual_seed(0)
+    m = asrn_b200.create_model(V=V, d=D, n_capas=12, semilla=0).to(dev).eval()
+    prompts = sorted(set([p for p in GEN_FLAT if p < args.gen_prompt] + [args.gen_prompt]))
+    out = {'sequences_per_gpu': B, 'prompts': {}}
+    for L0 in prompts:
+        x0 = torch.from_numpy(synthetic.config_tokens('cfg5', B=B, L=L0, seed=rank)).to(dev)
+        with torch.autocast('cuda', dtype=torch.bfloat16):
+            w = asrn_b200.Writer(m)
+            torch.cuda.synchronize()
+            p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            p0.record()
+            lg = w.inicio(x0, capacidad=L0 + args.gen_steps + 8)
+            p1.record()
+            nxt = lg.argmax(-1)
+            for _ in range(3):
+                nxt = w.paso(nxt, copiar=False).argmax(-1)
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(args.gen_steps):
+                nxt = w.paso(nxt, copiar=False).argmax(-1)
+            e1.record()
+            torch.cuda.synchronize()
+            status = w.status()
+            if any(status):
+                raise RuntimeError(f'generation step status {status}')
+            out['prompts'][str(L0)] = {'step_us': e0.elapsed_time(e1) / args.gen_steps * 1e3,
+                                       'prefill_tokens_per_s': B * L0 / (p0.elapsed_time(p1) * 1e-3)}
+            w.cerrar()
+            del w, lg, nxt, x0
+        torch.cuda.empty_cache()
+    # public API end to end (host tokens in, host tokens out, sampling as the reference's): per-token cost from two
+    # calls that differ only in the number of new tokens
+    L0 = prompts[0]
+    x0 = torch.from_numpy(synthetic.config_tokens('cfg5', B=B, L=L0, seed=rank))
+    n_a, n_b = 8, 72
+    times = []
+    with torch.autocast('cuda', dtype=torch.bfloat16):
+        asrn_b200.generate(m, x0, n_nuevos=4, top_k=1, devolver_logits=False)
+        for n in (n_a, n_b):
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            asrn_b200.generate(m, x0, n_nuevos=n, top_k=1, devolver_logits=False)
+            torch.cuda.synchronize()
+            times.append(time.perf_counter() - t0)
+    out['e2e_step_us'] = (times[1] - times[0]) / (n_b - n_a) * 1e6
+    out['e2e_prompt'] = L0
+    del m
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_ours(args):
     import numpy as np
     import torch
@@ -298,8 +368,8 @@ def run_ours(args):
         dist.barrier()
     clk = clocks.stop()
     # launches of our kernels per forward: context, clock, hash, bucket sort (1, or 3 when rows span tiles),
-    # scoring, n-gram rows, streak, gate
-    launches_per_step = 7 + (1 if args.seq <= 8192 else 3)
+    # scoring, n-gram rows, streak, gate prep, gate
+    launches_per_step = 8 + (1 if args.seq <= 8192 else 3)
 
     # dominant kernel (candidate scoring), timed on its launching stream with the forward's own intermediates
     with torch.no_grad():
@@ -344,10 +414,22 @@ def run_ours(args):
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1) / e_steps
 
-    times = torch.tensor([ms, e2e_ms, score_ms], device=dev, dtype=torch.float64)
+    del Eh, hh, xh, out_h, y, E, h, x
+    torch.cuda.empty_cache()
+    gen = None
+    if not args.no_gen:
+        gen = run_generation(args, dev, rank, world)
+    g_step = [gen['prompts'][k]['step_us'] for k in sorted(gen['prompts'], key=int)] if gen else []
+    vals = [ms, e2e_ms, score_ms] + g_step + ([gen['e2e_step_us']] if gen else [])
+    times = torch.tensor(vals, device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(times, op=dist.ReduceOp.MAX)
-    ms, e2e_ms, score_ms = times.tolist()
+    vals = times.tolist()
+    ms, e2e_ms, score_ms = vals[:3]
+    if gen:
+        for k, v in zip(sorted(gen['prompts'], key=int), vals[3:3 + len(g_step)]):
+            gen['prompts'][k]['step_us'] = v
+        gen['e2e_step_us'] = vals[-1]
     if rank == 0:
         import json as _json
         peaks = {}
@@ -378,6 +460,21 @@ def run_ours(args):
                'clocks': clk}
         if cpu_info is not None:
             out['cpu_baseline'] = cpu_info
+        if gen:
+            main = gen['prompts'][str(args.gen_prompt)]
+            out['generation'] = {
+                'metric': 'gen_us_per_token', 'value': main['step_us'], 'unit': 'us/token', 'higher_is_better': False,
+                'workload': 'cfg5: create_model(V=50304, d=768, n_capas=12) random init, %d sequences (%d per GPU), '
+                            'Zipf+repeat prompts of %d tokens, %d greedy steps (CUDA-graph step + device argmax), '
+                            'bf16 autocast' % (gen['sequences_per_gpu'] * world, gen['sequences_per_gpu'],
+                                               args.gen_prompt, args.gen_steps),
+                'step_us_by_prompt': {k: v['step_us'] for k, v in gen['prompts'].items()},
+                'prefill_tokens_per_s_by_prompt': {k: v['prefill_tokens_per_s'] * world
+                                                   for k, v in gen['prompts'].items()},
+                'tokens_per_s': gen['sequences_per_gpu'] * world / (main['step_us'] * 1e-6),
+                'e2e': {'value': gen['e2e_step_us'], 'unit': 'us/token',
+                        'api': 'asrn_b200.generate(top_k=1, devolver_logits=False), host prompt of %d tokens; '
+                               'per-token cost = difference of a 72- and an 8-token call / 64' % gen['e2e_prompt']}}
         print(json.dumps(out), flush=True)
     if world > 1:
         dist.barrier()

@@ -29,6 +29,8 @@
  *   asrn_gen_attend         _candidatos + _atender_cand        asrn/nucleo.py:1621-1631, asrn/estable.py:359-372
  *   asrn_gen_memory         _MemoriaHawkes.paso + _repeticion_o1  asrn/nucleo.py:1683-1714, 953-960
  *   asrn_gen_ring_insert    _anillo_meter                      asrn/nucleo.py:1610-1618
+ *   asrn_gen_front          _contexto + _phi_y_valores/_ids (one token)  asrn/estable.py:153-194, nucleo.py:639-664
+ *   asrn_gen_gate           _combinar (one token)              asrn/estable.py:376-403
  */
 #ifndef ASRN_B200_H
 #define ASRN_B200_H
@@ -203,6 +205,22 @@ size_t asrn_gen_hawkes_table_bytes(int64_t B, int32_t n, int64_t cap);
 int asrn_gen_hawkes_build(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared, int64_t L,
                           int64_t ld, const float* sig, const double* Bt, const float* log_alfa, const float* hawkes,
                           void* table, int64_t cap, void* stream);
+
+/* Context stage and sign-hash projection of one new token per sequence (cfg->B sequences, cfg->L = 1), with the
+ * whole-sequence stages' semantics (asrn_context, asrn_hash) for a token at t >= 1: h, e_t, e_prev (B, d) fp32 (the
+ * state, E of the token and of the previous token), tokens (B) int64 -> Qc, Kc (B, cf) in the compute type, beta (B)
+ * f64, log_alfa, glogit, sig (B) f32, phi (B, P) in the compute type, ids (B, T) uint16. One block per sequence,
+ * the weights read by every block (they stay in L2). */
+int asrn_gen_front(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared, const float* h,
+                   const float* e_t, const float* e_prev, const int64_t* tokens, void* Qc, void* Kc, double* beta,
+                   float* log_alfa, float* glogit, float* sig, void* phi, uint16_t* ids, void* stream);
+
+/* Gate of the new tokens (asrn_gate's semantics for cfg->B * cfg->L rows, no workspace): W_ov is spread over d / 32
+ * blocks. */
+int asrn_gen_gate(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared, const float* h,
+                  const float* glogit, const float* acc, const uint8_t* sen_hay, const float* sen_mx,
+                  const float* sen_pk, const uint8_t* vistos, const float* hawkes, const float* racha, float* h_out,
+                  void* stream);
 
 /* n-gram memory of the new token at position *t_pos (its signature already in sig_cache): appends its clock
  * Bt[t] = Bt[t-1] + beta_t and log_alfa_t to the caches, then vistos (B, n), hawkes (B, n) from the Hawkes table

@@ -114,6 +114,44 @@ def test_repetition_memory_matches_reference(name, cuda):
     assert rel_err(out['racha'].cpu().numpy(), z['racha']) <= 1e-5
 
 
+@pytest.mark.parametrize('L', [16385, 40000])
+def test_repetition_long_rows_match_oracle(L, cuda):
+    """Rows longer than one shared-memory tile (tile sort + merge passes + tiled scan): keys, sort permutation and
+    repeated flags bit-exact against the oracle; Hawkes intensity and streak within 1e-5. Repetitive text (12-token
+    vocabulary) so that n-gram groups are long and cross tile boundaries."""
+    import asrn_b200
+    from asrn_b200 import stages
+    from oracle import asrn_oracle as O
+    torch.manual_seed(3)
+    layer = asrn_b200.ASRNLayer(32)
+    g = torch.Generator().manual_seed(4)
+    with torch.no_grad():
+        for n_, p_ in layer.named_parameters():
+            if n_ in ('log_kappa', 'log_kappa_racha'):
+                p_.add_(torch.randn(p_.shape, generator=g) * 0.5)
+    params = {k: v.detach().numpy().copy() for k, v in layer.state_dict().items()}
+    rng = np.random.default_rng(5)
+    B = 2
+    tok = rng.integers(0, 12, size=(B, L)).astype(np.int64)
+    tok[:, L // 2:L // 2 + 5000] = tok[:, 100:5100]
+    sig = tok.astype(np.float32)
+    beta = rng.uniform(0.01, 2.0, size=(B, L))
+    Bt = np.cumsum(beta, axis=1)
+    log_alfa = rng.uniform(-3.0, 0.5, size=(B, L)).astype(np.float32)
+    lay = O.Layer(params, 32)
+    ref = O.repeticion(lay, sig, beta, Bt, log_alfa)
+    vis_ref, haw_ref, racha_ref = ref['vistos'], ref['hawkes'], ref['racha']
+    claves, orden_ref, rep_ref = ref['claves'], ref['orden_ng'], ref['repetido']
+    layer = layer.to(cuda)
+    out = stages.repetition(layer, _t(sig, cuda), _t(beta, cuda), _t(Bt, cuda), _t(log_alfa, cuda), debug=True)
+    assert np.array_equal(out['keys'].cpu().numpy(), claves, equal_nan=True)
+    assert np.array_equal(out['orden_ng'].cpu().numpy(), orden_ref)
+    assert np.array_equal(out['repetido'].cpu().numpy().astype(bool), rep_ref)
+    assert np.array_equal(out['vistos'].cpu().numpy().astype(bool), vis_ref.astype(bool))
+    assert rel_err(out['hawkes'].cpu().numpy(), haw_ref) <= 1e-5
+    assert rel_err(out['racha'].cpu().numpy(), racha_ref) <= 1e-5
+
+
 @pytest.mark.parametrize('name', LAYER_FIXTURES)
 def test_context_matches_reference(name, cuda):
     from asrn_b200 import stages
