@@ -78,6 +78,9 @@ _SIGS = {
     'asrn_gen_ring_insert': (ctypes.c_int, [ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                             _P, _P, _P, _P, _P]),
     'asrn_gen_front': (ctypes.c_int, [_P] * 16),
+    'asrn_shard_rows': (ctypes.c_int, [ctypes.c_int64, ctypes.c_int64, ctypes.c_int32, ctypes.c_int64, ctypes.c_int64,
+                                       _P, _P, ctypes.c_int64, _P, _P, _P, _P]),
+    'asrn_score_shard': (ctypes.c_int, [_P, _P, _P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64] + [_P] * 14),
     'asrn_gen_gate': (ctypes.c_int, [_P] * 14),
     'asrn_gate_workspace_bytes': (ctypes.c_size_t, [_P]),
     'asrn_gate': (ctypes.c_int, [_P] * 14 + [ctypes.c_size_t, _P]),

@@ -110,6 +110,7 @@ ScoreArgs score_args(const asrn_layer_config& c, const asrn_layer_weights& w, co
   const PreparedLayout pl = prepared_layout(c);
   ScoreArgs a{};
   a.B = c.B; a.L = c.L; a.d = (int)c.d; a.T = c.n_tablas; a.nb = c.n_bits; a.P = c.n_tablas * c.n_bits;
+  a.Lf = c.L; a.q_lo = 0; a.q_hi = c.L;
   a.C = c.chunk; a.cf = c.confirmar; a.K = c.sufijo;
   a.inv_temp_div = (float)sqrt((double)a.P);
   a.esc_c = (float)pow((double)c.confirmar, -0.5);
@@ -307,6 +308,35 @@ int asrn_score(const asrn_layer_config* cfg, const asrn_layer_weights* w, const 
       !sen_mx || !sen_pk)
     return ASRN_ERR_ARG;
   ScoreArgs a = score_args(*cfg, *w, reinterpret_cast<const char*>(prepared));
+  a.orden = orden; a.ids_o = ids_o; a.phi = phi; a.Qc = Qc; a.Kc = Kc; a.sig = sig; a.Bt = Bt; a.log_alfa = log_alfa;
+  a.Ea = Ea; a.acc = acc; a.sen_hay = sen_hay; a.sen_mx = sen_mx; a.sen_pk = sen_pk;
+  return launch_score(a, cfg->half, as_stream(stream));
+}
+
+int asrn_shard_rows(int64_t rows, int64_t L, int32_t C, int64_t q_lo, int64_t q_hi, const int32_t* orden,
+                    const uint16_t* ids_o, int64_t Lv, int32_t* orden_v, uint16_t* ids_v, int64_t* counts,
+                    void* stream) {
+  if (rows < 0 || L < 0 || C < 1 || C > 32 || q_lo < 0 || q_hi <= q_lo || q_hi > L || L >= ((int64_t)1 << 31) ||
+      (q_lo == 0 && q_hi == L) || (rows * L > 0 && (!orden || !ids_o)))
+    return ASRN_ERR_ARG;
+  if (orden_v ? (!ids_v || Lv < 1) : !counts) return ASRN_ERR_ARG;
+  const int32_t pad_pos = (int32_t)(q_lo > 0 ? 0 : q_hi);
+  return launch_shard_rows(rows, L, C, q_lo, q_hi, orden, ids_o, Lv, orden_v, ids_v, counts, pad_pos,
+                           as_stream(stream));
+}
+
+int asrn_score_shard(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared, int64_t L_feat,
+                     int64_t q_lo, int64_t q_hi, const int32_t* orden, const uint16_t* ids_o, const void* phi,
+                     const void* Qc, const void* Kc, const float* sig, const double* Bt, const float* log_alfa,
+                     const void* Ea, float* acc, uint8_t* sen_hay, float* sen_mx, float* sen_pk, void* stream) {
+  int st = check_config(cfg);
+  if (st) return st;
+  if ((st = check_weights(w))) return st;
+  if (!prepared || !orden || !ids_o || !phi || !Qc || !Kc || !sig || !Bt || !log_alfa || !Ea || !acc || !sen_hay ||
+      !sen_mx || !sen_pk || q_lo < 0 || q_hi <= q_lo || q_hi > L_feat || L_feat >= ((int64_t)1 << 31))
+    return ASRN_ERR_ARG;
+  ScoreArgs a = score_args(*cfg, *w, reinterpret_cast<const char*>(prepared));
+  a.Lf = L_feat; a.q_lo = q_lo; a.q_hi = q_hi;
   a.orden = orden; a.ids_o = ids_o; a.phi = phi; a.Qc = Qc; a.Kc = Kc; a.sig = sig; a.Bt = Bt; a.log_alfa = log_alfa;
   a.Ea = Ea; a.acc = acc; a.sen_hay = sen_hay; a.sen_mx = sen_mx; a.sen_pk = sen_pk;
   return launch_score(a, cfg->half, as_stream(stream));

@@ -315,7 +315,7 @@ int launch_gate(const GateArgs& a, bool half, cudaStream_t s) {
 // mma.sync. fp32 mode uses k_gate_simt.
 
 namespace {
-constexpr int kGGCols = 32, kGGRows = 64, kGGThreads = 128;
+constexpr int kGGCols = 32, kGGRows = 64, kGGThreads = 256, kGGUnroll = 8;
 
 __device__ __forceinline__ void mma_16816_bf16(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
   asm volatile(
@@ -324,10 +324,15 @@ __device__ __forceinline__ void mma_16816_bf16(float* c, const uint32_t* a, uint
       : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
+__device__ __forceinline__ void gg_cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+               : "memory");
+}
 }  // namespace
 
-// Block: kGGCols output columns for all rows, row tiles of 64 (warp w: rows 16w .. 16w + 15). Shared memory: the
-// block's W_ov rows (kGGCols x d) and the tile's operand c (64 x d), both bf16 with rows padded by 8 elements.
+// Block: kGGCols output columns for all rows, row tiles of 64; warp w: rows 16 (w % 4) .. + 15, columns
+// 16 (w / 4) .. + 15 of the block. Shared memory: the block's W_ov rows (kGGCols x d, by cp.async, in flight while
+// the gate scalars and the operand are computed) and the tile's operand c (64 x d), both bf16, rows padded by 8.
 __global__ void __launch_bounds__(kGGThreads) k_gen_gate_tc(GateArgs a) {
   extern __shared__ __align__(16) uint8_t smem_gg[];
   const int d = a.d, ld = d + 8;
@@ -340,14 +345,15 @@ __global__ void __launch_bounds__(kGGThreads) k_gen_gate_tc(GateArgs a) {
   float* s_sigma = reinterpret_cast<float*>(s_c + kGGRows * ld);
   float* s_pt = s_sigma + kGGRows;
   const __nv_bfloat16* W = reinterpret_cast<const __nv_bfloat16*>(a.wov);
-  // W_ov rows n0 .. n0 + 31 (16-byte chunks; rows past d are zero)
   const int cpr = d / 8;
   for (int e = tid; e < kGGCols * cpr; e += kGGThreads) {
     const int r = e / cpr, c8 = e % cpr;
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (n0 + r < d) v = __ldg(reinterpret_cast<const uint4*>(W + (int64_t)(n0 + r) * d) + c8);
-    *reinterpret_cast<uint4*>(s_w + r * ld + c8 * 8) = v;
+    __nv_bfloat16* dst = s_w + r * ld + c8 * 8;
+    if (n0 + r < d) gg_cp_async16(dst, W + (int64_t)(n0 + r) * d + c8 * 8);
+    else *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
   }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  const int rg = wid & 3, cg = wid >> 2;
   for (int64_t r0 = 0; r0 < M; r0 += kGGRows) {
     if (tid < kGGRows) {
       float sg = 0.f, pt = 1.f;
@@ -356,20 +362,33 @@ __global__ void __launch_bounds__(kGGThreads) k_gen_gate_tc(GateArgs a) {
       s_pt[tid] = pt;
     }
     __syncthreads();
-    const int cq = d / 4;
-    for (int e = tid; e < kGGRows * cq; e += kGGThreads) {
-      const int r = e / cq, c4 = e % cq;
-      float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (r0 + r < M) x = *reinterpret_cast<const float4*>(a.acc + (r0 + r) * d + c4 * 4);
-      const float p = s_pt[r];
-      __nv_bfloat162 lo = __floats2bfloat162_rn(__fdiv_rn(x.x, p), __fdiv_rn(x.y, p));
-      __nv_bfloat162 hi = __floats2bfloat162_rn(__fdiv_rn(x.z, p), __fdiv_rn(x.w, p));
-      *reinterpret_cast<__nv_bfloat162*>(s_c + r * ld + c4 * 4) = lo;
-      *reinterpret_cast<__nv_bfloat162*>(s_c + r * ld + c4 * 4 + 2) = hi;
+    // c = bf16(acc / pt): kGGUnroll independent 16-byte loads per thread in flight
+    const int cq = d / 4, tot = kGGRows * cq;
+    for (int e0 = tid; e0 < tot; e0 += kGGThreads * kGGUnroll) {
+      float4 x[kGGUnroll];
+#pragma unroll
+      for (int u = 0; u < kGGUnroll; ++u) {
+        const int e = e0 + u * kGGThreads;
+        const int r = e / cq, c4 = e % cq;
+        x[u] = (e < tot && r0 + r < M) ? __ldg(reinterpret_cast<const float4*>(a.acc + (r0 + r) * d + c4 * 4))
+                                       : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < kGGUnroll; ++u) {
+        const int e = e0 + u * kGGThreads;
+        if (e >= tot) continue;
+        const int r = e / cq, c4 = e % cq;
+        const float p = s_pt[r];
+        const __nv_bfloat162 lo = __floats2bfloat162_rn(__fdiv_rn(x[u].x, p), __fdiv_rn(x[u].y, p));
+        const __nv_bfloat162 hi = __floats2bfloat162_rn(__fdiv_rn(x[u].z, p), __fdiv_rn(x[u].w, p));
+        *reinterpret_cast<__nv_bfloat162*>(s_c + r * ld + c4 * 4) = lo;
+        *reinterpret_cast<__nv_bfloat162*>(s_c + r * ld + c4 * 4 + 2) = hi;
+      }
     }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
     __syncthreads();
-    float c[4][4] = {};
-    const __nv_bfloat16* ar0 = s_c + (wid * 16 + g) * ld + 2 * t4;
+    float c[2][4] = {};
+    const __nv_bfloat16* ar0 = s_c + (rg * 16 + g) * ld + 2 * t4;
     const __nv_bfloat16* ar1 = ar0 + 8 * ld;
     for (int k0 = 0; k0 < d; k0 += 16) {
       uint32_t af[4];
@@ -378,27 +397,26 @@ __global__ void __launch_bounds__(kGGThreads) k_gen_gate_tc(GateArgs a) {
       af[2] = *reinterpret_cast<const uint32_t*>(ar0 + k0 + 8);
       af[3] = *reinterpret_cast<const uint32_t*>(ar1 + k0 + 8);
 #pragma unroll
-      for (int nt = 0; nt < 4; ++nt) {
-        const __nv_bfloat16* br = s_w + (nt * 8 + g) * ld + k0 + 2 * t4;
+      for (int nt = 0; nt < 2; ++nt) {
+        const __nv_bfloat16* br = s_w + (cg * 16 + nt * 8 + g) * ld + k0 + 2 * t4;
         mma_16816_bf16(c[nt], af, *reinterpret_cast<const uint32_t*>(br),
                        *reinterpret_cast<const uint32_t*>(br + 8));
       }
     }
 #pragma unroll
-    for (int nt = 0; nt < 4; ++nt) {
+    for (int nt = 0; nt < 2; ++nt) {
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        const int r = wid * 16 + g + 8 * half;
+      for (int hf = 0; hf < 2; ++hf) {
+        const int r = rg * 16 + g + 8 * hf;
         const int64_t row = r0 + r;
-        if (row >= M) continue;
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int col = n0 + nt * 8 + 2 * t4 + e;
-          if (col >= d) continue;
-          const float o = round_bf16(c[nt][2 * half + e]);
-          const float add = round_bf16(__fmul_rn(s_sigma[r], o));
-          a.out[row * d + col] = __fadd_rn(a.h[row * d + col], add);
-        }
+        const int col = n0 + cg * 16 + nt * 8 + 2 * t4;
+        if (row >= M || col >= d) continue;
+        const float2 hv = *reinterpret_cast<const float2*>(a.h + row * d + col);
+        const float o0 = round_bf16(c[nt][2 * hf]), o1 = round_bf16(c[nt][2 * hf + 1]);
+        float2 ov;
+        ov.x = __fadd_rn(hv.x, round_bf16(__fmul_rn(s_sigma[r], o0)));
+        ov.y = __fadd_rn(hv.y, round_bf16(__fmul_rn(s_sigma[r], o1)));
+        *reinterpret_cast<float2*>(a.out + row * d + col) = ov;
       }
     }
     __syncthreads();
@@ -408,7 +426,7 @@ __global__ void __launch_bounds__(kGGThreads) k_gen_gate_tc(GateArgs a) {
 int launch_gen_gate(const GateArgs& a, bool half, cudaStream_t s) {
   const int64_t M = a.B * a.L;
   if (M == 0) return ASRN_OK;
-  if (half && a.d % 16 == 0) {
+  if (half && a.d % kGGCols == 0) {
     const int ld = a.d + 8;
     const size_t smem = (size_t)(kGGCols + kGGRows) * ld * 2 + 2 * kGGRows * sizeof(float);
     if (smem <= 220 * 1024) {

@@ -81,7 +81,9 @@ struct HashArgs {
 };
 
 struct ScoreArgs {
-  int64_t B, L;
+  int64_t B, L;            // sorted rows (B*T, L)
+  int64_t Lf;              // per-position features and the value rows: (B, Lf, ...), indexed by text position
+  int64_t q_lo, q_hi;      // slots whose position is in [q_lo, q_hi) are queries; outputs (B, q_hi - q_lo, ...)
   int d, T, nb, P, C, cf, K;
   float inv_temp_div;      // temperature (scores are divided by it)
   float esc_c;             // cf^-1/2
@@ -185,6 +187,9 @@ struct GenArgs {
 };
 
 int launch_context(const ContextArgs& a, bool half, cudaStream_t s);
+int launch_shard_rows(int64_t rows, int64_t L, int C, int64_t q_lo, int64_t q_hi, const int32_t* orden,
+                      const uint16_t* ids_o, int64_t Lv, int32_t* orden_v, uint16_t* ids_v, int64_t* counts,
+                      int32_t pad_pos, cudaStream_t s);
 int launch_gen_front(const GenFrontArgs& a, bool half, cudaStream_t s);
 int launch_gen_gate(const GateArgs& a, bool half, cudaStream_t s);
 size_t hawkes_table_bytes(int64_t B, int n, int64_t cap);

@@ -64,7 +64,7 @@ __device__ __forceinline__ void load_slots(const ScoreArgs& a, const ScoreSmem& 
     const int ri = (int)(s & (kRing - 1));
     const bool real = s >= 0 && s < a.L;
     const int pos = real ? a.orden[r * a.L + s] : 0;
-    const int64_t g = b * a.L + pos;
+    const int64_t g = b * a.Lf + pos;
     if (lane == 0) {
       S.pos[ri] = pos;
       S.id[ri] = real ? (int)a.ids_o[r * a.L + s] : -1;
@@ -73,7 +73,7 @@ __device__ __forceinline__ void load_slots(const ScoreArgs& a, const ScoreSmem& 
     }
     if (lane < S.K) {
       const int t = pos - 1 - lane;
-      S.pf[ri * S.K + lane] = (real && t >= 0) ? a.sig[b * a.L + t] : __int_as_float(0x7fc00000);
+      S.pf[ri * S.K + lane] = (real && t >= 0) ? a.sig[b * a.Lf + t] : __int_as_float(0x7fc00000);
     }
     if (real) {
       for (int p = lane; p < a.P; p += 32) S.phi[ri * S.Pp + p] = A::load(phi + g * a.P + p);
@@ -126,7 +126,8 @@ __global__ void __launch_bounds__(256) k_score_simt(ScoreArgs a) {
       const bool ok = lane < a.C && ks >= 0 && S.id[ks & (kRing - 1)] == idq;
       const int nv = __popc(__ballot_sync(0xffffffffu, ok));
       const int pos_q = S.pos[rq];
-      const int64_t gq = b * a.L + pos_q;
+      if (pos_q < a.q_lo || pos_q >= a.q_hi) continue;    // a key only (positions of another shard)
+      const int64_t gq = b * (a.q_hi - a.q_lo) + (pos_q - a.q_lo);
       if (nv == 0) {
         if (lane == 0) {
           a.sen_hay[gq * a.T + tau] = 0;
@@ -186,8 +187,8 @@ __global__ void __launch_bounds__(256) k_score_simt(ScoreArgs a) {
         for (int j = 0; j < nv; ++j) {
           const float wj = __shfl_sync(0xffffffffu, w, j);
           const int kp = __shfl_sync(0xffffffffu, kpos, j);
-          if (kp + 1 >= a.L) continue;
-          const typename A::T* row = Ea + (b * a.L + kp + 1) * (int64_t)d;
+          if (kp + 1 >= a.Lf) continue;
+          const typename A::T* row = Ea + (b * a.Lf + kp + 1) * (int64_t)d;
 #pragma unroll
           for (int i = 0; i < kMaxChunks; ++i) {
             const int c4 = lane + 32 * i;
@@ -211,7 +212,7 @@ __global__ void __launch_bounds__(256) k_score_simt(ScoreArgs a) {
           for (int j = 0; j < nv; ++j) {
             const float wj = __shfl_sync(0xffffffffu, w, j);
             const int kp = __shfl_sync(0xffffffffu, kpos, j);
-            if (kp + 1 < a.L) o = fmaf(wj, A::load(Ea + (b * a.L + kp + 1) * (int64_t)d + c), o);
+            if (kp + 1 < a.Lf) o = fmaf(wj, A::load(Ea + (b * a.Lf + kp + 1) * (int64_t)d + c), o);
           }
           red_add_f32(dst + c, o);
         }

@@ -21,7 +21,12 @@ constexpr int kR = 96;          // ring slots: the window plus the next sub-tile
 constexpr int kSpanTc = 512;    // sorted slots per block
 constexpr int kThreadsTc = 512; // 16 warps
 
+constexpr int kStage = 3;        // staging buffers of sorted-row entries (sub-tiles j + 1, j + 2 and one being freed)
+constexpr int kStageIds = 40;    // ids staged per sub-tile: its 32 slots and the next 8 (the `used` test reads s + 1)
+
 struct TcSmem {
+  int* st_pos;          // [kStage][kQ] orden entries of a staged sub-tile
+  uint16_t* st_id;      // [kStage][kStageIds] ids_o entries
   int* pos;
   int* id;
   int* used;
@@ -43,6 +48,8 @@ __host__ __device__ inline int pad16(int x) { return (x + 15) / 16 * 16; }
 __host__ __device__ inline size_t tc_smem_bytes(int P, int cf, int K, int dpart) {
   const int Pp = pad16(P) + 8, Cp = pad16(cf) + 8, Dp = dpart + 8;
   size_t b = 0;
+  b += kStage * kQ * 4 + kStage * kStageIds * 2;   // staging
+  b = (b + 15) / 16 * 16;
   b += kR * 8;                    // bt
   b += kR * 4 * 3;                // pos, id, used
   b += kR * 4;                    // la
@@ -62,6 +69,9 @@ __device__ inline TcSmem carve_tc(char* base, int P, int cf, int K, int dpart) {
   s.Dp = dpart + 8;
   s.K = K;
   char* p = base;
+  s.st_pos = reinterpret_cast<int*>(p); p += kStage * kQ * 4;
+  s.st_id = reinterpret_cast<uint16_t*>(p); p += kStage * kStageIds * 2;
+  p = base + ((p - base) + 15) / 16 * 16;
   s.bt = reinterpret_cast<double*>(p); p += kR * 8;
   s.pos = reinterpret_cast<int*>(p); p += kR * 4;
   s.id = reinterpret_cast<int*>(p); p += kR * 4;
@@ -86,6 +96,12 @@ __device__ __forceinline__ uint32_t su32(const void* p) { return (uint32_t)__cvt
 __device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(su32(dst)), "l"(src), "r"(valid ? 16 : 0)
                : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(su32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async8(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(su32(dst)), "l"(src) : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
@@ -114,34 +130,29 @@ __device__ __forceinline__ void red_add_v2(float* addr, float a, float b) {
 }
 }  // namespace
 
-// Slot scalars of slots [s_begin, s_end) of row r (one thread per slot) into their ring rows.
-__device__ __forceinline__ void tc_load_scalars(const ScoreArgs& a, const TcSmem& S, int64_t r, int64_t b,
-                                                int64_t s_begin, int64_t s_end) {
-  const int n = (int)(s_end - s_begin);
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const int64_t s = s_begin + i;
-    const int ri = ring(s);
-    const bool real = s >= 0 && s < a.L;
-    const int pos = real ? a.orden[r * a.L + s] : 0;
-    const int id = real ? (int)a.ids_o[r * a.L + s] : -1;
-    const bool used = real && s + 1 < a.L && (int)a.ids_o[r * a.L + s + 1] == id && pos + 1 < a.L;
-    const int64_t g = b * a.L + pos;
-    S.pos[ri] = pos;
-    S.id[ri] = id;
-    S.used[ri] = used ? 1 : 0;
-    S.bt[ri] = real ? a.Bt[g] : 0.0;
-    S.la[ri] = real ? a.log_alfa[g] : 0.f;
-    for (int c = 0; c < a.K; ++c) {
-      const int t = pos - 1 - c;
-      S.pf[ri * a.K + c] = (real && t >= 0) ? a.sig[b * a.L + t] : __int_as_float(0x7fc00000);
-    }
+// Stage 1 (two sub-tiles ahead): the sub-tile's 32 orden entries and 40 ids_o entries of row r, slots
+// [s0, s0 + 32 / 40), into staging buffer `buf` by 16-byte cp.async (zero-filled outside [0, L); rows are 16-byte
+// aligned: L % 8 == 0). Threads 0-7 copy orden, 8-12 ids.
+__device__ __forceinline__ void tc_stage1(const ScoreArgs& a, const TcSmem& S, int64_t r, int64_t s0, int buf) {
+  const int t = threadIdx.x;
+  if (t < kQ / 4) {
+    const int64_t s = s0 + 4 * t;
+    const bool ok = s >= 0 && s < a.L;
+    cp_async16(S.st_pos + buf * kQ + 4 * t, a.orden + r * a.L + (ok ? s : 0), ok);
+  } else if (t < kQ / 4 + kStageIds / 8) {
+    const int c = t - kQ / 4;
+    const int64_t s = s0 + 8 * c;
+    const bool ok = s >= 0 && s < a.L;
+    cp_async16(S.st_id + buf * kStageIds + 8 * c, a.ids_o + r * a.L + (ok ? s : 0), ok);
   }
 }
 
-// Vector rows (phi, Qc, Kc and the value row when used) of slots [s_begin, s_end): 16-byte asynchronous copies,
-// zero-filled where a slot is not real or its value row is not needed. Reads the slot scalars from shared memory.
-__device__ __forceinline__ void tc_load_vectors(const ScoreArgs& a, const TcSmem& S, int64_t b, int64_t s_begin,
-                                                int64_t s_end, int dp0, int dpart, int Ppad, int Cpad) {
+// Stage 2 (one sub-tile ahead): for the 32 slots [s0, s0 + 32) staged in `buf`, one warp per slot: lane 0 derives
+// (position, id, used) from the staging buffer and writes them to the slot's ring row; the lanes gather by cp.async
+// the clock (8 B), log_alfa and the K previous signatures (4 B each) of the position and its vector rows (phi, Qc,
+// Kc and, when some query can use it, the value row Ea[pos + 1]; 16 B each, zero-filled otherwise).
+__device__ __forceinline__ void tc_stage2(const ScoreArgs& a, const TcSmem& S, int64_t b, int64_t s0, int buf,
+                                          int dp0, int dpart, int Ppad, int Cpad) {
   const __nv_bfloat16* phi = reinterpret_cast<const __nv_bfloat16*>(a.phi);
   const __nv_bfloat16* Qc = reinterpret_cast<const __nv_bfloat16*>(a.Qc);
   const __nv_bfloat16* Kc = reinterpret_cast<const __nv_bfloat16*>(a.Kc);
@@ -149,13 +160,29 @@ __device__ __forceinline__ void tc_load_vectors(const ScoreArgs& a, const TcSmem
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
   const int cph = Ppad / 8, cpc = Cpad / 8, cpv = dpart / 8;
   const int per_slot = cph + 2 * cpc + cpv;
-  for (int64_t s = s_begin + wid; s < s_end; s += nw) {     // one warp per slot, lanes over its 16-byte chunks
+  for (int i = wid; i < kQ; i += nw) {
+    const int64_t s = s0 + i;
     const int ri = ring(s);
-    const bool real = S.id[ri] >= 0;
-    const int pos = S.pos[ri];
-    const bool used = S.used[ri] != 0;
-    const int64_t g = b * a.L + pos;
-    const __nv_bfloat16* vsrc = Ea + (b * a.L + (used ? pos + 1 : 0)) * (int64_t)a.d + dp0;
+    const bool real = s >= 0 && s < a.L;
+    const int pos = real ? S.st_pos[buf * kQ + i] : 0;
+    const int id = real ? (int)S.st_id[buf * kStageIds + i] : -1;
+    const bool used = real && s + 1 < a.L && (int)S.st_id[buf * kStageIds + i + 1] == id && pos + 1 < a.Lf;
+    const int64_t g = b * a.Lf + pos;
+    if (lane == 0) {
+      S.pos[ri] = pos;
+      S.id[ri] = id;
+      S.used[ri] = used ? 1 : 0;
+      if (real) cp_async8(S.bt + ri, a.Bt + g);
+      else S.bt[ri] = 0.0;
+      if (real) cp_async4(S.la + ri, a.log_alfa + g);
+      else S.la[ri] = 0.f;
+    } else if (lane <= a.K) {
+      const int c = lane - 1;
+      const int64_t t = (int64_t)pos - 1 - c;
+      if (real && t >= 0) cp_async4(S.pf + ri * a.K + c, a.sig + b * a.Lf + t);
+      else S.pf[ri * a.K + c] = __int_as_float(0x7fc00000);
+    }
+    const __nv_bfloat16* vsrc = Ea + (b * a.Lf + (used ? pos + 1 : 0)) * (int64_t)a.d + dp0;
     for (int c = lane; c < per_slot; c += 32) {
       if (c < cph) {
         const int col = c * 8;
@@ -193,25 +220,28 @@ __global__ void __launch_bounds__(kThreadsTc, 1) k_score_tc(ScoreArgs a, int nds
   const int C = a.C;
   const bool write_signals = part == 0;
 
-  // first window: slots [S0 - 32, S0 + 32)
-  tc_load_scalars(a, S, r, b, S0 - kQ, S0 + kQ);
+  // Pipeline over sub-tiles j = -1 (the window's first half, slots [S0 - 32, S0)), 0, 1, ...: staging buffer of
+  // sub-tile j = (j + 1) % kStage; stage 1 of j + 2 and stage 2 of j + 1 are issued while sub-tile j computes.
+  const int ntile = (int)((S1 - S0 + kQ - 1) / kQ);
+  tc_stage1(a, S, r, S0 - kQ, 0);
+  tc_stage1(a, S, r, S0, 1);
+  cp_async_commit();
+  cp_async_wait_all();
   __syncthreads();
-  tc_load_vectors(a, S, b, S0 - kQ, S0 + kQ, dp0, dpart, Ppad, Cpad);
+  tc_stage2(a, S, b, S0 - kQ, 0, dp0, dpart, Ppad, Cpad);
+  tc_stage2(a, S, b, S0, 1, dp0, dpart, Ppad, Cpad);
+  if (ntile > 1) tc_stage1(a, S, r, S0 + kQ, 2);
   cp_async_commit();
 
-  for (int64_t q0 = S0; q0 < S1; q0 += kQ) {
-    // ring rows: window key j (slot q0 - 32 + j) -> wrow(j); query i (slot q0 + i) -> wrow(32 + i)
+  for (int j = 0; j < ntile; ++j) {
+    const int64_t q0 = S0 + (int64_t)j * kQ;
+    // ring rows: window key k (slot q0 - 32 + k) -> wrow(k); query i (slot q0 + i) -> wrow(32 + i)
     const int rbase = ring(q0 - kQ);
-    auto wrow = [rbase](int j) { const int x = rbase + j; return x >= kR ? x - kR : x; };
+    auto wrow = [rbase](int k) { const int x = rbase + k; return x >= kR ? x - kR : x; };
     cp_async_wait_all();
     __syncthreads();
-    // prefetch the next sub-tile's slots into the free third of the ring while this one computes
-    const bool more = q0 + kQ < S1;
-    if (more) {
-      tc_load_scalars(a, S, r, b, q0 + kQ, q0 + 2 * kQ);
-    }
-    __syncthreads();
-    if (more) tc_load_vectors(a, S, b, q0 + kQ, q0 + 2 * kQ, dp0, dpart, Ppad, Cpad);
+    if (j + 1 < ntile) tc_stage2(a, S, b, q0 + kQ, (j + 2) % kStage, dp0, dpart, Ppad, Cpad);
+    if (j + 2 < ntile) tc_stage1(a, S, r, q0 + 2 * kQ, (j + 3) % kStage);
     cp_async_commit();
 
     // ---- scores: warp w -> m-tile (w >> 3), n-tile (w & 7) --------------------------------------------------------
@@ -276,7 +306,9 @@ __global__ void __launch_bounds__(kThreadsTc, 1) k_score_tc(ScoreArgs a, int nds
       const bool v0 = x0 != -INFINITY, v1 = x1 != -INFINITY;
       const bool anyv = __any_sync(0xffffffffu, v0 || v1);
       float w0 = 0.f, w1 = 0.f;
-      const bool mine = sq < S1;
+      const int posq = S.pos[wrow(kQ + qi)];
+      const bool mine = sq < S1 && posq >= a.q_lo && posq < a.q_hi;   // else a key only (another shard's position)
+      const int64_t gq = b * (a.q_hi - a.q_lo) + (posq - a.q_lo);
       if (anyv) {
         const float mx = warp_max(fmaxf(x0, x1));
         const float e0 = v0 ? expf(__fsub_rn(x0, mx)) : 0.f;
@@ -286,13 +318,11 @@ __global__ void __launch_bounds__(kThreadsTc, 1) k_score_tc(ScoreArgs a, int nds
         w1 = __fdiv_rn(e1, sum);
         const float peak = warp_max(fmaxf(w0, w1));
         if (lane == 0 && write_signals && mine) {
-          const int64_t gq = b * a.L + S.pos[wrow(kQ + qi)];
           a.sen_hay[gq * a.T + tau] = 1;
           a.sen_mx[gq * a.T + tau] = mx;
           a.sen_pk[gq * a.T + tau] = peak;
         }
       } else if (lane == 0 && write_signals && mine) {
-        const int64_t gq = b * a.L + S.pos[wrow(kQ + qi)];
         a.sen_hay[gq * a.T + tau] = 0;
         a.sen_mx[gq * a.T + tau] = kProhibido;
         a.sen_pk[gq * a.T + tau] = 0.f;
@@ -334,7 +364,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) k_score_tc(ScoreArgs a, int nds
         const int qd = lane & 3;
         const int rowq = qbase + (lane >> 2) + ((qd & 1) ? 8 : 0);
         const bool hasq = S.qhay[rowq] != 0;
-        const int64_t gq = b * a.L + S.pos[wrow(kQ + rowq)];
+        const int64_t gq = b * (a.q_hi - a.q_lo) + (S.pos[wrow(kQ + rowq)] - a.q_lo);
         float* dst = a.acc + gq * a.d + dp0 + (qd >> 1) * 4;
 #pragma unroll
         for (int j = 0; j < 6; ++j) {
@@ -356,7 +386,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) k_score_tc(ScoreArgs a, int nds
 
 bool score_tc_supported(const ScoreArgs& a) {
   return a.d % 64 == 0 && a.d <= 1024 && a.C <= 32 && a.P <= kMaxPhi && a.P % 8 == 0 && a.cf <= kMaxConfirm &&
-         a.cf % 8 == 0 && a.K <= kMaxSuffix;
+         a.cf % 8 == 0 && a.K <= kMaxSuffix && a.K <= 31 && a.L % 8 == 0;
 }
 
 int launch_score_tc(const ScoreArgs& a, cudaStream_t s) {

@@ -13,43 +13,50 @@ namespace asrn {
 
 namespace {
 
-constexpr int kFrontThreads = 256;
+constexpr int kFrontThreads = 512;
+constexpr int kDotWays = 4;   // dot products a warp advances together (independent loads in flight)
 
-// sum_j x[j] * w[j] over a row of d, x in shared memory (fp32), w in global memory; 16-byte weight loads when the row
-// is aligned. Result in every lane.
+// Element e of a 16-byte chunk of weights as fp32.
 template <typename W>
-__device__ __forceinline__ float dot_row(const float* x, const W* w, int d, int lane) {
+__device__ __forceinline__ float chunk_elem(const uint4& raw, int e) {
+  if constexpr (sizeof(W) == 2) {
+    const __nv_bfloat16* p = reinterpret_cast<const __nv_bfloat16*>(&raw);
+    return __bfloat162float(p[e]);
+  } else {
+    const float* p = reinterpret_cast<const float*>(&raw);
+    return p[e];
+  }
+}
+
+// r[k] = sum_j x_k[j] * w_k[j] for kDotWays rows of length d at once (x in shared memory, w in global memory, rows
+// 16-byte aligned and d a multiple of 16 / sizeof(W)); nrows <= kDotWays rows are valid. Results in every lane.
+template <typename W>
+__device__ __forceinline__ void dot_rows(const float* const* x, const W* const* w, int nrows, int d, int lane,
+                                         float* r) {
   constexpr int VW = 16 / sizeof(W);
-  float acc = 0.f;
-  int j0 = 0;
-  if (d % VW == 0 && (reinterpret_cast<uintptr_t>(w) & 15) == 0) {
-    const int nv = d / VW;
-    for (int v = lane; v < nv; v += 32) {
-      const uint4 raw = __ldg(reinterpret_cast<const uint4*>(w) + v);
-      const float* xv = x + v * VW;
-      if constexpr (sizeof(W) == 2) {
-        const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&raw);
+  float acc[kDotWays];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 f = __bfloat1622float2(p[e]);
-          acc = fmaf(xv[2 * e], f.x, acc);
-          acc = fmaf(xv[2 * e + 1], f.y, acc);
-        }
-      } else {
-        const float* f = reinterpret_cast<const float*>(&raw);
+  for (int k = 0; k < kDotWays; ++k) acc[k] = 0.f;
+  const int nv = d / VW;
+  for (int v = lane; v < nv; v += 32) {
+    uint4 raw[kDotWays];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) acc = fmaf(xv[e], f[e], acc);
+    for (int k = 0; k < kDotWays; ++k)
+      raw[k] = k < nrows ? __ldg(reinterpret_cast<const uint4*>(w[k]) + v) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int k = 0; k < kDotWays; ++k) {
+      float xv[VW];
+#pragma unroll
+      for (int e4 = 0; e4 < VW / 4; ++e4) {     // 16-byte shared-memory reads
+        const float4 q = *reinterpret_cast<const float4*>(x[k] + v * VW + 4 * e4);
+        xv[4 * e4] = q.x; xv[4 * e4 + 1] = q.y; xv[4 * e4 + 2] = q.z; xv[4 * e4 + 3] = q.w;
       }
+#pragma unroll
+      for (int e = 0; e < VW; ++e) acc[k] = fmaf(xv[e], chunk_elem<W>(raw[k], e), acc[k]);
     }
-    j0 = d;
   }
-  for (int j = j0 + lane; j < d; j += 32) {
-    float wv;
-    if constexpr (sizeof(W) == 2) wv = __bfloat162float(w[j]);
-    else wv = w[j];
-    acc = fmaf(x[j], wv, acc);
-  }
-  return warp_sum(acc);
+#pragma unroll
+  for (int k = 0; k < kDotWays; ++k) r[k] = warp_sum(acc[k]);
 }
 
 __device__ __forceinline__ float block_sum(float v, float* red) {
@@ -69,7 +76,7 @@ template <bool Half>
 __global__ void __launch_bounds__(kFrontThreads) k_gen_front(GenFrontArgs a) {
   using A = Act<Half>;
   using AT = typename A::T;
-  extern __shared__ float sm[];
+  extern __shared__ __align__(16) float sm[];
   const int d = a.d, cf = a.cf, m = a.m, P = a.P, nb = a.nb, T = a.T;
   const int64_t b = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, nw = kFrontThreads / 32;
@@ -80,7 +87,7 @@ __global__ void __launch_bounds__(kFrontThreads) k_gen_front(GenFrontArgs a) {
   float* s_p = s_e + d;            // act(E_{t-1})
   const int nq = 2 * cf + 3 + 3 * m;
   float* s_dot = s_p + d;          // nq dot products
-  float* s_hid = s_dot + nq;       // 2m hidden (after GELU)
+  float* s_hid = s_dot + ((nq + 3) & ~3);   // 2m hidden (after GELU), 16-byte aligned
   float* s_phi = s_hid + 2 * m;    // P
   float* s_red = s_phi + P;        // 32
 
@@ -108,19 +115,44 @@ __global__ void __launch_bounds__(kFrontThreads) k_gen_front(GenFrontArgs a) {
   __syncthreads();
 
   // dot products: [0, 2cf) Qc / Kc; 2cf, 2cf + 1 the clock projection; 2cf + 2 g(h); then the 3m hidden sums
-  // hp = act(E_t) . pal0, ca = act(E_t) . ctx0[:, :d], cb = act(E_{t-1}) . ctx0[:, d:]
+  // hp = act(E_t) . pal0, ca = act(E_t) . ctx0[:, :d], cb = act(E_{t-1}) . ctx0[:, d:]. The act-typed rows go
+  // kDotWays at a time per warp; the three fp32 rows one by one.
   const AT* wctx = reinterpret_cast<const AT*>(a.wctx);
   const AT* w1 = reinterpret_cast<const AT*>(a.w1);
-  for (int q = wid; q < nq; q += nw) {
-    float r;
-    if (q < 2 * cf) r = dot_row(s_hna, wctx + (int64_t)q * d, d, lane);
-    else if (q < 2 * cf + 2) r = dot_row(s_hn, a.w_reloj + (int64_t)(q - 2 * cf) * d, d, lane);
-    else if (q == 2 * cf + 2) r = dot_row(s_h, a.g_w, d, lane);
-    else {
-      const int i = q - (2 * cf + 3);
-      r = dot_row(i < 2 * m ? s_e : s_p, w1 + (int64_t)i * d, d, lane);
+  const int nact = 2 * cf + 3 * m;                        // act-typed rows: Qc/Kc then the hidden sums
+  for (int q0 = wid * kDotWays; q0 < nact; q0 += nw * kDotWays) {
+    const float* xs[kDotWays];
+    const AT* ws[kDotWays];
+    const int nrows = nact - q0 < kDotWays ? nact - q0 : kDotWays;
+#pragma unroll
+    for (int k = 0; k < kDotWays; ++k) {
+      const int q = q0 + (k < nrows ? k : 0);
+      if (q < 2 * cf) { xs[k] = s_hna; ws[k] = wctx + (int64_t)q * d; }
+      else {
+        const int i = q - 2 * cf;
+        xs[k] = i < 2 * m ? s_e : s_p;
+        ws[k] = w1 + (int64_t)i * d;
+      }
     }
-    if (lane == 0) s_dot[q] = r;
+    float r[kDotWays];
+    dot_rows<AT>(xs, ws, nrows, d, lane, r);
+    if (lane == 0) {
+      for (int k = 0; k < nrows; ++k) {
+        const int q = q0 + k;
+        s_dot[q < 2 * cf ? q : q + 3] = r[k];
+      }
+    }
+  }
+  if (wid == nw - 1) {
+    const float* xs[kDotWays] = {s_hn, s_hn, s_h, s_h};
+    const float* ws[kDotWays] = {a.w_reloj, a.w_reloj + d, a.g_w, a.g_w};
+    float r[kDotWays];
+    dot_rows<float>(xs, ws, 3, d, lane, r);
+    if (lane == 0) {
+      s_dot[2 * cf] = r[0];
+      s_dot[2 * cf + 1] = r[1];
+      s_dot[2 * cf + 2] = r[2];
+    }
   }
   __syncthreads();
 
@@ -143,15 +175,24 @@ __global__ void __launch_bounds__(kFrontThreads) k_gen_front(GenFrontArgs a) {
   __syncthreads();
   const AT* w2 = reinterpret_cast<const AT*>(a.w2);
   AT* phi = reinterpret_cast<AT*>(a.phi);
-  for (int o = wid; o < P; o += nw) {
-    const float* src = (o / nb < a.Tw) ? s_hid : s_hid + m;
-    float acc = 0.f;
-    for (int i = lane; i < m; i += 32) acc = fmaf(src[i], A::load(w2 + (int64_t)o * m + i), acc);
-    acc = warp_sum(acc);
+  for (int o0 = wid * kDotWays; o0 < P; o0 += nw * kDotWays) {
+    const float* xs[kDotWays];
+    const AT* ws[kDotWays];
+    const int nrows = P - o0 < kDotWays ? P - o0 : kDotWays;
+#pragma unroll
+    for (int k = 0; k < kDotWays; ++k) {
+      const int o = o0 + (k < nrows ? k : 0);
+      xs[k] = (o / nb < a.Tw) ? s_hid : s_hid + m;
+      ws[k] = w2 + (int64_t)o * m;
+    }
+    float r[kDotWays];
+    dot_rows<AT>(xs, ws, nrows, m, lane, r);
     if (lane == 0) {
-      const float val = act<Half>(acc + a.b2[o]);
-      s_phi[o] = val;
-      A::store(phi + b * P + o, val);
+      for (int k = 0; k < nrows; ++k) {
+        const float val = act<Half>(r[k] + a.b2[o0 + k]);
+        s_phi[o0 + k] = val;
+        A::store(phi + b * P + o0 + k, val);
+      }
     }
   }
   __syncthreads();
@@ -163,11 +204,14 @@ __global__ void __launch_bounds__(kFrontThreads) k_gen_front(GenFrontArgs a) {
 }
 
 size_t gen_front_smem(const GenFrontArgs& a) {
-  return sizeof(float) * (5 * (size_t)a.d + (2 * a.cf + 3 + 3 * a.m) + 2 * a.m + a.P + 32);
+  return sizeof(float) * (5 * (size_t)a.d + ((2 * a.cf + 3 + 3 * a.m + 3) & ~3) + 2 * a.m + a.P + 32);
 }
 
 int launch_gen_front(const GenFrontArgs& a, bool half, cudaStream_t s) {
   if (a.B == 0) return ASRN_OK;
+  // 16-byte weight rows: d and m multiples of 8 (bf16) / 4 (fp32); the prepared buffer's rows are then aligned
+  if (a.d % 8 != 0 || a.m % 8 != 0) return ASRN_ERR_UNSUPPORTED;
+  if ((reinterpret_cast<uintptr_t>(a.w_reloj) | reinterpret_cast<uintptr_t>(a.g_w)) & 15) return ASRN_ERR_ARG;
   const size_t smem = gen_front_smem(a);
   if (smem > 200 * 1024) return ASRN_ERR_UNSUPPORTED;
   if (half) {

@@ -138,12 +138,60 @@ __global__ void k_hawkes_fill(int64_t B, int64_t L, int64_t ld, int n, const dou
 }
 
 // One new token per sequence against its candidates (asrn/estable.py:359-372, asrn/nucleo.py:1621-1631).
-// Block (b, column slice of kGenCols): warp w scores the C ring slots of tables w, w + 8, ... (lane j = slot j; every
-// column block recomputes these few dot products), then the block sums att * E[k + 1] over all tables for its
-// columns: four thread groups take tables g, g + 4, ... in order and their partial sums are added in a fixed order,
-// so acc (B, d) is written once, deterministically, with no atomics.
+// Block (b, column slice of kGenCols), warp w = table w (and w + 8, ...): lane j scores ring slot j (its phi and Kc
+// rows by 16-byte loads, all in flight together), the warp's softmax, then the warp adds att * E[k + 1] of its 32
+// slots for the block's columns (lane: 4 consecutive columns; slots broadcast by shuffles, the 32 row loads unrolled).
+// The per-table partial sums are added in table order, so acc (B, d) is written once, deterministically.
 constexpr int kGenCols = 128;
 constexpr int kGenThreads = 256;
+constexpr int kGenWarps = kGenThreads / 32;
+
+template <bool Half>
+__device__ __forceinline__ void load4(const typename Act<Half>::T* p, float* v) {
+  if constexpr (Half) {
+    const uint2 raw = __ldg(reinterpret_cast<const uint2*>(p));
+    const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.x));
+    const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.y));
+    v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+  } else {
+    const float4 x = __ldg(reinterpret_cast<const float4*>(p));
+    v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
+  }
+}
+
+// dot of the shared-memory query x with a row of n act values (n a multiple of the 16-byte chunk): batches of 8
+// chunk loads in flight
+template <bool Half>
+__device__ __forceinline__ float dot_act_row(const float* x, const typename Act<Half>::T* row, int n) {
+  constexpr int VW = Half ? 8 : 4;
+  const int nc = n / VW;
+  float acc = 0.f;
+  for (int c0 = 0; c0 < nc; c0 += 8) {
+    uint4 raw[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      raw[u] = (c0 + u < nc) ? __ldg(reinterpret_cast<const uint4*>(row) + c0 + u) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      if (c0 + u >= nc) break;
+      const float* xc = x + (c0 + u) * VW;
+      if constexpr (Half) {
+        const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&raw[u]);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __bfloat1622float2(p[e]);
+          acc = fmaf(xc[2 * e], f.x, acc);
+          acc = fmaf(xc[2 * e + 1], f.y, acc);
+        }
+      } else {
+        const float* f = reinterpret_cast<const float*>(&raw[u]);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc = fmaf(xc[e], f[e], acc);
+      }
+    }
+  }
+  return acc;
+}
 
 template <bool Half>
 __global__ void __launch_bounds__(kGenThreads) k_gen_attend(GenArgs a) {
@@ -158,9 +206,7 @@ __global__ void __launch_bounds__(kGenThreads) k_gen_attend(GenArgs a) {
     return;
   }
   __shared__ float s_q[kMaxPhi + kMaxConfirm];
-  __shared__ float s_att[kMaxTables][32];
-  __shared__ int s_pos[kMaxTables][32];
-  __shared__ float s_part[4][kGenCols];
+  __shared__ __align__(16) float s_part[kMaxTables][kGenCols];
   const typename A::T* phi_q = reinterpret_cast<const typename A::T*>(a.phi_t) + b * P;
   const typename A::T* qc_q = reinterpret_cast<const typename A::T*>(a.qc_t) + b * cf;
   for (int i = threadIdx.x; i < P + cf; i += blockDim.x) s_q[i] = i < P ? A::load(phi_q + i) : A::load(qc_q + i - P);
@@ -176,18 +222,28 @@ __global__ void __launch_bounds__(kGenThreads) k_gen_attend(GenArgs a) {
   __syncthreads();
   const float* sg = a.sig_cache + b * a.cap;
   const double Bq = a.bt_cache[b * a.cap + t];
-  for (int tau = wid; tau < T; tau += kGenThreads / 32) {
+  float q_prev[kMaxSuffix];
+#pragma unroll
+  for (int c = 0; c < kMaxSuffix; ++c) q_prev[c] = (c < K && t - 1 - c >= 0) ? sg[t - 1 - c] : 0.f;
+  const typename A::T* Ea = reinterpret_cast<const typename A::T*>(a.ea_cache) + b * a.cap * (int64_t)a.d;
+  const int jc = col0 + 4 * lane;                  // this lane's 4 columns
+  const bool cols_ok = jc < a.d;
+  for (int tau = wid; tau < T; tau += kGenWarps) {
     const uint16_t id = a.ids_t[b * T + tau];
     const int32_t* slots = a.ring + ((b * T + tau) * ((int64_t)1 << a.nb) + id) * C;
     const int pos = lane < C ? slots[lane] : -1;
     const bool valid = pos >= 0;
+    const int pr = valid ? pos : 0;
+    const int64_t gk = b * a.cap + pr;
+    const float dphi = dot_act_row<Half>(s_q, reinterpret_cast<const typename A::T*>(a.phi_cache) + gk * P, P);
+    const float dqk = dot_act_row<Half>(s_q + P, reinterpret_cast<const typename A::T*>(a.kc_cache) + gk * cf, cf);
+    float k_prev[kMaxSuffix];
+#pragma unroll
+    for (int c = 0; c < kMaxSuffix; ++c) k_prev[c] = (c < K && pr - 1 - c >= 0) ? sg[pr - 1 - c] : 0.f;
+    const double bk = a.bt_cache[gk];
+    const float lak = a.la_cache[gk];
     float sc = -INFINITY;
     if (valid) {
-      const typename A::T* pk = reinterpret_cast<const typename A::T*>(a.phi_cache) + (b * a.cap + pos) * P;
-      const typename A::T* kk = reinterpret_cast<const typename A::T*>(a.kc_cache) + (b * a.cap + pos) * cf;
-      float dphi = 0.f, dqk = 0.f;
-      for (int p = 0; p < P; ++p) dphi = fmaf(s_q[p], A::load(pk + p), dphi);
-      for (int c = 0; c < cf; ++c) dqk = fmaf(s_q[P + c], A::load(kk + c), dqk);
       float t1;
       if (Half) {
         const float s1 = round_bf16(__fdiv_rn(round_bf16(dphi), a.inv_temp_div));
@@ -197,15 +253,16 @@ __global__ void __launch_bounds__(kGenThreads) k_gen_attend(GenArgs a) {
         t1 = __fadd_rn(__fdiv_rn(dphi, a.inv_temp_div), __fmul_rn(dqk, a.esc_c));
       }
       int ln = 0;
-      for (int c = 0; c < K; ++c) {
-        const int64_t tq = t - 1 - c, tk = (int64_t)pos - 1 - c;
-        if (tq >= 0 && tk >= 0 && sg[tq] == sg[tk]) ++ln; else break;
+      bool run = true;
+#pragma unroll
+      for (int c = 0; c < kMaxSuffix; ++c) {
+        if (c < K && run && t - 1 - c >= 0 && pr - 1 - c >= 0 && q_prev[c] == k_prev[c]) ++ln;
+        else run = false;
       }
       t1 = __fadd_rn(t1, a.w_suf[ln]);
       // _atender_cand: nucleo = log_alfa_k - (gamma / C) * float(B_q - B_k), added after the suffix weight
-      const float dB = __double2float_rn(Bq - a.bt_cache[b * a.cap + pos]);
-      const float nuc = __fsub_rn(a.la_cache[b * a.cap + pos], __fmul_rn(a.tasa[tau], dB));
-      sc = __fadd_rn(t1, nuc);
+      const float dB = __double2float_rn(Bq - bk);
+      sc = __fadd_rn(t1, __fsub_rn(lak, __fmul_rn(a.tasa[tau], dB)));
     }
     const bool any = __any_sync(0xffffffffu, valid);
     float att = 0.f;
@@ -225,86 +282,91 @@ __global__ void __launch_bounds__(kGenThreads) k_gen_attend(GenArgs a) {
       a.sen_mx[b * T + tau] = kProhibido;
       a.sen_pk[b * T + tau] = 0.f;
     }
-    s_att[tau][lane] = Half ? round_bf16(att) : att;
-    s_pos[tau][lane] = valid ? pos : -1;
-  }
-  __syncthreads();
-  // acc[b, j] = sum over tables and slots of att * E[pos + 1][j], j in this block's columns
-  const typename A::T* Ea = reinterpret_cast<const typename A::T*>(a.ea_cache) + b * a.cap * (int64_t)a.d;
-  const int g = threadIdx.x / (kGenThreads / 4);              // 4 groups of 64 threads
-  const int cl = threadIdx.x % (kGenThreads / 4);             // columns col0 + cl and col0 + cl + 64
-  const int j0 = col0 + cl, j1 = col0 + cl + kGenThreads / 4;
-  float o0 = 0.f, o1 = 0.f;
-  for (int tau = g; tau < T; tau += 4) {
-    for (int c = 0; c < C; ++c) {
-      const int pos = s_pos[tau][c];
-      if (pos < 0) continue;
-      const float w = s_att[tau][c];
-      const typename A::T* row = Ea + (int64_t)(pos + 1) * a.d;
-      if (j0 < a.d) o0 = fmaf(w, A::load(row + j0), o0);
-      if (j1 < a.d) o1 = fmaf(w, A::load(row + j1), o1);
+    if (Half) att = round_bf16(att);
+    // sum over this table's slots of att * E[pos + 1][cols] (invalid slots have att 0 and read row 1)
+    float o[4] = {0.f, 0.f, 0.f, 0.f};
+    if (any) {
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        float v[16][4];
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+          const int pc = __shfl_sync(0xffffffffu, pr, 16 * h + c);
+          if (cols_ok) load4<Half>(Ea + (int64_t)(pc + 1) * a.d + jc, v[c]);
+          else v[c][0] = v[c][1] = v[c][2] = v[c][3] = 0.f;
+        }
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+          const float w = __shfl_sync(0xffffffffu, att, 16 * h + c);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) o[e] = fmaf(w, v[c][e], o[e]);
+        }
+      }
     }
+    *reinterpret_cast<float4*>(&s_part[tau][4 * lane]) = make_float4(o[0], o[1], o[2], o[3]);
   }
-  s_part[g][cl] = o0;
-  s_part[g][cl + kGenThreads / 4] = o1;
   __syncthreads();
   if (threadIdx.x < kGenCols) {
     const int j = col0 + threadIdx.x;
     if (j < a.d) {
-      const float* q = &s_part[0][threadIdx.x];
-      a.acc[b * a.d + j] = __fadd_rn(__fadd_rn(__fadd_rn(q[0], q[kGenCols]), q[2 * kGenCols]), q[3 * kGenCols]);
+      float sum = 0.f;
+      for (int tau = 0; tau < T; ++tau) sum = __fadd_rn(sum, s_part[tau][threadIdx.x]);
+      a.acc[b * a.d + j] = sum;
     }
   }
 }
 
 // n-gram memory of the new token (asrn/nucleo.py:1683-1714) and the streak (asrn/nucleo.py:953-960).
-// One thread per sequence: its n orders in turn, then the streak from the longest order.
+// One thread per (sequence, order): each order has its own table; the order-0 thread appends the clock and
+// log_alfa of the new token, the last order's thread updates the streak from its "seen" flag.
 __global__ void k_gen_hawkes(GenArgs a, HawkesEntry* tab, int64_t hcap, const double* cv, const float* kappa,
                              const double* beta_t, const float* la_t, float* racha_state, uint8_t* vistos,
                              float* hawkes, float* racha_out, int* status) {
-  const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (b >= a.B) return;
   const int n = a.n;
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= a.B * n) return;
+  const int64_t b = i / n;
+  const int ni = (int)(i % n);
   const int64_t t = *a.t_pos;
   if (t < 1 || t >= a.cap) {
-    if (b == 0) atomicCAS(status, ASRN_OK, ASRN_ERR_ARG);
+    if (i == 0) atomicCAS(status, ASRN_OK, ASRN_ERR_ARG);
     return;
   }
-  // append the new token's clock (the inclusive fp64 sum, one more term) and log_alfa
+  // the new token's clock: the inclusive fp64 sum, one more term
   const double Bq = a.bt_w[b * a.cap + t - 1] + beta_t[b];
-  a.bt_w[b * a.cap + t] = Bq;
-  a.la_w[b * a.cap + t] = la_t[b];
-  const float alpha = expf(la_t[b]);
-  float r = 0.f;
-  for (int ni = 0; ni < n; ++ni) {
-    const double key = ngram_key(a.sig_cache + b * a.cap, t, ni, cv);
-    float lam = 0.f;
-    bool seen = false;
-    if (key == key) {
-      bool found;
-      HawkesEntry* tb = tab + (b * n + ni) * hcap;
-      const int64_t i = hawkes_slot(tb, hcap, key_bits(key), &found);
-      if (i < 0) {
-        atomicCAS(status, ASRN_OK, ASRN_ERR_WORKSPACE);
-      } else {
-        if (found) {
-          const float dB = __double2float_rn(Bq - tb[i].bu);
-          lam = __fmul_rn(expf(__fmul_rn(-kappa[ni], dB)), tb[i].a);
-          seen = true;
-        }
-        tb[i].bu = Bq;
-        tb[i].a = __fadd_rn(lam, alpha);
-      }
-    }
-    vistos[b * n + ni] = seen ? 1 : 0;
-    hawkes[b * n + ni] = lam;
-    if (ni == n - 1) r = seen ? 1.f : 0.f;
+  if (ni == 0) {
+    a.bt_w[b * a.cap + t] = Bq;
+    a.la_w[b * a.cap + t] = la_t[b];
   }
-  const float kr = kappa[n];
-  const float e = expf(__fmul_rn(-kr, (float)beta_t[b]));
-  const float s = __fmul_rn(r, __fadd_rn(__fmul_rn(e, racha_state[b]), 1.f));
-  racha_out[b] = s;
-  racha_state[b] = s;
+  const float alpha = expf(la_t[b]);
+  const double key = ngram_key(a.sig_cache + b * a.cap, t, ni, cv);
+  float lam = 0.f;
+  bool seen = false;
+  if (key == key) {
+    bool found;
+    HawkesEntry* tb = tab + (b * n + ni) * hcap;
+    const int64_t e = hawkes_slot(tb, hcap, key_bits(key), &found);
+    if (e < 0) {
+      atomicCAS(status, ASRN_OK, ASRN_ERR_WORKSPACE);
+    } else {
+      if (found) {
+        const float dB = __double2float_rn(Bq - tb[e].bu);
+        lam = __fmul_rn(expf(__fmul_rn(-kappa[ni], dB)), tb[e].a);
+        seen = true;
+      }
+      tb[e].bu = Bq;
+      tb[e].a = __fadd_rn(lam, alpha);
+    }
+  }
+  vistos[b * n + ni] = seen ? 1 : 0;
+  hawkes[b * n + ni] = lam;
+  if (ni == n - 1) {
+    const float r = seen ? 1.f : 0.f;
+    const float e = expf(__fmul_rn(-kappa[n], (float)beta_t[b]));
+    const float s = __fmul_rn(r, __fadd_rn(__fmul_rn(e, racha_state[b]), 1.f));
+    racha_out[b] = s;
+    racha_state[b] = s;
+  }
 }
 
 // Ring insert of position t for every (sequence, table) (asrn/nucleo.py:1610-1618).
@@ -361,7 +423,10 @@ int launch_hawkes_build(int64_t B, int64_t L, int64_t ld, int n, const float* si
 
 int launch_gen_attend(const GenArgs& a, bool half, cudaStream_t s) {
   if (a.B == 0) return ASRN_OK;
-  if (a.C > 32 || a.P > kMaxPhi || a.cf > kMaxConfirm || a.T > kMaxTables) return ASRN_ERR_UNSUPPORTED;
+  if (a.C > 32 || a.P > kMaxPhi || a.cf > kMaxConfirm || a.T > kMaxTables || a.K > kMaxSuffix) return ASRN_ERR_UNSUPPORTED;
+  // 16-byte rows of phi / Kc and 4-column value loads
+  const int vw = half ? 8 : 4;
+  if (a.P % vw != 0 || a.cf % vw != 0 || a.d % 4 != 0) return ASRN_ERR_UNSUPPORTED;
   dim3 grid((unsigned)a.B, (unsigned)((a.d + kGenCols - 1) / kGenCols));
   if (half) k_gen_attend<true><<<grid, kGenThreads, 0, s>>>(a);
   else k_gen_attend<false><<<grid, kGenThreads, 0, s>>>(a);
@@ -373,8 +438,10 @@ int launch_gen_memory(const GenArgs& a, void* table, int64_t hcap, const double*
                       float* racha, int* status, cudaStream_t s) {
   if (a.B == 0) return ASRN_OK;
   if (hcap <= 0 || (hcap & (hcap - 1)) != 0) return ASRN_ERR_ARG;
-  k_gen_hawkes<<<(unsigned)((a.B + 63) / 64), 64, 0, s>>>(a, reinterpret_cast<HawkesEntry*>(table), hcap, cv, kappa,
-                                                          beta_t, la_t, racha_state, vistos, hawkes, racha, status);
+  const int64_t threads = a.B * a.n;
+  k_gen_hawkes<<<(unsigned)((threads + 127) / 128), 128, 0, s>>>(a, reinterpret_cast<HawkesEntry*>(table), hcap, cv,
+                                                                kappa, beta_t, la_t, racha_state, vistos, hawkes,
+                                                                racha, status);
   return cudaGetLastError() == cudaSuccess ? ASRN_OK : ASRN_ERR_CUDA;
 }
 

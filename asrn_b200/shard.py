@@ -1,0 +1,194 @@
+"""Sequence-chunk sharding of one ASRN layer forward over several GPUs (one long sequence, e.g. 262,144 tokens).
+
+The reference runs a sequence on one device; here rank r of `world` owns the contiguous positions [c0, c1) of every
+sequence (L = world * Lc, equal chunks) and computes h' for them:
+
+  phase 1 (local)   the context stage and the sign-hash projection of the chunk (asrn/estable.py:153-194,
+                    asrn/nucleo.py:644-664); the hash of the chunk's first position needs E of the previous position,
+                    the one-row halo from rank r - 1 (zeros on rank 0, as the reference's E_{-1} = 0)
+  exchange (NCCL)   (1) the halo rows, (2) per sequence the chunk's sum of beta (fp64): rank r's clock is the
+                    exclusive sum of the earlier chunks plus its own cumulative sum (asrn/estable.py:418),
+                    (3) the chunk's bucket ids and per-position features (phi, Qc, Kc, signature, clock, beta,
+                    log_alfa, bf16 rows of E): all-gathers over NVLink; afterwards every rank holds them for all L
+  phase 2 (local)   sort of the full rows by bucket (asrn/estable.py:220-221); the shard's own rows: its slots plus
+                    each bucket's exclusive ring -- the <= C earlier-chunk slots some local query has as a candidate
+                    (asrn_shard_rows); candidate scoring of the local queries (asrn_score_shard); the n-gram memory
+                    over the full sequence (its Hawkes and streak scans carry state across chunks), kept for the
+                    chunk; the gate of the chunk.
+
+`forward` runs one rank under torch.distributed (NCCL); `forward_emulated` runs every rank's phases in one process
+(the exchange becomes concatenation), so that the sharded algorithm can be checked against the unsharded layer on one
+GPU. The exchange is NCCL collectives only (no peer-memory loads in the kernels).
+"""
+import torch
+
+from . import _lib, stages
+from .layer import compute_half, ctypes_ref
+
+_SEQ_KEYS = ('phi', 'Qc', 'Kc', 'sig', 'log_alfa', 'beta', 'Bt', 'Ea')
+
+
+def chunk_bounds(L, world, rank):
+    """[c0, c1) of rank `rank` when L positions are split in `world` equal contiguous chunks."""
+    if L % world:
+        raise ValueError(f'sequence length {L} is not a multiple of the {world} ranks')
+    Lc = L // world
+    return rank * Lc, (rank + 1) * Lc
+
+
+def _phase1(layer, E, h, tokens, E_halo, half):
+    """Local stages of one chunk. E, h (B, Lc, d) fp32, tokens (B, Lc) or None, E_halo (B, d): E of the position
+    before the chunk."""
+    ctx = stages.context(layer, h, tokens, E=None if tokens is not None else E, half=half)
+    Bt = stages.clock(ctx['beta'])
+    E_ext = torch.cat([E_halo.unsqueeze(1).to(E.dtype), E], 1)
+    hs = stages.hash(layer, E_ext, half=half)
+    B, Lc = E.shape[:2]
+    T = layer.n_tablas
+    loc = dict(phi=hs['phi'][:, 1:].contiguous(), Qc=ctx['Qc'], Kc=ctx['Kc'], sig=ctx['sig'],
+               log_alfa=ctx['log_alfa'], beta=ctx['beta'], Bt=Bt, Ea=hs['Ea'][:, 1:].contiguous(),
+               glogit=ctx['glogit'],
+               ids=hs['ids_rows'].view(B * T, Lc + 1)[:, 1:].contiguous())
+    return loc
+
+
+def _apply_clock_offsets(Bt_full, chunk_sums, Lc):
+    """Bt_full (B, L) of local cumulative sums per chunk; chunk_sums (world, B) fp64 -> global clock in place."""
+    world = chunk_sums.shape[0]
+    offs = torch.cumsum(chunk_sums, 0) - chunk_sums                # exclusive sum over the earlier chunks
+    Bt_full.view(Bt_full.shape[0], world, Lc).add_(offs.transpose(0, 1).unsqueeze(-1))
+    return Bt_full
+
+
+def _phase2(layer, loc, full, h, c0, c1, half):
+    """Scoring, n-gram memory and gate of the chunk [c0, c1) from the gathered full-sequence features."""
+    B, L = full['sig'].shape
+    T, nb, C = layer.n_tablas, layer.n_bits, layer.chunk
+    dev = h.device
+    lib = _lib.lib()
+    s = _lib.stream_ptr(dev)
+    orden, ids_o = stages.bucket_sort(full['ids'], nb)
+    rows = B * T
+    counts = torch.empty(rows, dtype=torch.int64, device=dev)
+    _lib.check(lib.asrn_shard_rows(rows, L, C, c0, c1, _lib.ptr(orden), _lib.ptr(ids_o), 0, None, None,
+                                   _lib.ptr(counts), s), 'asrn_shard_rows')
+    Lv = (max(1, int(counts.max())) + 31) // 32 * 32          # rows of whole 32-slot sub-tiles
+    orden_v = torch.empty(rows, Lv, dtype=torch.int32, device=dev)
+    ids_v = torch.empty(rows, Lv, dtype=torch.int16, device=dev)
+    _lib.check(lib.asrn_shard_rows(rows, L, C, c0, c1, _lib.ptr(orden), _lib.ptr(ids_o), Lv, _lib.ptr(orden_v),
+                                   _lib.ptr(ids_v), None, s), 'asrn_shard_rows')
+    Lc = c1 - c0
+    d = layer.d
+    w, _keep, prep = layer.prepared(dev, half)
+    cfg = _lib.make_config(layer, B, Lv, half)
+    acc = torch.zeros(B, Lc, d, dtype=torch.float32, device=dev)
+    hay = torch.empty(B, Lc, T, dtype=torch.uint8, device=dev)
+    mx = torch.empty(B, Lc, T, dtype=torch.float32, device=dev)
+    pk = torch.empty(B, Lc, T, dtype=torch.float32, device=dev)
+    _lib.check(lib.asrn_score_shard(ctypes_ref(cfg), ctypes_ref(w), _lib.ptr(prep), L, c0, c1, _lib.ptr(orden_v),
+                                    _lib.ptr(ids_v), _lib.ptr(full['phi']), _lib.ptr(full['Qc']),
+                                    _lib.ptr(full['Kc']), _lib.ptr(full['sig']), _lib.ptr(full['Bt']),
+                                    _lib.ptr(full['log_alfa']), _lib.ptr(full['Ea']), _lib.ptr(acc), _lib.ptr(hay),
+                                    _lib.ptr(mx), _lib.ptr(pk), s), 'asrn_score_shard')
+    rep = stages.repetition(layer, full['sig'], full['beta'], full['Bt'], full['log_alfa'])
+    vistos = rep['vistos'][:, c0:c1].contiguous()
+    hawkes = rep['hawkes'][:, c0:c1].contiguous()
+    racha = rep['racha'][:, c0:c1].contiguous()
+    return stages.gate(layer, h, loc['glogit'], acc, hay, mx, pk, vistos, hawkes, racha, half=half)
+
+
+def _check(layer, E, h, tokens):
+    if not (E.is_cuda and h.is_cuda):
+        raise RuntimeError('asrn_b200 runs on CUDA tensors only')
+    if E.shape != h.shape or E.dim() != 3 or E.shape[-1] != layer.d:
+        raise ValueError(f'E and h must be (B, L, {layer.d}); got {tuple(E.shape)} and {tuple(h.shape)}')
+    if tokens is not None and tokens.shape != E.shape[:2]:
+        raise ValueError(f'piezas must be {tuple(E.shape[:2])}; got {tuple(tokens.shape)}')
+
+
+@torch.no_grad()
+def forward_emulated(layer, E, h, tokens, world):
+    """Every rank's phases of the sharded forward in one process (the exchange becomes concatenation). E, h (B, L, d)
+    and tokens (B, L) of the whole sequences; returns h' (B, L, d) fp32."""
+    _check(layer, E, h, tokens)
+    half = compute_half('cuda')
+    B, L, d = E.shape
+    E, h = E.float(), h.float()
+    bounds = [chunk_bounds(L, world, r) for r in range(world)]
+    locs = []
+    for r, (c0, c1) in enumerate(bounds):
+        halo = E[:, c0 - 1] if c0 > 0 else torch.zeros(B, d, device=E.device)
+        locs.append(_phase1(layer, E[:, c0:c1].contiguous(), h[:, c0:c1].contiguous(),
+                            None if tokens is None else tokens[:, c0:c1].contiguous(), halo, half))
+    full = {k: torch.cat([lc[k] for lc in locs], 1) for k in _SEQ_KEYS}
+    full['ids'] = torch.cat([lc['ids'] for lc in locs], 1)
+    sums = torch.stack([lc['Bt'][:, -1] for lc in locs], 0)
+    _apply_clock_offsets(full['Bt'], sums, L // world)
+    outs = [_phase2(layer, lc, full, h[:, c0:c1].contiguous(), c0, c1, half) for lc, (c0, c1) in zip(locs, bounds)]
+    return torch.cat(outs, 1)
+
+
+def _gather_seq(x, world, group):
+    """All-gather of a per-chunk tensor (B, Lc, ...) into (B, world * Lc, ...) (rank order = position order)."""
+    import torch.distributed as dist
+    x = x.contiguous()
+    dt = x.dtype
+    xb = x.view(-1).view(torch.uint8)       # as bytes: int16 bucket ids have no NCCL / gloo type
+    if x.shape[0] == 1:                     # chunks are contiguous in position: one flat gather, no copy
+        out = torch.empty(world * xb.numel(), dtype=torch.uint8, device=x.device)
+        dist.all_gather_into_tensor(out, xb, group=group)
+        return out.view(dt).view((1, world * x.shape[1]) + tuple(x.shape[2:]))
+    parts = [torch.empty_like(xb) for _ in range(world)]
+    dist.all_gather(parts, xb, group=group)
+    return torch.cat([p.view(dt).view(x.shape) for p in parts], 1)
+
+
+def exchange_halo(last, world, rank, group=None):
+    """(B, d) E of this chunk's last position -> E of the position before this chunk (zeros on rank 0)."""
+    import torch.distributed as dist
+    lasts = [torch.empty_like(last) for _ in range(world)]
+    dist.all_gather(lasts, last.contiguous(), group=group)
+    return lasts[rank - 1] if rank > 0 else torch.zeros_like(last)
+
+
+def exchange_chunk_sums(chunk_sum, world, group=None):
+    """(B,) fp64 sum of this chunk's beta -> (world, B): every chunk's sum, in rank order."""
+    import torch.distributed as dist
+    flat = torch.empty(world * chunk_sum.numel(), dtype=chunk_sum.dtype, device=chunk_sum.device)
+    dist.all_gather_into_tensor(flat, chunk_sum.contiguous().view(-1), group=group)
+    return flat.view((world,) + tuple(chunk_sum.shape))
+
+
+def exchange_ids(ids_rows, B, T, world, group=None):
+    """(B*T, Lc) bucket ids of this chunk -> (B*T, world*Lc) of the whole sequences."""
+    Lc = ids_rows.shape[1]
+    ids_pm = ids_rows.view(B, T, Lc).permute(0, 2, 1)                  # (B, Lc, T) position-major
+    return _gather_seq(ids_pm, world, group).permute(0, 2, 1).reshape(B * T, world * Lc).contiguous()
+
+
+@torch.no_grad()
+def forward(layer, E, h, tokens=None, group=None):
+    """One rank of the sharded forward under torch.distributed: E, h (B, Lc, d), tokens (B, Lc) are this rank's chunk
+    of every sequence (chunks in rank order); returns h' (B, Lc, d) fp32 for the chunk. Every rank calls it with the
+    same shapes; the collectives are the same on every rank, in the same order."""
+    import torch.distributed as dist
+    _check(layer, E, h, tokens)
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    half = compute_half('cuda')
+    B, Lc, d = E.shape
+    L = world * Lc
+    c0, c1 = rank * Lc, (rank + 1) * Lc
+    E, h = E.float().contiguous(), h.float().contiguous()
+    if world == 1:
+        return layer(E, h, tokens)
+    # (1) halo rows: E of every chunk's last position
+    halo = exchange_halo(E[:, -1], world, rank, group)
+    loc = _phase1(layer, E, h, tokens, halo, half)
+    # (2) chunk sums of beta (= the last local clock value) -> clock offsets
+    sums = exchange_chunk_sums(loc['Bt'][:, -1], world, group)
+    # (3) bucket ids and features of every position
+    full = {k: _gather_seq(loc[k], world, group) for k in _SEQ_KEYS}
+    full['ids'] = exchange_ids(loc['ids'], B, layer.n_tablas, world, group)
+    _apply_clock_offsets(full['Bt'], sums, Lc)
+    return _phase2(layer, loc, full, h, c0, c1, half)

@@ -54,6 +54,9 @@ def parse():
     p.add_argument('--batch', type=int, default=B_PER_GPU, help='sequences per GPU')
     p.add_argument('--seq', type=int, default=L_SEQ)
     p.add_argument('--no-cpu-baseline', action='store_true')
+    p.add_argument('--workload', default='cfg3', choices=['cfg3', 'cfg4'],
+                   help='cfg3: the batch-sharded layer metric (default); cfg4: one 262,144-token sequence, d=512, '
+                        'sequence-sharded over the GPUs')
     p.add_argument('--no-gen', action='store_true', help='skip the generation leg')
     p.add_argument('--gen-prompt', type=int, default=GEN_L0, help='prompt length of the generation leg')
     p.add_argument('--gen-steps', type=int, default=GEN_NEW, help='timed generation steps')
@@ -73,13 +76,13 @@ def config(args, n):
 # inputs
 # ---------------------------------------------------------------------------------------------------------------------
 
-def make_layer_params(seed=0):
-    """Random-init ASRNLayer(768) weights with the neutral (zero-init) parameters moved off zero (the reference tests'
-    recipe), as a state_dict of CPU tensors."""
+def make_layer_params(seed=0, d=D):
+    """Random-init ASRNLayer(d) weights with the neutral (zero-init) parameters moved off zero (the reference tests'
+    recipe)."""
     import torch
     import asrn_b200
     torch.manual_seed(seed)
-    layer = asrn_b200.ASRNLayer(D)
+    layer = asrn_b200.ASRNLayer(d)
     g = torch.Generator().manual_seed(seed + 1)
     with torch.no_grad():
         for n, p in layer.named_parameters():
@@ -164,7 +167,7 @@ def _oracle_one(payload):
     sys.path.insert(0, HERE)
     from oracle import asrn_oracle as O
     params, x, E, h = payload
-    lay = O.Layer(params, D)
+    lay = O.Layer(params, E.shape[-1])
     t0 = time.perf_counter()
     O.layer_forward_fast(lay, E, h, x, half=True)
     return time.perf_counter() - t0
@@ -251,11 +254,11 @@ def run_reference(args):
 
 def load_profile_traffic():
     """Per-launch DRAM bytes of the scoring kernel from the committed ncu summary (profiles/), or None."""
-    p = os.path.join(HERE, 'profiles', 'traffic.json')
+    p = os.path.join(HERE, 'profiles', 'k_score_tc_cfg3_traffic.json')
     try:
         with open(p) as f:
             t = json.load(f)
-        return t.get('score_bytes_per_token')
+        return t.get('dram_bytes_per_token')
     except (OSError, ValueError):
         return None
 
@@ -482,10 +485,139 @@ def run_ours(args):
     return 0
 
 
+D4, L4 = 512, 262144
+CFG4_BYTES_PER_TOKEN = 24968     # algorithmic HBM bytes per token of one layer forward at d=512, bf16, fp32 E/h
+
+
+def run_cfg4(args):
+    """Configuration 4: one sequence of L4 tokens, ASRNLayer(512), bf16 autocast, sequence-sharded over the GPUs
+    (asrn_b200.shard: halo + clock-offset + feature all-gathers over NCCL); strong scaling. value = tokens of the
+    sequence per second (max-over-ranks device time of a step, exchange included)."""
+    import datetime
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    rank, world, local = dist_env()
+    if world > 1:
+        dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=120))
+    torch.cuda.set_device(local)
+    dev = torch.device('cuda', local)
+    from asrn_b200 import shard, synthetic
+    L = args.seq if args.seq != L_SEQ else L4
+    layer = make_layer_params(d=D4).to(dev).eval()
+    x = synthetic.config_tokens('cfg4', B=1, L=L, seed=0)
+    g = np.random.default_rng(7)
+    table = (g.standard_normal((V, D4)) * 0.02).astype(np.float32)
+    c0, c1 = shard.chunk_bounds(L, world, rank)
+    xc = np.ascontiguousarray(x[:, c0:c1])
+    Ec = table[xc]
+    hc = (Ec + np.random.default_rng(8 + rank).standard_normal(Ec.shape).astype(np.float32) * 0.5).astype(np.float32)
+    cpu_info = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        seg = 16384
+        nseg = max(1, min(host_cores(), L // seg, 16))
+        params = {k: v.detach().cpu().numpy() for k, v in layer.state_dict().items()}
+        xs = x[:, :nseg * seg].reshape(nseg, seg)
+        Es = table[xs]
+        hs = (Es + np.random.default_rng(9).standard_normal(Es.shape).astype(np.float32) * 0.5).astype(np.float32)
+        cpu_info = cpu_baseline(params, xs, Es, hs, seg)
+        cpu_info['sample'] = ('%d segments of %d tokens of the sequence, each run as its own sequence, one per host '
+                              'process (numpy oracle port, bf16 autocast emulated)' % (nseg, seg))
+    xd, Ed, hd = (torch.from_numpy(a).to(dev) for a in (xc, Ec, hc))
+
+    def step():
+        with torch.no_grad(), torch.autocast('cuda', dtype=torch.bfloat16):
+            if world == 1:
+                return layer(Ed, hd, xd)
+            return shard.forward(layer, Ed, hd, xd)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(args.steps):
+        y = step()
+    t1.record()
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1)
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    # end to end: this rank's chunk from pinned host buffers, h' back to the host
+    xh, Eh, hh = (torch.from_numpy(a).pin_memory() for a in (xc, Ec, hc))
+    out_h = torch.empty(hh.shape, dtype=torch.float32).pin_memory()
+
+    def e2e_step():
+        xe, Ee, he = xh.to(dev, non_blocking=True), Eh.to(dev, non_blocking=True), hh.to(dev, non_blocking=True)
+        with torch.no_grad(), torch.autocast('cuda', dtype=torch.bfloat16):
+            ye = layer(Ee, he, xe) if world == 1 else shard.forward(layer, Ee, he, xe)
+        out_h.copy_(ye, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_steps = max(2, min(args.steps, 5))
+    e0.record()
+    for _ in range(e_steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / e_steps
+    times = torch.tensor([ms, e2e_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    ms, e2e_ms = times.tolist()
+    if rank == 0:
+        peaks = {}
+        try:
+            with open(os.path.join(HERE, 'MEASURED_PEAKS.json')) as f:
+                peaks = json.load(f)
+        except (OSError, ValueError):
+            pass
+        hbm = peaks.get('hbm_gbs', 6650.0)
+        step_s = ms / args.steps * 1e-3
+        achieved = CFG4_BYTES_PER_TOKEN * (L // world) / step_s / 1e9
+        out = {'metric': METRIC, 'value': L / step_s, 'unit': UNIT, 'n_gpus': world, 'steps': args.steps,
+               'warmup': max(3, args.warmup), 'ms_per_step': ms / args.steps, 'higher_is_better': True,
+               'scaling': 'strong', 'vs_baseline': None, 'dtype': 'bf16', 'data': 'synthetic',
+               'config': {'workload': 'cfg4 layer: ASRNLayer(512) forward, 1 x %d tokens, bf16 autocast, fp32 E/h'
+                                      % L, 'global_batch': 1, 'seq_len': L, 'd': D4, 'vocab': V,
+                          'parallelism': ('sequence-sharded over %d GPUs (NCCL all-gathers of the halo, clock '
+                                          'offsets and per-position features)' % world) if world > 1 else 'single GPU',
+                          'l2': 'inputs larger than L2 (E and h are %.0f MB each per GPU), no flush'
+                                % (Ec.nbytes / 1e6)},
+               'e2e': {'value': L / (e2e_ms * 1e-3), 'unit': UNIT, 'h2d_bytes_per_step': int(xc.nbytes + Ec.nbytes +
+                                                                                             hc.nbytes),
+                       'd2h_bytes_per_step': int(hc.nbytes)},
+               'roofline': {'bound': 'hbm', 'kernel': 'whole layer forward (per GPU)', 'achieved': achieved,
+                            'peak': hbm, 'peak_source': 'measured' if 'hbm_gbs' in peaks else 'fallback',
+                            'unit': 'GB/s', 'frac': achieved / hbm,
+                            'algorithmic_bytes_per_token': CFG4_BYTES_PER_TOKEN, 'traffic': None},
+               'gpu_launches': None, 'clocks': clk}
+        if cpu_info is not None:
+            out['cpu_baseline'] = cpu_info
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == 'reference':
         return run_reference(args)
+    if args.workload == 'cfg4':
+        return run_cfg4(args)
     return run_ours(args)
 
 

@@ -30,6 +30,8 @@
  *   asrn_gen_memory         _MemoriaHawkes.paso + _repeticion_o1  asrn/nucleo.py:1683-1714, 953-960
  *   asrn_gen_ring_insert    _anillo_meter                      asrn/nucleo.py:1610-1618
  *   asrn_gen_front          _contexto + _phi_y_valores/_ids (one token)  asrn/estable.py:153-194, nucleo.py:639-664
+ *   asrn_shard_rows, asrn_score_shard   candidate windows / _acumular of one shard of a long sequence
+ *                                        (asrn/estable.py:220-300; the reference runs one GPU per sequence)
  *   asrn_gen_gate           _combinar (one token)              asrn/estable.py:376-403
  */
 #ifndef ASRN_B200_H
@@ -150,6 +152,22 @@ int asrn_score(const asrn_layer_config* cfg, const asrn_layer_weights* w, const 
                const int32_t* orden, const uint16_t* ids_o, const void* phi, const void* Qc, const void* Kc,
                const float* sig, const double* Bt, const float* log_alfa, const void* Ea, float* acc,
                uint8_t* sen_hay, float* sen_mx, float* sen_pk, void* stream);
+
+/* ---- sequence-chunk sharding (one long sequence over several GPUs) --------------------------------------------------
+ * Each shard owns positions [q_lo, q_hi) of an L-position sequence and, after exchanging bucket ids and features,
+ * holds them for all L positions. asrn_shard_rows turns full sorted rows (orden, ids_o: (rows, L) from
+ * asrn_bucket_sort) into the shard's rows: its own slots plus, before each bucket's local run, the up to C earlier
+ * slots some local query has as a candidate; with orden_v == NULL it only writes each row's length to counts (rows)
+ * int64; otherwise it writes rows of length Lv (>= every count), padded with id 0xFFFF. Requires 2+ shards
+ * (q_lo > 0 or q_hi < L). asrn_score_shard is asrn_score over such rows (cfg->L = Lv) with features of L_feat positions
+ * per sequence indexed by position, queries = the slots at positions [q_lo, q_hi), outputs (B, q_hi - q_lo, ...). */
+int asrn_shard_rows(int64_t rows, int64_t L, int32_t C, int64_t q_lo, int64_t q_hi, const int32_t* orden,
+                    const uint16_t* ids_o, int64_t Lv, int32_t* orden_v, uint16_t* ids_v, int64_t* counts,
+                    void* stream);
+int asrn_score_shard(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared, int64_t L_feat,
+                     int64_t q_lo, int64_t q_hi, const int32_t* orden, const uint16_t* ids_o, const void* phi,
+                     const void* Qc, const void* Kc, const float* sig, const double* Bt, const float* log_alfa,
+                     const void* Ea, float* acc, uint8_t* sen_hay, float* sen_mx, float* sen_pk, void* stream);
 
 /* The same bucket sort for callers that cannot allocate device memory when they sort (a plug-in inside a host process
  * whose allocator it does not own, a serving loop that keeps a fixed memory footprint after start-up): no workspace

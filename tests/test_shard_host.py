@@ -1,0 +1,71 @@
+"""Host logic of the sequence-chunk sharding (asrn_b200/shard.py) on the CPU: chunk bounds, clock offsets and the
+exchange steps as world-size-2 gloo ranks (the NCCL path runs the same calls on GPUs)."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+
+def test_chunk_bounds():
+    from asrn_b200 import shard
+    assert [shard.chunk_bounds(12, 3, r) for r in range(3)] == [(0, 4), (4, 8), (8, 12)]
+    with pytest.raises(ValueError):
+        shard.chunk_bounds(10, 3, 0)
+
+
+def test_clock_offsets_give_the_global_cumulative_sum():
+    from asrn_b200 import shard
+    rng = np.random.default_rng(0)
+    B, world, Lc = 2, 3, 5
+    beta = torch.from_numpy(rng.uniform(0.01, 2.0, (B, world * Lc)))
+    local = torch.cat([torch.cumsum(beta[:, r * Lc:(r + 1) * Lc], 1) for r in range(world)], 1)
+    sums = torch.stack([local[:, (r + 1) * Lc - 1] for r in range(world)], 0)
+    shard._apply_clock_offsets(local, sums, Lc)
+    assert torch.allclose(local, torch.cumsum(beta, 1), rtol=1e-14, atol=0)
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(('127.0.0.1', 0))
+        return s.getsockname()[1]
+
+
+def _rank(rank, world, port, out):
+    import torch.distributed as dist
+    os.environ['MASTER_ADDR'] = '127.0.0.1'
+    os.environ['MASTER_PORT'] = str(port)
+    dist.init_process_group('gloo', rank=rank, world_size=world)
+    try:
+        from asrn_b200 import shard
+        res = {}
+        last = torch.full((2, 3), float(rank + 1))
+        res['halo'] = shard.exchange_halo(last, world, rank)
+        res['sums'] = shard.exchange_chunk_sums(torch.tensor([rank + 0.5, 10.0 * rank], dtype=torch.float64), world)
+        res['seq1'] = shard._gather_seq(torch.arange(4).view(1, 4, 1) + 100 * rank, world, None)
+        res['seq2'] = shard._gather_seq(torch.arange(8).view(2, 4) + 100 * rank, world, None)
+        B, T, Lc = 2, 3, 4
+        ids = (torch.arange(B * T * Lc).view(B * T, Lc) + 1000 * rank).to(torch.int16)
+        res['ids'] = shard.exchange_ids(ids, B, T, world, None)
+        torch.save(res, os.path.join(out, f'rank{rank}.pt'))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_exchange_steps_with_two_gloo_ranks(tmp_path):
+    import torch.multiprocessing as mp
+    world = 2
+    mp.start_processes(_rank, args=(world, _free_port(), str(tmp_path)), nprocs=world, start_method='spawn')
+    r0 = torch.load(tmp_path / 'rank0.pt')
+    r1 = torch.load(tmp_path / 'rank1.pt')
+    assert torch.equal(r0['halo'], torch.zeros(2, 3)) and torch.equal(r1['halo'], torch.full((2, 3), 1.0))
+    for r in (r0, r1):
+        assert torch.equal(r['sums'], torch.tensor([[0.5, 0.0], [1.5, 10.0]], dtype=torch.float64))
+        assert torch.equal(r['seq1'].view(-1), torch.tensor([0, 1, 2, 3, 100, 101, 102, 103]))
+        expect2 = torch.cat([torch.arange(8).view(2, 4), torch.arange(8).view(2, 4) + 100], 1)
+        assert torch.equal(r['seq2'], expect2)
+        B, T, Lc = 2, 3, 4
+        full = torch.cat([torch.arange(B * T * Lc).view(B * T, Lc), torch.arange(B * T * Lc).view(B * T, Lc) + 1000],
+                         1).to(torch.int16)
+        assert torch.equal(r['ids'], full)
