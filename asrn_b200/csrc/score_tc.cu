@@ -53,8 +53,8 @@ __host__ __device__ inline size_t tc_smem_bytes(int P, int cf, int K, int dpart)
   b += kR * 8;                    // bt
   b += kR * 4 * 3;                // pos, id, used
   b += kR * 4;                    // la
-  b += kR * 4 * (size_t)K;        // pf
   b = (b + 15) / 16 * 16;
+  b += kR * 4 * (size_t)kMaxSuffix;   // pf (rows of 8, 16-byte aligned)
   b += (size_t)kR * Pp * 2 + 2 * (size_t)kR * Cp * 2 + (size_t)kR * Dp * 2;
   b += (size_t)kQ * 65 * 4;
   b += (size_t)kQ * 72 * 2;
@@ -77,8 +77,8 @@ __device__ inline TcSmem carve_tc(char* base, int P, int cf, int K, int dpart) {
   s.id = reinterpret_cast<int*>(p); p += kR * 4;
   s.used = reinterpret_cast<int*>(p); p += kR * 4;
   s.la = reinterpret_cast<float*>(p); p += kR * 4;
-  s.pf = reinterpret_cast<float*>(p); p += kR * 4 * K;
   p = base + ((p - base) + 15) / 16 * 16;
+  s.pf = reinterpret_cast<float*>(p); p += kR * 4 * kMaxSuffix;
   s.phi = reinterpret_cast<__nv_bfloat16*>(p); p += (size_t)kR * s.Pp * 2;
   s.qc = reinterpret_cast<__nv_bfloat16*>(p); p += (size_t)kR * s.Cp * 2;
   s.kc = reinterpret_cast<__nv_bfloat16*>(p); p += (size_t)kR * s.Cp * 2;
@@ -176,11 +176,12 @@ __device__ __forceinline__ void tc_stage2(const ScoreArgs& a, const TcSmem& S, i
       else S.bt[ri] = 0.0;
       if (real) cp_async4(S.la + ri, a.log_alfa + g);
       else S.la[ri] = 0.f;
-    } else if (lane <= a.K) {
+    } else if (lane <= kMaxSuffix) {
+      // previous signatures sig[pos - 1 - c]; NaN (never equal) before the text and past K
       const int c = lane - 1;
       const int64_t t = (int64_t)pos - 1 - c;
-      if (real && t >= 0) cp_async4(S.pf + ri * a.K + c, a.sig + b * a.Lf + t);
-      else S.pf[ri * a.K + c] = __int_as_float(0x7fc00000);
+      if (real && c < a.K && t >= 0) cp_async4(S.pf + ri * kMaxSuffix + c, a.sig + b * a.Lf + t);
+      else S.pf[ri * kMaxSuffix + c] = __int_as_float(0x7fc00000);
     }
     const __nv_bfloat16* vsrc = Ea + (b * a.Lf + (used ? pos + 1 : 0)) * (int64_t)a.d + dp0;
     for (int c = lane; c < per_slot; c += 32) {
@@ -259,77 +260,129 @@ __global__ void __launch_bounds__(kThreadsTc, 1) k_score_tc(ScoreArgs a, int nds
         const int key = nt * 8 + (lane & 7);
         const int rk = wrow(key);
         const int kb = ((lane >> 3) & 1) * 8;
+        const uint32_t phi_a = su32(S.phi) + 2u * (uint32_t)(ra * S.Pp + ka);
+        const uint32_t phi_b = su32(S.phi) + 2u * (uint32_t)(rk * S.Pp + kb);
+        const uint32_t qc_a = su32(S.qc) + 2u * (uint32_t)(ra * S.Cp + ka);
+        const uint32_t kc_b = su32(S.kc) + 2u * (uint32_t)(rk * S.Cp + kb);
         for (int k0 = 0; k0 < Ppad; k0 += 16) {
           uint32_t a0, a1, a2, a3, b0, b1;
-          ldsm_x4(su32(S.phi + ra * S.Pp + k0 + ka), a0, a1, a2, a3);
-          ldsm_x2(su32(S.phi + rk * S.Pp + k0 + kb), b0, b1);
+          ldsm_x4(phi_a + 2 * k0, a0, a1, a2, a3);
+          ldsm_x2(phi_b + 2 * k0, b0, b1);
           mma16816(cphi, a0, a1, a2, a3, b0, b1);
         }
         for (int k0 = 0; k0 < Cpad; k0 += 16) {
           uint32_t a0, a1, a2, a3, b0, b1;
-          ldsm_x4(su32(S.qc + ra * S.Cp + k0 + ka), a0, a1, a2, a3);
-          ldsm_x2(su32(S.kc + rk * S.Cp + k0 + kb), b0, b1);
+          ldsm_x4(qc_a + 2 * k0, a0, a1, a2, a3);
+          ldsm_x2(kc_b + 2 * k0, b0, b1);
           mma16816(cqk, a0, a1, a2, a3, b0, b1);
         }
       }
+      // this lane's two query rows (qi0, qi0 + 8) and two key columns (kj0, kj0 + 1): their ring-row scalars are
+      // read once, the suffix length is the count of leading equal previous signatures (compare mask, no branches)
+      const int qi0 = mt * 16 + (lane >> 2), kj0 = nt * 8 + (lane & 3) * 2;
+      int q_id[2], k_id[2];
+      float4 q_pf[2][2], k_pf[2][2];
+      double q_bt[2], k_bt[2];
+      float k_la[2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int rq = wrow(kQ + qi0 + 8 * u), rk = wrow(kj0 + u);
+        q_id[u] = S.id[rq];
+        k_id[u] = S.id[rk];
+        q_pf[u][0] = *reinterpret_cast<const float4*>(S.pf + rq * kMaxSuffix);
+        q_pf[u][1] = *reinterpret_cast<const float4*>(S.pf + rq * kMaxSuffix + 4);
+        k_pf[u][0] = *reinterpret_cast<const float4*>(S.pf + rk * kMaxSuffix);
+        k_pf[u][1] = *reinterpret_cast<const float4*>(S.pf + rk * kMaxSuffix + 4);
+        q_bt[u] = S.bt[rq];
+        k_bt[u] = S.bt[rk];
+        k_la[u] = S.la[rk];
+      }
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const int qi = mt * 16 + (lane >> 2) + (e >> 1) * 8;
-        const int kj = nt * 8 + (lane & 3) * 2 + (e & 1);
+        const int uq = e >> 1, uk = e & 1;
+        const int qi = qi0 + 8 * uq;
+        const int kj = kj0 + uk;
         const int64_t sq = q0 + qi, sk = q0 - kQ + kj;
         float val = -INFINITY;
-        if (band && kj < qi + 32 && kj >= qi + 32 - C && sq < a.L && sk >= 0) {
-          const int rq = wrow(kQ + qi), rk = wrow(kj);
-          if (S.id[rk] == S.id[rq]) {
-            const float s1 = round_bf16(__fdiv_rn(round_bf16(cphi[e]), a.inv_temp_div));
-            const float s2 = round_bf16(__fmul_rn(round_bf16(cqk[e]), a.esc_c));
-            float t1 = round_bf16(__fadd_rn(s1, s2));
-            int ln = 0;
-            for (int c = 0; c < a.K; ++c) {
-              if (S.pf[rq * a.K + c] == S.pf[rk * a.K + c]) ++ln; else break;
-            }
-            t1 = __fadd_rn(t1, a.w_suf[ln]);
-            t1 = __fadd_rn(t1, S.la[rk]);
-            const float dt = __double2float_rn(S.bt[rk] - S.bt[rq]);
-            val = __fadd_rn(t1, __fmul_rn(dt, tasa));
-          }
+        if (band && kj < qi + 32 && kj >= qi + 32 - C && sq < a.L && sk >= 0 && k_id[uk] == q_id[uq]) {
+          const float s1 = round_bf16(__fdiv_rn(round_bf16(cphi[e]), a.inv_temp_div));
+          const float s2 = round_bf16(__fmul_rn(round_bf16(cqk[e]), a.esc_c));
+          float t1 = round_bf16(__fadd_rn(s1, s2));
+          const float4 qa = q_pf[uq][0], qb = q_pf[uq][1], ka = k_pf[uk][0], kb = k_pf[uk][1];
+          const uint32_t eq = (qa.x == ka.x ? 1u : 0u) | (qa.y == ka.y ? 2u : 0u) | (qa.z == ka.z ? 4u : 0u) |
+                              (qa.w == ka.w ? 8u : 0u) | (qb.x == kb.x ? 16u : 0u) | (qb.y == kb.y ? 32u : 0u) |
+                              (qb.z == kb.z ? 64u : 0u) | (qb.w == kb.w ? 128u : 0u);
+          const int ln = __ffs(~eq) - 1;          // leading equal entries (entries past K are NaN: never equal)
+          t1 = __fadd_rn(t1, a.w_suf[ln]);
+          t1 = __fadd_rn(t1, k_la[uk]);
+          const float dt = __double2float_rn(k_bt[uk] - q_bt[uq]);
+          val = __fadd_rn(t1, __fmul_rn(dt, tasa));
         }
         S.sc[qi * 65 + kj] = val;
       }
     }
     __syncthreads();
 
-    // ---- softmax per query (warp w: queries 2w, 2w + 1; lane -> keys lane, lane + 32) --------------------------------
-    for (int qi = wid * 2; qi < wid * 2 + 2; ++qi) {
-      const int64_t sq = q0 + qi;
-      const float x0 = S.sc[qi * 65 + lane], x1 = S.sc[qi * 65 + lane + 32];
-      const bool v0 = x0 != -INFINITY, v1 = x1 != -INFINITY;
-      const bool anyv = __any_sync(0xffffffffu, v0 || v1);
-      float w0 = 0.f, w1 = 0.f;
-      const int posq = S.pos[wrow(kQ + qi)];
-      const bool mine = sq < S1 && posq >= a.q_lo && posq < a.q_hi;   // else a key only (another shard's position)
-      const int64_t gq = b * (a.q_hi - a.q_lo) + (posq - a.q_lo);
-      if (anyv) {
-        const float mx = warp_max(fmaxf(x0, x1));
-        const float e0 = v0 ? expf(__fsub_rn(x0, mx)) : 0.f;
-        const float e1 = v1 ? expf(__fsub_rn(x1, mx)) : 0.f;
-        const float sum = warp_sum(e0 + e1);
-        w0 = __fdiv_rn(e0, sum);
-        w1 = __fdiv_rn(e1, sum);
-        const float peak = warp_max(fmaxf(w0, w1));
-        if (lane == 0 && write_signals && mine) {
-          a.sen_hay[gq * a.T + tau] = 1;
-          a.sen_mx[gq * a.T + tau] = mx;
-          a.sen_pk[gq * a.T + tau] = peak;
-        }
-      } else if (lane == 0 && write_signals && mine) {
-        a.sen_hay[gq * a.T + tau] = 0;
-        a.sen_mx[gq * a.T + tau] = kProhibido;
-        a.sen_pk[gq * a.T + tau] = 0.f;
+    // ---- softmax per query (warp w: queries 2w, 2w + 1 together; lane -> keys lane, lane + 32) ----------------------
+    {
+      const int qa = wid * 2;
+      float x[2][2];
+      bool vv[2][2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        x[u][0] = S.sc[(qa + u) * 65 + lane];
+        x[u][1] = S.sc[(qa + u) * 65 + lane + 32];
+        vv[u][0] = x[u][0] != -INFINITY;
+        vv[u][1] = x[u][1] != -INFINITY;
       }
-      S.att[qi * 72 + lane] = __float2bfloat16_rn(w0);
-      S.att[qi * 72 + lane + 32] = __float2bfloat16_rn(w1);
-      if (lane == 0) S.qhay[qi] = (anyv && mine) ? 1 : 0;
+      const unsigned bal0 = __ballot_sync(0xffffffffu, vv[0][0] || vv[0][1]);
+      const unsigned bal1 = __ballot_sync(0xffffffffu, vv[1][0] || vv[1][1]);
+      float m0 = fmaxf(x[0][0], x[0][1]), m1 = fmaxf(x[1][0], x[1][1]);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, o));
+        m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, o));
+      }
+      const float mxs[2] = {m0, m1};
+      float e[2][2], sum[2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        e[u][0] = vv[u][0] ? expf(__fsub_rn(x[u][0], mxs[u])) : 0.f;
+        e[u][1] = vv[u][1] ? expf(__fsub_rn(x[u][1], mxs[u])) : 0.f;
+        sum[u] = e[u][0] + e[u][1];
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        sum[0] += __shfl_xor_sync(0xffffffffu, sum[0], o);
+        sum[1] += __shfl_xor_sync(0xffffffffu, sum[1], o);
+      }
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int qi = qa + u;
+        const int64_t sq = q0 + qi;
+        const bool anyv = (u == 0 ? bal0 : bal1) != 0;
+        const int posq = S.pos[wrow(kQ + qi)];
+        const bool mine = sq < S1 && posq >= a.q_lo && posq < a.q_hi;   // else a key only (another shard's position)
+        const int64_t gq = b * (a.q_hi - a.q_lo) + (posq - a.q_lo);
+        float w0 = 0.f, w1 = 0.f;
+        if (anyv) {
+          w0 = __fdiv_rn(e[u][0], sum[u]);
+          w1 = __fdiv_rn(e[u][1], sum[u]);
+          // the largest weight is the maximum's: exp(0) / sum
+          if (lane == 0 && write_signals && mine) {
+            a.sen_hay[gq * a.T + tau] = 1;
+            a.sen_mx[gq * a.T + tau] = mxs[u];
+            a.sen_pk[gq * a.T + tau] = __fdiv_rn(1.f, sum[u]);
+          }
+        } else if (lane == 0 && write_signals && mine) {
+          a.sen_hay[gq * a.T + tau] = 0;
+          a.sen_mx[gq * a.T + tau] = kProhibido;
+          a.sen_pk[gq * a.T + tau] = 0.f;
+        }
+        S.att[qi * 72 + lane] = __float2bfloat16_rn(w0);
+        S.att[qi * 72 + lane + 32] = __float2bfloat16_rn(w1);
+        if (lane == 0) S.qhay[qi] = (anyv && mine) ? 1 : 0;
+      }
     }
     __syncthreads();
 
@@ -345,16 +398,18 @@ __global__ void __launch_bounds__(kThreadsTc, 1) k_score_tc(ScoreArgs a, int nds
 #pragma unroll
         for (int j = 0; j < 6; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
         // queries of m-tile mt use window keys [qbase, qbase + 47]
+        const uint32_t att_a = su32(S.att) + 2u * (uint32_t)((qbase + (lane & 15)) * 72 + (lane >> 4) * 8);
         for (int ks = mt; ks < mt + 3; ++ks) {
           uint32_t a0, a1, a2, a3;
-          ldsm_x4(su32(S.att + (qbase + (lane & 15)) * 72 + ks * 16 + (lane >> 4) * 8), a0, a1, a2, a3);
+          ldsm_x4(att_a + 2u * (uint32_t)(ks * 16), a0, a1, a2, a3);
           const int rk = wrow(ks * 16 + (lane & 15));
+          const uint32_t v_row = su32(S.v) + 2u * (uint32_t)(rk * S.Dp);
 #pragma unroll
           for (int j = 0; j < 6; ++j) {
             const int tile = wid + 16 * j;
             if (tile < ntiles) {
               uint32_t b0, b1;
-              ldsm_x2_t(su32(S.v + rk * S.Dp + tile * 8), b0, b1);
+              ldsm_x2_t(v_row + 2u * (uint32_t)(tile * 8), b0, b1);
               mma16816(acc[j], a0, a1, a2, a3, b0, b1);
             }
           }
