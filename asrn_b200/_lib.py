@@ -73,7 +73,7 @@ _SIGS = {
     'asrn_gen_hawkes_table_bytes': (ctypes.c_size_t, [ctypes.c_int64, ctypes.c_int32, ctypes.c_int64]),
     'asrn_gen_hawkes_build': (ctypes.c_int, [_P, _P, _P, ctypes.c_int64, ctypes.c_int64, _P, _P, _P, _P, _P,
                                              ctypes.c_int64, _P]),
-    'asrn_gen_attend': (ctypes.c_int, [_P, _P, _P, _P, ctypes.c_int64] + [_P] * 16),
+    'asrn_gen_attend': (ctypes.c_int, [_P, _P, _P, _P, ctypes.c_int64] + [_P] * 22),
     'asrn_gen_memory': (ctypes.c_int, [_P] * 4 + [ctypes.c_int64] + [_P] * 6 + [ctypes.c_int64] + [_P] * 5),
     'asrn_gen_ring_insert': (ctypes.c_int, [ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                             _P, _P, _P, _P, _P]),
@@ -81,7 +81,7 @@ _SIGS = {
     'asrn_shard_rows': (ctypes.c_int, [ctypes.c_int64, ctypes.c_int64, ctypes.c_int32, ctypes.c_int64, ctypes.c_int64,
                                        _P, _P, ctypes.c_int64, _P, _P, _P, _P]),
     'asrn_score_shard': (ctypes.c_int, [_P, _P, _P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64] + [_P] * 14),
-    'asrn_gen_gate': (ctypes.c_int, [_P] * 14),
+    'asrn_gen_gate': (ctypes.c_int, [_P] * 16),
     'asrn_gate_workspace_bytes': (ctypes.c_size_t, [_P]),
     'asrn_gate': (ctypes.c_int, [_P] * 14 + [ctypes.c_size_t, _P]),
 }

@@ -444,19 +444,28 @@ int asrn_gen_attend(const asrn_layer_config* cfg, const asrn_layer_weights* w, c
                     const int64_t* t_pos, int64_t cap, const uint16_t* ids_t, const void* phi_t, const void* qc_t,
                     const void* kc_t, const int32_t* ring, const float* sig_cache, const double* bt_cache,
                     const float* la_cache, void* phi_cache, void* kc_cache, const void* ea_cache, float* acc,
-                    uint8_t* sen_hay, float* sen_mx, float* sen_pk, void* stream) {
+                    uint8_t* sen_hay, float* sen_mx, float* sen_pk, const float* glogit, const uint8_t* vistos,
+                    const float* hawkes, const float* racha, void* cbuf, float* sigma, void* stream) {
   int st = check_config(cfg);
   if (st) return st;
   if ((st = check_weights(w))) return st;
   if (!prepared || !t_pos || !ids_t || !phi_t || !qc_t || !kc_t || !ring || !sig_cache || !bt_cache || !la_cache ||
       !phi_cache || !kc_cache || !ea_cache || !acc || !sen_hay || !sen_mx || !sen_pk || cap < 2)
     return ASRN_ERR_ARG;
+  // optional gate precomputation (bf16 mode): all of glogit, vistos, hawkes, racha, cbuf, sigma, or none
+  const bool pre = cbuf || sigma;
+  if (pre && (!cfg->half || !cbuf || !sigma || !glogit || !vistos || !hawkes || !racha)) return ASRN_ERR_ARG;
+  GateArgs ga = gate_args(*cfg, *w, reinterpret_cast<const char*>(prepared));
+  if (pre) {
+    ga.glogit = glogit; ga.vistos = vistos; ga.hawkes = hawkes; ga.racha = racha;
+    ga.cbuf = reinterpret_cast<__nv_bfloat16*>(cbuf); ga.sigma = sigma;
+  }
   GenArgs a = gen_args(*cfg, *w, reinterpret_cast<const char*>(prepared), t_pos, cap);
   a.ids_t = ids_t; a.phi_t = phi_t; a.qc_t = qc_t; a.kc_t = kc_t; a.ring = ring; a.sig_cache = sig_cache;
   a.bt_cache = bt_cache; a.la_cache = la_cache; a.phi_cache = phi_cache; a.kc_cache = kc_cache;
   a.phi_cache_w = phi_cache; a.kc_cache_w = kc_cache; a.ea_cache = ea_cache; a.acc = acc;
   a.sen_hay = sen_hay; a.sen_mx = sen_mx; a.sen_pk = sen_pk;
-  return launch_gen_attend(a, cfg->half != 0, as_stream(stream));
+  return launch_gen_attend(a, ga, cfg->half != 0, as_stream(stream));
 }
 
 int asrn_gen_memory(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared,
@@ -510,7 +519,7 @@ int asrn_gen_front(const asrn_layer_config* cfg, const asrn_layer_weights* w, co
 int asrn_gen_gate(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared, const float* h,
                   const float* glogit, const float* acc, const uint8_t* sen_hay, const float* sen_mx,
                   const float* sen_pk, const uint8_t* vistos, const float* hawkes, const float* racha, float* h_out,
-                  void* stream) {
+                  const void* cbuf, const float* sigma, void* stream) {
   int st = check_config(cfg);
   if (st) return st;
   if ((st = check_weights(w))) return st;
@@ -520,6 +529,9 @@ int asrn_gen_gate(const asrn_layer_config* cfg, const asrn_layer_weights* w, con
   GateArgs a = gate_args(*cfg, *w, reinterpret_cast<const char*>(prepared));
   a.h = h; a.glogit = glogit; a.acc = acc; a.sen_hay = sen_hay; a.sen_mx = sen_mx; a.sen_pk = sen_pk;
   a.vistos = vistos; a.hawkes = hawkes; a.racha = racha; a.out = h_out;
+  if ((cbuf != nullptr) != (sigma != nullptr) || (cbuf && !cfg->half)) return ASRN_ERR_ARG;
+  a.cbuf = reinterpret_cast<__nv_bfloat16*>(const_cast<void*>(cbuf));
+  a.sigma = const_cast<float*>(sigma);
   return launch_gen_gate(a, cfg->half != 0, as_stream(stream));
 }
 

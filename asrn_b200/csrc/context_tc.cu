@@ -32,6 +32,8 @@ k_context_tc(const __grid_constant__ CUtensorMap tmap_wctx, ContextArgs a, int* 
   uint64_t* mma_done = full_b + 2;
   uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(full_b + 4);
   int* abort_s = reinterpret_cast<int*>(tmem_base_s + 1);
+  // per-column parameters, read as float4 from shared memory: ln_w, ln_b, w_reloj[0], w_reloj[1], g_w
+  float* s_par = reinterpret_cast<float*>(tail + 64);
 
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
   const int d = a.d;
@@ -48,10 +50,22 @@ k_context_tc(const __grid_constant__ CUtensorMap tmap_wctx, ContextArgs a, int* 
     tmem_alloc(tmem_base_s, 32);
     tmem_relinquish();
   }
+  for (int j = tid; j < d; j += kCThreads) {
+    s_par[j] = a.ln_w[j];
+    s_par[d + j] = a.ln_b[j];
+    s_par[2 * d + j] = a.w_reloj[j];
+    s_par[3 * d + j] = a.w_reloj[d + j];
+    s_par[4 * d + j] = a.g_w[j];
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_base_s;
+  const float4* p_lnw = reinterpret_cast<const float4*>(s_par);
+  const float4* p_lnb = reinterpret_cast<const float4*>(s_par + d);
+  const float4* p_w0 = reinterpret_cast<const float4*>(s_par + 2 * d);
+  const float4* p_w1 = reinterpret_cast<const float4*>(s_par + 3 * d);
+  const float4* p_g = reinterpret_cast<const float4*>(s_par + 4 * d);
 
   const int ar = tid >> 1, ah = tid & 1;
   const int64_t ag = m0 + ar;
@@ -71,9 +85,14 @@ k_context_tc(const __grid_constant__ CUtensorMap tmap_wctx, ContextArgs a, int* 
     }
     float sc = 0.f;
 #pragma unroll
-    for (int e = 0; e < 32; ++e) {
-      sc += xs[e];
-      gl = fmaf(xs[e], a.g_w[k * kCBK + ah * 32 + e], gl);
+    for (int e4 = 0; e4 < 8; ++e4) {
+      const float4 gw = p_g[(k * kCBK + ah * 32) / 4 + e4];
+      const float gv[4] = {gw.x, gw.y, gw.z, gw.w};
+#pragma unroll
+      for (int e = 4 * e4; e < 4 * e4 + 4; ++e) {
+        sc += xs[e];
+        gl = fmaf(xs[e], gv[e - 4 * e4], gl);
+      }
     }
     const float mc = sc * (1.f / 32.f);
     float m2c = 0.f;
@@ -122,12 +141,18 @@ k_context_tc(const __grid_constant__ CUtensorMap tmap_wctx, ContextArgs a, int* 
       float hn[8];
       const float4 x0 = pre[2 * c], x1 = pre[2 * c + 1];
       const float xs[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+      const int j4 = (c0 + c * 8) / 4;
+      const float4 lw0 = p_lnw[j4], lw1 = p_lnw[j4 + 1], lb0 = p_lnb[j4], lb1 = p_lnb[j4 + 1];
+      const float4 w00 = p_w0[j4], w01 = p_w0[j4 + 1], w10 = p_w1[j4], w11 = p_w1[j4 + 1];
+      const float lw[8] = {lw0.x, lw0.y, lw0.z, lw0.w, lw1.x, lw1.y, lw1.z, lw1.w};
+      const float lb[8] = {lb0.x, lb0.y, lb0.z, lb0.w, lb1.x, lb1.y, lb1.z, lb1.w};
+      const float wa[8] = {w00.x, w00.y, w00.z, w00.w, w01.x, w01.y, w01.z, w01.w};
+      const float wb[8] = {w10.x, w10.y, w10.z, w10.w, w11.x, w11.y, w11.z, w11.w};
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
-        const int j = c0 + c * 8 + e;
-        hn[e] = (xs[e] - mean) * rstd * a.ln_w[j] + a.ln_b[j];
-        u0 = fmaf(hn[e], a.w_reloj[j], u0);
-        u1 = fmaf(hn[e], a.w_reloj[d + j], u1);
+        hn[e] = (xs[e] - mean) * rstd * lw[e] + lb[e];
+        u0 = fmaf(hn[e], wa[e], u0);
+        u1 = fmaf(hn[e], wb[e], u1);
       }
       *reinterpret_cast<uint4*>(dstA + sw128_offset(ar, ah * 4 + c)) =
           make_uint4(pack_bf16x2(hn[0], hn[1]), pack_bf16x2(hn[2], hn[3]), pack_bf16x2(hn[4], hn[5]),
@@ -200,7 +225,7 @@ int launch_context_tc(const ContextArgs& a, int* status, cudaStream_t s) {
   CUtensorMap map;
   if (!make_tmap_bf16(&map, a.wctx, (uint64_t)a.d, (uint64_t)(2 * a.cf), (uint64_t)a.d * 2, 64, (uint32_t)(2 * a.cf)))
     return ASRN_ERR_CUDA;
-  const size_t smem = 1024 + 2 * (size_t)kCStageA + 2 * (size_t)(2 * a.cf) * 128 + 64;
+  const size_t smem = 1024 + 2 * (size_t)kCStageA + 2 * (size_t)(2 * a.cf) * 128 + 64 + 5 * (size_t)a.d * 4;
   cudaFuncSetAttribute(k_context_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   const int64_t M = a.B * a.L;
   k_context_tc<<<(unsigned)((M + kCTM - 1) / kCTM), kCThreads, smem, s>>>(map, a, status);

@@ -7,52 +7,13 @@
 // Here salida = W_v acc (acc = sum of att * Ea rows from the scoring kernel), so o(salida) = (W_o W_v) acc and the
 // projection is one GEMM against the prepared W_ov.
 #include "common.cuh"
+#include "gate.cuh"
 #include "layout.h"
 #include "umma.cuh"
 
 namespace asrn {
 
 constexpr int kGateTM = 64, kGateTN = 64, kGateKC = 32;
-
-// Gate of one token (sigmoid(logit), rounded to the compute type) and max(1, pt).
-template <bool Half>
-__device__ __forceinline__ void gate_of_token(const GateArgs& a, int64_t g, float* sigma, float* ptc) {
-  const int T = a.T;
-  float pt = 0.f, mejor = kProhibido, pico = 0.f, pctx = 0.f;
-  for (int tau = 0; tau < T; ++tau) {
-    const float hay = (float)a.sen_hay[g * T + tau];
-    pt = __fadd_rn(pt, hay);
-    if (hay > 0.f) mejor = fmaxf(mejor, a.sen_mx[g * T + tau]);
-    pico = __fadd_rn(pico, __fmul_rn(a.sen_pk[g * T + tau], hay));
-    if (tau >= T - a.Tc) pctx = __fadd_rn(pctx, hay);
-  }
-  mejor = fmaxf(mejor, kProhibido);
-  mejor = (pt > 0.f) ? mejor : 0.f;
-  mejor = fminf(fmaxf(mejor, -a.mejor_max), a.mejor_max);
-  const float pt1 = fmaxf(pt, 1.f);
-  float s[4] = {__fdiv_rn(pt, (float)T), mejor, __fdiv_rn(pico, pt1), __fdiv_rn(pctx, (float)a.Tc)};
-  float gc = 0.f;
-  for (int i = 0; i < 4; ++i) gc = fmaf(act<Half>(s[i]), a.gconf[i], gc);
-  gc = act<Half>(__fadd_rn(gc, a.gconf[4]));
-  float logit = __fadd_rn(a.glogit[g], gc);
-  float sv = 0.f;
-  for (int j = 0; j < a.n; ++j) sv = __fadd_rn(sv, __fmul_rn((float)a.vistos[g * a.n + j], a.w_vistos[j]));
-  logit = __fadd_rn(logit, sv);
-  float sh = 0.f;
-  for (int j = 0; j < a.n; ++j) sh = __fadd_rn(sh, __fmul_rn(log1pf(a.hawkes[g * a.n + j]), a.u_hawkes[j]));
-  logit = __fadd_rn(logit, sh);
-  // response to the streak: linear interpolation of u_racha on x = log1p(racha) / paso, flat past the last node
-  float x = __fdiv_rn(log1pf(a.racha[g]), a.racha_paso);
-  x = fminf(x, (float)(a.nodes - 1));
-  const float xf = (x != x) ? 0.f : x;
-  int i = (int)floorf(xf);
-  i = min(max(i, 0), a.nodes - 2);
-  const float resp = __fadd_rn(a.u_racha[i], __fmul_rn(__fsub_rn(x, (float)i), a.d_racha[i + 1]));
-  logit = __fadd_rn(logit, resp);
-  if (a.tope > 0.f) logit = __fmul_rn(a.tope, tanhf(__fdiv_rn(logit, a.tope)));
-  *sigma = act<Half>(1.f / (1.f + expf(-logit)));
-  *ptc = pt1;
-}
 
 template <bool Half>
 __global__ void __launch_bounds__(256) k_gate_simt(GateArgs a) {
@@ -122,8 +83,8 @@ __global__ void __launch_bounds__(256) k_gate_simt(GateArgs a) {
 //   c = bf16(acc / max(1, pt)) (asrn/estable.py:387, the autocast rounding of o's input); memory-bound.
 // k_gate_tc: h' = h + bf16(sigma * bf16(c . W_ov^T)). Tile 128 tokens (TMEM lanes) x NT columns (TMEM columns),
 //   K = d in chunks of 64; both operands by TMA (128-byte swizzle), one producer thread and one MMA thread
-//   (tcgen05.commit frees each stage), the fp32 accumulator in TMEM; the epilogue transposes 32 x 32 blocks
-//   through shared memory so that h is read and h' written in coalesced rows.
+//   (tcgen05.commit frees each stage), the fp32 accumulator in TMEM; in the epilogue each thread owns one tile row
+//   (its TMEM lane) and reads h / writes h' for 32 consecutive columns at a time with 16-byte accesses.
 __global__ void __launch_bounds__(256) k_gate_prep(GateArgs a) {
   const int lane = threadIdx.x & 31;
   const int64_t g = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -164,7 +125,6 @@ k_gate_tc(const __grid_constant__ CUtensorMap tmap_c, const __grid_constant__ CU
   uint64_t* acc_full = full + 4;
   uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(full + 5);
   int* abort_s = reinterpret_cast<int*>(tmem_base_s + 1);
-  float* tr = reinterpret_cast<float*>(sm);                    // epilogue: [8 warps][32][33], reuses the stages
 
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
   const int d = a.d;
@@ -219,25 +179,32 @@ k_gate_tc(const __grid_constant__ CUtensorMap tmap_c, const __grid_constant__ CU
   tc_fence_after();
   __syncthreads();
   if (ok && *abort_s == 0) {
+    // TMEM lane = tile row: each thread holds 32 consecutive columns of its row, so it reads its 128 bytes of h and
+    // writes its 128 bytes of h' with 16-byte accesses, all eight loads in flight together
     const int q4 = wid & 3, grp = wid >> 2;
     const uint32_t trow = tmem + ((uint32_t)(q4 * 32) << 16);
-    float* T = tr + wid * (32 * 33);
+    const int64_t g = m0 + q4 * 32 + lane;
+    const bool row_ok = g < M;
+    const float sg = row_ok ? a.sigma[g] : 0.f;
     for (int ch = grp; ch * 32 < NT; ch += 2) {
       float v[32];
       tmem_ld32(trow + ch * 32, v);
+      if (row_ok) {
+        const float4* hp = reinterpret_cast<const float4*>(a.h + g * d + n0 + ch * 32);
+        float4* op = reinterpret_cast<float4*>(a.out + g * d + n0 + ch * 32);
+        float4 hv[8];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) T[lane * 33 + i] = v[i];
-      __syncwarp();
-      const int col = n0 + ch * 32 + lane;
-      for (int rr = 0; rr < 32; ++rr) {
-        const int row = q4 * 32 + rr;
-        const int64_t g = m0 + row;
-        if (g >= M) break;
-        const float o = round_bf16(T[rr * 33 + lane]);
-        const float add = round_bf16(__fmul_rn(a.sigma[g], o));
-        a.out[g * d + col] = __fadd_rn(a.h[g * d + col], add);
+        for (int i = 0; i < 8; ++i) hv[i] = __ldg(hp + i);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          float4 o;
+          o.x = __fadd_rn(hv[i].x, round_bf16(__fmul_rn(sg, round_bf16(v[4 * i]))));
+          o.y = __fadd_rn(hv[i].y, round_bf16(__fmul_rn(sg, round_bf16(v[4 * i + 1]))));
+          o.z = __fadd_rn(hv[i].z, round_bf16(__fmul_rn(sg, round_bf16(v[4 * i + 2]))));
+          o.w = __fadd_rn(hv[i].w, round_bf16(__fmul_rn(sg, round_bf16(v[4 * i + 3]))));
+          op[i] = o;
+        }
       }
-      __syncwarp();
     }
   }
   tc_fence_before();
@@ -250,9 +217,7 @@ k_gate_tc(const __grid_constant__ CUtensorMap tmap_c, const __grid_constant__ CU
 
 template <int NT>
 static size_t gate_tc_smem() {
-  const size_t stages = 2 * (size_t)kGStageA + 2 * (size_t)NT * 128;
-  const size_t tr = 8 * 32 * 33 * 4;
-  return 1024 + (stages > tr ? stages : tr) + 64;
+  return 1024 + 2 * (size_t)kGStageA + 2 * (size_t)NT * 128 + 64;
 }
 
 int gate_tc_tile(int d) {
@@ -354,8 +319,18 @@ __global__ void __launch_bounds__(kGGThreads) k_gen_gate_tc(GateArgs a) {
   }
   asm volatile("cp.async.commit_group;" ::: "memory");
   const int rg = wid & 3, cg = wid >> 2;
+  const bool pre = a.cbuf != nullptr && a.sigma != nullptr;   // c and sigma computed by the attention kernel
   for (int64_t r0 = 0; r0 < M; r0 += kGGRows) {
-    if (tid < kGGRows) {
+    if (pre) {
+      for (int e = tid; e < kGGRows * cpr; e += kGGThreads) {
+        const int r = e / cpr, c8 = e % cpr;
+        __nv_bfloat16* dst = s_c + r * ld + c8 * 8;
+        if (r0 + r < M) gg_cp_async16(dst, a.cbuf + (r0 + r) * d + c8 * 8);
+        else *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
+      }
+      asm volatile("cp.async.commit_group;" ::: "memory");
+      if (tid < kGGRows) s_sigma[tid] = (r0 + tid < M) ? a.sigma[r0 + tid] : 0.f;
+    } else if (tid < kGGRows) {
       float sg = 0.f, pt = 1.f;
       if (r0 + tid < M) gate_of_token<true>(a, r0 + tid, &sg, &pt);
       s_sigma[tid] = sg;
@@ -363,7 +338,7 @@ __global__ void __launch_bounds__(kGGThreads) k_gen_gate_tc(GateArgs a) {
     }
     __syncthreads();
     // c = bf16(acc / pt): kGGUnroll independent 16-byte loads per thread in flight
-    const int cq = d / 4, tot = kGGRows * cq;
+    const int cq = d / 4, tot = pre ? 0 : kGGRows * cq;
     for (int e0 = tid; e0 < tot; e0 += kGGThreads * kGGUnroll) {
       float4 x[kGGUnroll];
 #pragma unroll

@@ -197,7 +197,7 @@ int launch_ring_build(int64_t B, int64_t L, int T, int nb, int C, int64_t n_vali
                       const uint16_t* ids_o, int32_t* ring, int32_t* count, cudaStream_t s);
 int launch_hawkes_build(int64_t B, int64_t L, int64_t ld, int n, const float* sig, const double* cv, const double* Bt,
                         const float* la, const float* hawkes, void* table, int64_t cap, int* status, cudaStream_t s);
-int launch_gen_attend(const GenArgs& a, bool half, cudaStream_t s);
+int launch_gen_attend(const GenArgs& a, const GateArgs& ga, bool half, cudaStream_t s);
 int launch_gen_memory(const GenArgs& a, void* table, int64_t hcap, const double* cv, const float* kappa,
                       const double* beta_t, const float* la_t, float* racha_state, uint8_t* vistos, float* hawkes,
                       float* racha, int* status, cudaStream_t s);

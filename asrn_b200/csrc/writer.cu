@@ -16,6 +16,7 @@
 // phi / Kc (k_gen_attend) to the caches. A t outside [1, cap) sets ASRN_ERR_ARG in the status word and writes
 // nothing.
 #include "common.cuh"
+#include "gate.cuh"
 #include "layout.h"
 
 namespace asrn {
@@ -193,8 +194,11 @@ __device__ __forceinline__ float dot_act_row(const float* x, const typename Act<
   return acc;
 }
 
+// With ga.cbuf set (bf16 mode), the block also writes the gate's GEMM operand c = bf16(acc / max(1, pt)) for its
+// columns, and block (b, 0) the gate value sigma of sequence b (gate_of_token on the block's own table signals), so
+// the gate kernel only multiplies.
 template <bool Half>
-__global__ void __launch_bounds__(kGenThreads) k_gen_attend(GenArgs a) {
+__global__ void __launch_bounds__(kGenThreads) k_gen_attend(GenArgs a, GateArgs ga) {
   using A = Act<Half>;
   const int64_t b = blockIdx.x;
   const int col0 = blockIdx.y * kGenCols;
@@ -207,6 +211,8 @@ __global__ void __launch_bounds__(kGenThreads) k_gen_attend(GenArgs a) {
   }
   __shared__ float s_q[kMaxPhi + kMaxConfirm];
   __shared__ __align__(16) float s_part[kMaxTables][kGenCols];
+  __shared__ uint8_t s_hay[kMaxTables];
+  __shared__ float s_mx[kMaxTables], s_pk[kMaxTables];
   const typename A::T* phi_q = reinterpret_cast<const typename A::T*>(a.phi_t) + b * P;
   const typename A::T* qc_q = reinterpret_cast<const typename A::T*>(a.qc_t) + b * cf;
   for (int i = threadIdx.x; i < P + cf; i += blockDim.x) s_q[i] = i < P ? A::load(phi_q + i) : A::load(qc_q + i - P);
@@ -272,15 +278,15 @@ __global__ void __launch_bounds__(kGenThreads) k_gen_attend(GenArgs a) {
       const float sum = warp_sum(e);
       att = __fdiv_rn(e, sum);
       const float peak = warp_max(att);
-      if (lane == 0 && blockIdx.y == 0) {
-        a.sen_hay[b * T + tau] = 1;
-        a.sen_mx[b * T + tau] = mx;
-        a.sen_pk[b * T + tau] = peak;
+      if (lane == 0) {
+        s_hay[tau] = 1;
+        s_mx[tau] = mx;
+        s_pk[tau] = peak;
       }
-    } else if (lane == 0 && blockIdx.y == 0) {
-      a.sen_hay[b * T + tau] = 0;
-      a.sen_mx[b * T + tau] = kProhibido;
-      a.sen_pk[b * T + tau] = 0.f;
+    } else if (lane == 0) {
+      s_hay[tau] = 0;
+      s_mx[tau] = kProhibido;
+      s_pk[tau] = 0.f;
     }
     if (Half) att = round_bf16(att);
     // sum over this table's slots of att * E[pos + 1][cols] (invalid slots have att 0 and read row 1)
@@ -306,12 +312,32 @@ __global__ void __launch_bounds__(kGenThreads) k_gen_attend(GenArgs a) {
     *reinterpret_cast<float4*>(&s_part[tau][4 * lane]) = make_float4(o[0], o[1], o[2], o[3]);
   }
   __syncthreads();
+  if (blockIdx.y == 0 && threadIdx.x < T) {
+    a.sen_hay[b * T + threadIdx.x] = s_hay[threadIdx.x];
+    a.sen_mx[b * T + threadIdx.x] = s_mx[threadIdx.x];
+    a.sen_pk[b * T + threadIdx.x] = s_pk[threadIdx.x];
+  }
+  if (ga.sigma && blockIdx.y == 0 && threadIdx.x == 0) {
+    GateArgs g = ga;
+    g.sen_hay = s_hay; g.sen_mx = s_mx; g.sen_pk = s_pk;
+    g.glogit = ga.glogit + b; g.vistos = ga.vistos + b * ga.n; g.hawkes = ga.hawkes + b * ga.n; g.racha = ga.racha + b;
+    float sg, ptc;
+    gate_of_token<Half>(g, 0, &sg, &ptc);
+    ga.sigma[b] = sg;
+  }
+  float pt1 = 1.f;
+  if (ga.cbuf) {
+    float pt = 0.f;
+    for (int tau = 0; tau < T; ++tau) pt = __fadd_rn(pt, (float)s_hay[tau]);
+    pt1 = fmaxf(pt, 1.f);
+  }
   if (threadIdx.x < kGenCols) {
     const int j = col0 + threadIdx.x;
     if (j < a.d) {
       float sum = 0.f;
       for (int tau = 0; tau < T; ++tau) sum = __fadd_rn(sum, s_part[tau][threadIdx.x]);
       a.acc[b * a.d + j] = sum;
+      if (ga.cbuf) ga.cbuf[b * a.d + j] = __float2bfloat16_rn(__fdiv_rn(sum, pt1));
     }
   }
 }
@@ -421,15 +447,15 @@ int launch_hawkes_build(int64_t B, int64_t L, int64_t ld, int n, const float* si
   return cudaGetLastError() == cudaSuccess ? ASRN_OK : ASRN_ERR_CUDA;
 }
 
-int launch_gen_attend(const GenArgs& a, bool half, cudaStream_t s) {
+int launch_gen_attend(const GenArgs& a, const GateArgs& ga, bool half, cudaStream_t s) {
   if (a.B == 0) return ASRN_OK;
   if (a.C > 32 || a.P > kMaxPhi || a.cf > kMaxConfirm || a.T > kMaxTables || a.K > kMaxSuffix) return ASRN_ERR_UNSUPPORTED;
   // 16-byte rows of phi / Kc and 4-column value loads
   const int vw = half ? 8 : 4;
   if (a.P % vw != 0 || a.cf % vw != 0 || a.d % 4 != 0) return ASRN_ERR_UNSUPPORTED;
   dim3 grid((unsigned)a.B, (unsigned)((a.d + kGenCols - 1) / kGenCols));
-  if (half) k_gen_attend<true><<<grid, kGenThreads, 0, s>>>(a);
-  else k_gen_attend<false><<<grid, kGenThreads, 0, s>>>(a);
+  if (half) k_gen_attend<true><<<grid, kGenThreads, 0, s>>>(a, ga);
+  else k_gen_attend<false><<<grid, kGenThreads, 0, s>>>(a, ga);
   return cudaGetLastError() == cudaSuccess ? ASRN_OK : ASRN_ERR_CUDA;
 }
 

@@ -254,14 +254,19 @@ class Writer:
         hay = torch.empty(B, T, dtype=torch.uint8, device=dev)
         mx = torch.empty(B, T, dtype=torch.float32, device=dev)
         pk = torch.empty(B, T, dtype=torch.float32, device=dev)
+        # bf16: the attention kernel also produces the gate's operand and gate values
+        cbuf = torch.empty(B, d, dtype=torch.bfloat16, device=dev) if half else None
+        sigma = torch.empty(B, dtype=torch.float32, device=dev) if half else None
+        gate_in = [_lib.ptr(x if half else None) for x in (glogit, vistos, hawkes, racha)]
         _lib.check(lib.asrn_gen_attend(cr, wr, pr, tp, self.cap, _lib.ptr(ids), _lib.ptr(phi), _lib.ptr(qc),
                                        _lib.ptr(kc), _lib.ptr(st.ring), _lib.ptr(self.sig), _lib.ptr(st.bt),
                                        _lib.ptr(st.la), _lib.ptr(st.phi), _lib.ptr(st.kc), _lib.ptr(self.ea),
-                                       _lib.ptr(acc), _lib.ptr(hay), _lib.ptr(mx), _lib.ptr(pk), s), 'asrn_gen_attend')
+                                       _lib.ptr(acc), _lib.ptr(hay), _lib.ptr(mx), _lib.ptr(pk), *gate_in,
+                                       _lib.ptr(cbuf), _lib.ptr(sigma), s), 'asrn_gen_attend')
         h_out = torch.empty(B, d, dtype=torch.float32, device=dev)
         _lib.check(lib.asrn_gen_gate(cr, wr, pr, _lib.ptr(h), _lib.ptr(glogit), _lib.ptr(acc), _lib.ptr(hay),
                                      _lib.ptr(mx), _lib.ptr(pk), _lib.ptr(vistos), _lib.ptr(hawkes), _lib.ptr(racha),
-                                     _lib.ptr(h_out), s), 'asrn_gen_gate')
+                                     _lib.ptr(h_out), _lib.ptr(cbuf), _lib.ptr(sigma), s), 'asrn_gen_gate')
         if not self.ajeno:
             _lib.check(lib.asrn_gen_ring_insert(B, T, nb, C, tp, _lib.ptr(ids), _lib.ptr(st.ring),
                                                 _lib.ptr(st.count), s), 'asrn_gen_ring_insert')

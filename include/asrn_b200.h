@@ -234,11 +234,11 @@ int asrn_gen_front(const asrn_layer_config* cfg, const asrn_layer_weights* w, co
                    float* log_alfa, float* glogit, float* sig, void* phi, uint16_t* ids, void* stream);
 
 /* Gate of the new tokens (asrn_gate's semantics for cfg->B * cfg->L rows, no workspace): W_ov is spread over d / 32
- * blocks. */
+ * blocks. cbuf / sigma (both or neither; bf16 mode): the operand and gate values asrn_gen_attend precomputed. */
 int asrn_gen_gate(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared, const float* h,
                   const float* glogit, const float* acc, const uint8_t* sen_hay, const float* sen_mx,
                   const float* sen_pk, const uint8_t* vistos, const float* hawkes, const float* racha, float* h_out,
-                  void* stream);
+                  const void* cbuf, const float* sigma, void* stream);
 
 /* n-gram memory of the new token at position *t_pos (its signature already in sig_cache): appends its clock
  * Bt[t] = Bt[t-1] + beta_t and log_alfa_t to the caches, then vistos (B, n), hawkes (B, n) from the Hawkes table
@@ -251,12 +251,15 @@ int asrn_gen_memory(const asrn_layer_config* cfg, const asrn_layer_weights* w, c
 /* The new token at position *t_pos (phi_t, Qc_t, Kc_t, ids_t; its clock / log_alfa already appended by
  * asrn_gen_memory) against the C candidates of each table from the rings: acc (B, d) = sum over tables of
  * att * E[k + 1] (summed in a fixed order: deterministic); per-table signals (B, T). Appends phi_t and Kc_t to the
- * caches. */
+ * caches. bf16 mode, optional (all six or none): given g(h) glogit (B), vistos (B, n), hawkes (B, n), racha (B) of
+ * the new token, it also writes the gate's operand cbuf (B, d) bf16 = bf16(acc / max(1, pt)) and gate values sigma
+ * (B), for asrn_gen_gate. */
 int asrn_gen_attend(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared,
                     const int64_t* t_pos, int64_t cap, const uint16_t* ids_t, const void* phi_t, const void* qc_t,
                     const void* kc_t, const int32_t* ring, const float* sig_cache, const double* bt_cache,
                     const float* la_cache, void* phi_cache, void* kc_cache, const void* ea_cache, float* acc,
-                    uint8_t* sen_hay, float* sen_mx, float* sen_pk, void* stream);
+                    uint8_t* sen_hay, float* sen_mx, float* sen_pk, const float* glogit, const uint8_t* vistos,
+                    const float* hawkes, const float* racha, void* cbuf, float* sigma, void* stream);
 
 /* Put position *t_pos into the ring of its bucket in every table. */
 int asrn_gen_ring_insert(int64_t B, int32_t T, int32_t nb, int32_t C, const int64_t* t_pos, const uint16_t* ids_t,
