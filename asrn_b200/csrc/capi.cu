@@ -535,4 +535,23 @@ int asrn_gen_gate(const asrn_layer_config* cfg, const asrn_layer_weights* w, con
   return launch_gen_gate(a, cfg->half != 0, as_stream(stream));
 }
 
+int asrn_local_in(int64_t B, int32_t d, int32_t k, const float* h_prev, const void* y_prev, float* h_out,
+                  const float* ln_w, const float* ln_b, float eps, void* win, int32_t half, void* stream) {
+  if (B < 0 || d < 1 || k < 1 || (B > 0 && (!h_prev || !ln_w || !ln_b || !win))) return ASRN_ERR_ARG;
+  if ((size_t)(2 * d + 32) * 4 > 48 * 1024) return ASRN_ERR_UNSUPPORTED;
+  return launch_local_in(B, d, k, h_prev, y_prev, h_out, ln_w, ln_b, eps, win, half != 0, as_stream(stream));
+}
+
+int asrn_local_mid(int64_t B, int32_t d, const float* h, const void* z, float* h1, const float* ln_w,
+                   const float* ln_b, float eps, void* v_out, int32_t half, void* stream) {
+  if (B < 0 || d < 1 || (B > 0 && (!h || !z || !h1 || !ln_w || !ln_b || !v_out))) return ASRN_ERR_ARG;
+  if ((size_t)(2 * d + 32) * 4 > 48 * 1024) return ASRN_ERR_UNSUPPORTED;
+  return launch_local_mid(B, d, h, z, h1, ln_w, ln_b, eps, v_out, half != 0, as_stream(stream));
+}
+
+int asrn_local_gelu(int64_t n, void* f, int32_t half, void* stream) {
+  if (n < 0 || (n > 0 && !f)) return ASRN_ERR_ARG;
+  return launch_local_gelu(n, f, half != 0, as_stream(stream));
+}
+
 }  // extern "C"

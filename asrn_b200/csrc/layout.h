@@ -187,6 +187,11 @@ struct GenArgs {
 };
 
 int launch_context(const ContextArgs& a, bool half, cudaStream_t s);
+int launch_local_in(int64_t B, int d, int k, const float* h_prev, const void* y_prev, float* h_out, const float* ln_w,
+                    const float* ln_b, float eps, void* win, bool half, cudaStream_t s);
+int launch_local_mid(int64_t B, int d, const float* h, const void* z, float* h1, const float* ln_w, const float* ln_b,
+                     float eps, void* v_out, bool half, cudaStream_t s);
+int launch_local_gelu(int64_t n, void* f, bool half, cudaStream_t s);
 int launch_shard_rows(int64_t rows, int64_t L, int C, int64_t q_lo, int64_t q_hi, const int32_t* orden,
                       const uint16_t* ids_o, int64_t Lv, int32_t* orden_v, uint16_t* ids_v, int64_t* counts,
                       int32_t pad_pos, cudaStream_t s);

@@ -158,59 +158,60 @@ __device__ __forceinline__ void tc_stage1(const ScoreArgs& a, const TcSmem& S, c
   }
 }
 
-// Scalars and feature rows of sub-tile t, one warp per slot: lane 0 derives (position, id, used) from the staging
-// buffer and writes them to the feature ring; cp.async gathers the clock (8 B), log_alfa and the previous signatures
-// (4 B each) and the phi / Qc / Kc rows (16 B chunks, zero-filled for slots outside the row).
+// Scalars and feature rows of sub-tile t, one warp per slot. Every lane derives (position, id, used) from the
+// staging buffer (lane 0 writes them to the feature ring) and copies its items of the slot in one pass: items
+// [0, cph) are 16-byte chunks of phi, then cpc chunks of Qc and of Kc, the clock (8 B), log_alfa (4 B) and the
+// kMaxSuffix previous signatures (4 B; NaN, never equal, before the text and past K). Slots outside the row get
+// zero-filled rows.
 __device__ __forceinline__ void tc_stage2_features(const ScoreArgs& a, const TcSmem& S, const TcBlock& k, int t) {
-  const __nv_bfloat16* phi = reinterpret_cast<const __nv_bfloat16*>(a.phi);
-  const __nv_bfloat16* Qc = reinterpret_cast<const __nv_bfloat16*>(a.Qc);
-  const __nv_bfloat16* Kc = reinterpret_cast<const __nv_bfloat16*>(a.Kc);
+  const char* phi = reinterpret_cast<const char*>(a.phi);
+  const char* Qc = reinterpret_cast<const char*>(a.Qc);
+  const char* Kc = reinterpret_cast<const char*>(a.Kc);
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
   const int buf = (t + 1) % kStage;
   const int cph = k.Ppad / 8, cpc = k.Cpad / 8;
-  const int per_slot = cph + 2 * cpc;
+  const int n_items = cph + 2 * cpc + 2 + kMaxSuffix;
   for (int i = wid; i < kQ; i += nw) {
     const int64_t s = k.S0 + (int64_t)t * kQ + i;
     const int fr = frow((t + 1) * kQ + i);
     const bool real = s >= 0 && s < a.L;
     const int pos = real ? S.st_pos[buf * kQ + i] : 0;
-    const int id = real ? (int)S.st_id[buf * kStageIds + i] : -1;
-    const bool used = real && s + 1 < a.L && (int)S.st_id[buf * kStageIds + i + 1] == id && pos + 1 < a.Lf;
-    const int64_t g = k.b * a.Lf + pos;
     if (lane == 0) {
+      const int id = real ? (int)S.st_id[buf * kStageIds + i] : -1;
+      const bool used = real && s + 1 < a.L && (int)S.st_id[buf * kStageIds + i + 1] == id && pos + 1 < a.Lf;
       S.pos[fr] = pos;
       S.id[fr] = id;
       S.used[fr] = used ? 1 : 0;
-      if (real) cp_async8(S.bt + fr, a.Bt + g);
-      else S.bt[fr] = 0.0;
-      if (real) cp_async4(S.la + fr, a.log_alfa + g);
-      else S.la[fr] = 0.f;
-    } else if (lane <= kMaxSuffix) {
-      // previous signatures sig[pos - 1 - c]; NaN (never equal) before the text and past K
-      const int c = lane - 1;
-      const int64_t tt = (int64_t)pos - 1 - c;
-      if (real && c < a.K && tt >= 0) cp_async4(S.pf + fr * kMaxSuffix + c, a.sig + k.b * a.Lf + tt);
-      else S.pf[fr * kMaxSuffix + c] = __int_as_float(0x7fc00000);
     }
-    for (int c = lane; c < per_slot; c += 32) {
-      if (c < cph) {
-        const int col = c * 8;
-        const bool ok = real && col < a.P;
-        cp_async16(S.phi + fr * S.Pp + col, phi + g * a.P + (ok ? col : 0), ok);
-      } else if (c < cph + cpc) {
-        const int col = (c - cph) * 8;
+    const int64_t g = k.b * a.Lf + pos;
+    for (int it = lane; it < n_items; it += 32) {
+      if (it < cph) {
+        const bool ok = real && it * 8 < a.P;
+        cp_async16(S.phi + fr * S.Pp + it * 8, phi + (g * a.P + (ok ? it * 8 : 0)) * 2, ok);
+      } else if (it < cph + 2 * cpc) {
+        const int c = it - cph;
+        const bool isq = c < cpc;
+        const int col = (isq ? c : c - cpc) * 8;
         const bool ok = real && col < a.cf;
-        cp_async16(S.qc + fr * S.Cp + col, Qc + g * a.cf + (ok ? col : 0), ok);
+        cp_async16((isq ? S.qc : S.kc) + fr * S.Cp + col, (isq ? Qc : Kc) + (g * a.cf + (ok ? col : 0)) * 2, ok);
+      } else if (it == cph + 2 * cpc) {
+        if (real) cp_async8(S.bt + fr, a.Bt + g);
+        else S.bt[fr] = 0.0;
+      } else if (it == cph + 2 * cpc + 1) {
+        if (real) cp_async4(S.la + fr, a.log_alfa + g);
+        else S.la[fr] = 0.f;
       } else {
-        const int col = (c - cph - cpc) * 8;
-        const bool ok = real && col < a.cf;
-        cp_async16(S.kc + fr * S.Cp + col, Kc + g * a.cf + (ok ? col : 0), ok);
+        const int c = it - (cph + 2 * cpc + 2);
+        const int64_t tt = (int64_t)pos - 1 - c;
+        if (real && c < a.K && tt >= 0) cp_async4(S.pf + fr * kMaxSuffix + c, a.sig + k.b * a.Lf + tt);
+        else S.pf[fr * kMaxSuffix + c] = __int_as_float(0x7fc00000);
       }
     }
   }
 }
 
-// Value rows Ea[pos + 1] of sub-tile t (its scalars already in the feature ring), one warp per slot.
+// Value rows Ea[pos + 1] of sub-tile t (its scalars already in the feature ring), one warp per slot: the row's
+// 16-byte chunks, lane-strided (consecutive lanes, consecutive chunks), from one base address per slot.
 __device__ __forceinline__ void tc_stage2_values(const ScoreArgs& a, const TcSmem& S, const TcBlock& k, int t) {
   const __nv_bfloat16* Ea = reinterpret_cast<const __nv_bfloat16*>(a.Ea);
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
@@ -219,8 +220,15 @@ __device__ __forceinline__ void tc_stage2_values(const ScoreArgs& a, const TcSme
     const int li = (t + 1) * kQ + i;
     const int fr = frow(li), vr = vrow(li);
     const bool used = S.used[fr] != 0;
-    const __nv_bfloat16* vsrc = Ea + (k.b * a.Lf + (used ? S.pos[fr] + 1 : 0)) * (int64_t)a.d + k.dp0;
-    for (int c = lane; c < cpv; c += 32) cp_async16(S.v + vr * S.Dp + c * 8, vsrc + (used ? c * 8 : 0), used);
+    const __nv_bfloat16* vsrc = Ea + (k.b * a.Lf + (used ? S.pos[fr] + 1 : 0)) * (int64_t)a.d + k.dp0 + lane * 8;
+    const uint32_t vdst = su32(S.v + vr * S.Dp + lane * 8);
+    for (int c = 0; c < cpv; c += 32) {
+      if (c + lane < cpv) {
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(vdst + 2u * (uint32_t)(c * 8)),
+                     "l"(vsrc + (used ? c * 8 : 0)), "r"(used ? 16 : 0)
+                     : "memory");
+      }
+    }
   }
 }
 

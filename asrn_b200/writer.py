@@ -96,7 +96,9 @@ class Writer:
         self.sig = torch.zeros(B, self.cap, dtype=torch.float32, device=dev)
         self.ea = torch.zeros(B, self.cap, d, dtype=act, device=dev)
         self.e_last = torch.zeros(B, d, dtype=torch.float32, device=dev)
-        self.buf = [torch.zeros(B, blq.k - 1, d, dtype=act, device=dev) for blq in m.bloques]
+        # per local block, its conv window: the LN1 outputs of the last k positions (oldest first)
+        self.buf = [torch.zeros(B, blq.k, d, dtype=act, device=dev) for blq in m.bloques]
+        self.lnf = torch.zeros(B, 1, d, dtype=act, device=dev)
         self.layers = [self._new_state(capa, B, dev) for capa in m.largos]
         lote = lote or max(1, min(B, (1 << 20) // max(L0, 1)))
         logits = [self._prompt(x0[b0:b0 + lote], b0) for b0 in range(0, B, lote)]
@@ -133,7 +135,7 @@ class Writer:
         h, j = E, 0
         for i, blq in enumerate(m.bloques):
             u = blq.ln1(h)
-            self.buf[i][b0:b1] = F.pad(u, (0, 0, blq.k - 1, 0))[:, L0:].to(act)
+            self.buf[i][b0:b1] = F.pad(u, (0, 0, blq.k, 0))[:, L0:].to(act)
             h = blq(h)
             if i in m.pos_largo:
                 h = self._prompt_layer(self.layers[j], E, h, xc, b0)
@@ -200,24 +202,44 @@ class Writer:
         self.graph = g
 
     def _step(self):
-        """The step's launches: position t is self.t_dev on the device, incremented at the end."""
+        """The step's launches: position t is self.t_dev on the device, incremented at the end. Per local block:
+        asrn_local_in (the previous block's residual, LN1, conv window), the conv GEMM, asrn_local_mid (GELU +
+        residual, LN2), the MLP GEMMs around asrn_local_gelu; the MLP output is added by the next block's
+        asrn_local_in (or before an ASRN layer / the head)."""
         m, sw, act, B = self.m, self.sw, self._act(), self.B
+        lib = _lib.lib()
+        s = _lib.stream_ptr(self.tok.device)
+        half = int(self.half)
         with torch.autocast('cuda', enabled=False):
             tok = self.tok
             e_t = F.embedding(tok, m.emb.weight)
             self.sig.index_copy_(1, self.t_dev, tok.to(torch.float32).view(B, 1))
             self.ea.index_copy_(1, self.t_dev, e_t.to(act).view(B, 1, -1))
-            h, j = e_t, 0
+            h, y, j = e_t, None, 0
+            d = h.shape[-1]
             for i, blq in enumerate(m.bloques):
                 wc, bc, w1, b1, w2, b2 = sw.blocks[i]
-                win = torch.cat([self.buf[i], _ln(blq.ln1, h).to(act).unsqueeze(1)], 1)
-                self.buf[i].copy_(win[:, 1:])
-                h = h + F.gelu(F.linear(win.reshape(B, -1), wc, bc))
-                h = h + F.linear(F.gelu(F.linear(_ln(blq.ln2, h).to(act), w1, b1)), w2, b2)
+                hin = torch.empty(B, d, dtype=torch.float32, device=h.device)
+                _lib.check(lib.asrn_local_in(B, d, blq.k, _lib.ptr(h), _lib.ptr(y), _lib.ptr(hin),
+                                             _lib.ptr(blq.ln1.weight), _lib.ptr(blq.ln1.bias), blq.ln1.eps,
+                                             _lib.ptr(self.buf[i]), half, s), 'asrn_local_in')
+                z = F.linear(self.buf[i].view(B, -1), wc, bc)
+                h1 = torch.empty(B, d, dtype=torch.float32, device=h.device)
+                v = torch.empty(B, d, dtype=act, device=h.device)
+                _lib.check(lib.asrn_local_mid(B, d, _lib.ptr(hin), _lib.ptr(z), _lib.ptr(h1),
+                                              _lib.ptr(blq.ln2.weight), _lib.ptr(blq.ln2.bias), blq.ln2.eps,
+                                              _lib.ptr(v), half, s), 'asrn_local_mid')
+                f = F.linear(v, w1, b1)
+                _lib.check(lib.asrn_local_gelu(f.numel(), _lib.ptr(f), half, s), 'asrn_local_gelu')
+                h, y = h1, F.linear(f, w2, b2)
                 if i in m.pos_largo:
-                    h = self._step_layer(self.layers[j], e_t, h.contiguous(), tok)
+                    h = self._step_layer(self.layers[j], e_t, h + y, tok)
+                    y = None
                     j += 1
-            lg = F.linear(_ln(m.ln_f, h).to(act), sw.head)
+            _lib.check(lib.asrn_local_in(B, d, 1, _lib.ptr(h), _lib.ptr(y), None, _lib.ptr(m.ln_f.weight),
+                                         _lib.ptr(m.ln_f.bias), m.ln_f.eps, _lib.ptr(self.lnf), half, s),
+                       'asrn_local_in')
+            lg = F.linear(self.lnf.view(B, d), sw.head)
             self.e_last.copy_(e_t)
             self.t_dev += 1
         return lg

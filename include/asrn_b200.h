@@ -153,6 +153,18 @@ int asrn_score(const asrn_layer_config* cfg, const asrn_layer_weights* w, const 
                const float* sig, const double* Bt, const float* log_alfa, const void* Ea, float* acc,
                uint8_t* sen_hay, float* sen_mx, float* sen_pk, void* stream);
 
+/* ---- local blocks of the model, one generation step (B rows; half: bf16 compute type, else fp32) ---------------
+ * The element-wise parts of BloqueLocal (asrn/nucleo.py:969-1014) around its three GEMMs, with the writer's conv
+ * buffer (asrn/nucleo.py:1816-1822): asrn_local_in: h = h_prev (+ y_prev, compute type, the previous block's MLP
+ * output; may be NULL) -> h_out (may be NULL), LN1(h) rounded to the compute type pushed into the conv window
+ * win (B, k, d) (rows shift down in place; k = 1 gives a plain LN into win); asrn_local_mid: h1 = h + act(gelu(z))
+ * and v_out = act(LN2(h1)); asrn_local_gelu: f = act(gelu(f)) in place (n values). */
+int asrn_local_in(int64_t B, int32_t d, int32_t k, const float* h_prev, const void* y_prev, float* h_out,
+                  const float* ln_w, const float* ln_b, float eps, void* win, int32_t half, void* stream);
+int asrn_local_mid(int64_t B, int32_t d, const float* h, const void* z, float* h1, const float* ln_w,
+                   const float* ln_b, float eps, void* v_out, int32_t half, void* stream);
+int asrn_local_gelu(int64_t n, void* f, int32_t half, void* stream);
+
 /* ---- sequence-chunk sharding (one long sequence over several GPUs) --------------------------------------------------
  * Each shard owns positions [q_lo, q_hi) of an L-position sequence and, after exchanging bucket ids and features,
  * holds them for all L positions. asrn_shard_rows turns full sorted rows (orden, ids_o: (rows, L) from
