@@ -111,6 +111,7 @@ ScoreArgs score_args(const asrn_layer_config& c, const asrn_layer_weights& w, co
   ScoreArgs a{};
   a.B = c.B; a.L = c.L; a.d = (int)c.d; a.T = c.n_tablas; a.nb = c.n_bits; a.P = c.n_tablas * c.n_bits;
   a.Lf = c.L; a.q_lo = 0; a.q_hi = c.L;
+  a.status = reinterpret_cast<int*>(const_cast<char*>(prep) + pl.status);
   a.C = c.chunk; a.cf = c.confirmar; a.K = c.sufijo;
   a.inv_temp_div = (float)sqrt((double)a.P);
   a.esc_c = (float)pow((double)c.confirmar, -0.5);

@@ -98,6 +98,7 @@ struct ScoreArgs {
   float* acc;
   uint8_t* sen_hay;
   float *sen_mx, *sen_pk;
+  int* status;             // device status word (bounded waits of the tensor-core path)
 };
 
 struct RepetitionArgs {

@@ -12,10 +12,15 @@
 // multiplies sub-tile i's weights by its value rows and reduces them into acc. The weights pass from A to B through
 // a double buffer; one block barrier per iteration. Every load is cp.async: the sorted entries of sub-tile i + 3,
 // the scalars and feature rows (phi, Qc, Kc) of sub-tile i + 2 into a 4-sub-tile feature ring, the value rows of
-// sub-tile i + 1 into a 3-sub-tile value ring; all land while the current iteration computes. d is split over two
-// blocks only when d > 768.
+// sub-tile i + 1 into a 3-sub-tile value ring; all land while the current iteration computes. The rows (phi, Qc,
+// Kc, values) move by bulk copies (cp.async.bulk, one per row, issued by one warp with lane = slot) counted on an
+// mbarrier per ring stage, so they do not occupy the warps' load slots; the small per-position gathers (clock,
+// log_alfa, previous signatures, the sorted entries) are cp.async. Rows that are not loaded (slots outside the row,
+// value rows no query uses) keep earlier finite contents (both rings are zeroed when the block starts): their scores
+// are masked and their weights are zero. d is split over two blocks only when d > 768.
 #include "common.cuh"
 #include "layout.h"
+#include "umma.cuh"
 
 namespace asrn {
 
@@ -46,6 +51,8 @@ struct TcSmem {
   float* sc;            // [32][65]
   __nv_bfloat16* att;   // [2][32][72]
   int* qhay;            // [2][32]
+  uint64_t* fbar;       // [4] feature-stage mbarriers
+  uint64_t* vbar;       // [3] value-stage mbarriers
   int Pp, Cp, Dp;
 };
 
@@ -63,6 +70,8 @@ __host__ __device__ inline size_t tc_smem_bytes(int P, int cf, int dpart) {
   b += (size_t)kQ * 65 * 4;
   b += 2 * (size_t)kQ * 72 * 2;
   b += 2 * kQ * 4;
+  b = (b + 15) / 16 * 16;
+  b += 8 * 8;                                    // mbarriers
   return b + 16;
 }
 
@@ -87,7 +96,10 @@ __device__ inline TcSmem carve_tc(char* base, int P, int cf, int dpart) {
   s.v = reinterpret_cast<__nv_bfloat16*>(p); p += (size_t)kRV * s.Dp * 2;
   s.sc = reinterpret_cast<float*>(p); p += kQ * 65 * 4;
   s.att = reinterpret_cast<__nv_bfloat16*>(p); p += 2 * kQ * 72 * 2;
-  s.qhay = reinterpret_cast<int*>(p);
+  s.qhay = reinterpret_cast<int*>(p); p += 2 * kQ * 4;
+  p = base + ((p - base) + 15) / 16 * 16;
+  s.fbar = reinterpret_cast<uint64_t*>(p); p += 4 * 8;
+  s.vbar = reinterpret_cast<uint64_t*>(p);
   return s;
 }
 
@@ -96,6 +108,18 @@ __device__ __forceinline__ int frow(int li) { return li & (kRF - 1); }
 __device__ __forceinline__ int vrow(int li) { return li % kRV; }
 
 __device__ __forceinline__ uint32_t su32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+// Bulk copy of `bytes` (a multiple of 16, 16-byte aligned ends) from global to shared memory, counted on `bar`.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(su32(dst)), "l"(src), "r"(bytes), "r"(su32(bar))
+               : "memory");
+}
+__device__ __forceinline__ int warp_sum_int(int v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(su32(dst)), "l"(src), "r"(valid ? 16 : 0)
@@ -158,77 +182,76 @@ __device__ __forceinline__ void tc_stage1(const ScoreArgs& a, const TcSmem& S, c
   }
 }
 
-// Scalars and feature rows of sub-tile t, one warp per slot. Every lane derives (position, id, used) from the
-// staging buffer (lane 0 writes them to the feature ring) and copies its items of the slot in one pass: items
-// [0, cph) are 16-byte chunks of phi, then cpc chunks of Qc and of Kc, the clock (8 B), log_alfa (4 B) and the
-// kMaxSuffix previous signatures (4 B; NaN, never equal, before the text and past K). Slots outside the row get
-// zero-filled rows.
-__device__ __forceinline__ void tc_stage2_features(const ScoreArgs& a, const TcSmem& S, const TcBlock& k, int t) {
-  const char* phi = reinterpret_cast<const char*>(a.phi);
-  const char* Qc = reinterpret_cast<const char*>(a.Qc);
-  const char* Kc = reinterpret_cast<const char*>(a.Kc);
+// Scalars and feature rows of sub-tile t. The slot scalars: warp per slot, lane 0 derives (position, id, used) from
+// the staging buffer and writes them to the feature ring, lanes 1.. gather the clock (8 B), log_alfa and the
+// kMaxSuffix previous signatures (4 B; NaN, never equal, before the text and past K) by cp.async. The phi / Qc / Kc
+// rows: warp `issuer`, lane = slot, one bulk copy per row onto the stage's mbarrier.
+__device__ __forceinline__ void tc_stage2_features(const ScoreArgs& a, const TcSmem& S, const TcBlock& k, int t,
+                                                   int issuer) {
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
   const int buf = (t + 1) % kStage;
-  const int cph = k.Ppad / 8, cpc = k.Cpad / 8;
-  const int n_items = cph + 2 * cpc + 2 + kMaxSuffix;
   for (int i = wid; i < kQ; i += nw) {
     const int64_t s = k.S0 + (int64_t)t * kQ + i;
     const int fr = frow((t + 1) * kQ + i);
     const bool real = s >= 0 && s < a.L;
     const int pos = real ? S.st_pos[buf * kQ + i] : 0;
+    const int64_t g = k.b * a.Lf + pos;
     if (lane == 0) {
       const int id = real ? (int)S.st_id[buf * kStageIds + i] : -1;
       const bool used = real && s + 1 < a.L && (int)S.st_id[buf * kStageIds + i + 1] == id && pos + 1 < a.Lf;
       S.pos[fr] = pos;
       S.id[fr] = id;
       S.used[fr] = used ? 1 : 0;
+      if (real) cp_async8(S.bt + fr, a.Bt + g);
+      else S.bt[fr] = 0.0;
+    } else if (lane == 1) {
+      if (real) cp_async4(S.la + fr, a.log_alfa + g);
+      else S.la[fr] = 0.f;
+    } else if (lane < 2 + kMaxSuffix) {
+      const int c = lane - 2;
+      const int64_t tt = (int64_t)pos - 1 - c;
+      if (real && c < a.K && tt >= 0) cp_async4(S.pf + fr * kMaxSuffix + c, a.sig + k.b * a.Lf + tt);
+      else S.pf[fr * kMaxSuffix + c] = __int_as_float(0x7fc00000);
     }
+  }
+  if (wid == issuer) {
+    const int i = lane;
+    const int64_t s = k.S0 + (int64_t)t * kQ + i;
+    const int fr = frow((t + 1) * kQ + i);
+    const bool real = s >= 0 && s < a.L;
+    const int pos = real ? S.st_pos[buf * kQ + i] : 0;
     const int64_t g = k.b * a.Lf + pos;
-    for (int it = lane; it < n_items; it += 32) {
-      if (it < cph) {
-        const bool ok = real && it * 8 < a.P;
-        cp_async16(S.phi + fr * S.Pp + it * 8, phi + (g * a.P + (ok ? it * 8 : 0)) * 2, ok);
-      } else if (it < cph + 2 * cpc) {
-        const int c = it - cph;
-        const bool isq = c < cpc;
-        const int col = (isq ? c : c - cpc) * 8;
-        const bool ok = real && col < a.cf;
-        cp_async16((isq ? S.qc : S.kc) + fr * S.Cp + col, (isq ? Qc : Kc) + (g * a.cf + (ok ? col : 0)) * 2, ok);
-      } else if (it == cph + 2 * cpc) {
-        if (real) cp_async8(S.bt + fr, a.Bt + g);
-        else S.bt[fr] = 0.0;
-      } else if (it == cph + 2 * cpc + 1) {
-        if (real) cp_async4(S.la + fr, a.log_alfa + g);
-        else S.la[fr] = 0.f;
-      } else {
-        const int c = it - (cph + 2 * cpc + 2);
-        const int64_t tt = (int64_t)pos - 1 - c;
-        if (real && c < a.K && tt >= 0) cp_async4(S.pf + fr * kMaxSuffix + c, a.sig + k.b * a.Lf + tt);
-        else S.pf[fr * kMaxSuffix + c] = __int_as_float(0x7fc00000);
-      }
+    const uint32_t bphi = (uint32_t)a.P * 2, bc = (uint32_t)a.cf * 2;
+    const int total = warp_sum_int(real ? (int)(bphi + 2 * bc) : 0);
+    uint64_t* bar = S.fbar + ((t + 1) & 3);
+    if (lane == 0) umma::mbar_expect_tx(bar, (uint32_t)total);
+    __syncwarp();
+    if (real) {
+      bulk_load(S.phi + fr * S.Pp, reinterpret_cast<const __nv_bfloat16*>(a.phi) + g * a.P, bphi, bar);
+      bulk_load(S.qc + fr * S.Cp, reinterpret_cast<const __nv_bfloat16*>(a.Qc) + g * a.cf, bc, bar);
+      bulk_load(S.kc + fr * S.Cp, reinterpret_cast<const __nv_bfloat16*>(a.Kc) + g * a.cf, bc, bar);
     }
   }
 }
 
-// Value rows Ea[pos + 1] of sub-tile t (its scalars already in the feature ring), one warp per slot: the row's
-// 16-byte chunks, lane-strided (consecutive lanes, consecutive chunks), from one base address per slot.
-__device__ __forceinline__ void tc_stage2_values(const ScoreArgs& a, const TcSmem& S, const TcBlock& k, int t) {
-  const __nv_bfloat16* Ea = reinterpret_cast<const __nv_bfloat16*>(a.Ea);
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  const int cpv = k.dpart / 8;
-  for (int i = wid; i < kQ; i += nw) {
-    const int li = (t + 1) * kQ + i;
-    const int fr = frow(li), vr = vrow(li);
-    const bool used = S.used[fr] != 0;
-    const __nv_bfloat16* vsrc = Ea + (k.b * a.Lf + (used ? S.pos[fr] + 1 : 0)) * (int64_t)a.d + k.dp0 + lane * 8;
-    const uint32_t vdst = su32(S.v + vr * S.Dp + lane * 8);
-    for (int c = 0; c < cpv; c += 32) {
-      if (c + lane < cpv) {
-        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(vdst + 2u * (uint32_t)(c * 8)),
-                     "l"(vsrc + (used ? c * 8 : 0)), "r"(used ? 16 : 0)
-                     : "memory");
-      }
-    }
+// Value rows Ea[pos + 1] of sub-tile t (its scalars already in the feature ring): warp `issuer`, lane = slot, one
+// bulk copy per used row onto the stage's mbarrier.
+__device__ __forceinline__ void tc_stage2_values(const ScoreArgs& a, const TcSmem& S, const TcBlock& k, int t,
+                                                 int issuer) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  if (wid != issuer) return;
+  const int li = (t + 1) * kQ + lane;
+  const int fr = frow(li), vr = vrow(li);
+  const bool used = S.used[fr] != 0;
+  const uint32_t bytes = (uint32_t)k.dpart * 2;
+  const int total = warp_sum_int(used ? (int)bytes : 0);
+  uint64_t* bar = S.vbar + ((t + 1) % 3);
+  if (lane == 0) umma::mbar_expect_tx(bar, (uint32_t)total);
+  __syncwarp();
+  if (used) {
+    const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(a.Ea) + (k.b * a.Lf + S.pos[fr] + 1) *
+                               (int64_t)a.d + k.dp0;
+    bulk_load(S.v + vr * S.Dp, src, bytes, bar);
   }
 }
 
@@ -453,30 +476,58 @@ __global__ void __launch_bounds__(kThreadsTc, 1) k_score_tc(ScoreArgs a, int nds
   const bool group_a = wid < kGroupWarps;
   const int ntile = (int)((k.S1 - k.S0 + kQ - 1) / kQ);
 
-  // prologue: sub-tiles -1 (the first window half) and 0 ready, the scores of 0 taken, 1 and 2 on their way
+  // zero both rings once (rows never loaded keep finite contents), set up the stage barriers
+  {
+    uint4* z0 = reinterpret_cast<uint4*>(S.phi);
+    const int nz = (int)(((char*)(S.v + kRV * S.Dp) - (char*)S.phi) / 16);
+    for (int i = threadIdx.x; i < nz; i += blockDim.x) z0[i] = make_uint4(0, 0, 0, 0);
+    umma::fence_proxy_async();                 // the zeros precede the bulk copies into the same rows
+    if (threadIdx.x == 0) {
+      for (int i = 0; i < 4; ++i) umma::mbar_init(S.fbar + i, 1);
+      for (int i = 0; i < 3; ++i) umma::mbar_init(S.vbar + i, 1);
+      umma::fence_mbar_init();
+    }
+  }
+  // bounded waits for the bulk copies of a stage, by every thread (each observes the completed phase)
+  auto wait_features = [&](int t) {
+    umma::mbar_wait(S.fbar + ((t + 1) & 3), (uint32_t)(((t + 1) >> 2) & 1), a.status);
+  };
+  auto wait_values = [&](int t) {
+    umma::mbar_wait(S.vbar + ((t + 1) % 3), (uint32_t)(((t + 1) / 3) & 1), a.status);
+  };
+  constexpr int kIssueF = 0, kIssueV = kGroupWarps;   // issuing warps of the feature / value bulk copies
+
+  // prologue: sub-tiles -1 (the first window half), 0 and 1 of the features, -1 and 0 of the values, the scores of
+  // 0 taken; sub-tile 2's sorted entries on their way
+  __syncthreads();
   tc_stage1(a, S, k, -1);
   tc_stage1(a, S, k, 0);
   if (ntile > 1) tc_stage1(a, S, k, 1);
   cp_async_commit();
   cp_async_wait_all();
   __syncthreads();
-  tc_stage2_features(a, S, k, -1);
-  tc_stage2_features(a, S, k, 0);
-  if (ntile > 1) tc_stage2_features(a, S, k, 1);
+  tc_stage2_features(a, S, k, -1, kIssueF);
+  tc_stage2_features(a, S, k, 0, kIssueF + 1);
+  if (ntile > 1) tc_stage2_features(a, S, k, 1, kIssueF + 2);
   cp_async_commit();
   cp_async_wait_all();
+  wait_features(-1);
+  wait_features(0);
+  if (ntile > 1) wait_features(1);
   __syncthreads();
-  tc_stage2_values(a, S, k, -1);
-  tc_stage2_values(a, S, k, 0);
+  tc_stage2_values(a, S, k, -1, kIssueV);
+  tc_stage2_values(a, S, k, 0, kIssueV + 1);
   if (ntile > 2) tc_stage1(a, S, k, 2);        // its buffer was read by sub-tile -1's feature stage above
   cp_async_commit();
   if (group_a) tc_scores(a, S, k, 0);
   cp_async_wait_all();
+  wait_values(-1);
+  wait_values(0);
   __syncthreads();
 
   for (int i = 0; i < ntile; ++i) {
-    if (i + 2 < ntile) tc_stage2_features(a, S, k, i + 2);
-    if (i + 1 < ntile) tc_stage2_values(a, S, k, i + 1);
+    if (i + 2 < ntile) tc_stage2_features(a, S, k, i + 2, kIssueF);
+    if (i + 1 < ntile) tc_stage2_values(a, S, k, i + 1, kIssueV);
     if (i + 3 < ntile) tc_stage1(a, S, k, i + 3);
     cp_async_commit();
     if (group_a) {
@@ -485,6 +536,8 @@ __global__ void __launch_bounds__(kThreadsTc, 1) k_score_tc(ScoreArgs a, int nds
       tc_values(a, S, k, i, wid - kGroupWarps);
     }
     cp_async_wait_all();
+    if (i + 2 < ntile) wait_features(i + 2);
+    if (i + 1 < ntile) wait_values(i + 1);
     __syncthreads();
   }
 }
