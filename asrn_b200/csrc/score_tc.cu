@@ -12,12 +12,12 @@
 // multiplies sub-tile i's weights by its value rows and reduces them into acc. The weights pass from A to B through
 // a double buffer; one block barrier per iteration. Every load is cp.async: the sorted entries of sub-tile i + 3,
 // the scalars and feature rows (phi, Qc, Kc) of sub-tile i + 2 into a 4-sub-tile feature ring, the value rows of
-// sub-tile i + 1 into a 3-sub-tile value ring; all land while the current iteration computes. The rows (phi, Qc,
-// Kc, values) move by bulk copies (cp.async.bulk, one per row, issued by one warp with lane = slot) counted on an
-// mbarrier per ring stage, so they do not occupy the warps' load slots; the small per-position gathers (clock,
-// log_alfa, previous signatures, the sorted entries) are cp.async. Rows that are not loaded (slots outside the row,
-// value rows no query uses) keep earlier finite contents (both rings are zeroed when the block starts): their scores
-// are masked and their weights are zero. d is split over two blocks only when d > 768.
+// sub-tile i + 1 into a 3-sub-tile value ring; all land while the current iteration computes. The value rows move
+// by bulk copies (cp.async.bulk, one per used row) counted on an mbarrier per ring stage, so the largest transfers do
+// not occupy the warps' load slots; value rows no query uses are not loaded and keep earlier finite contents (the
+// ring is zeroed when the block starts), multiplied by zero weights. The feature rows and the small per-position
+// gathers (clock, log_alfa, previous signatures, the sorted entries) are cp.async. d is split over two blocks only
+// when d > 768.
 #include "common.cuh"
 #include "layout.h"
 #include "umma.cuh"
@@ -51,7 +51,6 @@ struct TcSmem {
   float* sc;            // [32][65]
   __nv_bfloat16* att;   // [2][32][72]
   int* qhay;            // [2][32]
-  uint64_t* fbar;       // [4] feature-stage mbarriers
   uint64_t* vbar;       // [3] value-stage mbarriers
   int Pp, Cp, Dp;
 };
@@ -98,7 +97,6 @@ __device__ inline TcSmem carve_tc(char* base, int P, int cf, int dpart) {
   s.att = reinterpret_cast<__nv_bfloat16*>(p); p += 2 * kQ * 72 * 2;
   s.qhay = reinterpret_cast<int*>(p); p += 2 * kQ * 4;
   p = base + ((p - base) + 15) / 16 * 16;
-  s.fbar = reinterpret_cast<uint64_t*>(p); p += 4 * 8;
   s.vbar = reinterpret_cast<uint64_t*>(p);
   return s;
 }
@@ -182,76 +180,78 @@ __device__ __forceinline__ void tc_stage1(const ScoreArgs& a, const TcSmem& S, c
   }
 }
 
-// Scalars and feature rows of sub-tile t. The slot scalars: warp per slot, lane 0 derives (position, id, used) from
-// the staging buffer and writes them to the feature ring, lanes 1.. gather the clock (8 B), log_alfa and the
-// kMaxSuffix previous signatures (4 B; NaN, never equal, before the text and past K) by cp.async. The phi / Qc / Kc
-// rows: warp `issuer`, lane = slot, one bulk copy per row onto the stage's mbarrier.
-__device__ __forceinline__ void tc_stage2_features(const ScoreArgs& a, const TcSmem& S, const TcBlock& k, int t,
-                                                   int issuer) {
+// Scalars and feature rows of sub-tile t, one warp per slot. Lane 0 derives (position, id, used) from the staging
+// buffer and writes them to the feature ring; the lanes copy the slot's items in one pass by cp.async: 16-byte
+// chunks of phi, Qc and Kc (zero-filled outside the row), the clock (8 B), log_alfa (4 B) and the kMaxSuffix previous
+// signatures (4 B; NaN, never equal, before the text and past K).
+__device__ __forceinline__ void tc_stage2_features(const ScoreArgs& a, const TcSmem& S, const TcBlock& k, int t) {
+  const char* phi = reinterpret_cast<const char*>(a.phi);
+  const char* Qc = reinterpret_cast<const char*>(a.Qc);
+  const char* Kc = reinterpret_cast<const char*>(a.Kc);
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
   const int buf = (t + 1) % kStage;
+  const int cph = k.Ppad / 8, cpc = k.Cpad / 8;
+  const int n_items = cph + 2 * cpc + 2 + kMaxSuffix;
   for (int i = wid; i < kQ; i += nw) {
     const int64_t s = k.S0 + (int64_t)t * kQ + i;
     const int fr = frow((t + 1) * kQ + i);
     const bool real = s >= 0 && s < a.L;
     const int pos = real ? S.st_pos[buf * kQ + i] : 0;
-    const int64_t g = k.b * a.Lf + pos;
     if (lane == 0) {
       const int id = real ? (int)S.st_id[buf * kStageIds + i] : -1;
       const bool used = real && s + 1 < a.L && (int)S.st_id[buf * kStageIds + i + 1] == id && pos + 1 < a.Lf;
       S.pos[fr] = pos;
       S.id[fr] = id;
       S.used[fr] = used ? 1 : 0;
-      if (real) cp_async8(S.bt + fr, a.Bt + g);
-      else S.bt[fr] = 0.0;
-    } else if (lane == 1) {
-      if (real) cp_async4(S.la + fr, a.log_alfa + g);
-      else S.la[fr] = 0.f;
-    } else if (lane < 2 + kMaxSuffix) {
-      const int c = lane - 2;
-      const int64_t tt = (int64_t)pos - 1 - c;
-      if (real && c < a.K && tt >= 0) cp_async4(S.pf + fr * kMaxSuffix + c, a.sig + k.b * a.Lf + tt);
-      else S.pf[fr * kMaxSuffix + c] = __int_as_float(0x7fc00000);
     }
-  }
-  if (wid == issuer) {
-    const int i = lane;
-    const int64_t s = k.S0 + (int64_t)t * kQ + i;
-    const int fr = frow((t + 1) * kQ + i);
-    const bool real = s >= 0 && s < a.L;
-    const int pos = real ? S.st_pos[buf * kQ + i] : 0;
     const int64_t g = k.b * a.Lf + pos;
-    const uint32_t bphi = (uint32_t)a.P * 2, bc = (uint32_t)a.cf * 2;
-    const int total = warp_sum_int(real ? (int)(bphi + 2 * bc) : 0);
-    uint64_t* bar = S.fbar + ((t + 1) & 3);
-    if (lane == 0) umma::mbar_expect_tx(bar, (uint32_t)total);
-    __syncwarp();
-    if (real) {
-      bulk_load(S.phi + fr * S.Pp, reinterpret_cast<const __nv_bfloat16*>(a.phi) + g * a.P, bphi, bar);
-      bulk_load(S.qc + fr * S.Cp, reinterpret_cast<const __nv_bfloat16*>(a.Qc) + g * a.cf, bc, bar);
-      bulk_load(S.kc + fr * S.Cp, reinterpret_cast<const __nv_bfloat16*>(a.Kc) + g * a.cf, bc, bar);
+    for (int it = lane; it < n_items; it += 32) {
+      if (it < cph) {
+        const bool ok = real && it * 8 < a.P;
+        cp_async16(S.phi + fr * S.Pp + it * 8, phi + (g * a.P + (ok ? it * 8 : 0)) * 2, ok);
+      } else if (it < cph + 2 * cpc) {
+        const int c = it - cph;
+        const bool isq = c < cpc;
+        const int col = (isq ? c : c - cpc) * 8;
+        const bool ok = real && col < a.cf;
+        cp_async16((isq ? S.qc : S.kc) + fr * S.Cp + col, (isq ? Qc : Kc) + (g * a.cf + (ok ? col : 0)) * 2, ok);
+      } else if (it == cph + 2 * cpc) {
+        if (real) cp_async8(S.bt + fr, a.Bt + g);
+        else S.bt[fr] = 0.0;
+      } else if (it == cph + 2 * cpc + 1) {
+        if (real) cp_async4(S.la + fr, a.log_alfa + g);
+        else S.la[fr] = 0.f;
+      } else {
+        const int c = it - (cph + 2 * cpc + 2);
+        const int64_t tt = (int64_t)pos - 1 - c;
+        if (real && c < a.K && tt >= 0) cp_async4(S.pf + fr * kMaxSuffix + c, a.sig + k.b * a.Lf + tt);
+        else S.pf[fr * kMaxSuffix + c] = __int_as_float(0x7fc00000);
+      }
     }
   }
 }
 
-// Value rows Ea[pos + 1] of sub-tile t (its scalars already in the feature ring): warp `issuer`, lane = slot, one
-// bulk copy per used row onto the stage's mbarrier.
-__device__ __forceinline__ void tc_stage2_values(const ScoreArgs& a, const TcSmem& S, const TcBlock& k, int t,
-                                                 int issuer) {
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  if (wid != issuer) return;
-  const int li = (t + 1) * kQ + lane;
-  const int fr = frow(li), vr = vrow(li);
-  const bool used = S.used[fr] != 0;
-  const uint32_t bytes = (uint32_t)k.dpart * 2;
-  const int total = warp_sum_int(used ? (int)bytes : 0);
+// Value rows Ea[pos + 1] of sub-tile t (its scalars already in the feature ring): one bulk copy per used row onto
+// the stage's mbarrier, issued by lane 0 of warp slot % 16 (spread over the warps). Thread 0 first sets the stage's
+// transaction count from the used flags (arrive.expect_tx); the copies follow a block barrier.
+__device__ __forceinline__ int tc_value_bytes(const TcSmem& S, const TcBlock& k, int t) {
+  int n = 0;
+  for (int i = 0; i < kQ; ++i) n += S.used[frow((t + 1) * kQ + i)];
+  return n * k.dpart * 2;
+}
+__device__ __forceinline__ void tc_stage2_values(const ScoreArgs& a, const TcSmem& S, const TcBlock& k, int t) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  if (lane != 0) return;
   uint64_t* bar = S.vbar + ((t + 1) % 3);
-  if (lane == 0) umma::mbar_expect_tx(bar, (uint32_t)total);
-  __syncwarp();
-  if (used) {
-    const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(a.Ea) + (k.b * a.Lf + S.pos[fr] + 1) *
-                               (int64_t)a.d + k.dp0;
-    bulk_load(S.v + vr * S.Dp, src, bytes, bar);
+  const uint32_t bytes = (uint32_t)k.dpart * 2;
+  for (int i = wid; i < kQ; i += nw) {
+    const int li = (t + 1) * kQ + i;
+    const int fr = frow(li), vr = vrow(li);
+    if (S.used[fr]) {
+      const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(a.Ea) + (k.b * a.Lf + S.pos[fr] + 1) *
+                                 (int64_t)a.d + k.dp0;
+      bulk_load(S.v + vr * S.Dp, src, bytes, bar);
+    }
   }
 }
 
@@ -483,19 +483,18 @@ __global__ void __launch_bounds__(kThreadsTc, 1) k_score_tc(ScoreArgs a, int nds
     for (int i = threadIdx.x; i < nz; i += blockDim.x) z0[i] = make_uint4(0, 0, 0, 0);
     umma::fence_proxy_async();                 // the zeros precede the bulk copies into the same rows
     if (threadIdx.x == 0) {
-      for (int i = 0; i < 4; ++i) umma::mbar_init(S.fbar + i, 1);
       for (int i = 0; i < 3; ++i) umma::mbar_init(S.vbar + i, 1);
       umma::fence_mbar_init();
     }
   }
-  // bounded waits for the bulk copies of a stage, by every thread (each observes the completed phase)
-  auto wait_features = [&](int t) {
-    umma::mbar_wait(S.fbar + ((t + 1) & 3), (uint32_t)(((t + 1) >> 2) & 1), a.status);
-  };
+  // bounded wait for the value bulk copies of a stage, by every thread (each observes the completed phase)
   auto wait_values = [&](int t) {
     umma::mbar_wait(S.vbar + ((t + 1) % 3), (uint32_t)(((t + 1) / 3) & 1), a.status);
   };
-  constexpr int kIssueF = 0, kIssueV = kGroupWarps;   // issuing warps of the feature / value bulk copies
+  // the stage's transaction count (its used rows) is set by thread 0 before any copy of the stage is issued
+  auto expect_values = [&](int t) {
+    if (threadIdx.x == 0) umma::mbar_expect_tx(S.vbar + ((t + 1) % 3), (uint32_t)tc_value_bytes(S, k, t));
+  };
 
   // prologue: sub-tiles -1 (the first window half), 0 and 1 of the features, -1 and 0 of the values, the scores of
   // 0 taken; sub-tile 2's sorted entries on their way
@@ -506,19 +505,19 @@ __global__ void __launch_bounds__(kThreadsTc, 1) k_score_tc(ScoreArgs a, int nds
   cp_async_commit();
   cp_async_wait_all();
   __syncthreads();
-  tc_stage2_features(a, S, k, -1, kIssueF);
-  tc_stage2_features(a, S, k, 0, kIssueF + 1);
-  if (ntile > 1) tc_stage2_features(a, S, k, 1, kIssueF + 2);
+  tc_stage2_features(a, S, k, -1);
+  tc_stage2_features(a, S, k, 0);
+  if (ntile > 1) tc_stage2_features(a, S, k, 1);
   cp_async_commit();
   cp_async_wait_all();
-  wait_features(-1);
-  wait_features(0);
-  if (ntile > 1) wait_features(1);
   __syncthreads();
-  tc_stage2_values(a, S, k, -1, kIssueV);
-  tc_stage2_values(a, S, k, 0, kIssueV + 1);
+  expect_values(-1);
+  expect_values(0);
   if (ntile > 2) tc_stage1(a, S, k, 2);        // its buffer was read by sub-tile -1's feature stage above
   cp_async_commit();
+  __syncthreads();
+  tc_stage2_values(a, S, k, -1);
+  tc_stage2_values(a, S, k, 0);
   if (group_a) tc_scores(a, S, k, 0);
   cp_async_wait_all();
   wait_values(-1);
@@ -526,17 +525,21 @@ __global__ void __launch_bounds__(kThreadsTc, 1) k_score_tc(ScoreArgs a, int nds
   __syncthreads();
 
   for (int i = 0; i < ntile; ++i) {
-    if (i + 2 < ntile) tc_stage2_features(a, S, k, i + 2, kIssueF);
-    if (i + 1 < ntile) tc_stage2_values(a, S, k, i + 1, kIssueV);
+    // value rows of i + 1 (their scalars arrived with the features in iteration i - 1): count, then copy
+    if (i + 1 < ntile) expect_values(i + 1);
+    if (i + 2 < ntile) tc_stage2_features(a, S, k, i + 2);
     if (i + 3 < ntile) tc_stage1(a, S, k, i + 3);
     cp_async_commit();
+    if (i + 1 < ntile) {
+      asm volatile("bar.sync 2, 512;" ::: "memory");   // the expect_tx precedes every copy of the stage
+      tc_stage2_values(a, S, k, i + 1);
+    }
     if (group_a) {
       if (i + 1 < ntile) tc_scores(a, S, k, i + 1);
     } else {
       tc_values(a, S, k, i, wid - kGroupWarps);
     }
     cp_async_wait_all();
-    if (i + 2 < ntile) wait_features(i + 2);
     if (i + 1 < ntile) wait_values(i + 1);
     __syncthreads();
   }
