@@ -256,71 +256,96 @@ __device__ __forceinline__ void tc_stage2_values(const ScoreArgs& a, const TcSme
 }
 
 // Group A: scores of sub-tile t (queries: window slots 32 .. 63; keys: 0 .. 63, slot q0 - 32 + key), the exact-mask
-// softmax, the weights into att[t & 1] and the per-table gate signals. Warp w (0-7): n-tile w of both m-tiles.
+// softmax, the weights into att[t & 1] and the per-table gate signals. Warp w (0-7) owns n-tile w (keys 8w .. 8w + 7)
+// of both m-tiles: the two MMA chains run interleaved on the same key fragments, then one epilogue pass over the
+// warp's 8 elements per lane; the softmax takes the warp's 4 queries in one set of shuffle rounds.
 __device__ __forceinline__ void tc_scores(const ScoreArgs& a, const TcSmem& S, const TcBlock& k, int t) {
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const int C = a.C;
   const int64_t q0 = k.S0 + (int64_t)t * kQ;
   const int lb = t * kQ;                        // window index of key 0 (li of slot q0 - 32)
   const int nt = wid;
+  // band: keys [8 nt, 8 nt + 8) meet queries [16 mt, 16 mt + 16) only if some key is within C before one of them
+  bool band[2];
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt) band[mt] = nt * 8 + 7 >= mt * 16 + 32 - C && nt * 8 < mt * 16 + 16 + 32;
+  float cphi[2][4] = {}, cqk[2][4] = {};
+  if (band[0] || band[1]) {
+    const int ka = (lane >> 4) * 8;
+    const int rk = frow(lb + nt * 8 + (lane & 7));
+    const int kb = ((lane >> 3) & 1) * 8;
+    const int ra0 = frow(lb + kQ + (lane & 15)), ra1 = frow(lb + kQ + 16 + (lane & 15));
+    const uint32_t phi_b = su32(S.phi) + 2u * (uint32_t)(rk * S.Pp + kb);
+    const uint32_t kc_b = su32(S.kc) + 2u * (uint32_t)(rk * S.Cp + kb);
+    const uint32_t phi_a0 = su32(S.phi) + 2u * (uint32_t)(ra0 * S.Pp + ka);
+    const uint32_t phi_a1 = su32(S.phi) + 2u * (uint32_t)(ra1 * S.Pp + ka);
+    const uint32_t qc_a0 = su32(S.qc) + 2u * (uint32_t)(ra0 * S.Cp + ka);
+    const uint32_t qc_a1 = su32(S.qc) + 2u * (uint32_t)(ra1 * S.Cp + ka);
+    for (int k0 = 0; k0 < k.Ppad; k0 += 16) {
+      uint32_t b0, b1;
+      ldsm_x2(phi_b + 2 * k0, b0, b1);
+      if (band[0]) {
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4(phi_a0 + 2 * k0, a0, a1, a2, a3);
+        mma16816(cphi[0], a0, a1, a2, a3, b0, b1);
+      }
+      if (band[1]) {
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4(phi_a1 + 2 * k0, a0, a1, a2, a3);
+        mma16816(cphi[1], a0, a1, a2, a3, b0, b1);
+      }
+    }
+    for (int k0 = 0; k0 < k.Cpad; k0 += 16) {
+      uint32_t b0, b1;
+      ldsm_x2(kc_b + 2 * k0, b0, b1);
+      if (band[0]) {
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4(qc_a0 + 2 * k0, a0, a1, a2, a3);
+        mma16816(cqk[0], a0, a1, a2, a3, b0, b1);
+      }
+      if (band[1]) {
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4(qc_a1 + 2 * k0, a0, a1, a2, a3);
+        mma16816(cqk[1], a0, a1, a2, a3, b0, b1);
+      }
+    }
+  }
+  // this lane's four query rows (g, g + 8, 16 + g, 24 + g; g = lane / 4) and two key columns (kj0, kj0 + 1): their
+  // ring-row scalars are read once; the suffix length is the count of leading equal previous signatures
+  const int g4 = lane >> 2, kj0 = nt * 8 + (lane & 3) * 2;
+  int q_id[4], k_id[2];
+  float4 q_pf[4][2], k_pf[2][2];
+  double q_bt[4], k_bt[2];
+  float k_la[2];
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int rq = frow(lb + kQ + g4 + 8 * u);
+    q_id[u] = S.id[rq];
+    q_pf[u][0] = *reinterpret_cast<const float4*>(S.pf + rq * kMaxSuffix);
+    q_pf[u][1] = *reinterpret_cast<const float4*>(S.pf + rq * kMaxSuffix + 4);
+    q_bt[u] = S.bt[rq];
+  }
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const int rk = frow(lb + kj0 + u);
+    k_id[u] = S.id[rk];
+    k_pf[u][0] = *reinterpret_cast<const float4*>(S.pf + rk * kMaxSuffix);
+    k_pf[u][1] = *reinterpret_cast<const float4*>(S.pf + rk * kMaxSuffix + 4);
+    k_bt[u] = S.bt[rk];
+    k_la[u] = S.la[rk];
+  }
 #pragma unroll
   for (int mt = 0; mt < 2; ++mt) {
-    float cphi[4] = {0.f, 0.f, 0.f, 0.f}, cqk[4] = {0.f, 0.f, 0.f, 0.f};
-    // band: this tile's keys [8 nt, 8 nt + 8) meet queries [16 mt, 16 mt + 16) only if some key is within C before
-    const int key_lo = nt * 8, q_lo = mt * 16;
-    const bool band = key_lo + 7 >= q_lo + 32 - C && key_lo < q_lo + 16 + 32;
-    if (band) {
-      const int ra = frow(lb + kQ + mt * 16 + (lane & 15));
-      const int ka = (lane >> 4) * 8;
-      const int rk = frow(lb + nt * 8 + (lane & 7));
-      const int kb = ((lane >> 3) & 1) * 8;
-      const uint32_t phi_a = su32(S.phi) + 2u * (uint32_t)(ra * S.Pp + ka);
-      const uint32_t phi_b = su32(S.phi) + 2u * (uint32_t)(rk * S.Pp + kb);
-      const uint32_t qc_a = su32(S.qc) + 2u * (uint32_t)(ra * S.Cp + ka);
-      const uint32_t kc_b = su32(S.kc) + 2u * (uint32_t)(rk * S.Cp + kb);
-      for (int k0 = 0; k0 < k.Ppad; k0 += 16) {
-        uint32_t a0, a1, a2, a3, b0, b1;
-        ldsm_x4(phi_a + 2 * k0, a0, a1, a2, a3);
-        ldsm_x2(phi_b + 2 * k0, b0, b1);
-        mma16816(cphi, a0, a1, a2, a3, b0, b1);
-      }
-      for (int k0 = 0; k0 < k.Cpad; k0 += 16) {
-        uint32_t a0, a1, a2, a3, b0, b1;
-        ldsm_x4(qc_a + 2 * k0, a0, a1, a2, a3);
-        ldsm_x2(kc_b + 2 * k0, b0, b1);
-        mma16816(cqk, a0, a1, a2, a3, b0, b1);
-      }
-    }
-    // this lane's two query rows (qi0, qi0 + 8) and two key columns (kj0, kj0 + 1): their ring-row scalars are read
-    // once; the suffix length is the count of leading equal previous signatures (compare mask, no branches)
-    const int qi0 = mt * 16 + (lane >> 2), kj0 = nt * 8 + (lane & 3) * 2;
-    int q_id[2], k_id[2];
-    float4 q_pf[2][2], k_pf[2][2];
-    double q_bt[2], k_bt[2];
-    float k_la[2];
-#pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      const int rq = frow(lb + kQ + qi0 + 8 * u), rk = frow(lb + kj0 + u);
-      q_id[u] = S.id[rq];
-      k_id[u] = S.id[rk];
-      q_pf[u][0] = *reinterpret_cast<const float4*>(S.pf + rq * kMaxSuffix);
-      q_pf[u][1] = *reinterpret_cast<const float4*>(S.pf + rq * kMaxSuffix + 4);
-      k_pf[u][0] = *reinterpret_cast<const float4*>(S.pf + rk * kMaxSuffix);
-      k_pf[u][1] = *reinterpret_cast<const float4*>(S.pf + rk * kMaxSuffix + 4);
-      q_bt[u] = S.bt[rq];
-      k_bt[u] = S.bt[rk];
-      k_la[u] = S.la[rk];
-    }
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      const int uq = e >> 1, uk = e & 1;
-      const int qi = qi0 + 8 * uq;
+      const int uq = 2 * mt + (e >> 1), uk = e & 1;
+      const int qi = g4 + 8 * uq;
       const int kj = kj0 + uk;
       const int64_t sq = q0 + qi, sk = q0 - kQ + kj;
       float val = -INFINITY;
-      if (band && kj < qi + 32 && kj >= qi + 32 - C && sq < a.L && sk >= 0 && k_id[uk] == q_id[uq]) {
-        const float s1 = round_bf16(__fdiv_rn(round_bf16(cphi[e]), a.inv_temp_div));
-        const float s2 = round_bf16(__fmul_rn(round_bf16(cqk[e]), a.esc_c));
+      if (band[mt] && kj < qi + 32 && kj >= qi + 32 - C && sq < a.L && sk >= 0 && k_id[uk] == q_id[uq]) {
+        const float s1 = round_bf16(__fdiv_rn(round_bf16(cphi[mt][e]), a.inv_temp_div));
+        const float s2 = round_bf16(__fmul_rn(round_bf16(cqk[mt][e]), a.esc_c));
         float t1 = round_bf16(__fadd_rn(s1, s2));
         const float4 qa = q_pf[uq][0], qb = q_pf[uq][1], ka = k_pf[uk][0], kb = k_pf[uk][1];
         const uint32_t eq = (qa.x == ka.x ? 1u : 0u) | (qa.y == ka.y ? 2u : 0u) | (qa.z == ka.z ? 4u : 0u) |
@@ -336,69 +361,59 @@ __device__ __forceinline__ void tc_scores(const ScoreArgs& a, const TcSmem& S, c
     }
   }
   bar_group_a();
-  // softmax: warp w -> queries 4w .. 4w + 3, two at a time; lane -> keys lane, lane + 32
+  // softmax: warp w -> queries 4w .. 4w + 3 together; lane -> keys lane, lane + 32
   __nv_bfloat16* att = S.att + (t & 1) * kQ * 72;
   int* qhay = S.qhay + (t & 1) * kQ;
+  const int qa = wid * 4;
+  float x[4][2], m[4], sum[4], e[4][2];
+  unsigned bal[4];
 #pragma unroll
-  for (int pr = 0; pr < 2; ++pr) {
-    const int qa = wid * 4 + pr * 2;
-    float x[2][2];
-    bool vv[2][2];
+  for (int u = 0; u < 4; ++u) {
+    x[u][0] = S.sc[(qa + u) * 65 + lane];
+    x[u][1] = S.sc[(qa + u) * 65 + lane + 32];
+    bal[u] = __ballot_sync(0xffffffffu, x[u][0] != -INFINITY || x[u][1] != -INFINITY);
+    m[u] = fmaxf(x[u][0], x[u][1]);
+  }
 #pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      x[u][0] = S.sc[(qa + u) * 65 + lane];
-      x[u][1] = S.sc[(qa + u) * 65 + lane + 32];
-      vv[u][0] = x[u][0] != -INFINITY;
-      vv[u][1] = x[u][1] != -INFINITY;
-    }
-    const unsigned bal0 = __ballot_sync(0xffffffffu, vv[0][0] || vv[0][1]);
-    const unsigned bal1 = __ballot_sync(0xffffffffu, vv[1][0] || vv[1][1]);
-    float m0 = fmaxf(x[0][0], x[0][1]), m1 = fmaxf(x[1][0], x[1][1]);
+  for (int o = 16; o > 0; o >>= 1)
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, o));
-      m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, o));
-    }
-    const float mxs[2] = {m0, m1};
-    float e[2][2], sum[2];
+    for (int u = 0; u < 4; ++u) m[u] = fmaxf(m[u], __shfl_xor_sync(0xffffffffu, m[u], o));
 #pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      e[u][0] = vv[u][0] ? expf(__fsub_rn(x[u][0], mxs[u])) : 0.f;
-      e[u][1] = vv[u][1] ? expf(__fsub_rn(x[u][1], mxs[u])) : 0.f;
-      sum[u] = e[u][0] + e[u][1];
-    }
+  for (int u = 0; u < 4; ++u) {
+    e[u][0] = x[u][0] != -INFINITY ? expf(__fsub_rn(x[u][0], m[u])) : 0.f;
+    e[u][1] = x[u][1] != -INFINITY ? expf(__fsub_rn(x[u][1], m[u])) : 0.f;
+    sum[u] = e[u][0] + e[u][1];
+  }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      sum[0] += __shfl_xor_sync(0xffffffffu, sum[0], o);
-      sum[1] += __shfl_xor_sync(0xffffffffu, sum[1], o);
-    }
+  for (int o = 16; o > 0; o >>= 1)
 #pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      const int qi = qa + u;
-      const int64_t sq = q0 + qi;
-      const bool anyv = (u == 0 ? bal0 : bal1) != 0;
-      const int posq = S.pos[frow(lb + kQ + qi)];
-      const bool mine = sq < k.S1 && posq >= a.q_lo && posq < a.q_hi;   // else a key only (another shard's position)
-      const int64_t gq = k.b * (a.q_hi - a.q_lo) + (posq - a.q_lo);
-      float w0 = 0.f, w1 = 0.f;
-      if (anyv) {
-        w0 = __fdiv_rn(e[u][0], sum[u]);
-        w1 = __fdiv_rn(e[u][1], sum[u]);
-        // the largest weight is the maximum's: exp(0) / sum
-        if (lane == 0 && k.write_signals && mine) {
-          a.sen_hay[gq * a.T + k.tau] = 1;
-          a.sen_mx[gq * a.T + k.tau] = mxs[u];
-          a.sen_pk[gq * a.T + k.tau] = __fdiv_rn(1.f, sum[u]);
-        }
-      } else if (lane == 0 && k.write_signals && mine) {
-        a.sen_hay[gq * a.T + k.tau] = 0;
-        a.sen_mx[gq * a.T + k.tau] = kProhibido;
-        a.sen_pk[gq * a.T + k.tau] = 0.f;
+    for (int u = 0; u < 4; ++u) sum[u] += __shfl_xor_sync(0xffffffffu, sum[u], o);
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int qi = qa + u;
+    const int64_t sq = q0 + qi;
+    const bool anyv = bal[u] != 0;
+    const int posq = S.pos[frow(lb + kQ + qi)];
+    const bool mine = sq < k.S1 && posq >= a.q_lo && posq < a.q_hi;   // else a key only (another shard's position)
+    const int64_t gq = k.b * (a.q_hi - a.q_lo) + (posq - a.q_lo);
+    float w0 = 0.f, w1 = 0.f;
+    if (anyv) {
+      w0 = __fdiv_rn(e[u][0], sum[u]);
+      w1 = __fdiv_rn(e[u][1], sum[u]);
+      // the largest weight is the maximum's: exp(0) / sum
+      if (lane == 0 && k.write_signals && mine) {
+        a.sen_hay[gq * a.T + k.tau] = 1;
+        a.sen_mx[gq * a.T + k.tau] = m[u];
+        a.sen_pk[gq * a.T + k.tau] = __fdiv_rn(1.f, sum[u]);
       }
-      att[qi * 72 + lane] = __float2bfloat16_rn(w0);
-      att[qi * 72 + lane + 32] = __float2bfloat16_rn(w1);
-      if (lane == 0) qhay[qi] = (anyv && mine) ? 1 : 0;
+    } else if (lane == 0 && k.write_signals && mine) {
+      a.sen_hay[gq * a.T + k.tau] = 0;
+      a.sen_mx[gq * a.T + k.tau] = kProhibido;
+      a.sen_pk[gq * a.T + k.tau] = 0.f;
     }
+    att[qi * 72 + lane] = __float2bfloat16_rn(w0);
+    att[qi * 72 + lane + 32] = __float2bfloat16_rn(w1);
+    if (lane == 0) qhay[qi] = (anyv && mine) ? 1 : 0;
   }
 }
 

@@ -59,6 +59,25 @@ __device__ __forceinline__ void dot_rows(const float* const* x, const W* const* 
   for (int k = 0; k < kDotWays; ++k) r[k] = warp_sum(acc[k]);
 }
 
+// sum_j x[j] * w[j], both in shared memory (w: act-typed row of d values, 16-byte aligned); result in every lane.
+template <typename W>
+__device__ __forceinline__ float dot_row_smem(const float* x, const W* w, int d, int lane) {
+  constexpr int VW = 16 / sizeof(W);
+  float acc = 0.f;
+  for (int v = lane; v < d / VW; v += 32) {
+    const uint4 raw = *reinterpret_cast<const uint4*>(w + v * VW);
+    float xv[VW];
+#pragma unroll
+    for (int e4 = 0; e4 < VW / 4; ++e4) {
+      const float4 q = *reinterpret_cast<const float4*>(x + v * VW + 4 * e4);
+      xv[4 * e4] = q.x; xv[4 * e4 + 1] = q.y; xv[4 * e4 + 2] = q.z; xv[4 * e4 + 3] = q.w;
+    }
+#pragma unroll
+    for (int e = 0; e < VW; ++e) acc = fmaf(xv[e], chunk_elem<W>(raw, e), acc);
+  }
+  return warp_sum(acc);
+}
+
 __device__ __forceinline__ float block_sum(float v, float* red) {
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   v = warp_sum(v);
@@ -89,7 +108,7 @@ __global__ void __launch_bounds__(kFrontThreads) k_gen_front(GenFrontArgs a) {
   float* s_dot = s_p + d;          // nq dot products
   float* s_hid = s_dot + ((nq + 3) & ~3);   // 2m hidden (after GELU), 16-byte aligned
   float* s_phi = s_hid + 2 * m;    // P
-  float* s_red = s_phi + P;        // 32
+  float* s_red = s_phi + ((P + 3) & ~3);   // 32, then the weight double buffer (16-byte aligned)
 
   const float* hrow = a.h + b * d;
   float s = 0.f;
@@ -115,46 +134,60 @@ __global__ void __launch_bounds__(kFrontThreads) k_gen_front(GenFrontArgs a) {
   __syncthreads();
 
   // dot products: [0, 2cf) Qc / Kc; 2cf, 2cf + 1 the clock projection; 2cf + 2 g(h); then the 3m hidden sums
-  // hp = act(E_t) . pal0, ca = act(E_t) . ctx0[:, :d], cb = act(E_{t-1}) . ctx0[:, d:]. The act-typed rows go
-  // kDotWays at a time per warp; the three fp32 rows one by one.
+  // hp = act(E_t) . pal0, ca = act(E_t) . ctx0[:, :d], cb = act(E_{t-1}) . ctx0[:, d:]. The act-typed weight rows
+  // ([cq; ck] then the 3m hidden rows) stream through a double buffer of kFrontRows-row chunks by cp.async, a chunk in
+  // flight while the previous one is consumed (warp w: rows w and w + 16 of the chunk); the three fp32 rows are
+  // read directly by the last warp of the first chunk.
   const AT* wctx = reinterpret_cast<const AT*>(a.wctx);
   const AT* w1 = reinterpret_cast<const AT*>(a.w1);
   const int nact = 2 * cf + 3 * m;                        // act-typed rows: Qc/Kc then the hidden sums
-  for (int q0 = wid * kDotWays; q0 < nact; q0 += nw * kDotWays) {
-    const float* xs[kDotWays];
-    const AT* ws[kDotWays];
-    const int nrows = nact - q0 < kDotWays ? nact - q0 : kDotWays;
-#pragma unroll
-    for (int k = 0; k < kDotWays; ++k) {
-      const int q = q0 + (k < nrows ? k : 0);
-      if (q < 2 * cf) { xs[k] = s_hna; ws[k] = wctx + (int64_t)q * d; }
-      else {
-        const int i = q - 2 * cf;
-        xs[k] = i < 2 * m ? s_e : s_p;
-        ws[k] = w1 + (int64_t)i * d;
+  constexpr int kFrontRows = Half ? 32 : 16;
+  AT* s_w = reinterpret_cast<AT*>(s_red + 32);            // [2][kFrontRows][d] act weights
+  const int nch = (nact + kFrontRows - 1) / kFrontRows;
+  const int vpr = d * (int)sizeof(AT) / 16;               // 16-byte chunks per row
+  auto issue = [&](int c) {
+    AT* dst = s_w + (c & 1) * kFrontRows * d;
+    const int r0 = c * kFrontRows;
+    const int tot = kFrontRows * vpr;
+    for (int e = tid; e < tot; e += kFrontThreads) {
+      const int r = e / vpr, v = e % vpr;
+      const int q = r0 + r;
+      if (q < nact) {
+        const AT* src = (q < 2 * cf ? wctx + (int64_t)q * d : w1 + (int64_t)(q - 2 * cf) * d) + v * (16 / sizeof(AT));
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(
+                         dst + r * d + v * (16 / sizeof(AT)))), "l"(src) : "memory");
       }
     }
-    float r[kDotWays];
-    dot_rows<AT>(xs, ws, nrows, d, lane, r);
-    if (lane == 0) {
-      for (int k = 0; k < nrows; ++k) {
-        const int q = q0 + k;
-        s_dot[q < 2 * cf ? q : q + 3] = r[k];
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  issue(0);
+  if (nch > 1) issue(1);
+  for (int c = 0; c < nch; ++c) {
+    if (c + 1 < nch) asm volatile("cp.async.wait_group 1;" ::: "memory");
+    else asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncthreads();
+    const AT* wbuf = s_w + (c & 1) * kFrontRows * d;
+    for (int r = wid; r < kFrontRows; r += nw) {
+      const int q = c * kFrontRows + r;
+      if (q >= nact) break;
+      const float* x = q < 2 * cf ? s_hna : ((q - 2 * cf) < 2 * m ? s_e : s_p);
+      const float r0 = dot_row_smem<AT>(x, wbuf + r * d, d, lane);
+      if (lane == 0) s_dot[q < 2 * cf ? q : q + 3] = r0;
+    }
+    if (c == 0 && wid == nw - 1) {
+      const float* xs[kDotWays] = {s_hn, s_hn, s_h, s_h};
+      const float* ws[kDotWays] = {a.w_reloj, a.w_reloj + d, a.g_w, a.g_w};
+      float r[kDotWays];
+      dot_rows<float>(xs, ws, 3, d, lane, r);
+      if (lane == 0) {
+        s_dot[2 * cf] = r[0];
+        s_dot[2 * cf + 1] = r[1];
+        s_dot[2 * cf + 2] = r[2];
       }
     }
+    __syncthreads();
+    if (c + 2 < nch) issue(c + 2);
   }
-  if (wid == nw - 1) {
-    const float* xs[kDotWays] = {s_hn, s_hn, s_h, s_h};
-    const float* ws[kDotWays] = {a.w_reloj, a.w_reloj + d, a.g_w, a.g_w};
-    float r[kDotWays];
-    dot_rows<float>(xs, ws, 3, d, lane, r);
-    if (lane == 0) {
-      s_dot[2 * cf] = r[0];
-      s_dot[2 * cf + 1] = r[1];
-      s_dot[2 * cf + 2] = r[2];
-    }
-  }
-  __syncthreads();
 
   if (tid < 2 * cf) {
     AT* dst = reinterpret_cast<AT*>(tid < cf ? a.Qc : a.Kc);
@@ -203,8 +236,10 @@ __global__ void __launch_bounds__(kFrontThreads) k_gen_front(GenFrontArgs a) {
   }
 }
 
-size_t gen_front_smem(const GenFrontArgs& a) {
-  return sizeof(float) * (5 * (size_t)a.d + ((2 * a.cf + 3 + 3 * a.m + 3) & ~3) + 2 * a.m + a.P + 32);
+size_t gen_front_smem(const GenFrontArgs& a, bool half) {
+  const size_t f = sizeof(float) * (5 * (size_t)a.d + ((2 * a.cf + 3 + 3 * a.m + 3) & ~3) + 2 * a.m + ((a.P + 3) & ~3) + 32);
+  const size_t rows = half ? 32 : 16, es = half ? 2 : 4;
+  return ((f + 15) / 16) * 16 + 2 * rows * (size_t)a.d * es;
 }
 
 int launch_gen_front(const GenFrontArgs& a, bool half, cudaStream_t s) {
@@ -212,8 +247,8 @@ int launch_gen_front(const GenFrontArgs& a, bool half, cudaStream_t s) {
   // 16-byte weight rows: d and m multiples of 8 (bf16) / 4 (fp32); the prepared buffer's rows are then aligned
   if (a.d % 8 != 0 || a.m % 8 != 0) return ASRN_ERR_UNSUPPORTED;
   if ((reinterpret_cast<uintptr_t>(a.w_reloj) | reinterpret_cast<uintptr_t>(a.g_w)) & 15) return ASRN_ERR_ARG;
-  const size_t smem = gen_front_smem(a);
-  if (smem > 200 * 1024) return ASRN_ERR_UNSUPPORTED;
+  const size_t smem = gen_front_smem(a, half);
+  if (smem > 220 * 1024) return ASRN_ERR_UNSUPPORTED;
   if (half) {
     cudaFuncSetAttribute(k_gen_front<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     k_gen_front<true><<<(unsigned)a.B, kFrontThreads, smem, s>>>(a);
