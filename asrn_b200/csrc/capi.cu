@@ -514,6 +514,7 @@ int asrn_gen_front(const asrn_layer_config* cfg, const asrn_layer_weights* w, co
   a.w2 = prep + pl.w2; a.b2 = reinterpret_cast<const float*>(prep + pl.b2);
   a.beta_max = cfg->beta_max; a.log_alfa_min = cfg->log_alfa_min;
   a.Qc = Qc; a.Kc = Kc; a.beta = beta; a.log_alfa = log_alfa; a.glogit = glogit; a.sig = sig; a.phi = phi; a.ids = ids;
+  a.status = reinterpret_cast<int*>(const_cast<char*>(prep) + pl.status);
   return launch_gen_front(a, cfg->half != 0, as_stream(stream));
 }
 
@@ -538,15 +539,13 @@ int asrn_gen_gate(const asrn_layer_config* cfg, const asrn_layer_weights* w, con
 
 int asrn_local_in(int64_t B, int32_t d, int32_t k, const float* h_prev, const void* y_prev, float* h_out,
                   const float* ln_w, const float* ln_b, float eps, void* win, int32_t half, void* stream) {
-  if (B < 0 || d < 1 || k < 1 || (B > 0 && (!h_prev || !ln_w || !ln_b || !win))) return ASRN_ERR_ARG;
-  if ((size_t)(2 * d + 32) * 4 > 48 * 1024) return ASRN_ERR_UNSUPPORTED;
+  if (B < 0 || d < 1 || k < 1 || k > 16 || (B > 0 && (!h_prev || !ln_w || !ln_b || !win))) return ASRN_ERR_ARG;
   return launch_local_in(B, d, k, h_prev, y_prev, h_out, ln_w, ln_b, eps, win, half != 0, as_stream(stream));
 }
 
 int asrn_local_mid(int64_t B, int32_t d, const float* h, const void* z, float* h1, const float* ln_w,
                    const float* ln_b, float eps, void* v_out, int32_t half, void* stream) {
   if (B < 0 || d < 1 || (B > 0 && (!h || !z || !h1 || !ln_w || !ln_b || !v_out))) return ASRN_ERR_ARG;
-  if ((size_t)(2 * d + 32) * 4 > 48 * 1024) return ASRN_ERR_UNSUPPORTED;
   return launch_local_mid(B, d, h, z, h1, ln_w, ln_b, eps, v_out, half != 0, as_stream(stream));
 }
 

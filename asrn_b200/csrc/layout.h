@@ -156,6 +156,7 @@ struct GenFrontArgs {
   float *log_alfa, *glogit, *sig;  // (B)
   void* phi;               // act (B, P)
   uint16_t* ids;           // (B, T)
+  int* status;             // device status word (bounded waits)
 };
 
 // One generation step of one layer: B sequences, the new token at position t of caches of `cap` positions.

@@ -8,6 +8,7 @@
 // The gate of the new tokens (k_gen_gate_tc) is in gate.cu, beside the gate's other kernels.
 #include "common.cuh"
 #include "layout.h"
+#include "umma.cuh"
 
 namespace asrn {
 
@@ -135,9 +136,10 @@ __global__ void __launch_bounds__(kFrontThreads) k_gen_front(GenFrontArgs a) {
 
   // dot products: [0, 2cf) Qc / Kc; 2cf, 2cf + 1 the clock projection; 2cf + 2 g(h); then the 3m hidden sums
   // hp = act(E_t) . pal0, ca = act(E_t) . ctx0[:, :d], cb = act(E_{t-1}) . ctx0[:, d:]. The act-typed weight rows
-  // ([cq; ck] then the 3m hidden rows) stream through a double buffer of kFrontRows-row chunks by cp.async, a chunk in
-  // flight while the previous one is consumed (warp w: rows w and w + 16 of the chunk); the three fp32 rows are
-  // read directly by the last warp of the first chunk.
+  // ([cq; ck] then the 3m hidden rows) stream through a double buffer of kFrontRows-row chunks (48 KB) by bulk copies
+  // on an mbarrier per buffer (bounded waits), a chunk in flight while the previous one is consumed (warp w: rows w and
+  // w + 16 of the chunk); block b starts at chunk b % (number of chunks). The three fp32 rows are read directly by
+  // the last warp during the first chunk.
   const AT* wctx = reinterpret_cast<const AT*>(a.wctx);
   const AT* w1 = reinterpret_cast<const AT*>(a.w1);
   const int nact = 2 * cf + 3 * m;                        // act-typed rows: Qc/Kc then the hidden sums
@@ -145,30 +147,44 @@ __global__ void __launch_bounds__(kFrontThreads) k_gen_front(GenFrontArgs a) {
   AT* s_w = reinterpret_cast<AT*>(s_red + 32);            // [2][kFrontRows][d] act weights
   const int nch = (nact + kFrontRows - 1) / kFrontRows;
   const int vpr = d * (int)sizeof(AT) / 16;               // 16-byte chunks per row
+  const int rot = (int)(blockIdx.x % nch);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(s_w + 2 * kFrontRows * d);     // [2] buffer-full barriers
+  if (tid == 0) {
+    umma::mbar_init(bar, 1);
+    umma::mbar_init(bar + 1, 1);
+    umma::fence_mbar_init();
+  }
+  __syncthreads();
+  // chunk c (rows of the rotated order) into buffer c & 1: one or two bulk copies (the rows of [cq; ck] and of w1
+  // are contiguous in the prepared buffer), counted on bar[c & 1]
   auto issue = [&](int c) {
+    if (tid != 0) return;
+    const int r0 = ((c + rot) % nch) * kFrontRows;
+    const int r1 = min(r0 + kFrontRows, nact);
     AT* dst = s_w + (c & 1) * kFrontRows * d;
-    const int r0 = c * kFrontRows;
-    const int tot = kFrontRows * vpr;
-    for (int e = tid; e < tot; e += kFrontThreads) {
-      const int r = e / vpr, v = e % vpr;
-      const int q = r0 + r;
-      if (q < nact) {
-        const AT* src = (q < 2 * cf ? wctx + (int64_t)q * d : w1 + (int64_t)(q - 2 * cf) * d) + v * (16 / sizeof(AT));
-        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(
-                         dst + r * d + v * (16 / sizeof(AT)))), "l"(src) : "memory");
-      }
-    }
-    asm volatile("cp.async.commit_group;" ::: "memory");
+    const uint32_t row_bytes = (uint32_t)d * sizeof(AT);
+    umma::mbar_expect_tx(bar + (c & 1), (uint32_t)(r1 - r0) * row_bytes);
+    const int a0 = r0, a1 = min(r1, 2 * cf);
+    if (a1 > a0)
+      asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                   ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(wctx + (int64_t)a0 * d),
+                   "r"((uint32_t)(a1 - a0) * row_bytes), "r"((uint32_t)__cvta_generic_to_shared(bar + (c & 1)))
+                   : "memory");
+    const int b0 = max(r0, 2 * cf), b1 = r1;
+    if (b1 > b0)
+      asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                   ::"r"((uint32_t)__cvta_generic_to_shared(dst + (b0 - r0) * d)),
+                   "l"(w1 + (int64_t)(b0 - 2 * cf) * d), "r"((uint32_t)(b1 - b0) * row_bytes),
+                   "r"((uint32_t)__cvta_generic_to_shared(bar + (c & 1)))
+                   : "memory");
   };
   issue(0);
   if (nch > 1) issue(1);
   for (int c = 0; c < nch; ++c) {
-    if (c + 1 < nch) asm volatile("cp.async.wait_group 1;" ::: "memory");
-    else asm volatile("cp.async.wait_group 0;" ::: "memory");
-    __syncthreads();
+    umma::mbar_wait(bar + (c & 1), (uint32_t)((c >> 1) & 1), a.status);
     const AT* wbuf = s_w + (c & 1) * kFrontRows * d;
     for (int r = wid; r < kFrontRows; r += nw) {
-      const int q = c * kFrontRows + r;
+      const int q = ((c + rot) % nch) * kFrontRows + r;
       if (q >= nact) break;
       const float* x = q < 2 * cf ? s_hna : ((q - 2 * cf) < 2 * m ? s_e : s_p);
       const float r0 = dot_row_smem<AT>(x, wbuf + r * d, d, lane);
@@ -185,7 +201,7 @@ __global__ void __launch_bounds__(kFrontThreads) k_gen_front(GenFrontArgs a) {
         s_dot[2 * cf + 2] = r[2];
       }
     }
-    __syncthreads();
+    __syncthreads();                       // buffer c & 1 consumed
     if (c + 2 < nch) issue(c + 2);
   }
 
@@ -239,7 +255,7 @@ __global__ void __launch_bounds__(kFrontThreads) k_gen_front(GenFrontArgs a) {
 size_t gen_front_smem(const GenFrontArgs& a, bool half) {
   const size_t f = sizeof(float) * (5 * (size_t)a.d + ((2 * a.cf + 3 + 3 * a.m + 3) & ~3) + 2 * a.m + ((a.P + 3) & ~3) + 32);
   const size_t rows = half ? 32 : 16, es = half ? 2 : 4;
-  return ((f + 15) / 16) * 16 + 2 * rows * (size_t)a.d * es;
+  return ((f + 15) / 16) * 16 + 2 * rows * (size_t)a.d * es + 16;
 }
 
 int launch_gen_front(const GenFrontArgs& a, bool half, cudaStream_t s) {

@@ -157,8 +157,8 @@ int asrn_score(const asrn_layer_config* cfg, const asrn_layer_weights* w, const 
  * The element-wise parts of BloqueLocal (asrn/nucleo.py:969-1014) around its three GEMMs, with the writer's conv
  * buffer (asrn/nucleo.py:1816-1822): asrn_local_in: h = h_prev (+ y_prev, compute type, the previous block's MLP
  * output; may be NULL) -> h_out (may be NULL), LN1(h) rounded to the compute type pushed into the conv window
- * win (B, k, d) (rows shift down in place; k = 1 gives a plain LN into win); asrn_local_mid: h1 = h + act(gelu(z))
- * and v_out = act(LN2(h1)); asrn_local_gelu: f = act(gelu(f)) in place (n values). */
+ * win (B, k, d) (rows shift down in place; 1 <= k <= 16; k = 1 gives a plain LN into win); asrn_local_mid: h1 = h + act(gelu(z))
+ * and v_out = act(LN2(h1)); asrn_local_gelu: f = act(gelu(f)) in place (n values). d <= 1024. */
 int asrn_local_in(int64_t B, int32_t d, int32_t k, const float* h_prev, const void* y_prev, float* h_out,
                   const float* ln_w, const float* ln_b, float eps, void* win, int32_t half, void* stream);
 int asrn_local_mid(int64_t B, int32_t d, const float* h, const void* z, float* h1, const float* ln_w,
