@@ -148,13 +148,23 @@ __global__ void __launch_bounds__(kFrontThreads) k_gen_front(GenFrontArgs a) {
   const int nch = (nact + kFrontRows - 1) / kFrontRows;
   const int vpr = d * (int)sizeof(AT) / 16;               // 16-byte chunks per row
   const int rot = (int)(blockIdx.x % nch);
-  uint64_t* bar = reinterpret_cast<uint64_t*>(s_w + 2 * kFrontRows * d);     // [2] buffer-full barriers
+  uint64_t* bar = reinterpret_cast<uint64_t*>(s_w + 2 * kFrontRows * d);     // [2] buffer-full barriers, [2] W2
+  AT* s_w2 = reinterpret_cast<AT*>(bar + 4);                                    // (P, m) second hash layer
+  const uint32_t w2_bytes = (uint32_t)(P * m * sizeof(AT));
   if (tid == 0) {
     umma::mbar_init(bar, 1);
     umma::mbar_init(bar + 1, 1);
+    umma::mbar_init(bar + 2, 1);
     umma::fence_mbar_init();
   }
   __syncthreads();
+  if (tid == 0) {            // the second hash layer's weights arrive while the first layer streams
+    umma::mbar_expect_tx(bar + 2, w2_bytes);
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"((uint32_t)__cvta_generic_to_shared(s_w2)), "l"(a.w2), "r"(w2_bytes),
+                 "r"((uint32_t)__cvta_generic_to_shared(bar + 2))
+                 : "memory");
+  }
   // chunk c (rows of the rotated order) into buffer c & 1: one or two bulk copies (the rows of [cq; ck] and of w1
   // are contiguous in the prepared buffer), counted on bar[c & 1]
   auto issue = [&](int c) {
@@ -180,6 +190,17 @@ __global__ void __launch_bounds__(kFrontThreads) k_gen_front(GenFrontArgs a) {
   };
   issue(0);
   if (nch > 1) issue(1);
+  if (wid == nw - 1) {       // the three fp32 rows (global loads), overlapping the first chunk's copy
+    const float* xs[kDotWays] = {s_hn, s_hn, s_h, s_h};
+    const float* ws[kDotWays] = {a.w_reloj, a.w_reloj + d, a.g_w, a.g_w};
+    float r[kDotWays];
+    dot_rows<float>(xs, ws, 3, d, lane, r);
+    if (lane == 0) {
+      s_dot[2 * cf] = r[0];
+      s_dot[2 * cf + 1] = r[1];
+      s_dot[2 * cf + 2] = r[2];
+    }
+  }
   for (int c = 0; c < nch; ++c) {
     umma::mbar_wait(bar + (c & 1), (uint32_t)((c >> 1) & 1), a.status);
     const AT* wbuf = s_w + (c & 1) * kFrontRows * d;
@@ -189,17 +210,6 @@ __global__ void __launch_bounds__(kFrontThreads) k_gen_front(GenFrontArgs a) {
       const float* x = q < 2 * cf ? s_hna : ((q - 2 * cf) < 2 * m ? s_e : s_p);
       const float r0 = dot_row_smem<AT>(x, wbuf + r * d, d, lane);
       if (lane == 0) s_dot[q < 2 * cf ? q : q + 3] = r0;
-    }
-    if (c == 0 && wid == nw - 1) {
-      const float* xs[kDotWays] = {s_hn, s_hn, s_h, s_h};
-      const float* ws[kDotWays] = {a.w_reloj, a.w_reloj + d, a.g_w, a.g_w};
-      float r[kDotWays];
-      dot_rows<float>(xs, ws, 3, d, lane, r);
-      if (lane == 0) {
-        s_dot[2 * cf] = r[0];
-        s_dot[2 * cf + 1] = r[1];
-        s_dot[2 * cf + 2] = r[2];
-      }
     }
     __syncthreads();                       // buffer c & 1 consumed
     if (c + 2 < nch) issue(c + 2);
@@ -222,26 +232,15 @@ __global__ void __launch_bounds__(kFrontThreads) k_gen_front(GenFrontArgs a) {
     s_hid[m + i] = act<Half>(gelu_t(act<Half>((y[m + i] + y[2 * m + i]) + a.b1[m + i])));
   }
   __syncthreads();
-  const AT* w2 = reinterpret_cast<const AT*>(a.w2);
   AT* phi = reinterpret_cast<AT*>(a.phi);
-  for (int o0 = wid * kDotWays; o0 < P; o0 += nw * kDotWays) {
-    const float* xs[kDotWays];
-    const AT* ws[kDotWays];
-    const int nrows = P - o0 < kDotWays ? P - o0 : kDotWays;
-#pragma unroll
-    for (int k = 0; k < kDotWays; ++k) {
-      const int o = o0 + (k < nrows ? k : 0);
-      xs[k] = (o / nb < a.Tw) ? s_hid : s_hid + m;
-      ws[k] = w2 + (int64_t)o * m;
-    }
-    float r[kDotWays];
-    dot_rows<AT>(xs, ws, nrows, m, lane, r);
+  umma::mbar_wait(bar + 2, 0, a.status);
+  for (int o = wid; o < P; o += nw) {
+    const float* src = (o / nb < a.Tw) ? s_hid : s_hid + m;
+    const float acc = dot_row_smem<AT>(src, s_w2 + (int64_t)o * m, m, lane);
     if (lane == 0) {
-      for (int k = 0; k < nrows; ++k) {
-        const float val = act<Half>(r[k] + a.b2[o0 + k]);
-        s_phi[o0 + k] = val;
-        A::store(phi + b * P + o0 + k, val);
-      }
+      const float val = act<Half>(acc + a.b2[o]);
+      s_phi[o] = val;
+      A::store(phi + b * P + o, val);
     }
   }
   __syncthreads();
@@ -255,7 +254,7 @@ __global__ void __launch_bounds__(kFrontThreads) k_gen_front(GenFrontArgs a) {
 size_t gen_front_smem(const GenFrontArgs& a, bool half) {
   const size_t f = sizeof(float) * (5 * (size_t)a.d + ((2 * a.cf + 3 + 3 * a.m + 3) & ~3) + 2 * a.m + ((a.P + 3) & ~3) + 32);
   const size_t rows = half ? 32 : 16, es = half ? 2 : 4;
-  return ((f + 15) / 16) * 16 + 2 * rows * (size_t)a.d * es + 16;
+  return ((f + 15) / 16) * 16 + 2 * rows * (size_t)a.d * es + 32 + (size_t)a.P * a.m * es;
 }
 
 int launch_gen_front(const GenFrontArgs& a, bool half, cudaStream_t s) {
