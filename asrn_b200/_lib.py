@@ -9,7 +9,7 @@ import os
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, 'libasrn_b200.so')
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 ASRN_OK, ASRN_ERR_ARG, ASRN_ERR_UNSUPPORTED, ASRN_ERR_WORKSPACE, ASRN_ERR_CUDA, ASRN_ERR_TIMEOUT = range(6)
 
@@ -85,7 +85,13 @@ _SIGS = {
     'asrn_local_gelu': (ctypes.c_int, [ctypes.c_int64, _P, ctypes.c_int32, _P]),
     'asrn_shard_rows': (ctypes.c_int, [ctypes.c_int64, ctypes.c_int64, ctypes.c_int32, ctypes.c_int64, ctypes.c_int64,
                                        _P, _P, ctypes.c_int64, _P, _P, _P, _P]),
-    'asrn_score_shard': (ctypes.c_int, [_P, _P, _P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64] + [_P] * 14),
+    'asrn_score_shard': (ctypes.c_int, [_P, _P, _P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64] + [_P] * 15),
+    'asrn_shard_workspace_bytes': (ctypes.c_size_t, [ctypes.c_int64, ctypes.c_int32]),
+    'asrn_shard_tails': (ctypes.c_int, [ctypes.c_int64, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int64,
+                                        _P, _P, _P, _P, ctypes.c_size_t, _P]),
+    'asrn_shard_merge': (ctypes.c_int, [ctypes.c_int64, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int64,
+                                        ctypes.c_int32, _P, _P, _P, ctypes.c_int64, _P, _P, _P, ctypes.c_int64, _P,
+                                        ctypes.c_size_t, _P]),
     'asrn_gen_gate': (ctypes.c_int, [_P] * 16),
     'asrn_gate_workspace_bytes': (ctypes.c_size_t, [_P]),
     'asrn_gate': (ctypes.c_int, [_P] * 14 + [ctypes.c_size_t, _P]),

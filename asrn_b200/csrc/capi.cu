@@ -159,7 +159,7 @@ const char* asrn_status_string(int status) {
   }
 }
 
-int asrn_abi_version(void) { return 2; }
+int asrn_abi_version(void) { return 3; }
 
 size_t asrn_layer_prepared_bytes(const asrn_layer_config* cfg) {
   if (check_config(cfg) != ASRN_OK) return 0;
@@ -320,16 +320,49 @@ int asrn_shard_rows(int64_t rows, int64_t L, int32_t C, int64_t q_lo, int64_t q_
   if (rows < 0 || L < 0 || C < 1 || C > 32 || q_lo < 0 || q_hi <= q_lo || q_hi > L || L >= ((int64_t)1 << 31) ||
       (q_lo == 0 && q_hi == L) || (rows * L > 0 && (!orden || !ids_o)))
     return ASRN_ERR_ARG;
-  if (orden_v ? (!ids_v || Lv < 1) : !counts) return ASRN_ERR_ARG;
+  if (orden_v ? (!ids_v || Lv < 1) : !counts) return ASRN_ERR_ARG;   // counts is optional when compacting
   const int32_t pad_pos = (int32_t)(q_lo > 0 ? 0 : q_hi);
   return launch_shard_rows(rows, L, C, q_lo, q_hi, orden, ids_o, Lv, orden_v, ids_v, counts, pad_pos,
                            as_stream(stream));
 }
 
+size_t asrn_shard_workspace_bytes(int64_t rows, int32_t nb) {
+  if (rows < 0 || nb < 1 || nb > 15) return 0;
+  return shard_merge_workspace(rows, nb);
+}
+
+int asrn_shard_tails(int64_t rows, int64_t Lc, int32_t nb, int32_t C, int64_t c0, const int32_t* orden_loc,
+                     const uint16_t* ids_loc, int32_t* tails, void* workspace, size_t workspace_bytes, void* stream) {
+  if (rows < 0 || Lc < 0 || nb < 1 || nb > 15 || C < 1 || C > 32 || c0 < 0 || c0 + Lc >= ((int64_t)1 << 31) ||
+      (rows * Lc > 0 && (!orden_loc || !ids_loc)) || (rows > 0 && !tails))
+    return ASRN_ERR_ARG;
+  if (rows == 0) return ASRN_OK;
+  if (!workspace || workspace_bytes < shard_merge_workspace(rows, nb)) return ASRN_ERR_WORKSPACE;
+  return launch_shard_tails(rows, Lc, nb, C, c0, orden_loc, ids_loc, tails, workspace, as_stream(stream));
+}
+
+int asrn_shard_merge(int64_t rows, int64_t Lc, int32_t nb, int32_t C, int64_t c0, int32_t n_prev,
+                     const int32_t* tails_prev, const int32_t* orden_loc, const uint16_t* ids_loc, int64_t Lv,
+                     int32_t* orden_v, uint16_t* ids_v, int64_t* row_len, int64_t L, void* workspace,
+                     size_t workspace_bytes, void* stream) {
+  if (rows < 0 || Lc < 1 || nb < 1 || nb > 15 || C < 1 || C > 32 || c0 < 0 || n_prev < 0 || L < c0 + Lc ||
+      L >= ((int64_t)1 << 31) || (c0 == 0 && c0 + Lc == L) || (n_prev > 0 && !tails_prev) ||
+      (rows > 0 && (!orden_loc || !ids_loc || !orden_v || !ids_v || !row_len)))
+    return ASRN_ERR_ARG;
+  const int64_t ring_max = ((int64_t)1 << nb) * C;
+  if (Lv < Lc + (c0 < ring_max ? c0 : ring_max)) return ASRN_ERR_ARG;
+  if (rows == 0) return ASRN_OK;
+  if (!workspace || workspace_bytes < shard_merge_workspace(rows, nb)) return ASRN_ERR_WORKSPACE;
+  const int32_t pad_pos = (int32_t)(c0 > 0 ? 0 : c0 + Lc);
+  return launch_shard_merge(rows, Lc, nb, C, c0, n_prev, tails_prev, orden_loc, ids_loc, Lv, orden_v, ids_v, row_len,
+                            pad_pos, workspace, as_stream(stream));
+}
+
 int asrn_score_shard(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared, int64_t L_feat,
                      int64_t q_lo, int64_t q_hi, const int32_t* orden, const uint16_t* ids_o, const void* phi,
                      const void* Qc, const void* Kc, const float* sig, const double* Bt, const float* log_alfa,
-                     const void* Ea, float* acc, uint8_t* sen_hay, float* sen_mx, float* sen_pk, void* stream) {
+                     const void* Ea, const int64_t* row_len, float* acc, uint8_t* sen_hay, float* sen_mx,
+                     float* sen_pk, void* stream) {
   int st = check_config(cfg);
   if (st) return st;
   if ((st = check_weights(w))) return st;
@@ -339,7 +372,7 @@ int asrn_score_shard(const asrn_layer_config* cfg, const asrn_layer_weights* w, 
   ScoreArgs a = score_args(*cfg, *w, reinterpret_cast<const char*>(prepared));
   a.Lf = L_feat; a.q_lo = q_lo; a.q_hi = q_hi;
   a.orden = orden; a.ids_o = ids_o; a.phi = phi; a.Qc = Qc; a.Kc = Kc; a.sig = sig; a.Bt = Bt; a.log_alfa = log_alfa;
-  a.Ea = Ea; a.acc = acc; a.sen_hay = sen_hay; a.sen_mx = sen_mx; a.sen_pk = sen_pk;
+  a.Ea = Ea; a.row_len = row_len; a.acc = acc; a.sen_hay = sen_hay; a.sen_mx = sen_mx; a.sen_pk = sen_pk;
   return launch_score(a, cfg->half, as_stream(stream));
 }
 

@@ -84,6 +84,7 @@ struct ScoreArgs {
   int64_t B, L;            // sorted rows (B*T, L)
   int64_t Lf;              // per-position features and the value rows: (B, Lf, ...), indexed by text position
   int64_t q_lo, q_hi;      // slots whose position is in [q_lo, q_hi) are queries; outputs (B, q_hi - q_lo, ...)
+  const int64_t* row_len;  // (B*T) slots in use at the start of each sorted row (the rest padding), or null: all L
   int d, T, nb, P, C, cf, K;
   float inv_temp_div;      // temperature (scores are divided by it)
   float esc_c;             // cf^-1/2
@@ -197,6 +198,12 @@ int launch_local_gelu(int64_t n, void* f, bool half, cudaStream_t s);
 int launch_shard_rows(int64_t rows, int64_t L, int C, int64_t q_lo, int64_t q_hi, const int32_t* orden,
                       const uint16_t* ids_o, int64_t Lv, int32_t* orden_v, uint16_t* ids_v, int64_t* counts,
                       int32_t pad_pos, cudaStream_t s);
+size_t shard_merge_workspace(int64_t rows, int nb);
+int launch_shard_tails(int64_t rows, int64_t Lc, int nb, int C, int64_t c0, const int32_t* orden_loc,
+                       const uint16_t* ids_loc, int32_t* tails, void* ws, cudaStream_t s);
+int launch_shard_merge(int64_t rows, int64_t Lc, int nb, int C, int64_t c0, int n_prev, const int32_t* tails_prev,
+                       const int32_t* orden_loc, const uint16_t* ids_loc, int64_t Lv, int32_t* orden_v,
+                       uint16_t* ids_v, int64_t* row_len, int32_t pad_pos, void* ws, cudaStream_t s);
 int launch_gen_front(const GenFrontArgs& a, bool half, cudaStream_t s);
 int launch_gen_gate(const GateArgs& a, bool half, cudaStream_t s);
 size_t hawkes_table_bytes(int64_t B, int n, int64_t cap);

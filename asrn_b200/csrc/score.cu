@@ -108,7 +108,8 @@ __global__ void __launch_bounds__(256) k_score_simt(ScoreArgs a) {
   const int64_t b = r / a.T;
   const int tau = (int)(r % a.T);
   const int64_t S0 = (int64_t)blockIdx.x * kSpan;
-  const int64_t S1 = min(S0 + kSpan, a.L);
+  const int64_t S1 = min(min(S0 + kSpan, a.L), a.row_len ? a.row_len[r] : a.L);
+  if (S0 >= S1) return;
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const float tasa = a.tasa[tau];
   const typename A::T* Ea = reinterpret_cast<const typename A::T*>(a.Ea);

@@ -480,7 +480,8 @@ __global__ void __launch_bounds__(kThreadsTc, 1) k_score_tc(ScoreArgs a, int nds
   k.tau = (int)(k.r % a.T);
   const int part = blockIdx.x % nds;
   k.S0 = (int64_t)(blockIdx.x / nds) * kSpanTc;
-  k.S1 = min(k.S0 + kSpanTc, a.L);
+  k.S1 = min(min(k.S0 + kSpanTc, a.L), a.row_len ? a.row_len[k.r] : a.L);
+  if (k.S0 >= k.S1) return;                     // a span past the row's used slots (sharded rows)
   k.dp0 = part * dpart;
   k.dpart = dpart;
   k.Ppad = pad16(a.P);

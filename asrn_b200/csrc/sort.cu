@@ -3,9 +3,9 @@
 //
 // Design: a row is cut into tiles of at most kTile positions. Each tile sorts composite 32-bit keys
 // (id << 13 | local position) in shared memory (bitonic network; the keys are unique, so any sort is stable).
-// A single-tile row is written out directly. Longer rows add a per-tile histogram of the 2^nb buckets, a column
-// scan over tiles plus a scan over buckets (the global slot where each tile's run of a bucket starts), and a
-// scatter of every tile's runs to their slots.
+// A single-tile row is written out directly. Longer rows add a per-tile histogram of the 2^nb buckets, the global
+// slot where each tile's run of a bucket starts (bucket totals over the tiles, a scan over the buckets, running
+// offsets over the tiles), and a scatter of every tile's runs to their slots.
 #include <mutex>
 
 #include "common.cuh"
@@ -81,22 +81,30 @@ __global__ void __launch_bounds__(1024) k_bsort_tile(const uint16_t* __restrict_
   }
 }
 
-// Per row: hist[row][tile][bin] (counts) -> the global slot where the tile's run of bin starts.
-__global__ void __launch_bounds__(1024) k_bsort_offsets(int32_t* __restrict__ hist, int ntiles, int nb) {
+// hist[row][tile][bin] (counts) -> the global slot where the tile's run of bin starts, in three passes that keep
+// every SM busy (a row has 2^nb bins, up to 65536): (1) per bin its total over the tiles, a thread per bin, the
+// tiles' counts read coalesced across the bins; (2) per row an exclusive scan of the totals, one block per row;
+// (3) per bin the running offsets over the tiles, written in place.
+constexpr int kBinThreads = 256;
+
+__global__ void __launch_bounds__(kBinThreads) k_bsort_bin_totals(const int32_t* __restrict__ hist, int ntiles,
+                                                                  int nbins, int32_t* __restrict__ tot) {
+  const int64_t row = blockIdx.y;
+  const int bin = blockIdx.x * kBinThreads + threadIdx.x;
+  if (bin >= nbins) return;
+  const int32_t* h = hist + row * (int64_t)ntiles * nbins + bin;
+  int run = 0;
+  for (int tl = 0; tl < ntiles; ++tl) run += h[(int64_t)tl * nbins];
+  tot[row * nbins + bin] = run;
+}
+
+__global__ void __launch_bounds__(1024) k_bsort_bin_scan(int32_t* __restrict__ tot, int nbins) {
   const int64_t row = blockIdx.x;
-  const int nbins = 1 << nb;
   const int per = (nbins + blockDim.x - 1) / blockDim.x;
   const int b0 = threadIdx.x * per;
-  int32_t* h = hist + row * (int64_t)ntiles * nbins;
+  int32_t* t = tot + row * nbins;
   int local = 0;
-  for (int k = 0; k < per; ++k) {
-    const int bin = b0 + k;
-    if (bin >= nbins) break;
-    int run = 0;
-    for (int tl = 0; tl < ntiles; ++tl) run += h[(int64_t)tl * nbins + bin];
-    local += run;
-  }
-  // block exclusive scan of the per-thread totals
+  for (int k = 0; k < per && b0 + k < nbins; ++k) local += t[b0 + k];
   __shared__ int wsum[32];
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   int incl = local;
@@ -117,17 +125,25 @@ __global__ void __launch_bounds__(1024) k_bsort_offsets(int32_t* __restrict__ hi
     wsum[lane] = w;
   }
   __syncthreads();
-  int run_base = (wid > 0 ? wsum[wid - 1] : 0) + incl - local;
-  for (int k = 0; k < per; ++k) {
-    const int bin = b0 + k;
-    if (bin >= nbins) break;
-    int off = run_base;
-    for (int tl = 0; tl < ntiles; ++tl) {
-      const int c = h[(int64_t)tl * nbins + bin];
-      h[(int64_t)tl * nbins + bin] = off;
-      off += c;
-    }
-    run_base = off;
+  int run = (wid > 0 ? wsum[wid - 1] : 0) + incl - local;
+  for (int k = 0; k < per && b0 + k < nbins; ++k) {
+    const int c = t[b0 + k];
+    t[b0 + k] = run;
+    run += c;
+  }
+}
+
+__global__ void __launch_bounds__(kBinThreads) k_bsort_bin_offsets(int32_t* __restrict__ hist, int ntiles, int nbins,
+                                                                   const int32_t* __restrict__ tot) {
+  const int64_t row = blockIdx.y;
+  const int bin = blockIdx.x * kBinThreads + threadIdx.x;
+  if (bin >= nbins) return;
+  int32_t* h = hist + row * (int64_t)ntiles * nbins + bin;
+  int off = tot[row * nbins + bin];
+  for (int tl = 0; tl < ntiles; ++tl) {
+    const int c = h[(int64_t)tl * nbins];
+    h[(int64_t)tl * nbins] = off;
+    off += c;
   }
 }
 
@@ -159,7 +175,8 @@ static int ntiles_of(int64_t L) { return (int)((L + kTile - 1) / kTile); }
 size_t bucket_sort_workspace(int64_t rows, int64_t L, int nb) {
   const int nt = ntiles_of(L);
   if (nt <= 1) return 0;
-  return align_up((size_t)rows * L * 4) + align_up((size_t)rows * nt * ((size_t)1 << nb) * 4);
+  return align_up((size_t)rows * L * 4) + align_up((size_t)rows * nt * ((size_t)1 << nb) * 4) +
+         align_up((size_t)rows * ((size_t)1 << nb) * 4);
 }
 
 int launch_bucket_sort(int64_t rows, int64_t L, int nb, const uint16_t* ids_rows, int32_t* orden, uint16_t* ids_o,
@@ -180,9 +197,14 @@ int launch_bucket_sort(int64_t rows, int64_t L, int nb, const uint16_t* ids_rows
   uint32_t* tmp = reinterpret_cast<uint32_t*>(ws);
   int32_t* hist = reinterpret_cast<int32_t*>(reinterpret_cast<char*>(ws) + align_up((size_t)rows * L * 4));
   const size_t hist_bytes = (size_t)rows * nt * ((size_t)1 << nb) * 4;
+  int32_t* tot = reinterpret_cast<int32_t*>(reinterpret_cast<char*>(hist) + align_up(hist_bytes));
+  const int nbins = 1 << nb;
   if (cudaMemsetAsync(hist, 0, hist_bytes, s) != cudaSuccess) return ASRN_ERR_CUDA;
   k_bsort_tile<<<dim3(nt, (unsigned)rows), 1024, smem, s>>>(ids_rows, L, nt, n2, nb, orden, ids_o, tmp, hist);
-  k_bsort_offsets<<<(unsigned)rows, 1024, 0, s>>>(hist, nt, nb);
+  const dim3 bin_grid((unsigned)((nbins + kBinThreads - 1) / kBinThreads), (unsigned)rows);
+  k_bsort_bin_totals<<<bin_grid, kBinThreads, 0, s>>>(hist, nt, nbins, tot);
+  k_bsort_bin_scan<<<(unsigned)rows, 1024, 0, s>>>(tot, nbins);
+  k_bsort_bin_offsets<<<bin_grid, kBinThreads, 0, s>>>(hist, nt, nbins, tot);
   cudaFuncSetAttribute(k_bsort_scatter, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   k_bsort_scatter<<<dim3(nt, (unsigned)rows), 1024, smem, s>>>(tmp, hist, L, nt, nb, orden, ids_o);
   return cudaGetLastError() == cudaSuccess ? ASRN_OK : ASRN_ERR_CUDA;

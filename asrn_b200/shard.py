@@ -6,19 +6,22 @@ sequence (L = world * Lc, equal chunks) and computes h' for them:
   phase 1 (local)   the context stage and the sign-hash projection of the chunk (asrn/estable.py:153-194,
                     asrn/nucleo.py:644-664); the hash of the chunk's first position needs E of the previous position,
                     the one-row halo from rank r - 1 (zeros on rank 0, as the reference's E_{-1} = 0)
+                    then the sort of the chunk's rows by bucket (asrn/estable.py:220-221) and per (row, bucket) the
+                    bucket's tail, its last <= C positions (asrn_shard_tails)
   exchange (NCCL)   (1) the halo rows, (2) per sequence the chunk's sum of beta (fp64): rank r's clock is the
                     exclusive sum of the earlier chunks plus its own cumulative sum (asrn/estable.py:418),
-                    (3) the chunk's bucket ids and per-position features (phi, Qc, Kc, signature, clock, beta,
+                    (3) the bucket tails, (4) the per-position features (phi, Qc, Kc, signature, clock, beta,
                     log_alfa, bf16 rows of E): all-gathers over NVLink; afterwards every rank holds them for all L
-  phase 2 (local)   sort of the full rows by bucket (asrn/estable.py:220-221); the shard's own rows: its slots plus
-                    each bucket's exclusive ring -- the <= C earlier-chunk slots some local query has as a candidate
-                    (asrn_shard_rows); candidate scoring of the local queries (asrn_score_shard); the n-gram memory
-                    over the full sequence (its Hawkes and streak scans carry state across chunks), kept for the
-                    chunk; the gate of the chunk.
+  phase 2 (local)   the shard's own rows: for every bucket with local slots its exclusive ring -- the C most recent
+                    earlier-chunk positions, from the earlier ranks' tails -- then its local run (asrn_shard_merge);
+                    candidate scoring of the local queries (asrn_score_shard); the n-gram memory over the full
+                    sequence (its Hawkes and streak scans carry state across chunks), kept for the chunk; the gate
+                    of the chunk.
 
 `forward` runs one rank under torch.distributed (NCCL); `forward_emulated` runs every rank's phases in one process
 (the exchange becomes concatenation), so that the sharded algorithm can be checked against the unsharded layer on one
-GPU. The exchange is NCCL collectives only (no peer-memory loads in the kernels).
+GPU. The exchange is NCCL collectives only (no peer-memory loads in the kernels). No step waits on the host: every
+shard row's length stays on the device (the rows are sized by a bound, the scoring kernel stops at each row's end).
 """
 import torch
 
@@ -36,9 +39,9 @@ def chunk_bounds(L, world, rank):
     return rank * Lc, (rank + 1) * Lc
 
 
-def _phase1(layer, E, h, tokens, E_halo, half):
-    """Local stages of one chunk. E, h (B, Lc, d) fp32, tokens (B, Lc) or None, E_halo (B, d): E of the position
-    before the chunk."""
+def _phase1(layer, E, h, tokens, E_halo, half, c0):
+    """Local stages of one chunk starting at position c0. E, h (B, Lc, d) fp32, tokens (B, Lc) or None, E_halo (B, d):
+    E of the position before the chunk."""
     ctx = stages.context(layer, h, tokens, E=None if tokens is not None else E, half=half)
     Bt = stages.clock(ctx['beta'])
     E_ext = torch.cat([E_halo.unsqueeze(1).to(E.dtype), E], 1)
@@ -47,9 +50,51 @@ def _phase1(layer, E, h, tokens, E_halo, half):
     T = layer.n_tablas
     loc = dict(phi=hs['phi'][:, 1:].contiguous(), Qc=ctx['Qc'], Kc=ctx['Kc'], sig=ctx['sig'],
                log_alfa=ctx['log_alfa'], beta=ctx['beta'], Bt=Bt, Ea=hs['Ea'][:, 1:].contiguous(),
-               glogit=ctx['glogit'],
-               ids=hs['ids_rows'].view(B * T, Lc + 1)[:, 1:].contiguous())
+               glogit=ctx['glogit'])
+    ids = hs['ids_rows'].view(B * T, Lc + 1)[:, 1:].contiguous()
+    loc['orden'], loc['ids'] = stages.bucket_sort(ids, layer.n_bits)
+    loc['tails'] = _tails(layer, loc['orden'], loc['ids'], c0)
     return loc
+
+
+def _workspace(layer, rows, dev):
+    n = _lib.lib().asrn_shard_workspace_bytes(rows, layer.n_bits)
+    if n == 0:
+        raise ValueError(f'sequence sharding needs n_bits <= 15 (got {layer.n_bits})')
+    return torch.empty(n, dtype=torch.uint8, device=dev)
+
+
+def _tails(layer, orden_loc, ids_loc, c0):
+    """(rows, 2^nb, C + 1) int32 bucket tails of a sorted chunk: [0] = count, then its last <= C global positions."""
+    rows, Lc = orden_loc.shape
+    dev = orden_loc.device
+    C = layer.chunk
+    tails = torch.empty(rows, 1 << layer.n_bits, C + 1, dtype=torch.int32, device=dev)
+    ws = _workspace(layer, rows, dev)
+    _lib.check(_lib.lib().asrn_shard_tails(rows, Lc, layer.n_bits, C, c0, _lib.ptr(orden_loc), _lib.ptr(ids_loc),
+                                           _lib.ptr(tails), _lib.ptr(ws), ws.numel(), _lib.stream_ptr(dev)),
+               'asrn_shard_tails')
+    return tails
+
+
+def shard_rows(layer, orden_loc, ids_loc, tails_prev, c0, L):
+    """The shard's sorted rows from its sorted chunk and the earlier ranks' tails (n_prev, rows, 2^nb, C + 1):
+    (orden_v, ids_v) (rows, Lv) and the used length of every row (rows,) int64, all on the device."""
+    rows, Lc = orden_loc.shape
+    dev = orden_loc.device
+    C, nb = layer.chunk, layer.n_bits
+    Lv = (Lc + min(c0, (1 << nb) * C) + 31) // 32 * 32
+    orden_v = torch.empty(rows, Lv, dtype=torch.int32, device=dev)
+    ids_v = torch.empty(rows, Lv, dtype=torch.int16, device=dev)
+    row_len = torch.empty(rows, dtype=torch.int64, device=dev)
+    ws = _workspace(layer, rows, dev)
+    n_prev = 0 if tails_prev is None else tails_prev.shape[0]
+    _lib.check(_lib.lib().asrn_shard_merge(rows, Lc, nb, C, c0, n_prev,
+                                           None if n_prev == 0 else _lib.ptr(tails_prev), _lib.ptr(orden_loc),
+                                           _lib.ptr(ids_loc), Lv, _lib.ptr(orden_v), _lib.ptr(ids_v),
+                                           _lib.ptr(row_len), L, _lib.ptr(ws), ws.numel(), _lib.stream_ptr(dev)),
+               'asrn_shard_merge')
+    return orden_v, ids_v, row_len
 
 
 def _apply_clock_offsets(Bt_full, chunk_sums, Lc):
@@ -60,23 +105,16 @@ def _apply_clock_offsets(Bt_full, chunk_sums, Lc):
     return Bt_full
 
 
-def _phase2(layer, loc, full, h, c0, c1, half):
-    """Scoring, n-gram memory and gate of the chunk [c0, c1) from the gathered full-sequence features."""
+def _phase2(layer, loc, full, tails_prev, h, c0, c1, half):
+    """Scoring, n-gram memory and gate of the chunk [c0, c1) from the gathered full-sequence features and the
+    earlier ranks' bucket tails."""
     B, L = full['sig'].shape
-    T, nb, C = layer.n_tablas, layer.n_bits, layer.chunk
+    T = layer.n_tablas
     dev = h.device
     lib = _lib.lib()
     s = _lib.stream_ptr(dev)
-    orden, ids_o = stages.bucket_sort(full['ids'], nb)
-    rows = B * T
-    counts = torch.empty(rows, dtype=torch.int64, device=dev)
-    _lib.check(lib.asrn_shard_rows(rows, L, C, c0, c1, _lib.ptr(orden), _lib.ptr(ids_o), 0, None, None,
-                                   _lib.ptr(counts), s), 'asrn_shard_rows')
-    Lv = (max(1, int(counts.max())) + 31) // 32 * 32          # rows of whole 32-slot sub-tiles
-    orden_v = torch.empty(rows, Lv, dtype=torch.int32, device=dev)
-    ids_v = torch.empty(rows, Lv, dtype=torch.int16, device=dev)
-    _lib.check(lib.asrn_shard_rows(rows, L, C, c0, c1, _lib.ptr(orden), _lib.ptr(ids_o), Lv, _lib.ptr(orden_v),
-                                   _lib.ptr(ids_v), None, s), 'asrn_shard_rows')
+    orden_v, ids_v, row_len = shard_rows(layer, loc['orden'], loc['ids'], tails_prev, c0, L)
+    Lv = orden_v.shape[1]
     Lc = c1 - c0
     d = layer.d
     w, _keep, prep = layer.prepared(dev, half)
@@ -88,8 +126,8 @@ def _phase2(layer, loc, full, h, c0, c1, half):
     _lib.check(lib.asrn_score_shard(ctypes_ref(cfg), ctypes_ref(w), _lib.ptr(prep), L, c0, c1, _lib.ptr(orden_v),
                                     _lib.ptr(ids_v), _lib.ptr(full['phi']), _lib.ptr(full['Qc']),
                                     _lib.ptr(full['Kc']), _lib.ptr(full['sig']), _lib.ptr(full['Bt']),
-                                    _lib.ptr(full['log_alfa']), _lib.ptr(full['Ea']), _lib.ptr(acc), _lib.ptr(hay),
-                                    _lib.ptr(mx), _lib.ptr(pk), s), 'asrn_score_shard')
+                                    _lib.ptr(full['log_alfa']), _lib.ptr(full['Ea']), _lib.ptr(row_len),
+                                    _lib.ptr(acc), _lib.ptr(hay), _lib.ptr(mx), _lib.ptr(pk), s), 'asrn_score_shard')
     rep = stages.repetition(layer, full['sig'], full['beta'], full['Bt'], full['log_alfa'])
     vistos = rep['vistos'][:, c0:c1].contiguous()
     hawkes = rep['hawkes'][:, c0:c1].contiguous()
@@ -119,12 +157,13 @@ def forward_emulated(layer, E, h, tokens, world):
     for r, (c0, c1) in enumerate(bounds):
         halo = E[:, c0 - 1] if c0 > 0 else torch.zeros(B, d, device=E.device)
         locs.append(_phase1(layer, E[:, c0:c1].contiguous(), h[:, c0:c1].contiguous(),
-                            None if tokens is None else tokens[:, c0:c1].contiguous(), halo, half))
+                            None if tokens is None else tokens[:, c0:c1].contiguous(), halo, half, c0))
     full = {k: torch.cat([lc[k] for lc in locs], 1) for k in _SEQ_KEYS}
-    full['ids'] = torch.cat([lc['ids'] for lc in locs], 1)
+    tails = torch.stack([lc['tails'] for lc in locs], 0)
     sums = torch.stack([lc['Bt'][:, -1] for lc in locs], 0)
     _apply_clock_offsets(full['Bt'], sums, L // world)
-    outs = [_phase2(layer, lc, full, h[:, c0:c1].contiguous(), c0, c1, half) for lc, (c0, c1) in zip(locs, bounds)]
+    outs = [_phase2(layer, lc, full, tails[:r] if r > 0 else None, h[:, c0:c1].contiguous(), c0, c1, half)
+            for r, (lc, (c0, c1)) in enumerate(zip(locs, bounds))]
     return torch.cat(outs, 1)
 
 
@@ -159,11 +198,12 @@ def exchange_chunk_sums(chunk_sum, world, group=None):
     return flat.view((world,) + tuple(chunk_sum.shape))
 
 
-def exchange_ids(ids_rows, B, T, world, group=None):
-    """(B*T, Lc) bucket ids of this chunk -> (B*T, world*Lc) of the whole sequences."""
-    Lc = ids_rows.shape[1]
-    ids_pm = ids_rows.view(B, T, Lc).permute(0, 2, 1)                  # (B, Lc, T) position-major
-    return _gather_seq(ids_pm, world, group).permute(0, 2, 1).reshape(B * T, world * Lc).contiguous()
+def exchange_tails(tails, world, group=None):
+    """(rows, 2^nb, C + 1) int32 bucket tails of this chunk -> (world, rows, 2^nb, C + 1), in rank order."""
+    import torch.distributed as dist
+    flat = torch.empty((world,) + tuple(tails.shape), dtype=tails.dtype, device=tails.device)
+    dist.all_gather_into_tensor(flat.view(-1), tails.contiguous().view(-1), group=group)
+    return flat
 
 
 @torch.no_grad()
@@ -184,11 +224,11 @@ def forward(layer, E, h, tokens=None, group=None):
         return layer(E, h, tokens)
     # (1) halo rows: E of every chunk's last position
     halo = exchange_halo(E[:, -1], world, rank, group)
-    loc = _phase1(layer, E, h, tokens, halo, half)
+    loc = _phase1(layer, E, h, tokens, halo, half, c0)
     # (2) chunk sums of beta (= the last local clock value) -> clock offsets
     sums = exchange_chunk_sums(loc['Bt'][:, -1], world, group)
-    # (3) bucket ids and features of every position
+    # (3) bucket tails, (4) features of every position
+    tails = exchange_tails(loc['tails'], world, group)
     full = {k: _gather_seq(loc[k], world, group) for k in _SEQ_KEYS}
-    full['ids'] = exchange_ids(loc['ids'], B, layer.n_tablas, world, group)
     _apply_clock_offsets(full['Bt'], sums, Lc)
-    return _phase2(layer, loc, full, h, c0, c1, half)
+    return _phase2(layer, loc, full, tails[:rank] if rank > 0 else None, h, c0, c1, half)

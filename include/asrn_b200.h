@@ -30,7 +30,8 @@
  *   asrn_gen_memory         _MemoriaHawkes.paso + _repeticion_o1  asrn/nucleo.py:1683-1714, 953-960
  *   asrn_gen_ring_insert    _anillo_meter                      asrn/nucleo.py:1610-1618
  *   asrn_gen_front          _contexto + _phi_y_valores/_ids (one token)  asrn/estable.py:153-194, nucleo.py:639-664
- *   asrn_shard_rows, asrn_score_shard   candidate windows / _acumular of one shard of a long sequence
+ *   asrn_shard_tails, asrn_shard_merge, asrn_shard_rows, asrn_score_shard
+ *                                        candidate windows / _acumular of one shard of a long sequence
  *                                        (asrn/estable.py:220-300; the reference runs one GPU per sequence)
  *   asrn_gen_gate           _combinar (one token)              asrn/estable.py:376-403
  */
@@ -166,20 +167,39 @@ int asrn_local_mid(int64_t B, int32_t d, const float* h, const void* z, float* h
 int asrn_local_gelu(int64_t n, void* f, int32_t half, void* stream);
 
 /* ---- sequence-chunk sharding (one long sequence over several GPUs) --------------------------------------------------
- * Each shard owns positions [q_lo, q_hi) of an L-position sequence and, after exchanging bucket ids and features,
- * holds them for all L positions. asrn_shard_rows turns full sorted rows (orden, ids_o: (rows, L) from
- * asrn_bucket_sort) into the shard's rows: its own slots plus, before each bucket's local run, the up to C earlier
- * slots some local query has as a candidate; with orden_v == NULL it only writes each row's length to counts (rows)
- * int64; otherwise it writes rows of length Lv (>= every count), padded with id 0xFFFF. Requires 2+ shards
- * (q_lo > 0 or q_hi < L). asrn_score_shard is asrn_score over such rows (cfg->L = Lv) with features of L_feat positions
- * per sequence indexed by position, queries = the slots at positions [q_lo, q_hi), outputs (B, q_hi - q_lo, ...). */
+ * Shard r of `world` owns positions [c0, c0 + Lc) of every sequence (L = world * Lc). Its sorted rows hold its own
+ * slots and, before each bucket's local run, the up to C earlier-chunk slots some local query has as a candidate (the
+ * bucket's C most recent earlier positions): the candidates of every local query are then the same as in the full
+ * row (asrn/estable.py:220-236, 262-265). Rows are padded with id 0xFFFF, so nb <= 15 here.
+ *
+ * asrn_shard_tails: from the shard's own sorted chunk (orden_loc, ids_loc: (rows, Lc) from asrn_bucket_sort on the
+ * chunk's bucket ids, local positions), per (row, bucket) the bucket's last <= C global positions: tails
+ * (rows, 2^nb, C + 1) int32, [0] = count, [1 .. count] ascending. Every shard publishes its tails (all-gather).
+ * asrn_shard_merge: the shard's rows from its sorted chunk and the tails of the n_prev = r earlier shards
+ * (tails_prev: (n_prev, rows, 2^nb, C + 1), rank order): orden_v / ids_v (rows, Lv), the used length of each row in
+ * row_len (rows) int64 (the rest is padding); Lv >= Lc + min(c0, 2^nb * C) bounds every row, so no host round trip
+ * is needed. Requires 2+ shards (c0 > 0 or c0 + Lc < L). Both take a workspace of asrn_shard_workspace_bytes.
+ * asrn_shard_rows: the same rows from the FULL sorted rows (orden, ids_o: (rows, L) after exchanging all bucket ids);
+ * with orden_v == NULL it only writes each row's length to counts (rows) int64; otherwise it writes rows of length Lv
+ * (cut at Lv), padded with id 0xFFFF, and the lengths too when counts != NULL. q_lo = c0, q_hi = c0 + Lc.
+ * asrn_score_shard is asrn_score over such rows (cfg->L = Lv) with features of L_feat positions per sequence indexed
+ * by position, queries = the slots at positions [q_lo, q_hi), outputs (B, q_hi - q_lo, ...); row_len (B*T) int64 or
+ * NULL bounds the slots scored in each row (spans past it do no work). */
+size_t asrn_shard_workspace_bytes(int64_t rows, int32_t nb);
+int asrn_shard_tails(int64_t rows, int64_t Lc, int32_t nb, int32_t C, int64_t c0, const int32_t* orden_loc,
+                     const uint16_t* ids_loc, int32_t* tails, void* workspace, size_t workspace_bytes, void* stream);
+int asrn_shard_merge(int64_t rows, int64_t Lc, int32_t nb, int32_t C, int64_t c0, int32_t n_prev,
+                     const int32_t* tails_prev, const int32_t* orden_loc, const uint16_t* ids_loc, int64_t Lv,
+                     int32_t* orden_v, uint16_t* ids_v, int64_t* row_len, int64_t L, void* workspace,
+                     size_t workspace_bytes, void* stream);
 int asrn_shard_rows(int64_t rows, int64_t L, int32_t C, int64_t q_lo, int64_t q_hi, const int32_t* orden,
                     const uint16_t* ids_o, int64_t Lv, int32_t* orden_v, uint16_t* ids_v, int64_t* counts,
                     void* stream);
 int asrn_score_shard(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared, int64_t L_feat,
                      int64_t q_lo, int64_t q_hi, const int32_t* orden, const uint16_t* ids_o, const void* phi,
                      const void* Qc, const void* Kc, const float* sig, const double* Bt, const float* log_alfa,
-                     const void* Ea, float* acc, uint8_t* sen_hay, float* sen_mx, float* sen_pk, void* stream);
+                     const void* Ea, const int64_t* row_len, float* acc, uint8_t* sen_hay, float* sen_mx,
+                     float* sen_pk, void* stream);
 
 /* The same bucket sort for callers that cannot allocate device memory when they sort (a plug-in inside a host process
  * whose allocator it does not own, a serving loop that keeps a fixed memory footprint after start-up): no workspace

@@ -65,6 +65,44 @@ def test_shard_rows_follow_the_rule(q, cuda):
         assert (ov[r, n:].cpu().numpy() == pad).all() and (iv[r, n:].cpu().numpy().view(np.uint16) == 0xFFFF).all()
 
 
+@pytest.mark.parametrize('world,nb,C', [(2, 4, 8), (4, 4, 8), (3, 6, 32), (4, 14, 32)])
+def test_rows_from_tails_equal_rows_from_the_full_sort(world, nb, C, cuda):
+    """asrn_shard_merge (each shard sorts only its chunk; earlier chunks reach it as bucket tails) gives exactly the rows
+    of asrn_shard_rows over the full sorted rows, and the row lengths; integer work, so bit-exact. Rows span several
+    sort tiles (Lc > 8192) in the last case."""
+    from types import SimpleNamespace
+    from asrn_b200 import _lib, shard, stages
+    rng = np.random.default_rng(nb + world)
+    rows = 3
+    Lc = 12000 if nb == 14 else 700
+    L = world * Lc
+    ids = rng.integers(0, 1 << nb, (rows, L)).astype(np.int16)
+    ids[:, L // 2:L // 2 + 300] = ids[:, 100:400]                 # repeated stretches: long runs in some buckets
+    ids_t = torch.from_numpy(ids).to(cuda)
+    orden, ids_o = stages.bucket_sort(ids_t, nb)
+    layer = SimpleNamespace(n_bits=nb, chunk=C)
+    lib, s = _lib.lib(), _lib.stream_ptr(cuda)
+    tails = []
+    for r in range(world):
+        c0 = r * Lc
+        o_loc, i_loc = stages.bucket_sort(ids_t[:, c0:c0 + Lc].contiguous(), nb)
+        tails.append(shard._tails(layer, o_loc, i_loc, c0))
+    tails = torch.stack(tails, 0)
+    for r in range(world):
+        c0, c1 = r * Lc, (r + 1) * Lc
+        o_loc, i_loc = stages.bucket_sort(ids_t[:, c0:c1].contiguous(), nb)
+        ov, iv, row_len = shard.shard_rows(layer, o_loc, i_loc, tails[:r] if r > 0 else None, c0, L)
+        Lv = ov.shape[1]
+        counts = torch.empty(rows, dtype=torch.int64, device=cuda)
+        ov_ref = torch.empty(rows, Lv, dtype=torch.int32, device=cuda)
+        iv_ref = torch.empty(rows, Lv, dtype=torch.int16, device=cuda)
+        assert lib.asrn_shard_rows(rows, L, C, c0, c1, _lib.ptr(orden), _lib.ptr(ids_o), Lv, _lib.ptr(ov_ref),
+                                   _lib.ptr(iv_ref), _lib.ptr(counts), s) == 0
+        torch.cuda.synchronize()
+        assert torch.equal(row_len, counts)
+        assert torch.equal(ov, ov_ref) and torch.equal(iv, iv_ref)
+
+
 def _layer_and_inputs(cuda, d, B, L, nb, seed=0):
     import asrn_b200
     torch.manual_seed(seed)

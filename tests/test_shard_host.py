@@ -45,9 +45,8 @@ def _rank(rank, world, port, out):
         res['sums'] = shard.exchange_chunk_sums(torch.tensor([rank + 0.5, 10.0 * rank], dtype=torch.float64), world)
         res['seq1'] = shard._gather_seq(torch.arange(4).view(1, 4, 1) + 100 * rank, world, None)
         res['seq2'] = shard._gather_seq(torch.arange(8).view(2, 4) + 100 * rank, world, None)
-        B, T, Lc = 2, 3, 4
-        ids = (torch.arange(B * T * Lc).view(B * T, Lc) + 1000 * rank).to(torch.int16)
-        res['ids'] = shard.exchange_ids(ids, B, T, world, None)
+        tails = (torch.arange(2 * 4 * 3).view(2, 4, 3) + 1000 * rank).to(torch.int32)
+        res['tails'] = shard.exchange_tails(tails, world, None)
         torch.save(res, os.path.join(out, f'rank{rank}.pt'))
     finally:
         dist.destroy_process_group()
@@ -65,7 +64,5 @@ def test_exchange_steps_with_two_gloo_ranks(tmp_path):
         assert torch.equal(r['seq1'].view(-1), torch.tensor([0, 1, 2, 3, 100, 101, 102, 103]))
         expect2 = torch.cat([torch.arange(8).view(2, 4), torch.arange(8).view(2, 4) + 100], 1)
         assert torch.equal(r['seq2'], expect2)
-        B, T, Lc = 2, 3, 4
-        full = torch.cat([torch.arange(B * T * Lc).view(B * T, Lc), torch.arange(B * T * Lc).view(B * T, Lc) + 1000],
-                         1).to(torch.int16)
-        assert torch.equal(r['ids'], full)
+        t0 = torch.arange(2 * 4 * 3).view(2, 4, 3).to(torch.int32)
+        assert torch.equal(r['tails'], torch.stack([t0, t0 + 1000], 0))
