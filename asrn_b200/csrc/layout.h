@@ -234,6 +234,8 @@ int launch_gate(const GateArgs& a, bool half, cudaStream_t s);
 size_t gate_workspace(int64_t M, int d, bool half);
 int launch_prepare(const asrn_layer_config& c, const asrn_layer_weights& w, void* prepared, cudaStream_t s);
 // 2-D bf16 TMA tensor map, 128-byte swizzle: rows of `inner` elements (row stride in bytes), box inner x outer.
+bool make_tmap_rows_bf16(void* map /* CUtensorMap */, const void* base, uint64_t inner, uint64_t outer,
+                         uint64_t row_bytes, uint32_t box_inner);
 bool make_tmap_bf16(void* map /* CUtensorMap */, const void* base, uint64_t inner, uint64_t outer,
                     uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer);
 // GEMM implementation choice: false when ASRN_B200_GEMM=simt forces the CUDA-core kernels (for cross-checks).

@@ -18,6 +18,8 @@
 // ring is zeroed when the block starts), multiplied by zero weights. The feature rows and the small per-position
 // gathers (clock, log_alfa, previous signatures, the sorted entries) are cp.async. d is split over two blocks only
 // when d > 768.
+#include <cuda.h>
+
 #include "common.cuh"
 #include "layout.h"
 #include "umma.cuh"
@@ -51,24 +53,34 @@ struct TcSmem {
   float* sc;            // [32][65]
   __nv_bfloat16* att;   // [2][32][72]
   int* qhay;            // [2][32]
+  float* wsuf;          // [kMaxSuffix + 1] suffix weights w_sufijo
   uint64_t* vbar;       // [3] value-stage mbarriers
-  int Pp, Cp, Dp;
+  uint64_t* fbar;       // [4] feature-stage mbarriers (one per 32-row stage of the feature ring)
+  int Pp, Cp, Dp;        // row pitches (elements)
+  int Gp, Gc;            // 4-row group strides of the phi and Qc / Kc rings (elements)
+  __device__ __forceinline__ int prow(int fr) const { return (fr >> 2) * Gp + (fr & 3) * Pp; }
+  __device__ __forceinline__ int crow(int fr) const { return (fr >> 2) * Gc + (fr & 3) * Cp; }
 };
 
 __host__ __device__ inline int pad16(int x) { return (x + 15) / 16 * 16; }
+// Feature rings: rows of the padded pitch (an odd number of 16-byte chunks: the 4 rows of a group fall in distinct
+// bank groups) in groups of 4 rows -- one row gather -- each group starting on a 128-byte boundary.
+__host__ __device__ inline int group_elems(int pitch) { return (4 * pitch * 2 + 127) / 128 * 128 / 2; }
 
 __host__ __device__ inline size_t tc_smem_bytes(int P, int cf, int dpart) {
   const int Pp = pad16(P) + 8, Cp = pad16(cf) + 8, Dp = dpart + 8;
-  size_t b = 0;
+  size_t b = 128;                                // alignment slack of the dynamic shared memory base
+  b += (size_t)(kRF / 4) * (group_elems(Pp) + 2 * group_elems(Cp)) * 2;
   b += kStage * kQ * 4 + kStage * kStageIds * 2;
   b = (b + 15) / 16 * 16;
   b += kRF * 8;                                  // bt
   b += kRF * 4 * (size_t)kMaxSuffix;             // pf
   b += kRF * 4 * 4;                              // pos, id, used, la
-  b += (size_t)kRF * Pp * 2 + 2 * (size_t)kRF * Cp * 2 + (size_t)kRV * Dp * 2;
+  b += (size_t)kRV * Dp * 2;
   b += (size_t)kQ * 65 * 4;
   b += 2 * (size_t)kQ * 72 * 2;
   b += 2 * kQ * 4;
+  b += (kMaxSuffix + 8) * 4;
   b = (b + 15) / 16 * 16;
   b += 8 * 8;                                    // mbarriers
   return b + 16;
@@ -79,7 +91,13 @@ __device__ inline TcSmem carve_tc(char* base, int P, int cf, int dpart) {
   s.Pp = pad16(P) + 8;
   s.Cp = pad16(cf) + 8;
   s.Dp = dpart + 8;
+  s.Gp = group_elems(s.Pp);
+  s.Gc = group_elems(s.Cp);
+  base += (128 - (__cvta_generic_to_shared(base) & 127)) & 127;
   char* p = base;
+  s.phi = reinterpret_cast<__nv_bfloat16*>(p); p += (size_t)(kRF / 4) * s.Gp * 2;
+  s.qc = reinterpret_cast<__nv_bfloat16*>(p); p += (size_t)(kRF / 4) * s.Gc * 2;
+  s.kc = reinterpret_cast<__nv_bfloat16*>(p); p += (size_t)(kRF / 4) * s.Gc * 2;
   s.st_pos = reinterpret_cast<int*>(p); p += kStage * kQ * 4;
   s.st_id = reinterpret_cast<uint16_t*>(p); p += kStage * kStageIds * 2;
   p = base + ((p - base) + 15) / 16 * 16;
@@ -89,15 +107,14 @@ __device__ inline TcSmem carve_tc(char* base, int P, int cf, int dpart) {
   s.id = reinterpret_cast<int*>(p); p += kRF * 4;
   s.used = reinterpret_cast<int*>(p); p += kRF * 4;
   s.la = reinterpret_cast<float*>(p); p += kRF * 4;
-  s.phi = reinterpret_cast<__nv_bfloat16*>(p); p += (size_t)kRF * s.Pp * 2;
-  s.qc = reinterpret_cast<__nv_bfloat16*>(p); p += (size_t)kRF * s.Cp * 2;
-  s.kc = reinterpret_cast<__nv_bfloat16*>(p); p += (size_t)kRF * s.Cp * 2;
   s.v = reinterpret_cast<__nv_bfloat16*>(p); p += (size_t)kRV * s.Dp * 2;
   s.sc = reinterpret_cast<float*>(p); p += kQ * 65 * 4;
   s.att = reinterpret_cast<__nv_bfloat16*>(p); p += 2 * kQ * 72 * 2;
   s.qhay = reinterpret_cast<int*>(p); p += 2 * kQ * 4;
+  s.wsuf = reinterpret_cast<float*>(p); p += (kMaxSuffix + 8) * 4;
   p = base + ((p - base) + 15) / 16 * 16;
   s.vbar = reinterpret_cast<uint64_t*>(p);
+  s.fbar = s.vbar + 3;
   return s;
 }
 
@@ -113,10 +130,15 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
                ::"r"(su32(dst)), "l"(src), "r"(bytes), "r"(su32(bar))
                : "memory");
 }
-__device__ __forceinline__ int warp_sum_int(int v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  return v;
+// Four rows (row coordinates y0..y3, column 0) of a 2-D tensor map into consecutive rows at dst (the map's box is one
+// row of the ring's padded pitch), counted on `bar`; rows outside the tensor read zeros.
+__device__ __forceinline__ void gather4_rows(void* dst, const CUtensorMap* map, int y0, int y1, int y2, int y3,
+                                             uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, "
+      "%4, %5, %6}], [%7];" ::"r"(su32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(y0), "r"(y1), "r"(y2),
+      "r"(y3), "r"(su32(bar))
+      : "memory");
 }
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
@@ -158,6 +180,7 @@ struct TcBlock {
   int64_t r, b, S0, S1;
   int tau, dp0, dpart, Ppad, Cpad;
   float tasa;
+  float inv_temp;       // 1 / temperature: the scores' division becomes a product (within an fp32 ulp)
   bool write_signals;
 };
 }  // namespace
@@ -180,54 +203,57 @@ __device__ __forceinline__ void tc_stage1(const ScoreArgs& a, const TcSmem& S, c
   }
 }
 
-// Scalars and feature rows of sub-tile t, one warp per slot. Lane 0 derives (position, id, used) from the staging
-// buffer and writes them to the feature ring; the lanes copy the slot's items in one pass by cp.async: 16-byte
-// chunks of phi, Qc and Kc (zero-filled outside the row), the clock (8 B), log_alfa (4 B) and the kMaxSuffix previous
-// signatures (4 B; NaN, never equal, before the text and past K).
-__device__ __forceinline__ void tc_stage2_features(const ScoreArgs& a, const TcSmem& S, const TcBlock& k, int t) {
-  const char* phi = reinterpret_cast<const char*>(a.phi);
-  const char* Qc = reinterpret_cast<const char*>(a.Qc);
-  const char* Kc = reinterpret_cast<const char*>(a.Kc);
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+// Scalars and feature rows of sub-tile t, spread over the 16 warps. Warp w takes slots 2w and 2w + 1 (lanes 0 and 1):
+// it derives (position, id, used) from the staging buffer, writes them to the feature ring and copies the slot's
+// clock (8 B), log_alfa (4 B) and its kMaxSuffix previous signatures (4 B; NaN, never equal, before the text and past
+// K) by cp.async. The phi, Qc and Kc rows move as tensor-map row gathers of four slots each: lane 0 of warps 0-7
+// issues the three gathers of slots 4w .. 4w + 3, counted on the stage's mbarrier (its byte count is set by thread 0
+// beforehand, expect_features); a slot outside the row reads zero rows (row coordinate -1), and the ring's padding
+// columns beyond P / cf are zero-filled by the same copies.
+__device__ __forceinline__ void tc_stage2_features(const ScoreArgs& a, const TcSmem& S, const TcBlock& k, int t,
+                                                   const CUtensorMap* tm_phi, const CUtensorMap* tm_qc,
+                                                   const CUtensorMap* tm_kc) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const int buf = (t + 1) % kStage;
-  const int cph = k.Ppad / 8, cpc = k.Cpad / 8;
-  const int n_items = cph + 2 * cpc + 2 + kMaxSuffix;
-  for (int i = wid; i < kQ; i += nw) {
-    const int64_t s = k.S0 + (int64_t)t * kQ + i;
+  const int64_t s0 = k.S0 + (int64_t)t * kQ;
+  if (lane < 2) {
+    const int i = 2 * wid + lane;
+    const int64_t s = s0 + i;
     const int fr = frow((t + 1) * kQ + i);
     const bool real = s >= 0 && s < a.L;
     const int pos = real ? S.st_pos[buf * kQ + i] : 0;
-    if (lane == 0) {
-      const int id = real ? (int)S.st_id[buf * kStageIds + i] : -1;
-      const bool used = real && s + 1 < a.L && (int)S.st_id[buf * kStageIds + i + 1] == id && pos + 1 < a.Lf;
-      S.pos[fr] = pos;
-      S.id[fr] = id;
-      S.used[fr] = used ? 1 : 0;
-    }
+    const int id = real ? (int)S.st_id[buf * kStageIds + i] : -1;
+    const bool used = real && s + 1 < a.L && (int)S.st_id[buf * kStageIds + i + 1] == id && pos + 1 < a.Lf;
+    S.pos[fr] = pos;
+    S.id[fr] = id;
+    S.used[fr] = used ? 1 : 0;
     const int64_t g = k.b * a.Lf + pos;
-    for (int it = lane; it < n_items; it += 32) {
-      if (it < cph) {
-        const bool ok = real && it * 8 < a.P;
-        cp_async16(S.phi + fr * S.Pp + it * 8, phi + (g * a.P + (ok ? it * 8 : 0)) * 2, ok);
-      } else if (it < cph + 2 * cpc) {
-        const int c = it - cph;
-        const bool isq = c < cpc;
-        const int col = (isq ? c : c - cpc) * 8;
-        const bool ok = real && col < a.cf;
-        cp_async16((isq ? S.qc : S.kc) + fr * S.Cp + col, (isq ? Qc : Kc) + (g * a.cf + (ok ? col : 0)) * 2, ok);
-      } else if (it == cph + 2 * cpc) {
-        if (real) cp_async8(S.bt + fr, a.Bt + g);
-        else S.bt[fr] = 0.0;
-      } else if (it == cph + 2 * cpc + 1) {
-        if (real) cp_async4(S.la + fr, a.log_alfa + g);
-        else S.la[fr] = 0.f;
-      } else {
-        const int c = it - (cph + 2 * cpc + 2);
-        const int64_t tt = (int64_t)pos - 1 - c;
-        if (real && c < a.K && tt >= 0) cp_async4(S.pf + fr * kMaxSuffix + c, a.sig + k.b * a.Lf + tt);
-        else S.pf[fr * kMaxSuffix + c] = __int_as_float(0x7fc00000);
-      }
+    if (real) {
+      cp_async8(S.bt + fr, a.Bt + g);
+      cp_async4(S.la + fr, a.log_alfa + g);
+    } else {
+      S.bt[fr] = 0.0;
+      S.la[fr] = 0.f;
     }
+#pragma unroll
+    for (int c = 0; c < kMaxSuffix; ++c) {
+      const int64_t tt = (int64_t)pos - 1 - c;
+      if (real && c < a.K && tt >= 0) cp_async4(S.pf + fr * kMaxSuffix + c, a.sig + k.b * a.Lf + tt);
+      else S.pf[fr * kMaxSuffix + c] = __int_as_float(0x7fc00000);
+    }
+  } else if (lane == 2 && wid < kQ / 4) {
+    int y[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int i = 4 * wid + j;
+      const int64_t s = s0 + i;
+      y[j] = (s >= 0 && s < a.L) ? (int)(k.b * a.Lf + S.st_pos[buf * kQ + i]) : -1;
+    }
+    uint64_t* bar = S.fbar + ((t + 1) & 3);
+    const int fr0 = frow((t + 1) * kQ + 4 * wid);
+    gather4_rows(S.phi + S.prow(fr0), tm_phi, y[0], y[1], y[2], y[3], bar);
+    gather4_rows(S.qc + S.crow(fr0), tm_qc, y[0], y[1], y[2], y[3], bar);
+    gather4_rows(S.kc + S.crow(fr0), tm_kc, y[0], y[1], y[2], y[3], bar);
   }
 }
 
@@ -259,6 +285,7 @@ __device__ __forceinline__ void tc_stage2_values(const ScoreArgs& a, const TcSme
 // softmax, the weights into att[t & 1] and the per-table gate signals. Warp w (0-7) owns n-tile w (keys 8w .. 8w + 7)
 // of both m-tiles: the two MMA chains run interleaved on the same key fragments, then one epilogue pass over the
 // warp's 8 elements per lane; the softmax takes the warp's 4 queries in one set of shuffle rounds.
+template <bool kSuf4>
 __device__ __forceinline__ void tc_scores(const ScoreArgs& a, const TcSmem& S, const TcBlock& k, int t) {
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const int C = a.C;
@@ -275,12 +302,12 @@ __device__ __forceinline__ void tc_scores(const ScoreArgs& a, const TcSmem& S, c
     const int rk = frow(lb + nt * 8 + (lane & 7));
     const int kb = ((lane >> 3) & 1) * 8;
     const int ra0 = frow(lb + kQ + (lane & 15)), ra1 = frow(lb + kQ + 16 + (lane & 15));
-    const uint32_t phi_b = su32(S.phi) + 2u * (uint32_t)(rk * S.Pp + kb);
-    const uint32_t kc_b = su32(S.kc) + 2u * (uint32_t)(rk * S.Cp + kb);
-    const uint32_t phi_a0 = su32(S.phi) + 2u * (uint32_t)(ra0 * S.Pp + ka);
-    const uint32_t phi_a1 = su32(S.phi) + 2u * (uint32_t)(ra1 * S.Pp + ka);
-    const uint32_t qc_a0 = su32(S.qc) + 2u * (uint32_t)(ra0 * S.Cp + ka);
-    const uint32_t qc_a1 = su32(S.qc) + 2u * (uint32_t)(ra1 * S.Cp + ka);
+    const uint32_t phi_b = su32(S.phi) + 2u * (uint32_t)(S.prow(rk) + kb);
+    const uint32_t kc_b = su32(S.kc) + 2u * (uint32_t)(S.crow(rk) + kb);
+    const uint32_t phi_a0 = su32(S.phi) + 2u * (uint32_t)(S.prow(ra0) + ka);
+    const uint32_t phi_a1 = su32(S.phi) + 2u * (uint32_t)(S.prow(ra1) + ka);
+    const uint32_t qc_a0 = su32(S.qc) + 2u * (uint32_t)(S.crow(ra0) + ka);
+    const uint32_t qc_a1 = su32(S.qc) + 2u * (uint32_t)(S.crow(ra1) + ka);
     for (int k0 = 0; k0 < k.Ppad; k0 += 16) {
       uint32_t b0, b1;
       ldsm_x2(phi_b + 2 * k0, b0, b1);
@@ -342,21 +369,25 @@ __device__ __forceinline__ void tc_scores(const ScoreArgs& a, const TcSmem& S, c
       const int qi = g4 + 8 * uq;
       const int kj = kj0 + uk;
       const int64_t sq = q0 + qi, sk = q0 - kQ + kj;
-      float val = -INFINITY;
-      if (band[mt] && kj < qi + 32 && kj >= qi + 32 - C && sq < a.L && sk >= 0 && k_id[uk] == q_id[uq]) {
-        const float s1 = round_bf16(__fdiv_rn(round_bf16(cphi[mt][e]), a.inv_temp_div));
-        const float s2 = round_bf16(__fmul_rn(round_bf16(cqk[mt][e]), a.esc_c));
-        float t1 = round_bf16(__fadd_rn(s1, s2));
-        const float4 qa = q_pf[uq][0], qb = q_pf[uq][1], ka = k_pf[uk][0], kb = k_pf[uk][1];
-        const uint32_t eq = (qa.x == ka.x ? 1u : 0u) | (qa.y == ka.y ? 2u : 0u) | (qa.z == ka.z ? 4u : 0u) |
-                            (qa.w == ka.w ? 8u : 0u) | (qb.x == kb.x ? 16u : 0u) | (qb.y == kb.y ? 32u : 0u) |
-                            (qb.z == kb.z ? 64u : 0u) | (qb.w == kb.w ? 128u : 0u);
-        const int ln = __ffs(~eq) - 1;          // leading equal entries (entries past K are NaN: never equal)
-        t1 = __fadd_rn(t1, a.w_suf[ln]);
-        t1 = __fadd_rn(t1, k_la[uk]);
-        const float dt = __double2float_rn(k_bt[uk] - q_bt[uq]);
-        val = __fadd_rn(t1, __fmul_rn(dt, k.tasa));
+      // every element is computed (no divergent branch) and masked at the end: outside the band, the row or the
+      // bucket it is -inf
+      const bool ok = band[mt] && kj < qi + 32 && kj >= qi + 32 - C && sq < a.L && sk >= 0 && k_id[uk] == q_id[uq];
+      const float s1 = round_bf16(__fmul_rn(round_bf16(cphi[mt][e]), k.inv_temp));
+      const float s2 = round_bf16(__fmul_rn(round_bf16(cqk[mt][e]), a.esc_c));
+      float t1 = round_bf16(__fadd_rn(s1, s2));
+      const float4 qa = q_pf[uq][0], ka = k_pf[uk][0];
+      uint32_t eq = (qa.x == ka.x ? 1u : 0u) | (qa.y == ka.y ? 2u : 0u) | (qa.z == ka.z ? 4u : 0u) |
+                    (qa.w == ka.w ? 8u : 0u);
+      if (!kSuf4) {                             // entries 4 .. 7 are NaN (never equal) when K <= 4
+        const float4 qb = q_pf[uq][1], kb = k_pf[uk][1];
+        eq |= (qb.x == kb.x ? 16u : 0u) | (qb.y == kb.y ? 32u : 0u) | (qb.z == kb.z ? 64u : 0u) |
+              (qb.w == kb.w ? 128u : 0u);
       }
+      const int ln = __ffs(~eq) - 1;            // leading equal entries (entries past K are NaN: never equal)
+      t1 = __fadd_rn(t1, S.wsuf[ln]);
+      t1 = __fadd_rn(t1, k_la[uk]);
+      const float dt = __double2float_rn(k_bt[uk] - q_bt[uq]);
+      const float val = ok ? __fadd_rn(t1, __fmul_rn(dt, k.tasa)) : -INFINITY;
       S.sc[qi * 65 + kj] = val;
     }
   }
@@ -380,8 +411,8 @@ __device__ __forceinline__ void tc_scores(const ScoreArgs& a, const TcSmem& S, c
     for (int u = 0; u < 4; ++u) m[u] = fmaxf(m[u], __shfl_xor_sync(0xffffffffu, m[u], o));
 #pragma unroll
   for (int u = 0; u < 4; ++u) {
-    e[u][0] = x[u][0] != -INFINITY ? expf(__fsub_rn(x[u][0], m[u])) : 0.f;
-    e[u][1] = x[u][1] != -INFINITY ? expf(__fsub_rn(x[u][1], m[u])) : 0.f;
+    e[u][0] = x[u][0] != -INFINITY ? __expf(__fsub_rn(x[u][0], m[u])) : 0.f;
+    e[u][1] = x[u][1] != -INFINITY ? __expf(__fsub_rn(x[u][1], m[u])) : 0.f;
     sum[u] = e[u][0] + e[u][1];
   }
 #pragma unroll
@@ -398,13 +429,14 @@ __device__ __forceinline__ void tc_scores(const ScoreArgs& a, const TcSmem& S, c
     const int64_t gq = k.b * (a.q_hi - a.q_lo) + (posq - a.q_lo);
     float w0 = 0.f, w1 = 0.f;
     if (anyv) {
-      w0 = __fdiv_rn(e[u][0], sum[u]);
-      w1 = __fdiv_rn(e[u][1], sum[u]);
+      const float rs = __frcp_rn(sum[u]);
+      w0 = __fmul_rn(e[u][0], rs);
+      w1 = __fmul_rn(e[u][1], rs);
       // the largest weight is the maximum's: exp(0) / sum
       if (lane == 0 && k.write_signals && mine) {
         a.sen_hay[gq * a.T + k.tau] = 1;
         a.sen_mx[gq * a.T + k.tau] = m[u];
-        a.sen_pk[gq * a.T + k.tau] = __fdiv_rn(1.f, sum[u]);
+        a.sen_pk[gq * a.T + k.tau] = rs;
       }
     } else if (lane == 0 && k.write_signals && mine) {
       a.sen_hay[gq * a.T + k.tau] = 0;
@@ -471,7 +503,9 @@ __device__ __forceinline__ void tc_values(const ScoreArgs& a, const TcSmem& S, c
   }
 }
 
-__global__ void __launch_bounds__(kThreadsTc, 1) k_score_tc(ScoreArgs a, int nds, int dpart) {
+__global__ void __launch_bounds__(kThreadsTc, 1)
+k_score_tc(const __grid_constant__ CUtensorMap tm_phi, const __grid_constant__ CUtensorMap tm_qc,
+           const __grid_constant__ CUtensorMap tm_kc, ScoreArgs a, int nds, int dpart) {
   extern __shared__ __align__(16) char smem_raw[];
   const TcSmem S = carve_tc(smem_raw, a.P, a.cf, dpart);
   TcBlock k;
@@ -487,6 +521,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1) k_score_tc(ScoreArgs a, int nds
   k.Ppad = pad16(a.P);
   k.Cpad = pad16(a.cf);
   k.tasa = a.tasa[k.tau];
+  k.inv_temp = 1.f / a.inv_temp_div;
   k.write_signals = part == 0;
   const int wid = threadIdx.x >> 5;
   const bool group_a = wid < kGroupWarps;
@@ -497,9 +532,10 @@ __global__ void __launch_bounds__(kThreadsTc, 1) k_score_tc(ScoreArgs a, int nds
     uint4* z0 = reinterpret_cast<uint4*>(S.phi);
     const int nz = (int)(((char*)(S.v + kRV * S.Dp) - (char*)S.phi) / 16);
     for (int i = threadIdx.x; i < nz; i += blockDim.x) z0[i] = make_uint4(0, 0, 0, 0);
+    if (threadIdx.x <= kMaxSuffix) S.wsuf[threadIdx.x] = threadIdx.x <= a.K ? a.w_suf[threadIdx.x] : 0.f;
     umma::fence_proxy_async();                 // the zeros precede the bulk copies into the same rows
     if (threadIdx.x == 0) {
-      for (int i = 0; i < 3; ++i) umma::mbar_init(S.vbar + i, 1);
+      for (int i = 0; i < 7; ++i) umma::mbar_init(S.vbar + i, 1);   // 3 value stages, then 4 feature stages
       umma::fence_mbar_init();
     }
   }
@@ -507,9 +543,17 @@ __global__ void __launch_bounds__(kThreadsTc, 1) k_score_tc(ScoreArgs a, int nds
   auto wait_values = [&](int t) {
     umma::mbar_wait(S.vbar + ((t + 1) % 3), (uint32_t)(((t + 1) / 3) & 1), a.status);
   };
-  // the stage's transaction count (its used rows) is set by thread 0 before any copy of the stage is issued
+  // bounded wait for the feature rows of sub-tile t (stage (t + 1) % 4)
+  auto wait_features = [&](int t) {
+    umma::mbar_wait(S.fbar + ((t + 1) & 3), (uint32_t)(((t + 1) >> 2) & 1), a.status);
+  };
+  // the stages' transaction counts (the used value rows; the fixed feature rows) are set by thread 0 before any copy
+  // of the stage is issued
   auto expect_values = [&](int t) {
     if (threadIdx.x == 0) umma::mbar_expect_tx(S.vbar + ((t + 1) % 3), (uint32_t)tc_value_bytes(S, k, t));
+  };
+  auto expect_features = [&](int t) {
+    if (threadIdx.x == 0) umma::mbar_expect_tx(S.fbar + ((t + 1) & 3), (uint32_t)(kQ * (S.Pp + 2 * S.Cp) * 2));
   };
 
   // prologue: sub-tiles -1 (the first window half), 0 and 1 of the features, -1 and 0 of the values, the scores of
@@ -520,10 +564,13 @@ __global__ void __launch_bounds__(kThreadsTc, 1) k_score_tc(ScoreArgs a, int nds
   if (ntile > 1) tc_stage1(a, S, k, 1);
   cp_async_commit();
   cp_async_wait_all();
+  expect_features(-1);
+  expect_features(0);
+  if (ntile > 1) expect_features(1);
   __syncthreads();
-  tc_stage2_features(a, S, k, -1);
-  tc_stage2_features(a, S, k, 0);
-  if (ntile > 1) tc_stage2_features(a, S, k, 1);
+  tc_stage2_features(a, S, k, -1, &tm_phi, &tm_qc, &tm_kc);
+  tc_stage2_features(a, S, k, 0, &tm_phi, &tm_qc, &tm_kc);
+  if (ntile > 1) tc_stage2_features(a, S, k, 1, &tm_phi, &tm_qc, &tm_kc);
   cp_async_commit();
   cp_async_wait_all();
   __syncthreads();
@@ -534,36 +581,49 @@ __global__ void __launch_bounds__(kThreadsTc, 1) k_score_tc(ScoreArgs a, int nds
   __syncthreads();
   tc_stage2_values(a, S, k, -1);
   tc_stage2_values(a, S, k, 0);
-  if (group_a) tc_scores(a, S, k, 0);
+  wait_features(-1);
+  wait_features(0);
+  const bool suf4 = a.K <= 4;
+  if (group_a) {
+    if (suf4) tc_scores<true>(a, S, k, 0);
+    else tc_scores<false>(a, S, k, 0);
+  }
   cp_async_wait_all();
   wait_values(-1);
   wait_values(0);
+  if (ntile > 1) wait_features(1);
   __syncthreads();
 
   for (int i = 0; i < ntile; ++i) {
-    // value rows of i + 1 (their scalars arrived with the features in iteration i - 1): count, then copy
+    // value rows of i + 1 (their scalars arrived with the features in iteration i - 1) and feature rows of i + 2:
+    // byte counts first, then the copies, issued by all warps
     if (i + 1 < ntile) expect_values(i + 1);
-    if (i + 2 < ntile) tc_stage2_features(a, S, k, i + 2);
+    if (i + 2 < ntile) expect_features(i + 2);
     if (i + 3 < ntile) tc_stage1(a, S, k, i + 3);
-    cp_async_commit();
     if (i + 1 < ntile) {
-      asm volatile("bar.sync 2, 512;" ::: "memory");   // the expect_tx precedes every copy of the stage
+      asm volatile("bar.sync 2, 512;" ::: "memory");   // the expect_tx precedes every copy of the stages
+      if (i + 2 < ntile) tc_stage2_features(a, S, k, i + 2, &tm_phi, &tm_qc, &tm_kc);
       tc_stage2_values(a, S, k, i + 1);
     }
+    cp_async_commit();
     if (group_a) {
-      if (i + 1 < ntile) tc_scores(a, S, k, i + 1);
+      if (i + 1 < ntile) {
+        if (suf4) tc_scores<true>(a, S, k, i + 1);
+        else tc_scores<false>(a, S, k, i + 1);
+      }
     } else {
       tc_values(a, S, k, i, wid - kGroupWarps);
     }
     cp_async_wait_all();
     if (i + 1 < ntile) wait_values(i + 1);
+    if (i + 2 < ntile) wait_features(i + 2);
     __syncthreads();
   }
 }
 
 bool score_tc_supported(const ScoreArgs& a) {
-  return a.d % 64 == 0 && a.d <= 1024 && a.C <= 32 && a.P <= kMaxPhi && a.P % 8 == 0 && a.cf <= kMaxConfirm &&
-         a.cf % 8 == 0 && a.K <= kMaxSuffix && a.L % 8 == 0;
+  return a.d % 64 == 0 && a.d <= 1024 && a.C <= 32 && a.P <= kMaxPhi && a.P % 8 == 0 && pad16(a.P) + 8 <= 256 &&
+         a.cf <= kMaxConfirm && a.cf % 8 == 0 && a.K <= kMaxSuffix && a.L % 8 == 0 && a.B * a.Lf < ((int64_t)1 << 31);
 }
 
 int launch_score_tc(const ScoreArgs& a, cudaStream_t s) {
@@ -574,9 +634,16 @@ int launch_score_tc(const ScoreArgs& a, cudaStream_t s) {
   if (dpart / 8 > kGroupWarps * kMaxNt) return ASRN_ERR_UNSUPPORTED;
   const size_t smem = tc_smem_bytes(a.P, a.cf, dpart);
   if (smem > 227 * 1024) return ASRN_ERR_UNSUPPORTED;
+  // feature rows as one-row boxes of the ring's padded pitch (the padding columns lie outside the tensor: zeros)
+  CUtensorMap tm_phi, tm_qc, tm_kc;
+  const uint64_t rows = (uint64_t)(a.B * a.Lf);
+  if (!make_tmap_rows_bf16(&tm_phi, a.phi, (uint64_t)a.P, rows, (uint64_t)a.P * 2, (uint32_t)(pad16(a.P) + 8)) ||
+      !make_tmap_rows_bf16(&tm_qc, a.Qc, (uint64_t)a.cf, rows, (uint64_t)a.cf * 2, (uint32_t)(pad16(a.cf) + 8)) ||
+      !make_tmap_rows_bf16(&tm_kc, a.Kc, (uint64_t)a.cf, rows, (uint64_t)a.cf * 2, (uint32_t)(pad16(a.cf) + 8)))
+    return ASRN_ERR_CUDA;
   cudaFuncSetAttribute(k_score_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   dim3 grid((unsigned)(((a.L + kSpanTc - 1) / kSpanTc) * nds), (unsigned)(a.B * a.T));
-  k_score_tc<<<grid, kThreadsTc, smem, s>>>(a, nds, dpart);
+  k_score_tc<<<grid, kThreadsTc, smem, s>>>(tm_phi, tm_qc, tm_kc, a, nds, dpart);
   return cudaGetLastError() == cudaSuccess ? ASRN_OK : ASRN_ERR_CUDA;
 }
 

@@ -42,9 +42,12 @@ ASRN_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait for the phase with the given parity to complete. false: timed out (status word set).
+// Bounded wait for the phase with the given parity to complete. false: timed out (status word set). Once the status
+// word records a timeout, later waits that do not complete at once give up immediately, so a kernel whose copies
+// never arrive ends after one wait limit rather than one per wait.
 ASRN_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, int* status) {
   if (mbar_try_wait(bar, parity)) return true;
+  if (status && *reinterpret_cast<volatile int*>(status) == ASRN_ERR_TIMEOUT) return false;
   const uint64_t t0 = global_ns();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
