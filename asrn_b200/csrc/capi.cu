@@ -124,6 +124,7 @@ RepetitionArgs repetition_args(const asrn_layer_config& c, const asrn_layer_weig
   const PreparedLayout pl = prepared_layout(c);
   RepetitionArgs a{};
   a.B = c.B; a.L = c.L; a.n = c.vistos;
+  a.Lf = c.L; a.pos0 = 0;
   a.c = w.c_vistos;
   a.kappa = reinterpret_cast<const float*>(prep + pl.kappa);
   return a;
@@ -405,6 +406,57 @@ int asrn_repetition(const asrn_layer_config* cfg, const asrn_layer_weights* w, c
   a.sig = sig; a.beta = beta; a.Bt = Bt; a.log_alfa = log_alfa; a.vistos = vistos; a.hawkes = hawkes; a.racha = racha;
   a.keys = keys; a.orden_ng = orden_ng; a.repetido = repetido;
   return launch_repetition(a, workspace, workspace_bytes, as_stream(stream));
+}
+
+size_t asrn_ngram_chunk_workspace_bytes(const asrn_layer_config* cfg) {
+  if (check_config(cfg) != ASRN_OK) return 0;
+  return ngram_chunk_workspace(cfg->B, cfg->L, cfg->vistos);
+}
+
+int asrn_ngram_chunk_sort(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared,
+                          int64_t L_feat, int64_t c0, const float* sig, const double* Bt, const float* log_alfa,
+                          uint64_t* keys, void* summary, void* workspace, size_t workspace_bytes, void* stream) {
+  int st = check_config(cfg);
+  if (st) return st;
+  if ((st = check_weights(w))) return st;
+  if (!prepared || !sig || !Bt || !log_alfa || !keys || !summary || c0 < 0 || c0 + cfg->L > L_feat ||
+      L_feat >= ((int64_t)1 << 31))
+    return ASRN_ERR_ARG;
+  RepetitionArgs a = repetition_args(*cfg, *w, reinterpret_cast<const char*>(prepared));
+  a.Lf = L_feat; a.pos0 = c0;
+  a.sig = sig; a.Bt = Bt; a.log_alfa = log_alfa;
+  return launch_ngram_chunk_sort(a, keys, summary, workspace, workspace_bytes, as_stream(stream));
+}
+
+int asrn_ngram_chunk_finish(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared,
+                            int64_t L_feat, int64_t c0, int32_t n_prev, const uint64_t* keys_prev,
+                            const void* summary_prev, const uint64_t* keys, const double* Bt, const float* log_alfa,
+                            uint8_t* vistos, float* hawkes, void* workspace, size_t workspace_bytes, void* stream) {
+  int st = check_config(cfg);
+  if (st) return st;
+  if ((st = check_weights(w))) return st;
+  if (!prepared || !keys || !Bt || !log_alfa || !vistos || !hawkes || n_prev < 0 ||
+      (n_prev > 0 && (!keys_prev || !summary_prev)) || c0 < 0 || c0 + cfg->L > L_feat ||
+      L_feat >= ((int64_t)1 << 31))
+    return ASRN_ERR_ARG;
+  RepetitionArgs a = repetition_args(*cfg, *w, reinterpret_cast<const char*>(prepared));
+  a.Lf = L_feat; a.pos0 = c0;
+  a.Bt = Bt; a.log_alfa = log_alfa; a.vistos = vistos; a.hawkes = hawkes;
+  return launch_ngram_chunk_finish(a, n_prev, keys_prev, summary_prev, keys, workspace, workspace_bytes,
+                                   as_stream(stream));
+}
+
+int asrn_racha_chunk(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared,
+                     const uint8_t* vistos, const double* beta, const float* racha_in, float* racha, float* racha_map,
+                     void* stream) {
+  int st = check_config(cfg);
+  if (st) return st;
+  if ((st = check_weights(w))) return st;
+  if (!prepared || !vistos || !beta || (!racha && !racha_map)) return ASRN_ERR_ARG;
+  RepetitionArgs a = repetition_args(*cfg, *w, reinterpret_cast<const char*>(prepared));
+  a.vistos = const_cast<uint8_t*>(vistos); a.beta = beta; a.racha = racha;
+  a.racha_in = racha_in; a.racha_map = racha_map;
+  return launch_racha(a, as_stream(stream));
 }
 
 size_t asrn_gate_workspace_bytes(const asrn_layer_config* cfg) {

@@ -103,7 +103,9 @@ struct ScoreArgs {
 };
 
 struct RepetitionArgs {
-  int64_t B, L;
+  int64_t B, L;            // L: positions of the (chunk of the) rows this call sorts and scans
+  int64_t Lf, pos0;        // per-position inputs are (B, Lf) rows; local index i is position pos0 + i (Lf = L, pos0 = 0
+                           // for whole rows)
   int n;
   const float* sig;
   const double* c;         // c_vistos (n)
@@ -116,6 +118,8 @@ struct RepetitionArgs {
   double* keys;            // optional
   int32_t* orden_ng;       // optional
   uint8_t* repetido;       // optional
+  const float* racha_in;   // optional (B): streak value before the first position (0 when null)
+  float* racha_map;        // optional (B, 2): the rows' streak maps S_last = A * S_in + B (A, B)
 };
 
 struct GateArgs {
@@ -204,6 +208,12 @@ int launch_shard_tails(int64_t rows, int64_t Lc, int nb, int C, int64_t c0, cons
 int launch_shard_merge(int64_t rows, int64_t Lc, int nb, int C, int64_t c0, int n_prev, const int32_t* tails_prev,
                        const int32_t* orden_loc, const uint16_t* ids_loc, int64_t Lv, int32_t* orden_v,
                        uint16_t* ids_v, int64_t* row_len, int32_t pad_pos, void* ws, cudaStream_t s);
+size_t ngram_chunk_workspace(int64_t B, int64_t Lc, int n);
+int launch_ngram_chunk_sort(const RepetitionArgs& a, uint64_t* keys, void* summary, void* ws, size_t ws_bytes,
+                            cudaStream_t s);
+int launch_ngram_chunk_finish(const RepetitionArgs& a, int n_prev, const uint64_t* keys_prev, const void* summary_prev,
+                              const uint64_t* keys, void* ws, size_t ws_bytes, cudaStream_t s);
+int launch_racha(const RepetitionArgs& a, cudaStream_t s);
 int launch_gen_front(const GenFrontArgs& a, bool half, cudaStream_t s);
 int launch_gen_gate(const GateArgs& a, bool half, cudaStream_t s);
 size_t hawkes_table_bytes(int64_t B, int n, int64_t cap);

@@ -151,7 +151,8 @@ __global__ void __launch_bounds__(1024) k_racha(RepetitionArgs a) {
   const float kr = a.kappa[a.n];
   __shared__ Affine warp_agg[32];
   __shared__ Affine carry_s;
-  if (threadIdx.x == 0) carry_s = Affine{1.f, 0.f};
+  // the map from the streak before the row (0, or racha_in) to each position; with racha_in the carry is constant
+  if (threadIdx.x == 0) carry_s = a.racha_in ? Affine{0.f, a.racha_in[b]} : Affine{1.f, 0.f};
   __syncthreads();
   constexpr int kItems = 4;
   for (int64_t base = 0; base < L; base += 1024 * kItems) {
@@ -173,11 +174,15 @@ __global__ void __launch_bounds__(1024) k_racha(RepetitionArgs a) {
     for (int k = 0; k < kItems; ++k) {
       const int64_t t = base + (int64_t)threadIdx.x * kItems + k;
       const Affine s = compose(carry, v[k]);
-      if (t < L) a.racha[b * L + t] = s.b;
+      if (t < L && a.racha) a.racha[b * L + t] = s.b;
     }
     __syncthreads();
     if (threadIdx.x == blockDim.x - 1) carry_s = compose(carry, v[kItems - 1]);
     __syncthreads();
+  }
+  if (a.racha_map && threadIdx.x == 0) {
+    a.racha_map[2 * b] = carry_s.a;
+    a.racha_map[2 * b + 1] = carry_s.b;
   }
 }
 
@@ -211,14 +216,14 @@ __global__ void __launch_bounds__(1024) k_ngram_tile_sort(RepetitionArgs a, int6
   const int64_t b = row / a.n;
   const int ni = (int)(row % a.n);
   const int64_t L = a.L, base = tile * kRepTile;
-  const float* sig = a.sig + b * L;
+  const float* sig = a.sig + b * a.Lf;
   for (int i = threadIdx.x; i < kRepTile; i += blockDim.x) {
     const int64_t p = base + i;
     if (p < L) {
-      const double key = ngram_key_at(sig, p, ni, a.c);
+      const double key = ngram_key_at(sig, a.pos0 + p, ni, a.c);
       if (a.keys) a.keys[(b * L + p) * a.n + ni] = key;
       sk[i] = sortable_key(key);
-      sp[i] = (uint32_t)p;
+      sp[i] = (uint32_t)(a.pos0 + p);
     } else {
       sk[i] = 0xFFFFFFFFFFFFFFFFull;
       sp[i] = 0xFFFFFFFFu;
@@ -397,6 +402,288 @@ static int launch_repetition_long(const RepetitionArgs& a, void* ws, size_t ws_b
   }
   k_ngram_scan_tile<<<(unsigned)(rows * tiles), 1024, 0, s>>>(a, tiles, kin, pin, r.vloc, r.agg);
   k_ngram_apply<<<(unsigned)(rows * tiles), 1024, 0, s>>>(a, tiles, kin, pin, r.vloc, r.agg);
+  return cudaGetLastError() == cudaSuccess ? ASRN_OK : ASRN_ERR_CUDA;
+}
+
+// ---- chunk of a sequence-sharded row ---------------------------------------------------------------------------
+// Shard r owns positions [pos0, pos0 + Lc) of every sequence; the per-position inputs (signatures, clock, log alfa)
+// are the gathered full rows. The n-gram memory of the chunk (asrn/estable.py:304-321) in two calls around one
+// exchange:
+//   sort    the chunk's (key, position) pairs per (b, n) row (tile sort + merges), then two scans over the sorted row:
+//           lambda with the chunk alone (a group's first slot starts from 0) and P_i, the product of a_j over the
+//           group's slots after its first up to i. Out: the sorted keys and, at each group's first slot, its summary
+//           {B of its first and last occurrence, lambda and P at its last slot, alfa of its last occurrence}.
+//   finish  per group, the state after the earlier chunks: walk the earlier shards in order, find the key in each
+//           one's sorted keys (binary search) and fold its summary: lambda <- P_L * a(B_first - B) * (lambda + alfa)
+//           + lambda_L, then alfa, B <- the last occurrence's. The chunk's first occurrence of a key seen before is
+//           a repeat (vistos = 1) and every slot of its group gets lambda_i + P_i * a(B_first - B) * (lambda + alfa):
+//           the recursion lambda_i = a_i (lambda_{i-1} + alfa_{i-1}) is linear in the incoming state.
+// The streak (racha) carries across chunks as an affine map (k_racha with racha_in / racha_map).
+struct NgcSummary {
+  double b_first, b_last;
+  float lam, prod, alfa, pad;
+};
+
+struct NgcLayout {
+  uint64_t *k0, *k1;
+  uint32_t *p0, *p1;
+  float4* vloc;        // (rows, Lc) tile-local inclusive maps of both scans (lambda a, b; product a, b)
+  float4* agg;         // (rows, tiles)
+  float2* lp;          // (rows, Lc) (lambda, P) per sorted slot
+  float2* carry;       // (rows, Lc) at group-first slots: (c, seen)
+  uint32_t* pos;       // (rows, Lc) sorted positions (the final ping-pong buffer's copy)
+};
+
+static NgcLayout ngc_layout(void* ws, int64_t rows, int64_t Lc) {
+  char* p = reinterpret_cast<char*>(ws);
+  const size_t E = (size_t)rows * Lc;
+  const size_t tiles = (size_t)((Lc + kRepTile - 1) / kRepTile);
+  NgcLayout r;
+  size_t o = 0;
+  r.k0 = reinterpret_cast<uint64_t*>(p + o); o = align_up(o + E * 8);
+  r.k1 = reinterpret_cast<uint64_t*>(p + o); o = align_up(o + E * 8);
+  r.p0 = reinterpret_cast<uint32_t*>(p + o); o = align_up(o + E * 4);
+  r.p1 = reinterpret_cast<uint32_t*>(p + o); o = align_up(o + E * 4);
+  r.vloc = reinterpret_cast<float4*>(p + o); o = align_up(o + E * 16);
+  r.agg = reinterpret_cast<float4*>(p + o); o = align_up(o + rows * tiles * 16);
+  r.lp = reinterpret_cast<float2*>(p + o); o = align_up(o + E * 8);
+  r.carry = reinterpret_cast<float2*>(p + o); o = align_up(o + E * 8);
+  r.pos = reinterpret_cast<uint32_t*>(p + o);
+  return r;
+}
+
+size_t ngram_chunk_workspace(int64_t B, int64_t Lc, int n) {
+  const size_t rows = (size_t)B * n, E = rows * (size_t)Lc;
+  const size_t tiles = (size_t)((Lc + kRepTile - 1) / kRepTile);
+  return 2 * align_up(E * 8) + 2 * align_up(E * 4) + align_up(E * 16) + align_up(rows * tiles * 16) +
+         2 * align_up(E * 8) + align_up(E * 4);
+}
+
+// elements of the two scans at sorted slot i: lambda (as ngram_elem) and the in-group product
+__device__ __forceinline__ void ngc_elems(const RepetitionArgs& a, const uint64_t* K, const uint32_t* P, int64_t b,
+                                          int64_t i, float kappa, Affine* lam, Affine* prod) {
+  const bool rep = i > 0 && K[i] == K[i - 1] && K[i] != 0xFFFFFFFFFFFFFFFFull;
+  if (!rep) {
+    *lam = Affine{0.f, 0.f};
+    *prod = Affine{0.f, 1.f};
+    return;
+  }
+  const int64_t pc = P[i], pp = P[i - 1];
+  const double dB = fmax(a.Bt[b * a.Lf + pc] - a.Bt[b * a.Lf + pp], 0.0);
+  const float av = expf(__fmul_rn(-kappa, __double2float_rn(dB)));
+  *lam = Affine{av, __fmul_rn(av, expf(a.log_alfa[b * a.Lf + pp]))};
+  *prod = Affine{av, 0.f};
+}
+
+__global__ void __launch_bounds__(1024) k_ngc_scan_tile(RepetitionArgs a, int64_t tiles, const uint64_t* K,
+                                                        const uint32_t* Pp, float4* vloc, float4* agg) {
+  __shared__ Affine warp_agg[32];
+  const int64_t row = blockIdx.x / tiles, tile = blockIdx.x % tiles;
+  const int64_t b = row / a.n;
+  const int ni = (int)(row % a.n);
+  const int64_t L = a.L;
+  const float kappa = a.kappa[ni];
+  const uint64_t* Kr = K + row * L;
+  const uint32_t* Pr = Pp + row * L;
+  Affine v[kScanItems], w[kScanItems];
+  const int64_t i0 = tile * kRepTile + (int64_t)threadIdx.x * kScanItems;
+#pragma unroll
+  for (int k = 0; k < kScanItems; ++k) {
+    const int64_t i = i0 + k;
+    if (i < L) ngc_elems(a, Kr, Pr, b, i, kappa, &v[k], &w[k]);
+    else v[k] = w[k] = Affine{1.f, 0.f};
+  }
+  block_scan_affine<kScanItems>(v, warp_agg);
+  __syncthreads();
+  block_scan_affine<kScanItems>(w, warp_agg);
+#pragma unroll
+  for (int k = 0; k < kScanItems; ++k) {
+    const int64_t i = i0 + k;
+    if (i < L) vloc[row * L + i] = make_float4(v[k].a, v[k].b, w[k].a, w[k].b);
+  }
+  if (threadIdx.x == blockDim.x - 1)
+    agg[row * tiles + tile] = make_float4(v[kScanItems - 1].a, v[kScanItems - 1].b, w[kScanItems - 1].a,
+                                          w[kScanItems - 1].b);
+}
+
+__global__ void __launch_bounds__(1024) k_ngc_apply(RepetitionArgs a, int64_t tiles, const float4* vloc,
+                                                    const float4* agg, float2* lp, const uint32_t* Pin,
+                                                    uint32_t* Pout) {
+  __shared__ Affine carry_s[2];
+  const int64_t row = blockIdx.x / tiles, tile = blockIdx.x % tiles;
+  const int64_t L = a.L;
+  if (threadIdx.x == 0) {
+    Affine c{1.f, 0.f}, e{1.f, 0.f};
+    for (int64_t q = 0; q < tile; ++q) {
+      const float4 g = agg[row * tiles + q];
+      c = compose(c, Affine{g.x, g.y});
+      e = compose(e, Affine{g.z, g.w});
+    }
+    carry_s[0] = c;
+    carry_s[1] = e;
+  }
+  __syncthreads();
+  const Affine c = carry_s[0], e = carry_s[1];
+  const int64_t end = (tile + 1) * kRepTile < L ? (tile + 1) * kRepTile : L;
+  for (int64_t i = tile * kRepTile + threadIdx.x; i < end; i += blockDim.x) {
+    const float4 v = vloc[row * L + i];
+    lp[row * L + i] = make_float2(compose(c, Affine{v.x, v.y}).b, compose(e, Affine{v.z, v.w}).b);
+    Pout[row * L + i] = Pin[row * L + i];
+  }
+}
+
+// first index in K[lo, hi) with K[idx] >= v / > v
+__device__ __forceinline__ int64_t lower_u64(const uint64_t* K, int64_t lo, int64_t hi, uint64_t v) {
+  while (lo < hi) {
+    const int64_t mid = (lo + hi) >> 1;
+    if (K[mid] < v) lo = mid + 1; else hi = mid;
+  }
+  return lo;
+}
+__device__ __forceinline__ int64_t upper_u64(const uint64_t* K, int64_t lo, int64_t hi, uint64_t v) {
+  while (lo < hi) {
+    const int64_t mid = (lo + hi) >> 1;
+    if (K[mid] <= v) lo = mid + 1; else hi = mid;
+  }
+  return lo;
+}
+
+__global__ void k_ngc_summary(RepetitionArgs a, const uint64_t* K, const uint32_t* P, const float2* lp,
+                              uint64_t* keys_out, NgcSummary* summ) {
+  const int64_t L = a.L;
+  const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (g >= a.B * a.n * L) return;
+  const int64_t row = g / L, i = g % L;
+  const int64_t b = row / a.n;
+  const uint64_t* Kr = K + row * L;
+  const uint64_t k = Kr[i];
+  keys_out[g] = k;
+  if (k == 0xFFFFFFFFFFFFFFFFull || (i > 0 && Kr[i - 1] == k)) return;
+  const int64_t last = upper_u64(Kr, i, L, k) - 1;
+  const uint32_t* Pr = P + row * L;
+  NgcSummary r;
+  r.b_first = a.Bt[b * a.Lf + Pr[i]];
+  r.b_last = a.Bt[b * a.Lf + Pr[last]];
+  r.lam = lp[row * L + last].x;
+  r.prod = lp[row * L + last].y;
+  r.alfa = expf(a.log_alfa[b * a.Lf + Pr[last]]);
+  r.pad = 0.f;
+  summ[g] = r;
+}
+
+// per group-first slot of this chunk: (c, seen) from the earlier chunks' summaries, in rank order
+__global__ void k_ngc_resolve(RepetitionArgs a, int n_prev, const uint64_t* keys_prev, const NgcSummary* summ_prev,
+                              const uint64_t* K, const uint32_t* P, float2* carry) {
+  const int64_t L = a.L;
+  const int64_t rows = a.B * a.n;
+  const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (g >= rows * L) return;
+  const int64_t row = g / L, i = g % L;
+  const int64_t b = row / a.n;
+  const int ni = (int)(row % a.n);
+  const uint64_t* Kr = K + row * L;
+  const uint64_t k = Kr[i];
+  if (k == 0xFFFFFFFFFFFFFFFFull || (i > 0 && Kr[i - 1] == k)) return;
+  const float kappa = a.kappa[ni];
+  bool seen = false;
+  float lam = 0.f, alfa = 0.f;
+  double bt = 0.0;
+  for (int q = 0; q < n_prev; ++q) {
+    const uint64_t* Kq = keys_prev + ((int64_t)q * rows + row) * L;
+    const int64_t j = lower_u64(Kq, 0, L, k);
+    if (j >= L || Kq[j] != k) continue;
+    const NgcSummary r = summ_prev[((int64_t)q * rows + row) * L + j];
+    if (seen) {
+      const float a1 = expf(__fmul_rn(-kappa, __double2float_rn(fmax(r.b_first - bt, 0.0))));
+      const float c = __fadd_rn(__fmul_rn(a1, lam), __fmul_rn(a1, alfa));
+      lam = __fadd_rn(r.lam, __fmul_rn(r.prod, c));
+    } else {
+      lam = r.lam;
+    }
+    alfa = r.alfa;
+    bt = r.b_last;
+    seen = true;
+  }
+  float c = 0.f;
+  if (seen) {
+    const double b_first = a.Bt[b * a.Lf + P[row * L + i]];
+    const float a1 = expf(__fmul_rn(-kappa, __double2float_rn(fmax(b_first - bt, 0.0))));
+    c = __fadd_rn(__fmul_rn(a1, lam), __fmul_rn(a1, alfa));
+  }
+  carry[g] = make_float2(c, seen ? 1.f : 0.f);
+}
+
+// vistos / hawkes of every slot, scattered to the chunk's text order (B, Lc, n)
+__global__ void k_ngc_final(RepetitionArgs a, const uint64_t* K, const uint32_t* P, const float2* lp,
+                            const float2* carry) {
+  const int64_t L = a.L;
+  const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (g >= a.B * a.n * L) return;
+  const int64_t row = g / L, i = g % L;
+  const int64_t b = row / a.n;
+  const int ni = (int)(row % a.n);
+  const uint64_t* Kr = K + row * L;
+  const uint64_t k = Kr[i];
+  const int64_t t = (int64_t)P[g] - a.pos0;
+  const float2 v = lp[g];
+  float h = v.x;
+  uint8_t vis = 0;
+  if (k != 0xFFFFFFFFFFFFFFFFull) {
+    const bool first = i == 0 || Kr[i - 1] != k;
+    const int64_t f = first ? i : lower_u64(Kr, 0, i, k);
+    const float2 cs = carry[row * L + f];
+    h = __fadd_rn(v.x, __fmul_rn(v.y, cs.x));
+    vis = first ? (cs.y != 0.f ? 1 : 0) : 1;
+  }
+  a.hawkes[(b * L + t) * a.n + ni] = h;
+  a.vistos[(b * L + t) * a.n + ni] = vis;
+}
+
+int launch_ngram_chunk_sort(const RepetitionArgs& a, uint64_t* keys, void* summary, void* ws, size_t ws_bytes,
+                            cudaStream_t s) {
+  if (a.B == 0 || a.L == 0) return ASRN_OK;
+  if (a.n < 1 || a.n > kMaxSeen || a.pos0 + a.L > a.Lf || a.Lf >= ((int64_t)1 << 31)) return ASRN_ERR_ARG;
+  if (!ws || ws_bytes < ngram_chunk_workspace(a.B, a.L, a.n)) return ASRN_ERR_WORKSPACE;
+  const int64_t rows = a.B * a.n, L = a.L;
+  const int64_t tiles = (L + kRepTile - 1) / kRepTile;
+  NgcLayout r = ngc_layout(ws, rows, L);
+  const size_t smem = (size_t)kRepTile * 12;
+  cudaFuncSetAttribute(k_ngram_tile_sort, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  RepetitionArgs ak = a;
+  ak.keys = nullptr;
+  k_ngram_tile_sort<<<(unsigned)(rows * tiles), 1024, smem, s>>>(ak, tiles, r.k0, r.p0);
+  uint64_t *kin = r.k0, *kout = r.k1;
+  uint32_t *pin = r.p0, *pout = r.p1;
+  const int64_t per_row = (L + kMergeItems - 1) / kMergeItems;
+  for (int64_t w = kRepTile; w < L; w <<= 1) {
+    k_ngram_merge<<<(unsigned)((rows * per_row + 255) / 256), 256, 0, s>>>(kin, pin, kout, pout, rows, L, w);
+    uint64_t* tk = kin; kin = kout; kout = tk;
+    uint32_t* tp = pin; pin = pout; pout = tp;
+  }
+  k_ngc_scan_tile<<<(unsigned)(rows * tiles), 1024, 0, s>>>(a, tiles, kin, pin, r.vloc, r.agg);
+  k_ngc_apply<<<(unsigned)(rows * tiles), 1024, 0, s>>>(a, tiles, r.vloc, r.agg, r.lp, pin, r.pos);
+  const unsigned gb = (unsigned)((rows * L + 255) / 256);
+  k_ngc_summary<<<gb, 256, 0, s>>>(a, kin, r.pos, r.lp, keys, reinterpret_cast<NgcSummary*>(summary));
+  return cudaGetLastError() == cudaSuccess ? ASRN_OK : ASRN_ERR_CUDA;
+}
+
+int launch_ngram_chunk_finish(const RepetitionArgs& a, int n_prev, const uint64_t* keys_prev, const void* summary_prev,
+                              const uint64_t* keys, void* ws, size_t ws_bytes, cudaStream_t s) {
+  if (a.B == 0 || a.L == 0) return ASRN_OK;
+  if (a.n < 1 || a.n > kMaxSeen || n_prev < 0 || a.pos0 + a.L > a.Lf) return ASRN_ERR_ARG;
+  if (!ws || ws_bytes < ngram_chunk_workspace(a.B, a.L, a.n)) return ASRN_ERR_WORKSPACE;
+  const int64_t rows = a.B * a.n, L = a.L;
+  NgcLayout r = ngc_layout(ws, rows, L);
+  const unsigned gb = (unsigned)((rows * L + 255) / 256);
+  k_ngc_resolve<<<gb, 256, 0, s>>>(a, n_prev, keys_prev, reinterpret_cast<const NgcSummary*>(summary_prev), keys,
+                                   r.pos, r.carry);
+  k_ngc_final<<<gb, 256, 0, s>>>(a, keys, r.pos, r.lp, r.carry);
+  return cudaGetLastError() == cudaSuccess ? ASRN_OK : ASRN_ERR_CUDA;
+}
+
+int launch_racha(const RepetitionArgs& a, cudaStream_t s) {
+  if (a.B == 0) return ASRN_OK;
+  k_racha<<<(unsigned)a.B, 1024, 0, s>>>(a);
   return cudaGetLastError() == cudaSuccess ? ASRN_OK : ASRN_ERR_CUDA;
 }
 

@@ -105,9 +105,9 @@ def _apply_clock_offsets(Bt_full, chunk_sums, Lc):
     return Bt_full
 
 
-def _phase2(layer, loc, full, tails_prev, h, c0, c1, half):
-    """Scoring, n-gram memory and gate of the chunk [c0, c1) from the gathered full-sequence features and the
-    earlier ranks' bucket tails."""
+def _phase2(layer, loc, full, tails_prev, rep, h, c0, c1, half):
+    """Scoring and gate of the chunk [c0, c1) from the gathered full-sequence features, the earlier ranks' bucket
+    tails and the chunk's n-gram memory rep = (vistos, hawkes, racha)."""
     B, L = full['sig'].shape
     T = layer.n_tablas
     dev = h.device
@@ -128,11 +128,70 @@ def _phase2(layer, loc, full, tails_prev, h, c0, c1, half):
                                     _lib.ptr(full['Kc']), _lib.ptr(full['sig']), _lib.ptr(full['Bt']),
                                     _lib.ptr(full['log_alfa']), _lib.ptr(full['Ea']), _lib.ptr(row_len),
                                     _lib.ptr(acc), _lib.ptr(hay), _lib.ptr(mx), _lib.ptr(pk), s), 'asrn_score_shard')
-    rep = stages.repetition(layer, full['sig'], full['beta'], full['Bt'], full['log_alfa'])
-    vistos = rep['vistos'][:, c0:c1].contiguous()
-    hawkes = rep['hawkes'][:, c0:c1].contiguous()
-    racha = rep['racha'][:, c0:c1].contiguous()
+    vistos, hawkes, racha = rep
     return stages.gate(layer, h, loc['glogit'], acc, hay, mx, pk, vistos, hawkes, racha, half=half)
+
+
+# ---- n-gram memory of a chunk, carried across the shards ------------------------------------------------------------
+
+def ngram_sort(layer, full, c0, Lc, half):
+    """Sort and local scans of the chunk's n-gram keys (asrn_ngram_chunk_sort): the published part (sorted keys and
+    per-group summaries, each (B * n, Lc)) and the workspace the finish step continues from."""
+    B, L = full['sig'].shape
+    n = layer.vistos
+    dev = full['sig'].device
+    w, _keep, prep = layer.prepared(dev, half)
+    cfg = _lib.make_config(layer, B, Lc, half)
+    lib = _lib.lib()
+    ws = torch.empty(max(1, lib.asrn_ngram_chunk_workspace_bytes(ctypes_ref(cfg))), dtype=torch.uint8, device=dev)
+    keys = torch.empty(B * n, Lc, dtype=torch.int64, device=dev)
+    summ = torch.empty(B * n, Lc, 32, dtype=torch.uint8, device=dev)
+    _lib.check(lib.asrn_ngram_chunk_sort(ctypes_ref(cfg), ctypes_ref(w), _lib.ptr(prep), L, c0, _lib.ptr(full['sig']),
+                                         _lib.ptr(full['Bt']), _lib.ptr(full['log_alfa']), _lib.ptr(keys),
+                                         _lib.ptr(summ), _lib.ptr(ws), ws.numel(), _lib.stream_ptr(dev)),
+               'asrn_ngram_chunk_sort')
+    return dict(keys=keys, summ=summ, ws=ws)
+
+
+def ngram_finish(layer, full, ng, keys_prev, summ_prev, c0, Lc, half):
+    """vistos (B, Lc, n) and hawkes (B, Lc, n) of the chunk from its sort state and the earlier shards' published
+    keys / summaries ((n_prev, B * n, Lc), rank order; None for the first shard)."""
+    B, L = full['sig'].shape
+    n = layer.vistos
+    dev = full['sig'].device
+    w, _keep, prep = layer.prepared(dev, half)
+    cfg = _lib.make_config(layer, B, Lc, half)
+    vistos = torch.empty(B, Lc, n, dtype=torch.uint8, device=dev)
+    hawkes = torch.empty(B, Lc, n, dtype=torch.float32, device=dev)
+    n_prev = 0 if keys_prev is None else keys_prev.shape[0]
+    _lib.check(_lib.lib().asrn_ngram_chunk_finish(
+        ctypes_ref(cfg), ctypes_ref(w), _lib.ptr(prep), L, c0, n_prev, None if n_prev == 0 else _lib.ptr(keys_prev),
+        None if n_prev == 0 else _lib.ptr(summ_prev), _lib.ptr(ng['keys']), _lib.ptr(full['Bt']),
+        _lib.ptr(full['log_alfa']), _lib.ptr(vistos), _lib.ptr(hawkes), _lib.ptr(ng['ws']), ng['ws'].numel(),
+        _lib.stream_ptr(dev)), 'asrn_ngram_chunk_finish')
+    return vistos, hawkes
+
+
+def racha_chunk(layer, vistos, beta, racha_in, half, want_racha=True):
+    """Streak of a chunk from the value before it (racha_in (B,), None = 0): (racha (B, Lc) or None, map (B, 2))."""
+    B, Lc, _ = vistos.shape
+    dev = vistos.device
+    w, _keep, prep = layer.prepared(dev, half)
+    cfg = _lib.make_config(layer, B, Lc, half)
+    racha = torch.empty(B, Lc, dtype=torch.float32, device=dev) if want_racha else None
+    rmap = torch.empty(B, 2, dtype=torch.float32, device=dev)
+    _lib.check(_lib.lib().asrn_racha_chunk(ctypes_ref(cfg), ctypes_ref(w), _lib.ptr(prep), _lib.ptr(vistos),
+                                           _lib.ptr(beta), _lib.ptr(racha_in), _lib.ptr(racha), _lib.ptr(rmap),
+                                           _lib.stream_ptr(dev)), 'asrn_racha_chunk')
+    return racha, rmap
+
+
+def racha_before(maps, rank):
+    """maps (world, B, 2) of every chunk -> (B,) streak value before chunk `rank` (0 for the first)."""
+    S = torch.zeros(maps.shape[1], dtype=torch.float32, device=maps.device)
+    for q in range(rank):
+        S = maps[q, :, 0] * S + maps[q, :, 1]
+    return S
 
 
 def _check(layer, E, h, tokens):
@@ -162,8 +221,20 @@ def forward_emulated(layer, E, h, tokens, world):
     tails = torch.stack([lc['tails'] for lc in locs], 0)
     sums = torch.stack([lc['Bt'][:, -1] for lc in locs], 0)
     _apply_clock_offsets(full['Bt'], sums, L // world)
-    outs = [_phase2(layer, lc, full, tails[:r] if r > 0 else None, h[:, c0:c1].contiguous(), c0, c1, half)
-            for r, (lc, (c0, c1)) in enumerate(zip(locs, bounds))]
+    Lc = L // world
+    ngs = [ngram_sort(layer, full, c0, Lc, half) for c0, _ in bounds]
+    keys = torch.stack([g['keys'] for g in ngs], 0)
+    summ = torch.stack([g['summ'] for g in ngs], 0)
+    vh = [ngram_finish(layer, full, ngs[r], keys[:r] if r > 0 else None, summ[:r] if r > 0 else None, c0, Lc, half)
+          for r, (c0, _) in enumerate(bounds)]
+    maps = torch.stack([racha_chunk(layer, v, lc['beta'], None, half, want_racha=False)[1]
+                        for (v, _), lc in zip(vh, locs)], 0)
+    outs = []
+    for r, (lc, (c0, c1)) in enumerate(zip(locs, bounds)):
+        vistos, hawkes = vh[r]
+        racha, _ = racha_chunk(layer, vistos, lc['beta'], racha_before(maps, r), half)
+        outs.append(_phase2(layer, lc, full, tails[:r] if r > 0 else None, (vistos, hawkes, racha),
+                            h[:, c0:c1].contiguous(), c0, c1, half))
     return torch.cat(outs, 1)
 
 
@@ -206,6 +277,26 @@ def exchange_tails(tails, world, group=None):
     return flat
 
 
+def exchange_ngram(keys, summ, world, group=None):
+    """This chunk's sorted n-gram keys (B * n, Lc) int64 and summaries (B * n, Lc, 32) uint8 -> both with a leading
+    rank dimension (world, ...), in rank order."""
+    import torch.distributed as dist
+    out = []
+    for x in (keys, summ):
+        flat = torch.empty((world,) + tuple(x.shape), dtype=x.dtype, device=x.device)
+        dist.all_gather_into_tensor(flat.view(-1), x.contiguous().view(-1), group=group)
+        out.append(flat)
+    return out[0], out[1]
+
+
+def exchange_racha_maps(rmap, world, group=None):
+    """(B, 2) streak map of this chunk -> (world, B, 2)."""
+    import torch.distributed as dist
+    flat = torch.empty((world,) + tuple(rmap.shape), dtype=rmap.dtype, device=rmap.device)
+    dist.all_gather_into_tensor(flat.view(-1), rmap.contiguous().view(-1), group=group)
+    return flat
+
+
 @torch.no_grad()
 def forward(layer, E, h, tokens=None, group=None):
     """One rank of the sharded forward under torch.distributed: E, h (B, Lc, d), tokens (B, Lc) are this rank's chunk
@@ -231,4 +322,12 @@ def forward(layer, E, h, tokens=None, group=None):
     tails = exchange_tails(loc['tails'], world, group)
     full = {k: _gather_seq(loc[k], world, group) for k in _SEQ_KEYS}
     _apply_clock_offsets(full['Bt'], sums, Lc)
-    return _phase2(layer, loc, full, tails[:rank] if rank > 0 else None, h, c0, c1, half)
+    # (5) n-gram memory: per-group summaries of every chunk, then the streak maps
+    ng = ngram_sort(layer, full, c0, Lc, half)
+    keys, summ = exchange_ngram(ng['keys'], ng['summ'], world, group)
+    vistos, hawkes = ngram_finish(layer, full, ng, keys[:rank] if rank > 0 else None,
+                                  summ[:rank] if rank > 0 else None, c0, Lc, half)
+    _, rmap = racha_chunk(layer, vistos, loc['beta'], None, half, want_racha=False)
+    maps = exchange_racha_maps(rmap, world, group)
+    racha, _ = racha_chunk(layer, vistos, loc['beta'], racha_before(maps, rank), half)
+    return _phase2(layer, loc, full, tails[:rank] if rank > 0 else None, (vistos, hawkes, racha), h, c0, c1, half)

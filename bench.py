@@ -20,6 +20,7 @@ prefill rate, and the public generate() API end to end.
 --impl reference: times the CPU implementation of the path (oracle port) on the host cores instead.
 """
 import argparse
+import datetime
 import json
 import math
 import os
@@ -110,14 +111,17 @@ def make_inputs(batch, seq, rank, seed=0):
 # ---------------------------------------------------------------------------------------------------------------------
 
 class ClockSampler:
-    FIELDS = ('index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,'
-              'clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,'
-              'clocks_event_reasons.sw_power_cap')
+    """nvidia-smi clock / throttle-reason samples every 100 ms. Started before the warm-up (nvidia-smi's own start-up
+    then happens outside the timed region); mark() brackets the timed region, and only samples inside it count."""
+    FIELDS = ('timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,'
+              'clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,'
+              'clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap')
 
     def __init__(self, gpu_index):
         self.idx = gpu_index
         self.proc = None
         self.f = None
+        self.window = None
 
     def start(self):
         try:
@@ -127,10 +131,20 @@ class ClockSampler:
                                          stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None
+            return
+        # wait (up to 10 s) for the first sample: nvidia-smi is up before the GPU work that is measured
+        t_end = time.time() + 10
+        while time.time() < t_end and os.path.getsize(self.f.name) == 0 and self.proc.poll() is None:
+            time.sleep(0.05)
+
+    def mark(self, t0, t1):
+        """The timed region in host wall-clock seconds (time.time())."""
+        self.window = (t0, t1)
 
     def stop(self):
         if self.proc is None:
             return {'sm_mhz': None, 'sm_max_mhz': None, 'reasons': ['nvidia-smi unavailable']}
+        time.sleep(0.15)                      # one more sample after the timed region
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
@@ -140,13 +154,25 @@ class ClockSampler:
         self.f.seek(0)
         rows = [r.split(',') for r in self.f.read().strip().splitlines() if r.strip()]
         os.unlink(self.f.name)
-        sm, mx, reasons = [], [], set()
-        names = ('hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap')
+        parsed = []
         for r in rows:
             try:
-                sm.append(float(r[1]))
-                mx.append(float(r[2]))
-                for nm, v in zip(names, r[5:9]):
+                ts = datetime.datetime.strptime(r[0].strip(), '%Y/%m/%d %H:%M:%S.%f').timestamp()
+                parsed.append((ts, r))
+            except (ValueError, IndexError):
+                continue
+        inside = parsed
+        if self.window is not None:
+            lo, hi = self.window
+            sel = [(ts, r) for ts, r in parsed if lo - 0.1 <= ts <= hi + 0.1]
+            inside = sel if sel else parsed
+        sm, mx, reasons = [], [], set()
+        names = ('hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap')
+        for _, r in inside:
+            try:
+                sm.append(float(r[2]))
+                mx.append(float(r[3]))
+                for nm, v in zip(names, r[6:10]):
                     if v.strip().lower() in ('active', '1'):
                         reasons.add(nm)
             except (ValueError, IndexError):
@@ -351,21 +377,21 @@ def run_ours(args):
         with torch.no_grad(), torch.autocast('cuda', dtype=torch.bfloat16):
             return layer(E, h, x)
 
+    clocks = ClockSampler(local)
+    clocks.start()
     for _ in range(max(3, args.warmup)):
         step()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    clocks = ClockSampler(local)
-    clocks.start()
-    time.sleep(0.3)
-    torch.cuda.synchronize()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    w0 = time.time()
     t0.record()
     for _ in range(args.steps):
         y = step()
     t1.record()
     torch.cuda.synchronize()
+    clocks.mark(w0, time.time())
     ms = t0.elapsed_time(t1)
     if world > 1:
         dist.barrier()
@@ -531,21 +557,21 @@ def run_cfg4(args):
                 return layer(Ed, hd, xd)
             return shard.forward(layer, Ed, hd, xd)
 
+    clocks = ClockSampler(local)
+    clocks.start()
     for _ in range(max(3, args.warmup)):
         step()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    clocks = ClockSampler(local)
-    clocks.start()
-    time.sleep(0.3)
-    torch.cuda.synchronize()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    w0 = time.time()
     t0.record()
     for _ in range(args.steps):
         y = step()
     t1.record()
     torch.cuda.synchronize()
+    clocks.mark(w0, time.time())
     ms = t0.elapsed_time(t1)
     if world > 1:
         dist.barrier()

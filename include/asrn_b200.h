@@ -201,6 +201,30 @@ int asrn_score_shard(const asrn_layer_config* cfg, const asrn_layer_weights* w, 
                      const void* Ea, const int64_t* row_len, float* acc, uint8_t* sen_hay, float* sen_mx,
                      float* sen_pk, void* stream);
 
+/* n-gram memory of one shard's chunk [c0, c0 + cfg->L) of sequences of L_feat positions (asrn/estable.py:304-321
+ * carried across chunks; the reference runs whole sequences). sig, Bt, log_alfa: the gathered (B, L_feat) rows.
+ * asrn_ngram_chunk_sort: sorts the chunk's (key, position) pairs per (b, order) row and scans them with the chunk
+ * alone; writes the sorted keys (B*n, Lc) uint64 (order-preserving images of the fp64 keys) and per group a 32-byte
+ * summary (B*n, Lc) at the group's first slot: {fp64 clock of its first and last occurrence, fp32 intensity and
+ * decay product at its last slot, fp32 alfa of its last occurrence}. Every shard publishes both (all-gather).
+ * asrn_ngram_chunk_finish: with the n_prev = r earlier shards' keys and summaries ((n_prev, B*n, Lc), rank order)
+ * and the state the sort left in the workspace (same workspace), vistos (B, Lc, n) uint8 and hawkes (B, Lc, n)
+ * float32 of the chunk, equal to the whole-sequence values at its positions.
+ * asrn_racha_chunk: the streak of a chunk (cfg->L positions, vistos / beta of the chunk) from the value before it
+ * (racha_in (B), NULL = 0) into racha (B, Lc) (may be NULL); racha_map (B, 2) (may be NULL) receives the chunk's map
+ * S_last = A * S_before + B0 as (A, B0), from which the next shards' racha_in follow. */
+size_t asrn_ngram_chunk_workspace_bytes(const asrn_layer_config* cfg);
+int asrn_ngram_chunk_sort(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared,
+                          int64_t L_feat, int64_t c0, const float* sig, const double* Bt, const float* log_alfa,
+                          uint64_t* keys, void* summary, void* workspace, size_t workspace_bytes, void* stream);
+int asrn_ngram_chunk_finish(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared,
+                            int64_t L_feat, int64_t c0, int32_t n_prev, const uint64_t* keys_prev,
+                            const void* summary_prev, const uint64_t* keys, const double* Bt, const float* log_alfa,
+                            uint8_t* vistos, float* hawkes, void* workspace, size_t workspace_bytes, void* stream);
+int asrn_racha_chunk(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared,
+                     const uint8_t* vistos, const double* beta, const float* racha_in, float* racha, float* racha_map,
+                     void* stream);
+
 /* The same bucket sort for callers that cannot allocate device memory when they sort (a plug-in inside a host process
  * whose allocator it does not own, a serving loop that keeps a fixed memory footprint after start-up): no workspace
  * argument; rows longer than one tile (8192 positions) use a fixed 32 MiB scratch array inside this library, which

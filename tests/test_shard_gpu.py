@@ -103,6 +103,50 @@ def test_rows_from_tails_equal_rows_from_the_full_sort(world, nb, C, cuda):
         assert torch.equal(ov, ov_ref) and torch.equal(iv, iv_ref)
 
 
+@pytest.mark.parametrize('world,B,L', [(2, 2, 6000), (3, 1, 9000), (4, 2, 8192), (2, 1, 40000)])
+def test_chunk_ngram_memory_equals_whole_rows(world, B, L, cuda):
+    """The n-gram memory computed per chunk (local sort and scans, per-group summaries exchanged, carries folded in
+    rank order; the streak carried as an affine map) equals the whole-row computation at every position: seen flags
+    bit-exact, Hawkes intensity and streak within 1e-5. Repetitive text (12 symbols, a copied stretch) so that groups
+    span chunks; the last case has chunks longer than one sort tile."""
+    import asrn_b200
+    from asrn_b200 import shard, stages
+    torch.manual_seed(3)
+    layer = asrn_b200.ASRNLayer(32)
+    g = torch.Generator().manual_seed(4)
+    with torch.no_grad():
+        for n_, p_ in layer.named_parameters():
+            if n_ in ('log_kappa', 'log_kappa_racha'):
+                p_.add_(torch.randn(p_.shape, generator=g) * 0.5)
+    layer = layer.to(cuda)
+    rng = np.random.default_rng(world * 7 + L)
+    tok = rng.integers(0, 12, size=(B, L))
+    tok[:, L // 2:L // 2 + L // 8] = tok[:, 100:100 + L // 8]
+    sig = torch.from_numpy(tok.astype(np.float32)).to(cuda)
+    beta = torch.from_numpy(rng.uniform(0.01, 2.0, size=(B, L))).to(cuda)
+    Bt = torch.cumsum(beta, 1)
+    la = torch.from_numpy(rng.uniform(-3.0, 0.5, size=(B, L)).astype(np.float32)).to(cuda)
+    ref = stages.repetition(layer, sig, beta, Bt, la)
+    full = dict(sig=sig, Bt=Bt, log_alfa=la)
+    Lc = L // world
+    ngs = [shard.ngram_sort(layer, full, r * Lc, Lc, False) for r in range(world)]
+    keys = torch.stack([x['keys'] for x in ngs], 0)
+    summ = torch.stack([x['summ'] for x in ngs], 0)
+    vh = [shard.ngram_finish(layer, full, ngs[r], keys[:r] if r else None, summ[:r] if r else None, r * Lc, Lc,
+                             False) for r in range(world)]
+    betas = [beta[:, r * Lc:(r + 1) * Lc].contiguous() for r in range(world)]
+    maps = torch.stack([shard.racha_chunk(layer, vh[r][0], betas[r], None, False, want_racha=False)[1]
+                        for r in range(world)], 0)
+    vis = torch.cat([v for v, _ in vh], 1)
+    haw = torch.cat([h for _, h in vh], 1)
+    racha = torch.cat([shard.racha_chunk(layer, vh[r][0], betas[r], shard.racha_before(maps, r), False)[0]
+                       for r in range(world)], 1)
+    torch.cuda.synchronize()
+    assert torch.equal(vis, ref['vistos'])
+    assert rel_err(haw.cpu().numpy(), ref['hawkes'].cpu().numpy()) <= 1e-5
+    assert rel_err(racha.cpu().numpy(), ref['racha'].cpu().numpy()) <= 1e-5
+
+
 def _layer_and_inputs(cuda, d, B, L, nb, seed=0):
     import asrn_b200
     torch.manual_seed(seed)

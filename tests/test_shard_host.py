@@ -15,6 +15,28 @@ def test_chunk_bounds():
         shard.chunk_bounds(10, 3, 0)
 
 
+def test_streak_before_each_chunk_composes_the_earlier_maps():
+    """racha_before folds the earlier chunks' affine maps S_last = A S_before + B in rank order: equal to running the
+    streak recursion S_t = a_t S_{t-1} + r_t over the whole row."""
+    from asrn_b200 import shard
+    rng = np.random.default_rng(1)
+    world, Lc = 4, 6
+    a = rng.uniform(0.0, 1.0, (world * Lc,))
+    r = rng.integers(0, 2, (world * Lc,)).astype(np.float64)
+    S, before = 0.0, []
+    maps = []
+    for q in range(world):
+        before.append(S)
+        A, B0 = 1.0, 0.0
+        for t in range(q * Lc, (q + 1) * Lc):
+            S = a[t] * S + r[t]
+            A, B0 = a[t] * A, a[t] * B0 + r[t]
+        maps.append([A, B0])
+    m = torch.tensor(maps, dtype=torch.float32).view(world, 1, 2)
+    for q in range(world):
+        assert abs(shard.racha_before(m, q).item() - before[q]) <= 1e-5 * max(1.0, abs(before[q]))
+
+
 def test_clock_offsets_give_the_global_cumulative_sum():
     from asrn_b200 import shard
     rng = np.random.default_rng(0)
@@ -47,6 +69,10 @@ def _rank(rank, world, port, out):
         res['seq2'] = shard._gather_seq(torch.arange(8).view(2, 4) + 100 * rank, world, None)
         tails = (torch.arange(2 * 4 * 3).view(2, 4, 3) + 1000 * rank).to(torch.int32)
         res['tails'] = shard.exchange_tails(tails, world, None)
+        keys = (torch.arange(6).view(2, 3) + 10 * rank).to(torch.int64)
+        summ = torch.full((2, 3, 32), rank + 1, dtype=torch.uint8)
+        res['ng'] = shard.exchange_ngram(keys, summ, world, None)
+        res['maps'] = shard.exchange_racha_maps(torch.tensor([[0.5, 1.0 + rank]]), world, None)
         torch.save(res, os.path.join(out, f'rank{rank}.pt'))
     finally:
         dist.destroy_process_group()
@@ -66,3 +92,7 @@ def test_exchange_steps_with_two_gloo_ranks(tmp_path):
         assert torch.equal(r['seq2'], expect2)
         t0 = torch.arange(2 * 4 * 3).view(2, 4, 3).to(torch.int32)
         assert torch.equal(r['tails'], torch.stack([t0, t0 + 1000], 0))
+        k0 = torch.arange(6).view(2, 3).to(torch.int64)
+        assert torch.equal(r['ng'][0], torch.stack([k0, k0 + 10], 0))
+        assert (r['ng'][1][0] == 1).all() and (r['ng'][1][1] == 2).all()
+        assert torch.equal(r['maps'], torch.tensor([[[0.5, 1.0]], [[0.5, 2.0]]]))
