@@ -91,7 +91,8 @@ _SIGS = {
                               [ctypes.c_size_t, _P]),
     'asrn_ngram_chunk_finish': (ctypes.c_int, [_P, _P, _P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int32] +
                                 [_P] * 8 + [ctypes.c_size_t, _P]),
-    'asrn_racha_chunk': (ctypes.c_int, [_P] * 9),
+    'asrn_racha_workspace_bytes': (ctypes.c_size_t, [_P]),
+    'asrn_racha_chunk': (ctypes.c_int, [_P] * 8 + [_P, ctypes.c_size_t, _P]),
     'asrn_shard_workspace_bytes': (ctypes.c_size_t, [ctypes.c_int64, ctypes.c_int32]),
     'asrn_shard_tails': (ctypes.c_int, [ctypes.c_int64, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int64,
                                         _P, _P, _P, _P, ctypes.c_size_t, _P]),

@@ -446,9 +446,14 @@ int asrn_ngram_chunk_finish(const asrn_layer_config* cfg, const asrn_layer_weigh
                                    as_stream(stream));
 }
 
+size_t asrn_racha_workspace_bytes(const asrn_layer_config* cfg) {
+  if (check_config(cfg) != ASRN_OK) return 0;
+  return racha_workspace(cfg->B, cfg->L);
+}
+
 int asrn_racha_chunk(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared,
                      const uint8_t* vistos, const double* beta, const float* racha_in, float* racha, float* racha_map,
-                     void* stream) {
+                     void* workspace, size_t workspace_bytes, void* stream) {
   int st = check_config(cfg);
   if (st) return st;
   if ((st = check_weights(w))) return st;
@@ -456,7 +461,7 @@ int asrn_racha_chunk(const asrn_layer_config* cfg, const asrn_layer_weights* w, 
   RepetitionArgs a = repetition_args(*cfg, *w, reinterpret_cast<const char*>(prepared));
   a.vistos = const_cast<uint8_t*>(vistos); a.beta = beta; a.racha = racha;
   a.racha_in = racha_in; a.racha_map = racha_map;
-  return launch_racha(a, as_stream(stream));
+  return launch_racha_ws(a, workspace, workspace_bytes, as_stream(stream));
 }
 
 size_t asrn_gate_workspace_bytes(const asrn_layer_config* cfg) {

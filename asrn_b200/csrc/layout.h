@@ -214,6 +214,8 @@ int launch_ngram_chunk_sort(const RepetitionArgs& a, uint64_t* keys, void* summa
 int launch_ngram_chunk_finish(const RepetitionArgs& a, int n_prev, const uint64_t* keys_prev, const void* summary_prev,
                               const uint64_t* keys, void* ws, size_t ws_bytes, cudaStream_t s);
 int launch_racha(const RepetitionArgs& a, cudaStream_t s);
+size_t racha_workspace(int64_t B, int64_t L);
+int launch_racha_ws(const RepetitionArgs& a, void* ws, size_t ws_bytes, cudaStream_t s);
 int launch_gen_front(const GenFrontArgs& a, bool half, cudaStream_t s);
 int launch_gen_gate(const GateArgs& a, bool half, cudaStream_t s);
 size_t hawkes_table_bytes(int64_t B, int n, int64_t cap);
@@ -244,6 +246,8 @@ int launch_gate(const GateArgs& a, bool half, cudaStream_t s);
 size_t gate_workspace(int64_t M, int d, bool half);
 int launch_prepare(const asrn_layer_config& c, const asrn_layer_weights& w, void* prepared, cudaStream_t s);
 // 2-D bf16 TMA tensor map, 128-byte swizzle: rows of `inner` elements (row stride in bytes), box inner x outer.
+bool make_tmap_f32(void* map /* CUtensorMap */, const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes,
+                   uint32_t box_inner, uint32_t box_outer);
 bool make_tmap_rows_bf16(void* map /* CUtensorMap */, const void* base, uint64_t inner, uint64_t outer,
                          uint64_t row_bytes, uint32_t box_inner);
 bool make_tmap_bf16(void* map /* CUtensorMap */, const void* base, uint64_t inner, uint64_t outer,

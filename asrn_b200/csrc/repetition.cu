@@ -186,6 +186,67 @@ __global__ void __launch_bounds__(1024) k_racha(RepetitionArgs a) {
   }
 }
 
+// Streak over long rows of few sequences, in parallel over tiles of kRachaTile positions: each tile's local maps and
+// its aggregate, then each tile composes the aggregates before it (and racha_in) into its positions.
+constexpr int kRachaItems = 4;
+constexpr int kRachaTile = 1024 * kRachaItems;
+
+__global__ void __launch_bounds__(1024) k_racha_tile(RepetitionArgs a, int64_t tiles, float2* vloc, float2* agg) {
+  __shared__ Affine warp_agg[32];
+  const int64_t b = blockIdx.x / tiles, tile = blockIdx.x % tiles;
+  const int64_t L = a.L;
+  const float kr = a.kappa[a.n];
+  Affine v[kRachaItems];
+  const int64_t t0 = tile * kRachaTile + (int64_t)threadIdx.x * kRachaItems;
+#pragma unroll
+  for (int k = 0; k < kRachaItems; ++k) {
+    const int64_t t = t0 + k;
+    if (t < L) {
+      const float r = (float)a.vistos[(b * L + t) * a.n + (a.n - 1)];
+      const float e = expf(__fmul_rn(-kr, (float)a.beta[b * L + t]));
+      v[k] = Affine{__fmul_rn(r, e), r};
+    } else {
+      v[k] = Affine{1.f, 0.f};
+    }
+  }
+  block_scan_affine<kRachaItems>(v, warp_agg);
+#pragma unroll
+  for (int k = 0; k < kRachaItems; ++k) {
+    const int64_t t = t0 + k;
+    if (t < L) vloc[b * L + t] = make_float2(v[k].a, v[k].b);
+  }
+  if (threadIdx.x == blockDim.x - 1) agg[b * tiles + tile] = make_float2(v[kRachaItems - 1].a, v[kRachaItems - 1].b);
+}
+
+__global__ void __launch_bounds__(1024) k_racha_apply(RepetitionArgs a, int64_t tiles, const float2* vloc,
+                                                      const float2* agg) {
+  __shared__ Affine carry_s;
+  const int64_t b = blockIdx.x / tiles, tile = blockIdx.x % tiles;
+  const int64_t L = a.L;
+  if (threadIdx.x == 0) {
+    Affine c = a.racha_in ? Affine{0.f, a.racha_in[b]} : Affine{1.f, 0.f};
+    for (int64_t q = 0; q < tile; ++q) {
+      const float2 g = agg[b * tiles + q];
+      c = compose(c, Affine{g.x, g.y});
+    }
+    carry_s = c;
+  }
+  __syncthreads();
+  const Affine c = carry_s;
+  const int64_t end = (tile + 1) * kRachaTile < L ? (tile + 1) * kRachaTile : L;
+  for (int64_t t = tile * kRachaTile + threadIdx.x; t < end; t += blockDim.x) {
+    const float2 lv = vloc[b * L + t];
+    const Affine s = compose(c, Affine{lv.x, lv.y});
+    if (a.racha) a.racha[b * L + t] = s.b;
+  }
+  if (a.racha_map && tile == tiles - 1 && threadIdx.x == 0) {
+    const float2 lv = vloc[b * L + L - 1];
+    const Affine s = compose(c, Affine{lv.x, lv.y});
+    a.racha_map[2 * b] = s.a;
+    a.racha_map[2 * b + 1] = s.b;
+  }
+}
+
 // ---- rows longer than kRepMaxL ---------------------------------------------------------------------------------------
 
 constexpr int kRepTile = kRepMaxL;
@@ -681,11 +742,28 @@ int launch_ngram_chunk_finish(const RepetitionArgs& a, int n_prev, const uint64_
   return cudaGetLastError() == cudaSuccess ? ASRN_OK : ASRN_ERR_CUDA;
 }
 
-int launch_racha(const RepetitionArgs& a, cudaStream_t s) {
-  if (a.B == 0) return ASRN_OK;
-  k_racha<<<(unsigned)a.B, 1024, 0, s>>>(a);
+size_t racha_workspace(int64_t B, int64_t L) {
+  const int64_t tiles = (L + kRachaTile - 1) / kRachaTile;
+  return align_up((size_t)B * L * 8) + align_up((size_t)B * tiles * 8);
+}
+
+// Streak of rows of L positions: one block per row, or (rows that are few and long, and a workspace given) the tiled
+// scan over all SMs.
+int launch_racha_ws(const RepetitionArgs& a, void* ws, size_t ws_bytes, cudaStream_t s) {
+  if (a.B == 0 || a.L == 0) return ASRN_OK;
+  const int64_t tiles = (a.L + kRachaTile - 1) / kRachaTile;
+  if (ws && ws_bytes >= racha_workspace(a.B, a.L) && tiles >= 4 && a.B < 64) {
+    float2* vloc = reinterpret_cast<float2*>(ws);
+    float2* agg = reinterpret_cast<float2*>(reinterpret_cast<char*>(ws) + align_up((size_t)a.B * a.L * 8));
+    k_racha_tile<<<(unsigned)(a.B * tiles), 1024, 0, s>>>(a, tiles, vloc, agg);
+    k_racha_apply<<<(unsigned)(a.B * tiles), 1024, 0, s>>>(a, tiles, vloc, agg);
+  } else {
+    k_racha<<<(unsigned)a.B, 1024, 0, s>>>(a);
+  }
   return cudaGetLastError() == cudaSuccess ? ASRN_OK : ASRN_ERR_CUDA;
 }
+
+int launch_racha(const RepetitionArgs& a, cudaStream_t s) { return launch_racha_ws(a, nullptr, 0, s); }
 
 int launch_repetition(const RepetitionArgs& a, void* ws, size_t ws_bytes, cudaStream_t s) {
   if (a.B == 0 || a.L == 0) return ASRN_OK;
@@ -693,8 +771,7 @@ int launch_repetition(const RepetitionArgs& a, void* ws, size_t ws_bytes, cudaSt
   if (a.L > kRepMaxL) {
     const int st = launch_repetition_long(a, ws, ws_bytes, s);
     if (st) return st;
-    k_racha<<<(unsigned)a.B, 1024, 0, s>>>(a);
-    return cudaGetLastError() == cudaSuccess ? ASRN_OK : ASRN_ERR_CUDA;
+    return launch_racha_ws(a, ws, ws_bytes, s);   // the n-gram passes are done with the workspace
   }
   int n2 = 1;
   while (n2 < a.L) n2 <<= 1;

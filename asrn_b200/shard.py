@@ -180,9 +180,11 @@ def racha_chunk(layer, vistos, beta, racha_in, half, want_racha=True):
     cfg = _lib.make_config(layer, B, Lc, half)
     racha = torch.empty(B, Lc, dtype=torch.float32, device=dev) if want_racha else None
     rmap = torch.empty(B, 2, dtype=torch.float32, device=dev)
-    _lib.check(_lib.lib().asrn_racha_chunk(ctypes_ref(cfg), ctypes_ref(w), _lib.ptr(prep), _lib.ptr(vistos),
-                                           _lib.ptr(beta), _lib.ptr(racha_in), _lib.ptr(racha), _lib.ptr(rmap),
-                                           _lib.stream_ptr(dev)), 'asrn_racha_chunk')
+    lib = _lib.lib()
+    ws = torch.empty(max(1, lib.asrn_racha_workspace_bytes(ctypes_ref(cfg))), dtype=torch.uint8, device=dev)
+    _lib.check(lib.asrn_racha_chunk(ctypes_ref(cfg), ctypes_ref(w), _lib.ptr(prep), _lib.ptr(vistos),
+                                    _lib.ptr(beta), _lib.ptr(racha_in), _lib.ptr(racha), _lib.ptr(rmap),
+                                    _lib.ptr(ws), ws.numel(), _lib.stream_ptr(dev)), 'asrn_racha_chunk')
     return racha, rmap
 
 

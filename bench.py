@@ -12,7 +12,10 @@ over the GPU's batch. Batches shard across GPUs with no collective, so per-GPU w
 Printed (rank 0, one JSON line): value = tokens/s of the whole job (all ranks' tokens / max-over-ranks device time of
 K steps, inputs resident in HBM; the 805 MB E and h per GPU exceed the 126 MB L2, so no flush is needed), e2e = the
 same through ASRNLayer.forward with pinned host buffers and H2D/D2H copies in the timed region, roofline of the
-dominant kernel (candidate scoring, HBM-bound), the CPU baseline (the oracle port on the host cores), clocks.
+dominant kernel (candidate scoring, HBM-bound), the CPU baseline (the oracle port on the host cores), clocks (nvidia-smi
+samples inside the timed region; the sampler starts before the warm-up). Warm-up: at least W steps, then until two
+consecutive steps agree within 3 % (at most 20 more; "warmup" reports the count); "step_ms" gives the spread of the K
+timed steps (CUDA events between them).
 Generation leg (configuration 5, key "generation"): the configuration-3 model (random init), 64 sequences split over
 the GPUs with 65,536-token Zipf+repeat prompts, then greedy steps of the O(1) writer; value = device time per step
 (us per generated token of every sequence), with the same figure at 4,096 and 16,384-token prompts (flatness), the
@@ -179,6 +182,32 @@ class ClockSampler:
                 continue
         return {'sm_mhz': statistics.median(sm) if sm else None, 'sm_max_mhz': max(mx) if mx else None,
                 'reasons': sorted(reasons), 'samples': len(sm)}
+
+
+def warm_up(step, warmup, world):
+    """At least max(3, warmup) untimed steps; then, up to 20 more, until two consecutive steps agree within 3 % (the
+    first steps of a process run slower while allocations and the GPU's clocks settle). All ranks take the same number
+    of steps (the slowest rank's count decides). Returns the number of warm-up steps taken."""
+    import torch
+    n = 0
+    times = []
+    while True:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        step()
+        e1.record()
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1))
+        n += 1
+        settled = n >= max(3, warmup) and (n >= max(3, warmup) + 20 or
+                                           abs(times[-1] - times[-2]) <= 0.03 * min(times[-1], times[-2]))
+        if world > 1:
+            import torch.distributed as dist
+            flag = torch.tensor([0 if settled else 1], device='cuda')
+            dist.all_reduce(flag)
+            settled = flag.item() == 0
+        if settled:
+            return n
 
 
 # ---------------------------------------------------------------------------------------------------------------------
@@ -379,20 +408,21 @@ def run_ours(args):
 
     clocks = ClockSampler(local)
     clocks.start()
-    for _ in range(max(3, args.warmup)):
-        step()
-    torch.cuda.synchronize()
+    warm = warm_up(step, args.warmup, world)
     if world > 1:
         dist.barrier()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    marks = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     w0 = time.time()
     t0.record()
-    for _ in range(args.steps):
+    for i in range(args.steps):
         y = step()
+        marks[i].record()
     t1.record()
     torch.cuda.synchronize()
     clocks.mark(w0, time.time())
     ms = t0.elapsed_time(t1)
+    step_ms = [t0.elapsed_time(marks[0])] + [marks[i - 1].elapsed_time(marks[i]) for i in range(1, args.steps)]
     if world > 1:
         dist.barrier()
     clk = clocks.stop()
@@ -473,7 +503,9 @@ def run_ours(args):
         traffic_pt = load_profile_traffic()
         value = world * tokens * args.steps / (ms * 1e-3)
         out = {'metric': METRIC, 'value': value, 'unit': UNIT, 'n_gpus': world, 'steps': args.steps,
-               'warmup': max(3, args.warmup), 'ms_per_step': ms / args.steps, 'higher_is_better': True,
+               'warmup': warm, 'ms_per_step': ms / args.steps,
+               'step_ms': {'min': min(step_ms), 'median': statistics.median(step_ms), 'max': max(step_ms)},
+               'higher_is_better': True,
                'scaling': 'weak', 'vs_baseline': None, 'dtype': 'bf16', 'data': 'synthetic',
                'config': config(args, world),
                'e2e': {'value': world * tokens / (e2e_ms * 1e-3), 'unit': UNIT,
@@ -559,20 +591,21 @@ def run_cfg4(args):
 
     clocks = ClockSampler(local)
     clocks.start()
-    for _ in range(max(3, args.warmup)):
-        step()
-    torch.cuda.synchronize()
+    warm = warm_up(step, args.warmup, world)
     if world > 1:
         dist.barrier()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    marks = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     w0 = time.time()
     t0.record()
-    for _ in range(args.steps):
+    for i in range(args.steps):
         y = step()
+        marks[i].record()
     t1.record()
     torch.cuda.synchronize()
     clocks.mark(w0, time.time())
     ms = t0.elapsed_time(t1)
+    step_ms = [t0.elapsed_time(marks[0])] + [marks[i - 1].elapsed_time(marks[i]) for i in range(1, args.steps)]
     if world > 1:
         dist.barrier()
     clk = clocks.stop()
@@ -613,12 +646,15 @@ def run_cfg4(args):
         step_s = ms / args.steps * 1e-3
         achieved = CFG4_BYTES_PER_TOKEN * (L // world) / step_s / 1e9
         out = {'metric': METRIC, 'value': L / step_s, 'unit': UNIT, 'n_gpus': world, 'steps': args.steps,
-               'warmup': max(3, args.warmup), 'ms_per_step': ms / args.steps, 'higher_is_better': True,
+               'warmup': warm, 'ms_per_step': ms / args.steps,
+               'step_ms': {'min': min(step_ms), 'median': statistics.median(step_ms), 'max': max(step_ms)},
+               'higher_is_better': True,
                'scaling': 'strong', 'vs_baseline': None, 'dtype': 'bf16', 'data': 'synthetic',
                'config': {'workload': 'cfg4 layer: ASRNLayer(512) forward, 1 x %d tokens, bf16 autocast, fp32 E/h'
                                       % L, 'global_batch': 1, 'seq_len': L, 'd': D4, 'vocab': V,
                           'parallelism': ('sequence-sharded over %d GPUs (NCCL all-gathers of the halo, clock '
-                                          'offsets and per-position features)' % world) if world > 1 else 'single GPU',
+                                          'offsets, bucket tails, per-position features, n-gram summaries and '
+                                          'streak maps)' % world) if world > 1 else 'single GPU',
                           'l2': 'inputs larger than L2 (E and h are %.0f MB each per GPU), no flush'
                                 % (Ec.nbytes / 1e6)},
                'e2e': {'value': L / (e2e_ms * 1e-3), 'unit': UNIT, 'h2d_bytes_per_step': int(xc.nbytes + Ec.nbytes +

@@ -212,7 +212,8 @@ int asrn_score_shard(const asrn_layer_config* cfg, const asrn_layer_weights* w, 
  * float32 of the chunk, equal to the whole-sequence values at its positions.
  * asrn_racha_chunk: the streak of a chunk (cfg->L positions, vistos / beta of the chunk) from the value before it
  * (racha_in (B), NULL = 0) into racha (B, Lc) (may be NULL); racha_map (B, 2) (may be NULL) receives the chunk's map
- * S_last = A * S_before + B0 as (A, B0), from which the next shards' racha_in follow. */
+ * S_last = A * S_before + B0 as (A, B0), from which the next shards' racha_in follow. With a workspace of
+ * asrn_racha_workspace_bytes (may be NULL: one block per sequence) few long rows are scanned over all SMs. */
 size_t asrn_ngram_chunk_workspace_bytes(const asrn_layer_config* cfg);
 int asrn_ngram_chunk_sort(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared,
                           int64_t L_feat, int64_t c0, const float* sig, const double* Bt, const float* log_alfa,
@@ -221,9 +222,10 @@ int asrn_ngram_chunk_finish(const asrn_layer_config* cfg, const asrn_layer_weigh
                             int64_t L_feat, int64_t c0, int32_t n_prev, const uint64_t* keys_prev,
                             const void* summary_prev, const uint64_t* keys, const double* Bt, const float* log_alfa,
                             uint8_t* vistos, float* hawkes, void* workspace, size_t workspace_bytes, void* stream);
+size_t asrn_racha_workspace_bytes(const asrn_layer_config* cfg);
 int asrn_racha_chunk(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared,
                      const uint8_t* vistos, const double* beta, const float* racha_in, float* racha, float* racha_map,
-                     void* stream);
+                     void* workspace, size_t workspace_bytes, void* stream);
 
 /* The same bucket sort for callers that cannot allocate device memory when they sort (a plug-in inside a host process
  * whose allocator it does not own, a serving loop that keeps a fixed memory footprint after start-up): no workspace
