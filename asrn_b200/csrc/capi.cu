@@ -586,7 +586,8 @@ int asrn_gen_ring_insert(int64_t B, int32_t T, int32_t nb, int32_t C, const int6
 
 int asrn_gen_front(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared, const float* h,
                    const float* e_t, const float* e_prev, const int64_t* tokens, void* Qc, void* Kc, double* beta,
-                   float* log_alfa, float* glogit, float* sig, void* phi, uint16_t* ids, void* stream) {
+                   float* log_alfa, float* glogit, float* sig, void* phi, uint16_t* ids, float* scratch,
+                   void* stream) {
   int st = check_config(cfg);
   if (st) return st;
   if ((st = check_weights(w))) return st;
@@ -604,6 +605,7 @@ int asrn_gen_front(const asrn_layer_config* cfg, const asrn_layer_weights* w, co
   a.w2 = prep + pl.w2; a.b2 = reinterpret_cast<const float*>(prep + pl.b2);
   a.beta_max = cfg->beta_max; a.log_alfa_min = cfg->log_alfa_min;
   a.Qc = Qc; a.Kc = Kc; a.beta = beta; a.log_alfa = log_alfa; a.glogit = glogit; a.sig = sig; a.phi = phi; a.ids = ids;
+  a.dots = scratch;
   a.status = reinterpret_cast<int*>(const_cast<char*>(prep) + pl.status);
   return launch_gen_front(a, cfg->half != 0, as_stream(stream));
 }

@@ -161,6 +161,7 @@ struct GenFrontArgs {
   float *log_alfa, *glogit, *sig;  // (B)
   void* phi;               // act (B, P)
   uint16_t* ids;           // (B, T)
+  float* dots;             // optional scratch (B, 2cf + 3 + 3m): the front split over more blocks
   int* status;             // device status word (bounded waits)
 };
 

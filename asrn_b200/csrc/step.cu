@@ -251,6 +251,158 @@ __global__ void __launch_bounds__(kFrontThreads) k_gen_front(GenFrontArgs a) {
   }
 }
 
+// ---- the same front split over more blocks (with a scratch buffer of the dot products) ------------------------------
+// k_gen_front_dots: block (b, slice) recomputes LN(h), act(E_t), act(E_{t-1}) of sequence b (cheap) and takes the
+//   slice's kFrontRows act weight rows ([cq; ck] then the 3m hidden rows) in one bulk copy: B x ceil(nact / rows)
+//   blocks instead of B, each streaming 1 / nch of the weights. Slice 0 also takes the three fp32 rows. The dot
+//   products land in dots (B, nq) in the single-block kernel's order, with the same per-row arithmetic.
+// k_gen_front_out: one block per sequence turns them into the outputs (the second hash layer, the ids).
+constexpr int kF1Threads = 256;
+
+template <bool Half>
+__global__ void __launch_bounds__(kF1Threads) k_gen_front_dots(GenFrontArgs a) {
+  using AT = typename Act<Half>::T;
+  extern __shared__ __align__(16) float sm[];
+  const int d = a.d, cf = a.cf, m = a.m;
+  const int nq = 2 * cf + 3 + 3 * m, nact = 2 * cf + 3 * m;
+  constexpr int kRows = Half ? 32 : 16;
+  const int64_t b = blockIdx.x;
+  const int slice = blockIdx.y;
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, nw = kF1Threads / 32;
+  float* s_h = sm;
+  float* s_hn = s_h + d;
+  float* s_hna = s_hn + d;
+  float* s_e = s_hna + d;
+  float* s_p = s_e + d;
+  float* s_red = s_p + d;                                   // 32
+  AT* s_w = reinterpret_cast<AT*>(s_red + 32);              // [kRows][d]
+  uint64_t* bar = reinterpret_cast<uint64_t*>(s_w + kRows * d);
+  const int r0 = slice * kRows, r1 = min(r0 + kRows, nact);
+  if (tid == 0) {
+    umma::mbar_init(bar, 1);
+    umma::fence_mbar_init();
+    const AT* wctx = reinterpret_cast<const AT*>(a.wctx);
+    const AT* w1 = reinterpret_cast<const AT*>(a.w1);
+    const uint32_t row_bytes = (uint32_t)d * sizeof(AT);
+    umma::mbar_expect_tx(bar, (uint32_t)(r1 - r0) * row_bytes);
+    const int a0 = r0, a1 = min(r1, 2 * cf);
+    if (a1 > a0)
+      asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                   ::"r"((uint32_t)__cvta_generic_to_shared(s_w)), "l"(wctx + (int64_t)a0 * d),
+                   "r"((uint32_t)(a1 - a0) * row_bytes), "r"((uint32_t)__cvta_generic_to_shared(bar))
+                   : "memory");
+    const int b0 = max(r0, 2 * cf), b1 = r1;
+    if (b1 > b0)
+      asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                   ::"r"((uint32_t)__cvta_generic_to_shared(s_w + (b0 - r0) * d)),
+                   "l"(w1 + (int64_t)(b0 - 2 * cf) * d), "r"((uint32_t)(b1 - b0) * row_bytes),
+                   "r"((uint32_t)__cvta_generic_to_shared(bar))
+                   : "memory");
+  }
+  const float* hrow = a.h + b * d;
+  float s = 0.f;
+  for (int j = tid; j < d; j += kF1Threads) {
+    const float x = hrow[j];
+    s_h[j] = x;
+    s += x;
+    s_e[j] = act<Half>(a.e_t[b * d + j]);
+    s_p[j] = act<Half>(a.e_prev[b * d + j]);
+  }
+  const float mean = block_sum(s, s_red) / (float)d;
+  float v = 0.f;
+  for (int j = tid; j < d; j += kF1Threads) {
+    const float c = s_h[j] - mean;
+    v += c * c;
+  }
+  const float rstd = 1.f / sqrtf(block_sum(v, s_red) / (float)d + 1e-5f);
+  for (int j = tid; j < d; j += kF1Threads) {
+    const float hn = (s_h[j] - mean) * rstd * a.ln_w[j] + a.ln_b[j];
+    s_hn[j] = hn;
+    s_hna[j] = act<Half>(hn);
+  }
+  __syncthreads();
+  float* dots = a.dots + b * nq;
+  if (slice == 0 && wid == nw - 1) {      // the three fp32 rows, while the copy is in flight
+    const float* xs[kDotWays] = {s_hn, s_hn, s_h, s_h};
+    const float* ws[kDotWays] = {a.w_reloj, a.w_reloj + d, a.g_w, a.g_w};
+    float r[kDotWays];
+    dot_rows<float>(xs, ws, 3, d, lane, r);
+    if (lane == 0) {
+      dots[2 * cf] = r[0];
+      dots[2 * cf + 1] = r[1];
+      dots[2 * cf + 2] = r[2];
+    }
+  }
+  umma::mbar_wait(bar, 0u, a.status);
+  for (int r = wid; r < r1 - r0; r += nw) {
+    const int q = r0 + r;
+    const float* x = q < 2 * cf ? s_hna : ((q - 2 * cf) < 2 * m ? s_e : s_p);
+    const float rv = dot_row_smem<AT>(x, s_w + r * d, d, lane);
+    if (lane == 0) dots[q < 2 * cf ? q : q + 3] = rv;
+  }
+}
+
+template <bool Half>
+__global__ void __launch_bounds__(kF1Threads) k_gen_front_out(GenFrontArgs a) {
+  using A = Act<Half>;
+  using AT = typename A::T;
+  __shared__ __align__(16) float s_dot[2 * kMaxConfirm + 3 + 3 * 128 + 4];
+  __shared__ __align__(16) float s_hid[2 * 128];
+  __shared__ float s_phi[kMaxPhi];
+  const int cf = a.cf, m = a.m, P = a.P, nb = a.nb, T = a.T;
+  const int nq = 2 * cf + 3 + 3 * m;
+  const int64_t b = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, nw = kF1Threads / 32;
+  for (int i = tid; i < nq; i += kF1Threads) s_dot[i] = a.dots[b * nq + i];
+  __syncthreads();
+  if (tid < 2 * cf) {
+    AT* dst = reinterpret_cast<AT*>(tid < cf ? a.Qc : a.Kc);
+    A::store(dst + b * cf + (tid < cf ? tid : tid - cf), s_dot[tid]);
+  } else if (tid == 2 * cf) {
+    const float u0 = s_dot[2 * cf] + a.b_reloj[0];
+    const float u1 = s_dot[2 * cf + 1] + a.b_reloj[1];
+    a.beta[b] = (double)fminf(softplus_t(u0), a.beta_max);
+    a.log_alfa[b] = fmaxf(logsigmoid_t(u1) + 0.693147180559945309f, a.log_alfa_min);
+    a.glogit[b] = s_dot[2 * cf + 2] + a.g_b[0];
+    a.sig[b] = (float)a.tokens[b];
+  }
+  const float* y = s_dot + 2 * cf + 3;
+  for (int i = tid; i < m; i += kF1Threads) {
+    s_hid[i] = act<Half>(gelu_t(act<Half>(y[i] + a.b1[i])));
+    s_hid[m + i] = act<Half>(gelu_t(act<Half>((y[m + i] + y[2 * m + i]) + a.b1[m + i])));
+  }
+  __syncthreads();
+  AT* phi = reinterpret_cast<AT*>(a.phi);
+  const AT* w2 = reinterpret_cast<const AT*>(a.w2);
+  for (int o = wid * kDotWays; o < P; o += nw * kDotWays) {
+    const float* xs[kDotWays];
+    const AT* ws[kDotWays];
+#pragma unroll
+    for (int k = 0; k < kDotWays; ++k) {
+      const int oo = min(o + k, P - 1);
+      xs[k] = (oo / nb < a.Tw) ? s_hid : s_hid + m;
+      ws[k] = w2 + (int64_t)oo * m;
+    }
+    float r[kDotWays];
+    dot_rows<AT>(xs, ws, min(kDotWays, P - o), m, lane, r);
+    if (lane == 0) {
+#pragma unroll
+      for (int k = 0; k < kDotWays; ++k) {
+        if (o + k >= P) break;
+        const float val = act<Half>(r[k] + a.b2[o + k]);
+        s_phi[o + k] = val;
+        A::store(phi + b * P + o + k, val);
+      }
+    }
+  }
+  __syncthreads();
+  if (tid < T) {
+    uint32_t id = 0;
+    for (int j = 0; j < nb; ++j) id |= (s_phi[tid * nb + j] > 0.f ? 1u : 0u) << j;
+    a.ids[b * T + tid] = (uint16_t)id;
+  }
+}
+
 size_t gen_front_smem(const GenFrontArgs& a, bool half) {
   const size_t f = sizeof(float) * (5 * (size_t)a.d + ((2 * a.cf + 3 + 3 * a.m + 3) & ~3) + 2 * a.m + ((a.P + 3) & ~3) + 32);
   const size_t rows = half ? 32 : 16, es = half ? 2 : 4;
@@ -262,6 +414,23 @@ int launch_gen_front(const GenFrontArgs& a, bool half, cudaStream_t s) {
   // 16-byte weight rows: d and m multiples of 8 (bf16) / 4 (fp32); the prepared buffer's rows are then aligned
   if (a.d % 8 != 0 || a.m % 8 != 0) return ASRN_ERR_UNSUPPORTED;
   if ((reinterpret_cast<uintptr_t>(a.w_reloj) | reinterpret_cast<uintptr_t>(a.g_w)) & 15) return ASRN_ERR_ARG;
+  if (a.dots) {             // split over (sequence, slice of weight rows) blocks
+    if (a.m > 128 || a.cf > kMaxConfirm || a.P > kMaxPhi) return ASRN_ERR_UNSUPPORTED;
+    const int rows = half ? 32 : 16, es = half ? 2 : 4;
+    const int nact = 2 * a.cf + 3 * a.m;
+    const size_t smem1 = sizeof(float) * (5 * (size_t)a.d + 32) + (size_t)rows * a.d * es + 16;
+    const dim3 g1((unsigned)a.B, (unsigned)((nact + rows - 1) / rows));
+    if (half) {
+      cudaFuncSetAttribute(k_gen_front_dots<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem1);
+      k_gen_front_dots<true><<<g1, kF1Threads, smem1, s>>>(a);
+      k_gen_front_out<true><<<(unsigned)a.B, kF1Threads, 0, s>>>(a);
+    } else {
+      cudaFuncSetAttribute(k_gen_front_dots<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem1);
+      k_gen_front_dots<false><<<g1, kF1Threads, smem1, s>>>(a);
+      k_gen_front_out<false><<<(unsigned)a.B, kF1Threads, 0, s>>>(a);
+    }
+    return cudaGetLastError() == cudaSuccess ? ASRN_OK : ASRN_ERR_CUDA;
+  }
   const size_t smem = gen_front_smem(a, half);
   if (smem > 220 * 1024) return ASRN_ERR_UNSUPPORTED;
   if (half) {

@@ -68,6 +68,7 @@ class Writer:
         self.ajeno = memoria_de_lo_ajeno
         self.grafo = grafo
         self.graph = None
+        self._front_scratch = None     # (B, nq) dot products of the split front kernels
 
     def _act(self):
         return torch.bfloat16 if self.half else torch.float32
@@ -263,9 +264,13 @@ class Writer:
         sig = torch.empty(B, dtype=torch.float32, device=dev)
         phi = torch.empty(B, T * nb, dtype=act, device=dev)
         ids = torch.empty(B, T, dtype=torch.int16, device=dev)
+        nq = 2 * cf + 3 + 3 * cfg.hidden
+        if self._front_scratch is None or self._front_scratch.numel() < B * nq:
+            self._front_scratch = torch.empty(B * nq, dtype=torch.float32, device=dev)
         _lib.check(lib.asrn_gen_front(cr, wr, pr, _lib.ptr(h), _lib.ptr(e_t), _lib.ptr(self.e_last), _lib.ptr(tok),
                                       _lib.ptr(qc), _lib.ptr(kc), _lib.ptr(beta), _lib.ptr(la), _lib.ptr(glogit),
-                                      _lib.ptr(sig), _lib.ptr(phi), _lib.ptr(ids), s), 'asrn_gen_front')
+                                      _lib.ptr(sig), _lib.ptr(phi), _lib.ptr(ids), _lib.ptr(self._front_scratch), s),
+                   'asrn_gen_front')
         vistos = torch.empty(B, n, dtype=torch.uint8, device=dev)
         hawkes = torch.empty(B, n, dtype=torch.float32, device=dev)
         racha = torch.empty(B, dtype=torch.float32, device=dev)

@@ -285,11 +285,14 @@ int asrn_gen_hawkes_build(const asrn_layer_config* cfg, const asrn_layer_weights
 /* Context stage and sign-hash projection of one new token per sequence (cfg->B sequences, cfg->L = 1), with the
  * whole-sequence stages' semantics (asrn_context, asrn_hash) for a token at t >= 1: h, e_t, e_prev (B, d) fp32 (the
  * state, E of the token and of the previous token), tokens (B) int64 -> Qc, Kc (B, cf) in the compute type, beta (B)
- * f64, log_alfa, glogit, sig (B) f32, phi (B, P) in the compute type, ids (B, T) uint16. One block per sequence,
- * the weights read by every block (they stay in L2). */
+ * f64, log_alfa, glogit, sig (B) f32, phi (B, P) in the compute type, ids (B, T) uint16. With scratch (B, 2 *
+ * confirmar + 3 + 3 * hidden) float32 the projections are split over (sequence, slice of 32 weight rows) blocks and
+ * a second kernel finishes each sequence; with scratch NULL one block per sequence does all of it (the weights read
+ * by every block; they stay in L2). Both give the same bits. */
 int asrn_gen_front(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared, const float* h,
                    const float* e_t, const float* e_prev, const int64_t* tokens, void* Qc, void* Kc, double* beta,
-                   float* log_alfa, float* glogit, float* sig, void* phi, uint16_t* ids, void* stream);
+                   float* log_alfa, float* glogit, float* sig, void* phi, uint16_t* ids, float* scratch,
+                   void* stream);
 
 /* Gate of the new tokens (asrn_gate's semantics for cfg->B * cfg->L rows, no workspace): W_ov is spread over d / 32
  * blocks. cbuf / sigma (both or neither; bf16 mode): the operand and gate values asrn_gen_attend precomputed. */

@@ -202,3 +202,47 @@ def test_gen_position_out_of_range_sets_status(cuda):
         assert _lib.lib().asrn_layer_status(ctypes.byref(cfg), _lib.ptr(prep), 1, _lib.stream_ptr(cuda)) == \
             _lib.ASRN_ERR_ARG
     assert torch.equal(st.bt, bt_before) and torch.equal(st.la, la_before)
+
+
+@pytest.mark.parametrize('half', [False, True])
+def test_split_front_equals_single_block_front(half, cuda):
+    """asrn_gen_front with a scratch buffer (projections split over (sequence, weight-row slice) blocks, then a
+    finishing kernel) gives the same bits as the one-block-per-sequence kernel: every output, fp32 and bf16."""
+    import ctypes
+    import asrn_b200
+    from asrn_b200 import _lib
+    torch.manual_seed(5)
+    layer = asrn_b200.ASRNLayer(256)
+    g = torch.Generator().manual_seed(6)
+    with torch.no_grad():
+        for n_, p_ in layer.named_parameters():
+            if n_ in ('w_reloj', 'b_reloj', 'cq.weight', 'g_conf.weight'):
+                p_.add_(torch.randn(p_.shape, generator=g) * 0.5)
+    layer = layer.to(cuda)
+    B, d = 5, 256
+    wts, _keep, prep = layer.prepared(cuda, half)
+    cfg = _lib.make_config(layer, B, 1, half)
+    act = torch.bfloat16 if half else torch.float32
+    h = torch.randn(B, d, generator=g).to(cuda)
+    e_t = torch.randn(B, d, generator=g).to(cuda)
+    e_p = torch.randn(B, d, generator=g).to(cuda)
+    tok = torch.randint(0, 1000, (B,), generator=g).to(cuda)
+    T, nb, cf = layer.n_tablas, layer.n_bits, layer.confirmar
+    outs = []
+    for split in (False, True):
+        o = dict(qc=torch.empty(B, cf, dtype=act, device=cuda), kc=torch.empty(B, cf, dtype=act, device=cuda),
+                 beta=torch.empty(B, dtype=torch.float64, device=cuda), la=torch.empty(B, device=cuda),
+                 gl=torch.empty(B, device=cuda), sig=torch.empty(B, device=cuda),
+                 phi=torch.empty(B, T * nb, dtype=act, device=cuda), ids=torch.empty(B, T, dtype=torch.int16,
+                                                                                     device=cuda))
+        scratch = torch.empty(B * (2 * cf + 3 + 3 * cfg.hidden), device=cuda) if split else None
+        rc = _lib.lib().asrn_gen_front(ctypes.byref(cfg), ctypes.byref(wts), _lib.ptr(prep), _lib.ptr(h),
+                                       _lib.ptr(e_t), _lib.ptr(e_p), _lib.ptr(tok), _lib.ptr(o['qc']),
+                                       _lib.ptr(o['kc']), _lib.ptr(o['beta']), _lib.ptr(o['la']), _lib.ptr(o['gl']),
+                                       _lib.ptr(o['sig']), _lib.ptr(o['phi']), _lib.ptr(o['ids']), _lib.ptr(scratch),
+                                       _lib.stream_ptr(cuda))
+        assert rc == _lib.ASRN_OK
+        outs.append(o)
+    torch.cuda.synchronize()
+    for k in outs[0]:
+        assert torch.equal(outs[0][k], outs[1][k]), k
