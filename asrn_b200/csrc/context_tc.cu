@@ -26,8 +26,8 @@ k_context_tc(const __grid_constant__ CUtensorMap tmap_wctx, ContextArgs a, int* 
   const int N = 2 * a.cf;
   const int stageB = N * 128;
   uint8_t* sA = sm;
-  uint8_t* sB = sm + 2 * kCStageA;
-  uint8_t* tail = sB + 2 * stageB;
+  uint8_t* sB = sm + 2 * kCStageA;                  // all d / 64 weight chunks, resident (2cf x 64 each)
+  uint8_t* tail = sB + (a.d / kCBK) * stageB;
   uint64_t* full_b = reinterpret_cast<uint64_t*>(tail);
   uint64_t* mma_done = full_b + 2;
   uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(full_b + 4);
@@ -130,9 +130,9 @@ k_context_tc(const __grid_constant__ CUtensorMap tmap_wctx, ContextArgs a, int* 
   for (int k = 0; k < nk; ++k) {
     const int s = k & 1;
     if (k >= 2) ok = mbar_wait(mma_done + s, ((k - 2) >> 1) & 1, status) && ok;
-    if (tid == 0 && ok) {
-      mbar_expect_tx(full_b + s, (uint32_t)stageB);
-      tma_load_2d(sB + s * stageB, &tmap_wctx, k * kCBK, 0, full_b + s);
+    if (k == 0 && tid == 0) {        // the whole [cq; ck] at once, on one barrier: no per-chunk weight wait
+      mbar_expect_tx(full_b, (uint32_t)(nk * stageB));
+      for (int kk = 0; kk < nk; ++kk) tma_load_2d(sB + kk * stageB, &tmap_wctx, kk * kCBK, 0, full_b);
     }
     uint8_t* dstA = sA + s * kCStageA;
     const int c0 = k * kCBK + ah * 32;
@@ -164,9 +164,9 @@ k_context_tc(const __grid_constant__ CUtensorMap tmap_wctx, ContextArgs a, int* 
     __syncthreads();
     if (tid == 0) {
       tc_fence_after();
-      if (ok) ok = mbar_wait(full_b + s, (k >> 1) & 1, status);
+      if (ok && k == 0) ok = mbar_wait(full_b, 0u, status);
       if (ok) {
-        const uint32_t a0 = smem_u32(dstA), b0 = smem_u32(sB + s * stageB);
+        const uint32_t a0 = smem_u32(dstA), b0 = smem_u32(sB + k * stageB);
 #pragma unroll
         for (int j = 0; j < kCBK / 16; ++j)
           mma_bf16(tmem, desc_sw128(a0 + j * 32), desc_sw128(b0 + j * 32), idesc, (k > 0 || j > 0) ? 1u : 0u);
@@ -225,7 +225,7 @@ int launch_context_tc(const ContextArgs& a, int* status, cudaStream_t s) {
   CUtensorMap map;
   if (!make_tmap_bf16(&map, a.wctx, (uint64_t)a.d, (uint64_t)(2 * a.cf), (uint64_t)a.d * 2, 64, (uint32_t)(2 * a.cf)))
     return ASRN_ERR_CUDA;
-  const size_t smem = 1024 + 2 * (size_t)kCStageA + 2 * (size_t)(2 * a.cf) * 128 + 64 + 5 * (size_t)a.d * 4;
+  const size_t smem = 1024 + 2 * (size_t)kCStageA + (size_t)(a.d / kCBK) * (2 * a.cf) * 128 + 64 + 5 * (size_t)a.d * 4;
   cudaFuncSetAttribute(k_context_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   const int64_t M = a.B * a.L;
   k_context_tc<<<(unsigned)((M + kCTM - 1) / kCTM), kCThreads, smem, s>>>(map, a, status);

@@ -95,12 +95,15 @@ __global__ void __launch_bounds__(256) k_gate_prep(GateArgs a) {
   sg = __shfl_sync(0xffffffffu, sg, 0);
   pt = __shfl_sync(0xffffffffu, pt, 0);
   if (lane == 0) a.sigma[g] = sg;
+  // pt is a count of tables (1 .. T): the quotient is taken as a product with 1 / pt (exact for powers of two, else
+  // within one fp32 ulp of the quotient before the bf16 rounding)
+  const float rpt = __frcp_rn(pt);
   const float4* src = reinterpret_cast<const float4*>(a.acc + g * a.d);
   uint2* dst = reinterpret_cast<uint2*>(a.cbuf + g * a.d);
   for (int c = lane; c < a.d / 4; c += 32) {
     const float4 x = src[c];
-    dst[c] = make_uint2(umma::pack_bf16x2(__fdiv_rn(x.x, pt), __fdiv_rn(x.y, pt)),
-                        umma::pack_bf16x2(__fdiv_rn(x.z, pt), __fdiv_rn(x.w, pt)));
+    dst[c] = make_uint2(umma::pack_bf16x2(__fmul_rn(x.x, rpt), __fmul_rn(x.y, rpt)),
+                        umma::pack_bf16x2(__fmul_rn(x.z, rpt), __fmul_rn(x.w, rpt)));
   }
 }
 

@@ -90,14 +90,17 @@ k_hash_tc(const __grid_constant__ CUtensorMap tmap_w1, const __grid_constant__ C
   };
   load_chunk(0);
   const uint32_t idesc1 = idesc_bf16(kTM, N1);
+  // weight chunk k arrives one step ahead: chunk 0 here, chunk k + 1 once the MMAs of chunk k - 1 (its stage) are done
+  auto issue_w1 = [&](int k) {
+    const int s = k & 1;
+    mbar_expect_tx(full_b + s, (uint32_t)stageB);
+    tma_load_2d(sB + s * stageB, &tmap_w1, k * kBK, 0, full_b + s);
+  };
+  if (tid == 0) issue_w1(0);
   bool ok = true;
   for (int k = 0; k < nk; ++k) {
     const int s = k & 1;
     if (k >= 2) ok = mbar_wait(mma_done + s, ((k - 2) >> 1) & 1, p.status) && ok;
-    if (tid == 0 && ok) {
-      mbar_expect_tx(full_b + s, (uint32_t)stageB);
-      tma_load_2d(sB + s * stageB, &tmap_w1, k * kBK, 0, full_b + s);
-    }
     // convert this thread's 32 fp32 values to bf16: 4 chunks of 16 bytes
     uint8_t* dstA = sA + s * kStageA;
     uint4 q[4];
@@ -127,6 +130,10 @@ k_hash_tc(const __grid_constant__ CUtensorMap tmap_w1, const __grid_constant__ C
           mma_bf16(tmem, desc_sw128(a0 + j * 32), desc_sw128(b0 + j * 32), idesc1, (k > 0 || j > 0) ? 1u : 0u);
       }
       mma_commit(mma_done + s);
+      if (ok && k + 1 < nk) {
+        if (k >= 1) ok = mbar_wait(mma_done + (s ^ 1), ((k - 1) >> 1) & 1, p.status);
+        if (ok) issue_w1(k + 1);
+      }
       if (!ok) *abort_s = 1;
     }
   }
