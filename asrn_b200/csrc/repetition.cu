@@ -249,7 +249,8 @@ __global__ void __launch_bounds__(1024) k_racha_apply(RepetitionArgs a, int64_t 
 
 // ---- rows longer than kRepMaxL ---------------------------------------------------------------------------------------
 
-constexpr int kRepTile = kRepMaxL;
+constexpr int kRepTile = kRepMaxL;   // scan tiles
+constexpr int kSortTile = 4096;      // sort tiles: 4 keys per thread, 48 KB of shared memory, many blocks per row
 constexpr int kMergeItems = 8;
 
 struct RepLong {
@@ -272,13 +273,13 @@ __device__ __forceinline__ double ngram_key_at(const float* sig, int64_t i, int 
 __global__ void __launch_bounds__(1024) k_ngram_tile_sort(RepetitionArgs a, int64_t tiles, uint64_t* K, uint32_t* Pp) {
   extern __shared__ __align__(16) char smem_raw[];
   uint64_t* sk = reinterpret_cast<uint64_t*>(smem_raw);
-  uint32_t* sp = reinterpret_cast<uint32_t*>(sk + kRepTile);
+  uint32_t* sp = reinterpret_cast<uint32_t*>(sk + kSortTile);
   const int64_t row = blockIdx.x / tiles, tile = blockIdx.x % tiles;
   const int64_t b = row / a.n;
   const int ni = (int)(row % a.n);
-  const int64_t L = a.L, base = tile * kRepTile;
+  const int64_t L = a.L, base = tile * kSortTile;
   const float* sig = a.sig + b * a.Lf;
-  for (int i = threadIdx.x; i < kRepTile; i += blockDim.x) {
+  for (int i = threadIdx.x; i < kSortTile; i += blockDim.x) {
     const int64_t p = base + i;
     if (p < L) {
       const double key = ngram_key_at(sig, a.pos0 + p, ni, a.c);
@@ -291,9 +292,9 @@ __global__ void __launch_bounds__(1024) k_ngram_tile_sort(RepetitionArgs a, int6
     }
   }
   __syncthreads();
-  for (int k = 2; k <= kRepTile; k <<= 1) {
+  for (int k = 2; k <= kSortTile; k <<= 1) {
     for (int j = k >> 1; j > 0; j >>= 1) {
-      for (int i = threadIdx.x; i < kRepTile; i += blockDim.x) {
+      for (int i = threadIdx.x; i < kSortTile; i += blockDim.x) {
         const int ixj = i ^ j;
         if (ixj > i) {
           const uint64_t ka = sk[i], kb = sk[ixj];
@@ -308,7 +309,7 @@ __global__ void __launch_bounds__(1024) k_ngram_tile_sort(RepetitionArgs a, int6
       __syncthreads();
     }
   }
-  const int64_t cnt = L - base < kRepTile ? L - base : kRepTile;
+  const int64_t cnt = L - base < kSortTile ? L - base : kSortTile;
   for (int i = threadIdx.x; i < cnt; i += blockDim.x) {
     K[row * L + base + i] = sk[i];
     Pp[row * L + base + i] = sp[i];
@@ -449,14 +450,15 @@ static int launch_repetition_long(const RepetitionArgs& a, void* ws, size_t ws_b
   if (!ws || ws_bytes < repetition_workspace(a.B, a.L, a.n)) return ASRN_ERR_WORKSPACE;
   const int64_t rows = a.B * a.n, L = a.L;
   const int64_t tiles = (L + kRepTile - 1) / kRepTile;
+  const int64_t stiles = (L + kSortTile - 1) / kSortTile;
   RepLong r = rep_long_layout(ws, rows, L);
-  const size_t smem = (size_t)kRepTile * 12;
+  const size_t smem = (size_t)kSortTile * 12;
   cudaFuncSetAttribute(k_ngram_tile_sort, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  k_ngram_tile_sort<<<(unsigned)(rows * tiles), 1024, smem, s>>>(a, tiles, r.k0, r.p0);
+  k_ngram_tile_sort<<<(unsigned)(rows * stiles), 1024, smem, s>>>(a, stiles, r.k0, r.p0);
   uint64_t *kin = r.k0, *kout = r.k1;
   uint32_t *pin = r.p0, *pout = r.p1;
   const int64_t per_row = (L + kMergeItems - 1) / kMergeItems;
-  for (int64_t w = kRepTile; w < L; w <<= 1) {
+  for (int64_t w = kSortTile; w < L; w <<= 1) {
     k_ngram_merge<<<(unsigned)((rows * per_row + 255) / 256), 256, 0, s>>>(kin, pin, kout, pout, rows, L, w);
     uint64_t* tk = kin; kin = kout; kout = tk;
     uint32_t* tp = pin; pin = pout; pout = tp;
@@ -707,16 +709,17 @@ int launch_ngram_chunk_sort(const RepetitionArgs& a, uint64_t* keys, void* summa
   if (!ws || ws_bytes < ngram_chunk_workspace(a.B, a.L, a.n)) return ASRN_ERR_WORKSPACE;
   const int64_t rows = a.B * a.n, L = a.L;
   const int64_t tiles = (L + kRepTile - 1) / kRepTile;
+  const int64_t stiles = (L + kSortTile - 1) / kSortTile;
   NgcLayout r = ngc_layout(ws, rows, L);
-  const size_t smem = (size_t)kRepTile * 12;
+  const size_t smem = (size_t)kSortTile * 12;
   cudaFuncSetAttribute(k_ngram_tile_sort, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   RepetitionArgs ak = a;
   ak.keys = nullptr;
-  k_ngram_tile_sort<<<(unsigned)(rows * tiles), 1024, smem, s>>>(ak, tiles, r.k0, r.p0);
+  k_ngram_tile_sort<<<(unsigned)(rows * stiles), 1024, smem, s>>>(ak, stiles, r.k0, r.p0);
   uint64_t *kin = r.k0, *kout = r.k1;
   uint32_t *pin = r.p0, *pout = r.p1;
   const int64_t per_row = (L + kMergeItems - 1) / kMergeItems;
-  for (int64_t w = kRepTile; w < L; w <<= 1) {
+  for (int64_t w = kSortTile; w < L; w <<= 1) {
     k_ngram_merge<<<(unsigned)((rows * per_row + 255) / 256), 256, 0, s>>>(kin, pin, kout, pout, rows, L, w);
     uint64_t* tk = kin; kin = kout; kout = tk;
     uint32_t* tp = pin; pin = pout; pout = tp;
