@@ -438,8 +438,12 @@ static RepLong rep_long_layout(void* ws, int64_t rows, int64_t L) {
   return r;
 }
 
+// Rows longer than one block's shared-memory sort take the tiled path (tile sorts, merges, tiled scans); shorter rows
+// are sorted and scanned by one block each (measured as fast as the tiled path at 32 x 4 rows of 8192 positions).
+static bool rep_tiled(int64_t L) { return L > kRepMaxL; }
+
 size_t repetition_workspace(int64_t B, int64_t L, int n) {
-  if (L <= kRepMaxL) return 0;
+  if (!rep_tiled(L)) return 0;
   const size_t rows = (size_t)B * n, E = rows * (size_t)L;
   const size_t tiles = (size_t)((L + kRepTile - 1) / kRepTile);
   return align_up(E * 8) * 2 + align_up(E * 4) * 2 + align_up(E * 8) + align_up(rows * tiles * 8);
@@ -771,7 +775,7 @@ int launch_racha(const RepetitionArgs& a, cudaStream_t s) { return launch_racha_
 int launch_repetition(const RepetitionArgs& a, void* ws, size_t ws_bytes, cudaStream_t s) {
   if (a.B == 0 || a.L == 0) return ASRN_OK;
   if (a.n < 1 || a.n > kMaxSeen) return ASRN_ERR_ARG;
-  if (a.L > kRepMaxL) {
+  if (rep_tiled(a.L)) {
     const int st = launch_repetition_long(a, ws, ws_bytes, s);
     if (st) return st;
     return launch_racha_ws(a, ws, ws_bytes, s);   // the n-gram passes are done with the workspace
