@@ -255,6 +255,27 @@ def _gather_seq(x, world, group):
     return torch.cat([p.view(dt).view(x.shape) for p in parts], 1)
 
 
+def _gather_seq_async(x, world, group):
+    """_gather_seq issued without waiting: (gathered tensor, finish) where finish() makes the current stream wait for
+    the collective (no host synchronisation)."""
+    import torch.distributed as dist
+    x = x.contiguous()
+    dt = x.dtype
+    xb = x.view(-1).view(torch.uint8)
+    if x.shape[0] == 1:
+        out = torch.empty(world * xb.numel(), dtype=torch.uint8, device=x.device)
+        work = dist.all_gather_into_tensor(out, xb, group=group, async_op=True)
+        return out.view(dt).view((1, world * x.shape[1]) + tuple(x.shape[2:])), work.wait
+    parts = [torch.empty_like(xb) for _ in range(world)]
+    work = dist.all_gather(parts, xb, group=group, async_op=True)
+    holder = {}
+
+    def finish():
+        work.wait()
+        holder['t'] = torch.cat([q.view(dt).view(x.shape) for q in parts], 1)
+    return holder, finish
+
+
 def exchange_halo(last, world, rank, group=None):
     """(B, d) E of this chunk's last position -> E of the position before this chunk (zeros on rank 0)."""
     import torch.distributed as dist
@@ -320,12 +341,17 @@ def forward(layer, E, h, tokens=None, group=None):
     loc = _phase1(layer, E, h, tokens, halo, half, c0)
     # (2) chunk sums of beta (= the last local clock value) -> clock offsets
     sums = exchange_chunk_sums(loc['Bt'][:, -1], world, group)
-    # (3) bucket tails, (4) features of every position
+    # (3) bucket tails, (4) features of every position: the per-position scalars first; the feature rows (phi, Qc,
+    # Kc, the bf16 rows of E) are gathered while the n-gram memory sorts its chunk
     tails = exchange_tails(loc['tails'], world, group)
-    full = {k: _gather_seq(loc[k], world, group) for k in _SEQ_KEYS}
+    full = {k: _gather_seq(loc[k], world, group) for k in ('sig', 'log_alfa', 'beta', 'Bt')}
+    pending = {k: _gather_seq_async(loc[k], world, group) for k in ('phi', 'Qc', 'Kc', 'Ea')}
     _apply_clock_offsets(full['Bt'], sums, Lc)
     # (5) n-gram memory: per-group summaries of every chunk, then the streak maps
     ng = ngram_sort(layer, full, c0, Lc, half)
+    for k, (t, finish) in pending.items():
+        finish()
+        full[k] = t['t'] if isinstance(t, dict) else t
     keys, summ = exchange_ngram(ng['keys'], ng['summ'], world, group)
     vistos, hawkes = ngram_finish(layer, full, ng, keys[:rank] if rank > 0 else None,
                                   summ[:rank] if rank > 0 else None, c0, Lc, half)
