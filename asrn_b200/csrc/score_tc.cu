@@ -3,21 +3,22 @@
 //   window = the 64 sorted slots [q0 - 32, q0 + 32) of the row (the previous sub-tile + the current one);
 //   S = phi_q . phi_k and Qc . Kc (32 x 64 each) on mma.sync (fp32 accumulate), then the reference's rounding chain,
 //   suffix weight, log_alfa_k and the fp64 time difference, the exact-mask softmax per query, and
-//   out (32 x d_part) = att (32 x 64, bf16) . V (64 x d_part) on mma.sync, added into acc with vector L2 reductions.
+//   out^T (d_part x 32) = V^T (d_part x 64) . att^T (64 x 32) on tcgen05 (M = 128 rows of d per MMA, N = the 32
+//   queries, K = the 64 window keys; the accumulators in TMEM), added into acc with vector L2 reductions.
 // A value row Ea[pos + 1] is gathered only for slots some query can use (the next sorted slot is in the same bucket);
-// other rows are zero-filled without reading memory.
+// other rows keep earlier finite contents (the ring is zeroed when the block starts) and meet zero weights.
 //
 // One block of 16 warps per (row, span of 512 slots), two warp groups working on consecutive sub-tiles at once:
-// in iteration i group A (warps 0-7) scores sub-tile i + 1 and takes its softmax, while group B (warps 8-15)
-// multiplies sub-tile i's weights by its value rows and reduces them into acc. The weights pass from A to B through
-// a double buffer; one block barrier per iteration. Every load is cp.async: the sorted entries of sub-tile i + 3,
-// the scalars and feature rows (phi, Qc, Kc) of sub-tile i + 2 into a 4-sub-tile feature ring, the value rows of
-// sub-tile i + 1 into a 3-sub-tile value ring; all land while the current iteration computes. The value rows move
-// by bulk copies (cp.async.bulk, one per used row) counted on an mbarrier per ring stage, so the largest transfers do
-// not occupy the warps' load slots; value rows no query uses are not loaded and keep earlier finite contents (the
-// ring is zeroed when the block starts), multiplied by zero weights. The feature rows and the small per-position
-// gathers (clock, log_alfa, previous signatures, the sorted entries) are cp.async. d is split over two blocks only
-// when d > 768.
+// in iteration i group A (warps 0-7) scores sub-tile i + 1 and takes its softmax, while group B (warps 8-15) has the
+// value products of sub-tile i computed by the tensor cores (one thread issues them) and reduces them into acc. The
+// weights pass from A to B through a double buffer in the MMA's K-major swizzled layout; one block barrier per
+// iteration. Loads run ahead of use, issued by every warp after one named barrier: the sorted entries of sub-tile
+// i + 3 and the per-position scalars of i + 2 by cp.async, the phi / Qc / Kc rows of i + 2 by tensor-map row gathers
+// (four rows per instruction) into a 4-sub-tile feature ring, the used value rows of i + 1 by 16-byte cp.async into a
+// 3-sub-tile value ring kept in the MMA's MN-major 128-byte-swizzled layout (one 12 KB region per 64 columns of d).
+// The TMEM epilogue transposes 4 x 4 blocks across lanes so that each 16-byte reduction covers four consecutive
+// columns of one query row (a warp's reduction covers four rows x 128 bytes). d is split over blocks only when
+// d > 768 (d_part a multiple of 128).
 #include <cuda.h>
 
 #include "common.cuh"
@@ -33,7 +34,8 @@ constexpr int kRV = 96;          // value ring: 3 sub-tiles (window of i, prefet
 constexpr int kSpanTc = 512;     // sorted slots per block
 constexpr int kThreadsTc = 512;  // 16 warps: two groups of 8
 constexpr int kGroupWarps = 8;
-constexpr int kMaxNt = 12;       // n8 value tiles per group-B warp (d_part <= 768)
+constexpr int kMaxMt = 6;        // M = 128 tiles of d_part (d_part <= 768)
+constexpr int kVRegion = kRV * 128;   // one 64-column region of the value ring (bytes)
 constexpr int kStage = 3;        // staging buffers of sorted-row entries
 constexpr int kStageIds = 40;    // ids staged per sub-tile: its 32 slots and the next 8 (the `used` test reads s + 1)
 
@@ -49,13 +51,14 @@ struct TcSmem {
   __nv_bfloat16* phi;   // [kRF][Pp]
   __nv_bfloat16* qc;    // [kRF][Cp]
   __nv_bfloat16* kc;    // [kRF][Cp]
-  __nv_bfloat16* v;     // [kRV][Dp]
+  uint8_t* v;           // [d_part / 64][kRV rows][128 B], MN-major 128-byte swizzle (1024-byte aligned)
   float* sc;            // [32][65]
-  __nv_bfloat16* att;   // [2][32][72]
-  int* qhay;            // [2][32]
+  uint8_t* att;         // [2][32 rows][128 B], K-major 128-byte swizzle (1024-byte aligned)
+  int64_t* qoff;        // [2][32] acc element offset of the query's row, or -1 (no candidate / not this shard's)
   float* wsuf;          // [kMaxSuffix + 1] suffix weights w_sufijo
-  uint64_t* vbar;       // [3] value-stage mbarriers
   uint64_t* fbar;       // [4] feature-stage mbarriers (one per 32-row stage of the feature ring)
+  uint64_t* pvbar;      // value-product MMAs done
+  uint32_t* tmem;       // TMEM base address
   int Pp, Cp, Dp;        // row pitches (elements)
   int Gp, Gc;            // 4-row group strides of the phi and Qc / Kc rings (elements)
   __device__ __forceinline__ int prow(int fr) const { return (fr >> 2) * Gp + (fr & 3) * Pp; }
@@ -68,33 +71,34 @@ __host__ __device__ inline int pad16(int x) { return (x + 15) / 16 * 16; }
 __host__ __device__ inline int group_elems(int pitch) { return (4 * pitch * 2 + 127) / 128 * 128 / 2; }
 
 __host__ __device__ inline size_t tc_smem_bytes(int P, int cf, int dpart) {
-  const int Pp = pad16(P) + 8, Cp = pad16(cf) + 8, Dp = dpart + 8;
-  size_t b = 128;                                // alignment slack of the dynamic shared memory base
+  const int Pp = pad16(P) + 8, Cp = pad16(cf) + 8;
+  size_t b = 1024;                               // alignment slack of the dynamic shared memory base
+  b += (size_t)(dpart / 64) * kVRegion + 2 * kQ * 128;
   b += (size_t)(kRF / 4) * (group_elems(Pp) + 2 * group_elems(Cp)) * 2;
   b += kStage * kQ * 4 + kStage * kStageIds * 2;
   b = (b + 15) / 16 * 16;
   b += kRF * 8;                                  // bt
   b += kRF * 4 * (size_t)kMaxSuffix;             // pf
   b += kRF * 4 * 4;                              // pos, id, used, la
-  b += (size_t)kRV * Dp * 2;
   b += (size_t)kQ * 65 * 4;
-  b += 2 * (size_t)kQ * 72 * 2;
-  b += 2 * kQ * 4;
+  b += 2 * kQ * 8;                               // qoff
   b += (kMaxSuffix + 8) * 4;
   b = (b + 15) / 16 * 16;
-  b += 8 * 8;                                    // mbarriers
-  return b + 16;
+  b += 8 * 8 + 16;                               // mbarriers, TMEM address
+  return b;
 }
 
 __device__ inline TcSmem carve_tc(char* base, int P, int cf, int dpart) {
   TcSmem s;
   s.Pp = pad16(P) + 8;
   s.Cp = pad16(cf) + 8;
-  s.Dp = dpart + 8;
+  s.Dp = dpart;
   s.Gp = group_elems(s.Pp);
   s.Gc = group_elems(s.Cp);
-  base += (128 - (__cvta_generic_to_shared(base) & 127)) & 127;
+  base += (1024 - (__cvta_generic_to_shared(base) & 1023)) & 1023;
   char* p = base;
+  s.v = reinterpret_cast<uint8_t*>(p); p += (size_t)(dpart / 64) * kVRegion;
+  s.att = reinterpret_cast<uint8_t*>(p); p += 2 * kQ * 128;
   s.phi = reinterpret_cast<__nv_bfloat16*>(p); p += (size_t)(kRF / 4) * s.Gp * 2;
   s.qc = reinterpret_cast<__nv_bfloat16*>(p); p += (size_t)(kRF / 4) * s.Gc * 2;
   s.kc = reinterpret_cast<__nv_bfloat16*>(p); p += (size_t)(kRF / 4) * s.Gc * 2;
@@ -107,14 +111,13 @@ __device__ inline TcSmem carve_tc(char* base, int P, int cf, int dpart) {
   s.id = reinterpret_cast<int*>(p); p += kRF * 4;
   s.used = reinterpret_cast<int*>(p); p += kRF * 4;
   s.la = reinterpret_cast<float*>(p); p += kRF * 4;
-  s.v = reinterpret_cast<__nv_bfloat16*>(p); p += (size_t)kRV * s.Dp * 2;
   s.sc = reinterpret_cast<float*>(p); p += kQ * 65 * 4;
-  s.att = reinterpret_cast<__nv_bfloat16*>(p); p += 2 * kQ * 72 * 2;
-  s.qhay = reinterpret_cast<int*>(p); p += 2 * kQ * 4;
+  s.qoff = reinterpret_cast<int64_t*>(p); p += 2 * kQ * 8;
   s.wsuf = reinterpret_cast<float*>(p); p += (kMaxSuffix + 8) * 4;
   p = base + ((p - base) + 15) / 16 * 16;
-  s.vbar = reinterpret_cast<uint64_t*>(p);
-  s.fbar = s.vbar + 3;
+  s.fbar = reinterpret_cast<uint64_t*>(p);
+  s.pvbar = s.fbar + 4;
+  s.tmem = reinterpret_cast<uint32_t*>(s.fbar + 8);
   return s;
 }
 
@@ -257,27 +260,22 @@ __device__ __forceinline__ void tc_stage2_features(const ScoreArgs& a, const TcS
   }
 }
 
-// Value rows Ea[pos + 1] of sub-tile t (its scalars already in the feature ring): one bulk copy per used row onto
-// the stage's mbarrier, issued by lane 0 of warp slot % 16 (spread over the warps). Thread 0 first sets the stage's
-// transaction count from the used flags (arrive.expect_tx); the copies follow a block barrier.
-__device__ __forceinline__ int tc_value_bytes(const TcSmem& S, const TcBlock& k, int t) {
-  int n = 0;
-  for (int i = 0; i < kQ; ++i) n += S.used[frow((t + 1) * kQ + i)];
-  return n * k.dpart * 2;
-}
+// Value rows Ea[pos + 1] of sub-tile t (its scalars already in the feature ring) into the value ring, only the used
+// rows: warp w takes slots w and w + 16, its lanes the row's 16-byte chunks by cp.async, each chunk at its place in
+// the MN-major 128-byte-swizzled layout (region = 64 columns, row = key, chunk index XOR the key's row in its group of
+// 8).
 __device__ __forceinline__ void tc_stage2_values(const ScoreArgs& a, const TcSmem& S, const TcBlock& k, int t) {
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  if (lane != 0) return;
-  uint64_t* bar = S.vbar + ((t + 1) % 3);
-  const uint32_t bytes = (uint32_t)k.dpart * 2;
+  const int nch = k.dpart / 8;                 // 16-byte chunks per row
   for (int i = wid; i < kQ; i += nw) {
     const int li = (t + 1) * kQ + i;
     const int fr = frow(li), vr = vrow(li);
-    if (S.used[fr]) {
-      const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(a.Ea) + (k.b * a.Lf + S.pos[fr] + 1) *
-                                 (int64_t)a.d + k.dp0;
-      bulk_load(S.v + vr * S.Dp, src, bytes, bar);
-    }
+    if (!S.used[fr]) continue;
+    const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(a.Ea) + (k.b * a.Lf + S.pos[fr] + 1) *
+                               (int64_t)a.d + k.dp0;
+    uint8_t* row = S.v + (vr >> 3) * 1024 + (vr & 7) * 128;
+    for (int c = lane; c < nch; c += 32)
+      cp_async16(row + (c >> 3) * kVRegion + (((c & 7) ^ (vr & 7)) << 4), src + c * 8, true);
   }
 }
 
@@ -393,8 +391,8 @@ __device__ __forceinline__ void tc_scores(const ScoreArgs& a, const TcSmem& S, c
   }
   bar_group_a();
   // softmax: warp w -> queries 4w .. 4w + 3 together; lane -> keys lane, lane + 32
-  __nv_bfloat16* att = S.att + (t & 1) * kQ * 72;
-  int* qhay = S.qhay + (t & 1) * kQ;
+  uint8_t* att = S.att + (t & 1) * kQ * 128;
+  int64_t* qoff = S.qoff + (t & 1) * kQ;
   const int qa = wid * 4;
   float x[4][2], m[4], sum[4], e[4][2];
   unsigned bal[4];
@@ -443,64 +441,69 @@ __device__ __forceinline__ void tc_scores(const ScoreArgs& a, const TcSmem& S, c
       a.sen_mx[gq * a.T + k.tau] = kProhibido;
       a.sen_pk[gq * a.T + k.tau] = 0.f;
     }
-    att[qi * 72 + lane] = __float2bfloat16_rn(w0);
-    att[qi * 72 + lane + 32] = __float2bfloat16_rn(w1);
-    if (lane == 0) qhay[qi] = (anyv && mine) ? 1 : 0;
+    // weights of keys lane and lane + 32 at row qi of the swizzled K-major operand (128-byte rows of 64 keys)
+    uint8_t* arow = att + (qi >> 3) * 1024 + (qi & 7) * 128 + (lane & 7) * 2;
+    *reinterpret_cast<__nv_bfloat16*>(arow + ((((lane >> 3)) ^ (qi & 7)) << 4)) = __float2bfloat16_rn(w0);
+    *reinterpret_cast<__nv_bfloat16*>(arow + ((((lane >> 3) + 4) ^ (qi & 7)) << 4)) = __float2bfloat16_rn(w1);
+    if (lane == 0) qoff[qi] = (anyv && mine) ? gq * a.d + k.dp0 : -1;
   }
+  umma::fence_proxy_async();       // the weights are read by the tensor cores (async proxy) after the block barrier
 }
 
-// Group B: out = att[t & 1] . V for sub-tile t on tensor cores, reduced into acc. Warp w (0-7 within the group) owns
-// the n8 tiles w, w + 8, ... of the d_part columns.
-__device__ __forceinline__ void tc_values(const ScoreArgs& a, const TcSmem& S, const TcBlock& k, int t, int w) {
+// Group B: out^T = V^T . att^T for sub-tile t on tcgen05, reduced into acc. One thread issues the MMAs: M-tile mm
+// (rows 128 mm .. + 127 of d_part: two 64-column regions of the value ring, MN-major, 12 KB apart), K-step ks (window
+// keys 16 ks .. + 15: two 8-key groups of the ring, 1024 B apart), N = the 32 queries (att rows, K-major); D in TMEM
+// columns 32 mm .. + 31. Then warp w reads TMEM lanes 32 (w % 4) .. + 31 (32 rows of d) for M-tiles (w - 8) / 4,
+// + 2, + 4: each lane holds one row of d for the 32 queries; 4 x 4 transposes within lane quads give each lane four
+// consecutive rows of d for one query, reduced into acc with one 16-byte reduction.
+__device__ __forceinline__ void tc_values(const ScoreArgs& a, const TcSmem& S, const TcBlock& k, int t, int w,
+                                          uint32_t tmem) {
   const int lane = threadIdx.x & 31;
   const int lb = t * kQ;                        // window index of key 0 (li of slot q0 - 32)
-  const __nv_bfloat16* att = S.att + (t & 1) * kQ * 72;
-  const int* qhay = S.qhay + (t & 1) * kQ;
-  const int ntiles = k.dpart / 8;
+  const int nM = k.dpart / 128;
+  if (w == 0 && lane == 0) {
+    umma::tc_fence_after();
+    const uint32_t idesc = umma::idesc_bf16(128, kQ) | (1u << 15);      // A (the value rows) MN-major
+    const uint32_t v0 = su32(S.v), a0 = su32(S.att + (t & 1) * kQ * 128);
+    for (int mm = 0; mm < nM; ++mm) {
 #pragma unroll
-  for (int mt = 0; mt < 2; ++mt) {
-    const int qbase = mt * 16;
-    const bool any = qhay[qbase + (lane & 15)] != 0;
-    if (!__any_sync(0xffffffffu, any)) continue;
-    float acc[kMaxNt][4];
-#pragma unroll
-    for (int j = 0; j < kMaxNt; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
-    // queries of m-tile mt use window keys [qbase, qbase + 47]
-    const uint32_t att_a = su32(att) + 2u * (uint32_t)((qbase + (lane & 15)) * 72 + (lane >> 4) * 8);
-    for (int ks = mt; ks < mt + 3; ++ks) {
-      uint32_t a0, a1, a2, a3;
-      ldsm_x4(att_a + 2u * (uint32_t)(ks * 16), a0, a1, a2, a3);
-      const uint32_t v_row = su32(S.v) + 2u * (uint32_t)(vrow(lb + ks * 16 + (lane & 15)) * S.Dp);
-#pragma unroll
-      for (int j = 0; j < kMaxNt; ++j) {
-        const int tile = w + kGroupWarps * j;
-        if (tile < ntiles) {
-          uint32_t b0, b1;
-          ldsm_x2_t(v_row + 2u * (uint32_t)(tile * 8), b0, b1);
-          mma16816(acc[j], a0, a1, a2, a3, b0, b1);
-        }
+      for (int ks = 0; ks < 4; ++ks) {
+        const int r0 = vrow(lb + ks * 16);
+        const uint64_t adesc = umma::desc_mn_sw128(v0 + (uint32_t)(2 * mm) * kVRegion + (uint32_t)(r0 >> 3) * 1024,
+                                             (uint32_t)kVRegion);
+        const uint64_t bdesc = umma::desc_sw128(a0 + ks * 32);
+        umma::mma_bf16(tmem + (uint32_t)(mm * kQ), adesc, bdesc, idesc, ks > 0 ? 1u : 0u);
       }
     }
-    // one 16-byte reduction per lane and tile: lanes q and q ^ 1 of a quad swap halves so that the even lane holds
-    // columns 4 (q >> 1) .. + 3 of row r and the odd lane the same columns of row r + 8
-    const int qd = lane & 3;
-    const int rowq = qbase + (lane >> 2) + ((qd & 1) ? 8 : 0);
-    const bool hasq = qhay[rowq] != 0;
-    const int64_t gq = k.b * (a.q_hi - a.q_lo) + (S.pos[frow(lb + kQ + rowq)] - a.q_lo);
-    float* dst = a.acc + gq * a.d + k.dp0 + (qd >> 1) * 4;
+    umma::mma_commit(S.pvbar);
+  }
+  __syncwarp();
+  umma::mbar_wait(S.pvbar, (uint32_t)(t & 1), a.status);
+  umma::tc_fence_after();
+  const int q4 = w & 3;
+  const int64_t* qoff = S.qoff + (t & 1) * kQ;
+  const int qd = lane & 3, g = lane >> 2;
+  for (int mm = w >> 2; mm < nM; mm += 2) {
+    float v[32];
+    umma::tmem_ld32(tmem + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(mm * kQ), v);
+    const int dcol = mm * 128 + q4 * 32 + 4 * g;   // first of this lane's four d rows after the transpose
 #pragma unroll
-    for (int j = 0; j < kMaxNt; ++j) {
-      const int tile = w + kGroupWarps * j;
-      if (tile < ntiles) {
-        const bool odd = qd & 1;
-        const float s0 = odd ? acc[j][0] : acc[j][2], s1 = odd ? acc[j][1] : acc[j][3];
-        const float r0 = __shfl_xor_sync(0xffffffffu, s0, 1), r1 = __shfl_xor_sync(0xffffffffu, s1, 1);
-        const float v0 = odd ? r0 : acc[j][0], v1 = odd ? r1 : acc[j][1];
-        const float v2 = odd ? acc[j][2] : r0, v3 = odd ? acc[j][3] : r1;
-        if (hasq) red_add_v4(dst + tile * 8, v0, v1, v2, v3);
-      }
+    for (int c = 0; c < kQ / 4; ++c) {
+      float x0 = v[4 * c], x1 = v[4 * c + 1], x2 = v[4 * c + 2], x3 = v[4 * c + 3];
+      // across lane bit 1, then bit 0: lane qd ends with query 4c + qd of the quad's four d rows
+      float p0 = (qd & 2) ? x0 : x2, p1 = (qd & 2) ? x1 : x3;
+      float r0 = __shfl_xor_sync(0xffffffffu, p0, 2), r1 = __shfl_xor_sync(0xffffffffu, p1, 2);
+      if (qd & 2) { x0 = r0; x1 = r1; } else { x2 = r0; x3 = r1; }
+      p0 = (qd & 1) ? x0 : x1;
+      p1 = (qd & 1) ? x2 : x3;
+      r0 = __shfl_xor_sync(0xffffffffu, p0, 1);
+      r1 = __shfl_xor_sync(0xffffffffu, p1, 1);
+      if (qd & 1) { x0 = r0; x2 = r1; } else { x1 = r0; x3 = r1; }
+      const int64_t off = qoff[4 * c + qd];
+      if (off >= 0) red_add_v4(a.acc + off + dcol, x0, x1, x2, x3);
     }
   }
+  umma::tc_fence_before();
 }
 
 __global__ void __launch_bounds__(kThreadsTc, 1)
@@ -527,38 +530,42 @@ k_score_tc(const __grid_constant__ CUtensorMap tm_phi, const __grid_constant__ C
   const bool group_a = wid < kGroupWarps;
   const int ntile = (int)((k.S1 - k.S0 + kQ - 1) / kQ);
 
-  // zero both rings once (rows never loaded keep finite contents), set up the stage barriers
+  // zero both rings once (rows never loaded keep finite contents), set up the barriers, TMEM for the value products
   {
-    uint4* z0 = reinterpret_cast<uint4*>(S.phi);
-    const int nz = (int)(((char*)(S.v + kRV * S.Dp) - (char*)S.phi) / 16);
+    uint4* z0 = reinterpret_cast<uint4*>(S.v);
+    const int nz = (int)((reinterpret_cast<char*>(S.st_pos) - reinterpret_cast<char*>(S.v)) / 16);
     for (int i = threadIdx.x; i < nz; i += blockDim.x) z0[i] = make_uint4(0, 0, 0, 0);
     if (threadIdx.x <= kMaxSuffix) S.wsuf[threadIdx.x] = threadIdx.x <= a.K ? a.w_suf[threadIdx.x] : 0.f;
-    umma::fence_proxy_async();                 // the zeros precede the bulk copies into the same rows
+    umma::fence_proxy_async();                 // the zeros precede the tensor-map copies into the same rows
     if (threadIdx.x == 0) {
-      for (int i = 0; i < 7; ++i) umma::mbar_init(S.vbar + i, 1);   // 3 value stages, then 4 feature stages
+      for (int i = 0; i < 5; ++i) umma::mbar_init(S.fbar + i, 1);   // 4 feature stages, the value-product MMAs
       umma::fence_mbar_init();
     }
+    if (wid == kGroupWarps) {
+      umma::tmem_alloc(S.tmem, 256);
+      umma::tmem_relinquish();
+    }
   }
-  // bounded wait for the value bulk copies of a stage, by every thread (each observes the completed phase)
-  auto wait_values = [&](int t) {
-    umma::mbar_wait(S.vbar + ((t + 1) % 3), (uint32_t)(((t + 1) / 3) & 1), a.status);
-  };
   // bounded wait for the feature rows of sub-tile t (stage (t + 1) % 4)
   auto wait_features = [&](int t) {
     umma::mbar_wait(S.fbar + ((t + 1) & 3), (uint32_t)(((t + 1) >> 2) & 1), a.status);
   };
-  // the stages' transaction counts (the used value rows; the fixed feature rows) are set by thread 0 before any copy
-  // of the stage is issued
-  auto expect_values = [&](int t) {
-    if (threadIdx.x == 0) umma::mbar_expect_tx(S.vbar + ((t + 1) % 3), (uint32_t)tc_value_bytes(S, k, t));
-  };
+  // the stage's transaction count is set by thread 0 before any copy of the stage is issued
   auto expect_features = [&](int t) {
     if (threadIdx.x == 0) umma::mbar_expect_tx(S.fbar + ((t + 1) & 3), (uint32_t)(kQ * (S.Pp + 2 * S.Cp) * 2));
+  };
+  // this thread's cp.async copies (scalars, value rows) complete, then made visible to the tensor cores
+  auto wait_copies = [&]() {
+    cp_async_wait_all();
+    umma::fence_proxy_async();
   };
 
   // prologue: sub-tiles -1 (the first window half), 0 and 1 of the features, -1 and 0 of the values, the scores of
   // 0 taken; sub-tile 2's sorted entries on their way
+  umma::tc_fence_before();
   __syncthreads();
+  umma::tc_fence_after();
+  const uint32_t tmem = *S.tmem;
   tc_stage1(a, S, k, -1);
   tc_stage1(a, S, k, 0);
   if (ntile > 1) tc_stage1(a, S, k, 1);
@@ -574,13 +581,10 @@ k_score_tc(const __grid_constant__ CUtensorMap tm_phi, const __grid_constant__ C
   cp_async_commit();
   cp_async_wait_all();
   __syncthreads();
-  expect_values(-1);
-  expect_values(0);
   if (ntile > 2) tc_stage1(a, S, k, 2);        // its buffer was read by sub-tile -1's feature stage above
-  cp_async_commit();
-  __syncthreads();
   tc_stage2_values(a, S, k, -1);
   tc_stage2_values(a, S, k, 0);
+  cp_async_commit();
   wait_features(-1);
   wait_features(0);
   const bool suf4 = a.K <= 4;
@@ -588,20 +592,17 @@ k_score_tc(const __grid_constant__ CUtensorMap tm_phi, const __grid_constant__ C
     if (suf4) tc_scores<true>(a, S, k, 0);
     else tc_scores<false>(a, S, k, 0);
   }
-  cp_async_wait_all();
-  wait_values(-1);
-  wait_values(0);
+  wait_copies();
   if (ntile > 1) wait_features(1);
   __syncthreads();
 
   for (int i = 0; i < ntile; ++i) {
-    // value rows of i + 1 (their scalars arrived with the features in iteration i - 1) and feature rows of i + 2:
-    // byte counts first, then the copies, issued by all warps
-    if (i + 1 < ntile) expect_values(i + 1);
+    // value rows of i + 1 (their scalars arrived with the features in iteration i - 1) and feature rows of i + 2,
+    // issued by all warps once thread 0 has set the feature stage's byte count
     if (i + 2 < ntile) expect_features(i + 2);
     if (i + 3 < ntile) tc_stage1(a, S, k, i + 3);
     if (i + 1 < ntile) {
-      asm volatile("bar.sync 2, 512;" ::: "memory");   // the expect_tx precedes every copy of the stages
+      asm volatile("bar.sync 2, 512;" ::: "memory");   // the expect_tx precedes every copy of the stage
       if (i + 2 < ntile) tc_stage2_features(a, S, k, i + 2, &tm_phi, &tm_qc, &tm_kc);
       tc_stage2_values(a, S, k, i + 1);
     }
@@ -612,26 +613,30 @@ k_score_tc(const __grid_constant__ CUtensorMap tm_phi, const __grid_constant__ C
         else tc_scores<false>(a, S, k, i + 1);
       }
     } else {
-      tc_values(a, S, k, i, wid - kGroupWarps);
+      tc_values(a, S, k, i, wid - kGroupWarps, tmem);
     }
-    cp_async_wait_all();
-    if (i + 1 < ntile) wait_values(i + 1);
+    wait_copies();
     if (i + 2 < ntile) wait_features(i + 2);
     __syncthreads();
+  }
+  if (wid == kGroupWarps) {
+    umma::tc_fence_after();
+    umma::tmem_dealloc(tmem, 256);
   }
 }
 
 bool score_tc_supported(const ScoreArgs& a) {
-  return a.d % 64 == 0 && a.d <= 1024 && a.C <= 32 && a.P <= kMaxPhi && a.P % 8 == 0 && pad16(a.P) + 8 <= 256 &&
+  return a.d % 128 == 0 && a.d <= 1536 && a.C <= 32 && a.P <= kMaxPhi && a.P % 8 == 0 && pad16(a.P) + 8 <= 256 &&
          a.cf <= kMaxConfirm && a.cf % 8 == 0 && a.K <= kMaxSuffix && a.L % 8 == 0 && a.B * a.Lf < ((int64_t)1 << 31);
 }
 
 int launch_score_tc(const ScoreArgs& a, cudaStream_t s) {
-  // the whole width in one block when its 96-row value ring fits next to the features (d <= 768), else halves
+  // the whole width in one block when its 96-row value ring fits next to the features (d <= 768), else parts that are
+  // multiples of 128 (the value MMAs' M)
   int nds = (a.d + 767) / 768;
-  while (a.d % (nds * 64) != 0) ++nds;
+  while (a.d % (nds * 128) != 0) ++nds;
   const int dpart = a.d / nds;
-  if (dpart / 8 > kGroupWarps * kMaxNt) return ASRN_ERR_UNSUPPORTED;
+  if (dpart / 128 > kMaxMt) return ASRN_ERR_UNSUPPORTED;
   const size_t smem = tc_smem_bytes(a.P, a.cf, dpart);
   if (smem > 227 * 1024) return ASRN_ERR_UNSUPPORTED;
   // feature rows as one-row boxes of the ring's padded pitch (the padding columns lie outside the tensor: zeros)

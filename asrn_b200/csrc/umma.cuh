@@ -101,6 +101,18 @@ ASRN_DEV uint64_t desc_sw128(uint32_t saddr) {
   d |= (uint64_t)2 << 61;                 // 128-byte swizzle
   return d;
 }
+// Shared-memory descriptor of an MN-major, 128-byte-swizzled operand: atoms of 64 MN elements (128 B) x 8 K rows
+// (1024 B, the 16-byte chunk index XOR-ed with the row within the atom), consecutive 8-row K groups 1024 B apart
+// (stride byte offset), consecutive 64-element MN blocks `mn_stride` bytes apart (leading byte offset).
+ASRN_DEV uint64_t desc_mn_sw128(uint32_t saddr, uint32_t mn_stride) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((mn_stride >> 4) & 0x3FFFu) << 16;   // leading byte offset: the next 64 MN elements
+  d |= (uint64_t)(1024 >> 4) << 32;                     // stride byte offset: the next 8 K rows
+  d |= (uint64_t)1 << 46;                               // descriptor version of sm_100
+  d |= (uint64_t)2 << 61;                               // 128-byte swizzle
+  return d;
+}
 // D[tmem] (+)= A[smem] x B[smem]^T, issued by one thread.
 ASRN_DEV void mma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
   asm volatile(
