@@ -10,7 +10,7 @@
 //
 // One block of 16 warps per (row, span of 512 slots), two warp groups working on consecutive sub-tiles at once:
 // in iteration i group A (warps 0-7) scores sub-tile i + 1 and takes its softmax, while group B (warps 8-15) has the
-// value products of sub-tile i computed by the tensor cores (one thread issues them) and reduces them into acc. The
+// value products of sub-tile i computed by the tensor cores (lane 0 of warp m issues M-tile m) and reduces them into acc. The
 // weights pass from A to B through a double buffer in the MMA's K-major swizzled layout; one block barrier per
 // iteration. Loads run ahead of use, issued by every warp after one named barrier: the sorted entries of sub-tile
 // i + 3 and the per-position scalars of i + 2 by cp.async, the phi / Qc / Kc rows of i + 2 by tensor-map row gathers
@@ -153,6 +153,11 @@ __device__ __forceinline__ void cp_async4(void* dst, const void* src) {
 }
 __device__ __forceinline__ void cp_async8(void* dst, const void* src) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(su32(dst)), "l"(src) : "memory");
+}
+// 16-byte reduction into global memory with no compiler memory barrier (nothing in the kernel reads acc back, so
+// the surrounding shared-memory loads may move across it).
+__device__ __forceinline__ void red_add_v4_nc(float* addr, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b), "f"(c), "f"(d));
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
@@ -450,7 +455,7 @@ __device__ __forceinline__ void tc_scores(const ScoreArgs& a, const TcSmem& S, c
   umma::fence_proxy_async();       // the weights are read by the tensor cores (async proxy) after the block barrier
 }
 
-// Group B: out^T = V^T . att^T for sub-tile t on tcgen05, reduced into acc. One thread issues the MMAs: M-tile mm
+// Group B: out^T = V^T . att^T for sub-tile t on tcgen05, reduced into acc. Lane 0 of warp mm issues M-tile mm
 // (rows 128 mm .. + 127 of d_part: two 64-column regions of the value ring, MN-major, 12 KB apart), K-step ks (window
 // keys 16 ks .. + 15: two 8-key groups of the ring, 1024 B apart), N = the 32 queries (att rows, K-major); D in TMEM
 // columns 32 mm .. + 31. Then warp w reads TMEM lanes 32 (w % 4) .. + 31 (32 rows of d) for M-tiles (w - 8) / 4,
@@ -461,28 +466,28 @@ __device__ __forceinline__ void tc_values(const ScoreArgs& a, const TcSmem& S, c
   const int lane = threadIdx.x & 31;
   const int lb = t * kQ;                        // window index of key 0 (li of slot q0 - 32)
   const int nM = k.dpart / 128;
-  if (w == 0 && lane == 0) {
+  if (w < nM && lane == 0) {                    // warp w issues M-tile w (its own commit on the shared barrier)
     umma::tc_fence_after();
     const uint32_t idesc = umma::idesc_bf16(128, kQ) | (1u << 15);      // A (the value rows) MN-major
-    const uint32_t v0 = su32(S.v), a0 = su32(S.att + (t & 1) * kQ * 128);
-    for (int mm = 0; mm < nM; ++mm) {
+    const uint32_t v0 = su32(S.v) + (uint32_t)(2 * w) * kVRegion, a0 = su32(S.att + (t & 1) * kQ * 128);
 #pragma unroll
-      for (int ks = 0; ks < 4; ++ks) {
-        const int r0 = vrow(lb + ks * 16);
-        const uint64_t adesc = umma::desc_mn_sw128(v0 + (uint32_t)(2 * mm) * kVRegion + (uint32_t)(r0 >> 3) * 1024,
-                                             (uint32_t)kVRegion);
-        const uint64_t bdesc = umma::desc_sw128(a0 + ks * 32);
-        umma::mma_bf16(tmem + (uint32_t)(mm * kQ), adesc, bdesc, idesc, ks > 0 ? 1u : 0u);
-      }
+    for (int ks = 0; ks < 4; ++ks) {
+      const int r0 = vrow(lb + ks * 16);
+      const uint64_t adesc = umma::desc_mn_sw128(v0 + (uint32_t)(r0 >> 3) * 1024, (uint32_t)kVRegion);
+      umma::mma_bf16(tmem + (uint32_t)(w * kQ), adesc, umma::desc_sw128(a0 + ks * 32), idesc, ks > 0 ? 1u : 0u);
     }
     umma::mma_commit(S.pvbar);
   }
+  // this lane's queries 4c + (lane & 3) after the transposes: their acc offsets, read before the waits
+  const int qd = lane & 3, g = lane >> 2;
+  const int64_t* qoff_s = S.qoff + (t & 1) * kQ;
+  int64_t qoff[kQ / 4];
+#pragma unroll
+  for (int c = 0; c < kQ / 4; ++c) qoff[c] = qoff_s[4 * c + qd];
   __syncwarp();
   umma::mbar_wait(S.pvbar, (uint32_t)(t & 1), a.status);
   umma::tc_fence_after();
   const int q4 = w & 3;
-  const int64_t* qoff = S.qoff + (t & 1) * kQ;
-  const int qd = lane & 3, g = lane >> 2;
   for (int mm = w >> 2; mm < nM; mm += 2) {
     float v[32];
     umma::tmem_ld32(tmem + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(mm * kQ), v);
@@ -499,8 +504,7 @@ __device__ __forceinline__ void tc_values(const ScoreArgs& a, const TcSmem& S, c
       r0 = __shfl_xor_sync(0xffffffffu, p0, 1);
       r1 = __shfl_xor_sync(0xffffffffu, p1, 1);
       if (qd & 1) { x0 = r0; x2 = r1; } else { x1 = r0; x3 = r1; }
-      const int64_t off = qoff[4 * c + qd];
-      if (off >= 0) red_add_v4(a.acc + off + dcol, x0, x1, x2, x3);
+      if (qoff[c] >= 0) red_add_v4_nc(a.acc + qoff[c] + dcol, x0, x1, x2, x3);
     }
   }
   umma::tc_fence_before();
@@ -538,7 +542,8 @@ k_score_tc(const __grid_constant__ CUtensorMap tm_phi, const __grid_constant__ C
     if (threadIdx.x <= kMaxSuffix) S.wsuf[threadIdx.x] = threadIdx.x <= a.K ? a.w_suf[threadIdx.x] : 0.f;
     umma::fence_proxy_async();                 // the zeros precede the tensor-map copies into the same rows
     if (threadIdx.x == 0) {
-      for (int i = 0; i < 5; ++i) umma::mbar_init(S.fbar + i, 1);   // 4 feature stages, the value-product MMAs
+      for (int i = 0; i < 4; ++i) umma::mbar_init(S.fbar + i, 1);   // 4 feature stages
+      umma::mbar_init(S.pvbar, (uint32_t)(k.dpart / 128));           // one commit per M-tile's issuing warp
       umma::fence_mbar_init();
     }
     if (wid == kGroupWarps) {
