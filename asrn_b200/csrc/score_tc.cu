@@ -211,57 +211,58 @@ __device__ __forceinline__ void tc_stage1(const ScoreArgs& a, const TcSmem& S, c
   }
 }
 
-// Scalars and feature rows of sub-tile t, spread over the 16 warps. Warp w takes slots 2w and 2w + 1 (lanes 0 and 1):
-// it derives (position, id, used) from the staging buffer, writes them to the feature ring and copies the slot's
-// clock (8 B), log_alfa (4 B) and its kMaxSuffix previous signatures (4 B; NaN, never equal, before the text and past
-// K) by cp.async. The phi, Qc and Kc rows move as tensor-map row gathers of four slots each: lane 0 of warps 0-7
-// issues the three gathers of slots 4w .. 4w + 3, counted on the stage's mbarrier (its byte count is set by thread 0
-// beforehand, expect_features); a slot outside the row reads zero rows (row coordinate -1), and the ring's padding
-// columns beyond P / cf are zero-filled by the same copies.
+// Scalars and feature rows of sub-tile t, spread over the 16 warps and their lanes. Warp w takes slots 2w and 2w + 1:
+// one lane derives (position, id, used) from the staging buffer and writes them to the feature ring, others copy the
+// slot's clock (8 B), log_alfa (4 B) and its kMaxSuffix previous signatures (4 B each; NaN, never equal, before the
+// text and past K) by cp.async. The phi, Qc and Kc rows move as tensor-map row gathers of four slots each: three lanes
+// of warps 0-7 issue the three gathers of slots 4w .. 4w + 3 in one instruction, counted on the stage's mbarrier (its
+// byte count is set by thread 0 beforehand, expect_features); a slot outside the row reads zero rows (row coordinate
+// -1), and the ring's padding columns beyond P / cf are zero-filled by the same copies.
 __device__ __forceinline__ void tc_stage2_features(const ScoreArgs& a, const TcSmem& S, const TcBlock& k, int t,
                                                    const CUtensorMap* tm_phi, const CUtensorMap* tm_qc,
                                                    const CUtensorMap* tm_kc) {
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const int buf = (t + 1) % kStage;
   const int64_t s0 = k.S0 + (int64_t)t * kQ;
-  if (lane < 2) {
-    const int i = 2 * wid + lane;
-    const int64_t s = s0 + i;
-    const int fr = frow((t + 1) * kQ + i);
-    const bool real = s >= 0 && s < a.L;
-    const int pos = real ? S.st_pos[buf * kQ + i] : 0;
+  // lanes 0-15 serve slot 2w, lanes 16-31 slot 2w + 1; within a half, lane j copies previous signature j (j < 8),
+  // the clock (j == 8), log_alfa (j == 9), and lane 10 writes (position, id, used)
+  const int i = 2 * wid + (lane >> 4), j = lane & 15;
+  const int64_t s = s0 + i;
+  const int fr = frow((t + 1) * kQ + i);
+  const bool real = s >= 0 && s < a.L;
+  const int pos = real ? S.st_pos[buf * kQ + i] : 0;
+  const int64_t g = k.b * a.Lf + pos;
+  if (j < kMaxSuffix) {
+    const int64_t tt = (int64_t)pos - 1 - j;
+    if (real && j < a.K && tt >= 0) cp_async4(S.pf + fr * kMaxSuffix + j, a.sig + k.b * a.Lf + tt);
+    else S.pf[fr * kMaxSuffix + j] = __int_as_float(0x7fc00000);
+  } else if (j == 8) {
+    if (real) cp_async8(S.bt + fr, a.Bt + g);
+    else S.bt[fr] = 0.0;
+  } else if (j == 9) {
+    if (real) cp_async4(S.la + fr, a.log_alfa + g);
+    else S.la[fr] = 0.f;
+  } else if (j == 10) {
     const int id = real ? (int)S.st_id[buf * kStageIds + i] : -1;
     const bool used = real && s + 1 < a.L && (int)S.st_id[buf * kStageIds + i + 1] == id && pos + 1 < a.Lf;
     S.pos[fr] = pos;
     S.id[fr] = id;
     S.used[fr] = used ? 1 : 0;
-    const int64_t g = k.b * a.Lf + pos;
-    if (real) {
-      cp_async8(S.bt + fr, a.Bt + g);
-      cp_async4(S.la + fr, a.log_alfa + g);
-    } else {
-      S.bt[fr] = 0.0;
-      S.la[fr] = 0.f;
-    }
-#pragma unroll
-    for (int c = 0; c < kMaxSuffix; ++c) {
-      const int64_t tt = (int64_t)pos - 1 - c;
-      if (real && c < a.K && tt >= 0) cp_async4(S.pf + fr * kMaxSuffix + c, a.sig + k.b * a.Lf + tt);
-      else S.pf[fr * kMaxSuffix + c] = __int_as_float(0x7fc00000);
-    }
-  } else if (lane == 2 && wid < kQ / 4) {
+  } else if (j >= 11 && j < 14 && lane < 16 && wid < kQ / 4) {
+    // lanes 11, 12, 13 of warps 0-7: the phi, Qc and Kc rows of slots 4w .. 4w + 3 (one gather instruction)
     int y[4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int i = 4 * wid + j;
-      const int64_t s = s0 + i;
-      y[j] = (s >= 0 && s < a.L) ? (int)(k.b * a.Lf + S.st_pos[buf * kQ + i]) : -1;
+    for (int q = 0; q < 4; ++q) {
+      const int iq = 4 * wid + q;
+      const int64_t sq = s0 + iq;
+      y[q] = (sq >= 0 && sq < a.L) ? (int)(k.b * a.Lf + S.st_pos[buf * kQ + iq]) : -1;
     }
     uint64_t* bar = S.fbar + ((t + 1) & 3);
     const int fr0 = frow((t + 1) * kQ + 4 * wid);
-    gather4_rows(S.phi + S.prow(fr0), tm_phi, y[0], y[1], y[2], y[3], bar);
-    gather4_rows(S.qc + S.crow(fr0), tm_qc, y[0], y[1], y[2], y[3], bar);
-    gather4_rows(S.kc + S.crow(fr0), tm_kc, y[0], y[1], y[2], y[3], bar);
+    const CUtensorMap* map = j == 11 ? tm_phi : (j == 12 ? tm_qc : tm_kc);
+    void* dst = j == 11 ? (void*)(S.phi + S.prow(fr0)) : (j == 12 ? (void*)(S.qc + S.crow(fr0))
+                                                                 : (void*)(S.kc + S.crow(fr0)));
+    gather4_rows(dst, map, y[0], y[1], y[2], y[3], bar);
   }
 }
 
