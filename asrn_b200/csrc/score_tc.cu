@@ -48,39 +48,41 @@ struct TcSmem {
   double* bt;           // [kRF]
   float* la;            // [kRF]
   float* pf;            // [kRF][kMaxSuffix]
-  __nv_bfloat16* phi;   // [kRF][Pp]
-  __nv_bfloat16* qc;    // [kRF][Cp]
-  __nv_bfloat16* kc;    // [kRF][Cp]
+  uint8_t* phi;         // [nbp][kRF rows][128 B]: column blocks of 64 features, 128-byte swizzle
+  uint8_t* qc;          // [kRF rows][64 B], 64-byte swizzle
+  uint8_t* kc;          // [kRF rows][64 B]
   uint8_t* v;           // [d_part / 64][kRV rows][128 B], MN-major 128-byte swizzle (1024-byte aligned)
-  float* sc;            // [32][65]
+  float* sc;            // [32][64], key column kj of query qi at kj ^ sc_swz(qi)
   uint8_t* att;         // [2][32 rows][128 B], K-major 128-byte swizzle (1024-byte aligned)
   int64_t* qoff;        // [2][32] acc element offset of the query's row, or -1 (no candidate / not this shard's)
   float* wsuf;          // [kMaxSuffix + 1] suffix weights w_sufijo
   uint64_t* fbar;       // [4] feature-stage mbarriers (one per 32-row stage of the feature ring)
   uint64_t* pvbar;      // value-product MMAs done
   uint32_t* tmem;       // TMEM base address
-  int Pp, Cp, Dp;        // row pitches (elements)
-  int Gp, Gc;            // 4-row group strides of the phi and Qc / Kc rings (elements)
-  __device__ __forceinline__ int prow(int fr) const { return (fr >> 2) * Gp + (fr & 3) * Pp; }
-  __device__ __forceinline__ int crow(int fr) const { return (fr >> 2) * Gc + (fr & 3) * Cp; }
+  int nbp;               // phi column blocks
+  int Dp;
 };
 
 __host__ __device__ inline int pad16(int x) { return (x + 15) / 16 * 16; }
-// Feature rings: rows of the padded pitch (an odd number of 16-byte chunks: the 4 rows of a group fall in distinct
-// bank groups) in groups of 4 rows -- one row gather -- each group starting on a 128-byte boundary.
-__host__ __device__ inline int group_elems(int pitch) { return (4 * pitch * 2 + 127) / 128 * 128 / 2; }
+// Feature rings, written by tensor-map row gathers with the map's swizzle so that the 8 rows of an ldmatrix fall in 8
+// distinct bank groups (a gather's 4 rows start on a 128-byte boundary): phi in column blocks of 64 features, rows of
+// 128 B with the 128-byte swizzle (16-byte chunk c of ring row r at chunk c ^ (r mod 8)); Qc / Kc (cf <= 32) in rows
+// of 64 B with the 64-byte swizzle (chunk c of row r at c ^ ((r / 2) mod 4)).
+__host__ __device__ inline int ring_blocks(int cols) { return (pad16(cols) * 2 + 127) / 128; }
+__host__ __device__ inline int ring_bytes_phi(int P) { return ring_blocks(P) * kRF * 128; }
+constexpr int kRingBytesC = kRF * 64;
+__host__ __device__ inline int sc_swz(int qi) { return (qi & 1) | (((qi >> 1) & 3) << 3); }
 
 __host__ __device__ inline size_t tc_smem_bytes(int P, int cf, int dpart) {
-  const int Pp = pad16(P) + 8, Cp = pad16(cf) + 8;
   size_t b = 1024;                               // alignment slack of the dynamic shared memory base
   b += (size_t)(dpart / 64) * kVRegion + 2 * kQ * 128;
-  b += (size_t)(kRF / 4) * (group_elems(Pp) + 2 * group_elems(Cp)) * 2;
+  b += (size_t)ring_bytes_phi(P) + 2 * (size_t)kRingBytesC;
   b += kStage * kQ * 4 + kStage * kStageIds * 2;
   b = (b + 15) / 16 * 16;
   b += kRF * 8;                                  // bt
   b += kRF * 4 * (size_t)kMaxSuffix;             // pf
   b += kRF * 4 * 4;                              // pos, id, used, la
-  b += (size_t)kQ * 65 * 4;
+  b += (size_t)kQ * 64 * 4;
   b += 2 * kQ * 8;                               // qoff
   b += (kMaxSuffix + 8) * 4;
   b = (b + 15) / 16 * 16;
@@ -90,18 +92,15 @@ __host__ __device__ inline size_t tc_smem_bytes(int P, int cf, int dpart) {
 
 __device__ inline TcSmem carve_tc(char* base, int P, int cf, int dpart) {
   TcSmem s;
-  s.Pp = pad16(P) + 8;
-  s.Cp = pad16(cf) + 8;
+  s.nbp = ring_blocks(P);
   s.Dp = dpart;
-  s.Gp = group_elems(s.Pp);
-  s.Gc = group_elems(s.Cp);
   base += (1024 - (__cvta_generic_to_shared(base) & 1023)) & 1023;
   char* p = base;
   s.v = reinterpret_cast<uint8_t*>(p); p += (size_t)(dpart / 64) * kVRegion;
   s.att = reinterpret_cast<uint8_t*>(p); p += 2 * kQ * 128;
-  s.phi = reinterpret_cast<__nv_bfloat16*>(p); p += (size_t)(kRF / 4) * s.Gp * 2;
-  s.qc = reinterpret_cast<__nv_bfloat16*>(p); p += (size_t)(kRF / 4) * s.Gc * 2;
-  s.kc = reinterpret_cast<__nv_bfloat16*>(p); p += (size_t)(kRF / 4) * s.Gc * 2;
+  s.phi = reinterpret_cast<uint8_t*>(p); p += ring_bytes_phi(P);
+  s.qc = reinterpret_cast<uint8_t*>(p); p += kRingBytesC;
+  s.kc = reinterpret_cast<uint8_t*>(p); p += kRingBytesC;
   s.st_pos = reinterpret_cast<int*>(p); p += kStage * kQ * 4;
   s.st_id = reinterpret_cast<uint16_t*>(p); p += kStage * kStageIds * 2;
   p = base + ((p - base) + 15) / 16 * 16;
@@ -111,7 +110,7 @@ __device__ inline TcSmem carve_tc(char* base, int P, int cf, int dpart) {
   s.id = reinterpret_cast<int*>(p); p += kRF * 4;
   s.used = reinterpret_cast<int*>(p); p += kRF * 4;
   s.la = reinterpret_cast<float*>(p); p += kRF * 4;
-  s.sc = reinterpret_cast<float*>(p); p += kQ * 65 * 4;
+  s.sc = reinterpret_cast<float*>(p); p += kQ * 64 * 4;
   s.qoff = reinterpret_cast<int64_t*>(p); p += 2 * kQ * 8;
   s.wsuf = reinterpret_cast<float*>(p); p += (kMaxSuffix + 8) * 4;
   p = base + ((p - base) + 15) / 16 * 16;
@@ -133,13 +132,13 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
                ::"r"(su32(dst)), "l"(src), "r"(bytes), "r"(su32(bar))
                : "memory");
 }
-// Four rows (row coordinates y0..y3, column 0) of a 2-D tensor map into consecutive rows at dst (the map's box is one
-// row of the ring's padded pitch), counted on `bar`; rows outside the tensor read zeros.
-__device__ __forceinline__ void gather4_rows(void* dst, const CUtensorMap* map, int y0, int y1, int y2, int y3,
+// Four rows (row coordinates y0..y3, columns x .. x + box) of a 2-D tensor map into consecutive ring rows at dst
+// (the map's box is one ring row), counted on `bar`; rows and columns outside the tensor read zeros.
+__device__ __forceinline__ void gather4_rows(void* dst, const CUtensorMap* map, int x, int y0, int y1, int y2, int y3,
                                              uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, "
-      "%4, %5, %6}], [%7];" ::"r"(su32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(y0), "r"(y1), "r"(y2),
+      "%4, %5, %6}], [%7];" ::"r"(su32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y0), "r"(y1), "r"(y2),
       "r"(y3), "r"(su32(bar))
       : "memory");
 }
@@ -248,8 +247,10 @@ __device__ __forceinline__ void tc_stage2_features(const ScoreArgs& a, const TcS
     S.pos[fr] = pos;
     S.id[fr] = id;
     S.used[fr] = used ? 1 : 0;
-  } else if (j >= 11 && j < 14 && lane < 16 && wid < kQ / 4) {
-    // lanes 11, 12, 13 of warps 0-7: the phi, Qc and Kc rows of slots 4w .. 4w + 3 (one gather instruction)
+  } else if (j >= 11 && wid < kQ / 4 && (lane >> 4) * 5 + j - 11 < S.nbp + 2) {
+    // lanes 11-15 and 27-31 of warps 0-7: gather gi of slots 4w .. 4w + 3 (phi column blocks, then Qc and Kc) in one
+    // instruction
+    const int gi = (lane >> 4) * 5 + j - 11;
     int y[4];
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
@@ -259,10 +260,10 @@ __device__ __forceinline__ void tc_stage2_features(const ScoreArgs& a, const TcS
     }
     uint64_t* bar = S.fbar + ((t + 1) & 3);
     const int fr0 = frow((t + 1) * kQ + 4 * wid);
-    const CUtensorMap* map = j == 11 ? tm_phi : (j == 12 ? tm_qc : tm_kc);
-    void* dst = j == 11 ? (void*)(S.phi + S.prow(fr0)) : (j == 12 ? (void*)(S.qc + S.crow(fr0))
-                                                                 : (void*)(S.kc + S.crow(fr0)));
-    gather4_rows(dst, map, y[0], y[1], y[2], y[3], bar);
+    const int nbp = S.nbp;
+    const CUtensorMap* map = gi < nbp ? tm_phi : (gi == nbp ? tm_qc : tm_kc);
+    uint8_t* dst = gi < nbp ? S.phi + ((gi * kRF + fr0) << 7) : (gi == nbp ? S.qc : S.kc) + (fr0 << 6);
+    gather4_rows(dst, map, gi < nbp ? gi * 64 : 0, y[0], y[1], y[2], y[3], bar);
   }
 }
 
@@ -302,42 +303,53 @@ __device__ __forceinline__ void tc_scores(const ScoreArgs& a, const TcSmem& S, c
   for (int mt = 0; mt < 2; ++mt) band[mt] = nt * 8 + 7 >= mt * 16 + 32 - C && nt * 8 < mt * 16 + 16 + 32;
   float cphi[2][4] = {}, cqk[2][4] = {};
   if (band[0] || band[1]) {
-    const int ka = (lane >> 4) * 8;
+    // ldmatrix row addresses: A (queries) rows lane & 15, chunk half lane >> 4; B (keys) rows lane & 7, chunk half
+    // (lane >> 3) & 1
+    const int ha = lane >> 4, hb = (lane >> 3) & 1;
     const int rk = frow(lb + nt * 8 + (lane & 7));
-    const int kb = ((lane >> 3) & 1) * 8;
     const int ra0 = frow(lb + kQ + (lane & 15)), ra1 = frow(lb + kQ + 16 + (lane & 15));
-    const uint32_t phi_b = su32(S.phi) + 2u * (uint32_t)(S.prow(rk) + kb);
-    const uint32_t kc_b = su32(S.kc) + 2u * (uint32_t)(S.crow(rk) + kb);
-    const uint32_t phi_a0 = su32(S.phi) + 2u * (uint32_t)(S.prow(ra0) + ka);
-    const uint32_t phi_a1 = su32(S.phi) + 2u * (uint32_t)(S.prow(ra1) + ka);
-    const uint32_t qc_a0 = su32(S.qc) + 2u * (uint32_t)(S.crow(ra0) + ka);
-    const uint32_t qc_a1 = su32(S.qc) + 2u * (uint32_t)(S.crow(ra1) + ka);
-    for (int k0 = 0; k0 < k.Ppad; k0 += 16) {
-      uint32_t b0, b1;
-      ldsm_x2(phi_b + 2 * k0, b0, b1);
-      if (band[0]) {
-        uint32_t a0, a1, a2, a3;
-        ldsm_x4(phi_a0 + 2 * k0, a0, a1, a2, a3);
-        mma16816(cphi[0], a0, a1, a2, a3, b0, b1);
-      }
-      if (band[1]) {
-        uint32_t a0, a1, a2, a3;
-        ldsm_x4(phi_a1 + 2 * k0, a0, a1, a2, a3);
-        mma16816(cphi[1], a0, a1, a2, a3, b0, b1);
+    // per row: its ring address and (chunk half ^ the row's swizzle) << 4; chunk 2 i + h of the row then sits at
+    // row + ((2 i mod 8) << 4 ^ that) in column block 2 i / 8
+    const uint32_t pb = su32(S.phi) + (rk << 7), pbx = (uint32_t)((hb ^ (rk & 7)) << 4);
+    const uint32_t pa0 = su32(S.phi) + (ra0 << 7), pa0x = (uint32_t)((ha ^ (ra0 & 7)) << 4);
+    const uint32_t pa1 = su32(S.phi) + (ra1 << 7), pa1x = (uint32_t)((ha ^ (ra1 & 7)) << 4);
+    const uint32_t cb = su32(S.kc) + (rk << 6), cbx = (uint32_t)((hb ^ ((rk >> 1) & 3)) << 4);
+    const uint32_t ca0 = su32(S.qc) + (ra0 << 6), ca0x = (uint32_t)((ha ^ ((ra0 >> 1) & 3)) << 4);
+    const uint32_t ca1 = su32(S.qc) + (ra1 << 6), ca1x = (uint32_t)((ha ^ ((ra1 >> 1) & 3)) << 4);
+#pragma unroll
+    for (int i = 0; i < kMaxPhi / 16; ++i) {
+      if (16 * i < k.Ppad) {
+        const uint32_t blk = (uint32_t)((2 * i) >> 3) * (kRF * 128), cx = (uint32_t)(((2 * i) & 7) << 4);
+        uint32_t b0, b1;
+        ldsm_x2(pb + blk + (cx ^ pbx), b0, b1);
+        if (band[0]) {
+          uint32_t a0, a1, a2, a3;
+          ldsm_x4(pa0 + blk + (cx ^ pa0x), a0, a1, a2, a3);
+          mma16816(cphi[0], a0, a1, a2, a3, b0, b1);
+        }
+        if (band[1]) {
+          uint32_t a0, a1, a2, a3;
+          ldsm_x4(pa1 + blk + (cx ^ pa1x), a0, a1, a2, a3);
+          mma16816(cphi[1], a0, a1, a2, a3, b0, b1);
+        }
       }
     }
-    for (int k0 = 0; k0 < k.Cpad; k0 += 16) {
-      uint32_t b0, b1;
-      ldsm_x2(kc_b + 2 * k0, b0, b1);
-      if (band[0]) {
-        uint32_t a0, a1, a2, a3;
-        ldsm_x4(qc_a0 + 2 * k0, a0, a1, a2, a3);
-        mma16816(cqk[0], a0, a1, a2, a3, b0, b1);
-      }
-      if (band[1]) {
-        uint32_t a0, a1, a2, a3;
-        ldsm_x4(qc_a1 + 2 * k0, a0, a1, a2, a3);
-        mma16816(cqk[1], a0, a1, a2, a3, b0, b1);
+#pragma unroll
+    for (int i = 0; i < kMaxConfirm / 16; ++i) {
+      if (16 * i < k.Cpad) {
+        const uint32_t cx = (uint32_t)(((2 * i) & 3) << 4);
+        uint32_t b0, b1;
+        ldsm_x2(cb + (cx ^ cbx), b0, b1);
+        if (band[0]) {
+          uint32_t a0, a1, a2, a3;
+          ldsm_x4(ca0 + (cx ^ ca0x), a0, a1, a2, a3);
+          mma16816(cqk[0], a0, a1, a2, a3, b0, b1);
+        }
+        if (band[1]) {
+          uint32_t a0, a1, a2, a3;
+          ldsm_x4(ca1 + (cx ^ ca1x), a0, a1, a2, a3);
+          mma16816(cqk[1], a0, a1, a2, a3, b0, b1);
+        }
       }
     }
   }
@@ -392,7 +404,7 @@ __device__ __forceinline__ void tc_scores(const ScoreArgs& a, const TcSmem& S, c
       t1 = __fadd_rn(t1, k_la[uk]);
       const float dt = __double2float_rn(k_bt[uk] - q_bt[uq]);
       const float val = ok ? __fadd_rn(t1, __fmul_rn(dt, k.tasa)) : -INFINITY;
-      S.sc[qi * 65 + kj] = val;
+      S.sc[qi * 64 + (kj ^ sc_swz(qi))] = val;
     }
   }
   bar_group_a();
@@ -404,8 +416,8 @@ __device__ __forceinline__ void tc_scores(const ScoreArgs& a, const TcSmem& S, c
   unsigned bal[4];
 #pragma unroll
   for (int u = 0; u < 4; ++u) {
-    x[u][0] = S.sc[(qa + u) * 65 + lane];
-    x[u][1] = S.sc[(qa + u) * 65 + lane + 32];
+    x[u][0] = S.sc[(qa + u) * 64 + (lane ^ sc_swz(qa + u))];
+    x[u][1] = S.sc[(qa + u) * 64 + ((lane + 32) ^ sc_swz(qa + u))];
     bal[u] = __ballot_sync(0xffffffffu, x[u][0] != -INFINITY || x[u][1] != -INFINITY);
     m[u] = fmaxf(x[u][0], x[u][1]);
   }
@@ -558,7 +570,7 @@ k_score_tc(const __grid_constant__ CUtensorMap tm_phi, const __grid_constant__ C
   };
   // the stage's transaction count is set by thread 0 before any copy of the stage is issued
   auto expect_features = [&](int t) {
-    if (threadIdx.x == 0) umma::mbar_expect_tx(S.fbar + ((t + 1) & 3), (uint32_t)(kQ * (S.Pp + 2 * S.Cp) * 2));
+    if (threadIdx.x == 0) umma::mbar_expect_tx(S.fbar + ((t + 1) & 3), (uint32_t)(kQ * (S.nbp * 128 + 2 * 64)));
   };
   // this thread's cp.async copies (scalars, value rows) complete, then made visible to the tensor cores
   auto wait_copies = [&]() {
@@ -632,7 +644,7 @@ k_score_tc(const __grid_constant__ CUtensorMap tm_phi, const __grid_constant__ C
 }
 
 bool score_tc_supported(const ScoreArgs& a) {
-  return a.d % 128 == 0 && a.d <= 1536 && a.C <= 32 && a.P <= kMaxPhi && a.P % 8 == 0 && pad16(a.P) + 8 <= 256 &&
+  return a.d % 128 == 0 && a.d <= 1536 && a.C <= 32 && a.P <= kMaxPhi && a.P % 8 == 0 &&
          a.cf <= kMaxConfirm && a.cf % 8 == 0 && a.K <= kMaxSuffix && a.L % 8 == 0 && a.B * a.Lf < ((int64_t)1 << 31);
 }
 
@@ -645,12 +657,13 @@ int launch_score_tc(const ScoreArgs& a, cudaStream_t s) {
   if (dpart / 128 > kMaxMt) return ASRN_ERR_UNSUPPORTED;
   const size_t smem = tc_smem_bytes(a.P, a.cf, dpart);
   if (smem > 227 * 1024) return ASRN_ERR_UNSUPPORTED;
-  // feature rows as one-row boxes of the ring's padded pitch (the padding columns lie outside the tensor: zeros)
+  // feature rows as one-row boxes of one ring row (64 phi features / 32 Qc, Kc features with the ring's swizzle;
+  // columns past P / cf read zeros)
   CUtensorMap tm_phi, tm_qc, tm_kc;
   const uint64_t rows = (uint64_t)(a.B * a.Lf);
-  if (!make_tmap_rows_bf16(&tm_phi, a.phi, (uint64_t)a.P, rows, (uint64_t)a.P * 2, (uint32_t)(pad16(a.P) + 8)) ||
-      !make_tmap_rows_bf16(&tm_qc, a.Qc, (uint64_t)a.cf, rows, (uint64_t)a.cf * 2, (uint32_t)(pad16(a.cf) + 8)) ||
-      !make_tmap_rows_bf16(&tm_kc, a.Kc, (uint64_t)a.cf, rows, (uint64_t)a.cf * 2, (uint32_t)(pad16(a.cf) + 8)))
+  if (!make_tmap_rows_bf16(&tm_phi, a.phi, (uint64_t)a.P, rows, (uint64_t)a.P * 2, 64, 128) ||
+      !make_tmap_rows_bf16(&tm_qc, a.Qc, (uint64_t)a.cf, rows, (uint64_t)a.cf * 2, 32, 64) ||
+      !make_tmap_rows_bf16(&tm_kc, a.Kc, (uint64_t)a.cf, rows, (uint64_t)a.cf * 2, 32, 64))
     return ASRN_ERR_CUDA;
   cudaFuncSetAttribute(k_score_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   dim3 grid((unsigned)(((a.L + kSpanTc - 1) / kSpanTc) * nds), (unsigned)(a.B * a.T));

@@ -36,9 +36,13 @@ bool make_tmap_bf16(void* map, const void* base, uint64_t inner, uint64_t outer,
 }
 
 // Rows of a (outer, inner) bf16 matrix for row gathers: box = one row of box_inner elements (box_inner may exceed
-// inner: the columns past it read zeros), no swizzle.
+// inner: the columns past it read zeros), with the shared-memory swizzle of swizzle_bytes (0: none).
 bool make_tmap_rows_bf16(void* map, const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes,
-                         uint32_t box_inner) {
+                         uint32_t box_inner, int swizzle_bytes) {
+  const CUtensorMapSwizzle swz = swizzle_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                 : swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                 : swizzle_bytes == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
+                                                       : CU_TENSOR_MAP_SWIZZLE_NONE;
   PFN_cuTensorMapEncodeTiled_v12000 fn = encode_fn();
   if (!fn) return false;
   cuuint64_t dims[2] = {inner, outer};
@@ -46,7 +50,7 @@ bool make_tmap_rows_bf16(void* map, const void* base, uint64_t inner, uint64_t o
   cuuint32_t box[2] = {box_inner, 1};
   cuuint32_t elem[2] = {1, 1};
   CUresult r = fn(reinterpret_cast<CUtensorMap*>(map), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base),
-                  dims, strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                  dims, strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
