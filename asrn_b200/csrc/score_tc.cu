@@ -32,8 +32,10 @@ constexpr int kQ = 32;           // queries per sub-tile
 constexpr int kRF = 128;         // feature ring: 4 sub-tiles (score windows of i and i + 1, prefetch of i + 2)
 constexpr int kRV = 96;          // value ring: 3 sub-tiles (window of i, prefetch of i + 1)
 constexpr int kSpanTc = 512;     // sorted slots per block
-constexpr int kThreadsTc = 512;  // 16 warps: two groups of 8
-constexpr int kGroupWarps = 8;
+constexpr int kGroupWarps = 8;   // warps 0-7: scores (group A); 8-15: value products (group B)
+constexpr int kLoadWarps = 2;    // warps 16-17: every copy into shared memory (the load group)
+constexpr int kLoadThreads = kLoadWarps * 32;
+constexpr int kThreadsTc = (2 * kGroupWarps + kLoadWarps) * 32;
 constexpr int kMaxMt = 6;        // M = 128 tiles of d_part (d_part <= 768)
 constexpr int kVRegion = kRV * 128;   // one 64-column region of the value ring (bytes)
 constexpr int kStage = 3;        // staging buffers of sorted-row entries
@@ -195,9 +197,8 @@ struct TcBlock {
 }  // namespace
 
 // Sorted entries of sub-tile t (slots [S0 + 32 t, + 32 / 40)) into staging buffer (t + 1) % kStage by 16-byte
-// cp.async (zero-filled outside [0, L); rows are 16-byte aligned: L % 8 == 0). Threads 0-7 copy orden, 8-12 ids.
-__device__ __forceinline__ void tc_stage1(const ScoreArgs& a, const TcSmem& S, const TcBlock& k, int t) {
-  const int tid = threadIdx.x;
+// cp.async (zero-filled outside [0, L); rows are 16-byte aligned: L % 8 == 0). Load threads 0-7 copy orden, 8-12 ids.
+__device__ __forceinline__ void tc_stage1(const ScoreArgs& a, const TcSmem& S, const TcBlock& k, int t, int tid) {
   const int buf = (t + 1) % kStage;
   const int64_t s0 = k.S0 + (int64_t)t * kQ;
   if (tid < kQ / 4) {
@@ -212,56 +213,58 @@ __device__ __forceinline__ void tc_stage1(const ScoreArgs& a, const TcSmem& S, c
   }
 }
 
-// Scalars and feature rows of sub-tile t, spread over the 16 warps and their lanes. Warp w takes slots 2w and 2w + 1:
-// one lane derives (position, id, used) from the staging buffer and writes them to the feature ring, others copy the
-// slot's clock (8 B), log_alfa (4 B) and its kMaxSuffix previous signatures (4 B each; NaN, never equal, before the
-// text and past K) by cp.async. The phi, Qc and Kc rows move as tensor-map row gathers of four slots each: three lanes
-// of warps 0-7 issue the three gathers of slots 4w .. 4w + 3 in one instruction, counted on the stage's mbarrier (its
-// byte count is set by thread 0 beforehand, expect_features); a slot outside the row reads zero rows (row coordinate
-// -1), and the ring's padding columns beyond P / cf are zero-filled by the same copies.
-__device__ __forceinline__ void tc_stage2_features(const ScoreArgs& a, const TcSmem& S, const TcBlock& k, int t,
+// Scalars and feature rows of sub-tile t, issued by the load group (thread pt of kLoadThreads). Thread pt takes slot
+// pt / 2: even threads copy its kMaxSuffix previous signatures (4 B each by cp.async; NaN, never equal, before the text
+// and past K), odd threads its clock (8 B) and log_alfa (4 B) and write (position, id, used) from the staging buffer.
+// The phi, Qc and Kc rows move as tensor-map row gathers of four slots each: thread pt < 8 (nbp + 2) issues gather
+// pt / 8 (phi column blocks, then Qc, then Kc) of slots 4 (pt % 8) .. + 3, counted on the stage's mbarrier (its byte
+// count is set beforehand, expect_features); a slot outside the row reads zero rows (row coordinate -1), and the
+// columns past P / cf read zeros.
+__device__ __forceinline__ void tc_stage2_features(const ScoreArgs& a, const TcSmem& S, const TcBlock& k, int t, int pt,
                                                    const CUtensorMap* tm_phi, const CUtensorMap* tm_qc,
                                                    const CUtensorMap* tm_kc) {
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const int buf = (t + 1) % kStage;
   const int64_t s0 = k.S0 + (int64_t)t * kQ;
-  // lanes 0-15 serve slot 2w, lanes 16-31 slot 2w + 1; within a half, lane j copies previous signature j (j < 8),
-  // the clock (j == 8), log_alfa (j == 9), and lane 10 writes (position, id, used)
-  const int i = 2 * wid + (lane >> 4), j = lane & 15;
-  const int64_t s = s0 + i;
-  const int fr = frow((t + 1) * kQ + i);
-  const bool real = s >= 0 && s < a.L;
-  const int pos = real ? S.st_pos[buf * kQ + i] : 0;
-  const int64_t g = k.b * a.Lf + pos;
-  if (j < kMaxSuffix) {
-    const int64_t tt = (int64_t)pos - 1 - j;
-    if (real && j < a.K && tt >= 0) cp_async4(S.pf + fr * kMaxSuffix + j, a.sig + k.b * a.Lf + tt);
-    else S.pf[fr * kMaxSuffix + j] = __int_as_float(0x7fc00000);
-  } else if (j == 8) {
-    if (real) cp_async8(S.bt + fr, a.Bt + g);
-    else S.bt[fr] = 0.0;
-  } else if (j == 9) {
-    if (real) cp_async4(S.la + fr, a.log_alfa + g);
-    else S.la[fr] = 0.f;
-  } else if (j == 10) {
-    const int id = real ? (int)S.st_id[buf * kStageIds + i] : -1;
-    const bool used = real && s + 1 < a.L && (int)S.st_id[buf * kStageIds + i + 1] == id && pos + 1 < a.Lf;
-    S.pos[fr] = pos;
-    S.id[fr] = id;
-    S.used[fr] = used ? 1 : 0;
-  } else if (j >= 11 && wid < kQ / 4 && (lane >> 4) * 5 + j - 11 < S.nbp + 2) {
-    // lanes 11-15 and 27-31 of warps 0-7: gather gi of slots 4w .. 4w + 3 (phi column blocks, then Qc and Kc) in one
-    // instruction
-    const int gi = (lane >> 4) * 5 + j - 11;
+  {
+    const int i = pt >> 1;
+    const int64_t s = s0 + i;
+    const int fr = frow((t + 1) * kQ + i);
+    const bool real = s >= 0 && s < a.L;
+    const int pos = real ? S.st_pos[buf * kQ + i] : 0;
+    if ((pt & 1) == 0) {
+#pragma unroll
+      for (int j = 0; j < kMaxSuffix; ++j) {
+        const int64_t tt = (int64_t)pos - 1 - j;
+        if (real && j < a.K && tt >= 0) cp_async4(S.pf + fr * kMaxSuffix + j, a.sig + k.b * a.Lf + tt);
+        else S.pf[fr * kMaxSuffix + j] = __int_as_float(0x7fc00000);
+      }
+    } else {
+      const int64_t g = k.b * a.Lf + pos;
+      if (real) {
+        cp_async8(S.bt + fr, a.Bt + g);
+        cp_async4(S.la + fr, a.log_alfa + g);
+      } else {
+        S.bt[fr] = 0.0;
+        S.la[fr] = 0.f;
+      }
+      const int id = real ? (int)S.st_id[buf * kStageIds + i] : -1;
+      const bool used = real && s + 1 < a.L && (int)S.st_id[buf * kStageIds + i + 1] == id && pos + 1 < a.Lf;
+      S.pos[fr] = pos;
+      S.id[fr] = id;
+      S.used[fr] = used ? 1 : 0;
+    }
+  }
+  if (pt < 8 * (S.nbp + 2)) {
+    const int grp = pt & 7, gi = pt >> 3;
     int y[4];
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
-      const int iq = 4 * wid + q;
+      const int iq = 4 * grp + q;
       const int64_t sq = s0 + iq;
       y[q] = (sq >= 0 && sq < a.L) ? (int)(k.b * a.Lf + S.st_pos[buf * kQ + iq]) : -1;
     }
     uint64_t* bar = S.fbar + ((t + 1) & 3);
-    const int fr0 = frow((t + 1) * kQ + 4 * wid);
+    const int fr0 = frow((t + 1) * kQ + 4 * grp);
     const int nbp = S.nbp;
     const CUtensorMap* map = gi < nbp ? tm_phi : (gi == nbp ? tm_qc : tm_kc);
     uint8_t* dst = gi < nbp ? S.phi + ((gi * kRF + fr0) << 7) : (gi == nbp ? S.qc : S.kc) + (fr0 << 6);
@@ -272,24 +275,24 @@ __device__ __forceinline__ void tc_stage2_features(const ScoreArgs& a, const TcS
 // Value rows Ea[pos + 1] of sub-tile t (its scalars already in the feature ring) into the value ring as tensor-map
 // row gathers: 4 slots x one 64-column region per gather (box of 64 columns with the 128-byte swizzle, which is the
 // value MMA's MN-major layout: region = 64 columns, row = key, chunk index XOR the key's row in its group of 8), the
-// d_part / 64 regions of the 8 slot groups spread over lanes 0-5 of the 16 warps, counted on the value stage's
-// mbarrier. Unused rows read zeros (row coordinate -1).
-__device__ __forceinline__ void tc_stage2_values(const ScoreArgs& a, const TcSmem& S, const TcBlock& k, int t,
+// d_part / 64 regions of the 8 slot groups spread over the load group, counted on the value stage's mbarrier. Unused
+// rows read zeros (row coordinate -1).
+__device__ __forceinline__ void tc_stage2_values(const ScoreArgs& a, const TcSmem& S, const TcBlock& k, int t, int pt,
                                                  const CUtensorMap* tm_ea) {
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  const int item = wid + 16 * lane, nreg = k.dpart / 64;
-  if (item >= (kQ / 4) * nreg) return;
-  const int g = item & 7, reg = item >> 3;
-  const int li0 = (t + 1) * kQ + 4 * g;
-  int y[4];
+  const int nreg = k.dpart / 64;
+  for (int item = pt; item < (kQ / 4) * nreg; item += kLoadThreads) {
+    const int g = item & 7, reg = item >> 3;
+    const int li0 = (t + 1) * kQ + 4 * g;
+    int y[4];
 #pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    const int fr = frow(li0 + q);
-    y[q] = S.used[fr] ? (int)(k.b * a.Lf + S.pos[fr] + 1) : -1;
+    for (int q = 0; q < 4; ++q) {
+      const int fr = frow(li0 + q);
+      y[q] = S.used[fr] ? (int)(k.b * a.Lf + S.pos[fr] + 1) : -1;
+    }
+    const int vr = vrow(li0);
+    gather4_rows(S.v + reg * kVRegion + (vr >> 3) * 1024 + (vr & 7) * 128, tm_ea, k.dp0 + 64 * reg, y[0], y[1],
+                 y[2], y[3], S.vbar + ((t + 1) & 1));
   }
-  const int vr = vrow(li0);
-  gather4_rows(S.v + reg * kVRegion + (vr >> 3) * 1024 + (vr & 7) * 128, tm_ea, k.dp0 + 64 * reg, y[0], y[1], y[2],
-               y[3], S.vbar + ((t + 1) & 1));
 }
 
 // Group A: scores of sub-tile t (queries: window slots 32 .. 63; keys: 0 .. 63, slot q0 - 32 + key), the exact-mask
@@ -574,85 +577,87 @@ k_score_tc(const __grid_constant__ CUtensorMap tm_phi, const __grid_constant__ C
       umma::tmem_relinquish();
     }
   }
-  // bounded wait for the feature rows of sub-tile t (stage (t + 1) % 4)
+  const bool loader = wid >= 2 * kGroupWarps;
+  const int pt = threadIdx.x - 2 * kGroupWarps * 32;   // thread index within the load group
+  // bounded wait for the feature rows of sub-tile t (stage (t + 1) % 4): every thread of group A waits itself
   auto wait_features = [&](int t) {
     umma::mbar_wait(S.fbar + ((t + 1) & 3), (uint32_t)(((t + 1) >> 2) & 1), a.status);
   };
-  // the stage's transaction count is set by thread 0 before any copy of the stage is issued
+  // the stage's transaction count, set by load thread 0 before any copy of the stage is issued (bar_load)
   auto expect_features = [&](int t) {
-    if (threadIdx.x == 0) umma::mbar_expect_tx(S.fbar + ((t + 1) & 3), (uint32_t)(kQ * (S.nbp * 128 + 2 * 64)));
+    if (pt == 0) umma::mbar_expect_tx(S.fbar + ((t + 1) & 3), (uint32_t)(kQ * (S.nbp * 128 + 2 * 64)));
   };
   auto expect_values = [&](int t) {
-    if (threadIdx.x == 0) umma::mbar_expect_tx(S.vbar + ((t + 1) & 1), (uint32_t)(kQ * k.dpart * 2));
+    if (pt == 0) umma::mbar_expect_tx(S.vbar + ((t + 1) & 1), (uint32_t)(kQ * k.dpart * 2));
   };
-  // this thread's cp.async copies (the scalars) complete, then made visible to the tensor cores
-  auto wait_copies = [&]() {
-    cp_async_wait_all();
-    umma::fence_proxy_async();
-  };
+  auto bar_load = []() { asm volatile("bar.sync 2, %0;" ::"n"(kLoadThreads) : "memory"); };
 
-  // prologue: sub-tiles -1 (the first window half), 0 and 1 of the features, -1 and 0 of the values, the scores of
-  // 0 taken; sub-tile 2's sorted entries on their way
+  // prologue (load group): sub-tiles -1 (the first window half), 0 and 1 of the features, -1 and 0 of the values,
+  // sub-tile 2's sorted entries; then group A scores sub-tile 0
   umma::tc_fence_before();
   __syncthreads();
   umma::tc_fence_after();
   const uint32_t tmem = *S.tmem;
-  tc_stage1(a, S, k, -1);
-  tc_stage1(a, S, k, 0);
-  if (ntile > 1) tc_stage1(a, S, k, 1);
-  cp_async_commit();
-  cp_async_wait_all();
-  expect_features(-1);
-  expect_features(0);
-  if (ntile > 1) expect_features(1);
-  expect_values(-1);
-  expect_values(0);
+  if (loader) {
+    tc_stage1(a, S, k, -1, pt);
+    tc_stage1(a, S, k, 0, pt);
+    if (ntile > 1) tc_stage1(a, S, k, 1, pt);
+    cp_async_commit();
+    cp_async_wait_all();
+    expect_features(-1);
+    expect_features(0);
+    if (ntile > 1) expect_features(1);
+    expect_values(-1);
+    expect_values(0);
+    bar_load();
+    tc_stage2_features(a, S, k, -1, pt, &tm_phi, &tm_qc, &tm_kc);
+    tc_stage2_features(a, S, k, 0, pt, &tm_phi, &tm_qc, &tm_kc);
+    if (ntile > 1) tc_stage2_features(a, S, k, 1, pt, &tm_phi, &tm_qc, &tm_kc);
+    cp_async_commit();
+    cp_async_wait_all();
+    bar_load();
+    if (ntile > 2) tc_stage1(a, S, k, 2, pt);   // its buffer was read by sub-tile -1's feature stage above
+    tc_stage2_values(a, S, k, -1, pt, &tm_ea);
+    tc_stage2_values(a, S, k, 0, pt, &tm_ea);
+    cp_async_commit();
+    cp_async_wait_all();
+  }
   __syncthreads();
-  tc_stage2_features(a, S, k, -1, &tm_phi, &tm_qc, &tm_kc);
-  tc_stage2_features(a, S, k, 0, &tm_phi, &tm_qc, &tm_kc);
-  if (ntile > 1) tc_stage2_features(a, S, k, 1, &tm_phi, &tm_qc, &tm_kc);
-  cp_async_commit();
-  cp_async_wait_all();
-  __syncthreads();
-  if (ntile > 2) tc_stage1(a, S, k, 2);        // its buffer was read by sub-tile -1's feature stage above
-  tc_stage2_values(a, S, k, -1, &tm_ea);
-  tc_stage2_values(a, S, k, 0, &tm_ea);
-  cp_async_commit();
-  wait_features(-1);
-  wait_features(0);
   const bool suf4 = a.K <= 4;
   if (group_a) {
+    wait_features(-1);
+    wait_features(0);
     if (suf4) tc_scores<true>(a, S, k, 0);
     else tc_scores<false>(a, S, k, 0);
+  } else if (!loader) {
+    // sub-tile -1's value rows: waited here, before iteration 0 re-arms their barrier for sub-tile 1
+    umma::mbar_wait(S.vbar, 0u, a.status);
   }
-  wait_copies();
-  if (ntile > 1) wait_features(1);
-  // sub-tile -1's value rows: waited here, before iteration 0 re-arms their barrier for sub-tile 1
-  umma::mbar_wait(S.vbar, 0u, a.status);
   __syncthreads();
 
+  // iteration i: group A scores sub-tile i + 1, group B takes the value products of i, and meanwhile the load group
+  // copies the value rows of i + 1, the features of i + 2 and the sorted entries of i + 3
   for (int i = 0; i < ntile; ++i) {
-    // value rows of i + 1 (their scalars arrived with the features in iteration i - 1) and feature rows of i + 2,
-    // issued by all warps once thread 0 has set the feature stage's byte count
-    if (i + 2 < ntile) expect_features(i + 2);
-    if (i + 1 < ntile) expect_values(i + 1);
-    if (i + 3 < ntile) tc_stage1(a, S, k, i + 3);
-    if (i + 1 < ntile) {
-      asm volatile("bar.sync 2, 512;" ::: "memory");   // the expect_tx precedes every copy of the stage
-      if (i + 2 < ntile) tc_stage2_features(a, S, k, i + 2, &tm_phi, &tm_qc, &tm_kc);
-      tc_stage2_values(a, S, k, i + 1, &tm_ea);
-    }
-    cp_async_commit();
-    if (group_a) {
+    if (loader) {
+      if (i + 2 < ntile) expect_features(i + 2);
+      if (i + 1 < ntile) expect_values(i + 1);
+      if (i + 3 < ntile) tc_stage1(a, S, k, i + 3, pt);
       if (i + 1 < ntile) {
+        bar_load();                             // the expect_tx precedes every copy of the stage
+        if (i + 2 < ntile) tc_stage2_features(a, S, k, i + 2, pt, &tm_phi, &tm_qc, &tm_kc);
+        tc_stage2_values(a, S, k, i + 1, pt, &tm_ea);
+      }
+      cp_async_commit();
+      cp_async_wait_all();
+    } else if (group_a) {
+      if (i + 1 < ntile) {
+        wait_features(i + 1);
         if (suf4) tc_scores<true>(a, S, k, i + 1);
         else tc_scores<false>(a, S, k, i + 1);
       }
     } else {
       tc_values(a, S, k, i, wid - kGroupWarps, tmem);
     }
-    wait_copies();
-    if (i + 2 < ntile) wait_features(i + 2);
     __syncthreads();
   }
   if (wid == kGroupWarps) {
