@@ -60,7 +60,6 @@ struct TcSmem {
   float* wsuf;          // [kMaxSuffix + 1] suffix weights w_sufijo
   uint64_t* fbar;       // [4] feature-stage mbarriers (one per 32-row stage of the feature ring)
   uint64_t* pvbar;      // value-product MMAs done
-  uint64_t* vbar;       // [2] value-ring stages (sub-tile t on vbar[(t + 1) & 1])
   uint32_t* tmem;       // TMEM base address
   int nbp;               // phi column blocks
   int Dp;
@@ -119,7 +118,6 @@ __device__ inline TcSmem carve_tc(char* base, int P, int cf, int dpart) {
   p = base + ((p - base) + 15) / 16 * 16;
   s.fbar = reinterpret_cast<uint64_t*>(p);
   s.pvbar = s.fbar + 4;
-  s.vbar = s.fbar + 5;
   s.tmem = reinterpret_cast<uint32_t*>(s.fbar + 8);
   return s;
 }
@@ -272,26 +270,23 @@ __device__ __forceinline__ void tc_stage2_features(const ScoreArgs& a, const TcS
   }
 }
 
-// Value rows Ea[pos + 1] of sub-tile t (its scalars already in the feature ring) into the value ring as tensor-map
-// row gathers: 4 slots x one 64-column region per gather (box of 64 columns with the 128-byte swizzle, which is the
-// value MMA's MN-major layout: region = 64 columns, row = key, chunk index XOR the key's row in its group of 8), the
-// d_part / 64 regions of the 8 slot groups spread over the load group, counted on the value stage's mbarrier. Unused
-// rows read zeros (row coordinate -1).
-__device__ __forceinline__ void tc_stage2_values(const ScoreArgs& a, const TcSmem& S, const TcBlock& k, int t, int pt,
-                                                 const CUtensorMap* tm_ea) {
-  const int nreg = k.dpart / 64;
-  for (int item = pt; item < (kQ / 4) * nreg; item += kLoadThreads) {
-    const int g = item & 7, reg = item >> 3;
-    const int li0 = (t + 1) * kQ + 4 * g;
-    int y[4];
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const int fr = frow(li0 + q);
-      y[q] = S.used[fr] ? (int)(k.b * a.Lf + S.pos[fr] + 1) : -1;
-    }
-    const int vr = vrow(li0);
-    gather4_rows(S.v + reg * kVRegion + (vr >> 3) * 1024 + (vr & 7) * 128, tm_ea, k.dp0 + 64 * reg, y[0], y[1],
-                 y[2], y[3], S.vbar + ((t + 1) & 1));
+// Value rows Ea[pos + 1] of sub-tile t (its scalars already in the feature ring) into the value ring, only the used
+// rows, by group B (thread tb of its 256) at the start of the iteration before: warp w of the group takes slots w,
+// w + 8, ..., its lanes the row's 16-byte chunks by cp.async, each chunk at its place in the MN-major 128-byte-swizzled
+// layout (region = 64 columns, row = key, chunk index XOR the key's row in its group of 8). (As tensor-map row gathers
+// these take 12 gathers per 4 rows, which makes the tensor-map unit the bottleneck of the loop.)
+__device__ __forceinline__ void tc_stage2_values(const ScoreArgs& a, const TcSmem& S, const TcBlock& k, int t, int tb) {
+  const int lane = tb & 31, wb = tb >> 5;
+  const int nch = k.dpart / 8;                 // 16-byte chunks per row
+  for (int i = wb; i < kQ; i += kGroupWarps) {
+    const int li = (t + 1) * kQ + i;
+    const int fr = frow(li), vr = vrow(li);
+    if (!S.used[fr]) continue;
+    const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(a.Ea) + (k.b * a.Lf + S.pos[fr] + 1) *
+                               (int64_t)a.d + k.dp0;
+    uint8_t* row = S.v + (vr >> 3) * 1024 + (vr & 7) * 128;
+    for (int c = lane; c < nch; c += 32)
+      cp_async16(row + (c >> 3) * kVRegion + (((c & 7) ^ (vr & 7)) << 4), src + c * 8, true);
   }
 }
 
@@ -489,8 +484,6 @@ __device__ __forceinline__ void tc_values(const ScoreArgs& a, const TcSmem& S, c
   const int lb = t * kQ;                        // window index of key 0 (li of slot q0 - 32)
   const int nM = k.dpart / 128;
   if (w < nM && lane == 0) {                    // warp w issues M-tile w (its own commit on the shared barrier)
-    // the value rows of sub-tile t have landed (those of t - 1 were waited for one iteration earlier)
-    umma::mbar_wait(S.vbar + ((t + 1) & 1), (uint32_t)(((t + 1) >> 1) & 1), a.status);
     umma::tc_fence_after();
     const uint32_t idesc = umma::idesc_bf16(128, kQ) | (1u << 15);      // A (the value rows) MN-major
     const uint32_t v0 = su32(S.v) + (uint32_t)(2 * w) * kVRegion, a0 = su32(S.att + (t & 1) * kQ * 128);
@@ -536,8 +529,7 @@ __device__ __forceinline__ void tc_values(const ScoreArgs& a, const TcSmem& S, c
 
 __global__ void __launch_bounds__(kThreadsTc, 1)
 k_score_tc(const __grid_constant__ CUtensorMap tm_phi, const __grid_constant__ CUtensorMap tm_qc,
-           const __grid_constant__ CUtensorMap tm_kc, const __grid_constant__ CUtensorMap tm_ea, ScoreArgs a, int nds,
-           int dpart) {
+           const __grid_constant__ CUtensorMap tm_kc, ScoreArgs a, int nds, int dpart) {
   extern __shared__ __align__(16) char smem_raw[];
   const TcSmem S = carve_tc(smem_raw, a.P, a.cf, dpart);
   TcBlock k;
@@ -568,7 +560,6 @@ k_score_tc(const __grid_constant__ CUtensorMap tm_phi, const __grid_constant__ C
     umma::fence_proxy_async();                 // the zeros precede the tensor-map copies into the same rows
     if (threadIdx.x == 0) {
       for (int i = 0; i < 4; ++i) umma::mbar_init(S.fbar + i, 1);   // 4 feature stages
-      for (int i = 0; i < 2; ++i) umma::mbar_init(S.vbar + i, 1);   // 2 value stages
       umma::mbar_init(S.pvbar, (uint32_t)(k.dpart / 128));           // one commit per M-tile's issuing warp
       umma::fence_mbar_init();
     }
@@ -587,13 +578,15 @@ k_score_tc(const __grid_constant__ CUtensorMap tm_phi, const __grid_constant__ C
   auto expect_features = [&](int t) {
     if (pt == 0) umma::mbar_expect_tx(S.fbar + ((t + 1) & 3), (uint32_t)(kQ * (S.nbp * 128 + 2 * 64)));
   };
-  auto expect_values = [&](int t) {
-    if (pt == 0) umma::mbar_expect_tx(S.vbar + ((t + 1) & 1), (uint32_t)(kQ * k.dpart * 2));
+  // this thread's cp.async copies complete (value rows: then made visible to the tensor cores)
+  auto wait_copies = [&]() {
+    cp_async_wait_all();
+    umma::fence_proxy_async();
   };
   auto bar_load = []() { asm volatile("bar.sync 2, %0;" ::"n"(kLoadThreads) : "memory"); };
 
-  // prologue (load group): sub-tiles -1 (the first window half), 0 and 1 of the features, -1 and 0 of the values,
-  // sub-tile 2's sorted entries; then group A scores sub-tile 0
+  // prologue: the load group copies sub-tiles -1 (the first window half), 0 and 1 of the features and sub-tile 2's
+  // sorted entries; then group A scores sub-tile 0 while group B copies the value rows of -1 and 0
   umma::tc_fence_before();
   __syncthreads();
   umma::tc_fence_after();
@@ -607,8 +600,6 @@ k_score_tc(const __grid_constant__ CUtensorMap tm_phi, const __grid_constant__ C
     expect_features(-1);
     expect_features(0);
     if (ntile > 1) expect_features(1);
-    expect_values(-1);
-    expect_values(0);
     bar_load();
     tc_stage2_features(a, S, k, -1, pt, &tm_phi, &tm_qc, &tm_kc);
     tc_stage2_features(a, S, k, 0, pt, &tm_phi, &tm_qc, &tm_kc);
@@ -617,8 +608,6 @@ k_score_tc(const __grid_constant__ CUtensorMap tm_phi, const __grid_constant__ C
     cp_async_wait_all();
     bar_load();
     if (ntile > 2) tc_stage1(a, S, k, 2, pt);   // its buffer was read by sub-tile -1's feature stage above
-    tc_stage2_values(a, S, k, -1, pt, &tm_ea);
-    tc_stage2_values(a, S, k, 0, pt, &tm_ea);
     cp_async_commit();
     cp_async_wait_all();
   }
@@ -630,22 +619,22 @@ k_score_tc(const __grid_constant__ CUtensorMap tm_phi, const __grid_constant__ C
     if (suf4) tc_scores<true>(a, S, k, 0);
     else tc_scores<false>(a, S, k, 0);
   } else if (!loader) {
-    // sub-tile -1's value rows: waited here, before iteration 0 re-arms their barrier for sub-tile 1
-    umma::mbar_wait(S.vbar, 0u, a.status);
+    tc_stage2_values(a, S, k, -1, threadIdx.x - kGroupWarps * 32);
+    tc_stage2_values(a, S, k, 0, threadIdx.x - kGroupWarps * 32);
+    cp_async_commit();
+    wait_copies();
   }
   __syncthreads();
 
-  // iteration i: group A scores sub-tile i + 1, group B takes the value products of i, and meanwhile the load group
-  // copies the value rows of i + 1, the features of i + 2 and the sorted entries of i + 3
+  // iteration i: group A scores sub-tile i + 1; group B issues the value rows of i + 1, then takes the value products
+  // of i; meanwhile the load group copies the features of i + 2 and the sorted entries of i + 3
   for (int i = 0; i < ntile; ++i) {
     if (loader) {
       if (i + 2 < ntile) expect_features(i + 2);
-      if (i + 1 < ntile) expect_values(i + 1);
       if (i + 3 < ntile) tc_stage1(a, S, k, i + 3, pt);
-      if (i + 1 < ntile) {
+      if (i + 2 < ntile) {
         bar_load();                             // the expect_tx precedes every copy of the stage
-        if (i + 2 < ntile) tc_stage2_features(a, S, k, i + 2, pt, &tm_phi, &tm_qc, &tm_kc);
-        tc_stage2_values(a, S, k, i + 1, pt, &tm_ea);
+        tc_stage2_features(a, S, k, i + 2, pt, &tm_phi, &tm_qc, &tm_kc);
       }
       cp_async_commit();
       cp_async_wait_all();
@@ -656,7 +645,10 @@ k_score_tc(const __grid_constant__ CUtensorMap tm_phi, const __grid_constant__ C
         else tc_scores<false>(a, S, k, i + 1);
       }
     } else {
+      if (i + 1 < ntile) tc_stage2_values(a, S, k, i + 1, threadIdx.x - kGroupWarps * 32);
+      cp_async_commit();
       tc_values(a, S, k, i, wid - kGroupWarps, tmem);
+      wait_copies();
     }
     __syncthreads();
   }
@@ -688,12 +680,9 @@ int launch_score_tc(const ScoreArgs& a, cudaStream_t s) {
       !make_tmap_rows_bf16(&tm_qc, a.Qc, (uint64_t)a.cf, rows, (uint64_t)a.cf * 2, 32, 64) ||
       !make_tmap_rows_bf16(&tm_kc, a.Kc, (uint64_t)a.cf, rows, (uint64_t)a.cf * 2, 32, 64))
     return ASRN_ERR_CUDA;
-  // value rows: one-row boxes of 64 columns of the bf16 copy of E with the 128-byte swizzle
-  CUtensorMap tm_ea;
-  if (!make_tmap_rows_bf16(&tm_ea, a.Ea, (uint64_t)a.d, rows, (uint64_t)a.d * 2, 64, 128)) return ASRN_ERR_CUDA;
   cudaFuncSetAttribute(k_score_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   dim3 grid((unsigned)(((a.L + kSpanTc - 1) / kSpanTc) * nds), (unsigned)(a.B * a.T));
-  k_score_tc<<<grid, kThreadsTc, smem, s>>>(tm_phi, tm_qc, tm_kc, tm_ea, a, nds, dpart);
+  k_score_tc<<<grid, kThreadsTc, smem, s>>>(tm_phi, tm_qc, tm_kc, a, nds, dpart);
   return cudaGetLastError() == cudaSuccess ? ASRN_OK : ASRN_ERR_CUDA;
 }
 
