@@ -31,7 +31,7 @@ namespace {
 constexpr int kQ = 32;           // queries per sub-tile
 constexpr int kRF = 128;         // feature ring: 4 sub-tiles (score windows of i and i + 1, prefetch of i + 2)
 constexpr int kRV = 96;          // value ring: 3 sub-tiles (window of i, prefetch of i + 1)
-constexpr int kSpanTc = 512;     // sorted slots per block
+constexpr int kSpanTc = 512;     // sorted slots per block: the shortest span (longer ones when the grid stays large)
 constexpr int kGroupWarps = 8;   // warps 0-7: scores (group A); 8-15: value products (group B)
 constexpr int kLoadWarps = 2;    // warps 16-17: every copy into shared memory (the load group)
 constexpr int kLoadThreads = kLoadWarps * 32;
@@ -529,7 +529,7 @@ __device__ __forceinline__ void tc_values(const ScoreArgs& a, const TcSmem& S, c
 
 __global__ void __launch_bounds__(kThreadsTc, 1)
 k_score_tc(const __grid_constant__ CUtensorMap tm_phi, const __grid_constant__ CUtensorMap tm_qc,
-           const __grid_constant__ CUtensorMap tm_kc, ScoreArgs a, int nds, int dpart) {
+           const __grid_constant__ CUtensorMap tm_kc, ScoreArgs a, int nds, int dpart, int span) {
   extern __shared__ __align__(16) char smem_raw[];
   const TcSmem S = carve_tc(smem_raw, a.P, a.cf, dpart);
   TcBlock k;
@@ -537,8 +537,8 @@ k_score_tc(const __grid_constant__ CUtensorMap tm_phi, const __grid_constant__ C
   k.b = k.r / a.T;
   k.tau = (int)(k.r % a.T);
   const int part = blockIdx.x % nds;
-  k.S0 = (int64_t)(blockIdx.x / nds) * kSpanTc;
-  k.S1 = min(min(k.S0 + kSpanTc, a.L), a.row_len ? a.row_len[k.r] : a.L);
+  k.S0 = (int64_t)(blockIdx.x / nds) * span;
+  k.S1 = min(min(k.S0 + span, a.L), a.row_len ? a.row_len[k.r] : a.L);
   if (k.S0 >= k.S1) return;                     // a span past the row's used slots (sharded rows)
   k.dp0 = part * dpart;
   k.dpart = dpart;
@@ -681,8 +681,12 @@ int launch_score_tc(const ScoreArgs& a, cudaStream_t s) {
       !make_tmap_rows_bf16(&tm_kc, a.Kc, (uint64_t)a.cf, rows, (uint64_t)a.cf * 2, 32, 64))
     return ASRN_ERR_CUDA;
   cudaFuncSetAttribute(k_score_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  dim3 grid((unsigned)(((a.L + kSpanTc - 1) / kSpanTc) * nds), (unsigned)(a.B * a.T));
-  k_score_tc<<<grid, kThreadsTc, smem, s>>>(tm_phi, tm_qc, tm_kc, a, nds, dpart);
+  // each block pays a prologue (the first window half and two sub-tiles of latency): spans of 1024 or 2048 slots
+  // while the grid keeps at least 8 blocks per SM
+  int span = kSpanTc;
+  while (span < 2048 && ((a.L + 2 * span - 1) / (2 * span)) * nds * a.B * a.T >= 8 * 148) span *= 2;
+  dim3 grid((unsigned)(((a.L + span - 1) / span) * nds), (unsigned)(a.B * a.T));
+  k_score_tc<<<grid, kThreadsTc, smem, s>>>(tm_phi, tm_qc, tm_kc, a, nds, dpart, span);
   return cudaGetLastError() == cudaSuccess ? ASRN_OK : ASRN_ERR_CUDA;
 }
 
