@@ -83,7 +83,7 @@ __global__ void __launch_bounds__(256) k_gate_simt(GateArgs a) {
 //   c = bf16(acc / max(1, pt)) (asrn/estable.py:387, the autocast rounding of o's input); memory-bound.
 // k_gate_tc: h' = h + bf16(sigma * bf16(c . W_ov^T)). Tile 128 tokens (TMEM lanes) x NT columns (TMEM columns),
 //   K = d in chunks of 64; both operands by TMA (128-byte swizzle), one producer thread and one MMA thread
-//   (tcgen05.commit frees each stage), the fp32 accumulator in TMEM; in the epilogue each thread owns one tile row
+//   (tcgen05.commit frees each stage), the fp32 accumulators in TMEM; in the epilogue each thread owns one tile row
 //   (its TMEM lane) and reads h / writes h' for 32 consecutive columns at a time with 16-byte accesses.
 __global__ void __launch_bounds__(256) k_gate_prep(GateArgs a) {
   const int lane = threadIdx.x & 31;
@@ -108,42 +108,54 @@ __global__ void __launch_bounds__(256) k_gate_prep(GateArgs a) {
 }
 
 namespace {
-constexpr int kGTM = 128, kGBK = 64, kGThreads = 256;
+constexpr int kGTM = 128, kGBK = 64;
 constexpr int kGStageA = kGTM * 128;
+constexpr int kGStages = 4;
+constexpr int kGEpiWarps = 8;
+constexpr int kGThreads = (2 + kGEpiWarps) * 32;   // warp 0: TMA producer, warp 1: MMA issuer, warps 2-9: epilogue
 }  // namespace
 
+// Persistent: one block per SM walks the (128-token, NT-column) tiles of the output, n-tile fastest (the blocks of one
+// token tile run side by side and share its operand rows in L2). Warp 0 streams the K chunks of both operands through
+// kGStages shared-memory stages, warp 1 issues the MMAs into one of two TMEM accumulators (2 NT columns), and the 8
+// epilogue warps drain the other accumulator meanwhile: warp w reads TMEM lanes 32 (w % 4) .. + 31 (its tile rows) and
+// columns of its half, with the h rows of its next 32 columns in flight while it writes h' of the current ones.
 template <int NT>
-__global__ void __launch_bounds__(kGThreads, 2)
-k_gate_tc(const __grid_constant__ CUtensorMap tmap_c, const __grid_constant__ CUtensorMap tmap_wov, GateArgs a) {
+__global__ void __launch_bounds__(kGThreads, 1)
+k_gate_tc(const __grid_constant__ CUtensorMap tmap_c, const __grid_constant__ CUtensorMap tmap_wov, GateArgs a,
+          int ntn, int ntiles) {
   using namespace umma;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* sm = smem_raw + (((raw + 1023) & ~1023u) - raw);
   constexpr int kStageB = NT * 128;
   uint8_t* sA = sm;
-  uint8_t* sB = sm + 2 * kGStageA;
-  uint8_t* tail = sB + 2 * kStageB;
-  uint64_t* full = reinterpret_cast<uint64_t*>(tail);          // [2]
-  uint64_t* empty = full + 2;                                   // [2]
-  uint64_t* acc_full = full + 4;
-  uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(full + 5);
-  int* abort_s = reinterpret_cast<int*>(tmem_base_s + 1);
+  uint8_t* sB = sm + kGStages * kGStageA;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + kGStages * kStageB);   // [kGStages]
+  uint64_t* empty = full + kGStages;                                         // [kGStages]
+  uint64_t* tfull = empty + kGStages;                                        // [2] accumulator ready
+  uint64_t* tempty = tfull + 2;                                              // [2] accumulator drained
+  uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(tempty + 2);
 
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
   const int d = a.d;
   const int nk = d / kGBK;
-  const int n0 = blockIdx.x * NT;
   const int64_t M = a.B * a.L;
-  const int64_t m0 = (int64_t)blockIdx.y * kGTM;
   if (tid == 0) {
-    for (int i = 0; i < 5; ++i) mbar_init(full + i, 1);
-    *abort_s = 0;
+    for (int i = 0; i < kGStages; ++i) {
+      mbar_init(full + i, 1);
+      mbar_init(empty + i, 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(tfull + i, 1);
+      mbar_init(tempty + i, kGEpiWarps);
+    }
     fence_mbar_init();
     prefetch_tensormap(&tmap_c);
     prefetch_tensormap(&tmap_wov);
   }
-  if (wid == 0) {
-    tmem_alloc(tmem_base_s, NT < 32 ? 32 : NT);
+  if (wid == 1) {
+    tmem_alloc(tmem_base_s, 2 * NT);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -152,75 +164,117 @@ k_gate_tc(const __grid_constant__ CUtensorMap tmap_c, const __grid_constant__ CU
   const uint32_t tmem = *tmem_base_s;
   constexpr uint32_t kTx = (uint32_t)(kGStageA + kStageB);
 
-  if (tid == 0) {                         // producer
-    for (int k = 0; k < nk; ++k) {
-      const int s = k & 1;
-      if (k >= 2 && !mbar_wait(empty + s, ((k - 2) >> 1) & 1, a.status)) { *abort_s = 1; break; }
-      mbar_expect_tx(full + s, kTx);
-      tma_load_2d(sA + s * kGStageA, &tmap_c, k * kGBK, (int)m0, full + s);
-      tma_load_2d(sB + s * kStageB, &tmap_wov, k * kGBK, n0, full + s);
-    }
-  } else if (tid == 32) {                 // MMA issuer
-    const uint32_t idesc = idesc_bf16(kGTM, NT);
-    bool ok = true;
-    for (int k = 0; k < nk && ok; ++k) {
-      const int s = k & 1;
-      ok = mbar_wait(full + s, (k >> 1) & 1, a.status);
-      if (!ok) break;
-      tc_fence_after();
-      const uint32_t a0 = smem_u32(sA + s * kGStageA), b0 = smem_u32(sB + s * kStageB);
-#pragma unroll
-      for (int j = 0; j < kGBK / 16; ++j)
-        mma_bf16(tmem, desc_sw128(a0 + j * 32), desc_sw128(b0 + j * 32), idesc, (k > 0 || j > 0) ? 1u : 0u);
-      mma_commit(empty + s);
-    }
-    if (!ok) *abort_s = 1;
-    mma_commit(acc_full);
-  }
-  __syncwarp();
-  const bool ok = mbar_wait(acc_full, 0, a.status);
-  tc_fence_after();
-  __syncthreads();
-  if (ok && *abort_s == 0) {
-    // TMEM lane = tile row: each thread holds 32 consecutive columns of its row, so it reads its 128 bytes of h and
-    // writes its 128 bytes of h' with 16-byte accesses, all eight loads in flight together
-    const int q4 = wid & 3, grp = wid >> 2;
-    const uint32_t trow = tmem + ((uint32_t)(q4 * 32) << 16);
-    const int64_t g = m0 + q4 * 32 + lane;
-    const bool row_ok = g < M;
-    const float sg = row_ok ? a.sigma[g] : 0.f;
-    for (int ch = grp; ch * 32 < NT; ch += 2) {
-      float v[32];
-      tmem_ld32(trow + ch * 32, v);
-      if (row_ok) {
-        const float4* hp = reinterpret_cast<const float4*>(a.h + g * d + n0 + ch * 32);
-        float4* op = reinterpret_cast<float4*>(a.out + g * d + n0 + ch * 32);
-        float4 hv[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) hv[i] = __ldg(hp + i);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          float4 o;
-          o.x = __fadd_rn(hv[i].x, round_bf16(__fmul_rn(sg, round_bf16(v[4 * i]))));
-          o.y = __fadd_rn(hv[i].y, round_bf16(__fmul_rn(sg, round_bf16(v[4 * i + 1]))));
-          o.z = __fadd_rn(hv[i].z, round_bf16(__fmul_rn(sg, round_bf16(v[4 * i + 2]))));
-          o.w = __fadd_rn(hv[i].w, round_bf16(__fmul_rn(sg, round_bf16(v[4 * i + 3]))));
-          op[i] = o;
+  if (wid == 0) {
+    if (lane == 0) {                      // producer
+      int it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+        const int m0 = (tile / ntn) * kGTM, n0 = (tile % ntn) * NT;
+        for (int k = 0; k < nk; ++k, ++it) {
+          const int s = it % kGStages;
+          if (it >= kGStages && !(ok = mbar_wait(empty + s, ((it / kGStages) - 1) & 1, a.status))) break;
+          mbar_expect_tx(full + s, kTx);
+          tma_load_2d(sA + s * kGStageA, &tmap_c, k * kGBK, m0, full + s);
+          tma_load_2d(sB + s * kStageB, &tmap_wov, k * kGBK, n0, full + s);
         }
       }
+    }
+  } else if (wid == 1) {
+    if (lane == 0) {                      // MMA issuer
+      const uint32_t idesc = idesc_bf16(kGTM, NT);
+      int it = 0, j = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++j) {
+        const int b = j & 1;
+        if (j >= 2 && !(ok = mbar_wait(tempty + b, ((j >> 1) - 1) & 1, a.status))) break;
+        tc_fence_after();
+        for (int k = 0; k < nk; ++k, ++it) {
+          const int s = it % kGStages;
+          if (!(ok = mbar_wait(full + s, (it / kGStages) & 1, a.status))) break;
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + s * kGStageA), b0 = smem_u32(sB + s * kStageB);
+#pragma unroll
+          for (int q = 0; q < kGBK / 16; ++q)
+            mma_bf16(tmem + (uint32_t)(b * NT), desc_sw128(a0 + q * 32), desc_sw128(b0 + q * 32), idesc,
+                     (k > 0 || q > 0) ? 1u : 0u);
+          mma_commit(empty + s);
+        }
+        mma_commit(tfull + b);
+      }
+    }
+  } else {                                // epilogue
+    const int q4 = wid & 3, half = (wid - 2) >> 2;
+    const uint32_t trow = tmem + ((uint32_t)(q4 * 32) << 16);
+    int j = 0;
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++j) {
+      const int b = j & 1;
+      const int64_t m0 = (int64_t)(tile / ntn) * kGTM;
+      const int n0 = (tile % ntn) * NT;
+      const int64_t g = m0 + q4 * 32 + lane;
+      const bool row_ok = g < M;
+      const float sg = row_ok ? a.sigma[g] : 0.f;
+      const float4* hrow = reinterpret_cast<const float4*>(a.h + g * d + n0);
+      float4* orow = reinterpret_cast<float4*>(a.out + g * d + n0);
+      float4 hv[8];
+      if (row_ok) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) hv[i] = __ldg(hrow + half * 8 + i);
+      }
+      if (!mbar_wait(tfull + b, (j >> 1) & 1, a.status)) break;
+      tc_fence_after();
+#pragma unroll 1
+      for (int ch = half; ch * 32 < NT; ch += 2) {
+        float v[32];
+        tmem_ld32(trow + (uint32_t)(b * NT + ch * 32), v);
+        float4 hn[8];
+        const bool more = (ch + 2) * 32 < NT;
+        if (row_ok && more) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) hn[i] = __ldg(hrow + (ch + 2) * 8 + i);
+        }
+        if (row_ok) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            float4 o;
+            o.x = __fadd_rn(hv[i].x, round_bf16(__fmul_rn(sg, round_bf16(v[4 * i]))));
+            o.y = __fadd_rn(hv[i].y, round_bf16(__fmul_rn(sg, round_bf16(v[4 * i + 1]))));
+            o.z = __fadd_rn(hv[i].z, round_bf16(__fmul_rn(sg, round_bf16(v[4 * i + 2]))));
+            o.w = __fadd_rn(hv[i].w, round_bf16(__fmul_rn(sg, round_bf16(v[4 * i + 3]))));
+            orow[ch * 8 + i] = o;
+          }
+        }
+        if (more) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) hv[i] = hn[i];
+        }
+      }
+      // this warp has read its part of accumulator b
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tempty + b);
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (wid == 0) {
+  if (wid == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, NT < 32 ? 32 : NT);
+    tmem_dealloc(tmem, 2 * NT);
   }
 }
 
 template <int NT>
 static size_t gate_tc_smem() {
-  return 1024 + 2 * (size_t)kGStageA + 2 * (size_t)NT * 128 + 64;
+  return 1024 + (size_t)kGStages * (kGStageA + (size_t)NT * 128) + (2 * kGStages + 4) * 8 + 16;
+}
+
+static int sm_count() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+  }
+  return n;
 }
 
 int gate_tc_tile(int d) {
@@ -235,8 +289,10 @@ static int launch_gate_tc_t(const GateArgs& a, const CUtensorMap& mc, const CUte
   const size_t smem = gate_tc_smem<NT>();
   cudaFuncSetAttribute(k_gate_tc<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   const int64_t M = a.B * a.L;
-  dim3 grid((unsigned)(a.d / NT), (unsigned)((M + kGTM - 1) / kGTM));
-  k_gate_tc<NT><<<grid, kGThreads, smem, s>>>(mc, mw, a);
+  const int64_t ntiles = ((M + kGTM - 1) / kGTM) * (a.d / NT);
+  if (ntiles >= ((int64_t)1 << 31)) return ASRN_ERR_UNSUPPORTED;
+  const int grid = (int)std::min<int64_t>(ntiles, sm_count());
+  k_gate_tc<NT><<<grid, kGThreads, smem, s>>>(mc, mw, a, a.d / NT, (int)ntiles);
   return cudaGetLastError() == cudaSuccess ? ASRN_OK : ASRN_ERR_CUDA;
 }
 
