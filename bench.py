@@ -63,6 +63,7 @@ def parse():
                    help='cfg3: the batch-sharded layer metric (default); cfg4: one 262,144-token sequence, d=512, '
                         'sequence-sharded over the GPUs')
     p.add_argument('--no-gen', action='store_true', help='skip the generation leg')
+    p.add_argument('--eager', action='store_true', help='time the eager forward instead of its CUDA-graph replay')
     p.add_argument('--gen-prompt', type=int, default=GEN_L0, help='prompt length of the generation leg')
     p.add_argument('--gen-steps', type=int, default=GEN_NEW, help='timed generation steps')
     return p.parse_args()
@@ -410,6 +411,24 @@ def run_ours(args):
     clocks = ClockSampler(local)
     clocks.start()
     warm = warm_up(step, args.warmup, world)
+    # the forward (no collective on this path) captured once as a CUDA graph after the warm-up: the K timed steps are
+    # then K graph launches, all enqueued ahead of the device, so a host-side pause cannot leave the GPU idle between
+    # steps; the kernels and their work are those of the eager forward
+    run, launch_mode, graph = step, 'eager', None
+    if not args.eager:
+        try:
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                step()
+            torch.cuda.current_stream().wait_stream(side)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                step()
+            run, launch_mode = graph.replay, 'cuda_graph'
+            run()
+        except Exception as exc:          # capture unsupported here: time the eager forward
+            run, launch_mode = step, 'eager (graph capture failed: %s)' % type(exc).__name__
     if world > 1:
         dist.barrier()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -420,7 +439,7 @@ def run_ours(args):
     w0 = time.time()
     t0.record()
     for i in range(args.steps):
-        y = step()
+        run()
         marks[i].record()
     t1.record()
     torch.cuda.synchronize()
@@ -478,7 +497,7 @@ def run_ours(args):
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1) / e_steps
 
-    del Eh, hh, xh, out_h, y, E, h, x
+    del Eh, hh, xh, out_h, E, h, x, run, graph
     torch.cuda.empty_cache()
     gen = None
     if not args.no_gen:
@@ -524,6 +543,7 @@ def run_ours(args):
                             'kernel_ms': score_ms,
                             'layer_frac': LAYER_BYTES_PER_TOKEN * tokens / (ms / args.steps * 1e-3) / 1e9 / hbm},
                'gpu_launches': launches_per_step * args.steps,
+               'launch': launch_mode,
                'clocks': clk}
         if cpu_info is not None:
             out['cpu_baseline'] = cpu_info
