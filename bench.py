@@ -14,8 +14,10 @@ K steps, inputs resident in HBM; the 805 MB E and h per GPU exceed the 126 MB L2
 same through ASRNLayer.forward with pinned host buffers and H2D/D2H copies in the timed region, roofline of the
 dominant kernel (candidate scoring, HBM-bound), the CPU baseline (the oracle port on the host cores), clocks (nvidia-smi
 samples inside the timed region; the sampler starts before the warm-up). Warm-up: at least W steps, then until two
-consecutive steps agree within 3 % (at most 20 more; "warmup" reports the count); "step_ms" gives the spread of the K
-timed steps (CUDA events between them).
+consecutive steps agree within 3 % (at most 20 more; "warmup" reports the count); then the forward is captured once as a
+CUDA graph and the K timed steps are its replays ("launch": "cuda_graph"; --eager times the eager forward; the
+sequence-sharded cfg4 forward with its NCCL collectives stays eager); "step_ms" gives the spread of the K timed steps
+(CUDA events between them).
 Generation leg (configuration 5, key "generation"): the configuration-3 model (random init), 64 sequences split over
 the GPUs with 65,536-token Zipf+repeat prompts, then greedy steps of the O(1) writer; value = device time per step
 (us per generated token of every sequence), with the same figure at 4,096 and 16,384-token prompts (flatness), the
@@ -114,6 +116,28 @@ def make_inputs(batch, seq, rank, seed=0):
 # ---------------------------------------------------------------------------------------------------------------------
 # clocks during the timed region
 # ---------------------------------------------------------------------------------------------------------------------
+
+
+def graph_or_eager(step, eager):
+    """The forward captured once as a CUDA graph after the warm-up (only on paths with no collective): the K timed
+    steps are then K graph launches, all enqueued ahead of the device, so a host-side pause cannot leave the GPU idle
+    between steps; the kernels and their work are those of the eager forward. Returns (run, mode, graph)."""
+    import torch
+    if eager:
+        return step, 'eager', None
+    try:
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            step()
+        torch.cuda.current_stream().wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step()
+        graph.replay()
+        return graph.replay, 'cuda_graph', graph
+    except Exception as exc:              # capture unsupported here: time the eager forward
+        return step, 'eager (graph capture failed: %s)' % type(exc).__name__, None
 
 class ClockSampler:
     """nvidia-smi clock / throttle-reason samples every 100 ms. Started before the warm-up (nvidia-smi's own start-up
@@ -411,24 +435,7 @@ def run_ours(args):
     clocks = ClockSampler(local)
     clocks.start()
     warm = warm_up(step, args.warmup, world)
-    # the forward (no collective on this path) captured once as a CUDA graph after the warm-up: the K timed steps are
-    # then K graph launches, all enqueued ahead of the device, so a host-side pause cannot leave the GPU idle between
-    # steps; the kernels and their work are those of the eager forward
-    run, launch_mode, graph = step, 'eager', None
-    if not args.eager:
-        try:
-            side = torch.cuda.Stream()
-            side.wait_stream(torch.cuda.current_stream())
-            with torch.cuda.stream(side):
-                step()
-            torch.cuda.current_stream().wait_stream(side)
-            graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph):
-                step()
-            run, launch_mode = graph.replay, 'cuda_graph'
-            run()
-        except Exception as exc:          # capture unsupported here: time the eager forward
-            run, launch_mode = step, 'eager (graph capture failed: %s)' % type(exc).__name__
+    run, launch_mode, graph = graph_or_eager(step, args.eager)
     if world > 1:
         dist.barrier()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -618,6 +625,8 @@ def run_cfg4(args):
     clocks = ClockSampler(local)
     clocks.start()
     warm = warm_up(step, args.warmup, world)
+    # one GPU: the forward replayed as a CUDA graph; sharded: eager (its NCCL collectives stay outside graphs)
+    run, launch_mode, graph = graph_or_eager(step, args.eager or world > 1)
     if world > 1:
         dist.barrier()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -628,7 +637,7 @@ def run_cfg4(args):
     w0 = time.time()
     t0.record()
     for i in range(args.steps):
-        y = step()
+        run()
         marks[i].record()
     t1.record()
     torch.cuda.synchronize()
@@ -695,7 +704,7 @@ def run_cfg4(args):
                             'peak': hbm, 'peak_source': 'measured' if 'hbm_gbs' in peaks else 'fallback',
                             'unit': 'GB/s', 'frac': achieved / hbm,
                             'algorithmic_bytes_per_token': CFG4_BYTES_PER_TOKEN, 'traffic': None},
-               'gpu_launches': None, 'clocks': clk}
+               'gpu_launches': None, 'launch': launch_mode, 'clocks': clk}
         if cpu_info is not None:
             out['cpu_baseline'] = cpu_info
         print(json.dumps(out), flush=True)
