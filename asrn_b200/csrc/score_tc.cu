@@ -33,7 +33,7 @@ constexpr int kRF = 128;         // feature ring: 4 sub-tiles (score windows of 
 constexpr int kRV = 96;          // value ring: 3 sub-tiles (window of i, prefetch of i + 1)
 constexpr int kSpanTc = 512;     // sorted slots per block: the shortest span (longer ones when the grid stays large)
 constexpr int kGroupWarps = 8;   // warps 0-7: scores (group A); 8-15: value products (group B)
-constexpr int kLoadWarps = 2;    // warps 16-17: every copy into shared memory (the load group)
+constexpr int kLoadWarps = 4;    // warps 16-19: every copy into shared memory (the load group)
 constexpr int kLoadThreads = kLoadWarps * 32;
 constexpr int kThreadsTc = (2 * kGroupWarps + kLoadWarps) * 32;
 constexpr int kMaxMt = 6;        // M = 128 tiles of d_part (d_part <= 768)
@@ -211,19 +211,19 @@ __device__ __forceinline__ void tc_stage1(const ScoreArgs& a, const TcSmem& S, c
   }
 }
 
-// Scalars and feature rows of sub-tile t, issued by the load group (thread pt of kLoadThreads). Thread pt takes slot
-// pt / 2: even threads copy its kMaxSuffix previous signatures (4 B each by cp.async; NaN, never equal, before the text
-// and past K), odd threads its clock (8 B) and log_alfa (4 B) and write (position, id, used) from the staging buffer.
-// The phi, Qc and Kc rows move as tensor-map row gathers of four slots each: thread pt < 8 (nbp + 2) issues gather
-// pt / 8 (phi column blocks, then Qc, then Kc) of slots 4 (pt % 8) .. + 3, counted on the stage's mbarrier (its byte
-// count is set beforehand, expect_features); a slot outside the row reads zero rows (row coordinate -1), and the
-// columns past P / cf read zeros.
+// Scalars and feature rows of sub-tile t, issued by the load group (thread pt of kLoadThreads). Thread pt < 64 takes
+// slot pt / 2: even threads copy its kMaxSuffix previous signatures (4 B each by cp.async; NaN, never equal, before the
+// text and past K), odd threads its clock (8 B) and log_alfa (4 B) and write (position, id, used) from the staging
+// buffer. The phi, Qc and Kc rows move as tensor-map row gathers of four slots each: thread 64 + j, j < 8 (nbp + 2),
+// issues gather j / 8 (phi column blocks, then Qc, then Kc) of slots 4 (j % 8) .. + 3, counted on the stage's mbarrier
+// (its byte count is set beforehand, expect_features); a slot outside the row reads zero rows (row coordinate -1), and
+// the columns past P / cf read zeros.
 __device__ __forceinline__ void tc_stage2_features(const ScoreArgs& a, const TcSmem& S, const TcBlock& k, int t, int pt,
                                                    const CUtensorMap* tm_phi, const CUtensorMap* tm_qc,
                                                    const CUtensorMap* tm_kc) {
   const int buf = (t + 1) % kStage;
   const int64_t s0 = k.S0 + (int64_t)t * kQ;
-  {
+  if (pt < 2 * kQ) {
     const int i = pt >> 1;
     const int64_t s = s0 + i;
     const int fr = frow((t + 1) * kQ + i);
@@ -252,8 +252,9 @@ __device__ __forceinline__ void tc_stage2_features(const ScoreArgs& a, const TcS
       S.used[fr] = used ? 1 : 0;
     }
   }
-  if (pt < 8 * (S.nbp + 2)) {
-    const int grp = pt & 7, gi = pt >> 3;
+  const int gp = pt - 2 * kQ;
+  if (gp >= 0 && gp < 8 * (S.nbp + 2)) {
+    const int grp = gp & 7, gi = gp >> 3;
     int y[4];
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
@@ -271,14 +272,14 @@ __device__ __forceinline__ void tc_stage2_features(const ScoreArgs& a, const TcS
 }
 
 // Value rows Ea[pos + 1] of sub-tile t (its scalars already in the feature ring) into the value ring, only the used
-// rows, by group B (thread tb of its 256) at the start of the iteration before: warp w of the group takes slots w,
-// w + 8, ..., its lanes the row's 16-byte chunks by cp.async, each chunk at its place in the MN-major 128-byte-swizzled
-// layout (region = 64 columns, row = key, chunk index XOR the key's row in its group of 8). (As tensor-map row gathers
-// these take 12 gathers per 4 rows, which makes the tensor-map unit the bottleneck of the loop.)
-__device__ __forceinline__ void tc_stage2_values(const ScoreArgs& a, const TcSmem& S, const TcBlock& k, int t, int tb) {
-  const int lane = tb & 31, wb = tb >> 5;
+// rows, by the load group (thread pt) one iteration ahead of their MMAs: load warp w takes slots w, w + 4, ..., its
+// lanes the row's 16-byte chunks by cp.async, each chunk at its place in the MN-major 128-byte-swizzled layout (region
+// = 64 columns, row = key, chunk index XOR the key's row in its group of 8). (As tensor-map row gathers these take 12
+// gathers per 4 rows, which makes the tensor-map unit the bottleneck of the loop.)
+__device__ __forceinline__ void tc_stage2_values(const ScoreArgs& a, const TcSmem& S, const TcBlock& k, int t, int pt) {
+  const int lane = pt & 31, wb = pt >> 5;
   const int nch = k.dpart / 8;                 // 16-byte chunks per row
-  for (int i = wb; i < kQ; i += kGroupWarps) {
+  for (int i = wb; i < kQ; i += kLoadWarps) {
     const int li = (t + 1) * kQ + i;
     const int fr = frow(li), vr = vrow(li);
     if (!S.used[fr]) continue;
@@ -412,63 +413,54 @@ __device__ __forceinline__ void tc_scores(const ScoreArgs& a, const TcSmem& S, c
     }
   }
   bar_group_a();
-  // softmax: warp w -> queries 4w .. 4w + 3 together; lane -> keys lane, lane + 32
+  // softmax: warp w -> queries 4w .. 4w + 3, eight lanes per query; lane -> keys 8 kg .. 8 kg + 7 (kg = lane % 8) of
+  // query qi = 4w + lane / 8. In the score tile these keys are the 8-aligned group 8 (kg ^ (swz / 8)) with adjacent
+  // pairs swapped when bit 0 of the row's swizzle is set.
   uint8_t* att = S.att + (t & 1) * kQ * 128;
   int64_t* qoff = S.qoff + (t & 1) * kQ;
-  const int qa = wid * 4;
-  float x[4][2], m[4], sum[4], e[4][2];
-  unsigned bal[4];
+  const int qi = wid * 4 + (lane >> 3), kg = lane & 7;
+  const int swz = sc_swz(qi);
+  const float* srow = S.sc + qi * 64 + 8 * (kg ^ (swz >> 3));
+  const float4 lo = *reinterpret_cast<const float4*>(srow), hi = *reinterpret_cast<const float4*>(srow + 4);
+  float x[8];
+  if (swz & 1) {
+    x[0] = lo.y; x[1] = lo.x; x[2] = lo.w; x[3] = lo.z; x[4] = hi.y; x[5] = hi.x; x[6] = hi.w; x[7] = hi.z;
+  } else {
+    x[0] = lo.x; x[1] = lo.y; x[2] = lo.z; x[3] = lo.w; x[4] = hi.x; x[5] = hi.y; x[6] = hi.z; x[7] = hi.w;
+  }
+  float m = x[0];
 #pragma unroll
-  for (int u = 0; u < 4; ++u) {
-    x[u][0] = S.sc[(qa + u) * 64 + (lane ^ sc_swz(qa + u))];
-    x[u][1] = S.sc[(qa + u) * 64 + ((lane + 32) ^ sc_swz(qa + u))];
-    bal[u] = __ballot_sync(0xffffffffu, x[u][0] != -INFINITY || x[u][1] != -INFINITY);
-    m[u] = fmaxf(x[u][0], x[u][1]);
+  for (int j = 1; j < 8; ++j) m = fmaxf(m, x[j]);
+#pragma unroll
+  for (int o = 1; o < 8; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  const bool anyv = m != -INFINITY;             // the query has at least one candidate in this table
+  float e[8], sum = 0.f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    e[j] = x[j] != -INFINITY ? __expf(__fsub_rn(x[j], m)) : 0.f;
+    sum += e[j];
   }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-    for (int u = 0; u < 4; ++u) m[u] = fmaxf(m[u], __shfl_xor_sync(0xffffffffu, m[u], o));
-#pragma unroll
-  for (int u = 0; u < 4; ++u) {
-    e[u][0] = x[u][0] != -INFINITY ? __expf(__fsub_rn(x[u][0], m[u])) : 0.f;
-    e[u][1] = x[u][1] != -INFINITY ? __expf(__fsub_rn(x[u][1], m[u])) : 0.f;
-    sum[u] = e[u][0] + e[u][1];
+  for (int o = 1; o < 8; o <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  const int64_t sq = q0 + qi;
+  const int posq = S.pos[frow(lb + kQ + qi)];
+  const bool mine = sq < k.S1 && posq >= a.q_lo && posq < a.q_hi;   // else a key only (another shard's position)
+  const int64_t gq = k.b * (a.q_hi - a.q_lo) + (posq - a.q_lo);
+  const float rs = anyv ? __frcp_rn(sum) : 0.f;
+  if (kg == 0 && k.write_signals && mine) {
+    // the largest weight is the maximum's: exp(0) / sum
+    a.sen_hay[gq * a.T + k.tau] = anyv ? 1 : 0;
+    a.sen_mx[gq * a.T + k.tau] = anyv ? m : kProhibido;
+    a.sen_pk[gq * a.T + k.tau] = rs;
   }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-    for (int u = 0; u < 4; ++u) sum[u] += __shfl_xor_sync(0xffffffffu, sum[u], o);
-#pragma unroll
-  for (int u = 0; u < 4; ++u) {
-    const int qi = qa + u;
-    const int64_t sq = q0 + qi;
-    const bool anyv = bal[u] != 0;
-    const int posq = S.pos[frow(lb + kQ + qi)];
-    const bool mine = sq < k.S1 && posq >= a.q_lo && posq < a.q_hi;   // else a key only (another shard's position)
-    const int64_t gq = k.b * (a.q_hi - a.q_lo) + (posq - a.q_lo);
-    float w0 = 0.f, w1 = 0.f;
-    if (anyv) {
-      const float rs = __frcp_rn(sum[u]);
-      w0 = __fmul_rn(e[u][0], rs);
-      w1 = __fmul_rn(e[u][1], rs);
-      // the largest weight is the maximum's: exp(0) / sum
-      if (lane == 0 && k.write_signals && mine) {
-        a.sen_hay[gq * a.T + k.tau] = 1;
-        a.sen_mx[gq * a.T + k.tau] = m[u];
-        a.sen_pk[gq * a.T + k.tau] = rs;
-      }
-    } else if (lane == 0 && k.write_signals && mine) {
-      a.sen_hay[gq * a.T + k.tau] = 0;
-      a.sen_mx[gq * a.T + k.tau] = kProhibido;
-      a.sen_pk[gq * a.T + k.tau] = 0.f;
-    }
-    // weights of keys lane and lane + 32 at row qi of the swizzled K-major operand (128-byte rows of 64 keys)
-    uint8_t* arow = att + (qi >> 3) * 1024 + (qi & 7) * 128 + (lane & 7) * 2;
-    *reinterpret_cast<__nv_bfloat16*>(arow + ((((lane >> 3)) ^ (qi & 7)) << 4)) = __float2bfloat16_rn(w0);
-    *reinterpret_cast<__nv_bfloat16*>(arow + ((((lane >> 3) + 4) ^ (qi & 7)) << 4)) = __float2bfloat16_rn(w1);
-    if (lane == 0) qoff[qi] = (anyv && mine) ? gq * a.d + k.dp0 : -1;
-  }
+  // the 8 weights as one 16-byte chunk (keys 8 kg .. + 7) of row qi of the swizzled K-major operand
+  uint4 wv;
+  wv.x = umma::pack_bf16x2(__fmul_rn(e[0], rs), __fmul_rn(e[1], rs));
+  wv.y = umma::pack_bf16x2(__fmul_rn(e[2], rs), __fmul_rn(e[3], rs));
+  wv.z = umma::pack_bf16x2(__fmul_rn(e[4], rs), __fmul_rn(e[5], rs));
+  wv.w = umma::pack_bf16x2(__fmul_rn(e[6], rs), __fmul_rn(e[7], rs));
+  *reinterpret_cast<uint4*>(att + (qi >> 3) * 1024 + (qi & 7) * 128 + ((kg ^ (qi & 7)) << 4)) = wv;
+  if (kg == 0) qoff[qi] = (anyv && mine) ? gq * a.d + k.dp0 : -1;
   umma::fence_proxy_async();       // the weights are read by the tensor cores (async proxy) after the block barrier
 }
 
@@ -585,8 +577,8 @@ k_score_tc(const __grid_constant__ CUtensorMap tm_phi, const __grid_constant__ C
   };
   auto bar_load = []() { asm volatile("bar.sync 2, %0;" ::"n"(kLoadThreads) : "memory"); };
 
-  // prologue: the load group copies sub-tiles -1 (the first window half), 0 and 1 of the features and sub-tile 2's
-  // sorted entries; then group A scores sub-tile 0 while group B copies the value rows of -1 and 0
+  // prologue: the load group copies sub-tiles -1 (the first window half), 0 and 1 of the features, sub-tile 2's
+  // sorted entries and the value rows of -1 and 0; then group A scores sub-tile 0
   umma::tc_fence_before();
   __syncthreads();
   umma::tc_fence_after();
@@ -608,8 +600,10 @@ k_score_tc(const __grid_constant__ CUtensorMap tm_phi, const __grid_constant__ C
     cp_async_wait_all();
     bar_load();
     if (ntile > 2) tc_stage1(a, S, k, 2, pt);   // its buffer was read by sub-tile -1's feature stage above
+    tc_stage2_values(a, S, k, -1, pt);
+    tc_stage2_values(a, S, k, 0, pt);
     cp_async_commit();
-    cp_async_wait_all();
+    wait_copies();
   }
   __syncthreads();
   const bool suf4 = a.K <= 4;
@@ -618,16 +612,11 @@ k_score_tc(const __grid_constant__ CUtensorMap tm_phi, const __grid_constant__ C
     wait_features(0);
     if (suf4) tc_scores<true>(a, S, k, 0);
     else tc_scores<false>(a, S, k, 0);
-  } else if (!loader) {
-    tc_stage2_values(a, S, k, -1, threadIdx.x - kGroupWarps * 32);
-    tc_stage2_values(a, S, k, 0, threadIdx.x - kGroupWarps * 32);
-    cp_async_commit();
-    wait_copies();
   }
   __syncthreads();
 
-  // iteration i: group A scores sub-tile i + 1; group B issues the value rows of i + 1, then takes the value products
-  // of i; meanwhile the load group copies the features of i + 2 and the sorted entries of i + 3
+  // iteration i: group A scores sub-tile i + 1, group B takes the value products of i; meanwhile the load group copies
+  // the value rows of i + 1, the features of i + 2 and the sorted entries of i + 3
   for (int i = 0; i < ntile; ++i) {
     if (loader) {
       if (i + 2 < ntile) expect_features(i + 2);
@@ -636,8 +625,9 @@ k_score_tc(const __grid_constant__ CUtensorMap tm_phi, const __grid_constant__ C
         bar_load();                             // the expect_tx precedes every copy of the stage
         tc_stage2_features(a, S, k, i + 2, pt, &tm_phi, &tm_qc, &tm_kc);
       }
+      if (i + 1 < ntile) tc_stage2_values(a, S, k, i + 1, pt);
       cp_async_commit();
-      cp_async_wait_all();
+      wait_copies();
     } else if (group_a) {
       if (i + 1 < ntile) {
         wait_features(i + 1);
@@ -645,10 +635,7 @@ k_score_tc(const __grid_constant__ CUtensorMap tm_phi, const __grid_constant__ C
         else tc_scores<false>(a, S, k, i + 1);
       }
     } else {
-      if (i + 1 < ntile) tc_stage2_values(a, S, k, i + 1, threadIdx.x - kGroupWarps * 32);
-      cp_async_commit();
       tc_values(a, S, k, i, wid - kGroupWarps, tmem);
-      wait_copies();
     }
     __syncthreads();
   }
