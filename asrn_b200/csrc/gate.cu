@@ -110,20 +110,24 @@ __global__ void __launch_bounds__(256) k_gate_prep(GateArgs a) {
 namespace {
 constexpr int kGTM = 128, kGBK = 64;
 constexpr int kGStageA = kGTM * 128;
-constexpr int kGStages = 4;
+constexpr int kGStages = 3;
 constexpr int kGEpiWarps = 8;
-constexpr int kGThreads = (2 + kGEpiWarps) * 32;   // warp 0: TMA producer, warp 1: MMA issuer, warps 2-9: epilogue
+constexpr int kGHSlots = 4;                         // h tiles (128 rows x 32 fp32, 16 KB) staged for the epilogue
+constexpr int kGHTile = kGTM * 128;
+// warp 0: operand TMA producer, warp 1: MMA issuer, warp 2: h TMA producer, warps 3-10: epilogue
+constexpr int kGThreads = (3 + kGEpiWarps) * 32;
 }  // namespace
 
 // Persistent: one block per SM walks the (128-token, NT-column) tiles of the output, n-tile fastest (the blocks of one
 // token tile run side by side and share its operand rows in L2). Warp 0 streams the K chunks of both operands through
-// kGStages shared-memory stages, warp 1 issues the MMAs into one of two TMEM accumulators (2 NT columns), and the 8
-// epilogue warps drain the other accumulator meanwhile: warp w reads TMEM lanes 32 (w % 4) .. + 31 (its tile rows) and
-// columns of its half, with the h rows of its next 32 columns in flight while it writes h' of the current ones.
+// kGStages shared-memory stages, warp 1 issues the MMAs into one of two TMEM accumulators (2 NT columns), warp 2
+// streams the tile's h as 128 x 32 fp32 boxes (128-byte swizzle) through kGHSlots slots, and the 8 epilogue warps
+// drain the other accumulator meanwhile: warp w reads TMEM lanes 32 (w % 4) .. + 31 (its tile rows) for the 32-column
+// chunks of its half (even or odd chunks), adds the staged h and writes h'.
 template <int NT>
 __global__ void __launch_bounds__(kGThreads, 1)
-k_gate_tc(const __grid_constant__ CUtensorMap tmap_c, const __grid_constant__ CUtensorMap tmap_wov, GateArgs a,
-          int ntn, int ntiles) {
+k_gate_tc(const __grid_constant__ CUtensorMap tmap_c, const __grid_constant__ CUtensorMap tmap_wov,
+          const __grid_constant__ CUtensorMap tmap_h, GateArgs a, int ntn, int ntiles) {
   using namespace umma;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -131,11 +135,14 @@ k_gate_tc(const __grid_constant__ CUtensorMap tmap_c, const __grid_constant__ CU
   constexpr int kStageB = NT * 128;
   uint8_t* sA = sm;
   uint8_t* sB = sm + kGStages * kGStageA;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + kGStages * kStageB);   // [kGStages]
+  uint8_t* sH = sB + kGStages * kStageB;                                     // [kGHSlots][128 rows][128 B]
+  uint64_t* full = reinterpret_cast<uint64_t*>(sH + kGHSlots * kGHTile);     // [kGStages]
   uint64_t* empty = full + kGStages;                                         // [kGStages]
   uint64_t* tfull = empty + kGStages;                                        // [2] accumulator ready
   uint64_t* tempty = tfull + 2;                                              // [2] accumulator drained
-  uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* hfull = tempty + 2;                                              // [kGHSlots]
+  uint64_t* hempty = hfull + kGHSlots;                                       // [kGHSlots]
+  uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(hempty + kGHSlots);
 
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
   const int d = a.d;
@@ -150,9 +157,14 @@ k_gate_tc(const __grid_constant__ CUtensorMap tmap_c, const __grid_constant__ CU
       mbar_init(tfull + i, 1);
       mbar_init(tempty + i, kGEpiWarps);
     }
+    for (int i = 0; i < kGHSlots; ++i) {
+      mbar_init(hfull + i, 1);
+      mbar_init(hempty + i, 4);                // the four warps (row quadrants) of one half read a chunk
+    }
     fence_mbar_init();
     prefetch_tensormap(&tmap_c);
     prefetch_tensormap(&tmap_wov);
+    prefetch_tensormap(&tmap_h);
   }
   if (wid == 1) {
     tmem_alloc(tmem_base_s, 2 * NT);
@@ -202,52 +214,60 @@ k_gate_tc(const __grid_constant__ CUtensorMap tmap_c, const __grid_constant__ CU
         mma_commit(tfull + b);
       }
     }
+  } else if (wid == 2) {
+    if (lane == 0) {                      // h producer: chunk cc (tile j, column chunk ch) into slot cc % kGHSlots
+      int cc = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+        const int m0 = (tile / ntn) * kGTM, n0 = (tile % ntn) * NT;
+        for (int ch = 0; ch * 32 < NT; ++ch, ++cc) {
+          const int sl = cc % kGHSlots;
+          if (cc >= kGHSlots && !(ok = mbar_wait(hempty + sl, ((cc / kGHSlots) - 1) & 1, a.status))) break;
+          mbar_expect_tx(hfull + sl, (uint32_t)kGHTile);
+          tma_load_2d(sH + sl * kGHTile, &tmap_h, n0 + ch * 32, m0, hfull + sl);
+        }
+      }
+    }
   } else {                                // epilogue
-    const int q4 = wid & 3, half = (wid - 2) >> 2;
+    const int q4 = wid & 3, half = (wid - 3) >> 2;
     const uint32_t trow = tmem + ((uint32_t)(q4 * 32) << 16);
+    const int r = q4 * 32 + lane;         // tile row of this thread
+    const int nch = NT / 32;
     int j = 0;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++j) {
       const int b = j & 1;
       const int64_t m0 = (int64_t)(tile / ntn) * kGTM;
       const int n0 = (tile % ntn) * NT;
-      const int64_t g = m0 + q4 * 32 + lane;
+      const int64_t g = m0 + r;
       const bool row_ok = g < M;
       const float sg = row_ok ? a.sigma[g] : 0.f;
-      const float4* hrow = reinterpret_cast<const float4*>(a.h + g * d + n0);
       float4* orow = reinterpret_cast<float4*>(a.out + g * d + n0);
-      float4 hv[8];
-      if (row_ok) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) hv[i] = __ldg(hrow + half * 8 + i);
-      }
       if (!mbar_wait(tfull + b, (j >> 1) & 1, a.status)) break;
       tc_fence_after();
+      bool ok = true;
 #pragma unroll 1
-      for (int ch = half; ch * 32 < NT; ch += 2) {
+      for (int ch = half; ch < nch; ch += 2) {
+        const int cc = j * nch + ch, sl = cc % kGHSlots;
         float v[32];
         tmem_ld32(trow + (uint32_t)(b * NT + ch * 32), v);
-        float4 hn[8];
-        const bool more = (ch + 2) * 32 < NT;
-        if (row_ok && more) {
-#pragma unroll
-          for (int i = 0; i < 8; ++i) hn[i] = __ldg(hrow + (ch + 2) * 8 + i);
-        }
+        if (!(ok = mbar_wait(hfull + sl, (cc / kGHSlots) & 1, a.status))) break;
+        const uint8_t* hs = sH + sl * kGHTile + r * 128;
         if (row_ok) {
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
+            const float4 hv = *reinterpret_cast<const float4*>(hs + ((i ^ (r & 7)) << 4));
             float4 o;
-            o.x = __fadd_rn(hv[i].x, round_bf16(__fmul_rn(sg, round_bf16(v[4 * i]))));
-            o.y = __fadd_rn(hv[i].y, round_bf16(__fmul_rn(sg, round_bf16(v[4 * i + 1]))));
-            o.z = __fadd_rn(hv[i].z, round_bf16(__fmul_rn(sg, round_bf16(v[4 * i + 2]))));
-            o.w = __fadd_rn(hv[i].w, round_bf16(__fmul_rn(sg, round_bf16(v[4 * i + 3]))));
+            o.x = __fadd_rn(hv.x, round_bf16(__fmul_rn(sg, round_bf16(v[4 * i]))));
+            o.y = __fadd_rn(hv.y, round_bf16(__fmul_rn(sg, round_bf16(v[4 * i + 1]))));
+            o.z = __fadd_rn(hv.z, round_bf16(__fmul_rn(sg, round_bf16(v[4 * i + 2]))));
+            o.w = __fadd_rn(hv.w, round_bf16(__fmul_rn(sg, round_bf16(v[4 * i + 3]))));
             orow[ch * 8 + i] = o;
           }
         }
-        if (more) {
-#pragma unroll
-          for (int i = 0; i < 8; ++i) hv[i] = hn[i];
-        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(hempty + sl);
       }
+      if (!ok) break;
       // this warp has read its part of accumulator b
       tc_fence_before();
       __syncwarp();
@@ -264,7 +284,8 @@ k_gate_tc(const __grid_constant__ CUtensorMap tmap_c, const __grid_constant__ CU
 
 template <int NT>
 static size_t gate_tc_smem() {
-  return 1024 + (size_t)kGStages * (kGStageA + (size_t)NT * 128) + (2 * kGStages + 4) * 8 + 16;
+  return 1024 + (size_t)kGStages * (kGStageA + (size_t)NT * 128) + (size_t)kGHSlots * kGHTile +
+         (2 * kGStages + 4 + 2 * kGHSlots) * 8 + 16;
 }
 
 static int sm_count() {
@@ -285,14 +306,15 @@ int gate_tc_tile(int d) {
 }
 
 template <int NT>
-static int launch_gate_tc_t(const GateArgs& a, const CUtensorMap& mc, const CUtensorMap& mw, cudaStream_t s) {
+static int launch_gate_tc_t(const GateArgs& a, const CUtensorMap& mc, const CUtensorMap& mw, const CUtensorMap& mh,
+                            cudaStream_t s) {
   const size_t smem = gate_tc_smem<NT>();
   cudaFuncSetAttribute(k_gate_tc<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   const int64_t M = a.B * a.L;
   const int64_t ntiles = ((M + kGTM - 1) / kGTM) * (a.d / NT);
   if (ntiles >= ((int64_t)1 << 31)) return ASRN_ERR_UNSUPPORTED;
   const int grid = (int)std::min<int64_t>(ntiles, sm_count());
-  k_gate_tc<NT><<<grid, kGThreads, smem, s>>>(mc, mw, a, a.d / NT, (int)ntiles);
+  k_gate_tc<NT><<<grid, kGThreads, smem, s>>>(mc, mw, mh, a, a.d / NT, (int)ntiles);
   return cudaGetLastError() == cudaSuccess ? ASRN_OK : ASRN_ERR_CUDA;
 }
 
@@ -300,14 +322,15 @@ int launch_gate_tc(const GateArgs& a, int nt, cudaStream_t s) {
   const int64_t M = a.B * a.L;
   k_gate_prep<<<(unsigned)((M + 7) / 8), 256, 0, s>>>(a);
   if (cudaGetLastError() != cudaSuccess) return ASRN_ERR_CUDA;
-  CUtensorMap mc, mw;
+  CUtensorMap mc, mw, mh;
   if (!make_tmap_bf16(&mc, a.cbuf, (uint64_t)a.d, (uint64_t)M, (uint64_t)a.d * 2, 64, 128) ||
-      !make_tmap_bf16(&mw, a.wov, (uint64_t)a.d, (uint64_t)a.d, (uint64_t)a.d * 2, 64, (uint32_t)nt))
+      !make_tmap_bf16(&mw, a.wov, (uint64_t)a.d, (uint64_t)a.d, (uint64_t)a.d * 2, 64, (uint32_t)nt) ||
+      !make_tmap_f32_sw128(&mh, a.h, (uint64_t)a.d, (uint64_t)M, (uint64_t)a.d * 4, 32, 128))
     return ASRN_ERR_CUDA;
   switch (nt) {
-    case 256: return launch_gate_tc_t<256>(a, mc, mw, s);
-    case 128: return launch_gate_tc_t<128>(a, mc, mw, s);
-    case 64: return launch_gate_tc_t<64>(a, mc, mw, s);
+    case 256: return launch_gate_tc_t<256>(a, mc, mw, mh, s);
+    case 128: return launch_gate_tc_t<128>(a, mc, mw, mh, s);
+    case 64: return launch_gate_tc_t<64>(a, mc, mw, mh, s);
     default: return ASRN_ERR_UNSUPPORTED;
   }
 }

@@ -249,6 +249,9 @@ int launch_prepare(const asrn_layer_config& c, const asrn_layer_weights& w, void
 // 2-D bf16 TMA tensor map, 128-byte swizzle: rows of `inner` elements (row stride in bytes), box inner x outer.
 bool make_tmap_f32(void* map /* CUtensorMap */, const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes,
                    uint32_t box_inner, uint32_t box_outer);
+// The same with the 128-byte shared-memory swizzle (box_inner = 32 fp32).
+bool make_tmap_f32_sw128(void* map /* CUtensorMap */, const void* base, uint64_t inner, uint64_t outer,
+                         uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer);
 // Rows of a bf16 matrix for row gathers: box = one row of box_inner elements, swizzle of `swizzle_bytes` (0, 32, 64
 // or 128; with a swizzle, box_inner * 2 equals it).
 bool make_tmap_rows_bf16(void* map /* CUtensorMap */, const void* base, uint64_t inner, uint64_t outer,

@@ -70,6 +70,21 @@ bool make_tmap_f32(void* map, const void* base, uint64_t inner, uint64_t outer, 
   return r == CUDA_SUCCESS;
 }
 
+// Row-major fp32 matrix (outer, inner), boxes of box_inner x box_outer with the 128-byte swizzle (box_inner = 32).
+bool make_tmap_f32_sw128(void* map, const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes,
+                         uint32_t box_inner, uint32_t box_outer) {
+  PFN_cuTensorMapEncodeTiled_v12000 fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t elem[2] = {1, 1};
+  CUresult r = fn(reinterpret_cast<CUtensorMap*>(map), CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base),
+                  dims, strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 bool tensor_cores_enabled() {
   const char* v = getenv("ASRN_B200_GEMM");
   return !(v && strcmp(v, "simt") == 0);
