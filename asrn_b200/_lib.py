@@ -9,9 +9,9 @@ import os
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, 'libasrn_b200.so')
-ABI_VERSION = 3
+ABI_VERSION = 4
 
-ASRN_OK, ASRN_ERR_ARG, ASRN_ERR_UNSUPPORTED, ASRN_ERR_WORKSPACE, ASRN_ERR_CUDA, ASRN_ERR_TIMEOUT = range(6)
+ASRN_OK, ASRN_ERR_ARG, ASRN_ERR_UNSUPPORTED, ASRN_ERR_WORKSPACE, ASRN_ERR_CUDA, ASRN_ERR_TIMEOUT, ASRN_ERR_DATA = range(7)
 
 
 class LayerConfig(ctypes.Structure):
@@ -98,10 +98,12 @@ _SIGS = {
                                         _P, _P, _P, _P, ctypes.c_size_t, _P]),
     'asrn_shard_merge': (ctypes.c_int, [ctypes.c_int64, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int64,
                                         ctypes.c_int32, _P, _P, _P, ctypes.c_int64, _P, _P, _P, ctypes.c_int64, _P,
-                                        ctypes.c_size_t, _P]),
+                                        ctypes.c_size_t, _P, _P]),
     'asrn_gen_gate': (ctypes.c_int, [_P] * 16),
     'asrn_gate_workspace_bytes': (ctypes.c_size_t, [_P]),
     'asrn_gate': (ctypes.c_int, [_P] * 14 + [ctypes.c_size_t, _P]),
+    'asrn_test_force_cuda_core': (ctypes.c_int, [ctypes.c_int]),
+    'asrn_test_bounded_wait': (ctypes.c_int, [ctypes.c_uint64, _P, _P, _P]),
 }
 
 
@@ -127,6 +129,24 @@ def lib():
             raise RuntimeError(f'libasrn_b200.so ABI version {v}, expected {ABI_VERSION}: rebuild it')
         _lib = handle
     return _lib
+
+
+def gemm_override():
+    """'cuda_core' while the test hook asrn_test_force_cuda_core holds the bf16 work on the CUDA-core kernels, else
+    None (the default: tensor cores)."""
+    return 'cuda_core' if lib().asrn_test_force_cuda_core(-1) else None
+
+
+class force_cuda_core:
+    """Test hook as a context manager: the bf16 work inside runs on the CUDA-core kernels."""
+
+    def __enter__(self):
+        self.prev = lib().asrn_test_force_cuda_core(1)
+        return self
+
+    def __exit__(self, *exc):
+        lib().asrn_test_force_cuda_core(self.prev)
+        return False
 
 
 def check(status, what):

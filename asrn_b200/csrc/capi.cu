@@ -155,12 +155,13 @@ const char* asrn_status_string(int status) {
     case ASRN_ERR_UNSUPPORTED: return "option combination not supported by this build";
     case ASRN_ERR_WORKSPACE: return "workspace or prepared buffer too small";
     case ASRN_ERR_CUDA: return "CUDA kernel launch failed";
+    case ASRN_ERR_DATA: return "state received from another shard failed validation (corrupt or from a faulty rank)";
     case ASRN_ERR_TIMEOUT: return "bounded device wait timed out";
     default: return "unknown status";
   }
 }
 
-int asrn_abi_version(void) { return 3; }
+int asrn_abi_version(void) { return 4; }
 
 size_t asrn_layer_prepared_bytes(const asrn_layer_config* cfg) {
   if (check_config(cfg) != ASRN_OK) return 0;
@@ -345,7 +346,7 @@ int asrn_shard_tails(int64_t rows, int64_t Lc, int32_t nb, int32_t C, int64_t c0
 int asrn_shard_merge(int64_t rows, int64_t Lc, int32_t nb, int32_t C, int64_t c0, int32_t n_prev,
                      const int32_t* tails_prev, const int32_t* orden_loc, const uint16_t* ids_loc, int64_t Lv,
                      int32_t* orden_v, uint16_t* ids_v, int64_t* row_len, int64_t L, void* workspace,
-                     size_t workspace_bytes, void* stream) {
+                     size_t workspace_bytes, int* status, void* stream) {
   if (rows < 0 || Lc < 1 || nb < 1 || nb > 15 || C < 1 || C > 32 || c0 < 0 || n_prev < 0 || L < c0 + Lc ||
       L >= ((int64_t)1 << 31) || (c0 == 0 && c0 + Lc == L) || (n_prev > 0 && !tails_prev) ||
       (rows > 0 && (!orden_loc || !ids_loc || !orden_v || !ids_v || !row_len)))
@@ -356,7 +357,7 @@ int asrn_shard_merge(int64_t rows, int64_t Lc, int32_t nb, int32_t C, int64_t c0
   if (!workspace || workspace_bytes < shard_merge_workspace(rows, nb)) return ASRN_ERR_WORKSPACE;
   const int32_t pad_pos = (int32_t)(c0 > 0 ? 0 : c0 + Lc);
   return launch_shard_merge(rows, Lc, nb, C, c0, n_prev, tails_prev, orden_loc, ids_loc, Lv, orden_v, ids_v, row_len,
-                            pad_pos, workspace, as_stream(stream));
+                            pad_pos, status, workspace, as_stream(stream));
 }
 
 int asrn_score_shard(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared, int64_t L_feat,

@@ -208,7 +208,7 @@ int launch_shard_tails(int64_t rows, int64_t Lc, int nb, int C, int64_t c0, cons
                        const uint16_t* ids_loc, int32_t* tails, void* ws, cudaStream_t s);
 int launch_shard_merge(int64_t rows, int64_t Lc, int nb, int C, int64_t c0, int n_prev, const int32_t* tails_prev,
                        const int32_t* orden_loc, const uint16_t* ids_loc, int64_t Lv, int32_t* orden_v,
-                       uint16_t* ids_v, int64_t* row_len, int32_t pad_pos, void* ws, cudaStream_t s);
+                       uint16_t* ids_v, int64_t* row_len, int32_t pad_pos, int* status, void* ws, cudaStream_t s);
 size_t ngram_chunk_workspace(int64_t B, int64_t Lc, int n);
 int launch_ngram_chunk_sort(const RepetitionArgs& a, uint64_t* keys, void* summary, void* ws, size_t ws_bytes,
                             cudaStream_t s);
@@ -258,7 +258,8 @@ bool make_tmap_rows_bf16(void* map /* CUtensorMap */, const void* base, uint64_t
                          uint64_t row_bytes, uint32_t box_inner, int swizzle_bytes);
 bool make_tmap_bf16(void* map /* CUtensorMap */, const void* base, uint64_t inner, uint64_t outer,
                     uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer);
-// GEMM implementation choice: false when ASRN_B200_GEMM=simt forces the CUDA-core kernels (for cross-checks).
+// GEMM implementation choice: false while the test hook asrn_test_force_cuda_core holds the CUDA-core kernels.
 bool tensor_cores_enabled();
+int set_force_cuda_core(int on);
 
 }  // namespace asrn

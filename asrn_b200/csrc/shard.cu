@@ -145,16 +145,39 @@ __global__ void k_shard_tails(int64_t rows, int nbins, int C, int64_t c0, const 
   for (int j = 0; j < cnt; ++j) t[1 + j] = (int32_t)(c0 + orden_loc[row * Lc + end - cnt + j]);
 }
 
+// A tail received from shard p (chunk [p Lc, (p + 1) Lc)) is used only if it is consistent: count in [0, C] and its
+// positions strictly ascending inside the sender's chunk. Anything else (a carry corrupted in transit, a faulty rank)
+// would index features out of range later: such a tail is treated as empty and ASRN_ERR_DATA is recorded.
+__device__ __forceinline__ bool tail_valid(const int32_t* t, int C, int64_t lo, int64_t hi) {
+  const int cnt = t[0];
+  if (cnt < 0 || cnt > C) return false;
+  int64_t prev = lo - 1;
+  for (int e = 1; e <= cnt; ++e) {
+    const int64_t q = t[e];
+    if (q <= prev || q >= hi) return false;
+    prev = q;
+  }
+  return true;
+}
+
 // per (row, bucket): ring length (0 without local slots) and ring + local length
-__global__ void k_shard_sizes(int64_t rows, int nbins, int C, int n_prev, const int32_t* __restrict__ tails_prev,
-                              const int32_t* __restrict__ run_beg, const int32_t* __restrict__ run_end,
-                              int32_t* __restrict__ ring, int32_t* __restrict__ tot) {
+__global__ void k_shard_sizes(int64_t rows, int64_t Lc, int nbins, int C, int n_prev,
+                              const int32_t* __restrict__ tails_prev, const int32_t* __restrict__ run_beg,
+                              const int32_t* __restrict__ run_end, int32_t* __restrict__ ring,
+                              int32_t* __restrict__ tot, int* status) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= rows * nbins) return;
   const int local = run_end[i] - run_beg[i];
   int r = 0;
   if (local > 0)
-    for (int p = n_prev - 1; p >= 0 && r < C; --p) r += tails_prev[((int64_t)p * rows * nbins + i) * (C + 1)];
+    for (int p = n_prev - 1; p >= 0 && r < C; --p) {
+      const int32_t* t = tails_prev + ((int64_t)p * rows * nbins + i) * (C + 1);
+      if (!tail_valid(t, C, p * Lc, (p + 1) * Lc)) {
+        if (status) atomicCAS(status, ASRN_OK, ASRN_ERR_DATA);
+        continue;
+      }
+      r += t[0];
+    }
   r = min(r, C);
   ring[i] = r;
   tot[i] = r + local;
@@ -205,9 +228,10 @@ __global__ void k_shard_pad(int64_t n, int32_t pad_pos, int32_t* __restrict__ or
 }
 
 // ring entries: the j-th most recent earlier position of the bucket goes to slot off + ring - 1 - j
-__global__ void k_shard_write_ring(int64_t rows, int nbins, int C, int n_prev, const int32_t* __restrict__ tails_prev,
-                                   const int32_t* __restrict__ ring, const int32_t* __restrict__ off, int64_t Lv,
-                                   int32_t* __restrict__ orden_v, uint16_t* __restrict__ ids_v) {
+__global__ void k_shard_write_ring(int64_t rows, int64_t Lc, int nbins, int C, int n_prev,
+                                   const int32_t* __restrict__ tails_prev, const int32_t* __restrict__ ring,
+                                   const int32_t* __restrict__ off, int64_t Lv, int32_t* __restrict__ orden_v,
+                                   uint16_t* __restrict__ ids_v) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= rows * nbins) return;
   const int r = ring[i];
@@ -218,6 +242,7 @@ __global__ void k_shard_write_ring(int64_t rows, int nbins, int C, int n_prev, c
   int j = 0;
   for (int p = n_prev - 1; p >= 0 && j < r; --p) {
     const int32_t* t = tails_prev + ((int64_t)p * rows * nbins + i) * (C + 1);
+    if (!tail_valid(t, C, p * Lc, (p + 1) * Lc)) continue;      // skipped by k_shard_sizes too
     for (int e = t[0]; e >= 1 && j < r; --e, ++j) {
       orden_v[base + r - 1 - j] = t[e];
       ids_v[base + r - 1 - j] = (uint16_t)bucket;
@@ -261,7 +286,7 @@ int launch_shard_tails(int64_t rows, int64_t Lc, int nb, int C, int64_t c0, cons
 
 int launch_shard_merge(int64_t rows, int64_t Lc, int nb, int C, int64_t c0, int n_prev, const int32_t* tails_prev,
                        const int32_t* orden_loc, const uint16_t* ids_loc, int64_t Lv, int32_t* orden_v,
-                       uint16_t* ids_v, int64_t* row_len, int32_t pad_pos, void* ws, cudaStream_t s) {
+                       uint16_t* ids_v, int64_t* row_len, int32_t pad_pos, int* status, void* ws, cudaStream_t s) {
   const int nbins = 1 << nb;
   const size_t part = align_up((size_t)rows * nbins * 4);
   char* w = reinterpret_cast<char*>(ws);
@@ -272,10 +297,10 @@ int launch_shard_merge(int64_t rows, int64_t Lc, int nb, int C, int64_t c0, int 
   if (cudaMemsetAsync(ws, 0, 2 * part, s) != cudaSuccess) return ASRN_ERR_CUDA;
   const unsigned gb = blocks_for(rows * nbins, kBinT);
   if (rows * Lc > 0) k_shard_runs<<<blocks_for(rows * Lc, kBinT), kBinT, 0, s>>>(rows, Lc, nbins, ids_loc, beg, end);
-  k_shard_sizes<<<gb, kBinT, 0, s>>>(rows, nbins, C, n_prev, tails_prev, beg, end, ring, off);
+  k_shard_sizes<<<gb, kBinT, 0, s>>>(rows, Lc, nbins, C, n_prev, tails_prev, beg, end, ring, off, status);
   k_shard_scan<<<(unsigned)rows, 1024, 0, s>>>(off, nbins, row_len);
   k_shard_pad<<<blocks_for(rows * Lv, kBinT), kBinT, 0, s>>>(rows * Lv, pad_pos, orden_v, ids_v);
-  k_shard_write_ring<<<gb, kBinT, 0, s>>>(rows, nbins, C, n_prev, tails_prev, ring, off, Lv, orden_v, ids_v);
+  k_shard_write_ring<<<gb, kBinT, 0, s>>>(rows, Lc, nbins, C, n_prev, tails_prev, ring, off, Lv, orden_v, ids_v);
   if (rows * Lc > 0)
     k_shard_write_local<<<blocks_for(rows * Lc, kBinT), kBinT, 0, s>>>(rows, Lc, nbins, c0, orden_loc, ids_loc, beg,
                                                                        ring, off, Lv, orden_v, ids_v);

@@ -1,5 +1,6 @@
 // Host helpers: TMA tensor maps (through the driver entry point, so the library needs no -lcuda) and the GEMM
 // implementation switch.
+#include <atomic>
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <stdlib.h>
@@ -85,9 +86,15 @@ bool make_tmap_f32_sw128(void* map, const void* base, uint64_t inner, uint64_t o
   return r == CUDA_SUCCESS;
 }
 
-bool tensor_cores_enabled() {
-  const char* v = getenv("ASRN_B200_GEMM");
-  return !(v && strcmp(v, "simt") == 0);
+// Test hook (asrn_test_force_cuda_core): 1 routes bf16 work to the CUDA-core kernels for cross-checks. Only that
+// entry point sets it; nothing reads the environment.
+static std::atomic<int> g_force_cuda_core{0};
+
+bool tensor_cores_enabled() { return g_force_cuda_core.load(std::memory_order_relaxed) == 0; }
+
+int set_force_cuda_core(int on) {
+  if (on < 0) return g_force_cuda_core.load();
+  return g_force_cuda_core.exchange(on ? 1 : 0);
 }
 
 }  // namespace asrn

@@ -48,17 +48,20 @@ ASRN_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // Bounded wait for the phase with the given parity to complete. false: timed out (status word set). Once the status
 // word records a timeout, later waits that do not complete at once give up immediately, so a kernel whose copies
 // never arrive ends after one wait limit rather than one per wait.
-ASRN_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, int* status) {
+ASRN_DEV bool mbar_wait_limit(uint64_t* bar, uint32_t parity, int* status, uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   if (status && *reinterpret_cast<volatile int*>(status) == ASRN_ERR_TIMEOUT) return false;
   const uint64_t t0 = global_ns();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (global_ns() - t0 > kWaitLimitNs) {
+    if (global_ns() - t0 > limit_ns) {
       if (status) atomicCAS(status, ASRN_OK, ASRN_ERR_TIMEOUT);
       return false;
     }
   }
+}
+ASRN_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, int* status) {
+  return mbar_wait_limit(bar, parity, status, kWaitLimitNs);
 }
 
 // 2-D tiled TMA load of a box into shared memory, completing transaction bytes on `bar`.

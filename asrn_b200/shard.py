@@ -22,6 +22,14 @@ sequence (L = world * Lc, equal chunks) and computes h' for them:
 (the exchange becomes concatenation), so that the sharded algorithm can be checked against the unsharded layer on one
 GPU. The exchange is NCCL collectives only (no peer-memory loads in the kernels). No step waits on the host: every
 shard row's length stays on the device (the rows are sized by a bound, the scoring kernel stops at each row's end).
+
+Failure detection. Every received carry is checked on the device: the chunk sums of beta (finite, >= 0), the streak
+maps (A in [0, 1], B0 finite and >= 0), the sorted n-gram keys (ascending) and, inside asrn_shard_merge, each bucket
+tail it uses (count in [0, C], positions ascending inside the sender's chunk; an inconsistent tail is treated as empty,
+so it cannot index features out of range). The result lands in a device status word whose copy to the host is read
+without stalling the stream: the next forward raises ShardExchangeError if the previous one saw a violation, and
+check_exchange(device) waits for it. A rank that is late beyond the process group's timeout, or that left, makes the
+other ranks' next collective fail with the backend's error (give the group a short timeout).
 """
 import torch
 
@@ -29,6 +37,76 @@ from . import _lib, stages
 from .layer import compute_half, ctypes_ref
 
 _SEQ_KEYS = ('phi', 'Qc', 'Kc', 'sig', 'log_alfa', 'beta', 'Bt', 'Ea')
+
+
+class ShardExchangeError(RuntimeError):
+    """State received from another shard broke its invariants (corrupted in transit or sent by a faulty rank)."""
+
+
+def carry_violations(sums=None, maps=None, keys=None, tails=None, Lc=None, C=None):
+    """Number of invariant violations (int64 tensor on the carries' device; 0 = consistent) in exchanged carries:
+      sums  (world, B) fp64 chunk sums of beta: finite and >= 0 (beta = min(softplus, beta_max) >= 0);
+      maps  (world, B, 2) streak maps S_last = A S_before + B0: A in [0, 1], B0 finite and >= 0;
+      keys  (world, B * n, Lc) sorted n-gram keys: ascending along the last dimension;
+      tails (world, rows, 2^nb, C + 1) bucket tails: count in [0, C], positions strictly ascending inside the sender's
+            chunk [r Lc, (r + 1) Lc). (On the GPU the merge kernel checks the tails it uses; this full scan is for the
+            host-side path.)"""
+    bad = []
+    if sums is not None:
+        bad.append((~torch.isfinite(sums) | (sums < 0)).sum())
+    if maps is not None:
+        A, B0 = maps[..., 0], maps[..., 1]
+        bad.append((~torch.isfinite(maps).all(-1) | (A < 0) | (A > 1) | (B0 < 0)).sum())
+    if keys is not None and keys.shape[-1] > 1:
+        k = keys.view(torch.int64) if keys.dtype != torch.int64 else keys
+        # order-preserving images of the fp64 keys are unsigned 64-bit: compare with the sign bit flipped
+        flip = torch.bitwise_xor(k, torch.tensor(-(1 << 63), dtype=torch.int64, device=k.device))
+        bad.append((flip[..., 1:] < flip[..., :-1]).sum())
+    if tails is not None:
+        world = tails.shape[0]
+        cnt = tails[..., 0].to(torch.int64)
+        pos = tails[..., 1:].to(torch.int64)
+        used = torch.arange(C, device=tails.device) < cnt.unsqueeze(-1)
+        lo = (torch.arange(world, device=tails.device, dtype=torch.int64) * Lc).view(world, 1, 1, 1)
+        out = used & ((pos < lo) | (pos >= lo + Lc))
+        desc = used[..., 1:] & (pos[..., 1:] <= pos[..., :-1])
+        bad += [((cnt < 0) | (cnt > C)).sum(), out.sum(), desc.sum()]
+    if not bad:
+        return torch.zeros((), dtype=torch.int64)
+    return torch.stack([b.to(torch.int64) for b in bad]).sum()
+
+
+_pending = {}
+
+
+def _defer_status(status):
+    """Copy a step's status word to pinned host memory behind the step's work; read it at the next forward."""
+    dev = status.device
+    host = torch.empty(1, dtype=torch.int32, pin_memory=True)
+    host.copy_(status.view(1), non_blocking=True)
+    ev = torch.cuda.Event()
+    ev.record(torch.cuda.current_stream(dev))
+    _pending[dev] = (host, ev)
+
+
+def _raise_reported(dev, block):
+    item = _pending.get(dev)
+    if item is None:
+        return
+    host, ev = item
+    if not block and not ev.query():
+        return
+    ev.synchronize()
+    del _pending[dev]
+    st = int(host.item())
+    if st != 0:
+        raise ShardExchangeError(f'a sharded forward received inconsistent state from another shard (status {st}: '
+                                 f'{_lib.lib().asrn_status_string(st).decode() if st < 16 else "invalid carries"})')
+
+
+def check_exchange(device):
+    """Wait for the last sharded forward on `device` and raise ShardExchangeError if it received inconsistent state."""
+    _raise_reported(torch.device(device), block=True)
 
 
 def chunk_bounds(L, world, rank):
@@ -77,9 +155,10 @@ def _tails(layer, orden_loc, ids_loc, c0):
     return tails
 
 
-def shard_rows(layer, orden_loc, ids_loc, tails_prev, c0, L):
+def shard_rows(layer, orden_loc, ids_loc, tails_prev, c0, L, status=None):
     """The shard's sorted rows from its sorted chunk and the earlier ranks' tails (n_prev, rows, 2^nb, C + 1):
-    (orden_v, ids_v) (rows, Lv) and the used length of every row (rows,) int64, all on the device."""
+    (orden_v, ids_v) (rows, Lv) and the used length of every row (rows,) int64, all on the device. status (1,) int32
+    on the device (optional) receives ASRN_ERR_DATA if a received tail is inconsistent."""
     rows, Lc = orden_loc.shape
     dev = orden_loc.device
     C, nb = layer.chunk, layer.n_bits
@@ -92,7 +171,8 @@ def shard_rows(layer, orden_loc, ids_loc, tails_prev, c0, L):
     _lib.check(_lib.lib().asrn_shard_merge(rows, Lc, nb, C, c0, n_prev,
                                            None if n_prev == 0 else _lib.ptr(tails_prev), _lib.ptr(orden_loc),
                                            _lib.ptr(ids_loc), Lv, _lib.ptr(orden_v), _lib.ptr(ids_v),
-                                           _lib.ptr(row_len), L, _lib.ptr(ws), ws.numel(), _lib.stream_ptr(dev)),
+                                           _lib.ptr(row_len), L, _lib.ptr(ws), ws.numel(), _lib.ptr(status),
+                                           _lib.stream_ptr(dev)),
                'asrn_shard_merge')
     return orden_v, ids_v, row_len
 
@@ -105,7 +185,7 @@ def _apply_clock_offsets(Bt_full, chunk_sums, Lc):
     return Bt_full
 
 
-def _phase2(layer, loc, full, tails_prev, rep, h, c0, c1, half):
+def _phase2(layer, loc, full, tails_prev, rep, h, c0, c1, half, status=None):
     """Scoring and gate of the chunk [c0, c1) from the gathered full-sequence features, the earlier ranks' bucket
     tails and the chunk's n-gram memory rep = (vistos, hawkes, racha)."""
     B, L = full['sig'].shape
@@ -113,7 +193,7 @@ def _phase2(layer, loc, full, tails_prev, rep, h, c0, c1, half):
     dev = h.device
     lib = _lib.lib()
     s = _lib.stream_ptr(dev)
-    orden_v, ids_v, row_len = shard_rows(layer, loc['orden'], loc['ids'], tails_prev, c0, L)
+    orden_v, ids_v, row_len = shard_rows(layer, loc['orden'], loc['ids'], tails_prev, c0, L, status)
     Lv = orden_v.shape[1]
     Lc = c1 - c0
     d = layer.d
@@ -327,6 +407,7 @@ def forward(layer, E, h, tokens=None, group=None):
     same shapes; the collectives are the same on every rank, in the same order."""
     import torch.distributed as dist
     _check(layer, E, h, tokens)
+    _raise_reported(E.device, block=False)
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
     half = compute_half('cuda')
@@ -358,4 +439,9 @@ def forward(layer, E, h, tokens=None, group=None):
     _, rmap = racha_chunk(layer, vistos, loc['beta'], None, half, want_racha=False)
     maps = exchange_racha_maps(rmap, world, group)
     racha, _ = racha_chunk(layer, vistos, loc['beta'], racha_before(maps, rank), half)
-    return _phase2(layer, loc, full, tails[:rank] if rank > 0 else None, (vistos, hawkes, racha), h, c0, c1, half)
+    status = carry_violations(sums=sums, maps=maps, keys=keys).clamp(max=1).to(torch.int32).mul(
+        _lib.ASRN_ERR_DATA).view(1)
+    out = _phase2(layer, loc, full, tails[:rank] if rank > 0 else None, (vistos, hawkes, racha), h, c0, c1, half,
+                  status)
+    _defer_status(status)
+    return out

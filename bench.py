@@ -3,26 +3,36 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
     python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 --master-port P bench.py --gpus N ...
 
-Workload (configuration 3 of the benchmark, the layer metric): one ASRNLayer(768) forward with default options on
-32 sequences x 8192 tokens per GPU, fp32 E/h as the model passes them, bf16 autocast; tokens Zipf(1.1) over 50,304
+Headline workload (configuration 3 of the benchmark, the layer metric): one ASRNLayer(768) forward with default options
+on 32 sequences x 8192 tokens per GPU, fp32 E/h as the model passes them, bf16 autocast; tokens Zipf(1.1) over 50,304
 with 20 % of positions in planted repeats of length 16-256 (seeded synthetic data, asrn_b200/synthetic.py), E rows from
-a random embedding table, random-init weights with the neutral parameters moved off zero. A step is one layer forward
-over the GPU's batch. Batches shard across GPUs with no collective, so per-GPU work is fixed (weak scaling).
+a random embedding table (std 0.02, the model's initialisation), random-init weights with the neutral parameters moved
+off zero. A step is one layer forward over the GPU's batch. Batches shard across GPUs with no collective, so per-GPU
+work is fixed (weak scaling).
 
-Printed (rank 0, one JSON line): value = tokens/s of the whole job (all ranks' tokens / max-over-ranks device time of
-K steps, inputs resident in HBM; the 805 MB E and h per GPU exceed the 126 MB L2, so no flush is needed), e2e = the
-same through ASRNLayer.forward with pinned host buffers and H2D/D2H copies in the timed region, roofline of the
-dominant kernel (candidate scoring, HBM-bound), the CPU baseline (the oracle port on the host cores), clocks (nvidia-smi
-samples inside the timed region; the sampler starts before the warm-up). Warm-up: at least W steps, then until two
-consecutive steps agree within 3 % (at most 20 more; "warmup" reports the count); then the forward is captured once as a
-CUDA graph and the K timed steps are its replays ("launch": "cuda_graph"; --eager times the eager forward; the
-sequence-sharded cfg4 forward with its NCCL collectives stays eager); "step_ms" gives the spread of the K timed steps
-(CUDA events between them).
-Generation leg (configuration 5, key "generation"): the configuration-3 model (random init), 64 sequences split over
-the GPUs with 65,536-token Zipf+repeat prompts, then greedy steps of the O(1) writer; value = device time per step
-(us per generated token of every sequence), with the same figure at 4,096 and 16,384-token prompts (flatness), the
-prefill rate, and the public generate() API end to end.
---impl reference: times the CPU implementation of the path (oracle port) on the host cores instead.
+Printed (rank 0, one JSON line):
+  value      tokens/s of the whole job: all ranks' tokens / the max-over-ranks device time of K steps, inputs resident
+             in HBM (the 805 MB E and h per GPU exceed the 126 MB L2, so no flush is needed). After the warm-up the
+             forward is captured once as a CUDA graph and the K timed steps are its replays.
+  e2e        the same through ASRNLayer.forward from pinned host buffers: every step copies its E, h and tokens to the
+             device and h' back, on copy streams that overlap step k's compute with step k+1's upload and step k-1's
+             download (PCIe is full duplex).
+  roofline   the dominant kernel (candidate scoring, HBM-bound): its algorithmic bytes per launch / its CUDA-event
+             launch time, against the measured HBM peak (MEASURED_PEAKS.json); traffic from the committed ncu summary.
+  cpu_baseline  the reference's own CPU implementation (asrn.ASRNLayer installed into baseline/_ref, PyTorch on the
+             host cores) on a bounded sample of the same workload.
+  gpu_launches  kernel nodes of the captured forward (ours are named k_*) x K.
+  clocks     nvidia-smi samples inside the timed region.
+Legs in the same line (each with its own value, device timing and the reference's CPU time beside it):
+  generation configuration 5: the configuration-3 model, 64 sequences split over the GPUs, 65,536-token Zipf+repeat
+             prompts, greedy steps of the O(1) writer (CUDA-graph step + device argmax); flatness at 4,096 and 16,384;
+             the public generate() end to end; the reference's _Escritor(o1=True) at batch 4 on the host cores.
+  cfg4       one 262,144-token sequence, ASRNLayer(512), bf16: one GPU, or sequence-sharded over the GPUs of the run
+             (NCCL exchanges of halo, clock offsets, bucket tails, features, n-gram summaries and streak maps).
+  cfg2       ASRNLayer(256) forward in fp32, 16 x 4096 tokens (batch-sharded).
+  cfg1       create_model(V=256, d=64, n_capas=4) forward on 8 x 256 bytes, then generate(top_k=1) of 200 tokens.
+--impl reference: times the reference's CPU implementation of the headline workload (asrn.ASRNLayer from
+baseline/_ref, torch on the host cores, bf16 autocast, chunks of 4 sequences per step) and its O(1) writer.
 """
 import argparse
 import datetime
@@ -38,6 +48,7 @@ import time
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, HERE)
+REF_PATH = os.path.join(HERE, 'baseline', '_ref')
 
 D, L_SEQ, B_PER_GPU, V = 768, 8192, 32, 50304
 METRIC = 'asrn_layer_fwd_tokens_per_s'
@@ -50,6 +61,11 @@ LAYER_BYTES_PER_TOKEN = 34696
 # generation leg (configuration 5): the configuration-3 model, 64 sequences split over the GPUs, 65,536-token prompts,
 # greedy steps; flatness is checked at shorter prompts too
 GEN_B, GEN_L0, GEN_NEW, GEN_FLAT = 64, 65536, 1024, (4096, 16384)
+D4, L4 = 512, 262144
+CFG4_BYTES_PER_TOKEN = 24968     # algorithmic HBM bytes per token of one layer forward at d=512, bf16, fp32 E/h
+D2, B2, L2 = 256, 16, 4096
+CFG2_BYTES_PER_TOKEN = 25256     # d=256, fp32
+REF_CHUNK = 4                    # sequences per step of the reference's CPU timing (its V_o buffer is ~6.5 GB per 4)
 
 
 def parse():
@@ -62,12 +78,14 @@ def parse():
     p.add_argument('--seq', type=int, default=L_SEQ)
     p.add_argument('--no-cpu-baseline', action='store_true')
     p.add_argument('--workload', default='cfg3', choices=['cfg3', 'cfg4'],
-                   help='cfg3: the batch-sharded layer metric (default); cfg4: one 262,144-token sequence, d=512, '
-                        'sequence-sharded over the GPUs')
+                   help='cfg3: the batch-sharded layer metric (default); cfg4: only the cfg4 leg')
     p.add_argument('--no-gen', action='store_true', help='skip the generation leg')
+    p.add_argument('--no-legs', action='store_true', help='skip the cfg1 / cfg2 / cfg4 legs')
     p.add_argument('--eager', action='store_true', help='time the eager forward instead of its CUDA-graph replay')
     p.add_argument('--gen-prompt', type=int, default=GEN_L0, help='prompt length of the generation leg')
     p.add_argument('--gen-steps', type=int, default=GEN_NEW, help='timed generation steps')
+    p.add_argument('--gen-cpu-prompts', default='4096',
+                   help='prompt lengths of the reference writer on the host (comma list; 16384 and 65536 take minutes)')
     return p.parse_args()
 
 
@@ -78,6 +96,15 @@ def config(args, n):
             'parallelism': 'dp%d (batch sharded, no collective)' % n,
             'l2': 'inputs larger than L2 (E and h are %.0f MB each per GPU; L2 is 126 MB), no flush'
                   % (args.batch * args.seq * D * 4 / 1e6)}
+
+
+def peaks():
+    try:
+        with open(os.path.join(HERE, 'MEASURED_PEAKS.json')) as f:
+            p = json.load(f)
+    except (OSError, ValueError):
+        p = {}
+    return p.get('hbm_gbs', 6650.0), ('measured' if 'hbm_gbs' in p else 'fallback')
 
 
 # ---------------------------------------------------------------------------------------------------------------------
@@ -113,31 +140,30 @@ def make_inputs(batch, seq, rank, seed=0):
     return x, E, h, table
 
 
-# ---------------------------------------------------------------------------------------------------------------------
-# clocks during the timed region
-# ---------------------------------------------------------------------------------------------------------------------
+def make_cfg4_inputs(L, c0, c1, rank):
+    import numpy as np
+    from asrn_b200 import synthetic
+    x = synthetic.config_tokens('cfg4', B=1, L=L, seed=0)
+    table = (np.random.default_rng(7).standard_normal((V, D4)) * 0.02).astype(np.float32)
+    xc = np.ascontiguousarray(x[:, c0:c1])
+    Ec = table[xc]
+    hc = (Ec + np.random.default_rng(8 + rank).standard_normal(Ec.shape).astype(np.float32) * 0.5).astype(np.float32)
+    return x, xc, Ec, hc, table
 
 
-def graph_or_eager(step, eager):
-    """The forward captured once as a CUDA graph after the warm-up (only on paths with no collective): the K timed
-    steps are then K graph launches, all enqueued ahead of the device, so a host-side pause cannot leave the GPU idle
-    between steps; the kernels and their work are those of the eager forward. Returns (run, mode, graph)."""
-    import torch
-    if eager:
-        return step, 'eager', None
-    try:
-        side = torch.cuda.Stream()
-        side.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(side):
-            step()
-        torch.cuda.current_stream().wait_stream(side)
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            step()
-        graph.replay()
-        return graph.replay, 'cuda_graph', graph
-    except Exception as exc:              # capture unsupported here: time the eager forward
-        return step, 'eager (graph capture failed: %s)' % type(exc).__name__, None
+def make_cfg2_inputs(batch, rank):
+    import numpy as np
+    from asrn_b200 import synthetic
+    x = synthetic.config_tokens('cfg2', B=batch, L=L2, seed=1000 * rank)
+    g = np.random.default_rng(20 + rank)
+    E = g.standard_normal((batch, L2, D2)).astype(np.float32)
+    h = g.standard_normal((batch, L2, D2)).astype(np.float32)
+    return x, E, h
+
+
+# ---------------------------------------------------------------------------------------------------------------------
+# clocks during the timed region, warm-up, graph capture
+# ---------------------------------------------------------------------------------------------------------------------
 
 class ClockSampler:
     """nvidia-smi clock / throttle-reason samples every 100 ms. Started before the warm-up (nvidia-smi's own start-up
@@ -161,7 +187,6 @@ class ClockSampler:
         except (OSError, FileNotFoundError):
             self.proc = None
             return
-        # wait (up to 10 s) for the first sample: nvidia-smi is up before the GPU work that is measured
         t_end = time.time() + 10
         while time.time() < t_end and os.path.getsize(self.f.name) == 0 and self.proc.poll() is None:
             time.sleep(0.05)
@@ -236,23 +261,136 @@ def warm_up(step, warmup, world):
             return n
 
 
-# ---------------------------------------------------------------------------------------------------------------------
-# CPU baseline: the oracle port (the reference's algorithm restated in numpy) on the host cores
-# ---------------------------------------------------------------------------------------------------------------------
+def count_graph_kernels(graph):
+    """(all kernel nodes, those of libasrn_b200 (named k_*), names) of a captured CUDA graph, or Nones."""
+    try:
+        from cuda.bindings import runtime as rt
+        g = graph.raw_cuda_graph()
+        err, _, n = rt.cudaGraphGetNodes(g, 0)
+        err, nodes, n = rt.cudaGraphGetNodes(g, n)
+        kernels, ours, names = 0, 0, {}
+        for nd in nodes:
+            err, ty = rt.cudaGraphNodeGetType(nd)
+            if ty != rt.cudaGraphNodeType.cudaGraphNodeTypeKernel:
+                continue
+            kernels += 1
+            name = '?'
+            try:
+                err, prm = rt.cudaGraphKernelNodeGetParams(nd)
+                err, nm = rt.cudaFuncGetName(prm.func)
+                name = nm.decode() if isinstance(nm, bytes) else str(nm)
+            except Exception:                         # names are a nicety; the count is what matters
+                pass
+            names[name] = names.get(name, 0) + 1
+            if name.startswith('k_') or 'asrn' in name:
+                ours += 1
+        return kernels, ours, names
+    except Exception:
+        return None, None, None
 
-def _oracle_one(payload):
-    """One sequence through the oracle's vectorised layer forward; returns seconds. Runs in a spawned worker."""
-    os.environ.setdefault('OMP_NUM_THREADS', '1')
-    os.environ.setdefault('OPENBLAS_NUM_THREADS', '1')
-    import numpy as np
-    sys.path.insert(0, HERE)
-    from oracle import asrn_oracle as O
-    params, x, E, h = payload
-    lay = O.Layer(params, E.shape[-1])
-    t0 = time.perf_counter()
-    O.layer_forward_fast(lay, E, h, x, half=True)
-    return time.perf_counter() - t0
 
+def graph_or_eager(step, eager):
+    """The forward captured once as a CUDA graph after the warm-up (only on paths with no collective): the K timed
+    steps are then K graph launches, all enqueued ahead of the device, so a host-side pause cannot leave the GPU idle
+    between steps; the kernels and their work are those of the eager forward. Returns (run, mode, graph)."""
+    import torch
+    if eager:
+        return step, 'eager', None
+    try:
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            step()
+        torch.cuda.current_stream().wait_stream(side)
+        graph = torch.cuda.CUDAGraph(keep_graph=True)
+        with torch.cuda.graph(graph):
+            step()
+        graph.instantiate()
+        graph.replay()
+        return graph.replay, 'cuda_graph', graph
+    except Exception as exc:              # capture unsupported here: time the eager forward
+        return step, 'eager (graph capture failed: %s)' % type(exc).__name__, None
+
+
+def timed(run, steps, clocks=None):
+    """K back-to-back steps between two CUDA events on the current stream: (total ms, per-step ms list)."""
+    import torch
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    marks = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    gc.collect()
+    gc.disable()                  # no collector pause while the steps are enqueued
+    torch.cuda.synchronize()
+    w0 = time.time()
+    t0.record()
+    for i in range(steps):
+        run()
+        marks[i].record()
+    t1.record()
+    torch.cuda.synchronize()
+    gc.enable()
+    if clocks is not None:
+        clocks.mark(w0, time.time())
+    step_ms = [t0.elapsed_time(marks[0])] + [marks[i - 1].elapsed_time(marks[i]) for i in range(1, steps)]
+    return t0.elapsed_time(t1), step_ms
+
+
+def spread(step_ms):
+    return {'min': min(step_ms), 'median': statistics.median(step_ms), 'max': max(step_ms),
+            'argmax': step_ms.index(max(step_ms))}
+
+
+def e2e_pipelined(forward, host_in, host_out, dev, steps):
+    """Public-API throughput from pinned host buffers: step k uploads its inputs on a copy stream while step k-1
+    computes, and downloads its h' on a second copy stream while step k+1 computes (two device buffer sets). Returns
+    ms per step (CUDA events around all the copies and forwards)."""
+    import torch
+    comp = torch.cuda.current_stream(dev)
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    bufs = [[torch.empty(t.shape, dtype=t.dtype, device=dev) for t in host_in] for _ in range(2)]
+    outs = [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in (host_out, host_out)]
+    uploaded = [torch.cuda.Event() for _ in range(2)]
+    consumed = [torch.cuda.Event() for _ in range(2)]
+    computed = [torch.cuda.Event() for _ in range(2)]
+
+    def upload(k):
+        i = k % 2
+        with torch.cuda.stream(s_in):
+            s_in.wait_event(consumed[i])
+            for dst, src in zip(bufs[i], host_in):
+                dst.copy_(src, non_blocking=True)
+            uploaded[i].record(s_in)
+
+    def run(n):
+        upload(0)
+        for k in range(n):
+            i = k % 2
+            comp.wait_event(uploaded[i])
+            y = forward(*bufs[i])
+            consumed[i].record(comp)
+            computed[i].record(comp)
+            if k + 1 < n:
+                upload(k + 1)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(computed[i])
+                outs[i].copy_(y, non_blocking=True)
+                y.record_stream(s_out)
+        comp.wait_stream(s_out)
+        comp.wait_stream(s_in)
+
+    run(2)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(comp)
+    run(steps)
+    e1.record(comp)
+    torch.cuda.synchronize()
+    host_out.copy_(outs[(steps - 1) % 2])
+    return e0.elapsed_time(e1) / steps
+
+
+# ---------------------------------------------------------------------------------------------------------------------
+# the reference's own CPU implementation (installed into baseline/_ref)
+# ---------------------------------------------------------------------------------------------------------------------
 
 def host_cores():
     """Host cores this process may use: the affinity mask, capped by a cgroup CPU quota if one is set."""
@@ -267,38 +405,110 @@ def host_cores():
     return max(1, n)
 
 
-def cpu_baseline(layer_params, x, E, h, seq, workers=None):
-    """Tokens/s of the oracle port on `workers` host processes (one sequence each, spawn pool)."""
-    import multiprocessing as mp
-    workers = workers or max(1, min(host_cores(), x.shape[0], 32))
-    ctx = mp.get_context('spawn')
-    n = min(workers, x.shape[0])
-    payloads = [(layer_params, x[i:i + 1, :seq], E[i:i + 1, :seq], h[i:i + 1, :seq]) for i in range(n)]
-    # one BLAS thread per worker process: the workers import numpy while unpickling their task, so the limit has to be
-    # in the environment they inherit (16 workers x 16 BLAS threads each oversubscribe the cores 16 times)
-    saved = {k: os.environ.get(k) for k in ('OMP_NUM_THREADS', 'OPENBLAS_NUM_THREADS', 'MKL_NUM_THREADS')}
-    os.environ.update({k: '1' for k in saved})
-    try:
-        with ctx.Pool(n) as pool:
-            pool.map(_oracle_one, payloads[:n])          # warm-up: imports, first-touch of the arrays
+def import_reference():
+    """The reference package (KIROKOWA/ASRN) as pip installed it into baseline/_ref; ImportError if absent."""
+    if not os.path.isdir(os.path.join(REF_PATH, 'asrn')):
+        raise ImportError('baseline/_ref/asrn is not installed')
+    if REF_PATH not in sys.path:
+        sys.path.insert(0, REF_PATH)
+    import asrn
+    if not os.path.abspath(asrn.__file__).startswith(os.path.abspath(REF_PATH)):
+        raise ImportError('asrn resolves to %s, not baseline/_ref' % asrn.__file__)
+    return asrn
+
+
+def ref_layer_steps(state, x, E, h, half, per_step, steps, warmup):
+    """The reference's ASRNLayer forward on the host (torch CPU, all granted cores), `per_step` sequences per step
+    cycling over the sample: per-step seconds of `steps` timed steps after `warmup`."""
+    import torch
+    asrn = import_reference()
+    torch.set_num_threads(host_cores())
+    d = E.shape[-1]
+    layer = asrn.ASRNLayer(d)
+    layer.load_state_dict(state)
+    layer.eval()
+    xs, Es, hs = (torch.from_numpy(a) for a in (x, E, h))
+    n = x.shape[0]
+    secs = []
+    for i in range(warmup + steps):
+        b0 = (i * per_step) % n
+        sl = slice(b0, min(n, b0 + per_step))
+        t0 = time.perf_counter()
+        with torch.no_grad(), torch.autocast('cpu', dtype=torch.bfloat16, enabled=half):
+            layer(Es[sl], hs[sl], xs[sl])
+        if i >= warmup:
+            secs.append(time.perf_counter() - t0)
+    return secs, min(per_step, n)
+
+
+def ref_layer_baseline(state, x, E, h, half, per_step, steps, warmup, what):
+    import torch
+    secs, nb = ref_layer_steps(state, x, E, h, half, per_step, steps, warmup)
+    tok = nb * x.shape[1]
+    return {'value': tok * len(secs) / sum(secs), 'unit': UNIT, 'cores': torch.get_num_threads(),
+            'kind': 'reference', 'ms_per_step': 1e3 * statistics.median(secs),
+            'sample': '%s: asrn.ASRNLayer of the reference (baseline/_ref) on the host cores, torch CPU%s, %d step(s) '
+                      'of %d sequence(s) x %d tokens after %d warm-up' % (what, ', bf16 autocast' if half else '',
+                                                                          len(secs), nb, x.shape[1], warmup)}
+
+
+def ref_generation(prompts, B=4, steps=6, warmup=2):
+    """The reference's O(1) writer (_Escritor(o1=True), asrn/nucleo.py:1717-1854) on the host cores: the
+    configuration-3 model (create_model(V=50304, d=768, n_capas=12, semilla=0): the same weights as ours), batch B,
+    bf16 autocast, greedy steps fed back. Returns {prompt: {step_ms, prefill_s}}."""
+    import torch
+    from asrn_b200 import synthetic
+    asrn = import_reference()
+    from asrn import nucleo
+    torch.set_num_threads(host_cores())
+    m = asrn.create_model(V=V, d=D, n_capas=12, semilla=0).eval()
+    out = {}
+    for L0 in prompts:
+        x0 = torch.from_numpy(synthetic.config_tokens('cfg5', B=B, L=L0, seed=0))
+        with torch.no_grad(), torch.autocast('cpu', dtype=torch.bfloat16):
+            esc = nucleo._Escritor(m, True, o1=True)
             t0 = time.perf_counter()
-            secs = pool.map(_oracle_one, payloads)
-            wall = time.perf_counter() - t0
-    finally:
-        for k, v in saved.items():
-            if v is None:
-                os.environ.pop(k, None)
-            else:
-                os.environ[k] = v
-    tok = n * seq
-    return {'value': tok / wall, 'unit': UNIT, 'cores': n, 'kind': 'port',
-            'sample': '%d sequence(s) x %d tokens of the same workload, one per host process (numpy oracle port of '
-                      'the reference CPU path, bf16 autocast emulated); wall %.1f s, per-sequence %.1f s'
-                      % (n, seq, wall, statistics.median(secs))}
+            lg = esc.inicio(x0, L0 + steps + warmup + 2)
+            pre = time.perf_counter() - t0
+            nxt = lg.argmax(-1)
+            secs = []
+            for k in range(warmup + steps):
+                t0 = time.perf_counter()
+                lg = esc.paso(nxt)
+                nxt = lg.argmax(-1)
+                if k >= warmup:
+                    secs.append(time.perf_counter() - t0)
+        out[str(L0)] = {'step_ms': 1e3 * statistics.median(secs), 'prefill_s': pre}
+        del esc
+    return out, torch.get_num_threads()
+
+
+def ref_cfg1():
+    """The reference on configuration 1 (host cores, fp32): model forward on 8 x 256 bytes and generate(top_k=1) of
+    200 tokens from a 512-token prompt."""
+    import torch
+    from asrn_b200 import synthetic
+    asrn = import_reference()
+    torch.set_num_threads(host_cores())
+    m = asrn.create_model(V=256, d=64, n_capas=4, semilla=0).eval()
+    x = torch.from_numpy(synthetic.config_tokens('cfg1', B=8, L=256, seed=0))
+    x0 = torch.from_numpy(synthetic.uniform_bytes_with_repeats(1, 4096, seed=0)[:, :512])
+    with torch.no_grad():
+        m(x)
+        secs = []
+        for _ in range(3):
+            t0 = time.perf_counter()
+            m(x)
+            secs.append(time.perf_counter() - t0)
+    t0 = time.perf_counter()
+    asrn.generate(m, x0, n_nuevos=200, top_k=1, devolver_logits=False)
+    gen_s = time.perf_counter() - t0
+    return {'forward_ms': 1e3 * statistics.median(secs), 'generate_ms_per_token': gen_s / 200 * 1e3,
+            'cores': torch.get_num_threads(), 'kind': 'reference'}
 
 
 # ---------------------------------------------------------------------------------------------------------------------
-# main
+# main leg: configuration 3 (the headline)
 # ---------------------------------------------------------------------------------------------------------------------
 
 def dist_env():
@@ -308,33 +518,8 @@ def dist_env():
     return rank, world, local
 
 
-def run_reference(args):
-    rank, world, _ = dist_env()
-    if rank != 0:
-        return 0
-    import numpy as np
-    import torch
-    layer = make_layer_params()
-    params = {k: v.detach().numpy() for k, v in layer.state_dict().items()}
-    seq = args.seq
-    x, E, h, _ = make_inputs(max(1, min(32, host_cores())), seq, 0)
-    vals = []
-    info = None
-    for _ in range(max(1, min(args.steps, 3))):
-        info = cpu_baseline(params, x, E, h, seq)
-        vals.append(info['value'])
-    v = statistics.median(vals)
-    info['value'] = v
-    out = {'metric': METRIC, 'value': v, 'unit': UNIT, 'n_gpus': world, 'steps': args.steps, 'warmup': args.warmup,
-           'ms_per_step': None, 'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'bf16',
-           'data': 'synthetic', 'impl': 'reference', 'config': config(args, world), 'cpu_baseline': info,
-           'e2e': {'value': v, 'unit': UNIT, 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}}
-    print(json.dumps(out), flush=True)
-    return 0
-
-
 def load_profile_traffic():
-    """Per-launch DRAM bytes of the scoring kernel from the committed ncu summary (profiles/), or None."""
+    """Per-token DRAM bytes of the scoring kernel from the committed ncu summary (profiles/), or None."""
     p = os.path.join(HERE, 'profiles', 'k_score_tc_cfg3_traffic.json')
     try:
         with open(p) as f:
@@ -344,10 +529,303 @@ def load_profile_traffic():
         return None
 
 
-def run_generation(args, dev, rank, world):
+def run_ours(args):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    rank, world, local = dist_env()
+    if world > 1:
+        dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=120))
+    torch.cuda.set_device(local)
+    dev = torch.device('cuda', local)
+    from asrn_b200 import _lib, stages
+    hbm, peak_src = peaks()
+    out = None
+    legs = {}
+    if args.workload == 'cfg3':
+        layer = make_layer_params().to(dev).eval()
+        x_np, E_np, h_np, _table = make_inputs(args.batch, args.seq, rank)
+        cpu_info = None
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            try:
+                state = {k: v.detach().cpu() for k, v in layer.state_dict().items()}
+                n = min(REF_CHUNK, args.batch)
+                cpu_info = ref_layer_baseline(state, x_np[:n], E_np[:n], h_np[:n], True, n, 2, 1,
+                                              'the headline workload')
+            except Exception as exc:                              # the reference is not installed here
+                cpu_info = {'unavailable': '%s: %s' % (type(exc).__name__, exc)}
+        x = torch.from_numpy(x_np).to(dev)
+        E = torch.from_numpy(E_np).to(dev)
+        h = torch.from_numpy(h_np).to(dev)
+        tokens = args.batch * args.seq
+
+        def step():
+            with torch.no_grad(), torch.autocast('cuda', dtype=torch.bfloat16):
+                return layer(E, h, x)
+
+        clocks = ClockSampler(local)
+        clocks.start()
+        warm = warm_up(step, args.warmup, world)
+        run, launch_mode, graph = graph_or_eager(step, args.eager)
+        kern, ours_k, names = count_graph_kernels(graph) if graph is not None else (None, None, None)
+        if world > 1:
+            dist.barrier()
+        ms, step_ms = timed(run, args.steps, clocks)
+        if world > 1:
+            dist.barrier()
+        clk = clocks.stop()
+
+        # dominant kernel (candidate scoring), timed on its launching stream with the forward's own intermediates
+        with torch.no_grad():
+            ctx = stages.context(layer, h, x, half=True)
+            Bt = stages.clock(ctx['beta'])
+            hs = stages.hash(layer, E, half=True)
+            orden, ids_o = stages.bucket_sort(hs['ids_rows'], layer.n_bits)
+            call = lambda: stages.score(layer, orden, ids_o, hs['phi'], ctx['Qc'], ctx['Kc'], ctx['sig'], Bt,
+                                        ctx['log_alfa'], hs['Ea'], half=True)
+            for _ in range(2):
+                call()
+            score_ms, _ = timed(call, args.steps)
+            score_ms /= args.steps
+            del ctx, Bt, hs, orden, ids_o
+
+        del run, graph
+        torch.cuda.empty_cache()
+
+        # end to end through the public API with pinned host buffers, copies overlapped with compute
+        host_in = [torch.from_numpy(a).pin_memory() for a in (E_np, h_np, x_np)]
+        host_out = torch.empty(h_np.shape, dtype=torch.float32).pin_memory()
+
+        def fwd(Ed, hd, xd):
+            with torch.no_grad(), torch.autocast('cuda', dtype=torch.bfloat16):
+                return layer(Ed, hd, xd)
+
+        e2e_ms = e2e_pipelined(fwd, host_in, host_out, dev, max(3, min(args.steps, 6)))
+        del host_in, host_out, E, h, x
+        torch.cuda.empty_cache()
+        vals = torch.tensor([ms, e2e_ms, score_ms], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+        ms, e2e_ms, score_ms = vals.tolist()
+        if rank == 0:
+            achieved = SCORE_BYTES_PER_TOKEN * tokens / (score_ms * 1e-3) / 1e9
+            traffic_pt = load_profile_traffic()
+            out = {'metric': METRIC, 'value': world * tokens * args.steps / (ms * 1e-3), 'unit': UNIT,
+                   'n_gpus': world, 'steps': args.steps, 'warmup': warm, 'ms_per_step': ms / args.steps,
+                   'step_ms': spread(step_ms), 'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None,
+                   'dtype': 'bf16', 'data': 'synthetic', 'config': config(args, world),
+                   'e2e': {'value': world * tokens / (e2e_ms * 1e-3), 'unit': UNIT,
+                           'h2d_bytes_per_step': int(E_np.nbytes + h_np.nbytes + x_np.nbytes),
+                           'd2h_bytes_per_step': int(h_np.nbytes),
+                           'how': 'ASRNLayer.forward on each step\'s inputs uploaded from pinned host memory, h\' '
+                                  'downloaded; uploads, forwards and downloads of consecutive steps overlap on three '
+                                  'streams (two device buffer sets)'},
+                   'roofline': {'bound': 'hbm', 'kernel': 'k_score_tc (candidate scoring)', 'achieved': achieved,
+                                'peak': hbm, 'peak_source': peak_src, 'unit': 'GB/s', 'frac': achieved / hbm,
+                                'algorithmic_bytes_per_token': SCORE_BYTES_PER_TOKEN,
+                                'traffic': None if traffic_pt is None else traffic_pt * tokens,
+                                'kernel_ms': score_ms,
+                                'layer_frac': LAYER_BYTES_PER_TOKEN * tokens / (ms / args.steps * 1e-3) / 1e9 / hbm},
+                   'gpu_launches': (ours_k * args.steps) if ours_k else None,
+                   'graph_kernels_per_step': {'all': kern, 'ours': ours_k, 'by_name': names},
+                   'launch': launch_mode, 'clocks': clk,
+                   'test_hooks': {'ASRN_B200_GEMM': _lib.gemm_override()}}
+            if cpu_info is not None:
+                out['cpu_baseline'] = cpu_info
+        del layer
+        torch.cuda.empty_cache()
+    if not args.no_legs:
+        legs['cfg4'] = leg_cfg4(args, dev, rank, world)
+    if args.workload == 'cfg3':
+        if not args.no_gen:
+            legs['generation'] = leg_generation(args, dev, rank, world)
+        if not args.no_legs:
+            legs['cfg2'] = leg_cfg2(args, dev, rank, world)
+            legs['cfg1'] = leg_cfg1(args, dev, rank, world)
+    if rank == 0:
+        if out is None:                       # --workload cfg4: the cfg4 leg is the line
+            out = dict(legs.pop('cfg4'))
+        out.update({k: v for k, v in legs.items() if v is not None})
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+# ---------------------------------------------------------------------------------------------------------------------
+# legs
+# ---------------------------------------------------------------------------------------------------------------------
+
+def _max_over_ranks(vals, dev, world):
+    import torch
+    t = torch.tensor(vals, device=dev, dtype=torch.float64)
+    if world > 1:
+        import torch.distributed as dist
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.tolist()
+
+
+def leg_cfg4(args, dev, rank, world):
+    """Configuration 4: one sequence of L4 tokens, ASRNLayer(512), bf16 autocast; one GPU (graph replay) or
+    sequence-sharded over the run's GPUs (asrn_b200.shard, eager: its NCCL collectives stay outside graphs). Strong
+    scaling: value = tokens of the sequence per second (max-over-ranks device time)."""
+    import torch
+    from asrn_b200 import shard
+    L = L4
+    layer = make_layer_params(d=D4).to(dev).eval()
+    c0, c1 = shard.chunk_bounds(L, world, rank)
+    x, xc, Ec, hc, _ = make_cfg4_inputs(L, c0, c1, rank)
+    xd, Ed, hd = (torch.from_numpy(a).to(dev) for a in (xc, Ec, hc))
+
+    def step():
+        with torch.no_grad(), torch.autocast('cuda', dtype=torch.bfloat16):
+            if world == 1:
+                return layer(Ed, hd, xd)
+            return shard.forward(layer, Ed, hd, xd)
+
+    warm = warm_up(step, args.warmup, world)
+    run, mode, graph = graph_or_eager(step, args.eager or world > 1)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    steps = max(5, args.steps // 2)
+    ms, step_ms = timed(run, steps)
+    del run, graph
+    ms, = _max_over_ranks([ms], dev, world)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            seg = 16384             # the reference on a quarter-million-token row needs ~40 GB of host memory
+            xs = x[:, :seg]
+            Es = _table_rows(xs, D4, 7)
+            hs = (Es + torch.randn(Es.shape, generator=torch.Generator().manual_seed(9)).numpy() * 0.5)
+            state = {k: v.detach().cpu() for k, v in layer.state_dict().items()}
+            cpu = ref_layer_baseline(state, xs, Es, hs.astype('float32'), True, 1, 1, 1,
+                                     'the first %d tokens of the sequence' % seg)
+        except Exception as exc:
+            cpu = {'unavailable': '%s: %s' % (type(exc).__name__, exc)}
+    del layer, xd, Ed, hd
+    torch.cuda.empty_cache()
+    if rank != 0:
+        return None
+    hbm, src = peaks()
+    step_s = ms / steps * 1e-3
+    achieved = CFG4_BYTES_PER_TOKEN * (L // world) / step_s / 1e9
+    leg = {'metric': METRIC, 'value': L / step_s, 'unit': UNIT, 'n_gpus': world, 'steps': steps, 'warmup': warm,
+           'ms_per_step': ms / steps, 'step_ms': spread(step_ms), 'higher_is_better': True, 'scaling': 'strong',
+           'dtype': 'bf16', 'data': 'synthetic', 'launch': mode,
+           'config': {'workload': 'cfg4 layer: ASRNLayer(512) forward, 1 x %d tokens, bf16 autocast, fp32 E/h' % L,
+                      'parallelism': ('sequence-sharded over %d GPUs (NCCL all-gathers of the halo, clock offsets, '
+                                      'bucket tails, per-position features, n-gram summaries and streak maps)'
+                                      % world) if world > 1 else 'single GPU'},
+           'roofline': {'bound': 'hbm', 'kernel': 'whole layer forward (per GPU)', 'achieved': achieved, 'peak': hbm,
+                        'peak_source': src, 'unit': 'GB/s', 'frac': achieved / hbm,
+                        'algorithmic_bytes_per_token': CFG4_BYTES_PER_TOKEN}}
+    if cpu is not None:
+        leg['cpu_baseline'] = cpu
+    return leg
+
+
+def _table_rows(x, d, seed):
+    import numpy as np
+    table = (np.random.default_rng(seed).standard_normal((V, d)) * 0.02).astype(np.float32)
+    return table[x]
+
+
+def leg_cfg2(args, dev, rank, world):
+    """Configuration 2: ASRNLayer(256) forward in fp32, 16 x 4096 tokens sharded over the GPUs (graph replay)."""
+    import torch
+    b = max(1, B2 // world)
+    layer = make_layer_params(d=D2).to(dev).eval()
+    x, E, h = make_cfg2_inputs(b, rank)
+    xd, Ed, hd = (torch.from_numpy(a).to(dev) for a in (x, E, h))
+
+    def step():
+        with torch.no_grad():
+            return layer(Ed, hd, xd)
+
+    warm_up(step, args.warmup, world)
+    run, mode, graph = graph_or_eager(step, args.eager)
+    ms, step_ms = timed(run, args.steps)
+    del run, graph
+    ms, = _max_over_ranks([ms], dev, world)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            state = {k: v.detach().cpu() for k, v in layer.state_dict().items()}
+            cpu = ref_layer_baseline(state, x[:REF_CHUNK], E[:REF_CHUNK], h[:REF_CHUNK], False, REF_CHUNK, 2, 1,
+                                     'configuration 2')
+        except Exception as exc:
+            cpu = {'unavailable': '%s: %s' % (type(exc).__name__, exc)}
+    del layer, xd, Ed, hd
+    torch.cuda.empty_cache()
+    if rank != 0:
+        return None
+    hbm, src = peaks()
+    tokens = world * b * L2
+    step_s = ms / args.steps * 1e-3
+    achieved = CFG2_BYTES_PER_TOKEN * b * L2 / step_s / 1e9
+    leg = {'metric': METRIC, 'value': tokens / step_s, 'unit': UNIT, 'ms_per_step': ms / args.steps,
+           'step_ms': spread(step_ms), 'dtype': 'f32', 'launch': mode, 'scaling': 'weak',
+           'config': {'workload': 'cfg2 layer: ASRNLayer(256) forward, fp32, %d x %d tokens per GPU' % (b, L2)},
+           'roofline': {'bound': 'hbm', 'kernel': 'whole layer forward (per GPU)', 'achieved': achieved, 'peak': hbm,
+                        'peak_source': src, 'unit': 'GB/s', 'frac': achieved / hbm,
+                        'algorithmic_bytes_per_token': CFG2_BYTES_PER_TOKEN}}
+    if cpu is not None:
+        leg['cpu_baseline'] = cpu
+    return leg
+
+
+def leg_cfg1(args, dev, rank, world):
+    """Configuration 1 on one GPU (rank 0; the other ranks skip it): create_model(V=256, d=64, n_capas=4, semilla=0)
+    forward on 8 x 256 bytes (fp32, graph replay), then generate(top_k=1) of 200 tokens from a 512-token prompt end to
+    end through the public API."""
+    import torch
+    import asrn_b200
+    from asrn_b200 import synthetic
+    vals = [0.0, 0.0]
+    if rank == 0:
+        m = asrn_b200.create_model(V=256, d=64, n_capas=4, semilla=0).to(dev).eval()
+        x = torch.from_numpy(synthetic.config_tokens('cfg1', B=8, L=256, seed=0)).to(dev)
+        x0 = torch.from_numpy(synthetic.uniform_bytes_with_repeats(1, 4096, seed=0)[:, :512])
+
+        def step():
+            with torch.no_grad():
+                return m(x)
+
+        warm_up(step, args.warmup, 1)
+        run, mode, graph = graph_or_eager(step, args.eager)
+        ms, _ = timed(run, args.steps)
+        del run, graph
+        asrn_b200.generate(m, x0, n_nuevos=8, top_k=1, devolver_logits=False)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        asrn_b200.generate(m, x0, n_nuevos=200, top_k=1, devolver_logits=False)
+        torch.cuda.synchronize()
+        vals = [ms / args.steps, (time.perf_counter() - t0) / 200 * 1e3]
+        del m
+        torch.cuda.empty_cache()
+    if rank != 0:
+        return None
+    leg = {'forward_ms': vals[0], 'forward_tokens_per_s': 8 * 256 / (vals[0] * 1e-3),
+           'generate_ms_per_token': vals[1], 'dtype': 'f32', 'launch': mode,
+           'config': {'workload': 'cfg1: create_model(V=256, d=64, n_capas=4, semilla=0); forward on 8 x 256 '
+                                  'bytes with 30 % planted repeats; generate(top_k=1) of 200 tokens from a 512-token '
+                                  'prompt (host tokens in and out)'}}
+    if not args.no_cpu_baseline:
+        try:
+            leg['cpu_baseline'] = ref_cfg1()
+        except Exception as exc:
+            leg['cpu_baseline'] = {'unavailable': '%s: %s' % (type(exc).__name__, exc)}
+    return leg
+
+
+def leg_generation(args, dev, rank, world):
     """Generation leg: per prompt length, the prompt pass (prefill) then args.gen_steps greedy steps of the O(1)
     writer, each step the CUDA-graph replay of the model's step plus a device argmax feeding the next token (no host
-    sync), timed with CUDA events; then the public API (generate, top_k=1) end to end at the shortest prompt."""
+    sync), timed with CUDA events; then the public API (generate, top_k=1) end to end at the shortest prompt; then the
+    reference's writer on the host cores."""
     import torch
     import asrn_b200
     from asrn_b200 import synthetic
@@ -355,7 +833,7 @@ def run_generation(args, dev, rank, world):
     torch.manual_seed(0)
     m = asrn_b200.create_model(V=V, d=D, n_capas=12, semilla=0).to(dev).eval()
     prompts = sorted(set([p for p in GEN_FLAT if p < args.gen_prompt] + [args.gen_prompt]))
-    out = {'sequences_per_gpu': B, 'prompts': {}}
+    res = {}
     for L0 in prompts:
         x0 = torch.from_numpy(synthetic.config_tokens('cfg5', B=B, L=L0, seed=rank)).to(dev)
         with torch.autocast('cuda', dtype=torch.bfloat16):
@@ -378,8 +856,7 @@ def run_generation(args, dev, rank, world):
             status = w.status()
             if any(status):
                 raise RuntimeError(f'generation step status {status}')
-            out['prompts'][str(L0)] = {'step_us': e0.elapsed_time(e1) / args.gen_steps * 1e3,
-                                       'prefill_tokens_per_s': B * L0 / (p0.elapsed_time(p1) * 1e-3)}
+            res[L0] = [e0.elapsed_time(e1) / args.gen_steps * 1e3, B * L0 / (p0.elapsed_time(p1) * 1e-3)]
             w.cerrar()
             del w, lg, nxt, x0
         torch.cuda.empty_cache()
@@ -397,320 +874,89 @@ def run_generation(args, dev, rank, world):
             asrn_b200.generate(m, x0, n_nuevos=n, top_k=1, devolver_logits=False)
             torch.cuda.synchronize()
             times.append(time.perf_counter() - t0)
-    out['e2e_step_us'] = (times[1] - times[0]) / (n_b - n_a) * 1e6
-    out['e2e_prompt'] = L0
+    e2e_us = (times[1] - times[0]) / (n_b - n_a) * 1e6
     del m
     torch.cuda.empty_cache()
-    return out
-
-
-def run_ours(args):
-    import numpy as np
-    import torch
-    import torch.distributed as dist
-    rank, world, local = dist_env()
-    if world > 1:
-        import datetime
-        dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=120))
-    torch.cuda.set_device(local)
-    dev = torch.device('cuda', local)
-    import asrn_b200
-    from asrn_b200 import stages
-
-    layer = make_layer_params().to(dev).eval()
-    x_np, E_np, h_np, _table = make_inputs(args.batch, args.seq, rank)
-    cpu_info = None
+    flat = [res[p][0] for p in prompts]
+    vals = _max_over_ranks(flat + [e2e_us], dev, world)
+    step_us = dict(zip(prompts, vals[:len(prompts)]))
+    e2e_us = vals[-1]
+    cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        params = {k: v.detach().cpu().numpy() for k, v in layer.state_dict().items()}
-        cpu_info = cpu_baseline(params, x_np, E_np, h_np, args.seq)
-    x = torch.from_numpy(x_np).to(dev)
-    E = torch.from_numpy(E_np).to(dev)
-    h = torch.from_numpy(h_np).to(dev)
-    tokens = args.batch * args.seq
+        try:
+            ps = [int(p) for p in args.gen_cpu_prompts.split(',') if p]
+            ref, cores = ref_generation(ps)
+            cpu = {'value': statistics.median([r['step_ms'] for r in ref.values()]) * 1e3, 'unit': 'us/token',
+                   'cores': cores, 'kind': 'reference', 'step_us_by_prompt': {k: r['step_ms'] * 1e3
+                                                                               for k, r in ref.items()},
+                   'prefill_s_by_prompt': {k: r['prefill_s'] for k, r in ref.items()},
+                   'sample': "the reference's _Escritor(o1=True) (baseline/_ref) on the host cores, torch CPU, bf16 "
+                             "autocast, batch 4 (a step writes one token of each of the 4 sequences), the same "
+                             "model weights and prompt generator, greedy steps fed back"}
+        except Exception as exc:
+            cpu = {'unavailable': '%s: %s' % (type(exc).__name__, exc)}
+    if rank != 0:
+        return None
+    main = step_us[args.gen_prompt]
+    leg = {'metric': 'gen_us_per_token', 'value': main, 'unit': 'us/token', 'higher_is_better': False,
+           'workload': 'cfg5: create_model(V=50304, d=768, n_capas=12) random init, %d sequences (%d per GPU), '
+                       'Zipf+repeat prompts of %d tokens, %d greedy steps (CUDA-graph step + device argmax), bf16 '
+                       'autocast' % (B * world, B, args.gen_prompt, args.gen_steps),
+           'step_us_by_prompt': {str(k): v for k, v in step_us.items()},
+           'prefill_tokens_per_s_by_prompt': {str(k): res[k][1] * world for k in prompts},
+           'tokens_per_s': B * world / (main * 1e-6),
+           'e2e': {'value': e2e_us, 'unit': 'us/token',
+                   'api': 'asrn_b200.generate(top_k=1, devolver_logits=False), host prompt of %d tokens; per-token '
+                          'cost = difference of a %d- and an %d-token call / %d' % (L0, n_b, n_a, n_b - n_a)}}
+    if cpu is not None:
+        leg['cpu_baseline'] = cpu
+    return leg
 
-    def step():
-        with torch.no_grad(), torch.autocast('cuda', dtype=torch.bfloat16):
-            return layer(E, h, x)
 
-    clocks = ClockSampler(local)
-    clocks.start()
-    warm = warm_up(step, args.warmup, world)
-    run, launch_mode, graph = graph_or_eager(step, args.eager)
-    if world > 1:
-        dist.barrier()
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    marks = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    gc.collect()
-    gc.disable()                  # no collector pause while the steps are enqueued
-    torch.cuda.synchronize()
-    w0 = time.time()
-    t0.record()
-    for i in range(args.steps):
-        run()
-        marks[i].record()
-    t1.record()
-    torch.cuda.synchronize()
-    gc.enable()
-    clocks.mark(w0, time.time())
-    ms = t0.elapsed_time(t1)
-    step_ms = [t0.elapsed_time(marks[0])] + [marks[i - 1].elapsed_time(marks[i]) for i in range(1, args.steps)]
-    if world > 1:
-        dist.barrier()
-    clk = clocks.stop()
-    # launches of our kernels per forward: context, clock, hash, bucket sort (1, or 3 when rows span tiles),
-    # scoring, n-gram rows, streak, gate prep, gate
-    launches_per_step = 8 + (1 if args.seq <= 8192 else 3)
+# ---------------------------------------------------------------------------------------------------------------------
+# --impl reference
+# ---------------------------------------------------------------------------------------------------------------------
 
-    # dominant kernel (candidate scoring), timed on its launching stream with the forward's own intermediates
-    with torch.no_grad():
-        ctx = stages.context(layer, h, x, half=True)
-        Bt = stages.clock(ctx['beta'])
-        hs = stages.hash(layer, E, half=True)
-        orden, ids_o = stages.bucket_sort(hs['ids_rows'], layer.n_bits)
-        call = lambda: stages.score(layer, orden, ids_o, hs['phi'], ctx['Qc'], ctx['Kc'], ctx['sig'], Bt,
-                                    ctx['log_alfa'], hs['Ea'], half=True)
-        for _ in range(2):
-            call()
-        torch.cuda.synchronize()
-        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s0.record()
-        for _ in range(args.steps):
-            call()
-        s1.record()
-        torch.cuda.synchronize()
-        score_ms = s0.elapsed_time(s1) / args.steps
-        del ctx, Bt, hs, orden, ids_o
-
-    # end to end through the public API with pinned host buffers
-    Eh = torch.from_numpy(E_np).pin_memory()
-    hh = torch.from_numpy(h_np).pin_memory()
-    xh = torch.from_numpy(x_np).pin_memory()
-    out_h = torch.empty_like(hh).pin_memory()
-
-    def e2e_step():
-        Ed, hd, xd = Eh.to(dev, non_blocking=True), hh.to(dev, non_blocking=True), xh.to(dev, non_blocking=True)
-        with torch.no_grad(), torch.autocast('cuda', dtype=torch.bfloat16):
-            yd = layer(Ed, hd, xd)
-        out_h.copy_(yd, non_blocking=True)
-
-    e2e_step()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e_steps = max(2, min(args.steps, 5))
-    e0.record()
-    for _ in range(e_steps):
-        e2e_step()
-    e1.record()
-    torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1) / e_steps
-
-    del Eh, hh, xh, out_h, E, h, x, run, graph
-    torch.cuda.empty_cache()
-    gen = None
+def run_reference(args):
+    """The reference's own CPU implementation of the headline workload, on rank 0 (other ranks exit without work):
+    asrn.ASRNLayer from baseline/_ref, torch on the host cores, bf16 autocast, REF_CHUNK sequences per step."""
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return 0
+    try:
+        import_reference()
+    except Exception as exc:
+        print(json.dumps({'impl': 'reference', 'unavailable': 'the reference is not installed in baseline/_ref (%s)'
+                          % exc}), flush=True)
+        return 0
+    import torch
+    layer = make_layer_params()
+    state = {k: v.detach() for k, v in layer.state_dict().items()}
+    n = max(REF_CHUNK, min(2 * REF_CHUNK, args.batch))
+    x, E, h, _ = make_inputs(n, args.seq, 0)
+    steps = max(1, min(args.steps, 12))
+    secs, nb = ref_layer_steps(state, x, E, h, True, REF_CHUNK, steps, max(1, min(args.warmup, 2)))
+    tok = nb * args.seq
+    v = tok * len(secs) / sum(secs)
+    info = {'value': v, 'unit': UNIT, 'cores': torch.get_num_threads(), 'kind': 'reference',
+            'sample': 'asrn.ASRNLayer of the reference (baseline/_ref), torch CPU on the host cores, bf16 autocast: '
+                      '%d steps of %d sequences x %d tokens of the headline workload (the same weights and input '
+                      'generator)' % (len(secs), nb, args.seq)}
+    out = {'metric': METRIC, 'value': v, 'unit': UNIT, 'n_gpus': world, 'steps': len(secs), 'warmup': args.warmup,
+           'ms_per_step': 1e3 * sum(secs) / len(secs), 'higher_is_better': True, 'scaling': 'weak',
+           'vs_baseline': None, 'dtype': 'bf16', 'data': 'synthetic', 'impl': 'reference', 'config': config(args, world),
+           'cpu_baseline': info,
+           'e2e': {'value': v, 'unit': UNIT, 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}}
     if not args.no_gen:
-        gen = run_generation(args, dev, rank, world)
-    g_step = [gen['prompts'][k]['step_us'] for k in sorted(gen['prompts'], key=int)] if gen else []
-    vals = [ms, e2e_ms, score_ms] + g_step + ([gen['e2e_step_us']] if gen else [])
-    times = torch.tensor(vals, device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(times, op=dist.ReduceOp.MAX)
-    vals = times.tolist()
-    ms, e2e_ms, score_ms = vals[:3]
-    if gen:
-        for k, v in zip(sorted(gen['prompts'], key=int), vals[3:3 + len(g_step)]):
-            gen['prompts'][k]['step_us'] = v
-        gen['e2e_step_us'] = vals[-1]
-    if rank == 0:
-        import json as _json
-        peaks = {}
         try:
-            with open(os.path.join(HERE, 'MEASURED_PEAKS.json')) as f:
-                peaks = _json.load(f)
-        except (OSError, ValueError):
-            pass
-        hbm = peaks.get('hbm_gbs', 6650.0)
-        peak_src = 'measured' if 'hbm_gbs' in peaks else 'fallback'
-        achieved = SCORE_BYTES_PER_TOKEN * tokens / (score_ms * 1e-3) / 1e9
-        traffic_pt = load_profile_traffic()
-        value = world * tokens * args.steps / (ms * 1e-3)
-        out = {'metric': METRIC, 'value': value, 'unit': UNIT, 'n_gpus': world, 'steps': args.steps,
-               'warmup': warm, 'ms_per_step': ms / args.steps,
-               'step_ms': {'min': min(step_ms), 'median': statistics.median(step_ms), 'max': max(step_ms),
-                           'argmax': step_ms.index(max(step_ms))},
-               'higher_is_better': True,
-               'scaling': 'weak', 'vs_baseline': None, 'dtype': 'bf16', 'data': 'synthetic',
-               'config': config(args, world),
-               'e2e': {'value': world * tokens / (e2e_ms * 1e-3), 'unit': UNIT,
-                       'h2d_bytes_per_step': int(E_np.nbytes + h_np.nbytes + x_np.nbytes),
-                       'd2h_bytes_per_step': int(h_np.nbytes)},
-               'roofline': {'bound': 'hbm', 'kernel': 'k_score (candidate scoring)', 'achieved': achieved,
-                            'peak': hbm, 'peak_source': peak_src, 'unit': 'GB/s', 'frac': achieved / hbm,
-                            'algorithmic_bytes_per_token': SCORE_BYTES_PER_TOKEN,
-                            'traffic': None if traffic_pt is None else traffic_pt * tokens,
-                            'kernel_ms': score_ms,
-                            'layer_frac': LAYER_BYTES_PER_TOKEN * tokens / (ms / args.steps * 1e-3) / 1e9 / hbm},
-               'gpu_launches': launches_per_step * args.steps,
-               'launch': launch_mode,
-               'clocks': clk}
-        if cpu_info is not None:
-            out['cpu_baseline'] = cpu_info
-        if gen:
-            main = gen['prompts'][str(args.gen_prompt)]
-            out['generation'] = {
-                'metric': 'gen_us_per_token', 'value': main['step_us'], 'unit': 'us/token', 'higher_is_better': False,
-                'workload': 'cfg5: create_model(V=50304, d=768, n_capas=12) random init, %d sequences (%d per GPU), '
-                            'Zipf+repeat prompts of %d tokens, %d greedy steps (CUDA-graph step + device argmax), '
-                            'bf16 autocast' % (gen['sequences_per_gpu'] * world, gen['sequences_per_gpu'],
-                                               args.gen_prompt, args.gen_steps),
-                'step_us_by_prompt': {k: v['step_us'] for k, v in gen['prompts'].items()},
-                'prefill_tokens_per_s_by_prompt': {k: v['prefill_tokens_per_s'] * world
-                                                   for k, v in gen['prompts'].items()},
-                'tokens_per_s': gen['sequences_per_gpu'] * world / (main['step_us'] * 1e-6),
-                'e2e': {'value': gen['e2e_step_us'], 'unit': 'us/token',
-                        'api': 'asrn_b200.generate(top_k=1, devolver_logits=False), host prompt of %d tokens; '
-                               'per-token cost = difference of a 72- and an 8-token call / 64' % gen['e2e_prompt']}}
-        print(json.dumps(out), flush=True)
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
-    return 0
-
-
-D4, L4 = 512, 262144
-CFG4_BYTES_PER_TOKEN = 24968     # algorithmic HBM bytes per token of one layer forward at d=512, bf16, fp32 E/h
-
-
-def run_cfg4(args):
-    """Configuration 4: one sequence of L4 tokens, ASRNLayer(512), bf16 autocast, sequence-sharded over the GPUs
-    (asrn_b200.shard: halo + clock-offset + feature all-gathers over NCCL); strong scaling. value = tokens of the
-    sequence per second (max-over-ranks device time of a step, exchange included)."""
-    import datetime
-    import numpy as np
-    import torch
-    import torch.distributed as dist
-    rank, world, local = dist_env()
-    if world > 1:
-        dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=120))
-    torch.cuda.set_device(local)
-    dev = torch.device('cuda', local)
-    from asrn_b200 import shard, synthetic
-    L = args.seq if args.seq != L_SEQ else L4
-    layer = make_layer_params(d=D4).to(dev).eval()
-    x = synthetic.config_tokens('cfg4', B=1, L=L, seed=0)
-    g = np.random.default_rng(7)
-    table = (g.standard_normal((V, D4)) * 0.02).astype(np.float32)
-    c0, c1 = shard.chunk_bounds(L, world, rank)
-    xc = np.ascontiguousarray(x[:, c0:c1])
-    Ec = table[xc]
-    hc = (Ec + np.random.default_rng(8 + rank).standard_normal(Ec.shape).astype(np.float32) * 0.5).astype(np.float32)
-    cpu_info = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        seg = 16384
-        nseg = max(1, min(host_cores(), L // seg, 16))
-        params = {k: v.detach().cpu().numpy() for k, v in layer.state_dict().items()}
-        xs = x[:, :nseg * seg].reshape(nseg, seg)
-        Es = table[xs]
-        hs = (Es + np.random.default_rng(9).standard_normal(Es.shape).astype(np.float32) * 0.5).astype(np.float32)
-        cpu_info = cpu_baseline(params, xs, Es, hs, seg)
-        cpu_info['sample'] = ('%d segments of %d tokens of the sequence, each run as its own sequence, one per host '
-                              'process (numpy oracle port, bf16 autocast emulated)' % (nseg, seg))
-    xd, Ed, hd = (torch.from_numpy(a).to(dev) for a in (xc, Ec, hc))
-
-    def step():
-        with torch.no_grad(), torch.autocast('cuda', dtype=torch.bfloat16):
-            if world == 1:
-                return layer(Ed, hd, xd)
-            return shard.forward(layer, Ed, hd, xd)
-
-    clocks = ClockSampler(local)
-    clocks.start()
-    warm = warm_up(step, args.warmup, world)
-    # one GPU: the forward replayed as a CUDA graph; sharded: eager (its NCCL collectives stay outside graphs)
-    run, launch_mode, graph = graph_or_eager(step, args.eager or world > 1)
-    if world > 1:
-        dist.barrier()
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    marks = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    gc.collect()
-    gc.disable()                  # no collector pause while the steps are enqueued
-    torch.cuda.synchronize()
-    w0 = time.time()
-    t0.record()
-    for i in range(args.steps):
-        run()
-        marks[i].record()
-    t1.record()
-    torch.cuda.synchronize()
-    gc.enable()
-    clocks.mark(w0, time.time())
-    ms = t0.elapsed_time(t1)
-    step_ms = [t0.elapsed_time(marks[0])] + [marks[i - 1].elapsed_time(marks[i]) for i in range(1, args.steps)]
-    if world > 1:
-        dist.barrier()
-    clk = clocks.stop()
-    # end to end: this rank's chunk from pinned host buffers, h' back to the host
-    xh, Eh, hh = (torch.from_numpy(a).pin_memory() for a in (xc, Ec, hc))
-    out_h = torch.empty(hh.shape, dtype=torch.float32).pin_memory()
-
-    def e2e_step():
-        xe, Ee, he = xh.to(dev, non_blocking=True), Eh.to(dev, non_blocking=True), hh.to(dev, non_blocking=True)
-        with torch.no_grad(), torch.autocast('cuda', dtype=torch.bfloat16):
-            ye = layer(Ee, he, xe) if world == 1 else shard.forward(layer, Ee, he, xe)
-        out_h.copy_(ye, non_blocking=True)
-
-    e2e_step()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e_steps = max(2, min(args.steps, 5))
-    e0.record()
-    for _ in range(e_steps):
-        e2e_step()
-    e1.record()
-    torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1) / e_steps
-    times = torch.tensor([ms, e2e_ms], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(times, op=dist.ReduceOp.MAX)
-    ms, e2e_ms = times.tolist()
-    if rank == 0:
-        peaks = {}
-        try:
-            with open(os.path.join(HERE, 'MEASURED_PEAKS.json')) as f:
-                peaks = json.load(f)
-        except (OSError, ValueError):
-            pass
-        hbm = peaks.get('hbm_gbs', 6650.0)
-        step_s = ms / args.steps * 1e-3
-        achieved = CFG4_BYTES_PER_TOKEN * (L // world) / step_s / 1e9
-        out = {'metric': METRIC, 'value': L / step_s, 'unit': UNIT, 'n_gpus': world, 'steps': args.steps,
-               'warmup': warm, 'ms_per_step': ms / args.steps,
-               'step_ms': {'min': min(step_ms), 'median': statistics.median(step_ms), 'max': max(step_ms),
-                           'argmax': step_ms.index(max(step_ms))},
-               'higher_is_better': True,
-               'scaling': 'strong', 'vs_baseline': None, 'dtype': 'bf16', 'data': 'synthetic',
-               'config': {'workload': 'cfg4 layer: ASRNLayer(512) forward, 1 x %d tokens, bf16 autocast, fp32 E/h'
-                                      % L, 'global_batch': 1, 'seq_len': L, 'd': D4, 'vocab': V,
-                          'parallelism': ('sequence-sharded over %d GPUs (NCCL all-gathers of the halo, clock '
-                                          'offsets, bucket tails, per-position features, n-gram summaries and '
-                                          'streak maps)' % world) if world > 1 else 'single GPU',
-                          'l2': 'inputs larger than L2 (E and h are %.0f MB each per GPU), no flush'
-                                % (Ec.nbytes / 1e6)},
-               'e2e': {'value': L / (e2e_ms * 1e-3), 'unit': UNIT, 'h2d_bytes_per_step': int(xc.nbytes + Ec.nbytes +
-                                                                                             hc.nbytes),
-                       'd2h_bytes_per_step': int(hc.nbytes)},
-               'roofline': {'bound': 'hbm', 'kernel': 'whole layer forward (per GPU)', 'achieved': achieved,
-                            'peak': hbm, 'peak_source': 'measured' if 'hbm_gbs' in peaks else 'fallback',
-                            'unit': 'GB/s', 'frac': achieved / hbm,
-                            'algorithmic_bytes_per_token': CFG4_BYTES_PER_TOKEN, 'traffic': None},
-               'gpu_launches': None, 'launch': launch_mode, 'clocks': clk}
-        if cpu_info is not None:
-            out['cpu_baseline'] = cpu_info
-        print(json.dumps(out), flush=True)
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+            ref, cores = ref_generation([int(p) for p in args.gen_cpu_prompts.split(',') if p])
+            out['generation'] = {'metric': 'gen_us_per_token', 'unit': 'us/token', 'higher_is_better': False,
+                                 'value': statistics.median([r['step_ms'] for r in ref.values()]) * 1e3,
+                                 'step_us_by_prompt': {k: r['step_ms'] * 1e3 for k, r in ref.items()},
+                                 'cores': cores, 'workload': "_Escritor(o1=True), batch 4, bf16 autocast, host cores"}
+        except Exception as exc:
+            out['generation'] = {'unavailable': '%s: %s' % (type(exc).__name__, exc)}
+    print(json.dumps(out), flush=True)
     return 0
 
 
@@ -718,8 +964,6 @@ def main():
     args = parse()
     if args.impl == 'reference':
         return run_reference(args)
-    if args.workload == 'cfg4':
-        return run_cfg4(args)
     return run_ours(args)
 
 

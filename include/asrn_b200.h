@@ -51,7 +51,8 @@ enum {
   ASRN_ERR_UNSUPPORTED = 2,  /* option combination this build does not implement */
   ASRN_ERR_WORKSPACE = 3,    /* workspace / prepared buffer too small or misaligned */
   ASRN_ERR_CUDA = 4,         /* a kernel launch failed (cudaGetLastError) */
-  ASRN_ERR_TIMEOUT = 5       /* a bounded device wait gave up */
+  ASRN_ERR_TIMEOUT = 5,      /* a bounded device wait gave up */
+  ASRN_ERR_DATA = 6          /* state received from another shard failed validation (recorded in a status word) */
 };
 
 /* Layer options (asrn/nucleo.py:585-630) and protections (asrn/estable.py:57-77). */
@@ -179,6 +180,9 @@ int asrn_local_gelu(int64_t n, void* f, int32_t half, void* stream);
  * (tails_prev: (n_prev, rows, 2^nb, C + 1), rank order): orden_v / ids_v (rows, Lv), the used length of each row in
  * row_len (rows) int64 (the rest is padding); Lv >= Lc + min(c0, 2^nb * C) bounds every row, so no host round trip
  * is needed. Requires 2+ shards (c0 > 0 or c0 + Lc < L). Both take a workspace of asrn_shard_workspace_bytes.
+ * A received tail is used only if its count is in [0, C] and its positions ascend strictly inside its sender's chunk
+ * [p Lc, (p + 1) Lc); any other tail is treated as empty and ASRN_ERR_DATA is recorded in *status (a device int, may
+ * be NULL), so corrupt state never indexes features out of range.
  * asrn_shard_rows: the same rows from the FULL sorted rows (orden, ids_o: (rows, L) after exchanging all bucket ids);
  * with orden_v == NULL it only writes each row's length to counts (rows) int64; otherwise it writes rows of length Lv
  * (cut at Lv), padded with id 0xFFFF, and the lengths too when counts != NULL. q_lo = c0, q_hi = c0 + Lc.
@@ -191,7 +195,7 @@ int asrn_shard_tails(int64_t rows, int64_t Lc, int32_t nb, int32_t C, int64_t c0
 int asrn_shard_merge(int64_t rows, int64_t Lc, int32_t nb, int32_t C, int64_t c0, int32_t n_prev,
                      const int32_t* tails_prev, const int32_t* orden_loc, const uint16_t* ids_loc, int64_t Lv,
                      int32_t* orden_v, uint16_t* ids_v, int64_t* row_len, int64_t L, void* workspace,
-                     size_t workspace_bytes, void* stream);
+                     size_t workspace_bytes, int* status, void* stream);
 int asrn_shard_rows(int64_t rows, int64_t L, int32_t C, int64_t q_lo, int64_t q_hi, const int32_t* orden,
                     const uint16_t* ids_o, int64_t Lv, int32_t* orden_v, uint16_t* ids_v, int64_t* counts,
                     void* stream);
@@ -232,8 +236,10 @@ int asrn_racha_chunk(const asrn_layer_config* cfg, const asrn_layer_weights* w, 
  * argument; rows longer than one tile (8192 positions) use a fixed 32 MiB scratch array inside this library, which
  * every GPU that loads the library keeps until the process exits. Requests whose scratch would exceed 32 MiB
  * (rows * L * 4 + rows * ceil(L / 8192) * 2^nb * 4 bytes, each rounded up to 256) return ASRN_ERR_WORKSPACE.
- * The first call on a device looks up the array's device address (once per device, with that device current): make
- * it before any stream capture. Calls share the array: calls that overlap on the GPU race, so order them on one stream.
+ * Every call looks up the array's device address in the current context (a host-side query, no stream work), so the
+ * entry point stays valid after the context is destroyed and created again. Calls share the array: calls that overlap
+ * on the GPU race, so order them on one stream. Empty input (rows or L zero) returns ASRN_OK before any other check,
+ * as asrn_bucket_sort does.
  * No counterpart in the reference (its sort is torch.argsort, which allocates through PyTorch). */
 int asrn_bucket_sort_noalloc(int64_t rows, int64_t L, int32_t nb, const uint16_t* ids_rows, int32_t* orden,
                              uint16_t* ids_o, void* stream);
@@ -325,6 +331,17 @@ int asrn_gen_attend(const asrn_layer_config* cfg, const asrn_layer_weights* w, c
 /* Put position *t_pos into the ring of its bucket in every table. */
 int asrn_gen_ring_insert(int64_t B, int32_t T, int32_t nb, int32_t C, const int64_t* t_pos, const uint16_t* ids_t,
                          int32_t* ring, int32_t* count, void* stream);
+
+/* ---- test hooks (no counterpart in the reference; the layer forward never calls them) ------------------------------
+ * asrn_test_force_cuda_core: 1 routes the bfloat16 work of later calls to the CUDA-core kernels (the fp32 path's), so
+ * tests can compare them with the tensor-core kernels; 0 restores the default; a negative value only queries. Returns
+ * the previous setting.
+ * asrn_test_bounded_wait: one kernel holding TMEM waits, with the limit limit_ns, on an mbarrier that nothing arrives
+ * on, through the same bounded wait every tcgen05 kernel uses; the wait gives up, records ASRN_ERR_TIMEOUT in *status
+ * (device int, ASRN_OK before) and the kernel frees its TMEM and returns; *result (device int) = 1 if the wait had
+ * completed, 0 if it gave up. */
+int asrn_test_force_cuda_core(int on);
+int asrn_test_bounded_wait(uint64_t limit_ns, int* status, int* result, void* stream);
 
 #ifdef __cplusplus
 }

@@ -400,17 +400,18 @@ def layer_forward(lay, E, h, tokens, half=False, return_parts=False, ids_overrid
 # Vectorised restatement (the reference's window formulation), for timing the CPU path on realistic sizes
 # --------------------------------------------------------------------------------------------------------------------
 
-def acumular_fast(lay, E, Qc, Kc, Bt, log_alfa, sig, half):
+def acumular_fast(lay, E, Qc, Kc, Bt, log_alfa, sig, half, ids_override=None):
     """asrn/estable.py:204-272 as the reference computes it on the CPU: every row sorted by bucket, cut into blocks of
     C with a zero block in front, windows (W, C, 2C) of the previous + current block, batched products, exact-mask
-    softmax, copy of the next token's value, back to text order and summed over the tables."""
+    softmax, copy of the next token's value, back to text order and summed over the tables. ids_override (B, L, T):
+    bucket ids to use instead of this restatement's own."""
     B, L, d = E.shape
     T, C, K = lay.T, lay.C, lay.K
     n_pad = (-L) % C
     R = (L + n_pad) // C + 1
     BT = B * T
     phi, V = phi_y_valores(lay, E, half)
-    ids = ids_de(phi, T, lay.nb)
+    ids = ids_de(phi, T, lay.nb) if ids_override is None else np.asarray(ids_override, np.int32)
     rows = ids.transpose(0, 2, 1).reshape(BT, L)
     orden = np.argsort(rows, axis=-1, kind='stable')
     nulo = B * L
@@ -480,11 +481,15 @@ def acumular_fast(lay, E, Qc, Kc, Bt, log_alfa, sig, half):
             'orden': orden.astype(np.int32)}
 
 
-def layer_forward_fast(lay, E, h, tokens, half=False):
+def layer_forward_fast(lay, E, h, tokens, half=False, return_parts=False, ids_override=None):
     """layer_forward with the vectorised scoring (same results up to fp32 summation order)."""
     sig = firmas_de_piezas(tokens)
     Qc, Kc, beta, log_alfa = contexto(lay, h, half)
     Bt = np.cumsum(beta, axis=1)
-    acc = acumular_fast(lay, E, Qc, Kc, Bt, log_alfa, sig, half)
+    acc = acumular_fast(lay, E, Qc, Kc, Bt, log_alfa, sig, half, ids_override=ids_override)
     acc.update(repeticion(lay, sig, beta, Bt, log_alfa))
-    return combinar(lay, acc, h, half)
+    out = combinar(lay, acc, h, half)
+    if return_parts:
+        acc.update(Qc=Qc, Kc=Kc, beta=beta, log_alfa=log_alfa, Bt=Bt, sig=sig, out=out)
+        return acc
+    return out

@@ -12,6 +12,10 @@ reference's own intermediates and outputs, captured by calling the reference's m
   _claves_vistos / _ordenar_claves / _repeticion (asrn/nucleo.py:688-701, asrn/estable.py:304-321)
   forward -> h' (asrn/estable.py:407-421)
 The model fixture adds create_model + forward + generate (asrn/__init__.py:60-64, asrn/nucleo.py:1088-1103, 1965-2043).
+The generation-state fixture runs the O(1) writer _Escritor(o1=True) (asrn/nucleo.py:1717-1854) on a model whose rings
+overflow (chunk 4, 2 bits) and records, after the prompt and after every step, each layer's rings and counts
+(_anillo_desde / _anillo_meter, asrn/nucleo.py:1585-1618), the candidate positions of the step (_candidatos,
+asrn/nucleo.py:1621-1631) and the Hawkes state of every n-gram key (_MemoriaHawkes, asrn/nucleo.py:1634-1714).
 The fixtures are read by the tests on any machine; this script is the only place that imports the reference.
 """
 import os
@@ -129,6 +133,73 @@ def model_case(name, V, d, n_capas, B, L, L0, n_new, seed=0):
     print(f'{name}: {os.path.getsize(path) / 1024:.0f} KB')
 
 
+def _hawkes_dump(mem, B, n):
+    """(b, order, key, Bu, A) of every key of a _MemoriaHawkes, sorted by (b, order, key)."""
+    rows = []
+    for b in range(B):
+        for j in range(n):
+            for key, r in mem.mapas[b * n + j].items():
+                rows.append((b, j, key, float(mem.Bu[r]), float(mem.A[r])))
+    rows.sort(key=lambda t: (t[0], t[1], t[2]))
+    a = np.array(rows, dtype=np.float64).reshape(-1, 5)
+    return a[:, :2].astype(np.int32), a[:, 2], a[:, 3], a[:, 4].astype(np.float32)
+
+
+def gen_state_case(name, B=2, L0=40, n_new=24, seed=0):
+    """The O(1) writer's state on overflowing rings (chunk 4, 2 bits: 4 buckets per table), moved parameters, for
+    memoria_de_lo_ajeno on and off; the steps are fed the text's own next tokens (teacher forcing)."""
+    import asrn
+    from asrn import nucleo
+    torch.manual_seed(seed + 1)
+    m = asrn.create_model(V=60, d=32, n_capas=3, largo_cada=1, chunk=4, n_bits=2)
+    for c in m.largos:
+        _move(c, seed=seed + 3)
+    m.eval()
+    g = torch.Generator().manual_seed(seed + 2)
+    N = L0 + n_new
+    x = torch.randint(0, 60, (B, N), generator=g)
+    x[:, N // 2:N // 2 + N // 4] = x[:, :N // 4]
+    out = dict(tokens=x.numpy())
+    for ajeno in (True, False):
+        tag = 'ajeno' if ajeno else 'propia'
+        esc = nucleo._Escritor(m, ajeno, o1=True)
+        with torch.no_grad():
+            lg = esc.inicio(x[:, :L0], capacidad=N)
+            logits = [lg]
+            for j, (anillo, cuenta) in enumerate(esc.anillos):
+                out[f'{tag}.prompt.l{j}.ring'] = anillo.numpy()
+                out[f'{tag}.prompt.l{j}.count'] = cuenta.numpy()
+                out[f'{tag}.prompt.l{j}.ids'] = esc.cache[j]['ids'][:, :L0].numpy()
+                bj, key, bu, A = _hawkes_dump(esc.hawkes[j], B, m.largos[j].vistos)
+                out[f'{tag}.prompt.l{j}.hawkes_bj'], out[f'{tag}.prompt.l{j}.hawkes_key'] = bj, key
+                out[f'{tag}.prompt.l{j}.hawkes_bu'], out[f'{tag}.prompt.l{j}.hawkes_a'] = bu, A
+            for k in range(n_new - 1):
+                t = L0 + k
+                before = [a.clone() for a, _ in esc.anillos]
+                lg = esc.paso(x[:, t])
+                logits.append(lg)
+                for j, (anillo, cuenta) in enumerate(esc.anillos):
+                    ids_t = esc.cache[j]['ids'][:, t].long()                           # (B, T)
+                    Tn = ids_t.shape[1]
+                    cand = before[j][torch.arange(B).unsqueeze(1), torch.arange(Tn).unsqueeze(0), ids_t]
+                    out[f'{tag}.step{k}.l{j}.ids_t'] = ids_t.numpy().astype(np.int32)
+                    out[f'{tag}.step{k}.l{j}.cand'] = cand.numpy()
+                    out[f'{tag}.step{k}.l{j}.ring'] = anillo.numpy()
+                    out[f'{tag}.step{k}.l{j}.count'] = cuenta.numpy()
+                    bj, key, bu, A = _hawkes_dump(esc.hawkes[j], B, m.largos[j].vistos)
+                    out[f'{tag}.step{k}.l{j}.hawkes_bj'], out[f'{tag}.step{k}.l{j}.hawkes_key'] = bj, key
+                    out[f'{tag}.step{k}.l{j}.hawkes_bu'], out[f'{tag}.step{k}.l{j}.hawkes_a'] = bu, A
+        out[f'{tag}.logits'] = torch.stack(logits, 1).numpy()
+    for k, v in m.state_dict().items():
+        out['param.' + k] = _np(v)
+    meta = dict(V=60, d=32, n_capas=3, largo_cada=1, chunk=4, n_bits=2, B=B, L0=L0, n_new=n_new, seed=seed)
+    for k, v in meta.items():
+        out['meta.' + k] = np.array(v)
+    path = os.path.join(HERE, name + '.npz')
+    np.savez_compressed(path, **out)
+    print(f'{name}: {os.path.getsize(path) / 1024:.0f} KB')
+
+
 def init_case(name, V, d, n_capas, seed):
     """Checksums of create_model's freshly initialised weights (same seed -> same weights in the build)."""
     import asrn
@@ -157,7 +228,16 @@ def main(ref):
     layer_case('layer_f32_d256', 256, 1, 512, 256, False, {}, keep_values=False)
     model_case('model_small', V=256, d=64, n_capas=4, B=2, L=192, L0=96, n_new=24)
     init_case('init_cfg1', V=256, d=64, n_capas=4, seed=0)
+    gen_state_case('gen_state')
 
 
 if __name__ == '__main__':
-    main(sys.argv[1] if len(sys.argv) > 1 else '/root/reference')
+    if len(sys.argv) < 2:
+        sys.exit('usage: python tests/golden/make_golden.py <path of the reference checkout> [case ...]')
+    if len(sys.argv) > 2:                       # only the named cases
+        sys.path.insert(0, sys.argv[1])
+        torch.set_num_threads(8)
+        for case in sys.argv[2:]:
+            {'gen_state': lambda: gen_state_case('gen_state')}[case]()
+    else:
+        main(sys.argv[1])

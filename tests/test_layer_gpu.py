@@ -1,15 +1,15 @@
 """GPU parity of the CUDA path (libasrn_b200.so through the C ABI) against the reference's own outputs
 (tests/golden/*.npz) and the CPU oracle (oracle/asrn_oracle.py).
 
-Bars: bucket ids from the reference's phi, sort permutations, candidate indices and
-suffix-match lengths bit-exact; fp32 outputs within 1e-4 max-norm relative error; bf16 outputs within 2e-2.
-End-to-end bucket ids from our own phi may differ from the reference only where |phi_ref| is within rounding of 0.
+Bars: bucket ids from the reference's phi, sort permutations, candidate indices and suffix-match lengths bit-exact;
+fp32 outputs within 1e-4 max-norm relative error; bf16 outputs within 2e-2. End-to-end bucket ids from our own phi may
+differ from the reference only where |phi_ref| is within the precision's rounding of 0 (conftest.check_ids_agree).
 """
 import numpy as np
 import pytest
 import torch
 
-from conftest import LAYER_FIXTURES, layer_options, load_fixture, rel_err
+from conftest import LAYER_FIXTURES, check_ids_agree, layer_options, load_fixture, rel_err
 from oracle import asrn_oracle as O
 
 pytestmark = pytest.mark.gpu
@@ -59,9 +59,11 @@ def test_bucket_sort_of_reference_ids_is_bit_exact(name, cuda):
 
 
 @pytest.mark.parametrize('L,nb,rows', [(20000, 14, 3), (8193, 4, 2), (30000, 2, 2), (65536, 16, 1), (8192, 14, 2),
-                                       (1, 14, 1), (37, 3, 4)])
+                                       (1, 14, 1), (37, 3, 4), (5000, 9, 3), (1000, 16, 2), (2048, 1, 2),
+                                       (24, 14, 70000), (9000, 5, 3)])
 def test_bucket_sort_long_rows_match_stable_argsort(L, nb, rows, cuda):
-    """Rows longer than one tile (the per-tile histogram merge), many ties, and tiny rows."""
+    """Rows longer than one tile (the per-tile histogram merge), many ties, tiny rows, one- to three-pass digit splits
+    (1, 9, 14, 16 bits) and more rows than one launch's grid holds (70,000)."""
     from asrn_b200 import stages
     g = np.random.default_rng(L + nb)
     ids = g.integers(0, 1 << nb, (rows, L)).astype(np.int64)
@@ -170,19 +172,6 @@ def test_context_matches_reference(name, cuda):
     assert rel_err(Bt.cpu().numpy(), z['Bt']) <= 1e-6
 
 
-def _check_ids_agree(ids_got, ids_ref, phi_ref, nb):
-    """Our end-to-end bucket ids differ from the reference only on bits whose phi is within rounding of zero."""
-    if np.array_equal(ids_got, ids_ref):
-        return 1.0
-    B, L, T = ids_ref.shape
-    diff = ids_got ^ ids_ref
-    bits = (diff[..., None] >> np.arange(nb)) & 1                           # (B, L, T, nb)
-    ph = np.abs(phi_ref.reshape(B, L, T, nb))
-    scale = np.abs(phi_ref).max()
-    assert (ph[bits.astype(bool)] <= 2e-2 * scale).all(), 'a bucket bit flipped on a phi far from zero'
-    return float((ids_got == ids_ref).mean())
-
-
 @pytest.mark.parametrize('name', LAYER_FIXTURES)
 def test_hash_projection_matches_reference(name, cuda):
     from asrn_b200 import stages
@@ -193,7 +182,7 @@ def test_hash_projection_matches_reference(name, cuda):
     assert rel_err(out['phi'].float().cpu().numpy(), z['phi']) <= (TOL_BF16 if half else 1e-5)
     B, L, T = z['ids'].shape
     ids = stages.ids_rows_to_btl(out['ids_rows'], B, T).cpu().numpy()
-    agree = _check_ids_agree(ids, z['ids'], z['phi'], layer.n_bits)
+    agree = check_ids_agree(ids, z['ids'], z['phi'], layer.n_bits, half)
     assert agree >= 0.99
     if half:
         assert np.array_equal(out['Ea'].float().cpu().numpy(), O.bf16(z['E']))
@@ -239,7 +228,7 @@ def test_layer_forward_matches_reference(name, cuda):
     y = y.cpu().numpy()
     B, L, T = z['ids'].shape
     ids = stages.ids_rows_to_btl(stages.hash(layer, E, half=half)['ids_rows'], B, T).cpu().numpy()
-    _check_ids_agree(ids, z['ids'], z['phi'], layer.n_bits)
+    check_ids_agree(ids, z['ids'], z['phi'], layer.n_bits, half)
     if np.array_equal(ids, z['ids']):
         ref = z['out']
     else:                                                  # compare with the oracle conditioned on our bucket ids
@@ -284,7 +273,7 @@ def test_layer_forward_matches_oracle_on_seeded_inputs(d, B, L, half, opts, cuda
     lay = O.Layer(params, d, **opts)
     parts = O.layer_forward(lay, E, h, x, half=half, return_parts=True, ids_override=ids)
     ids_oracle = O.ids_de(O.phi_y_valores(lay, E, half)[0], layer.n_tablas, layer.n_bits)
-    _check_ids_agree(ids, ids_oracle, O.phi_y_valores(lay, E, half)[0], layer.n_bits)
+    check_ids_agree(ids, ids_oracle, O.phi_y_valores(lay, E, half)[0], layer.n_bits, half)
     tol = TOL_BF16 if half else TOL_F32
     assert rel_err(y, parts['out']) <= tol
     assert rel_err(y - h, parts['out'] - h) <= tol
@@ -329,7 +318,7 @@ def test_signatures_from_vectors_when_no_token_ids(cuda):
 
 
 @pytest.mark.parametrize('d,B,L', [(768, 2, 1000), (64, 3, 300), (256, 1, 4096)])
-def test_tensor_core_gemms_match_cuda_core_kernels(d, B, L, cuda, monkeypatch):
+def test_tensor_core_gemms_match_cuda_core_kernels(d, B, L, cuda):
     """The tcgen05 hash projection and gate GEMM (bf16) against the CUDA-core kernels on the same inputs: bf16 E copy
     bit-exact, phi within bf16 rounding, bucket ids equal except on bits whose phi is within rounding of 0, h' within
     the bf16 tolerance, and the device status word clean (no bounded wait timed out)."""
@@ -345,24 +334,24 @@ def test_tensor_core_gemms_match_cuda_core_kernels(d, B, L, cuda, monkeypatch):
     x[:, L // 2:L // 2 + L // 4] = x[:, :L // 4]
     E = (torch.randn(300, d, generator=g)[x]).to(cuda)
     h = torch.randn(B, L, d, generator=g).to(cuda)
-    outs = {}
-    for mode in ('tc', 'simt'):
-        if mode == 'simt':
-            monkeypatch.setenv('ASRN_B200_GEMM', 'simt')
-        else:
-            monkeypatch.delenv('ASRN_B200_GEMM', raising=False)
+
+    def run():
         hs = stages.hash(layer, E, half=True)
         with torch.no_grad(), torch.autocast('cuda', dtype=torch.bfloat16):
             y = layer(E, h, x.to(cuda))
-        outs[mode] = (hs, y)
-    monkeypatch.delenv('ASRN_B200_GEMM', raising=False)
+        return hs, y
+
+    outs = {'tc': run()}
+    with _lib.force_cuda_core():
+        outs['simt'] = run()
+    assert _lib.gemm_override() is None
     (h_tc, y_tc), (h_si, y_si) = outs['tc'], outs['simt']
     assert torch.equal(h_tc['Ea'], h_si['Ea'])
     phi_tc, phi_si = h_tc['phi'].float().cpu().numpy(), h_si['phi'].float().cpu().numpy()
     assert rel_err(phi_tc, phi_si) <= 2e-2
     ids_tc = stages.ids_rows_to_btl(h_tc['ids_rows'], B, 8).cpu().numpy()
     ids_si = stages.ids_rows_to_btl(h_si['ids_rows'], B, 8).cpu().numpy()
-    _check_ids_agree(ids_tc, ids_si, phi_si, layer.n_bits)
+    check_ids_agree(ids_tc, ids_si, phi_si, layer.n_bits, True)
     if np.array_equal(ids_tc, ids_si):
         assert rel_err(y_tc.cpu().numpy(), y_si.cpu().numpy()) <= TOL_BF16
         assert rel_err((y_tc - h).cpu().numpy(), (y_si - h).cpu().numpy()) <= TOL_BF16
@@ -370,3 +359,27 @@ def test_tensor_core_gemms_match_cuda_core_kernels(d, B, L, cuda, monkeypatch):
     cfg = _lib.make_config(layer, B, L, True)
     import ctypes
     assert _lib.lib().asrn_layer_status(ctypes.byref(cfg), _lib.ptr(prep), 0, _lib.stream_ptr(cuda)) == 0
+
+
+def test_bounded_wait_gives_up_and_the_context_stays_usable(cuda):
+    """A bounded mbarrier wait (the one every tcgen05 kernel uses) on a barrier nothing arrives on, with a 50 ms
+    limit: the kernel returns, ASRN_ERR_TIMEOUT is in the status word, its TMEM is freed (a second probe can allocate
+    it again) and the next layer forward runs and is correct."""
+    import time
+    from asrn_b200 import _lib
+    lib = _lib.lib()
+    for _ in range(2):
+        status = torch.zeros(1, dtype=torch.int32, device=cuda)
+        result = torch.full((1,), 7, dtype=torch.int32, device=cuda)
+        t0 = time.perf_counter()
+        assert lib.asrn_test_bounded_wait(50_000_000, _lib.ptr(status), _lib.ptr(result), _lib.stream_ptr(cuda)) == 0
+        torch.cuda.synchronize()
+        elapsed = time.perf_counter() - t0
+        assert int(status.item()) == _lib.ASRN_ERR_TIMEOUT
+        assert int(result.item()) == 0
+        assert 0.04 <= elapsed < 5.0
+    z, params, meta = load_fixture('layer_f32')
+    layer = _layer(params, meta, cuda)
+    with torch.no_grad():
+        y = layer(_t(z['E'], cuda), _t(z['h'], cuda), _t(z['tokens'], cuda)).cpu().numpy()
+    assert rel_err(y, z['out']) <= TOL_F32

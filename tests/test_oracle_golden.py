@@ -77,3 +77,57 @@ def test_hawkes_matches_quadratic_definition():
         kern = np.exp(log_alfa)[:, None, :] * np.exp(-kappa[k] * np.maximum(Bt[:, :, None] - Bt[:, None, :], 0))
         assert np.allclose(r['hawkes'][..., k], (same * kern).sum(-1), atol=1e-4)
     assert np.array_equal((r['hawkes'] > 0).astype(np.float32), r['vistos'])
+
+
+@pytest.mark.parametrize('name', ['layer_f32', 'layer_bf16', 'layer_f32_opts', 'layer_f32_d96', 'layer_bf16_d256'])
+def test_vectorised_oracle_matches_reference_layer(name):
+    """The vectorised restatement (the reference's window formulation, used at benchmark sizes) against the
+    reference's outputs, and conditioned on the reference's own bucket ids (ids_override) it gives the same h'."""
+    z, params, meta = load_fixture(name)
+    half = bool(meta['bf16'])
+    lay = O.Layer(params, meta['d'], **layer_options(meta))
+    tol = 2e-3 if half else 1e-5
+    parts = O.layer_forward_fast(lay, z['E'], z['h'], z['tokens'], half=half, return_parts=True)
+    assert np.array_equal(parts['ids'], z['ids'])
+    assert np.array_equal(parts['orden'], z['orden'])
+    for k in ('salida', 'mejor', 'pico', 'out'):
+        assert rel_err(parts[k], z[k]) <= tol, (k, rel_err(parts[k], z[k]))
+    assert rel_err(parts['out'] - z['h'], z['out'] - z['h']) <= tol
+    over = O.layer_forward_fast(lay, z['E'], z['h'], z['tokens'], half=half, ids_override=z['ids'])
+    assert np.array_equal(over, parts['out'])
+
+
+def test_vectorised_oracle_equals_per_query_definition_in_the_full_bucket_regime():
+    """Small embeddings make the hash bias-dominated, so long bucket runs give every query C candidates (the regime of
+    the benchmark): the vectorised windows and the per-query definition agree."""
+    z, params, meta = load_fixture('layer_bf16')
+    lay = O.Layer(params, meta['d'])
+    g = np.random.default_rng(11)
+    B, L, d = 1, 300, meta['d']
+    x = g.integers(0, 40, (B, L))
+    E = (g.standard_normal((40, d)) * 0.02).astype(np.float32)[x]
+    h = g.standard_normal((B, L, d)).astype(np.float32)
+    for half in (False, True):
+        a = O.layer_forward(lay, E, h, x, half=half, return_parts=True)
+        b = O.layer_forward_fast(lay, E, h, x, half=half)
+        same = (a['ids_o'][:, 1:] == a['ids_o'][:, :-1]).mean()
+        assert same > 0.5
+        assert rel_err(b, a['out']) <= (2e-3 if half else 1e-5)
+
+
+def test_flip_bound_rejects_a_flip_far_from_zero():
+    """A planted bucket-bit flip on a phi far from zero fails the agreement check; one within rounding passes."""
+    from conftest import check_ids_agree
+    z, params, meta = load_fixture('layer_f32')
+    ids, phi = z['ids'].copy(), z['phi']
+    B, L, T = ids.shape
+    nb = phi.shape[-1] // T
+    ph = np.abs(phi.reshape(B, L, T, nb))
+    big = np.unravel_index(np.argmax(ph), ph.shape)
+    bad = ids.copy()
+    bad[big[:3]] ^= 1 << big[3]
+    with pytest.raises(AssertionError):
+        check_ids_agree(bad, ids, phi, nb, half=False)
+    phi_small = phi.copy().reshape(B, L, T, nb)
+    phi_small[big] = 1e-9
+    assert check_ids_agree(bad, ids, phi_small.reshape(phi.shape), nb, half=False) < 1.0

@@ -96,3 +96,133 @@ def test_exchange_steps_with_two_gloo_ranks(tmp_path):
         assert torch.equal(r['ng'][0], torch.stack([k0, k0 + 10], 0))
         assert (r['ng'][1][0] == 1).all() and (r['ng'][1][1] == 2).all()
         assert torch.equal(r['maps'], torch.tensor([[[0.5, 1.0]], [[0.5, 2.0]]]))
+
+
+# ---- failure detection of the exchange (host-side faults on gloo ranks; no GPU involved) -----------------------------
+
+def _carries(rank, world, Lc=4, C=3, rows=2, nbins=4, B=2):
+    """A consistent set of one rank's carries: chunk sums of beta, bucket tails inside the rank's chunk, sorted n-gram
+    keys and streak maps."""
+    sums = torch.tensor([1.5 + rank, 0.25], dtype=torch.float64)
+    tails = torch.zeros(rows, nbins, C + 1, dtype=torch.int32)
+    for r in range(rows):
+        for b in range(nbins):
+            n = (r + b + rank) % (C + 1)
+            tails[r, b, 0] = n
+            tails[r, b, 1:1 + n] = torch.arange(n, dtype=torch.int32) + rank * Lc
+    keys = torch.arange(B * 3 * Lc, dtype=torch.int64).view(B * 3, Lc) * 7 + 5     # unsigned images: ascending
+    maps = torch.tensor([[0.5, 1.0 + rank]] * B, dtype=torch.float32)
+    return sums, tails, keys, maps
+
+
+def _exchange_and_validate(world, rank, corrupt=None, Lc=4, C=3):
+    from asrn_b200 import shard
+    sums, tails, keys, maps = _carries(rank, world, Lc, C)
+    if corrupt == 'tail_count' and rank == 1:
+        tails[0, 1, 0] = C + 2
+    if corrupt == 'tail_position' and rank == 1:
+        tails[1, 2, 0] = 2
+        tails[1, 2, 1:3] = torch.tensor([0, 1], dtype=torch.int32)          # rank 0's chunk, not rank 1's
+    if corrupt == 'sum' and rank == 1:
+        sums[0] = float('nan')
+    if corrupt == 'map' and rank == 1:
+        maps[0, 0] = 3.0
+    if corrupt == 'keys' and rank == 1:
+        keys[0, 1] = keys[0, 2] + 1                                         # out of order
+    s = shard.exchange_chunk_sums(sums, world)
+    t = shard.exchange_tails(tails, world)
+    k, _ = shard.exchange_ngram(keys, torch.zeros(keys.shape + (32,), dtype=torch.uint8), world)
+    m = shard.exchange_racha_maps(maps, world)
+    n = int(shard.carry_violations(sums=s, maps=m, keys=k, tails=t, Lc=Lc, C=C))
+    if n:
+        raise shard.ShardExchangeError(f'{n} violations')
+    return 'ok'
+
+
+def _fault_rank(rank, world, port, out, scenario, timeout_s):
+    """One gloo rank of a fault scenario; records what it observed in out/rank<r>.txt and exits 0 (a rank that hit
+    an error leaves without tearing the group down: its peers may be gone)."""
+    import datetime
+    import time
+    import torch.distributed as dist
+    os.environ['MASTER_ADDR'] = '127.0.0.1'
+    os.environ['MASTER_PORT'] = str(port)
+    dist.init_process_group('gloo', rank=rank, world_size=world, timeout=datetime.timedelta(seconds=timeout_s))
+    from asrn_b200 import shard
+    t0 = time.time()
+    try:
+        if scenario.startswith('corrupt_'):
+            res = _exchange_and_validate(world, rank, corrupt=scenario[len('corrupt_'):])
+        elif scenario == 'clean':
+            res = _exchange_and_validate(world, rank)
+        elif scenario == 'late_within_timeout':
+            if rank == 1:
+                time.sleep(1.0)
+            res = _exchange_and_validate(world, rank)
+        elif scenario == 'late_past_timeout':
+            if rank == 1:
+                time.sleep(3 * timeout_s)
+            res = _exchange_and_validate(world, rank)
+        elif scenario == 'leaves_between_steps':
+            _exchange_and_validate(world, rank)                            # step 1: every rank
+            if rank == 1:
+                with open(os.path.join(out, f'rank{rank}.txt'), 'w') as f:
+                    f.write('left 0.0')
+                os._exit(0)                                                  # gone before step 2
+            res = _exchange_and_validate(world, rank)                        # step 2: the peer has left
+        else:
+            raise ValueError(scenario)
+    except shard.ShardExchangeError:
+        res = 'invalid'
+    except Exception as exc:                                                # the backend's error for a lost peer
+        res = 'error:' + type(exc).__name__
+    with open(os.path.join(out, f'rank{rank}.txt'), 'w') as f:
+        f.write(f'{res} {time.time() - t0:.2f}')
+    if res == 'ok':
+        dist.destroy_process_group()
+    os._exit(0)
+
+
+def _run_fault(tmp_path, scenario, timeout_s=3):
+    import torch.multiprocessing as mp
+    world = 2
+    mp.start_processes(_fault_rank, args=(world, _free_port(), str(tmp_path), scenario, timeout_s), nprocs=world,
+                       start_method='spawn')
+    out = []
+    for r in range(world):
+        res, secs = (tmp_path / f'rank{r}.txt').read_text().split()
+        out.append((res, float(secs)))
+    return out
+
+
+@pytest.mark.timeout(120)
+@pytest.mark.parametrize('what', ['tail_count', 'tail_position', 'sum', 'map', 'keys'])
+def test_exchange_detects_a_corrupted_carry(tmp_path, what):
+    """A rank that sends inconsistent carry state: every rank's validation of the gathered state reports it."""
+    res = _run_fault(tmp_path, 'corrupt_' + what)
+    assert [r for r, _ in res] == ['invalid', 'invalid']
+
+
+@pytest.mark.timeout(120)
+@pytest.mark.parametrize('scenario', ['clean', 'late_within_timeout'])
+def test_exchange_of_consistent_carries_passes(tmp_path, scenario):
+    """Consistent carries pass validation, also when one rank reaches the exchange late but within the timeout."""
+    assert [r for r, _ in _run_fault(tmp_path, scenario)] == ['ok', 'ok']
+
+
+@pytest.mark.timeout(120)
+def test_exchange_reports_a_rank_late_past_the_timeout(tmp_path):
+    """Rank 1 reaches the exchange three timeouts late: rank 0's collective ends with the backend's error within a
+    few timeouts instead of waiting for it."""
+    res = _run_fault(tmp_path, 'late_past_timeout', timeout_s=2)
+    assert res[0][0].startswith('error:')
+    assert res[0][1] < 5 * 2
+
+
+@pytest.mark.timeout(120)
+def test_exchange_reports_a_rank_that_left_between_steps(tmp_path):
+    """Rank 1 leaves after step 1: rank 0's step-2 exchange ends with an error instead of hanging."""
+    res = _run_fault(tmp_path, 'leaves_between_steps', timeout_s=3)
+    assert res[1][0] == 'left'
+    assert res[0][0].startswith('error:')
+    assert res[0][1] < 5 * 3

@@ -73,3 +73,13 @@ def test_noalloc_bucket_sort_rejects_requests_beyond_its_scratch():
     assert st == 0
     assert np.array_equal(orden.cpu().numpy(), np.argsort(small.cpu().numpy().view(np.uint16).astype(np.int64),
                                                            axis=-1, kind='stable'))
+
+
+def test_noalloc_bucket_sort_empty_input_matches_workspace_version():
+    """Empty input returns ASRN_OK from both entry points, whatever the bit count (nothing is sorted or checked)."""
+    from asrn_b200 import _lib
+    dev = torch.device('cuda:0')
+    lib = _lib.lib()
+    for rows, L, nb in ((0, 100, 14), (3, 0, 14), (0, 0, 99)):
+        assert lib.asrn_bucket_sort_noalloc(rows, L, nb, None, None, None, _lib.stream_ptr(dev)) == 0
+        assert lib.asrn_bucket_sort(rows, L, nb, None, None, None, None, 0, _lib.stream_ptr(dev)) == 0
