@@ -261,8 +261,30 @@ def warm_up(step, warmup, world):
             return n
 
 
+def _kernel_node_name(nd):
+    """Name of a graph kernel node's function (driver API, then runtime API), or '?'."""
+    try:
+        from cuda.bindings import driver as cu
+        err, prm = cu.cuGraphKernelNodeGetParams(cu.CUgraphNode(int(nd)))
+        if int(err) == 0:
+            err, nm = cu.cuFuncGetName(prm.func)
+            if int(err) == 0:
+                return nm.decode() if isinstance(nm, bytes) else str(nm)
+    except Exception:
+        pass
+    try:
+        from cuda.bindings import runtime as rt
+        err, prm = rt.cudaGraphKernelNodeGetParams(nd)
+        err, nm = rt.cudaFuncGetName(prm.func)
+        if int(err) == 0:
+            return nm.decode() if isinstance(nm, bytes) else str(nm)
+    except Exception:
+        pass
+    return '?'
+
+
 def count_graph_kernels(graph):
-    """(all kernel nodes, those of libasrn_b200 (named k_*), names) of a captured CUDA graph, or Nones."""
+    """(all kernel nodes, those of libasrn_b200 (named k_*), {name: count}) of a captured CUDA graph, or Nones."""
     try:
         from cuda.bindings import runtime as rt
         g = graph.raw_cuda_graph()
@@ -274,15 +296,10 @@ def count_graph_kernels(graph):
             if ty != rt.cudaGraphNodeType.cudaGraphNodeTypeKernel:
                 continue
             kernels += 1
-            name = '?'
-            try:
-                err, prm = rt.cudaGraphKernelNodeGetParams(nd)
-                err, nm = rt.cudaFuncGetName(prm.func)
-                name = nm.decode() if isinstance(nm, bytes) else str(nm)
-            except Exception:                         # names are a nicety; the count is what matters
-                pass
-            names[name] = names.get(name, 0) + 1
-            if name.startswith('k_') or 'asrn' in name:
+            name = _kernel_node_name(nd)
+            short = name.split('(')[0].split('<')[0].replace('asrn::', '')
+            names[short] = names.get(short, 0) + 1
+            if 'asrn' in name or short.startswith('k_') or short.startswith('_ZN4asrn'):
                 ours += 1
         return kernels, ours, names
     except Exception:

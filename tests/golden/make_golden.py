@@ -167,9 +167,10 @@ def gen_state_case(name, B=2, L0=40, n_new=24, seed=0):
             lg = esc.inicio(x[:, :L0], capacidad=N)
             logits = [lg]
             for j, (anillo, cuenta) in enumerate(esc.anillos):
-                out[f'{tag}.prompt.l{j}.ring'] = anillo.numpy()
-                out[f'{tag}.prompt.l{j}.count'] = cuenta.numpy()
-                out[f'{tag}.prompt.l{j}.ids'] = esc.cache[j]['ids'][:, :L0].numpy()
+                # copies: the writer updates its rings and caches in place at every step
+                out[f'{tag}.prompt.l{j}.ring'] = anillo.numpy().copy()
+                out[f'{tag}.prompt.l{j}.count'] = cuenta.numpy().copy()
+                out[f'{tag}.prompt.l{j}.ids'] = esc.cache[j]['ids'][:, :L0].numpy().copy()
                 bj, key, bu, A = _hawkes_dump(esc.hawkes[j], B, m.largos[j].vistos)
                 out[f'{tag}.prompt.l{j}.hawkes_bj'], out[f'{tag}.prompt.l{j}.hawkes_key'] = bj, key
                 out[f'{tag}.prompt.l{j}.hawkes_bu'], out[f'{tag}.prompt.l{j}.hawkes_a'] = bu, A
@@ -183,13 +184,13 @@ def gen_state_case(name, B=2, L0=40, n_new=24, seed=0):
                     Tn = ids_t.shape[1]
                     cand = before[j][torch.arange(B).unsqueeze(1), torch.arange(Tn).unsqueeze(0), ids_t]
                     out[f'{tag}.step{k}.l{j}.ids_t'] = ids_t.numpy().astype(np.int32)
-                    out[f'{tag}.step{k}.l{j}.cand'] = cand.numpy()
-                    out[f'{tag}.step{k}.l{j}.ring'] = anillo.numpy()
-                    out[f'{tag}.step{k}.l{j}.count'] = cuenta.numpy()
+                    out[f'{tag}.step{k}.l{j}.cand'] = cand.numpy().copy()
+                    out[f'{tag}.step{k}.l{j}.ring'] = anillo.numpy().copy()
+                    out[f'{tag}.step{k}.l{j}.count'] = cuenta.numpy().copy()
                     bj, key, bu, A = _hawkes_dump(esc.hawkes[j], B, m.largos[j].vistos)
                     out[f'{tag}.step{k}.l{j}.hawkes_bj'], out[f'{tag}.step{k}.l{j}.hawkes_key'] = bj, key
                     out[f'{tag}.step{k}.l{j}.hawkes_bu'], out[f'{tag}.step{k}.l{j}.hawkes_a'] = bu, A
-        out[f'{tag}.logits'] = torch.stack(logits, 1).numpy()
+        out[f'{tag}.logits'] = torch.stack(logits, 1).numpy().copy()
     for k, v in m.state_dict().items():
         out['param.' + k] = _np(v)
     meta = dict(V=60, d=32, n_capas=3, largo_cada=1, chunk=4, n_bits=2, B=B, L0=L0, n_new=n_new, seed=seed)
