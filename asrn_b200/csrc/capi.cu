@@ -62,7 +62,7 @@ Workspace workspace_layout(const asrn_layer_config& c) {
   w.ids_rows = take(M * T * 2);
   w.orden = take(M * T * 4);
   w.ids_o = take(M * T * 2);
-  w.acc = take(M * d * 4);
+  w.acc = take(M * d * (c.half ? 2 : 4));      // bf16 accumulator under autocast
   w.hay = take(M * T);
   w.mx = take(M * T * 4);
   w.pk = take(M * T * 4);
@@ -71,7 +71,7 @@ Workspace workspace_layout(const asrn_layer_config& c) {
   w.racha = take(M * 4);
   w.sort_bytes = bucket_sort_workspace((int64_t)c.B * T, c.L, c.n_bits);
   w.sort = take(w.sort_bytes);
-  w.sigma = take(M * 4);
+  w.sigma = take(M * 8);                       // gate values and 1 / max(1, pt) (tensor-core gate)
   w.rep = take(repetition_workspace(c.B, c.L, c.vistos));
   w.total = o;
   return w;
@@ -221,7 +221,7 @@ int asrn_layer_forward(const asrn_layer_config* cfg, const asrn_layer_weights* w
   uint16_t* ids_rows = reinterpret_cast<uint16_t*>(base + ws.ids_rows);
   int32_t* orden = reinterpret_cast<int32_t*>(base + ws.orden);
   uint16_t* ids_o = reinterpret_cast<uint16_t*>(base + ws.ids_o);
-  float* acc = reinterpret_cast<float*>(base + ws.acc);
+  void* acc = base + ws.acc;
   uint8_t* hay = reinterpret_cast<uint8_t*>(base + ws.hay);
   float* mx = reinterpret_cast<float*>(base + ws.mx);
   float* pk = reinterpret_cast<float*>(base + ws.pk);
@@ -238,7 +238,7 @@ int asrn_layer_forward(const asrn_layer_config* cfg, const asrn_layer_weights* w
   if ((st = launch_bucket_sort(c.B * c.n_tablas, c.L, c.n_bits, ids_rows, orden, ids_o, base + ws.sort,
                                ws.sort_bytes, s)))
     return st;
-  if (cudaMemsetAsync(acc, 0, (size_t)M * c.d * 4, s) != cudaSuccess) return ASRN_ERR_CUDA;
+  if (cudaMemsetAsync(acc, 0, (size_t)M * c.d * (c.half ? 2 : 4), s) != cudaSuccess) return ASRN_ERR_CUDA;
   ScoreArgs sa = score_args(c, *w, prep);
   sa.orden = orden; sa.ids_o = ids_o; sa.phi = phi; sa.Qc = base + ws.qc; sa.Kc = base + ws.kc; sa.sig = sig;
   sa.Bt = Bt; sa.log_alfa = la; sa.Ea = Ea; sa.acc = acc; sa.sen_hay = hay; sa.sen_mx = mx; sa.sen_pk = pk;
@@ -248,11 +248,14 @@ int asrn_layer_forward(const asrn_layer_config* cfg, const asrn_layer_weights* w
   ra.racha = racha;
   if ((st = launch_repetition(ra, base + ws.rep, repetition_workspace(c.B, c.L, c.vistos), s))) return st;
   GateArgs ga = gate_args(c, *w, prep);
-  ga.h = h; ga.glogit = glogit; ga.acc = acc; ga.sen_hay = hay; ga.sen_mx = mx; ga.sen_pk = pk;
+  ga.h = h; ga.glogit = glogit; ga.sen_hay = hay; ga.sen_mx = mx; ga.sen_pk = pk;
   ga.vistos = vistos; ga.hawkes = hawkes; ga.racha = racha; ga.out = h_out;
-  if (c.half) {   // the bf16 copy of E is dead after scoring: it holds the gate's GEMM operand
-    ga.cbuf = reinterpret_cast<__nv_bfloat16*>(base + ws.ea);
+  if (c.half) {
+    ga.acc16 = reinterpret_cast<const __nv_bfloat16*>(acc);
     ga.sigma = reinterpret_cast<float*>(base + ws.sigma);
+    ga.rpt = ga.sigma + M;
+  } else {
+    ga.acc = reinterpret_cast<const float*>(acc);
   }
   return launch_gate(ga, c.half, s);
 }
@@ -302,7 +305,7 @@ int asrn_bucket_sort(int64_t rows, int64_t L, int32_t nb, const uint16_t* ids_ro
 
 int asrn_score(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared,
                const int32_t* orden, const uint16_t* ids_o, const void* phi, const void* Qc, const void* Kc,
-               const float* sig, const double* Bt, const float* log_alfa, const void* Ea, float* acc,
+               const float* sig, const double* Bt, const float* log_alfa, const void* Ea, void* acc,
                uint8_t* sen_hay, float* sen_mx, float* sen_pk, void* stream) {
   int st = check_config(cfg);
   if (st) return st;
@@ -363,7 +366,7 @@ int asrn_shard_merge(int64_t rows, int64_t Lc, int32_t nb, int32_t C, int64_t c0
 int asrn_score_shard(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared, int64_t L_feat,
                      int64_t q_lo, int64_t q_hi, const int32_t* orden, const uint16_t* ids_o, const void* phi,
                      const void* Qc, const void* Kc, const float* sig, const double* Bt, const float* log_alfa,
-                     const void* Ea, const int64_t* row_len, float* acc, uint8_t* sen_hay, float* sen_mx,
+                     const void* Ea, const int64_t* row_len, void* acc, uint8_t* sen_hay, float* sen_mx,
                      float* sen_pk, void* stream) {
   int st = check_config(cfg);
   if (st) return st;
@@ -471,7 +474,7 @@ size_t asrn_gate_workspace_bytes(const asrn_layer_config* cfg) {
 }
 
 int asrn_gate(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared, const float* h,
-              const float* glogit, const float* acc, const uint8_t* sen_hay, const float* sen_mx,
+              const float* glogit, const void* acc, const uint8_t* sen_hay, const float* sen_mx,
               const float* sen_pk, const uint8_t* vistos, const float* hawkes, const float* racha, float* h_out,
               void* workspace, size_t workspace_bytes, void* stream) {
   int st = check_config(cfg);
@@ -480,14 +483,15 @@ int asrn_gate(const asrn_layer_config* cfg, const asrn_layer_weights* w, const v
   if (!prepared || !h || !glogit || !acc || !sen_hay || !sen_mx || !sen_pk || !vistos || !hawkes || !racha || !h_out)
     return ASRN_ERR_ARG;
   GateArgs a = gate_args(*cfg, *w, reinterpret_cast<const char*>(prepared));
-  a.h = h; a.glogit = glogit; a.acc = acc; a.sen_hay = sen_hay; a.sen_mx = sen_mx; a.sen_pk = sen_pk;
+  a.h = h; a.glogit = glogit; a.sen_hay = sen_hay; a.sen_mx = sen_mx; a.sen_pk = sen_pk;
   a.vistos = vistos; a.hawkes = hawkes; a.racha = racha; a.out = h_out;
+  if (cfg->half) a.acc16 = reinterpret_cast<const __nv_bfloat16*>(acc);
+  else a.acc = reinterpret_cast<const float*>(acc);
   const size_t need = gate_workspace(cfg->B * cfg->L, (int)cfg->d, cfg->half != 0);
   if (need > 0) {
     if (!workspace || workspace_bytes < need) return ASRN_ERR_WORKSPACE;
-    a.cbuf = reinterpret_cast<__nv_bfloat16*>(workspace);
-    a.sigma = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) +
-                                       align_up((size_t)cfg->B * cfg->L * cfg->d * 2));
+    a.sigma = reinterpret_cast<float*>(workspace);
+    a.rpt = a.sigma + cfg->B * cfg->L;
   }
   return launch_gate(a, cfg->half, as_stream(stream));
 }

@@ -66,6 +66,25 @@ ASRN_DEV void red_add_v4(float* addr, float a, float b, float c, float d) {
 ASRN_DEV void red_add_f32(float* addr, float a) {
   asm volatile("red.global.add.f32 [%0], %1;" ::"l"(addr), "f"(a) : "memory");
 }
+// bf16 reductions into global memory (resolved in L2): each element rounds (its value + the addend) to bf16.
+ASRN_DEV uint32_t pack2_bf16(float lo, float hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+ASRN_DEV void red_add_bf16x8(__nv_bfloat16* addr, uint32_t p0, uint32_t p1, uint32_t p2, uint32_t p3) {
+  asm volatile("red.global.add.noftz.v4.bf16x2 [%0], {%1, %2, %3, %4};" ::"l"(addr), "r"(p0), "r"(p1), "r"(p2),
+               "r"(p3)
+               : "memory");
+}
+ASRN_DEV void red_add_bf16x4(__nv_bfloat16* addr, float a, float b, float c, float d) {
+  asm volatile("red.global.add.noftz.v2.bf16x2 [%0], {%1, %2};" ::"l"(addr), "r"(pack2_bf16(a, b)),
+               "r"(pack2_bf16(c, d))
+               : "memory");
+}
+ASRN_DEV void red_add_bf16(__nv_bfloat16* addr, float a) {
+  const unsigned short v = __bfloat16_as_ushort(__float2bfloat16_rn(a));
+  asm volatile("red.global.add.noftz.bf16 [%0], %1;" ::"l"(addr), "h"(v) : "memory");
+}
 
 // ---- torch-compatible scalar math ----------------------------------------------------------------------------------
 // torch.nn.functional.softplus with beta = 1, threshold = 20.

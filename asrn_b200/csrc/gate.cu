@@ -4,8 +4,8 @@
 //   logit = g(h) + g_conf([pt/T, mejor, pico/max(1,pt), pt_ctx/Tc]) + w_vistos . vistos + u_hawkes . log1p(hawkes)
 //           + response(racha)                                     (all fp32; g_conf in bf16 under autocast)
 //   h' = h + sigmoid(logit) * o(salida / max(1, pt))
-// Here salida = W_v acc (acc = sum of att * Ea rows from the scoring kernel), so o(salida) = (W_o W_v) acc and the
-// projection is one GEMM against the prepared W_ov.
+// Here salida = W_v acc (acc = sum of att * Ea rows from the scoring kernel; a bf16 accumulator under autocast), so
+// o(salida / pt) = (W_o W_v) acc / pt and the projection is one GEMM against the prepared W_ov.
 #include "common.cuh"
 #include "gate.cuh"
 #include "layout.h"
@@ -42,7 +42,8 @@ __global__ void __launch_bounds__(256) k_gate_simt(GateArgs a) {
       const int r = e / kGateKC, kk = e % kGateKC;
       const int64_t g = t0 + r;
       const int k = k0 + kk;
-      As[kk][r] = (g < M && k < d) ? act<Half>(__fdiv_rn(a.acc[g * d + k], s_pt[r])) : 0.f;
+      const float av = (g < M && k < d) ? (a.acc16 ? __bfloat162float(a.acc16[g * d + k]) : a.acc[g * d + k]) : 0.f;
+      As[kk][r] = (g < M && k < d) ? act<Half>(__fdiv_rn(av, s_pt[r])) : 0.f;
     }
     for (int e = tid; e < kGateTN * kGateKC; e += blockDim.x) {
       const int c = e / kGateKC, kk = e % kGateKC;
@@ -79,32 +80,23 @@ __global__ void __launch_bounds__(256) k_gate_simt(GateArgs a) {
 }
 
 // ---- tensor-core version (bf16 autocast mode) -------------------------------------------------------------------
-// k_gate_prep: one warp per token computes the gate sigmoid(logit) (rounded to bf16) and the GEMM operand
-//   c = bf16(acc / max(1, pt)) (asrn/estable.py:387, the autocast rounding of o's input); memory-bound.
-// k_gate_tc: h' = h + bf16(sigma * bf16(c . W_ov^T)). Tile 128 tokens (TMEM lanes) x NT columns (TMEM columns),
-//   K = d in chunks of 64; both operands by TMA (128-byte swizzle), one producer thread and one MMA thread
-//   (tcgen05.commit frees each stage), the fp32 accumulators in TMEM; in the epilogue each thread owns one tile row
-//   (its TMEM lane) and reads h / writes h' for 32 consecutive columns at a time with 16-byte accesses.
-__global__ void __launch_bounds__(256) k_gate_prep(GateArgs a) {
-  const int lane = threadIdx.x & 31;
-  const int64_t g = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int64_t M = a.B * a.L;
-  if (g >= M) return;
-  float sg = 0.f, pt = 1.f;
-  if (lane == 0) gate_of_token<true>(a, g, &sg, &pt);
-  sg = __shfl_sync(0xffffffffu, sg, 0);
-  pt = __shfl_sync(0xffffffffu, pt, 0);
-  if (lane == 0) a.sigma[g] = sg;
-  // pt is a count of tables (1 .. T): the quotient is taken as a product with 1 / pt (exact for powers of two, else
+// k_gate_scalars: one thread per token computes the gate sigmoid(logit) (rounded to bf16) and 1 / max(1, pt).
+// k_gate_tc: h' = h + bf16(sigma * bf16((acc . W_ov^T) / max(1, pt))) with acc the scoring's bf16 accumulator read as
+//   the A operand (the reference rounds acc / pt to bf16 before o; here the division follows the GEMM: the same value
+//   up to bf16 rounding). Tile 128 tokens (TMEM lanes) x NT columns (TMEM columns), K = d in chunks of 64; both
+//   operands by TMA (128-byte swizzle), one producer thread and one MMA thread (tcgen05.commit frees each stage), the
+//   fp32 accumulators in TMEM; in the epilogue each thread owns one tile row (its TMEM lane) and reads h / writes h'
+//   for 32 consecutive columns at a time with 16-byte accesses.
+template <bool Half>
+__global__ void __launch_bounds__(256) k_gate_scalars(GateArgs a) {
+  const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (g >= a.B * a.L) return;
+  float sg, pt;
+  gate_of_token<Half>(a, g, &sg, &pt);
+  a.sigma[g] = sg;
+  // pt is a count of tables (1 .. T): the division becomes a product with 1 / pt (exact for powers of two, else
   // within one fp32 ulp of the quotient before the bf16 rounding)
-  const float rpt = __frcp_rn(pt);
-  const float4* src = reinterpret_cast<const float4*>(a.acc + g * a.d);
-  uint2* dst = reinterpret_cast<uint2*>(a.cbuf + g * a.d);
-  for (int c = lane; c < a.d / 4; c += 32) {
-    const float4 x = src[c];
-    dst[c] = make_uint2(umma::pack_bf16x2(__fmul_rn(x.x, rpt), __fmul_rn(x.y, rpt)),
-                        umma::pack_bf16x2(__fmul_rn(x.z, rpt), __fmul_rn(x.w, rpt)));
-  }
+  a.rpt[g] = __frcp_rn(pt);
 }
 
 namespace {
@@ -241,6 +233,7 @@ k_gate_tc(const __grid_constant__ CUtensorMap tmap_c, const __grid_constant__ CU
       const int64_t g = m0 + r;
       const bool row_ok = g < M;
       const float sg = row_ok ? a.sigma[g] : 0.f;
+      const float rp = row_ok ? a.rpt[g] : 0.f;
       float4* orow = reinterpret_cast<float4*>(a.out + g * d + n0);
       if (!mbar_wait(tfull + b, (j >> 1) & 1, a.status)) break;
       tc_fence_after();
@@ -257,10 +250,10 @@ k_gate_tc(const __grid_constant__ CUtensorMap tmap_c, const __grid_constant__ CU
           for (int i = 0; i < 8; ++i) {
             const float4 hv = *reinterpret_cast<const float4*>(hs + ((i ^ (r & 7)) << 4));
             float4 o;
-            o.x = __fadd_rn(hv.x, round_bf16(__fmul_rn(sg, round_bf16(v[4 * i]))));
-            o.y = __fadd_rn(hv.y, round_bf16(__fmul_rn(sg, round_bf16(v[4 * i + 1]))));
-            o.z = __fadd_rn(hv.z, round_bf16(__fmul_rn(sg, round_bf16(v[4 * i + 2]))));
-            o.w = __fadd_rn(hv.w, round_bf16(__fmul_rn(sg, round_bf16(v[4 * i + 3]))));
+            o.x = __fadd_rn(hv.x, round_bf16(__fmul_rn(sg, round_bf16(__fmul_rn(v[4 * i], rp)))));
+            o.y = __fadd_rn(hv.y, round_bf16(__fmul_rn(sg, round_bf16(__fmul_rn(v[4 * i + 1], rp)))));
+            o.z = __fadd_rn(hv.z, round_bf16(__fmul_rn(sg, round_bf16(__fmul_rn(v[4 * i + 2], rp)))));
+            o.w = __fadd_rn(hv.w, round_bf16(__fmul_rn(sg, round_bf16(__fmul_rn(v[4 * i + 3], rp)))));
             orow[ch * 8 + i] = o;
           }
         }
@@ -320,10 +313,10 @@ static int launch_gate_tc_t(const GateArgs& a, const CUtensorMap& mc, const CUte
 
 int launch_gate_tc(const GateArgs& a, int nt, cudaStream_t s) {
   const int64_t M = a.B * a.L;
-  k_gate_prep<<<(unsigned)((M + 7) / 8), 256, 0, s>>>(a);
+  k_gate_scalars<true><<<(unsigned)((M + 255) / 256), 256, 0, s>>>(a);
   if (cudaGetLastError() != cudaSuccess) return ASRN_ERR_CUDA;
   CUtensorMap mc, mw, mh;
-  if (!make_tmap_bf16(&mc, a.cbuf, (uint64_t)a.d, (uint64_t)M, (uint64_t)a.d * 2, 64, 128) ||
+  if (!make_tmap_bf16(&mc, a.acc16, (uint64_t)a.d, (uint64_t)M, (uint64_t)a.d * 2, 64, 128) ||
       !make_tmap_bf16(&mw, a.wov, (uint64_t)a.d, (uint64_t)a.d, (uint64_t)a.d * 2, 64, (uint32_t)nt) ||
       !make_tmap_f32_sw128(&mh, a.h, (uint64_t)a.d, (uint64_t)M, (uint64_t)a.d * 4, 32, 128))
     return ASRN_ERR_CUDA;
@@ -337,15 +330,17 @@ int launch_gate_tc(const GateArgs& a, int nt, cudaStream_t s) {
 
 size_t gate_workspace(int64_t M, int d, bool half) {
   if (!half || gate_tc_tile(d) == 0) return 0;
-  return align_up((size_t)M * d * 2) + align_up((size_t)M * 4);
+  return align_up((size_t)M * 8);                 // sigma and 1 / max(1, pt) per token
 }
 
 int launch_gate(const GateArgs& a, bool half, cudaStream_t s) {
   const int64_t M = a.B * a.L;
   if (M == 0) return ASRN_OK;
   const int nt = gate_tc_tile(a.d);
+  if (half && !a.acc16) return ASRN_ERR_ARG;
+  if (!half && !a.acc) return ASRN_ERR_ARG;
   if (half && tensor_cores_enabled() && nt > 0) {
-    if (!a.cbuf || !a.sigma) return ASRN_ERR_WORKSPACE;
+    if (!a.sigma || !a.rpt) return ASRN_ERR_WORKSPACE;
     return launch_gate_tc(a, nt, s);
   }
   dim3 grid((unsigned)((a.d + kGateTN - 1) / kGateTN), (unsigned)((M + kGateTM - 1) / kGateTM));

@@ -96,7 +96,7 @@ struct ScoreArgs {
   const float* log_alfa;
   const float* w_suf;      // (K + 1)
   const float* tasa;       // (T)
-  float* acc;
+  void* acc;               // (B, q_hi - q_lo, d): bf16 in bf16 mode (added to by bf16 reductions), else fp32
   uint8_t* sen_hay;
   float *sen_mx, *sen_pk;
   int* status;             // device status word (bounded waits of the tensor-core path)
@@ -137,8 +137,10 @@ struct GateArgs {
   const float *w_vistos, *u_hawkes, *u_racha, *d_racha;
   float* out;
   int* status;             // device status word
-  __nv_bfloat16* cbuf;     // tensor-core path: (M, d) bf16 GEMM operand bf16(acc / max(1, pt)) (workspace)
-  float* sigma;            // tensor-core path: (M) gate values (workspace)
+  const __nv_bfloat16* acc16;   // whole-sequence bf16 mode: the scoring's bf16 accumulator (acc unused)
+  __nv_bfloat16* cbuf;     // generation step: (B, d) bf16 GEMM operand bf16(acc / max(1, pt)) (precomputed)
+  float* sigma;            // gate values: (M) from k_gate_scalars (tensor-core path) or the generation step
+  float* rpt;              // tensor-core path: (M) 1 / max(1, pt) from k_gate_scalars (workspace)
 };
 
 // Context + sign-hash projection of one new token per sequence (generation step).

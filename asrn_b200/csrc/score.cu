@@ -7,8 +7,9 @@
 //        + (gamma_tau / C) * float(B_k - B_q)                      (clock difference in fp64, asrn/estable.py:101-118)
 // in exactly that order of fp32 additions (bf16 rounding of the two dot-product terms under autocast), exact-mask
 // softmax over the candidates (asrn/estable.py:121-138), and the copy of the next token's value: the kernel adds
-// att * Ea[k + 1] into acc[b, t_q] (the table sum of _DesordenarSumar, asrn/nucleo.py:116-133) with vector fp32
-// reductions in L2; the gate applies W_o W_v to it. Per-table gate signals (hay, max, peak) go to (B, L, T).
+// att * Ea[k + 1] into acc[b, t_q] (the table sum of _DesordenarSumar, asrn/nucleo.py:116-133) with vector
+// reductions in L2 (fp32, or bf16 into the bf16 accumulator of autocast mode); the gate applies W_o W_v to it.
+// Per-table gate signals (hay, max, peak) go to (B, L, T).
 //
 // Blocks run row-major over (b, tau) so every table of a sequence is scored together and the sequence's
 // accumulator stays resident in L2 while its T tables add into it.
@@ -179,7 +180,8 @@ __global__ void __launch_bounds__(256) k_score_simt(ScoreArgs a) {
         a.sen_pk[gq * a.T + tau] = peak;
       }
       const float w = Half ? round_bf16(att) : att;
-      float* dst = a.acc + gq * d;
+      float* dst = reinterpret_cast<float*>(a.acc) + gq * d;                       // fp32 accumulator
+      __nv_bfloat16* dst16 = reinterpret_cast<__nv_bfloat16*>(a.acc) + gq * d;    // bf16 accumulator
       if (Vec) {
         const int nch = d >> 2;
         float4 o[kMaxChunks];
@@ -205,7 +207,10 @@ __global__ void __launch_bounds__(256) k_score_simt(ScoreArgs a) {
 #pragma unroll
         for (int i = 0; i < kMaxChunks; ++i) {
           const int c4 = lane + 32 * i;
-          if (c4 < nch) red_add_v4(dst + 4 * c4, o[i].x, o[i].y, o[i].z, o[i].w);
+          if (c4 < nch) {
+            if (Half) red_add_bf16x4(dst16 + 4 * c4, o[i].x, o[i].y, o[i].z, o[i].w);
+            else red_add_v4(dst + 4 * c4, o[i].x, o[i].y, o[i].z, o[i].w);
+          }
         }
       } else {
         for (int c = lane; c < d; c += 32) {
@@ -215,7 +220,8 @@ __global__ void __launch_bounds__(256) k_score_simt(ScoreArgs a) {
             const int kp = __shfl_sync(0xffffffffu, kpos, j);
             if (kp + 1 < a.Lf) o = fmaf(wj, A::load(Ea + (b * a.Lf + kp + 1) * (int64_t)d + c), o);
           }
-          red_add_f32(dst + c, o);
+          if (Half) red_add_bf16(dst16 + c, o);
+          else red_add_f32(dst + c, o);
         }
       }
     }

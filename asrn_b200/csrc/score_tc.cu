@@ -4,21 +4,24 @@
 //   S = phi_q . phi_k and Qc . Kc (32 x 64 each) on mma.sync (fp32 accumulate), then the reference's rounding chain,
 //   suffix weight, log_alfa_k and the fp64 time difference, the exact-mask softmax per query, and
 //   out^T (d_part x 32) = V^T (d_part x 64) . att^T (64 x 32) on tcgen05 (M = 128 rows of d per MMA, N = the 32
-//   queries, K = the 64 window keys; the accumulators in TMEM), added into acc with vector L2 reductions.
+//   queries, K = the 64 window keys; the accumulators in TMEM), added into the bf16 accumulator acc by bf16 reductions
+//   in L2.
 // A value row Ea[pos + 1] is gathered only for slots some query can use (the next sorted slot is in the same bucket);
-// other rows keep earlier finite contents (the ring is zeroed when the block starts) and meet zero weights.
+// other rows keep finite contents (zeros) and meet zero weights.
 //
-// One block of 16 warps per (row, span of 512 slots), two warp groups working on consecutive sub-tiles at once:
+// One block of 20 warps per (row, span of 512-2048 slots), three warp groups working on consecutive sub-tiles at once:
 // in iteration i group A (warps 0-7) scores sub-tile i + 1 and takes its softmax, while group B (warps 8-15) has the
-// value products of sub-tile i computed by the tensor cores (lane 0 of warp m issues M-tile m) and reduces them into acc. The
-// weights pass from A to B through a double buffer in the MMA's K-major swizzled layout; one block barrier per
-// iteration. Loads run ahead of use, issued by every warp after one named barrier: the sorted entries of sub-tile
-// i + 3 and the per-position scalars of i + 2 by cp.async, the phi / Qc / Kc rows of i + 2 by tensor-map row gathers
-// (four rows per instruction) into a 4-sub-tile feature ring, the used value rows of i + 1 by 16-byte cp.async into a
-// 3-sub-tile value ring kept in the MMA's MN-major 128-byte-swizzled layout (one 12 KB region per 64 columns of d).
-// The TMEM epilogue transposes 4 x 4 blocks across lanes so that each 16-byte reduction covers four consecutive
-// columns of one query row (a warp's reduction covers four rows x 128 bytes). d is split over blocks only when
-// d > 768 (d_part a multiple of 128).
+// value products of sub-tile i computed by the tensor cores (lane 0 of warp m issues M-tile m) and reduces them into
+// acc, and the load group (warps 16-19) issues the copies: the sorted entries of sub-tile i + 3 and the per-position
+// scalars of i + 2 by cp.async, the phi / Qc / Kc rows of i + 2 by tensor-map row gathers (four rows per instruction)
+// into a 4-sub-tile feature ring, the used value rows of i + 1 by 16-byte cp.async into a 3-sub-tile value ring kept
+// in the MMA's MN-major 128-byte-swizzled layout (one 12 KB region per 64 columns of d). The weights pass from A to B
+// through a double buffer in the MMA's K-major swizzled layout; one block barrier per iteration.
+// The value epilogue stages each warp's 32 rows of d x 16 queries in shared memory and reads them back transposed, so
+// that each lane adds 8 consecutive values of one query row with one 16-byte bf16 reduction (no lane shuffles). The
+// table sum thus moves 2 bytes per value into L2 instead of 4: L2 sustains about 6 TB/s of reductions on B200, so the
+// fp32 sum of 8 tables x d values per token would bound the kernel at about 1.1 ms for 32 x 8192 tokens at d = 768.
+// d is split over blocks only when d > 768 (d_part a multiple of 128).
 #include <cuda.h>
 
 #include "common.cuh"
@@ -159,6 +162,19 @@ __device__ __forceinline__ void cp_async8(void* dst, const void* src) {
 // the surrounding shared-memory loads may move across it).
 __device__ __forceinline__ void red_add_v4_nc(float* addr, float a, float b, float c, float d) {
   asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b), "f"(c), "f"(d));
+}
+// 16 consecutive fp32 columns of this thread's TMEM lane
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
@@ -464,12 +480,18 @@ __device__ __forceinline__ void tc_scores(const ScoreArgs& a, const TcSmem& S, c
   umma::fence_proxy_async();       // the weights are read by the tensor cores (async proxy) after the block barrier
 }
 
-// Group B: out^T = V^T . att^T for sub-tile t on tcgen05, reduced into acc. Lane 0 of warp mm issues M-tile mm
-// (rows 128 mm .. + 127 of d_part: two 64-column regions of the value ring, MN-major, 12 KB apart), K-step ks (window
-// keys 16 ks .. + 15: two 8-key groups of the ring, 1024 B apart), N = the 32 queries (att rows, K-major); D in TMEM
-// columns 32 mm .. + 31. Then warp w reads TMEM lanes 32 (w % 4) .. + 31 (32 rows of d) for M-tiles (w - 8) / 4,
-// + 2, + 4: each lane holds one row of d for the 32 queries; 4 x 4 transposes within lane quads give each lane four
-// consecutive rows of d for one query, reduced into acc with one 16-byte reduction.
+// Group B: out^T = V^T . att^T for sub-tile t on tcgen05, reduced into the bf16 accumulator. Lane 0 of warp mm issues
+// M-tile mm (rows 128 mm .. + 127 of d_part: two 64-column regions of the value ring, MN-major, 12 KB apart), K-step
+// ks (window keys 16 ks .. + 15: two 8-key groups of the ring, 1024 B apart), N = the 32 queries (att rows, K-major);
+// D in TMEM columns 32 mm .. + 31. Then warp w reads TMEM lanes 32 (w % 4) .. + 31 (32 rows of d) for M-tiles
+// (w - 8) / 4, + 2, + 4, 16 query columns at a time: each lane holds one row of d for 16 queries and stores them into
+// a 2 KB staging piece laid out [query][32 rows of d], the 16-byte granules of a query's row rotated by the query
+// (granule g of query q at (g + q) mod 8) so that both the stores (one query row per instruction) and the reads
+// (eight queries x four granule pairs per instruction) are free of bank conflicts. Each lane then reads 8 consecutive
+// rows of d of one query and adds them, rounded to bf16, with one 16-byte bf16 reduction: a warp instruction covers
+// 8 queries x 64 bytes. The pieces sit in the value ring's rows of sub-tile t - 1, which no MMA reads once sub-tile
+// t's products are done; they are zeroed afterwards, since ring rows that are not reloaded must keep finite bf16
+// contents (they meet zero weights).
 __device__ __forceinline__ void tc_values(const ScoreArgs& a, const TcSmem& S, const TcBlock& k, int t, int w,
                                           uint32_t tmem) {
   const int lane = threadIdx.x & 31;
@@ -487,34 +509,51 @@ __device__ __forceinline__ void tc_values(const ScoreArgs& a, const TcSmem& S, c
     }
     umma::mma_commit(S.pvbar);
   }
-  // this lane's queries 4c + (lane & 3) after the transposes: their acc offsets, read before the waits
-  const int qd = lane & 3, g = lane >> 2;
+  // this lane's reductions: query rq(hq, j) = 16 hq + 8 j + lane / 4, rows of d 8 (lane % 4) .. + 7 of the warp's 32
   const int64_t* qoff_s = S.qoff + (t & 1) * kQ;
-  int64_t qoff[kQ / 4];
+  const int kq = lane >> 2, kg = lane & 3;
+  int64_t qo[2][2];
 #pragma unroll
-  for (int c = 0; c < kQ / 4; ++c) qoff[c] = qoff_s[4 * c + qd];
+  for (int hq = 0; hq < 2; ++hq)
+#pragma unroll
+    for (int j = 0; j < 2; ++j) qo[hq][j] = qoff_s[16 * hq + 8 * j + kq];
+  // this warp's staging piece: 2 KB of the ring rows of sub-tile t - 1 (32 rows x 128 B per 64-column region; warp w
+  // takes half w % 2 of region w / 2, so the 4 nM pieces of the active warps fit in the 2 nM regions)
+  float* piece = reinterpret_cast<float*>(S.v + (w >> 1) * kVRegion + vrow(lb) * 128 + (w & 1) * 2048);
   __syncwarp();
   umma::mbar_wait(S.pvbar, (uint32_t)(t & 1), a.status);
   umma::tc_fence_after();
   const int q4 = w & 3;
+  __nv_bfloat16* acc16 = reinterpret_cast<__nv_bfloat16*>(a.acc);
+  bool staged = false;
   for (int mm = w >> 2; mm < nM; mm += 2) {
-    float v[32];
-    umma::tmem_ld32(tmem + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(mm * kQ), v);
-    const int dcol = mm * 128 + q4 * 32 + 4 * g;   // first of this lane's four d rows after the transpose
+    __nv_bfloat16* dst_base = acc16 + mm * 128 + q4 * 32 + 8 * kg;
 #pragma unroll
-    for (int c = 0; c < kQ / 4; ++c) {
-      float x0 = v[4 * c], x1 = v[4 * c + 1], x2 = v[4 * c + 2], x3 = v[4 * c + 3];
-      // across lane bit 1, then bit 0: lane qd ends with query 4c + qd of the quad's four d rows
-      float p0 = (qd & 2) ? x0 : x2, p1 = (qd & 2) ? x1 : x3;
-      float r0 = __shfl_xor_sync(0xffffffffu, p0, 2), r1 = __shfl_xor_sync(0xffffffffu, p1, 2);
-      if (qd & 2) { x0 = r0; x1 = r1; } else { x2 = r0; x3 = r1; }
-      p0 = (qd & 1) ? x0 : x1;
-      p1 = (qd & 1) ? x2 : x3;
-      r0 = __shfl_xor_sync(0xffffffffu, p0, 1);
-      r1 = __shfl_xor_sync(0xffffffffu, p1, 1);
-      if (qd & 1) { x0 = r0; x2 = r1; } else { x1 = r0; x3 = r1; }
-      if (qoff[c] >= 0) red_add_v4_nc(a.acc + qoff[c] + dcol, x0, x1, x2, x3);
+    for (int hq = 0; hq < 2; ++hq) {
+      float v[16];
+      tmem_ld16(tmem + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(mm * kQ + hq * 16), v);
+      __syncwarp();                             // the previous reads of the piece are done
+#pragma unroll
+      for (int c = 0; c < 16; ++c) piece[c * 32 + ((((lane >> 2) + c) & 7) << 2) + (lane & 3)] = v[c];
+      __syncwarp();
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int q = 8 * j + kq;               // query within the half
+        const float4 lo = *reinterpret_cast<const float4*>(piece + q * 32 + (((2 * kg + q) & 7) << 2));
+        const float4 hi = *reinterpret_cast<const float4*>(piece + q * 32 + (((2 * kg + 1 + q) & 7) << 2));
+        if (qo[hq][j] >= 0)
+          red_add_bf16x8(dst_base + qo[hq][j], pack2_bf16(lo.x, lo.y), pack2_bf16(lo.z, lo.w),
+                         pack2_bf16(hi.x, hi.y), pack2_bf16(hi.z, hi.w));
+      }
+      staged = true;
     }
+  }
+  if (staged) {
+    __syncwarp();
+    uint4* z = reinterpret_cast<uint4*>(piece);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) z[lane + 32 * i] = make_uint4(0, 0, 0, 0);
+    umma::fence_proxy_async();                  // the zeros precede later tensor-core reads of these rows
   }
   umma::tc_fence_before();
 }

@@ -199,7 +199,7 @@ def _phase2(layer, loc, full, tails_prev, rep, h, c0, c1, half, status=None):
     d = layer.d
     w, _keep, prep = layer.prepared(dev, half)
     cfg = _lib.make_config(layer, B, Lv, half)
-    acc = torch.zeros(B, Lc, d, dtype=torch.float32, device=dev)
+    acc = torch.zeros(B, Lc, d, dtype=torch.bfloat16 if half else torch.float32, device=dev)
     hay = torch.empty(B, Lc, T, dtype=torch.uint8, device=dev)
     mx = torch.empty(B, Lc, T, dtype=torch.float32, device=dev)
     pk = torch.empty(B, Lc, T, dtype=torch.float32, device=dev)

@@ -119,7 +119,7 @@ def score(layer, orden, ids_o, phi, Qc, Kc, sig, Bt, log_alfa, Ea, half=False):
     orden, ids_o = orden.to(torch.int32).contiguous(), ids_o.contiguous()
     sig, la = sig.float().contiguous(), log_alfa.float().contiguous()
     Bt = Bt.to(torch.float64).contiguous()
-    acc = torch.zeros(B, L, d, dtype=torch.float32, device=dev)
+    acc = torch.zeros(B, L, d, dtype=act, device=dev)            # the compute type: bf16 accumulator under autocast
     hay = torch.empty(B, L, T, dtype=torch.uint8, device=dev)
     mx = torch.empty(B, L, T, dtype=torch.float32, device=dev)
     pk = torch.empty(B, L, T, dtype=torch.float32, device=dev)
@@ -172,6 +172,7 @@ def gate(layer, h, glogit, acc, hay, mx, pk, vistos, hawkes, racha, half=False):
     cfg = _cfg(layer, B, L, half)
     h = h.float().contiguous()
     out = torch.empty_like(h)
+    acc = acc.to(_ACT[half])                                    # the compute type (as score leaves it)
     args = [x.contiguous() for x in (glogit, acc, hay, mx, pk, vistos, hawkes, racha)]
     nbytes = _L().asrn_gate_workspace_bytes(ctypes_ref(cfg))
     ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=dev)

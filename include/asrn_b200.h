@@ -147,12 +147,15 @@ int asrn_bucket_sort(int64_t rows, int64_t L, int32_t nb, const uint16_t* ids_ro
                      uint16_t* ids_o, void* workspace, size_t workspace_bytes, void* stream);
 
 /* Candidate scoring of every (row, sorted slot) against its <= C bucket mates, exact-mask softmax, copy of the next
- * token's value row: acc (B, L, d) float32 += sum over tables and candidates of att * Ea[k + 1] (acc must be zeroed
- * by the caller; apply W_v to acc to get the reference's `salida`). Per-table gate signals in text order, (B, L, T):
- * hay (uint8), mx (float32, -1e9 when no candidate), pk (float32). */
+ * token's value row: acc (B, L, d) += sum over tables and candidates of att * Ea[k + 1] (acc must be zeroed by the
+ * caller; apply W_v to acc to get the reference's `salida`). acc is in the compute type: under bfloat16 autocast a
+ * bf16 accumulator that the tables add into with bf16 reductions in L2 (the reference's per-table outputs are bf16 as
+ * well; the order of the additions is not fixed, so results vary run to run by a few bf16 roundings: about 5e-3 of
+ * max|h' - h| at the benchmark shapes), fp32 otherwise (within fp32 rounding). Per-table gate signals in text order,
+ * (B, L, T): hay (uint8), mx (float32, -1e9 when no candidate), pk (float32). */
 int asrn_score(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared,
                const int32_t* orden, const uint16_t* ids_o, const void* phi, const void* Qc, const void* Kc,
-               const float* sig, const double* Bt, const float* log_alfa, const void* Ea, float* acc,
+               const float* sig, const double* Bt, const float* log_alfa, const void* Ea, void* acc,
                uint8_t* sen_hay, float* sen_mx, float* sen_pk, void* stream);
 
 /* ---- local blocks of the model, one generation step (B rows; half: bf16 compute type, else fp32) ---------------
@@ -202,7 +205,7 @@ int asrn_shard_rows(int64_t rows, int64_t L, int32_t C, int64_t q_lo, int64_t q_
 int asrn_score_shard(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared, int64_t L_feat,
                      int64_t q_lo, int64_t q_hi, const int32_t* orden, const uint16_t* ids_o, const void* phi,
                      const void* Qc, const void* Kc, const float* sig, const double* Bt, const float* log_alfa,
-                     const void* Ea, const int64_t* row_len, float* acc, uint8_t* sen_hay, float* sen_mx,
+                     const void* Ea, const int64_t* row_len, void* acc, uint8_t* sen_hay, float* sen_mx,
                      float* sen_pk, void* stream);
 
 /* n-gram memory of one shard's chunk [c0, c0 + cfg->L) of sequences of L_feat positions (asrn/estable.py:304-321
@@ -259,11 +262,12 @@ int asrn_repetition(const asrn_layer_config* cfg, const asrn_layer_weights* w, c
                     float* hawkes, float* racha, double* keys, int32_t* orden_ng, uint8_t* repetido,
                     void* workspace, size_t workspace_bytes, void* stream);
 
-/* Gate and output projection: h_out = h + sigmoid(logit) * (W_o W_v)(acc / max(1, tables with candidates)).
- * The bf16 tensor-core path needs a workspace of asrn_gate_workspace_bytes(cfg) (0 when it is not used). */
+/* Gate and output projection: h_out = h + sigmoid(logit) * (W_o W_v)(acc / max(1, tables with candidates)), acc in
+ * the compute type (as asrn_score leaves it). The bf16 tensor-core path needs a workspace of
+ * asrn_gate_workspace_bytes(cfg) (the per-token gate values; 0 when it is not used). */
 size_t asrn_gate_workspace_bytes(const asrn_layer_config* cfg);
 int asrn_gate(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared, const float* h,
-              const float* glogit, const float* acc, const uint8_t* sen_hay, const float* sen_mx,
+              const float* glogit, const void* acc, const uint8_t* sen_hay, const float* sen_mx,
               const float* sen_pk, const uint8_t* vistos, const float* hawkes, const float* racha, float* h_out,
               void* workspace, size_t workspace_bytes, void* stream);
 
