@@ -152,6 +152,9 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src, bool vali
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(su32(dst)), "l"(src), "r"(valid ? 16 : 0)
                : "memory");
 }
+__device__ __forceinline__ void cp_async16_s(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
 __device__ __forceinline__ void cp_async4(void* dst, const void* src) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(su32(dst)), "l"(src) : "memory");
 }
@@ -177,6 +180,12 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// Round two fp32 values to bf16 (nearest even) in one conversion, back as fp32.
+__device__ __forceinline__ void round2_bf16(float& a, float& b) {
+  const uint32_t u = pack2_bf16(a, b);           // a in the low half, b in the high half
+  a = __uint_as_float(u << 16);
+  b = __uint_as_float(u & 0xFFFF0000u);
+}
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 __device__ __forceinline__ void bar_group_a() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
@@ -294,16 +303,24 @@ __device__ __forceinline__ void tc_stage2_features(const ScoreArgs& a, const TcS
 // gathers per 4 rows, which makes the tensor-map unit the bottleneck of the loop.)
 __device__ __forceinline__ void tc_stage2_values(const ScoreArgs& a, const TcSmem& S, const TcBlock& k, int t, int pt) {
   const int lane = pt & 31, wb = pt >> 5;
-  const int nch = k.dpart / 8;                 // 16-byte chunks per row
+  const int nch = k.dpart / 8;                 // 16-byte chunks per row (<= 96: chunks lane, lane + 32, lane + 64)
+  // chunk c = lane + 32 u of a row sits in region c / 8 = lane / 8 + 4 u at chunk (c % 8) ^ (row % 8) = (lane % 8) ^ ...
+  const uint32_t v_lane = su32(S.v) + (uint32_t)(lane >> 3) * kVRegion;
+  const uint32_t x_lane = (uint32_t)(lane & 7) << 4;
+  const bool c0 = lane < nch, c1 = lane + 32 < nch, c2 = lane + 64 < nch;
+  // the value of position p is row p + 1 of Ea
+  const __nv_bfloat16* ea = reinterpret_cast<const __nv_bfloat16*>(a.Ea) + (k.b * a.Lf + 1) * (int64_t)a.d + k.dp0 +
+                            lane * 8;
   for (int i = wb; i < kQ; i += kLoadWarps) {
     const int li = (t + 1) * kQ + i;
     const int fr = frow(li), vr = vrow(li);
     if (!S.used[fr]) continue;
-    const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(a.Ea) + (k.b * a.Lf + S.pos[fr] + 1) *
-                               (int64_t)a.d + k.dp0;
-    uint8_t* row = S.v + (vr >> 3) * 1024 + (vr & 7) * 128;
-    for (int c = lane; c < nch; c += 32)
-      cp_async16(row + (c >> 3) * kVRegion + (((c & 7) ^ (vr & 7)) << 4), src + c * 8, true);
+    const __nv_bfloat16* src = ea + (int64_t)S.pos[fr] * a.d;
+    const uint32_t x = (uint32_t)(vr & 7);
+    const uint32_t dst = v_lane + (uint32_t)(vr >> 3) * 1024 + (x << 7) + (x_lane ^ (x << 4));
+    if (c0) cp_async16_s(dst, src);
+    if (c1) cp_async16_s(dst + 4 * kVRegion, src + 256);
+    if (c2) cp_async16_s(dst + 8 * kVRegion, src + 512);
   }
 }
 
@@ -398,34 +415,61 @@ __device__ __forceinline__ void tc_scores(const ScoreArgs& a, const TcSmem& S, c
     k_bt[u] = S.bt[rk];
     k_la[u] = S.la[rk];
   }
+  // per query row u: inside the row (slot < L) and its score-tile row address; per key: slot >= 0
+  const int64_t rem = a.L - q0;
+  const int qlim = rem < kQ ? (int)rem : kQ;
+  const bool kv[2] = {q0 - kQ + kj0 >= 0, q0 - kQ + kj0 + 1 >= 0};
+  const int wlo = kQ - C;                        // window: key kj is a candidate of query qi iff kj - qi in [32 - C, 32)
 #pragma unroll
   for (int mt = 0; mt < 2; ++mt) {
+    if (!band[mt]) {                             // the whole 16 x 8 tile is outside the window band (warp-uniform)
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int uq = 2 * mt + (e >> 1), uk = e & 1;
-      const int qi = g4 + 8 * uq;
-      const int kj = kj0 + uk;
-      const int64_t sq = q0 + qi, sk = q0 - kQ + kj;
-      // every element is computed (no divergent branch) and masked at the end: outside the band, the row or the
-      // bucket it is -inf
-      const bool ok = band[mt] && kj < qi + 32 && kj >= qi + 32 - C && sq < a.L && sk >= 0 && k_id[uk] == q_id[uq];
-      const float s1 = round_bf16(__fmul_rn(round_bf16(cphi[mt][e]), k.inv_temp));
-      const float s2 = round_bf16(__fmul_rn(round_bf16(cqk[mt][e]), a.esc_c));
-      float t1 = round_bf16(__fadd_rn(s1, s2));
-      const float4 qa = q_pf[uq][0], ka = k_pf[uk][0];
-      uint32_t eq = (qa.x == ka.x ? 1u : 0u) | (qa.y == ka.y ? 2u : 0u) | (qa.z == ka.z ? 4u : 0u) |
-                    (qa.w == ka.w ? 8u : 0u);
-      if (!kSuf4) {                             // entries 4 .. 7 are NaN (never equal) when K <= 4
-        const float4 qb = q_pf[uq][1], kb = k_pf[uk][1];
-        eq |= (qb.x == kb.x ? 16u : 0u) | (qb.y == kb.y ? 32u : 0u) | (qb.z == kb.z ? 64u : 0u) |
-              (qb.w == kb.w ? 128u : 0u);
+      for (int e = 0; e < 4; ++e) {
+        const int qi = g4 + 8 * (2 * mt + (e >> 1)), kj = kj0 + (e & 1);
+        S.sc[qi * 64 + (kj ^ sc_swz(qi))] = -INFINITY;
       }
-      const int ln = __ffs(~eq) - 1;            // leading equal entries (entries past K are NaN: never equal)
-      t1 = __fadd_rn(t1, S.wsuf[ln]);
-      t1 = __fadd_rn(t1, k_la[uk]);
-      const float dt = __double2float_rn(k_bt[uk] - q_bt[uq]);
-      const float val = ok ? __fadd_rn(t1, __fmul_rn(dt, k.tasa)) : -INFINITY;
-      S.sc[qi * 64 + (kj ^ sc_swz(qi))] = val;
+      continue;
+    }
+#pragma unroll
+    for (int hr = 0; hr < 2; ++hr) {             // elements 2 hr, 2 hr + 1: query row uq, keys kj0, kj0 + 1
+      const int uq = 2 * mt + hr;
+      const int qi = g4 + 8 * uq;
+      // the reference's rounding chain, two elements per conversion: s1 = bf16(bf16(phi.phi) / T),
+      // s2 = bf16(bf16(Qc.Kc) * cf^-1/2), t1 = bf16(s1 + s2)
+      float s1a = cphi[mt][2 * hr], s1b = cphi[mt][2 * hr + 1], s2a = cqk[mt][2 * hr], s2b = cqk[mt][2 * hr + 1];
+      round2_bf16(s1a, s1b);
+      round2_bf16(s2a, s2b);
+      s1a = __fmul_rn(s1a, k.inv_temp);
+      s1b = __fmul_rn(s1b, k.inv_temp);
+      s2a = __fmul_rn(s2a, a.esc_c);
+      s2b = __fmul_rn(s2b, a.esc_c);
+      round2_bf16(s1a, s1b);
+      round2_bf16(s2a, s2b);
+      float t1[2] = {__fadd_rn(s1a, s2a), __fadd_rn(s1b, s2b)};
+      round2_bf16(t1[0], t1[1]);
+      const bool qv = qi < qlim;
+      const int row = qi * 64, swz = sc_swz(qi);
+#pragma unroll
+      for (int uk = 0; uk < 2; ++uk) {
+        const int kj = kj0 + uk;
+        const bool ok = qv && kv[uk] && (unsigned)(kj - qi - wlo) < (unsigned)C && k_id[uk] == q_id[uq];
+        const float4 qa = q_pf[uq][0], ka = k_pf[uk][0];
+        int ln;
+        if (kSuf4) {                             // entries past K are NaN (never equal)
+          ln = qa.x == ka.x ? (qa.y == ka.y ? (qa.z == ka.z ? (qa.w == ka.w ? 4 : 3) : 2) : 1) : 0;
+        } else {
+          const float4 qb = q_pf[uq][1], kb = k_pf[uk][1];
+          const uint32_t eq = (qa.x == ka.x ? 1u : 0u) | (qa.y == ka.y ? 2u : 0u) | (qa.z == ka.z ? 4u : 0u) |
+                              (qa.w == ka.w ? 8u : 0u) | (qb.x == kb.x ? 16u : 0u) | (qb.y == kb.y ? 32u : 0u) |
+                              (qb.z == kb.z ? 64u : 0u) | (qb.w == kb.w ? 128u : 0u);
+          ln = __ffs(~eq) - 1;                   // leading equal entries
+        }
+        float v = __fadd_rn(t1[uk], S.wsuf[ln]);
+        v = __fadd_rn(v, k_la[uk]);
+        const float dt = __double2float_rn(k_bt[uk] - q_bt[uq]);
+        v = __fadd_rn(v, __fmul_rn(dt, k.tasa));
+        S.sc[row + (kj ^ swz)] = ok ? v : -INFINITY;
+      }
     }
   }
   bar_group_a();
@@ -485,8 +529,8 @@ __device__ __forceinline__ void tc_scores(const ScoreArgs& a, const TcSmem& S, c
 // ks (window keys 16 ks .. + 15: two 8-key groups of the ring, 1024 B apart), N = the 32 queries (att rows, K-major);
 // D in TMEM columns 32 mm .. + 31. Then warp w reads TMEM lanes 32 (w % 4) .. + 31 (32 rows of d) for M-tiles
 // (w - 8) / 4, + 2, + 4, 16 query columns at a time: each lane holds one row of d for 16 queries and stores them into
-// a 2 KB staging piece laid out [query][32 rows of d], the 16-byte granules of a query's row rotated by the query
-// (granule g of query q at (g + q) mod 8) so that both the stores (one query row per instruction) and the reads
+// a 2 KB staging piece laid out [query][32 rows of d], the 16-byte granules of a query's row permuted by the query
+// (granule g of query q at g ^ (q mod 8)) so that both the stores (one query row per instruction) and the reads
 // (eight queries x four granule pairs per instruction) are free of bank conflicts. Each lane then reads 8 consecutive
 // rows of d of one query and adds them, rounded to bf16, with one 16-byte bf16 reduction: a warp instruction covers
 // 8 queries x 64 bytes. The pieces sit in the value ring's rows of sub-tile t - 1, which no MMA reads once sub-tile
@@ -510,8 +554,10 @@ __device__ __forceinline__ void tc_values(const ScoreArgs& a, const TcSmem& S, c
     umma::mma_commit(S.pvbar);
   }
   // this lane's reductions: query rq(hq, j) = 16 hq + 8 j + lane / 4, rows of d 8 (lane % 4) .. + 7 of the warp's 32
+  // (granules 2 (lane % 4) and + 1 of the query's staged row, at g ^ (lane / 4))
   const int64_t* qoff_s = S.qoff + (t & 1) * kQ;
   const int kq = lane >> 2, kg = lane & 3;
+  const int rd0 = kq * 32 + (((2 * kg) ^ kq) << 2), rd1 = kq * 32 + (((2 * kg + 1) ^ kq) << 2);
   int64_t qo[2][2];
 #pragma unroll
   for (int hq = 0; hq < 2; ++hq)
@@ -534,13 +580,12 @@ __device__ __forceinline__ void tc_values(const ScoreArgs& a, const TcSmem& S, c
       tmem_ld16(tmem + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(mm * kQ + hq * 16), v);
       __syncwarp();                             // the previous reads of the piece are done
 #pragma unroll
-      for (int c = 0; c < 16; ++c) piece[c * 32 + ((((lane >> 2) + c) & 7) << 2) + (lane & 3)] = v[c];
+      for (int c = 0; c < 16; ++c) piece[c * 32 + (lane ^ ((c & 7) << 2))] = v[c];
       __syncwarp();
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
-        const int q = 8 * j + kq;               // query within the half
-        const float4 lo = *reinterpret_cast<const float4*>(piece + q * 32 + (((2 * kg + q) & 7) << 2));
-        const float4 hi = *reinterpret_cast<const float4*>(piece + q * 32 + (((2 * kg + 1 + q) & 7) << 2));
+        const float4 lo = *reinterpret_cast<const float4*>(piece + 256 * j + rd0);
+        const float4 hi = *reinterpret_cast<const float4*>(piece + 256 * j + rd1);
         if (qo[hq][j] >= 0)
           red_add_bf16x8(dst_base + qo[hq][j], pack2_bf16(lo.x, lo.y), pack2_bf16(lo.z, lo.w),
                          pack2_bf16(hi.x, hi.y), pack2_bf16(hi.z, hi.w));
