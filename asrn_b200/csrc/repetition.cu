@@ -6,9 +6,10 @@
 //   a_i = repetido_i * exp(-kappa_n * float(max(0, B_i - B_{i-1}))),  lambda_i = a_i (lambda_{i-1} + alfa_{i-1})
 //   hawkes / vistos scattered back to text order; streak S_t = r_t exp(-kappa_r beta_t) S_{t-1} + r_t with
 //   r_t = vistos of the longest order.
-// Rows of at most 16384 positions: one block per (b, n) row sorts (key, position) pairs in shared memory with a
-// bitonic network, then runs a block-wide scan of affine maps over the sorted row.
-// Longer rows (workspace from repetition_workspace): tiles of 16384 are sorted the same way and written out, runs are
+// Rows of at most 8192 positions: one block per (b, n) row sorts (key, position) pairs in shared memory with an LSD
+// radix sort on the 64-bit order-preserving key (8-bit digits, per-warp histograms, __match_any_sync ranking; a pass
+// whose digit is the same for every key is skipped), then runs a block-wide scan of affine maps over the sorted row.
+// Longer rows (workspace from repetition_workspace): tiles are sorted with a bitonic network and written out, runs are
 // merged pairwise (merge path, log2(tiles) passes), then a tiled scan writes each tile's local inclusive maps and its
 // aggregate, and a last pass composes the aggregates of the earlier tiles into each element and scatters to text
 // order. Keys are unique as (key, position) pairs, so every correct sort gives the stable argsort of the reference.
@@ -17,7 +18,79 @@
 
 namespace asrn {
 
-constexpr int kRepMaxL = 16384;   // rows sorted in one block (16384 x 12 B of shared memory)
+constexpr int kRepMaxL = 16384;   // tile of the long-row path (16384 x 12 B of shared memory)
+constexpr int kRepRowMaxL = 8192; // rows radix-sorted in one block: 2 x 8192 x 12 B of key / position buffers
+constexpr int kRxThreads = 1024, kRxWarps = kRxThreads / 32;
+constexpr size_t kRxTabBytes = (size_t)kRxWarps * 256 * 2;   // (digit, warp) counts / offsets, 16-bit
+
+// One stable counting-sort pass of n_pad (key, position) pairs by the digit (key >> shift) & 255, src -> dst, with
+// the rank of each key among equal digits of its 32-key group from __match_any_sync. Returns false (and moves
+// nothing) when every key has the same digit: the order is already sorted by it.
+__device__ __forceinline__ bool radix_pass64(const uint64_t* sk, const uint32_t* sp, uint64_t* dk, uint32_t* dp,
+                                             uint16_t* tab, int n_pad, int shift) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int seg = n_pad / kRxWarps;                   // a multiple of 32
+  const uint32_t lt = (1u << lane) - 1;
+  const uint32_t d0 = (uint32_t)(sk[0] >> shift) & 255u;
+  for (int i = threadIdx.x; i < kRxWarps * 256; i += kRxThreads) tab[i] = 0;
+  __syncthreads();
+  int differs = 0;
+  for (int j = 0; j < seg; j += 32) {
+    const uint32_t d = (uint32_t)(sk[w * seg + j + lane] >> shift) & 255u;
+    differs |= d != d0;
+    const uint32_t peers = __match_any_sync(0xffffffffu, d);
+    if ((peers & lt) == 0) tab[d * kRxWarps + w] += (uint16_t)__popc(peers);
+  }
+  if (!__syncthreads_or(differs)) return false;
+  {   // exclusive scan of tab in (digit, warp) order, 8 consecutive entries per thread
+    __shared__ int wsum[kRxWarps];
+    const int e0 = threadIdx.x * 8;
+    int local = 0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) local += tab[e0 + k];
+    int incl = local;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    if (lane == 31) wsum[w] = incl;
+    __syncthreads();
+    if (w == 0) {
+      int v = wsum[lane];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += y;
+      }
+      wsum[lane] = v;
+    }
+    __syncthreads();
+    int run = (w > 0 ? wsum[w - 1] : 0) + incl - local;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int c = tab[e0 + k];
+      tab[e0 + k] = (uint16_t)run;
+      run += c;
+    }
+  }
+  __syncthreads();
+  for (int j = 0; j < seg; j += 32) {
+    const int i = w * seg + j + lane;
+    const uint64_t k = sk[i];
+    const uint32_t d = (uint32_t)(k >> shift) & 255u;
+    const uint32_t peers = __match_any_sync(0xffffffffu, d);
+    const int base = tab[d * kRxWarps + w];
+    const int at = base + __popc(peers & lt);
+    dk[at] = k;
+    dp[at] = sp[i];
+    __syncwarp();
+    if ((peers & lt) == 0) tab[d * kRxWarps + w] = (uint16_t)(base + __popc(peers));
+    __syncwarp();
+  }
+  __syncthreads();
+  return true;
+}
 
 __device__ __forceinline__ bool pair_less(uint64_t ka, uint32_t pa, uint64_t kb, uint32_t pb) {
   return ka < kb || (ka == kb && pa < pb);
@@ -64,10 +137,14 @@ __device__ __forceinline__ void block_scan_affine(Affine* v, Affine* warp_agg) {
 }
 
 template <int kItems>
-__global__ void __launch_bounds__(1024) k_ngram_row(RepetitionArgs a, int n2) {
+__global__ void __launch_bounds__(kRxThreads) k_ngram_row(RepetitionArgs a, int n2) {
+  // n2: the row length rounded up to a multiple of 1024 (the sort's padding keys are all ones: they sort last)
   extern __shared__ __align__(16) char smem_raw[];
-  uint64_t* sk = reinterpret_cast<uint64_t*>(smem_raw);
-  uint32_t* sp = reinterpret_cast<uint32_t*>(sk + n2);
+  uint64_t* k0 = reinterpret_cast<uint64_t*>(smem_raw);
+  uint64_t* k1 = k0 + n2;
+  uint32_t* p0 = reinterpret_cast<uint32_t*>(k1 + n2);
+  uint32_t* p1 = p0 + n2;
+  uint16_t* tab = reinterpret_cast<uint16_t*>(p1 + n2);
   __shared__ Affine warp_agg[32];
   const int64_t b = blockIdx.x / a.n;
   const int ni = (int)(blockIdx.x % a.n);
@@ -83,29 +160,23 @@ __global__ void __launch_bounds__(1024) k_ngram_row(RepetitionArgs a, int n2) {
         key = __dadd_rn(key, __dmul_rn(s, a.c[j]));
       }
       if (a.keys) a.keys[(b * L + i) * a.n + ni] = key;
-      sk[i] = sortable_key(key);
-      sp[i] = (uint32_t)i;
+      k0[i] = sortable_key(key);
+      p0[i] = (uint32_t)i;
     } else {
-      sk[i] = 0xFFFFFFFFFFFFFFFFull;
-      sp[i] = 0xFFFFFFFFu;
+      k0[i] = 0xFFFFFFFFFFFFFFFFull;
+      p0[i] = 0xFFFFFFFFu;
     }
   }
   __syncthreads();
-  for (int k = 2; k <= n2; k <<= 1) {
-    for (int j = k >> 1; j > 0; j >>= 1) {
-      for (int i = threadIdx.x; i < n2; i += blockDim.x) {
-        const int ixj = i ^ j;
-        if (ixj > i) {
-          const uint64_t ka = sk[i], kb = sk[ixj];
-          const uint32_t pa = sp[i], pb = sp[ixj];
-          const bool up = (i & k) == 0;
-          if (pair_less(kb, pb, ka, pa) == up) {
-            sk[i] = kb; sk[ixj] = ka;
-            sp[i] = pb; sp[ixj] = pa;
-          }
-        }
-      }
-      __syncthreads();
+  // stable LSD radix sort by key: positions start ascending, so equal keys keep position order
+  uint64_t* sk = k0;
+  uint32_t* sp = p0;
+  for (int shift = 0; shift < 64; shift += 8) {
+    uint64_t* dk = sk == k0 ? k1 : k0;
+    uint32_t* dp = sp == p0 ? p1 : p0;
+    if (radix_pass64(sk, sp, dk, dp, tab, n2, shift)) {
+      sk = dk;
+      sp = dp;
     }
   }
   // affine elements in sorted order; thread owns kItems consecutive slots
@@ -440,7 +511,7 @@ static RepLong rep_long_layout(void* ws, int64_t rows, int64_t L) {
 
 // Rows longer than one block's shared-memory sort take the tiled path (tile sorts, merges, tiled scans); shorter rows
 // are sorted and scanned by one block each (measured as fast as the tiled path at 32 x 4 rows of 8192 positions).
-static bool rep_tiled(int64_t L) { return L > kRepMaxL; }
+static bool rep_tiled(int64_t L) { return L > kRepRowMaxL; }
 
 size_t repetition_workspace(int64_t B, int64_t L, int n) {
   if (!rep_tiled(L)) return 0;
@@ -780,11 +851,10 @@ int launch_repetition(const RepetitionArgs& a, void* ws, size_t ws_bytes, cudaSt
     if (st) return st;
     return launch_racha_ws(a, ws, ws_bytes, s);   // the n-gram passes are done with the workspace
   }
-  int n2 = 1;
-  while (n2 < a.L) n2 <<= 1;
-  const size_t smem = (size_t)n2 * 12;
+  const int n2 = (int)((a.L + kRxThreads - 1) / kRxThreads * kRxThreads);
+  const size_t smem = (size_t)n2 * 24 + kRxTabBytes;
   dim3 grid((unsigned)(a.B * a.n));
-  const int items = (n2 + 1023) / 1024;
+  const int items = n2 / 1024;
   if (items <= 1) {
     cudaFuncSetAttribute(k_ngram_row<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     k_ngram_row<1><<<grid, 1024, smem, s>>>(a, n2);

@@ -112,3 +112,75 @@ def crear_modelo(V, d=64, n_capas=2, largo_cada=2, semilla=None, protecciones=No
 
 
 create_model = crear_modelo
+
+
+# ---- model files (the reference's format: asrn/nucleo.py:2050-2133) --------------------------------------------------
+# A file holds {'config': model.config, 'pesos': state_dict} as torch.save wrote it; the parameter names are the
+# reference's, so files written by the reference's guardar() / entrenar() load here and the other way round.
+
+_NEW_IN_V87 = ('w_reloj', 'b_reloj', 'gamma', 'log_kappa', 'log_kappa_racha', 'u_hawkes', 'd_racha')
+
+
+def guardar(modelo, archivo):
+    """Write the model's configuration and weights (asrn/nucleo.py:2068-2074); written to a temporary file, flushed to
+    disk and renamed, so an interrupted write leaves the previous file intact."""
+    import os
+    carpeta = os.path.dirname(os.path.abspath(archivo))
+    os.makedirs(carpeta, exist_ok=True)
+    tmp = archivo + '.tmp'
+    estado = {k: v.detach().cpu() for k, v in modelo.state_dict().items()}
+    try:
+        with open(tmp, 'wb') as f:
+            torch.save({'config': modelo.config, 'pesos': estado}, f)
+            f.flush()
+            os.fsync(f.fileno())
+        os.replace(tmp, archivo)
+    except BaseException:
+        if os.path.exists(tmp):
+            os.remove(tmp)
+        raise
+
+
+def _migrate_streak(pesos):
+    """Files of the reference's v86 stored the streak response per node ('u_racha'); v87 stores its increments
+    ('d_racha'): d = [u_0, u_1 - u_0, ...], an exact conversion (asrn/nucleo.py:2096-2107)."""
+    viejos = [n for n in pesos if n.rsplit('.', 1)[-1] == 'u_racha']
+    if not viejos:
+        return pesos
+    pesos = dict(pesos)
+    for n in viejos:
+        u = pesos.pop(n)
+        pesos[n[:-len('u_racha')] + 'd_racha'] = torch.cat([u[:1], u[1:] - u[:-1]])
+    return pesos
+
+
+def cargar(archivo, dispositivo=None, confiar=False, protecciones=None):
+    """Load a model written by guardar() here or by the reference's guardar() / entrenar() (its v83 to v89 files;
+    asrn/nucleo.py:2110-2133, asrn/__init__.py:73-75). Read with torch.load(weights_only=True) unless confiar=True.
+    Weights missing from files older than v87 keep their initial (neutral) values, as the reference does; any other
+    missing or unexpected weight is an error. Returns the model on `dispositivo` (default: cuda) in eval mode."""
+    import os
+    if not os.path.isfile(archivo):
+        raise FileNotFoundError(f'no such file: {archivo}')
+    try:
+        r = torch.load(archivo, map_location='cpu', weights_only=True)
+    except Exception as e:
+        if not confiar:
+            raise ValueError(f'{archivo}: could not be read in safe mode ({type(e).__name__}); pass confiar=True for a '
+                             'file of your own') from e
+        r = torch.load(archivo, map_location='cpu', weights_only=False)
+    if not isinstance(r, dict) or 'config' not in r or 'pesos' not in r:
+        raise ValueError(f'{archivo}: not a model written by guardar() / entrenar() of ASRN')
+    c = dict(r['config'])
+    m = ModeloASRN(c['V'], c['d'], c['n_capas'], c['largo_cada'], c['ff'], c['k'], init_profundo=False,
+                   dropout=c.get('dropout', 0.0), mezcla=c.get('mezcla', 'conv'), memoria_max=c.get('memoria_max', 1024),
+                   protecciones=protecciones, **c['opciones_capa'])
+    faltan, sobran = m.load_state_dict(_migrate_streak(r['pesos']), strict=False)
+    raros = [n for n in faltan if n.rsplit('.', 1)[-1] not in _NEW_IN_V87]
+    if sobran or raros:
+        raise ValueError(f'weights that are not ASRN v83-v89 weights: missing {raros}, unexpected {list(sobran)}')
+    return m.to(dispositivo or ('cuda' if torch.cuda.is_available() else 'cpu')).eval()
+
+
+save = guardar
+load = cargar

@@ -77,8 +77,8 @@ def parse():
     p.add_argument('--batch', type=int, default=B_PER_GPU, help='sequences per GPU')
     p.add_argument('--seq', type=int, default=L_SEQ)
     p.add_argument('--no-cpu-baseline', action='store_true')
-    p.add_argument('--workload', default='cfg3', choices=['cfg3', 'cfg4'],
-                   help='cfg3: the batch-sharded layer metric (default); cfg4: only the cfg4 leg')
+    p.add_argument('--workload', default='cfg3', choices=['cfg3', 'cfg4', 'gen'],
+                   help='cfg3: the batch-sharded layer metric (default); cfg4 / gen: only that leg (for profiling)')
     p.add_argument('--no-gen', action='store_true', help='skip the generation leg')
     p.add_argument('--no-legs', action='store_true', help='skip the cfg1 / cfg2 / cfg4 legs')
     p.add_argument('--eager', action='store_true', help='time the eager forward instead of its CUDA-graph replay')
@@ -651,8 +651,10 @@ def run_ours(args):
                 out['cpu_baseline'] = cpu_info
         del layer
         torch.cuda.empty_cache()
-    if not args.no_legs:
+    if not args.no_legs and args.workload in ('cfg3', 'cfg4'):
         legs['cfg4'] = leg_cfg4(args, dev, rank, world)
+    if args.workload == 'gen':
+        legs['generation'] = leg_generation(args, dev, rank, world)
     if args.workload == 'cfg3':
         if not args.no_gen:
             legs['generation'] = leg_generation(args, dev, rank, world)
@@ -660,8 +662,8 @@ def run_ours(args):
             legs['cfg2'] = leg_cfg2(args, dev, rank, world)
             legs['cfg1'] = leg_cfg1(args, dev, rank, world)
     if rank == 0:
-        if out is None:                       # --workload cfg4: the cfg4 leg is the line
-            out = dict(legs.pop('cfg4'))
+        if out is None:                       # --workload cfg4 / gen: that leg is the line
+            out = dict(legs.pop('cfg4' if args.workload == 'cfg4' else 'generation'))
         out.update({k: v for k, v in legs.items() if v is not None})
         print(json.dumps(out), flush=True)
     if world > 1:
@@ -865,10 +867,12 @@ def leg_generation(args, dev, rank, world):
                 nxt = w.paso(nxt, copiar=False).argmax(-1)
             torch.cuda.synchronize()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.nvtx.range_push('gen_steps')          # lets a profiler select the timed steps' kernels
             e0.record()
             for _ in range(args.gen_steps):
                 nxt = w.paso(nxt, copiar=False).argmax(-1)
             e1.record()
+            torch.cuda.nvtx.range_pop()
             torch.cuda.synchronize()
             status = w.status()
             if any(status):

@@ -201,6 +201,27 @@ def gen_state_case(name, B=2, L0=40, n_new=24, seed=0):
     print(f'{name}: {os.path.getsize(path) / 1024:.0f} KB')
 
 
+def checkpoint_case(name, seed=0):
+    """A model file written by the reference's own guardar() (asrn/nucleo.py:2068-2074), the same weights as a v86
+    file (the streak response stored per node as 'u_racha', asrn/nucleo.py:2096-2107), and the reference's logits of
+    a forward on seeded tokens (fp32)."""
+    import asrn
+    m = asrn.create_model(V=64, d=32, n_capas=3, largo_cada=1, semilla=seed, chunk=8, n_bits=4)
+    for c in m.largos:
+        _move(c, seed=seed + 5)
+    m.eval()
+    asrn.guardar(m, os.path.join(HERE, name + '.pt'))
+    pesos = {k: v.detach().clone() for k, v in m.state_dict().items()}
+    for k in [k for k in pesos if k.endswith('d_racha')]:
+        pesos[k[:-len('d_racha')] + 'u_racha'] = torch.cumsum(pesos.pop(k), 0)
+    torch.save({'config': m.config, 'pesos': pesos}, os.path.join(HERE, name + '_v86.pt'))
+    x = torch.from_numpy(synthetic.uniform_bytes_with_repeats(2, 96, seed) % 64)
+    with torch.no_grad():
+        lg = m(x)
+    np.savez_compressed(os.path.join(HERE, name + '.npz'), tokens=x.numpy(), logits=lg.numpy())
+    print(f'{name}: {os.path.getsize(os.path.join(HERE, name + ".pt")) / 1024:.0f} KB')
+
+
 def init_case(name, V, d, n_capas, seed):
     """Checksums of create_model's freshly initialised weights (same seed -> same weights in the build)."""
     import asrn
@@ -230,6 +251,7 @@ def main(ref):
     model_case('model_small', V=256, d=64, n_capas=4, B=2, L=192, L0=96, n_new=24)
     init_case('init_cfg1', V=256, d=64, n_capas=4, seed=0)
     gen_state_case('gen_state')
+    checkpoint_case('ckpt_ref')
 
 
 if __name__ == '__main__':
@@ -239,6 +261,7 @@ if __name__ == '__main__':
         sys.path.insert(0, sys.argv[1])
         torch.set_num_threads(8)
         for case in sys.argv[2:]:
-            {'gen_state': lambda: gen_state_case('gen_state')}[case]()
+            {'gen_state': lambda: gen_state_case('gen_state'),
+             'checkpoint': lambda: checkpoint_case('ckpt_ref')}[case]()
     else:
         main(sys.argv[1])

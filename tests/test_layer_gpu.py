@@ -116,10 +116,11 @@ def test_repetition_memory_matches_reference(name, cuda):
     assert rel_err(out['racha'].cpu().numpy(), z['racha']) <= 1e-5
 
 
-@pytest.mark.parametrize('L', [8192, 16385, 40000])
+@pytest.mark.parametrize('L', [1000, 3000, 8192, 12000, 16385, 40000])
 def test_repetition_long_rows_match_oracle(L, cuda):
-    """Rows longer than one shared-memory tile (tile sort + merge passes + tiled scan): keys, sort permutation and
-    repeated flags bit-exact against the oracle; Hawkes intensity and streak within 1e-5. Repetitive text (12-token
+    """Rows sorted in one block (radix sort, row lengths not multiples of 1024) and rows longer than 8192 (tile sort +
+    merge passes + tiled scan): keys, sort permutation and repeated flags bit-exact against the oracle; Hawkes
+    intensity and streak within 1e-5. Repetitive text (12-token
     vocabulary) so that n-gram groups are long and cross tile boundaries."""
     import asrn_b200
     from asrn_b200 import stages
