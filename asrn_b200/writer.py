@@ -13,8 +13,9 @@ run in explicit dtypes with weight copies made once (under bf16 autocast: the bf
 conv as a (d, k*d) matrix), so after one eager step the writer captures the step in a CUDA graph and replays it.
 
 generate() keeps the reference's sampling semantics (temperature, top_k, top_p, repetition penalty, no-repeat
-n-grams, stop token, conserving the probability of continuing a quote), sampling on the host with the same seeded
-generator, so greedy decoding (top_k=1) and seeded sampling give the reference's tokens.
+n-grams, stop token, conserving the probability of continuing a quote). The multinomial draw runs on the device with the
+random numbers of the reference's seeded CPU generator (asrn_b200.sampling), so greedy decoding (top_k=1) and seeded
+sampling give the reference's tokens; per step only the B drawn tokens and a status word come back to the host.
 """
 import ctypes
 
@@ -23,6 +24,7 @@ import torch.nn.functional as F
 
 from . import _lib, stages
 from .layer import compute_half, ctypes_ref
+from .sampling import DeviceSampler
 
 
 def _next_pow2(x):
@@ -373,18 +375,9 @@ def _keep_quote_mass(q, p, quote):
     return torch.where(ok, q * scale, q)
 
 
-def _advance(gen, pending, shape):
-    """Advance the CPU generator by `pending` multinomial draws over `shape`: torch.multinomial(p, 1) draws one Exp(1)
-    per entry of p (argmax of p / q, q ~ Exp(1)), so skipping a draw and replaying it later leaves the generator where
-    the reference's is."""
-    if pending:
-        buf = torch.empty(shape)
-        for _ in range(pending):
-            buf.exponential_(1, generator=gen)
-
-
-def _sample(lg, temperature, top_k, gen, top_p=1.0, quote=None):
-    """Temperature, top-k, top-p and the multinomial draw with the seeded CPU generator (asrn/nucleo.py:1945-1962)."""
+def _sample(lg, temperature, top_k, sampler, top_p=1.0, quote=None):
+    """Temperature, top-k, top-p and the multinomial draw (asrn/nucleo.py:1945-1962); the draw is the device replay of
+    the reference's seeded CPU generator (asrn_b200.sampling.DeviceSampler)."""
     p1 = torch.softmax(lg, -1) if quote is not None else None
     lg = lg / max(temperature, 1e-6)
     if top_k and top_k < lg.shape[-1]:
@@ -399,7 +392,7 @@ def _sample(lg, temperature, top_k, gen, top_p=1.0, quote=None):
     prob = torch.softmax(lg, -1)
     if quote is not None:
         prob = _keep_quote_mass(prob, p1, quote)
-    return torch.multinomial(prob.cpu(), 1, generator=gen).to(lg.device)
+    return sampler.sample(prob)
 
 
 @torch.no_grad()
@@ -414,7 +407,6 @@ def escribir(modelo, inicio, n_nuevos=200, temperatura=0.8, top_k=40, semilla=0,
         if modelo.emb.weight.dtype in (torch.float16, torch.bfloat16):
             raise ValueError('ASRN needs float32 weights; use torch.autocast for bf16 (asrn/nucleo.py:1025-1032)')
         dev = next(modelo.parameters()).device
-        gen = torch.Generator(device='cpu').manual_seed(semilla)
         w = Writer(modelo, memoria_de_lo_ajeno)
         x = inicio.to(dev)
         if x.dim() == 1:
@@ -424,8 +416,10 @@ def escribir(modelo, inicio, n_nuevos=200, temperatura=0.8, top_k=40, semilla=0,
         V = modelo.config['V']
         if int(x.min()) < 0 or int(x.max()) >= V:
             raise ValueError(f'inicio: tokens outside [0, {V}) (min {int(x.min())}, max {int(x.max())})')
-        lg = w.inicio(x, capacidad=L0 + n_nuevos)
         B = x.shape[0]
+        # the reference's torch.Generator('cpu').manual_seed(semilla), replayed on the device (asrn/nucleo.py:1996)
+        sampler = DeviceSampler(semilla, B, V, n_nuevos, dev)
+        lg = w.inicio(x, capacidad=L0 + n_nuevos)
         text = x.new_empty(B, L0 + n_nuevos)
         text[:, :L0] = x
         length = L0
@@ -433,11 +427,7 @@ def escribir(modelo, inicio, n_nuevos=200, temperatura=0.8, top_k=40, semilla=0,
         written = _NgramIndex([[] for _ in range(B)], no_repetir_ngramas) if no_repetir_ngramas else None
         steps = []
         done = torch.zeros(B, dtype=torch.bool, device=dev)
-        # Greedy decoding (top_k = 1): the distribution is one-hot unless a row's maximum is tied, and then the
-        # multinomial draw returns the argmax whatever its random numbers; such steps take the argmax on the device
-        # and only count the skipped draw, replayed before the next real draw (ties, sampling).
-        greedy = top_k == 1
-        pending = 0
+        done_host = [False] * B
         for k in range(n_nuevos):
             lg = lg.float()
             if devolver_logits:
@@ -446,30 +436,20 @@ def escribir(modelo, inicio, n_nuevos=200, temperatura=0.8, top_k=40, semilla=0,
                             written.next_mask(V, dev) if written else None)
             all_out = torch.isneginf(braked).all(-1, keepdim=True)
             lg = torch.where(all_out, lg, braked)
-            nxt = None
-            if greedy:
-                lt = lg / max(temperatura, 1e-6)
-                top = lt.max(-1, keepdim=True).values
-                tied = ((lt == top).sum(-1) > 1).any()
-                cand = lt.argmax(-1, keepdim=True)
-                if not bool(tied):
-                    nxt = cand
-                    pending += 1
-            if nxt is None:
-                _advance(gen, pending, tuple(lg.shape))
-                pending = 0
-                quote = quote_ng.next_mask(V, dev) if conservar_cita else None
-                nxt = _sample(lg, temperatura, top_k, gen, top_p, quote)
+            quote = quote_ng.next_mask(V, dev) if conservar_cita else None
+            nxt = _sample(lg, temperatura, top_k, sampler, top_p, quote)
+            toks = sampler.tokens_and_check()            # the step's only device sync: B tokens and a status word
             if parar_en is not None:
                 nxt = torch.where(done.unsqueeze(1), torch.full_like(nxt, parar_en), nxt)
                 done = done | (nxt[:, 0] == parar_en)
+                toks = [parar_en if dn else t for t, dn in zip(toks, done_host)]
+                done_host = [dn or t == parar_en for t, dn in zip(toks, done_host)]
             text[:, length] = nxt[:, 0]
             length += 1
-            nxt_cpu = nxt[:, 0].cpu()
             for ng in (quote_ng, written):
                 if ng is not None:
-                    ng.add(nxt_cpu.tolist())
-            if parar_en is not None and bool(done.all()):
+                    ng.add(toks)
+            if parar_en is not None and all(done_host):
                 break
             if k < n_nuevos - 1:
                 lg = w.paso(nxt[:, 0])

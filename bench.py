@@ -882,26 +882,30 @@ def leg_generation(args, dev, rank, world):
             del w, lg, nxt, x0
         torch.cuda.empty_cache()
     # public API end to end (host tokens in, host tokens out, sampling as the reference's): per-token cost from two
-    # calls that differ only in the number of new tokens
+    # calls that differ only in the number of new tokens; greedy (top_k=1) and the API's default sampling
+    # (temperature 0.8, top_k 40), both drawn on the device from the reference's seeded generator stream
     L0 = prompts[0]
     x0 = torch.from_numpy(synthetic.config_tokens('cfg5', B=B, L=L0, seed=rank))
     n_a, n_b = 8, 72
-    times = []
+    e2e_by_mode = {}
     with torch.autocast('cuda', dtype=torch.bfloat16):
-        asrn_b200.generate(m, x0, n_nuevos=4, top_k=1, devolver_logits=False)
-        for n in (n_a, n_b):
-            torch.cuda.synchronize()
-            t0 = time.perf_counter()
-            asrn_b200.generate(m, x0, n_nuevos=n, top_k=1, devolver_logits=False)
-            torch.cuda.synchronize()
-            times.append(time.perf_counter() - t0)
-    e2e_us = (times[1] - times[0]) / (n_b - n_a) * 1e6
+        for mode, kw in (('greedy', dict(top_k=1)), ('sampled', dict(temperatura=0.8, top_k=40))):
+            asrn_b200.generate(m, x0, n_nuevos=4, devolver_logits=False, **kw)
+            times = []
+            for n in (n_a, n_b):
+                torch.cuda.synchronize()
+                t0 = time.perf_counter()
+                asrn_b200.generate(m, x0, n_nuevos=n, devolver_logits=False, **kw)
+                torch.cuda.synchronize()
+                times.append(time.perf_counter() - t0)
+            e2e_by_mode[mode] = (times[1] - times[0]) / (n_b - n_a) * 1e6
+    e2e_us = e2e_by_mode['greedy']
     del m
     torch.cuda.empty_cache()
     flat = [res[p][0] for p in prompts]
-    vals = _max_over_ranks(flat + [e2e_us], dev, world)
+    vals = _max_over_ranks(flat + [e2e_us, e2e_by_mode['sampled']], dev, world)
     step_us = dict(zip(prompts, vals[:len(prompts)]))
-    e2e_us = vals[-1]
+    e2e_us, e2e_sampled_us = vals[-2], vals[-1]
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
@@ -927,8 +931,11 @@ def leg_generation(args, dev, rank, world):
            'prefill_tokens_per_s_by_prompt': {str(k): res[k][1] * world for k in prompts},
            'tokens_per_s': B * world / (main * 1e-6),
            'e2e': {'value': e2e_us, 'unit': 'us/token',
+                   'sampled_us_per_token': e2e_sampled_us,
                    'api': 'asrn_b200.generate(top_k=1, devolver_logits=False), host prompt of %d tokens; per-token '
-                          'cost = difference of a %d- and an %d-token call / %d' % (L0, n_b, n_a, n_b - n_a)}}
+                          'cost = difference of a %d- and an %d-token call / %d; sampled_us_per_token: the same with '
+                          'temperatura=0.8, top_k=40 (the API default); draws on the device from the reference\'s '
+                          'seeded CPU generator stream' % (L0, n_b, n_a, n_b - n_a)}}
     if cpu is not None:
         leg['cpu_baseline'] = cpu
     return leg

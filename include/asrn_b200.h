@@ -336,6 +336,31 @@ int asrn_gen_attend(const asrn_layer_config* cfg, const asrn_layer_weights* w, c
 int asrn_gen_ring_insert(int64_t B, int32_t T, int32_t nb, int32_t C, const int64_t* t_pos, const uint16_t* ids_t,
                          int32_t* ring, int32_t* count, void* stream);
 
+/* ---- device sampling with the reference's random numbers ----------------------------------------------------------
+ * Replaces the host draw torch.multinomial(prob.cpu(), 1, generator=g) of asrn/nucleo.py:1962 on the CPU generator
+ * g = torch.Generator('cpu').manual_seed(semilla) of asrn/nucleo.py:1996. For one sample torch takes, per row, the
+ * argmax of prob / q with q an Exp(1) draw per element of prob (one MT19937 64-bit value each, in memory order), so
+ * step k of a call on a (B, V) matrix reads the generator's 32-bit outputs [2 B V k, 2 B V (k + 1)).
+ * asrn_sampler_seed_state (host): the 624-word MT19937 array manual_seed(seed) starts from (uses seed mod 2^32).
+ * asrn_sampler_jump_poly (host): x^distance modulo the generator's characteristic polynomial, 624 words (bit b of word
+ *   w = coefficient 32 w + b); the polynomial is found once per process (Berlekamp-Massey, tens of ms) and each
+ *   distance is cached. Returns ASRN_ERR_UNSUPPORTED if the polynomial could not be found.
+ * asrn_sampler_fill (device): for k < steps, q[k * draws + i] = the i-th Exp(1) draw of the k-th draws-element tensor
+ *   made after `state` (624 device words: the window of untempered words the next draw starts from; the seed state
+ *   before any draw); polys = levels device polynomials, polys[l] = x^(2^l * 2 * draws) mod phi; steps <= 2^levels.
+ *   end_state (device, may be null) receives the window after steps * draws draws. One block per step. q matches
+ *   torch's CPU exponential_ bit for bit except where CUDA's double log1p and the host's differ by an ulp at a float
+ *   rounding boundary (about 2^-29 of the draws; such a q moves by one float ulp).
+ * asrn_sample_argmax (device): out[r] = argmax_j prob[r, j] / q[r, j] (IEEE float division; NaN wins; ties keep the
+ *   lower index), torch.multinomial's one-sample rule. A row with an element that is negative, infinite or NaN, or
+ *   whose elements are all zero, records ASRN_ERR_DATA in *status (device int, may be null; torch raises there). */
+int asrn_sampler_seed_state(uint64_t seed, uint32_t* state);
+int asrn_sampler_jump_poly(uint64_t distance, uint32_t* poly);
+int asrn_sampler_fill(int64_t draws, int64_t steps, int32_t levels, const uint32_t* state, const uint32_t* polys,
+                      float* q, uint32_t* end_state, void* stream);
+int asrn_sample_argmax(int64_t rows, int64_t V, const float* prob, const float* q, int64_t* out, int* status,
+                       void* stream);
+
 /* ---- test hooks (no counterpart in the reference; the layer forward never calls them) ------------------------------
  * asrn_test_force_cuda_core: 1 routes the bfloat16 work of later calls to the CUDA-core kernels (the fp32 path's), so
  * tests can compare them with the tensor-core kernels; 0 restores the default; a negative value only queries. Returns

@@ -18,6 +18,7 @@ overflow (chunk 4, 2 bits) and records, after the prompt and after every step, e
 asrn/nucleo.py:1621-1631) and the Hawkes state of every n-gram key (_MemoriaHawkes, asrn/nucleo.py:1634-1714).
 The fixtures are read by the tests on any machine; this script is the only place that imports the reference.
 """
+import json
 import os
 import sys
 
@@ -128,6 +129,34 @@ def model_case(name, V, d, n_capas, B, L, L0, n_new, seed=0):
     meta = dict(V=V, d=d, n_capas=n_capas, B=B, L=L, L0=L0, n_new=n_new, seed=seed)
     for k, v in meta.items():
         out['meta.' + k] = np.array(v)
+    path = os.path.join(HERE, name + '.npz')
+    np.savez_compressed(path, **out)
+    print(f'{name}: {os.path.getsize(path) / 1024:.0f} KB')
+
+
+SAMPLED_SETTINGS = [
+    dict(temperatura=0.8, top_k=40, semilla=3),
+    dict(temperatura=0.9, top_k=20, top_p=0.9, semilla=5, pena_repeticion=1.3, no_repetir_ngramas=3),
+    dict(temperatura=1.0, top_k=0, semilla=11, conservar_cita=False),
+    dict(temperatura=0.7, top_k=8, semilla=2**40 + 17),
+]
+
+
+def gen_sampled_case(name):
+    """Seeded sampling by the reference's generate on the model_small fixture's weights and prompts: the tokens of
+    each setting of SAMPLED_SETTINGS (its draws come from torch.multinomial on a seeded CPU generator)."""
+    import asrn
+    z = np.load(os.path.join(HERE, 'model_small.npz'))
+    V, d, n_capas = int(z['meta.V']), int(z['meta.d']), int(z['meta.n_capas'])
+    L0, n_new = int(z['meta.L0']), int(z['meta.n_new'])
+    m = asrn.create_model(V=V, d=d, n_capas=n_capas)
+    m.load_state_dict({k[6:]: torch.from_numpy(np.asarray(z[k])) for k in z.files if k.startswith('param.')})
+    m.eval()
+    x0 = torch.from_numpy(z['tokens'][:, :L0])
+    out = {'settings': np.array(json.dumps(SAMPLED_SETTINGS))}
+    for i, kw in enumerate(SAMPLED_SETTINGS):
+        seqs, _ = asrn.generate(m, x0, n_nuevos=n_new, devolver_logits=False, **kw)
+        out[f'seqs_{i}'] = seqs.numpy()
     path = os.path.join(HERE, name + '.npz')
     np.savez_compressed(path, **out)
     print(f'{name}: {os.path.getsize(path) / 1024:.0f} KB')
@@ -252,6 +281,7 @@ def main(ref):
     init_case('init_cfg1', V=256, d=64, n_capas=4, seed=0)
     gen_state_case('gen_state')
     checkpoint_case('ckpt_ref')
+    gen_sampled_case('gen_sampled')
 
 
 if __name__ == '__main__':
@@ -262,6 +292,7 @@ if __name__ == '__main__':
         torch.set_num_threads(8)
         for case in sys.argv[2:]:
             {'gen_state': lambda: gen_state_case('gen_state'),
-             'checkpoint': lambda: checkpoint_case('ckpt_ref')}[case]()
+             'checkpoint': lambda: checkpoint_case('ckpt_ref'),
+             'gen_sampled': lambda: gen_sampled_case('gen_sampled')}[case]()
     else:
         main(sys.argv[1])

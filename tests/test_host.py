@@ -90,19 +90,3 @@ def test_synthetic_streams_are_seeded():
     assert np.array_equal(a, b) and a.max() < 50304 and a.min() >= 0
     x = synthetic.config_tokens('cfg2', B=1, L=4096)
     assert x.max() < 256
-
-
-def test_skipped_greedy_draws_replay_the_generator():
-    """generate()'s greedy path skips the multinomial draw of steps whose maximum is unique and replays it before the
-    next real draw: the generator must end where the reference's (one torch.multinomial per step) ends, and the
-    draws after it must agree."""
-    import torch
-    from asrn_b200.writer import _advance
-    B, V = 3, 257
-    probs = [torch.softmax(torch.randn(B, V), -1) for _ in range(4)]
-    g_ref = torch.Generator().manual_seed(11)
-    ref = [torch.multinomial(p, 1, generator=g_ref) for p in probs]
-    g = torch.Generator().manual_seed(11)
-    _advance(g, 3, (B, V))
-    assert torch.equal(torch.multinomial(probs[3], 1, generator=g), ref[3])
-    assert torch.equal(g.get_state(), g_ref.get_state())
