@@ -102,6 +102,10 @@ _SIGS = {
     'asrn_gen_gate': (ctypes.c_int, [_P] * 16),
     'asrn_gate_workspace_bytes': (ctypes.c_size_t, [_P]),
     'asrn_gate': (ctypes.c_int, [_P] * 14 + [ctypes.c_size_t, _P]),
+    'asrn_ngram_shared_bytes': (ctypes.c_size_t, [_P]),
+    'asrn_ngram_shared_sort': (ctypes.c_int, [_P, _P, _P, _P, _P, ctypes.c_size_t, _P, ctypes.c_size_t, _P]),
+    'asrn_layer_forward_ngram': (ctypes.c_int, [_P, _P, _P, _P, _P, _P, _P, ctypes.c_size_t, _P, _P, ctypes.c_size_t,
+                                                _P]),
     'asrn_sampler_seed_state': (ctypes.c_int, [ctypes.c_uint64, _P]),
     'asrn_sampler_jump_poly': (ctypes.c_int, [ctypes.c_uint64, _P]),
     'asrn_sampler_fill': (ctypes.c_int, [ctypes.c_int64, ctypes.c_int64, ctypes.c_int32, _P, _P, _P, _P, _P]),

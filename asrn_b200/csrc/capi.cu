@@ -196,15 +196,20 @@ size_t asrn_layer_workspace_bytes(const asrn_layer_config* cfg) {
   return workspace_layout(*cfg).total;
 }
 
-int asrn_layer_forward(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared,
-                       const float* E, const float* h, const int64_t* tokens, float* h_out, void* workspace,
-                       size_t workspace_bytes, void* stream) {
+}  // extern "C"
+
+// The layer forward; with `ngram` (asrn_ngram_shared_sort's output for the same tokens) the repetition stage runs
+// only its scans.
+static int layer_forward(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared,
+                         const float* E, const float* h, const int64_t* tokens, const void* ngram, size_t ngram_bytes,
+                         float* h_out, void* workspace, size_t workspace_bytes, void* stream) {
   int st = check_config(cfg);
   if (st) return st;
   if ((st = check_weights(w))) return st;
   const asrn_layer_config& c = *cfg;
   if ((int64_t)c.B * c.L == 0) return ASRN_OK;
   if (!E || !h || !h_out || !prepared) return ASRN_ERR_ARG;
+  if (ngram && (!tokens || ngram_bytes < ngram_shared_bytes(c.B, c.L, c.vistos))) return ASRN_ERR_ARG;
   const Workspace ws = workspace_layout(c);
   if (!workspace || workspace_bytes < ws.total) return ASRN_ERR_WORKSPACE;
   cudaStream_t s = as_stream(stream);
@@ -246,6 +251,12 @@ int asrn_layer_forward(const asrn_layer_config* cfg, const asrn_layer_weights* w
   RepetitionArgs ra = repetition_args(c, *w, prep);
   ra.sig = sig; ra.beta = beta; ra.Bt = Bt; ra.log_alfa = la; ra.vistos = vistos; ra.hawkes = hawkes;
   ra.racha = racha;
+  if (ngram) {
+    char* ng = const_cast<char*>(reinterpret_cast<const char*>(ngram));
+    ra.ng_mode = kNgScanOnly;
+    ra.ng_keys = reinterpret_cast<uint64_t*>(ng);
+    ra.ng_pos = reinterpret_cast<uint32_t*>(ng + align_up((size_t)c.B * c.vistos * c.L * 8));
+  }
   if ((st = launch_repetition(ra, base + ws.rep, repetition_workspace(c.B, c.L, c.vistos), s))) return st;
   GateArgs ga = gate_args(c, *w, prep);
   ga.h = h; ga.glogit = glogit; ga.sen_hay = hay; ga.sen_mx = mx; ga.sen_pk = pk;
@@ -258,6 +269,44 @@ int asrn_layer_forward(const asrn_layer_config* cfg, const asrn_layer_weights* w
     ga.acc = reinterpret_cast<const float*>(acc);
   }
   return launch_gate(ga, c.half, s);
+}
+
+extern "C" {
+
+int asrn_layer_forward(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared,
+                       const float* E, const float* h, const int64_t* tokens, float* h_out, void* workspace,
+                       size_t workspace_bytes, void* stream) {
+  return layer_forward(cfg, w, prepared, E, h, tokens, nullptr, 0, h_out, workspace, workspace_bytes, stream);
+}
+
+size_t asrn_ngram_shared_bytes(const asrn_layer_config* cfg) {
+  if (check_config(cfg) != ASRN_OK) return 0;
+  return ngram_shared_bytes(cfg->B, cfg->L, cfg->vistos);
+}
+
+int asrn_ngram_shared_sort(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared,
+                           const int64_t* tokens, void* ngram, size_t ngram_bytes, void* workspace,
+                           size_t workspace_bytes, void* stream) {
+  int st = check_config(cfg);
+  if (st) return st;
+  if ((st = check_weights(w))) return st;
+  const asrn_layer_config& c = *cfg;
+  if ((int64_t)c.B * c.L == 0) return ASRN_OK;
+  if (!prepared || !tokens || !ngram || ngram_bytes < ngram_shared_bytes(c.B, c.L, c.vistos)) return ASRN_ERR_ARG;
+  RepetitionArgs ra = repetition_args(c, *w, reinterpret_cast<const char*>(prepared));
+  char* ng = reinterpret_cast<char*>(ngram);
+  ra.tok = tokens;
+  ra.ng_mode = kNgSortOnly;
+  ra.ng_keys = reinterpret_cast<uint64_t*>(ng);
+  ra.ng_pos = reinterpret_cast<uint32_t*>(ng + align_up((size_t)c.B * c.vistos * c.L * 8));
+  return launch_repetition(ra, workspace, workspace_bytes, as_stream(stream));
+}
+
+int asrn_layer_forward_ngram(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared,
+                             const float* E, const float* h, const int64_t* tokens, const void* ngram,
+                             size_t ngram_bytes, float* h_out, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!ngram) return ASRN_ERR_ARG;
+  return layer_forward(cfg, w, prepared, E, h, tokens, ngram, ngram_bytes, h_out, workspace, workspace_bytes, stream);
 }
 
 int asrn_context(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared, const float* h,

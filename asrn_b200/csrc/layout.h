@@ -120,7 +120,15 @@ struct RepetitionArgs {
   uint8_t* repetido;       // optional
   const float* racha_in;   // optional (B): streak value before the first position (0 when null)
   float* racha_map;        // optional (B, 2): the rows' streak maps S_last = A * S_in + B (A, B)
+  // The n-gram sort shared by the layers of a model (whole rows only): ng_mode 1 sorts and writes the sorted keys and
+  // positions of every (b, n) row to ng_keys / ng_pos and stops; ng_mode 2 takes them from there instead of sorting.
+  int ng_mode;
+  uint64_t* ng_keys;       // (B, n, L) order-preserving keys, sorted per row
+  uint32_t* ng_pos;        // (B, n, L) their positions
+  const int64_t* tok;      // optional: signatures are the token ids (as fp32) instead of sig
 };
+
+enum { kNgFull = 0, kNgSortOnly = 1, kNgScanOnly = 2 };
 
 struct GateArgs {
   int64_t B, L;
@@ -245,6 +253,7 @@ int launch_candidates(int64_t B, int64_t L, int T, int C, int K, const int32_t* 
                       const float* sig, int32_t* cand, uint8_t* suffix, cudaStream_t s);
 size_t repetition_workspace(int64_t B, int64_t L, int n);
 int launch_repetition(const RepetitionArgs& a, void* ws, size_t ws_bytes, cudaStream_t s);
+size_t ngram_shared_bytes(int64_t B, int64_t L, int n);
 int launch_gate(const GateArgs& a, bool half, cudaStream_t s);
 size_t gate_workspace(int64_t M, int d, bool half);
 int launch_prepare(const asrn_layer_config& c, const asrn_layer_weights& w, void* prepared, cudaStream_t s);

@@ -136,48 +136,77 @@ __device__ __forceinline__ void block_scan_affine(Affine* v, Affine* warp_agg) {
   for (int k = 0; k < kItems; ++k) v[k] = compose(pre, v[k]);
 }
 
+// The signature at t of a row: the token id as fp32 when the row's tokens are given, else sig (firmas_de_piezas,
+// asrn/nucleo.py:161-164, or E . r_firma).
+__device__ __forceinline__ double sig_at(const float* sig, const int64_t* tok, int64_t t) {
+  return tok ? (double)(float)tok[t] : (double)sig[t];
+}
+
+__device__ __forceinline__ double ngram_key_at(const float* sig, const int64_t* tok, int64_t i, int ni,
+                                               const double* c) {
+  double key = 0.0;
+  for (int j = 0; j <= ni; ++j) {
+    const int64_t t = i - j;
+    const double s = (t >= 0) ? sig_at(sig, tok, t) : __longlong_as_double(0x7ff8000000000000ll);
+    key = __dadd_rn(key, __dmul_rn(s, c[j]));
+  }
+  return key;
+}
+
 template <int kItems>
 __global__ void __launch_bounds__(kRxThreads) k_ngram_row(RepetitionArgs a, int n2) {
   // n2: the row length rounded up to a multiple of 1024 (the sort's padding keys are all ones: they sort last)
   extern __shared__ __align__(16) char smem_raw[];
-  uint64_t* k0 = reinterpret_cast<uint64_t*>(smem_raw);
-  uint64_t* k1 = k0 + n2;
-  uint32_t* p0 = reinterpret_cast<uint32_t*>(k1 + n2);
-  uint32_t* p1 = p0 + n2;
-  uint16_t* tab = reinterpret_cast<uint16_t*>(p1 + n2);
   __shared__ Affine warp_agg[32];
   const int64_t b = blockIdx.x / a.n;
   const int ni = (int)(blockIdx.x % a.n);
   const int64_t L = a.L;
-  const float* sig = a.sig + b * L;
-  // keys of the (ni + 1)-token groups ending at t (asrn/nucleo.py:175-185)
-  for (int i = threadIdx.x; i < n2; i += blockDim.x) {
-    if (i < L) {
-      double key = 0.0;
-      for (int j = 0; j <= ni; ++j) {
-        const int64_t t = i - j;
-        const double s = (t >= 0) ? (double)sig[t] : __longlong_as_double(0x7ff8000000000000ll);
-        key = __dadd_rn(key, __dmul_rn(s, a.c[j]));
+  const uint64_t* sk;
+  const uint32_t* sp;
+  if (a.ng_mode == kNgScanOnly) {
+    sk = a.ng_keys + (int64_t)blockIdx.x * L;
+    sp = a.ng_pos + (int64_t)blockIdx.x * L;
+  } else {
+    uint64_t* k0 = reinterpret_cast<uint64_t*>(smem_raw);
+    uint64_t* k1 = k0 + n2;
+    uint32_t* p0 = reinterpret_cast<uint32_t*>(k1 + n2);
+    uint32_t* p1 = p0 + n2;
+    uint16_t* tab = reinterpret_cast<uint16_t*>(p1 + n2);
+    const float* sig = a.sig ? a.sig + b * L : nullptr;
+    const int64_t* tok = a.tok ? a.tok + b * L : nullptr;
+    // keys of the (ni + 1)-token groups ending at t (asrn/nucleo.py:175-185)
+    for (int i = threadIdx.x; i < n2; i += blockDim.x) {
+      if (i < L) {
+        const double key = ngram_key_at(sig, tok, i, ni, a.c);
+        if (a.keys) a.keys[(b * L + i) * a.n + ni] = key;
+        k0[i] = sortable_key(key);
+        p0[i] = (uint32_t)i;
+      } else {
+        k0[i] = 0xFFFFFFFFFFFFFFFFull;
+        p0[i] = 0xFFFFFFFFu;
       }
-      if (a.keys) a.keys[(b * L + i) * a.n + ni] = key;
-      k0[i] = sortable_key(key);
-      p0[i] = (uint32_t)i;
-    } else {
-      k0[i] = 0xFFFFFFFFFFFFFFFFull;
-      p0[i] = 0xFFFFFFFFu;
     }
-  }
-  __syncthreads();
-  // stable LSD radix sort by key: positions start ascending, so equal keys keep position order
-  uint64_t* sk = k0;
-  uint32_t* sp = p0;
-  for (int shift = 0; shift < 64; shift += 8) {
-    uint64_t* dk = sk == k0 ? k1 : k0;
-    uint32_t* dp = sp == p0 ? p1 : p0;
-    if (radix_pass64(sk, sp, dk, dp, tab, n2, shift)) {
-      sk = dk;
-      sp = dp;
+    __syncthreads();
+    // stable LSD radix sort by key: positions start ascending, so equal keys keep position order
+    uint64_t* ck = k0;
+    uint32_t* cp = p0;
+    for (int shift = 0; shift < 64; shift += 8) {
+      uint64_t* dk = ck == k0 ? k1 : k0;
+      uint32_t* dp = cp == p0 ? p1 : p0;
+      if (radix_pass64(ck, cp, dk, dp, tab, n2, shift)) {
+        ck = dk;
+        cp = dp;
+      }
     }
+    if (a.ng_mode == kNgSortOnly) {
+      for (int i = threadIdx.x; i < L; i += blockDim.x) {
+        a.ng_keys[(int64_t)blockIdx.x * L + i] = ck[i];
+        a.ng_pos[(int64_t)blockIdx.x * L + i] = cp[i];
+      }
+      return;
+    }
+    sk = ck;
+    sp = cp;
   }
   // affine elements in sorted order; thread owns kItems consecutive slots
   const float kappa = a.kappa[ni];
@@ -331,15 +360,6 @@ struct RepLong {
   float2* agg;         // (rows, tiles) tile aggregates
 };
 
-__device__ __forceinline__ double ngram_key_at(const float* sig, int64_t i, int ni, const double* c) {
-  double key = 0.0;
-  for (int j = 0; j <= ni; ++j) {
-    const int64_t t = i - j;
-    const double s = (t >= 0) ? (double)sig[t] : __longlong_as_double(0x7ff8000000000000ll);
-    key = __dadd_rn(key, __dmul_rn(s, c[j]));
-  }
-  return key;
-}
 
 __global__ void __launch_bounds__(1024) k_ngram_tile_sort(RepetitionArgs a, int64_t tiles, uint64_t* K, uint32_t* Pp) {
   extern __shared__ __align__(16) char smem_raw[];
@@ -349,11 +369,12 @@ __global__ void __launch_bounds__(1024) k_ngram_tile_sort(RepetitionArgs a, int6
   const int64_t b = row / a.n;
   const int ni = (int)(row % a.n);
   const int64_t L = a.L, base = tile * kSortTile;
-  const float* sig = a.sig + b * a.Lf;
+  const float* sig = a.sig ? a.sig + b * a.Lf : nullptr;
+  const int64_t* tok = a.tok ? a.tok + b * a.Lf : nullptr;
   for (int i = threadIdx.x; i < kSortTile; i += blockDim.x) {
     const int64_t p = base + i;
     if (p < L) {
-      const double key = ngram_key_at(sig, a.pos0 + p, ni, a.c);
+      const double key = ngram_key_at(sig, tok, a.pos0 + p, ni, a.c);
       if (a.keys) a.keys[(b * L + p) * a.n + ni] = key;
       sk[i] = sortable_key(key);
       sp[i] = (uint32_t)(a.pos0 + p);
@@ -527,16 +548,29 @@ static int launch_repetition_long(const RepetitionArgs& a, void* ws, size_t ws_b
   const int64_t tiles = (L + kRepTile - 1) / kRepTile;
   const int64_t stiles = (L + kSortTile - 1) / kSortTile;
   RepLong r = rep_long_layout(ws, rows, L);
-  const size_t smem = (size_t)kSortTile * 12;
-  cudaFuncSetAttribute(k_ngram_tile_sort, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  k_ngram_tile_sort<<<(unsigned)(rows * stiles), 1024, smem, s>>>(a, stiles, r.k0, r.p0);
-  uint64_t *kin = r.k0, *kout = r.k1;
-  uint32_t *pin = r.p0, *pout = r.p1;
-  const int64_t per_row = (L + kMergeItems - 1) / kMergeItems;
-  for (int64_t w = kSortTile; w < L; w <<= 1) {
-    k_ngram_merge<<<(unsigned)((rows * per_row + 255) / 256), 256, 0, s>>>(kin, pin, kout, pout, rows, L, w);
-    uint64_t* tk = kin; kin = kout; kout = tk;
-    uint32_t* tp = pin; pin = pout; pout = tp;
+  uint64_t* kin = r.k0;
+  uint32_t* pin = r.p0;
+  if (a.ng_mode == kNgScanOnly) {
+    kin = a.ng_keys;
+    pin = a.ng_pos;
+  } else {
+    const size_t smem = (size_t)kSortTile * 12;
+    cudaFuncSetAttribute(k_ngram_tile_sort, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    k_ngram_tile_sort<<<(unsigned)(rows * stiles), 1024, smem, s>>>(a, stiles, r.k0, r.p0);
+    uint64_t* kout = r.k1;
+    uint32_t* pout = r.p1;
+    const int64_t per_row = (L + kMergeItems - 1) / kMergeItems;
+    for (int64_t w = kSortTile; w < L; w <<= 1) {
+      k_ngram_merge<<<(unsigned)((rows * per_row + 255) / 256), 256, 0, s>>>(kin, pin, kout, pout, rows, L, w);
+      uint64_t* tk = kin; kin = kout; kout = tk;
+      uint32_t* tp = pin; pin = pout; pout = tp;
+    }
+    if (a.ng_mode == kNgSortOnly) {
+      if (cudaMemcpyAsync(a.ng_keys, kin, (size_t)rows * L * 8, cudaMemcpyDeviceToDevice, s) != cudaSuccess ||
+          cudaMemcpyAsync(a.ng_pos, pin, (size_t)rows * L * 4, cudaMemcpyDeviceToDevice, s) != cudaSuccess)
+        return ASRN_ERR_CUDA;
+      return cudaGetLastError() == cudaSuccess ? ASRN_OK : ASRN_ERR_CUDA;
+    }
   }
   k_ngram_scan_tile<<<(unsigned)(rows * tiles), 1024, 0, s>>>(a, tiles, kin, pin, r.vloc, r.agg);
   k_ngram_apply<<<(unsigned)(rows * tiles), 1024, 0, s>>>(a, tiles, kin, pin, r.vloc, r.agg);
@@ -846,13 +880,14 @@ int launch_racha(const RepetitionArgs& a, cudaStream_t s) { return launch_racha_
 int launch_repetition(const RepetitionArgs& a, void* ws, size_t ws_bytes, cudaStream_t s) {
   if (a.B == 0 || a.L == 0) return ASRN_OK;
   if (a.n < 1 || a.n > kMaxSeen) return ASRN_ERR_ARG;
+  if (a.ng_mode != kNgFull && (!a.ng_keys || !a.ng_pos || a.pos0 != 0 || a.Lf != a.L)) return ASRN_ERR_ARG;
   if (rep_tiled(a.L)) {
     const int st = launch_repetition_long(a, ws, ws_bytes, s);
-    if (st) return st;
+    if (st || a.ng_mode == kNgSortOnly) return st;
     return launch_racha_ws(a, ws, ws_bytes, s);   // the n-gram passes are done with the workspace
   }
   const int n2 = (int)((a.L + kRxThreads - 1) / kRxThreads * kRxThreads);
-  const size_t smem = (size_t)n2 * 24 + kRxTabBytes;
+  const size_t smem = a.ng_mode == kNgScanOnly ? 0 : (size_t)n2 * 24 + kRxTabBytes;
   dim3 grid((unsigned)(a.B * a.n));
   const int items = n2 / 1024;
   if (items <= 1) {
@@ -872,8 +907,14 @@ int launch_repetition(const RepetitionArgs& a, void* ws, size_t ws_bytes, cudaSt
     k_ngram_row<16><<<grid, 1024, smem, s>>>(a, n2);
   }
   if (cudaGetLastError() != cudaSuccess) return ASRN_ERR_CUDA;
+  if (a.ng_mode == kNgSortOnly) return ASRN_OK;
   k_racha<<<(unsigned)a.B, 1024, 0, s>>>(a);
   return cudaGetLastError() == cudaSuccess ? ASRN_OK : ASRN_ERR_CUDA;
+}
+
+size_t ngram_shared_bytes(int64_t B, int64_t L, int n) {
+  const size_t e = (size_t)B * n * L;
+  return align_up(e * 8) + align_up(e * 4);
 }
 
 }  // namespace asrn

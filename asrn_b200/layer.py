@@ -53,8 +53,8 @@ class _LayerForward(torch.autograd.Function):
     """Forward through the C ABI; this build has no backward (the reference's training path is out of scope)."""
 
     @staticmethod
-    def forward(ctx, layer, E, h, piezas, half):
-        return layer._run(E, h, piezas, half)
+    def forward(ctx, layer, E, h, piezas, half, ngram):
+        return layer._run(E, h, piezas, half, ngram)
 
     @staticmethod
     def backward(ctx, *grads):
@@ -156,13 +156,38 @@ class ASRNLayer(nn.Module):
 
     # ---- forward -------------------------------------------------------------------------------------------------
 
-    def forward(self, E, h, piezas=None):
+    def forward(self, E, h, piezas=None, ngram=None):
         """E (B, L, d) token vectors, h (B, L, d) state, piezas (B, L) token ids (or None: signatures E . r_firma).
-        Returns h' (B, L, d)."""
+        Returns h' (B, L, d). ngram: the n-gram sort of piezas made by ngram_sort() (by this layer or another one with
+        the same vistos and c_vistos); the layer then skips its own sort (the result is the same)."""
         half = compute_half(h.device.type) if h.is_cuda else False
-        return _LayerForward.apply(self, E, h, piezas, half)
+        return _LayerForward.apply(self, E, h, piezas, half, ngram)
 
-    def _run(self, E, h, piezas, half):
+    def ngram_sort(self, piezas):
+        """The n-gram sort of the token rows piezas (B, L) that every ASRN layer of a model repeats (its keys depend
+        only on the tokens and on c_vistos, equal in every layer: asrn/nucleo.py:610, :691-701), made once on the
+        device; pass it to forward(..., ngram=...)."""
+        if not piezas.is_cuda:
+            raise RuntimeError('asrn_b200: the n-gram sort runs on CUDA tensors only')
+        B, L = piezas.shape
+        dev = piezas.device
+        tok = piezas.detach().to(torch.int64).contiguous()
+        half = compute_half(dev.type)
+        self._check_supported()
+        w, _keep, prep = self.prepared(dev, half)
+        cfg = _lib.make_config(self, B, L, half)
+        L_ = _lib.lib()
+        nbytes = L_.asrn_ngram_shared_bytes(ctypes_ref(cfg))
+        buf = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=dev)
+        wsb = L_.asrn_repetition_workspace_bytes(ctypes_ref(cfg))
+        ws = torch.empty(max(wsb, 1), dtype=torch.uint8, device=dev)
+        if B * L:
+            _lib.check(L_.asrn_ngram_shared_sort(ctypes_ref(cfg), ctypes_ref(w), _lib.ptr(prep), _lib.ptr(tok),
+                                                 _lib.ptr(buf), nbytes, _lib.ptr(ws), wsb, _lib.stream_ptr(dev)),
+                       'asrn_ngram_shared_sort')
+        return NgramSort(buf, nbytes, tok, self.vistos)
+
+    def _run(self, E, h, piezas, half, ngram=None):
         self._check_supported()
         if not (E.is_cuda and h.is_cuda):
             raise RuntimeError('asrn_b200.ASRNLayer runs on CUDA tensors only (there is no CPU implementation)')
@@ -185,10 +210,27 @@ class ASRNLayer(nn.Module):
         L_ = _lib.lib()
         nbytes = L_.asrn_layer_workspace_bytes(ctypes_ref(cfg))
         ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
-        _lib.check(L_.asrn_layer_forward(ctypes_ref(cfg), ctypes_ref(w), _lib.ptr(prep), _lib.ptr(E32), _lib.ptr(h32),
-                                         _lib.ptr(tok), _lib.ptr(out), _lib.ptr(ws), nbytes, _lib.stream_ptr(dev)),
-                   'asrn_layer_forward')
+        if ngram is None:
+            _lib.check(L_.asrn_layer_forward(ctypes_ref(cfg), ctypes_ref(w), _lib.ptr(prep), _lib.ptr(E32),
+                                             _lib.ptr(h32), _lib.ptr(tok), _lib.ptr(out), _lib.ptr(ws), nbytes,
+                                             _lib.stream_ptr(dev)), 'asrn_layer_forward')
+        else:
+            if tok is None or ngram.vistos != self.vistos or ngram.tokens.shape != (B, L) or \
+                    ngram.tokens.data_ptr() != tok.data_ptr() and not torch.equal(ngram.tokens, tok):
+                raise ValueError('ngram: made for other tokens or another number of n-gram orders')
+            _lib.check(L_.asrn_layer_forward_ngram(ctypes_ref(cfg), ctypes_ref(w), _lib.ptr(prep), _lib.ptr(E32),
+                                                   _lib.ptr(h32), _lib.ptr(tok), _lib.ptr(ngram.buf), ngram.nbytes,
+                                                   _lib.ptr(out), _lib.ptr(ws), nbytes, _lib.stream_ptr(dev)),
+                       'asrn_layer_forward_ngram')
         return out if h.dtype == torch.float32 else out.to(h.dtype)
+
+
+class NgramSort:
+    """The sorted n-gram keys and positions of a batch of token rows (ASRNLayer.ngram_sort), shared by the ASRN
+    layers of a model forward."""
+
+    def __init__(self, buf, nbytes, tokens, vistos):
+        self.buf, self.nbytes, self.tokens, self.vistos = buf, nbytes, tokens, vistos
 
 
 def ctypes_ref(x):

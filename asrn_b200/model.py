@@ -88,13 +88,26 @@ class ModeloASRN(nn.Module):
             raise ValueError(f'the model has {self.emb.weight.dtype} weights: ASRN needs float32 weights; use '
                              'torch.autocast for bf16 (asrn/nucleo.py:1025-1032)')
         E = self.emb(x)
+        # the n-gram sort depends only on the tokens and on c_vistos: made once for every ASRN layer (the reference
+        # repeats it in each one; docs/ARCHITECTURE.md:525, asrn/nucleo.py:1088-1103)
+        ng = self.largos[0].ngram_sort(x) if x.is_cuda and len(self.largos) > 1 and self._ngram_shared() else None
         h, j = E, 0
         for i, blq in enumerate(self.bloques):
             h = blq(h)
             if i in self.pos_largo:
-                h = self.largos[j](E, h, x)
+                h = self.largos[j](E, h, x, ngram=ng)
                 j += 1
         return self.head(self.ln_f(h))
+
+    def _ngram_shared(self):
+        """True when every ASRN layer has the same n-gram orders and c_vistos (checked again after a change)."""
+        key = tuple((c.vistos, c.c_vistos.data_ptr(), c.c_vistos._version) for c in self.largos)
+        if getattr(self, '_ng_key', None) != key:
+            c0 = self.largos[0]
+            self._ng_ok = all(c.vistos == c0.vistos and torch.equal(c.c_vistos.cpu(), c0.c_vistos.cpu())
+                              for c in self.largos)
+            self._ng_key = key
+        return self._ng_ok
 
     def num_parametros(self):
         return sum(p.numel() for p in self.parameters())

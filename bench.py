@@ -661,6 +661,7 @@ def run_ours(args):
         if not args.no_legs:
             legs['cfg2'] = leg_cfg2(args, dev, rank, world)
             legs['cfg1'] = leg_cfg1(args, dev, rank, world)
+            legs['model'] = leg_model(args, dev, rank, world)
     if rank == 0:
         if out is None:                       # --workload cfg4 / gen: that leg is the line
             out = dict(legs.pop('cfg4' if args.workload == 'cfg4' else 'generation'))
@@ -838,6 +839,46 @@ def leg_cfg1(args, dev, rank, world):
         except Exception as exc:
             leg['cpu_baseline'] = {'unavailable': '%s: %s' % (type(exc).__name__, exc)}
     return leg
+
+
+MODEL_B = 4
+
+
+def leg_model(args, dev, rank, world):
+    """The cfg3 model forward on one GPU (rank 0; the other ranks skip it): create_model(V=50304, d=768, n_capas=12)
+    (6 ASRN layers, 12 local blocks, tied head) random init, MODEL_B x 8192 Zipf+repeat tokens, bf16 autocast, the
+    whole forward replayed as one CUDA graph; also with each ASRN layer sorting the n-grams itself (the reference's
+    order of work) to show what the shared sort saves."""
+    import torch
+    import asrn_b200
+    from asrn_b200 import synthetic
+    vals = [0.0, 0.0]
+    mode = None
+    if rank == 0:
+        m = asrn_b200.create_model(V=V, d=D, n_capas=12, semilla=0).to(dev).eval()
+        x = torch.from_numpy(synthetic.config_tokens('cfg3', B=MODEL_B, L=L_SEQ, seed=0)).to(dev)
+
+        def step():
+            with torch.no_grad(), torch.autocast('cuda', dtype=torch.bfloat16):
+                return m(x)
+
+        for i, shared in enumerate((True, False)):
+            m._ngram_shared = (lambda ok: (lambda: ok))(shared)    # sort once, or in every layer
+            warm_up(step, args.warmup, 1)
+            run, mode, graph = graph_or_eager(step, args.eager)
+            ms, _ = timed(run, max(3, args.steps // 4))
+            vals[i] = ms / max(3, args.steps // 4)
+            del run, graph
+        del m
+        torch.cuda.empty_cache()
+    if rank != 0:
+        return None
+    tokens = MODEL_B * L_SEQ
+    return {'metric': 'model_fwd_tokens_per_s', 'value': tokens / (vals[0] * 1e-3), 'unit': 'tokens/s',
+            'forward_ms': vals[0], 'forward_ms_sorting_in_every_layer': vals[1], 'dtype': 'bf16', 'launch': mode,
+            'config': {'workload': 'cfg3 model: create_model(V=50304, d=768, n_capas=12) random init, forward on '
+                                   '%d x %d Zipf+repeat tokens, bf16 autocast (logits included)' % (MODEL_B, L_SEQ),
+                       'ngram_sort': 'once per forward, shared by the 6 ASRN layers'}}
 
 
 def leg_generation(args, dev, rank, world):

@@ -121,6 +121,20 @@ int asrn_layer_forward(const asrn_layer_config* cfg, const asrn_layer_weights* w
                        const float* E, const float* h, const int64_t* tokens, float* h_out, void* workspace,
                        size_t workspace_bytes, void* stream);
 
+/* The n-gram sort shared by the ASRN layers of a model (the reference sorts the same keys in every layer: its
+ * repetition memory depends only on the tokens and on c_vistos, a buffer drawn from a fixed seed and equal in every
+ * layer; asrn/nucleo.py:610, :691-701, asrn/estable.py:304-321). asrn_ngram_shared_sort sorts the (B, n) rows of
+ * n-gram keys of `tokens` once (workspace: asrn_repetition_workspace_bytes); asrn_layer_forward_ngram is
+ * asrn_layer_forward with that sort given (same tokens, same vistos and c_vistos): it runs only the scans. The
+ * results equal asrn_layer_forward's bit for bit. */
+size_t asrn_ngram_shared_bytes(const asrn_layer_config* cfg);
+int asrn_ngram_shared_sort(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared,
+                           const int64_t* tokens, void* ngram, size_t ngram_bytes, void* workspace,
+                           size_t workspace_bytes, void* stream);
+int asrn_layer_forward_ngram(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared,
+                             const float* E, const float* h, const int64_t* tokens, const void* ngram,
+                             size_t ngram_bytes, float* h_out, void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---- stages (each one seam of the reference; the layer forward runs them in this order) -------------------------- */
 
 /* LN(h) -> Qc, Kc (act, (B, L, cf)), beta (float64), log_alfa (float32); glogit = g(h) (float32); sig (float32). */
