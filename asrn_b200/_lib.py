@@ -106,6 +106,11 @@ _SIGS = {
     'asrn_ngram_shared_sort': (ctypes.c_int, [_P, _P, _P, _P, _P, ctypes.c_size_t, _P, ctypes.c_size_t, _P]),
     'asrn_layer_forward_ngram': (ctypes.c_int, [_P, _P, _P, _P, _P, _P, _P, ctypes.c_size_t, _P, _P, ctypes.c_size_t,
                                                 _P]),
+    'asrn_local_block_workspace_bytes': (ctypes.c_size_t, [ctypes.c_int64, ctypes.c_int64, ctypes.c_int32,
+                                                           ctypes.c_int32]),
+    'asrn_local_block': (ctypes.c_int, [ctypes.c_int64, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                        _P, _P, _P, _P, ctypes.c_float, _P, _P, _P, _P, ctypes.c_float, _P, _P, _P, _P,
+                                        _P, ctypes.c_size_t, _P, _P]),
     'asrn_sampler_seed_state': (ctypes.c_int, [ctypes.c_uint64, _P]),
     'asrn_sampler_jump_poly': (ctypes.c_int, [ctypes.c_uint64, _P]),
     'asrn_sampler_fill': (ctypes.c_int, [ctypes.c_int64, ctypes.c_int64, ctypes.c_int32, _P, _P, _P, _P, _P]),

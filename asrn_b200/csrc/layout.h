@@ -263,6 +263,12 @@ bool make_tmap_f32(void* map /* CUtensorMap */, const void* base, uint64_t inner
 // The same with the 128-byte shared-memory swizzle (box_inner = 32 fp32).
 bool make_tmap_f32_sw128(void* map /* CUtensorMap */, const void* base, uint64_t inner, uint64_t outer,
                          uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer);
+// 3-D maps over row-major (d2, d1, d0) tensors (innermost d0), boxes box0 x box1 x 1, 128-byte swizzle; a box reaching
+// outside [0, d1) of its sequence reads zeros there.
+bool make_tmap_bf16_3d(void* map /* CUtensorMap */, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
+                       uint32_t box0, uint32_t box1);
+bool make_tmap_f32_3d_sw128(void* map /* CUtensorMap */, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
+                            uint32_t box0, uint32_t box1);
 // Rows of a bf16 matrix for row gathers: box = one row of box_inner elements, swizzle of `swizzle_bytes` (0, 32, 64
 // or 128; with a swizzle, box_inner * 2 equals it).
 bool make_tmap_rows_bf16(void* map /* CUtensorMap */, const void* base, uint64_t inner, uint64_t outer,

@@ -86,6 +86,37 @@ bool make_tmap_f32_sw128(void* map, const void* base, uint64_t inner, uint64_t o
   return r == CUDA_SUCCESS;
 }
 
+// Row-major bf16 tensor (d2, d1, d0) as a 3-D map (innermost d0), boxes of box0 x box1 x 1 with the 128-byte swizzle:
+// per-sequence rows, so a box that starts before row 0 or runs past row d1 - 1 of its sequence reads zeros there.
+bool make_tmap_bf16_3d(void* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint32_t box0,
+                       uint32_t box1) {
+  PFN_cuTensorMapEncodeTiled_v12000 fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[3] = {d0, d1, d2};
+  cuuint64_t strides[2] = {d0 * 2, d0 * d1 * 2};
+  cuuint32_t box[3] = {box0, box1, 1};
+  cuuint32_t elem[3] = {1, 1, 1};
+  CUresult r = fn(reinterpret_cast<CUtensorMap*>(map), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base),
+                  dims, strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// The same for an fp32 tensor (box0 = 32: 128-byte rows).
+bool make_tmap_f32_3d_sw128(void* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint32_t box0,
+                            uint32_t box1) {
+  PFN_cuTensorMapEncodeTiled_v12000 fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[3] = {d0, d1, d2};
+  cuuint64_t strides[2] = {d0 * 4, d0 * d1 * 4};
+  cuuint32_t box[3] = {box0, box1, 1};
+  cuuint32_t elem[3] = {1, 1, 1};
+  CUresult r = fn(reinterpret_cast<CUtensorMap*>(map), CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void*>(base),
+                  dims, strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 // Test hook (asrn_test_force_cuda_core): 1 routes bf16 work to the CUDA-core kernels for cross-checks. Only that
 // entry point sets it; nothing reads the environment.
 static std::atomic<int> g_force_cuda_core{0};

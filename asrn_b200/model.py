@@ -2,8 +2,9 @@
 blocks -> ln_f -> tied head. Mirror of asrn.nucleo.ModeloASRN / BloqueLocal / crear_modelo
 (asrn/nucleo.py:969-1119) with the same module names (state_dict compatible) and initialisation order.
 
-The local blocks, embedding and head are plain PyTorch (cuDNN / cuBLAS): they are outside the ASRN hot path. The
-ASRN layers are asrn_b200.ASRNLayer (CUDA kernels of libasrn_b200.so).
+The ASRN layers are asrn_b200.ASRNLayer (CUDA kernels of libasrn_b200.so). Under bf16 autocast on CUDA each local
+block runs as the fused asrn_local_block (an LN kernel and three persistent tcgen05 GEMMs with the conv, GELU, bias and
+residual folded in); in fp32 the local blocks, and in every mode the embedding and head, are PyTorch ops.
 """
 import math
 
@@ -35,10 +36,58 @@ class BloqueLocal(nn.Module):
         self.drop = nn.Dropout(dropout)
 
     def forward(self, h):
+        if self._fused_ok(h):
+            return self._fused(h)
         z = self.ln1(h)
         c = F.gelu(self.conv(F.pad(z.transpose(1, 2), (self.k - 1, 0))).transpose(1, 2))
         h = h + self.drop(c)
         return h + self.drop(self.ff(self.ln2(h)))
+
+    def _fused_ok(self, h):
+        """The fused CUDA block (asrn_local_block) serves bf16 autocast on CUDA, fp32 h, no dropout at work, and the
+        widths its tiles take; the fp32 model keeps PyTorch's exact fp32 ops."""
+        if not (h.is_cuda and h.dtype == torch.float32 and h.dim() == 3 and torch.is_autocast_enabled('cuda')
+                and torch.get_autocast_dtype('cuda') == torch.bfloat16):
+            return False
+        if self.training and self.drop.p > 0:
+            return False
+        d, ff = self.conv.in_channels, self.ff[0].out_features
+        return d % 128 == 0 and d <= 1024 and ff % 128 == 0 and self.k <= 16 and not torch.is_grad_enabled()
+
+    def _fused_weights(self, dev):
+        """bf16 copies autocast would make, the conv as a (d, k d) matrix [o][j d + c] (cached per weight version)."""
+        ver = tuple((p.data_ptr(), p._version) for p in self.parameters())
+        hit = getattr(self, '_fused_cache', None)
+        if hit is not None and hit[0] == ver and hit[1] == str(dev):
+            return hit[2]
+        d = self.conv.in_channels
+        w = {'conv': self.conv.weight.detach().permute(0, 2, 1).reshape(d, self.k * d).to(dev, torch.bfloat16)
+                                                            .contiguous(),
+             'w1': self.ff[0].weight.detach().to(dev, torch.bfloat16).contiguous(),
+             'w2': self.ff[2].weight.detach().to(dev, torch.bfloat16).contiguous()}
+        for name, t in (('ln1_w', self.ln1.weight), ('ln1_b', self.ln1.bias), ('bc', self.conv.bias),
+                        ('ln2_w', self.ln2.weight), ('ln2_b', self.ln2.bias), ('b1', self.ff[0].bias),
+                        ('b2', self.ff[2].bias)):
+            w[name] = t.detach().to(dev, torch.float32).contiguous()
+        self._fused_cache = (ver, str(dev), w)
+        return w
+
+    def _fused(self, h):
+        from . import _lib
+        h = h.contiguous()
+        B, L, d = h.shape
+        ff = self.ff[0].out_features
+        w = self._fused_weights(h.device)
+        L_ = _lib.lib()
+        nbytes = L_.asrn_local_block_workspace_bytes(B, L, d, ff)
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=h.device)
+        out = torch.empty_like(h)
+        P = _lib.ptr
+        _lib.check(L_.asrn_local_block(B, L, d, self.k, ff, P(h), P(out), P(w['ln1_w']), P(w['ln1_b']), self.ln1.eps,
+                                       P(w['conv']), P(w['bc']), P(w['ln2_w']), P(w['ln2_b']), self.ln2.eps,
+                                       P(w['w1']), P(w['b1']), P(w['w2']), P(w['b2']), P(ws), nbytes, None,
+                                       _lib.stream_ptr(h.device)), 'asrn_local_block')
+        return out
 
 
 LocalBlock = BloqueLocal

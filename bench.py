@@ -77,8 +77,8 @@ def parse():
     p.add_argument('--batch', type=int, default=B_PER_GPU, help='sequences per GPU')
     p.add_argument('--seq', type=int, default=L_SEQ)
     p.add_argument('--no-cpu-baseline', action='store_true')
-    p.add_argument('--workload', default='cfg3', choices=['cfg3', 'cfg4', 'gen'],
-                   help='cfg3: the batch-sharded layer metric (default); cfg4 / gen: only that leg (for profiling)')
+    p.add_argument('--workload', default='cfg3', choices=['cfg3', 'cfg4', 'gen', 'model'],
+                   help='cfg3: the batch-sharded layer metric (default); cfg4 / gen / model: only that leg (for profiling)')
     p.add_argument('--no-gen', action='store_true', help='skip the generation leg')
     p.add_argument('--no-legs', action='store_true', help='skip the cfg1 / cfg2 / cfg4 legs')
     p.add_argument('--eager', action='store_true', help='time the eager forward instead of its CUDA-graph replay')
@@ -655,6 +655,8 @@ def run_ours(args):
         legs['cfg4'] = leg_cfg4(args, dev, rank, world)
     if args.workload == 'gen':
         legs['generation'] = leg_generation(args, dev, rank, world)
+    if args.workload == 'model':
+        legs['model'] = leg_model(args, dev, rank, world)
     if args.workload == 'cfg3':
         if not args.no_gen:
             legs['generation'] = leg_generation(args, dev, rank, world)
@@ -664,7 +666,7 @@ def run_ours(args):
             legs['model'] = leg_model(args, dev, rank, world)
     if rank == 0:
         if out is None:                       # --workload cfg4 / gen: that leg is the line
-            out = dict(legs.pop('cfg4' if args.workload == 'cfg4' else 'generation'))
+            out = dict(legs.pop({'cfg4': 'cfg4', 'gen': 'generation', 'model': 'model'}[args.workload]))
         out.update({k: v for k, v in legs.items() if v is not None})
         print(json.dumps(out), flush=True)
     if world > 1:
@@ -847,12 +849,13 @@ MODEL_B = 4
 def leg_model(args, dev, rank, world):
     """The cfg3 model forward on one GPU (rank 0; the other ranks skip it): create_model(V=50304, d=768, n_capas=12)
     (6 ASRN layers, 12 local blocks, tied head) random init, MODEL_B x 8192 Zipf+repeat tokens, bf16 autocast, the
-    whole forward replayed as one CUDA graph; also with each ASRN layer sorting the n-grams itself (the reference's
-    order of work) to show what the shared sort saves."""
+    whole forward replayed as one CUDA graph. Also timed: each ASRN layer sorting the n-grams itself, and the local
+    blocks as PyTorch ops, to show what the shared sort and the fused blocks save."""
     import torch
     import asrn_b200
     from asrn_b200 import synthetic
-    vals = [0.0, 0.0]
+    from asrn_b200.model import BloqueLocal
+    vals = [0.0, 0.0, 0.0]
     mode = None
     if rank == 0:
         m = asrn_b200.create_model(V=V, d=D, n_capas=12, semilla=0).to(dev).eval()
@@ -862,23 +865,32 @@ def leg_model(args, dev, rank, world):
             with torch.no_grad(), torch.autocast('cuda', dtype=torch.bfloat16):
                 return m(x)
 
-        for i, shared in enumerate((True, False)):
-            m._ngram_shared = (lambda ok: (lambda: ok))(shared)    # sort once, or in every layer
-            warm_up(step, args.warmup, 1)
-            run, mode, graph = graph_or_eager(step, args.eager)
-            ms, _ = timed(run, max(3, args.steps // 4))
-            vals[i] = ms / max(3, args.steps // 4)
-            del run, graph
+        fused_ok = BloqueLocal._fused_ok
+        for i, (shared, fused) in enumerate(((True, True), (False, True), (True, False))):
+            m._ngram_shared = (lambda ok: (lambda: ok))(shared)        # sort once, or in every layer
+            BloqueLocal._fused_ok = fused_ok if fused else (lambda self, h: False)
+            try:
+                warm_up(step, args.warmup, 1)
+                run, mode_i, graph = graph_or_eager(step, args.eager)
+                n = max(3, args.steps // 4)
+                ms, _ = timed(run, n)
+                vals[i] = ms / n
+                mode = mode or mode_i
+                del run, graph
+            finally:
+                BloqueLocal._fused_ok = fused_ok
         del m
         torch.cuda.empty_cache()
     if rank != 0:
         return None
     tokens = MODEL_B * L_SEQ
     return {'metric': 'model_fwd_tokens_per_s', 'value': tokens / (vals[0] * 1e-3), 'unit': 'tokens/s',
-            'forward_ms': vals[0], 'forward_ms_sorting_in_every_layer': vals[1], 'dtype': 'bf16', 'launch': mode,
+            'forward_ms': vals[0], 'forward_ms_sorting_in_every_layer': vals[1],
+            'forward_ms_pytorch_local_blocks': vals[2], 'dtype': 'bf16', 'launch': mode,
             'config': {'workload': 'cfg3 model: create_model(V=50304, d=768, n_capas=12) random init, forward on '
                                    '%d x %d Zipf+repeat tokens, bf16 autocast (logits included)' % (MODEL_B, L_SEQ),
-                       'ngram_sort': 'once per forward, shared by the 6 ASRN layers'}}
+                       'ngram_sort': 'once per forward, shared by the 6 ASRN layers',
+                       'local_blocks': 'fused (asrn_local_block: LN kernel + three tcgen05 GEMMs)'}}
 
 
 def leg_generation(args, dev, rank, world):

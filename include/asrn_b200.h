@@ -184,6 +184,21 @@ int asrn_local_mid(int64_t B, int32_t d, const float* h, const void* z, float* h
                    const float* ln_b, float eps, void* v_out, int32_t half, void* stream);
 int asrn_local_gelu(int64_t n, void* f, int32_t half, void* stream);
 
+/* ---- local block of the model over whole sequences, bfloat16 autocast (BloqueLocal.forward, asrn/nucleo.py:969-1014,
+ * mezcla='conv') -------------------------------------------------------------------------------------------------------
+ * h_out = h1 + bf16(W2 gelu(bf16(W1 LN2(h1) + b1)) + b2), h1 = h + gelu(bf16(bf16(conv_k(pad(LN1(h)))) + b_conv)),
+ * with autocast's bf16 operands and roundings. h, h_out: (B, L, d) fp32 (h_out may not alias h). w_conv: bf16
+ * (d, k * d), element [o][j * d + c] = conv.weight[o][c][j] (tap j reads position t - (k - 1) + j); w1: bf16 (ff, d);
+ * w2: bf16 (d, ff); LayerNorm weights and biases fp32 (biases are rounded to bf16 as autocast does). d a multiple of
+ * 128 and at most 1024, ff a multiple of 128 (else ASRN_ERR_UNSUPPORTED). status: device int for the bounded waits
+ * (may be null). Workspace: asrn_local_block_workspace_bytes. */
+size_t asrn_local_block_workspace_bytes(int64_t B, int64_t L, int32_t d, int32_t ff);
+int asrn_local_block(int64_t B, int64_t L, int32_t d, int32_t k, int32_t ff, const float* h, float* h_out,
+                     const float* ln1_w, const float* ln1_b, float eps1, const void* w_conv, const float* b_conv,
+                     const float* ln2_w, const float* ln2_b, float eps2, const void* w1, const float* b1,
+                     const void* w2, const float* b2, void* workspace, size_t workspace_bytes, int* status,
+                     void* stream);
+
 /* ---- sequence-chunk sharding (one long sequence over several GPUs) --------------------------------------------------
  * Shard r of `world` owns positions [c0, c0 + Lc) of every sequence (L = world * Lc). Its sorted rows hold its own
  * slots and, before each bucket's local run, the up to C earlier-chunk slots some local query has as a candidate (the
