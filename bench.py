@@ -77,8 +77,9 @@ def parse():
     p.add_argument('--batch', type=int, default=B_PER_GPU, help='sequences per GPU')
     p.add_argument('--seq', type=int, default=L_SEQ)
     p.add_argument('--no-cpu-baseline', action='store_true')
-    p.add_argument('--workload', default='cfg3', choices=['cfg3', 'cfg4', 'gen', 'model'],
-                   help='cfg3: the batch-sharded layer metric (default); cfg4 / gen / model: only that leg (for profiling)')
+    p.add_argument('--workload', default='cfg3', choices=['cfg3', 'cfg4', 'gen', 'model', 'localblock'],
+                   help='cfg3: the batch-sharded layer metric (default); cfg4 / gen / model / localblock: only that '
+                        'leg (for profiling)')
     p.add_argument('--no-gen', action='store_true', help='skip the generation leg')
     p.add_argument('--no-legs', action='store_true', help='skip the cfg1 / cfg2 / cfg4 legs')
     p.add_argument('--eager', action='store_true', help='time the eager forward instead of its CUDA-graph replay')
@@ -657,6 +658,8 @@ def run_ours(args):
         legs['generation'] = leg_generation(args, dev, rank, world)
     if args.workload == 'model':
         legs['model'] = leg_model(args, dev, rank, world)
+    if args.workload == 'localblock':
+        legs['localblock'] = leg_localblock(args, dev, rank, world)
     if args.workload == 'cfg3':
         if not args.no_gen:
             legs['generation'] = leg_generation(args, dev, rank, world)
@@ -666,7 +669,8 @@ def run_ours(args):
             legs['model'] = leg_model(args, dev, rank, world)
     if rank == 0:
         if out is None:                       # --workload cfg4 / gen: that leg is the line
-            out = dict(legs.pop({'cfg4': 'cfg4', 'gen': 'generation', 'model': 'model'}[args.workload]))
+            out = dict(legs.pop({'cfg4': 'cfg4', 'gen': 'generation', 'model': 'model',
+                                 'localblock': 'localblock'}[args.workload]))
         out.update({k: v for k, v in legs.items() if v is not None})
         print(json.dumps(out), flush=True)
     if world > 1:
@@ -891,6 +895,48 @@ def leg_model(args, dev, rank, world):
                                    '%d x %d Zipf+repeat tokens, bf16 autocast (logits included)' % (MODEL_B, L_SEQ),
                        'ngram_sort': 'once per forward, shared by the 6 ASRN layers',
                        'local_blocks': 'fused (asrn_local_block: LN kernel + three tcgen05 GEMMs)'}}
+
+
+LB_B = 8
+LB_BYTES_PER_TOKEN = 4 * 768 * 6 + 2 * 768 * 4 + 2 * 1536 * 2      # fp32 stream 4 reads + 2 writes, bf16 z/u, f
+
+
+def leg_localblock(args, dev, rank, world):
+    """One cfg3 local block (BloqueLocal(768), k = 4, ff = 1536) on LB_B x 8192 tokens under bf16 autocast, fused
+    (asrn_local_block) and as PyTorch ops; roofline on the fused block's HBM bytes (the fp32 residual stream read four
+    times and written twice, the bf16 z / u / f intermediates written and read once)."""
+    import torch
+    from asrn_b200.model import BloqueLocal
+    torch.manual_seed(0)
+    blq = BloqueLocal(D, 4, 2 * D).to(dev).eval()
+    h = torch.randn(LB_B, L_SEQ, D, device=dev)
+    res = []
+
+    def step():
+        with torch.no_grad(), torch.autocast('cuda', dtype=torch.bfloat16):
+            return blq(h)
+
+    fused_ok = BloqueLocal._fused_ok
+    for fused in (True, False):
+        BloqueLocal._fused_ok = fused_ok if fused else (lambda self, x: False)
+        try:
+            warm_up(step, args.warmup, 1)
+            run, mode, graph = graph_or_eager(step, args.eager)
+            ms, _ = timed(run, args.steps)
+            res.append(ms / args.steps)
+            del run, graph
+        finally:
+            BloqueLocal._fused_ok = fused_ok
+    if rank != 0:
+        return None
+    hbm, src = peaks()
+    tokens = LB_B * L_SEQ
+    achieved = LB_BYTES_PER_TOKEN * tokens / (res[0] * 1e-3) / 1e9
+    return {'metric': 'local_block_tokens_per_s', 'value': tokens / (res[0] * 1e-3), 'unit': 'tokens/s',
+            'ms_per_step': res[0], 'pytorch_ms_per_step': res[1], 'dtype': 'bf16', 'launch': mode,
+            'config': {'workload': 'BloqueLocal(768, k=4, ff=1536), %d x %d tokens, bf16 autocast' % (LB_B, L_SEQ)},
+            'roofline': {'bound': 'hbm', 'achieved': achieved, 'peak': hbm, 'peak_source': src, 'unit': 'GB/s',
+                         'frac': achieved / hbm, 'algorithmic_bytes_per_token': LB_BYTES_PER_TOKEN}}
 
 
 def leg_generation(args, dev, rank, world):
