@@ -12,8 +12,9 @@
 //   k_local_gemm<1>    f = gelu(bf16(u . W1^T + b1)) (bf16)
 //   k_local_gemm<2>    h' = h1 + bf16(f . W2^T + b2)
 // Each GEMM is the persistent tcgen05 pipeline of the gate (one block per SM over 128-token x NT-column tiles, a TMA
-// producer warp for both operands through three stages, an MMA warp filling one of two TMEM accumulators, a TMA warp
-// staging the fp32 residual rows, eight epilogue warps draining the other accumulator). Per token and block the HBM
+// producer warp for both operands through four stages of 16 + NT / 8 KB, an MMA warp filling one of two TMEM
+// accumulators, a TMA warp staging the fp32 residual rows through two 16 KB slots, eight epilogue warps draining the
+// other accumulator). Per token and block the HBM
 // traffic is about 31 KB (the fp32 residual stream read four times and written twice, the bf16 intermediates once each
 // way), against about 90 KB for the PyTorch sequence.
 #include "common.cuh"
@@ -36,9 +37,9 @@ struct LocalGemmArgs {
 namespace {
 constexpr int kLTM = 128, kLBK = 64;
 constexpr int kLStageA = kLTM * 128;
-constexpr int kLStages = 3;
+constexpr int kLStages = 4;
 constexpr int kLEpiWarps = 8;
-constexpr int kLHSlots = 4;
+constexpr int kLHSlots = 2;
 constexpr int kLHTile = kLTM * 128;
 constexpr int kLThreads = (3 + kLEpiWarps) * 32;
 constexpr int kLnThreads = 256;
@@ -231,9 +232,15 @@ k_local_gemm(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__
         float v[32];
         tmem_ld32(trow + (uint32_t)(acc * NT + ch * 32), v);
         // the bias as autocast passes it (bf16), then the mode's rounding chain
+        float bias[32];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float4 b4 = __ldg(reinterpret_cast<const float4*>(a.bias + c0) + i);
+          bias[4 * i] = b4.x; bias[4 * i + 1] = b4.y; bias[4 * i + 2] = b4.z; bias[4 * i + 3] = b4.w;
+        }
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          const float bb = round_bf16(__ldg(a.bias + c0 + i));
+          const float bb = round_bf16(bias[i]);
           if (Mode == 0) v[i] = round_bf16(gelu_f(round_bf16(__fadd_rn(round_bf16(v[i]), bb))));
           else if (Mode == 1) v[i] = gelu_f(round_bf16(__fadd_rn(v[i], bb)));
           else v[i] = round_bf16(__fadd_rn(v[i], bb));
