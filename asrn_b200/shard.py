@@ -10,8 +10,12 @@ sequence (L = world * Lc, equal chunks) and computes h' for them:
                     bucket's tail, its last <= C positions (asrn_shard_tails)
   exchange (NCCL)   (1) the halo rows, (2) per sequence the chunk's sum of beta (fp64): rank r's clock is the
                     exclusive sum of the earlier chunks plus its own cumulative sum (asrn/estable.py:418),
-                    (3) the bucket tails, (4) the per-position features (phi, Qc, Kc, signature, clock, beta,
-                    log_alfa, bf16 rows of E): all-gathers over NVLink; afterwards every rank holds them for all L
+                    (3) the bucket tails, (4) the per-position scalars (signature, clock, beta, log_alfa) of all L
+                    positions, (5) the feature rows (phi, Qc, Kc) and value rows (bf16 E of the next position) of
+                    only the positions in each rank's tails: a later rank's rows hold no other earlier-chunk position,
+                    so the rows every rank receives shrink from all L positions to the union of the tails, plus the
+                    first bf16 E row of every chunk (the value row of the chunk before's last position); all-gathers
+                    over NVLink
   phase 2 (local)   the shard's own rows: for every bucket with local slots its exclusive ring -- the C most recent
                     earlier-chunk positions, from the earlier ranks' tails -- then its local run (asrn_shard_merge);
                     candidate scoring of the local queries (asrn_score_shard); the n-gram memory over the full
@@ -37,6 +41,92 @@ from . import _lib, stages
 from .layer import compute_half, ctypes_ref
 
 _SEQ_KEYS = ('phi', 'Qc', 'Kc', 'sig', 'log_alfa', 'beta', 'Bt', 'Ea')
+_SCALAR_KEYS = ('sig', 'log_alfa', 'beta', 'Bt')      # gathered for every position (24 B each)
+last_exchange = {}    # this rank's last compact row exchange: rows sent, padded rows per rank, rows in the chunk
+_ROW_KEYS = ('phi', 'Qc', 'Kc')                       # gathered only for the positions in the tails
+
+
+def tail_index(tails, c0, Lc, B, T):
+    """Local flat indices b * Lc + (p - c0), ascending, of the positions p of this chunk that appear in its bucket
+    tails (rows b * T + tau): the only positions of the chunk that a later shard's rows hold."""
+    dev = tails.device
+    rows, _, C1 = tails.shape
+    C = C1 - 1
+    cnt = tails[..., 0].long().clamp(0, C)
+    valid = torch.arange(C, device=dev) < cnt.unsqueeze(-1)
+    rel = torch.where(valid, tails[..., 1:].long() - c0, Lc).clamp(0, Lc)
+    b = (torch.arange(rows, device=dev) // T).view(rows, 1, 1)
+    flags = torch.zeros(B * (Lc + 1), dtype=torch.bool, device=dev)
+    flags[(b * (Lc + 1) + rel).view(-1)] = True
+    return flags.view(B, Lc + 1)[:, :Lc].reshape(-1).nonzero().squeeze(1)
+
+
+def compact_tails(tails):
+    """The non-empty bucket tails of a chunk: flat indices row * 2^nb + bucket (int64) and their (count, positions)
+    entries as raw bytes (n, (C + 1) * 4). In the heavy regime few buckets are used, so this is far smaller than the
+    dense (rows, 2^nb, C + 1) array the merge kernel reads."""
+    flat = tails.reshape(-1, tails.shape[-1])
+    nz = (flat[:, 0] != 0).nonzero().squeeze(1)
+    return flat[nz].contiguous().view(torch.uint8), nz
+
+
+def expand_tails(ent_all, idx_all, shape):
+    """(world, m, bytes) entries and (world, m) indices (-1 = padding) -> dense (world,) + shape int32 tails, zeros
+    (empty tails) elsewhere."""
+    world = ent_all.shape[0]
+    dense = torch.zeros((world,) + tuple(shape), dtype=torch.int32, device=ent_all.device)
+    for q in range(world):
+        keep = idx_all[q] >= 0
+        rows = ent_all[q][keep].contiguous().view(torch.int32).view(-1, shape[-1])
+        dense[q].view(-1, shape[-1]).index_copy_(0, idx_all[q][keep], rows)
+    return dense
+
+
+def _row_payload(loc, sel, Ea_next):
+    """(n, row bytes) uint8: for each selected local position its phi, Qc and Kc rows and the bf16 E row of the
+    next position (its value row), as raw bytes."""
+    parts = []
+    for k in _ROW_KEYS:
+        x = loc[k]
+        parts.append(x.reshape(-1, x.shape[-1])[sel].contiguous().view(torch.uint8))
+    parts.append(Ea_next.reshape(-1, Ea_next.shape[-1])[sel].contiguous().view(torch.uint8))
+    return torch.cat(parts, 1)
+
+
+def _row_widths(loc, Ea_next):
+    return [loc[k].shape[-1] * loc[k].element_size() for k in _ROW_KEYS] + \
+        [Ea_next.shape[-1] * Ea_next.element_size()]
+
+
+def _full_rows(loc, B, L, c0, c1, Ea_first_next):
+    """Zero-filled (B, L, .) feature tensors holding this chunk's own rows and, at c1, the next chunk's first value
+    row; the earlier chunks' rows are scattered in by _scatter_rows."""
+    full = {}
+    for k in _ROW_KEYS + ('Ea',):
+        x = loc[k]
+        t = torch.zeros((B, L) + tuple(x.shape[2:]), dtype=x.dtype, device=x.device)
+        t[:, c0:c1] = x
+        full[k] = t
+    if Ea_first_next is not None and c1 < L:
+        full['Ea'][:, c1] = Ea_first_next
+    return full
+
+
+def _scatter_rows(full, payload, gidx, widths, L):
+    """Rows of another chunk (payload (n, bytes), global flat indices b * L + p, -1 = padding) into full: phi, Qc, Kc
+    at p, the value row at p + 1 (where the scoring kernel reads the value of key p)."""
+    keep = gidx >= 0
+    gidx, payload = gidx[keep], payload[keep]
+    off = 0
+    for k, w in zip(_ROW_KEYS + ('Ea',), widths):
+        t = full[k]
+        rows = payload[:, off:off + w].contiguous().view(t.dtype).view(-1, t.shape[-1])
+        dst = gidx + 1 if k == 'Ea' else gidx
+        if k == 'Ea':                                   # the value row of the sequence's last position is unused
+            ok = (dst % L) != 0
+            dst, rows = dst[ok], rows[ok]
+        t.view(-1, t.shape[-1]).index_copy_(0, dst, rows)
+        off += w
 
 
 class ShardExchangeError(RuntimeError):
@@ -299,11 +389,27 @@ def forward_emulated(layer, E, h, tokens, world):
         halo = E[:, c0 - 1] if c0 > 0 else torch.zeros(B, d, device=E.device)
         locs.append(_phase1(layer, E[:, c0:c1].contiguous(), h[:, c0:c1].contiguous(),
                             None if tokens is None else tokens[:, c0:c1].contiguous(), halo, half, c0))
-    full = {k: torch.cat([lc[k] for lc in locs], 1) for k in _SEQ_KEYS}
-    tails = torch.stack([lc['tails'] for lc in locs], 0)
+    full = {k: torch.cat([lc[k] for lc in locs], 1) for k in _SCALAR_KEYS}
+    packed = [compact_tails(lc['tails']) for lc in locs]          # the exchanged form of the tails
+    m = max(1, max(ix.numel() for _, ix in packed))
+    ent_all = torch.zeros(world, m, packed[0][0].shape[1], dtype=torch.uint8, device=E.device)
+    idx_all = torch.full((world, m), -1, dtype=torch.int64, device=E.device)
+    for q, (ent, ix) in enumerate(packed):
+        ent_all[q, :ix.numel()] = ent
+        idx_all[q, :ix.numel()] = ix
+    tails = expand_tails(ent_all, idx_all, locs[0]['tails'].shape)
     sums = torch.stack([lc['Bt'][:, -1] for lc in locs], 0)
     _apply_clock_offsets(full['Bt'], sums, L // world)
     Lc = L // world
+    # the compact row exchange: each chunk publishes the rows of its tail positions; rank r sees the earlier ranks'
+    T = layer.n_tablas
+    pubs = []
+    for r, (c0, c1) in enumerate(bounds):
+        nxt = locs[r + 1]['Ea'][:, :1] if r + 1 < world else torch.zeros_like(locs[r]['Ea'][:, :1])
+        Ea_next = torch.cat([locs[r]['Ea'][:, 1:], nxt], 1)
+        sel = tail_index(locs[r]['tails'], c0, Lc, B, T)
+        gidx = (sel // Lc) * L + c0 + sel % Lc
+        pubs.append((_row_payload(locs[r], sel, Ea_next), gidx, _row_widths(locs[r], Ea_next)))
     ngs = [ngram_sort(layer, full, c0, Lc, half) for c0, _ in bounds]
     keys = torch.stack([g['keys'] for g in ngs], 0)
     summ = torch.stack([g['summ'] for g in ngs], 0)
@@ -315,7 +421,11 @@ def forward_emulated(layer, E, h, tokens, world):
     for r, (lc, (c0, c1)) in enumerate(zip(locs, bounds)):
         vistos, hawkes = vh[r]
         racha, _ = racha_chunk(layer, vistos, lc['beta'], racha_before(maps, r), half)
-        outs.append(_phase2(layer, lc, full, tails[:r] if r > 0 else None, (vistos, hawkes, racha),
+        fr = dict(full)
+        fr.update(_full_rows(lc, B, L, c0, c1, locs[r + 1]['Ea'][:, 0] if r + 1 < world else None))
+        for q in range(r):
+            _scatter_rows(fr, pubs[q][0], pubs[q][1], pubs[q][2], L)
+        outs.append(_phase2(layer, lc, fr, tails[:r] if r > 0 else None, (vistos, hawkes, racha),
                             h[:, c0:c1].contiguous(), c0, c1, half))
     return torch.cat(outs, 1)
 
@@ -335,25 +445,50 @@ def _gather_seq(x, world, group):
     return torch.cat([p.view(dt).view(x.shape) for p in parts], 1)
 
 
-def _gather_seq_async(x, world, group):
-    """_gather_seq issued without waiting: (gathered tensor, finish) where finish() makes the current stream wait for
-    the collective (no host synchronisation)."""
+def exchange_first_rows(first, world, group=None):
+    """(B, d) bf16 E of this chunk's first position -> (world, B, d): every chunk's, in rank order."""
     import torch.distributed as dist
-    x = x.contiguous()
-    dt = x.dtype
-    xb = x.view(-1).view(torch.uint8)
-    if x.shape[0] == 1:
-        out = torch.empty(world * xb.numel(), dtype=torch.uint8, device=x.device)
-        work = dist.all_gather_into_tensor(out, xb, group=group, async_op=True)
-        return out.view(dt).view((1, world * x.shape[1]) + tuple(x.shape[2:])), work.wait
-    parts = [torch.empty_like(xb) for _ in range(world)]
-    work = dist.all_gather(parts, xb, group=group, async_op=True)
-    holder = {}
+    x = first.contiguous()
+    flat = torch.empty((world,) + tuple(x.shape), dtype=x.dtype, device=x.device)
+    dist.all_gather_into_tensor(flat.view(-1).view(torch.uint8), x.view(-1).view(torch.uint8), group=group)
+    return flat
+
+
+def exchange_varlen_async(items, world, group=None):
+    """Variable-length exchange of several items, each this rank's (n, bytes) uint8 payload and (n,) int64 indices:
+    returns per item (payloads (world, m, bytes), indices (world, m)) padded to the largest n of any rank (index -1
+    marks padding), and finish(), which makes the current stream wait for the collectives. The counts of all items go
+    in one small all-gather that the host reads (the padded sizes must be known to allocate); the rest is issued
+    without waiting."""
+    import torch.distributed as dist
+    dev = items[0][0].device
+    n = torch.tensor([p.shape[0] for p, _ in items], dtype=torch.int64, device=dev)
+    counts = torch.empty(world, len(items), dtype=torch.int64, device=dev)
+    dist.all_gather_into_tensor(counts.view(-1), n, group=group)
+    ms = [max(1, int(m)) for m in counts.max(0).values.tolist()]
+    out, works = [], []
+    for (payload, gidx), m in zip(items, ms):
+        pad = torch.zeros(m, payload.shape[1], dtype=torch.uint8, device=dev)
+        pad[:payload.shape[0]] = payload
+        idx = torch.full((m,), -1, dtype=torch.int64, device=dev)
+        idx[:gidx.shape[0]] = gidx
+        pay_all = torch.empty(world, m, payload.shape[1], dtype=torch.uint8, device=dev)
+        idx_all = torch.empty(world, m, dtype=torch.int64, device=dev)
+        works.append(dist.all_gather_into_tensor(pay_all.view(-1), pad.view(-1), group=group, async_op=True))
+        works.append(dist.all_gather_into_tensor(idx_all.view(-1), idx, group=group, async_op=True))
+        out.append((pay_all, idx_all))
 
     def finish():
-        work.wait()
-        holder['t'] = torch.cat([q.view(dt).view(x.shape) for q in parts], 1)
-    return holder, finish
+        for w in works:
+            w.wait()
+    return out, finish
+
+
+def exchange_rows_async(payload, gidx, world, group=None):
+    """exchange_varlen_async of one item: (payloads (world, m, bytes), indices (world, m), finish)."""
+    parts, finish = exchange_varlen_async([(payload, gidx)], world, group)
+    pay_all, idx_all = parts[0]
+    return pay_all, idx_all, finish
 
 
 def exchange_halo(last, world, rank, group=None):
@@ -422,17 +557,30 @@ def forward(layer, E, h, tokens=None, group=None):
     loc = _phase1(layer, E, h, tokens, halo, half, c0)
     # (2) chunk sums of beta (= the last local clock value) -> clock offsets
     sums = exchange_chunk_sums(loc['Bt'][:, -1], world, group)
-    # (3) bucket tails, (4) features of every position: the per-position scalars first; the feature rows (phi, Qc,
-    # Kc, the bf16 rows of E) are gathered while the n-gram memory sorts its chunk
-    tails = exchange_tails(loc['tails'], world, group)
-    full = {k: _gather_seq(loc[k], world, group) for k in ('sig', 'log_alfa', 'beta', 'Bt')}
-    pending = {k: _gather_seq_async(loc[k], world, group) for k in ('phi', 'Qc', 'Kc', 'Ea')}
+    # (3) bucket tails, (4) the per-position scalars of every position, (5) the feature and value rows of the tail
+    # positions only (gathered while the n-gram memory sorts its chunk)
+    full = {k: _gather_seq(loc[k], world, group) for k in _SCALAR_KEYS}
+    firsts = exchange_first_rows(loc['Ea'][:, 0], world, group)
+    nxt = firsts[rank + 1].unsqueeze(1) if rank + 1 < world else torch.zeros_like(loc['Ea'][:, :1])
+    Ea_next = torch.cat([loc['Ea'][:, 1:], nxt], 1)
+    sel = tail_index(loc['tails'], c0, Lc, B, layer.n_tablas)
+    payload = _row_payload(loc, sel, Ea_next)
+    gidx = (sel // Lc) * L + c0 + sel % Lc
+    widths = _row_widths(loc, Ea_next)
+    t_ent, t_idx = compact_tails(loc['tails'])
+    ((ent_all, tidx_all), (pay_all, gidx_all)), finish = exchange_varlen_async([(t_ent, t_idx), (payload, gidx)],
+                                                                                world, group)
+    last_exchange.update(rows_sent=int(payload.shape[0]), rows_padded=int(pay_all.shape[1]), rows_chunk=B * Lc,
+                         row_bytes=int(payload.shape[1]), tails_sent=int(t_idx.shape[0]),
+                         tails_padded=int(tidx_all.shape[1]), tails_dense=int(loc['tails'][..., 0].numel()))
     _apply_clock_offsets(full['Bt'], sums, Lc)
-    # (5) n-gram memory: per-group summaries of every chunk, then the streak maps
+    # (6) n-gram memory: per-group summaries of every chunk, then the streak maps
     ng = ngram_sort(layer, full, c0, Lc, half)
-    for k, (t, finish) in pending.items():
-        finish()
-        full[k] = t['t'] if isinstance(t, dict) else t
+    full.update(_full_rows(loc, B, L, c0, c1, firsts[rank + 1] if rank + 1 < world else None))
+    finish()
+    for q in range(rank):
+        _scatter_rows(full, pay_all[q], gidx_all[q], widths, L)
+    tails = expand_tails(ent_all[:rank], tidx_all[:rank], loc['tails'].shape) if rank > 0 else None
     keys, summ = exchange_ngram(ng['keys'], ng['summ'], world, group)
     vistos, hawkes = ngram_finish(layer, full, ng, keys[:rank] if rank > 0 else None,
                                   summ[:rank] if rank > 0 else None, c0, Lc, half)
@@ -441,7 +589,7 @@ def forward(layer, E, h, tokens=None, group=None):
     racha, _ = racha_chunk(layer, vistos, loc['beta'], racha_before(maps, rank), half)
     status = carry_violations(sums=sums, maps=maps, keys=keys).clamp(max=1).to(torch.int32).mul(
         _lib.ASRN_ERR_DATA).view(1)
-    out = _phase2(layer, loc, full, tails[:rank] if rank > 0 else None, (vistos, hawkes, racha), h, c0, c1, half,
+    out = _phase2(layer, loc, full, tails, (vistos, hawkes, racha), h, c0, c1, half,
                   status)
     _defer_status(status)
     return out

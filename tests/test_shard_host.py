@@ -73,6 +73,12 @@ def _rank(rank, world, port, out):
         summ = torch.full((2, 3, 32), rank + 1, dtype=torch.uint8)
         res['ng'] = shard.exchange_ngram(keys, summ, world, None)
         res['maps'] = shard.exchange_racha_maps(torch.tensor([[0.5, 1.0 + rank]]), world, None)
+        n = 2 + rank                                          # ranks publish different numbers of rows
+        payload = (torch.arange(n * 6).view(n, 6) + 100 * rank).to(torch.uint8)
+        pay_all, idx_all, finish = shard.exchange_rows_async(payload, torch.arange(n) * 10 + rank, world, None)
+        finish()
+        res['rows'] = (pay_all, idx_all)
+        res['firsts'] = shard.exchange_first_rows(torch.full((2, 4), float(rank + 1)).to(torch.bfloat16), world, None)
         torch.save(res, os.path.join(out, f'rank{rank}.pt'))
     finally:
         dist.destroy_process_group()
@@ -96,6 +102,11 @@ def test_exchange_steps_with_two_gloo_ranks(tmp_path):
         assert torch.equal(r['ng'][0], torch.stack([k0, k0 + 10], 0))
         assert (r['ng'][1][0] == 1).all() and (r['ng'][1][1] == 2).all()
         assert torch.equal(r['maps'], torch.tensor([[[0.5, 1.0]], [[0.5, 2.0]]]))
+        pay_all, idx_all = r['rows']
+        assert pay_all.shape == (2, 3, 6) and idx_all.tolist() == [[0, 10, -1], [1, 11, 21]]
+        assert torch.equal(pay_all[0, :2], torch.arange(12).view(2, 6).to(torch.uint8))
+        assert torch.equal(pay_all[1], (torch.arange(18).view(3, 6) + 100).to(torch.uint8))
+        assert torch.equal(r['firsts'].float(), torch.stack([torch.full((2, 4), 1.0), torch.full((2, 4), 2.0)]))
 
 
 # ---- failure detection of the exchange (host-side faults on gloo ranks; no GPU involved) -----------------------------
@@ -226,3 +237,63 @@ def test_exchange_reports_a_rank_that_left_between_steps(tmp_path):
     assert res[1][0] == 'left'
     assert res[0][0].startswith('error:')
     assert res[0][1] < 5 * 3
+
+
+# ---- the compact row exchange (host logic of shard.tail_index / _row_payload / _scatter_rows) ------------------------
+
+def test_tail_index_lists_each_tail_position_once():
+    from asrn_b200 import shard
+    B, T, nb, C, Lc, c0 = 2, 3, 3, 4, 10, 20
+    tails = torch.zeros(B * T, 1 << nb, C + 1, dtype=torch.int32)
+    tails[0, 1, 0] = 2
+    tails[0, 1, 1:3] = torch.tensor([c0 + 3, c0 + 7])
+    tails[2, 4, 0] = 3                                   # the same sequence (row 2 -> b = 0), one position repeated
+    tails[2, 4, 1:4] = torch.tensor([c0 + 1, c0 + 3, c0 + 9])
+    tails[4, 5, 0] = 1                                   # row 4 -> b = 1
+    tails[4, 5, 1] = c0 + 9
+    tails[5, 6, 1:] = c0 + 5                             # count 0: these entries are not part of the tail
+    assert shard.tail_index(tails, c0, Lc, B, T).tolist() == [1, 3, 7, 9, 19]
+
+
+def test_scattered_rows_land_at_the_key_and_the_value_after_it():
+    """A published row of position p fills phi / Qc / Kc at p and the value row (E of p + 1) at p + 1, as the scoring
+    kernel reads them; the value row of a sequence's last position is dropped."""
+    from asrn_b200 import shard
+    B, Lc, L, c0, d, P, cf = 1, 4, 8, 0, 4, 3, 2
+    loc = {'phi': torch.arange(B * Lc * P, dtype=torch.float32).view(B, Lc, P).to(torch.bfloat16),
+           'Qc': torch.ones(B, Lc, cf, dtype=torch.bfloat16), 'Kc': torch.full((B, Lc, cf), 2.0).to(torch.bfloat16),
+           'Ea': (torch.arange(B * Lc * d, dtype=torch.float32).view(B, Lc, d) + 100).to(torch.bfloat16)}
+    nxt = torch.full((B, 1, d), 7.0).to(torch.bfloat16)   # the next chunk's first row
+    Ea_next = torch.cat([loc['Ea'][:, 1:], nxt], 1)
+    sel = torch.tensor([1, 3])
+    payload = shard._row_payload(loc, sel, Ea_next)
+    widths = shard._row_widths(loc, Ea_next)
+    full = {k: torch.zeros((B, L) + tuple(loc[k].shape[2:]), dtype=torch.bfloat16) for k in ('phi', 'Qc', 'Kc', 'Ea')}
+    padded = torch.cat([payload, torch.zeros_like(payload[:1])])          # a padding row, index -1
+    shard._scatter_rows(full, padded, torch.tensor([1, 3, -1]), widths, L)
+    assert torch.equal(full['phi'][0, 1], loc['phi'][0, 1]) and torch.equal(full['phi'][0, 3], loc['phi'][0, 3])
+    assert torch.equal(full['Kc'][0, 3], loc['Kc'][0, 3]) and full['phi'][0, 2].abs().sum() == 0
+    assert torch.equal(full['Ea'][0, 2], loc['Ea'][0, 2]) and torch.equal(full['Ea'][0, 4], nxt[0, 0])
+    shard._scatter_rows(full, payload[1:], torch.tensor([L - 1]), widths, L)   # last position: no value row
+    assert full['Ea'].shape == (B, L, d)
+
+
+def test_compact_tails_round_trip():
+    """The exchanged form of the tails (non-empty buckets only) expands back to the dense array."""
+    from asrn_b200 import shard
+    g = torch.Generator().manual_seed(0)
+    tails = torch.zeros(2, 3, 8, 5, dtype=torch.int32)
+    for q in range(2):
+        for _ in range(6):
+            r, b = int(torch.randint(3, (1,), generator=g)), int(torch.randint(8, (1,), generator=g))
+            n = int(torch.randint(1, 5, (1,), generator=g))
+            tails[q, r, b, 0] = n
+            tails[q, r, b, 1:1 + n] = torch.arange(n, dtype=torch.int32) + 10 * q
+    packed = [shard.compact_tails(tails[q]) for q in range(2)]
+    m = max(ix.numel() for _, ix in packed) + 1
+    ent = torch.zeros(2, m, 20, dtype=torch.uint8)
+    idx = torch.full((2, m), -1, dtype=torch.int64)
+    for q, (e, ix) in enumerate(packed):
+        ent[q, :ix.numel()] = e
+        idx[q, :ix.numel()] = ix
+    assert torch.equal(shard.expand_tails(ent, idx, tails.shape[1:]), tails)
