@@ -1,7 +1,7 @@
 // Candidate scoring on tensor cores (bf16 autocast mode). Same computation as k_score_simt (asrn/estable.py:204-300,
 // asrn/nucleo.py:279-382), organised per sub-tile of 32 sorted query slots:
 //   window = the 64 sorted slots [q0 - 32, q0 + 32) of the row (the previous sub-tile + the current one);
-//   S = phi_q . phi_k and Qc . Kc (32 x 64 each) on mma.sync (fp32 accumulate), then the reference's rounding chain,
+//   S = phi_q . phi_k and Qc . Kc on tcgen05 (fp32 accumulators in TMEM), then the reference's rounding chain,
 //   suffix weight, log_alfa_k and the fp64 time difference, the exact-mask softmax per query, and
 //   out^T (d_part x 32) = V^T (d_part x 64) . att^T (64 x 32) on tcgen05 (M = 128 rows of d per MMA, N = the 32
 //   queries, K = the 64 window keys; the accumulators in TMEM), added into the bf16 accumulator acc by bf16 reductions
@@ -10,9 +10,10 @@
 // other rows keep finite contents (zeros) and meet zero weights.
 //
 // One block of 20 warps per (row, span of 512-2048 slots), three warp groups working on consecutive sub-tiles at once:
-// in iteration i group A (warps 0-7) scores sub-tile i + 1 and takes its softmax, while group B (warps 8-15) has the
-// value products of sub-tile i computed by the tensor cores (lane 0 of warp m issues M-tile m) and reduces them into
-// acc, and the load group (warps 16-19) issues the copies: the sorted entries of sub-tile i + 3 and the per-position
+// in iteration i group A (warps 0-7) scores sub-tile i + 1 (S products issued to the tensor cores by one thread, the
+// element epilogue by the four warps whose TMEM lanes hold the window's keys) and takes its softmax, while group B
+// (warps 8-15) has the value products of sub-tile i computed by the tensor cores (lane 0 of warp m issues M-tile m)
+// and reduces them into acc, and the load group (warps 16-19) issues the copies: the sorted entries of sub-tile i + 3 and the per-position
 // scalars of i + 2 by cp.async, the phi / Qc / Kc rows of i + 2 by tensor-map row gathers (four rows per instruction)
 // into a 4-sub-tile feature ring, the used value rows of i + 1 by 16-byte cp.async into a 3-sub-tile value ring kept
 // in the MMA's MN-major 128-byte-swizzled layout (one 12 KB region per 64 columns of d). The weights pass from A to B
@@ -63,6 +64,7 @@ struct TcSmem {
   float* wsuf;          // [kMaxSuffix + 1] suffix weights w_sufijo
   uint64_t* fbar;       // [4] feature-stage mbarriers (one per 32-row stage of the feature ring)
   uint64_t* pvbar;      // value-product MMAs done
+  uint64_t* sbar;       // [2] score MMAs of a sub-tile done (sub-tile t on t & 1)
   uint32_t* tmem;       // TMEM base address
   int nbp;               // phi column blocks
   int Dp;
@@ -121,6 +123,7 @@ __device__ inline TcSmem carve_tc(char* base, int P, int cf, int dpart) {
   p = base + ((p - base) + 15) / 16 * 16;
   s.fbar = reinterpret_cast<uint64_t*>(p);
   s.pvbar = s.fbar + 4;
+  s.sbar = s.fbar + 5;
   s.tmem = reinterpret_cast<uint32_t*>(s.fbar + 8);
   return s;
 }
@@ -189,25 +192,6 @@ __device__ __forceinline__ void round2_bf16(float& a, float& b) {
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 __device__ __forceinline__ void bar_group_a() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
-__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr));
-}
-__device__ __forceinline__ void ldsm_x2(uint32_t addr, uint32_t& r0, uint32_t& r1) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0, %1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
-}
-__device__ __forceinline__ void ldsm_x2_t(uint32_t addr, uint32_t& r0, uint32_t& r1) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0, %1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
-}
-__device__ __forceinline__ void mma16816(float* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
-                                         uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
-      "{%0, %1, %2, %3};"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
 
 // Block context shared by the phases.
 struct TcBlock {
@@ -324,154 +308,12 @@ __device__ __forceinline__ void tc_stage2_values(const ScoreArgs& a, const TcSme
   }
 }
 
-// Group A: scores of sub-tile t (queries: window slots 32 .. 63; keys: 0 .. 63, slot q0 - 32 + key), the exact-mask
-// softmax, the weights into att[t & 1] and the per-table gate signals. Warp w (0-7) owns n-tile w (keys 8w .. 8w + 7)
-// of both m-tiles: the two MMA chains run interleaved on the same key fragments, then one epilogue pass over the
-// warp's 8 elements per lane; the softmax takes the warp's 4 queries in one set of shuffle rounds.
-template <bool kSuf4>
-__device__ __forceinline__ void tc_scores(const ScoreArgs& a, const TcSmem& S, const TcBlock& k, int t) {
+// Group A: the exact-mask softmax of sub-tile t's score tile (eight lanes per query), the weights into att[t & 1] in
+// the K-major 128-byte-swizzled layout and the per-table gate signals.
+__device__ __forceinline__ void tc_softmax(const ScoreArgs& a, const TcSmem& S, const TcBlock& k, int t) {
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  const int C = a.C;
   const int64_t q0 = k.S0 + (int64_t)t * kQ;
-  const int lb = t * kQ;                        // window index of key 0 (li of slot q0 - 32)
-  const int nt = wid;
-  // band: keys [8 nt, 8 nt + 8) meet queries [16 mt, 16 mt + 16) only if some key is within C before one of them
-  bool band[2];
-#pragma unroll
-  for (int mt = 0; mt < 2; ++mt) band[mt] = nt * 8 + 7 >= mt * 16 + 32 - C && nt * 8 < mt * 16 + 16 + 32;
-  float cphi[2][4] = {}, cqk[2][4] = {};
-  if (band[0] || band[1]) {
-    // ldmatrix row addresses: A (queries) rows lane & 15, chunk half lane >> 4; B (keys) rows lane & 7, chunk half
-    // (lane >> 3) & 1
-    const int ha = lane >> 4, hb = (lane >> 3) & 1;
-    const int rk = frow(lb + nt * 8 + (lane & 7));
-    const int ra0 = frow(lb + kQ + (lane & 15)), ra1 = frow(lb + kQ + 16 + (lane & 15));
-    // per row: its ring address and (chunk half ^ the row's swizzle) << 4; chunk 2 i + h of the row then sits at
-    // row + ((2 i mod 8) << 4 ^ that) in column block 2 i / 8
-    const uint32_t pb = su32(S.phi) + (rk << 7), pbx = (uint32_t)((hb ^ (rk & 7)) << 4);
-    const uint32_t pa0 = su32(S.phi) + (ra0 << 7), pa0x = (uint32_t)((ha ^ (ra0 & 7)) << 4);
-    const uint32_t pa1 = su32(S.phi) + (ra1 << 7), pa1x = (uint32_t)((ha ^ (ra1 & 7)) << 4);
-    const uint32_t cb = su32(S.kc) + (rk << 6), cbx = (uint32_t)((hb ^ ((rk >> 1) & 3)) << 4);
-    const uint32_t ca0 = su32(S.qc) + (ra0 << 6), ca0x = (uint32_t)((ha ^ ((ra0 >> 1) & 3)) << 4);
-    const uint32_t ca1 = su32(S.qc) + (ra1 << 6), ca1x = (uint32_t)((ha ^ ((ra1 >> 1) & 3)) << 4);
-#pragma unroll
-    for (int i = 0; i < kMaxPhi / 16; ++i) {
-      if (16 * i < k.Ppad) {
-        const uint32_t blk = (uint32_t)((2 * i) >> 3) * (kRF * 128), cx = (uint32_t)(((2 * i) & 7) << 4);
-        uint32_t b0, b1;
-        ldsm_x2(pb + blk + (cx ^ pbx), b0, b1);
-        if (band[0]) {
-          uint32_t a0, a1, a2, a3;
-          ldsm_x4(pa0 + blk + (cx ^ pa0x), a0, a1, a2, a3);
-          mma16816(cphi[0], a0, a1, a2, a3, b0, b1);
-        }
-        if (band[1]) {
-          uint32_t a0, a1, a2, a3;
-          ldsm_x4(pa1 + blk + (cx ^ pa1x), a0, a1, a2, a3);
-          mma16816(cphi[1], a0, a1, a2, a3, b0, b1);
-        }
-      }
-    }
-#pragma unroll
-    for (int i = 0; i < kMaxConfirm / 16; ++i) {
-      if (16 * i < k.Cpad) {
-        const uint32_t cx = (uint32_t)(((2 * i) & 3) << 4);
-        uint32_t b0, b1;
-        ldsm_x2(cb + (cx ^ cbx), b0, b1);
-        if (band[0]) {
-          uint32_t a0, a1, a2, a3;
-          ldsm_x4(ca0 + (cx ^ ca0x), a0, a1, a2, a3);
-          mma16816(cqk[0], a0, a1, a2, a3, b0, b1);
-        }
-        if (band[1]) {
-          uint32_t a0, a1, a2, a3;
-          ldsm_x4(ca1 + (cx ^ ca1x), a0, a1, a2, a3);
-          mma16816(cqk[1], a0, a1, a2, a3, b0, b1);
-        }
-      }
-    }
-  }
-  // this lane's four query rows (g, g + 8, 16 + g, 24 + g; g = lane / 4) and two key columns (kj0, kj0 + 1): their
-  // ring-row scalars are read once; the suffix length is the count of leading equal previous signatures
-  const int g4 = lane >> 2, kj0 = nt * 8 + (lane & 3) * 2;
-  int q_id[4], k_id[2];
-  float4 q_pf[4][2], k_pf[2][2];
-  double q_bt[4], k_bt[2];
-  float k_la[2];
-#pragma unroll
-  for (int u = 0; u < 4; ++u) {
-    const int rq = frow(lb + kQ + g4 + 8 * u);
-    q_id[u] = S.id[rq];
-    q_pf[u][0] = *reinterpret_cast<const float4*>(S.pf + rq * kMaxSuffix);
-    q_pf[u][1] = *reinterpret_cast<const float4*>(S.pf + rq * kMaxSuffix + 4);
-    q_bt[u] = S.bt[rq];
-  }
-#pragma unroll
-  for (int u = 0; u < 2; ++u) {
-    const int rk = frow(lb + kj0 + u);
-    k_id[u] = S.id[rk];
-    k_pf[u][0] = *reinterpret_cast<const float4*>(S.pf + rk * kMaxSuffix);
-    k_pf[u][1] = *reinterpret_cast<const float4*>(S.pf + rk * kMaxSuffix + 4);
-    k_bt[u] = S.bt[rk];
-    k_la[u] = S.la[rk];
-  }
-  // per query row u: inside the row (slot < L) and its score-tile row address; per key: slot >= 0
-  const int64_t rem = a.L - q0;
-  const int qlim = rem < kQ ? (int)rem : kQ;
-  const bool kv[2] = {q0 - kQ + kj0 >= 0, q0 - kQ + kj0 + 1 >= 0};
-  const int wlo = kQ - C;                        // window: key kj is a candidate of query qi iff kj - qi in [32 - C, 32)
-#pragma unroll
-  for (int mt = 0; mt < 2; ++mt) {
-    if (!band[mt]) {                             // the whole 16 x 8 tile is outside the window band (warp-uniform)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int qi = g4 + 8 * (2 * mt + (e >> 1)), kj = kj0 + (e & 1);
-        S.sc[qi * 64 + (kj ^ sc_swz(qi))] = -INFINITY;
-      }
-      continue;
-    }
-#pragma unroll
-    for (int hr = 0; hr < 2; ++hr) {             // elements 2 hr, 2 hr + 1: query row uq, keys kj0, kj0 + 1
-      const int uq = 2 * mt + hr;
-      const int qi = g4 + 8 * uq;
-      // the reference's rounding chain, two elements per conversion: s1 = bf16(bf16(phi.phi) / T),
-      // s2 = bf16(bf16(Qc.Kc) * cf^-1/2), t1 = bf16(s1 + s2)
-      float s1a = cphi[mt][2 * hr], s1b = cphi[mt][2 * hr + 1], s2a = cqk[mt][2 * hr], s2b = cqk[mt][2 * hr + 1];
-      round2_bf16(s1a, s1b);
-      round2_bf16(s2a, s2b);
-      s1a = __fmul_rn(s1a, k.inv_temp);
-      s1b = __fmul_rn(s1b, k.inv_temp);
-      s2a = __fmul_rn(s2a, a.esc_c);
-      s2b = __fmul_rn(s2b, a.esc_c);
-      round2_bf16(s1a, s1b);
-      round2_bf16(s2a, s2b);
-      float t1[2] = {__fadd_rn(s1a, s2a), __fadd_rn(s1b, s2b)};
-      round2_bf16(t1[0], t1[1]);
-      const bool qv = qi < qlim;
-      const int row = qi * 64, swz = sc_swz(qi);
-#pragma unroll
-      for (int uk = 0; uk < 2; ++uk) {
-        const int kj = kj0 + uk;
-        const bool ok = qv && kv[uk] && (unsigned)(kj - qi - wlo) < (unsigned)C && k_id[uk] == q_id[uq];
-        const float4 qa = q_pf[uq][0], ka = k_pf[uk][0];
-        int ln;
-        if (kSuf4) {                             // entries past K are NaN (never equal)
-          ln = qa.x == ka.x ? (qa.y == ka.y ? (qa.z == ka.z ? (qa.w == ka.w ? 4 : 3) : 2) : 1) : 0;
-        } else {
-          const float4 qb = q_pf[uq][1], kb = k_pf[uk][1];
-          const uint32_t eq = (qa.x == ka.x ? 1u : 0u) | (qa.y == ka.y ? 2u : 0u) | (qa.z == ka.z ? 4u : 0u) |
-                              (qa.w == ka.w ? 8u : 0u) | (qb.x == kb.x ? 16u : 0u) | (qb.y == kb.y ? 32u : 0u) |
-                              (qb.z == kb.z ? 64u : 0u) | (qb.w == kb.w ? 128u : 0u);
-          ln = __ffs(~eq) - 1;                   // leading equal entries
-        }
-        float v = __fadd_rn(t1[uk], S.wsuf[ln]);
-        v = __fadd_rn(v, k_la[uk]);
-        const float dt = __double2float_rn(k_bt[uk] - q_bt[uq]);
-        v = __fadd_rn(v, __fmul_rn(dt, k.tasa));
-        S.sc[row + (kj ^ swz)] = ok ? v : -INFINITY;
-      }
-    }
-  }
+  const int lb = t * kQ;
   bar_group_a();
   // softmax: warp w -> queries 4w .. 4w + 3, eight lanes per query; lane -> keys 8 kg .. 8 kg + 7 (kg = lane % 8) of
   // query qi = 4w + lane / 8. In the score tile these keys are the 8-aligned group 8 (kg ^ (swz / 8)) with adjacent
@@ -522,6 +364,147 @@ __device__ __forceinline__ void tc_scores(const ScoreArgs& a, const TcSmem& S, c
   *reinterpret_cast<uint4*>(att + (qi >> 3) * 1024 + (qi & 7) * 128 + ((kg ^ (qi & 7)) << 4)) = wv;
   if (kg == 0) qoff[qi] = (anyv && mine) ? gq * a.d + k.dp0 : -1;
   umma::fence_proxy_async();       // the weights are read by the tensor cores (async proxy) after the block barrier
+}
+
+// Group A: scores of sub-tile t (queries: window slots 32 .. 63; keys: 0 .. 63, slot q0 - 32 + key), the exact-mask
+// softmax, the weights into att[t & 1] and the per-table gate signals.
+// S^T = phi_k . phi_q^T and Kc . Qc^T on tcgen05, issued by lane 0 of warp 0 once the features are in: A = all 128 rows
+// of the feature ring (the keys: lane r of the accumulator is ring row r), B = the sub-tile's 32 query rows (N = 32),
+// K = P (phi, 64 features per 128-byte-swizzled column block) and cf (Qc / Kc, 64-byte swizzle); fp32 accumulators in
+// TMEM columns kScol + 64 (t & 1) (phi) and + 32 (Qc . Kc). Rows of the ring that are not the window's (a sub-tile being
+// loaded) give accumulator lanes nobody reads. The window's keys are two 32-row stages of the ring, i.e. two TMEM lane
+// quadrants: the four warps of those quadrants (warp w reads lanes 32 (w % 4) .. + 31) take one key per lane and 16
+// queries each (half w / 4) and write t1 (the bf16 rounding chain of the two products) into the score tile; then all
+// eight warps add the suffix weight, log_alfa_k and the fp64 time difference and apply the masks in place, eight
+// elements per lane.
+constexpr uint32_t kScol = 256;     // TMEM columns of the score accumulators (the value products use 0 .. 191)
+
+// The score MMAs of sub-tile t (one thread, once the sub-tile's feature rows are in the ring).
+__device__ __forceinline__ void tc_issue_scores(const TcSmem& S, const TcBlock& k, int t, uint32_t tmem) {
+  const int lb = t * kQ;
+  const uint32_t scol = kScol + 64u * (uint32_t)(t & 1);
+  umma::tc_fence_after();
+  const uint32_t idesc = umma::idesc_bf16(128, kQ);
+  const int rq0 = frow(lb + kQ);                 // first query row (a 32-row stage: 4 KB / 2 KB aligned)
+  const uint32_t phi0 = su32(S.phi);
+  for (int i = 0; 16 * i < k.Ppad; ++i) {
+    const uint32_t blk = phi0 + (uint32_t)(i >> 2) * (kRF * 128), off = (uint32_t)(i & 3) * 32;
+    umma::mma_bf16(tmem + scol, umma::desc_sw128(blk + off), umma::desc_sw128(blk + (uint32_t)rq0 * 128 + off), idesc,
+                   i > 0 ? 1u : 0u);
+  }
+  for (int i = 0; 16 * i < k.Cpad; ++i)
+    umma::mma_bf16(tmem + scol + kQ, umma::desc_sw64(su32(S.kc) + (uint32_t)i * 32),
+                   umma::desc_sw64(su32(S.qc) + (uint32_t)rq0 * 64 + (uint32_t)i * 32), idesc, i > 0 ? 1u : 0u);
+  umma::mma_commit(S.sbar + (t & 1));
+}
+
+template <bool kSuf4>
+__device__ __forceinline__ void tc_scores(const ScoreArgs& a, const TcSmem& S, const TcBlock& k, int t, uint32_t tmem,
+                                          bool issue_next) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int C = a.C;
+  const int64_t q0 = k.S0 + (int64_t)t * kQ;
+  const int lb = t * kQ;                        // window index of key 0 (li of slot q0 - 32)
+  const uint32_t scol = kScol + 64u * (uint32_t)(t & 1);
+  const int q4 = wid & 3, hq = wid >> 2;
+  const int qa = t & 3, qb = (t + 1) & 3;       // the quadrants (ring stages) of the window's two key halves
+  if (q4 == qa || q4 == qb) {
+    // t1 of the warp's 32 keys x 16 queries into the score tile (key kj of query qi at qi * 64 + (kj ^ sc_swz(qi)))
+    const int kj = (q4 == qa ? 0 : kQ) + lane;   // this lane's key (window index)
+    float sp[16], sq[16];
+    umma::mbar_wait(S.sbar + (t & 1), (uint32_t)((t >> 1) & 1), a.status);
+    __syncwarp();                                // lane 0 of warp 0 may have issued the MMAs: converge for tcgen05.ld
+    umma::tc_fence_after();
+    const uint32_t trow = tmem + ((uint32_t)(q4 * 32) << 16) + scol + (uint32_t)(16 * hq);
+    tmem_ld16(trow, sp);
+    tmem_ld16(trow + kQ, sq);
+    umma::tc_fence_before();                     // the TMEM reads precede the next MMA into this buffer
+#pragma unroll
+    for (int j = 0; j < 16; j += 2) {
+      // the reference's rounding chain, two queries per conversion: s1 = bf16(bf16(phi.phi) / T),
+      // s2 = bf16(bf16(Qc.Kc) * cf^-1/2), t1 = bf16(s1 + s2)
+      float s1a = sp[j], s1b = sp[j + 1], s2a = sq[j], s2b = sq[j + 1];
+      round2_bf16(s1a, s1b);
+      round2_bf16(s2a, s2b);
+      s1a = __fmul_rn(s1a, k.inv_temp);
+      s1b = __fmul_rn(s1b, k.inv_temp);
+      s2a = __fmul_rn(s2a, a.esc_c);
+      s2b = __fmul_rn(s2b, a.esc_c);
+      round2_bf16(s1a, s1b);
+      round2_bf16(s2a, s2b);
+      float t1a = __fadd_rn(s1a, s2a), t1b = __fadd_rn(s1b, s2b);
+      round2_bf16(t1a, t1b);
+      const int qi = 16 * hq + j;
+      S.sc[qi * 64 + (kj ^ sc_swz(qi))] = t1a;
+      S.sc[(qi + 1) * 64 + (kj ^ sc_swz(qi + 1))] = t1b;
+    }
+  }
+  bar_group_a();
+  // every warp: the rest of the score of 8 elements per lane (key columns kj0, kj0 + 1 of warp n-tile wid; query rows
+  // g, g + 8, g + 16, g + 24): suffix weight, log_alfa_k, the fp64 time difference and the masks, in place
+  {
+    const int nt = wid;
+    const int g4 = lane >> 2, kj0 = nt * 8 + (lane & 3) * 2;
+    int k_id[2];
+    float4 k_pf[2][2];
+    double k_bt[2];
+    float k_la[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int rk = frow(lb + kj0 + u);
+      k_id[u] = S.id[rk];
+      k_pf[u][0] = *reinterpret_cast<const float4*>(S.pf + rk * kMaxSuffix);
+      k_pf[u][1] = *reinterpret_cast<const float4*>(S.pf + rk * kMaxSuffix + 4);
+      k_bt[u] = S.bt[rk];
+      k_la[u] = S.la[rk];
+    }
+    const int64_t rem = a.L - q0;
+    const int qlim = rem < kQ ? (int)rem : kQ;
+    const bool kv[2] = {q0 - kQ + kj0 >= 0, q0 - kQ + kj0 + 1 >= 0};
+    const int wlo = kQ - C;                      // key kj is a candidate of query qi iff kj - qi in [32 - C, 32)
+#pragma unroll
+    for (int uq = 0; uq < 4; ++uq) {
+      const int qi = g4 + 8 * uq;
+      const int rq = frow(lb + kQ + qi);
+      const int q_id = S.id[rq];
+      const float4 qa4 = *reinterpret_cast<const float4*>(S.pf + rq * kMaxSuffix);
+      const double q_bt = S.bt[rq];
+      const bool qv = qi < qlim;
+      const int row = qi * 64, swz = sc_swz(qi);
+#pragma unroll
+      for (int uk = 0; uk < 2; ++uk) {
+        const int kj = kj0 + uk;
+        float* cell = S.sc + row + (kj ^ swz);
+        const bool ok = qv && kv[uk] && (unsigned)(kj - qi - wlo) < (unsigned)C && k_id[uk] == q_id;
+        if (!ok) {
+          *cell = -INFINITY;
+          continue;
+        }
+        const float4 ka = k_pf[uk][0];
+        int ln;
+        if (kSuf4) {                             // entries past K are NaN (never equal)
+          ln = qa4.x == ka.x ? (qa4.y == ka.y ? (qa4.z == ka.z ? (qa4.w == ka.w ? 4 : 3) : 2) : 1) : 0;
+        } else {
+          const float4 qb4 = *reinterpret_cast<const float4*>(S.pf + rq * kMaxSuffix + 4), kb = k_pf[uk][1];
+          const uint32_t eq = (qa4.x == ka.x ? 1u : 0u) | (qa4.y == ka.y ? 2u : 0u) | (qa4.z == ka.z ? 4u : 0u) |
+                              (qa4.w == ka.w ? 8u : 0u) | (qb4.x == kb.x ? 16u : 0u) | (qb4.y == kb.y ? 32u : 0u) |
+                              (qb4.z == kb.z ? 64u : 0u) | (qb4.w == kb.w ? 128u : 0u);
+          ln = __ffs(~eq) - 1;                   // leading equal entries
+        }
+        float v = __fadd_rn(*cell, S.wsuf[ln]);
+        v = __fadd_rn(v, k_la[uk]);
+        const float dt = __double2float_rn(k_bt[uk] - q_bt);
+        v = __fadd_rn(v, __fmul_rn(dt, k.tasa));
+        *cell = v;
+      }
+    }
+  }
+  tc_softmax(a, S, k, t);
+  // the next sub-tile's score MMAs, one iteration ahead of their epilogue (its feature rows were copied meanwhile)
+  if (issue_next && wid == 0 && lane == 0) {
+    umma::mbar_wait(S.fbar + ((t + 2) & 3), (uint32_t)(((t + 2) >> 2) & 1), a.status);
+    tc_issue_scores(S, k, t + 1, tmem);
+  }
 }
 
 // Group B: out^T = V^T . att^T for sub-tile t on tcgen05, reduced into the bf16 accumulator. Lane 0 of warp mm issues
@@ -637,16 +620,18 @@ k_score_tc(const __grid_constant__ CUtensorMap tm_phi, const __grid_constant__ C
     if (threadIdx.x == 0) {
       for (int i = 0; i < 4; ++i) umma::mbar_init(S.fbar + i, 1);   // 4 feature stages
       umma::mbar_init(S.pvbar, (uint32_t)(k.dpart / 128));           // one commit per M-tile's issuing warp
+      umma::mbar_init(S.sbar, 1);                                      // score MMAs of even / odd sub-tiles
+      umma::mbar_init(S.sbar + 1, 1);
       umma::fence_mbar_init();
     }
     if (wid == kGroupWarps) {
-      umma::tmem_alloc(S.tmem, 256);
+      umma::tmem_alloc(S.tmem, 512);
       umma::tmem_relinquish();
     }
   }
   const bool loader = wid >= 2 * kGroupWarps;
   const int pt = threadIdx.x - 2 * kGroupWarps * 32;   // thread index within the load group
-  // bounded wait for the feature rows of sub-tile t (stage (t + 1) % 4): every thread of group A waits itself
+  // bounded wait for the feature rows of sub-tile t (stage (t + 1) % 4), by the thread that issues its score MMAs
   auto wait_features = [&](int t) {
     umma::mbar_wait(S.fbar + ((t + 1) & 3), (uint32_t)(((t + 1) >> 2) & 1), a.status);
   };
@@ -692,10 +677,13 @@ k_score_tc(const __grid_constant__ CUtensorMap tm_phi, const __grid_constant__ C
   __syncthreads();
   const bool suf4 = a.K <= 4;
   if (group_a) {
-    wait_features(-1);
-    wait_features(0);
-    if (suf4) tc_scores<true>(a, S, k, 0);
-    else tc_scores<false>(a, S, k, 0);
+    if (threadIdx.x == 0) {                     // the issuer of the score MMAs waits for the feature rows
+      wait_features(-1);
+      wait_features(0);
+      tc_issue_scores(S, k, 0, tmem);
+    }
+    if (suf4) tc_scores<true>(a, S, k, 0, tmem, ntile > 1);
+    else tc_scores<false>(a, S, k, 0, tmem, ntile > 1);
   }
   __syncthreads();
 
@@ -714,9 +702,8 @@ k_score_tc(const __grid_constant__ CUtensorMap tm_phi, const __grid_constant__ C
       wait_copies();
     } else if (group_a) {
       if (i + 1 < ntile) {
-        wait_features(i + 1);
-        if (suf4) tc_scores<true>(a, S, k, i + 1);
-        else tc_scores<false>(a, S, k, i + 1);
+        if (suf4) tc_scores<true>(a, S, k, i + 1, tmem, i + 2 < ntile);
+        else tc_scores<false>(a, S, k, i + 1, tmem, i + 2 < ntile);
       }
     } else {
       tc_values(a, S, k, i, wid - kGroupWarps, tmem);
@@ -725,7 +712,7 @@ k_score_tc(const __grid_constant__ CUtensorMap tm_phi, const __grid_constant__ C
   }
   if (wid == kGroupWarps) {
     umma::tc_fence_after();
-    umma::tmem_dealloc(tmem, 256);
+    umma::tmem_dealloc(tmem, 512);
   }
 }
 

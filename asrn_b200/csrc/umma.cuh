@@ -107,6 +107,17 @@ ASRN_DEV uint64_t desc_sw128(uint32_t saddr) {
   d |= (uint64_t)2 << 61;                 // 128-byte swizzle
   return d;
 }
+// The same for a K-major operand in the 64-byte-swizzled layout (rows of 32 bf16 = 64 B, 8-row groups of 512 B, the
+// 16-byte chunk index XOR-ed with (row / 2) mod 4); the tile starts on a 512-byte boundary.
+ASRN_DEV uint64_t desc_sw64(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)1 << 16;
+  d |= (uint64_t)(512 >> 4) << 32;        // stride byte offset: 8 rows x 64 B
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)4 << 61;                 // 64-byte swizzle
+  return d;
+}
 // Shared-memory descriptor of an MN-major, 128-byte-swizzled operand: atoms of 64 MN elements (128 B) x 8 K rows
 // (1024 B, the 16-byte chunk index XOR-ed with the row within the atom), consecutive 8-row K groups 1024 B apart
 // (stride byte offset), consecutive 64-element MN blocks `mn_stride` bytes apart (leading byte offset).
