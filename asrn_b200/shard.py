@@ -46,9 +46,9 @@ last_exchange = {}    # this rank's last compact row exchange: rows sent, padded
 _ROW_KEYS = ('phi', 'Qc', 'Kc')                       # gathered only for the positions in the tails
 
 
-def tail_index(tails, c0, Lc, B, T):
-    """Local flat indices b * Lc + (p - c0), ascending, of the positions p of this chunk that appear in its bucket
-    tails (rows b * T + tau): the only positions of the chunk that a later shard's rows hold."""
+def tail_flags(tails, c0, Lc, B, T):
+    """(B * Lc,) bool: which positions p of this chunk (flat index b * Lc + p - c0) appear in its bucket tails (rows
+    b * T + tau), the only positions of the chunk that a later shard's rows hold. No host synchronisation."""
     dev = tails.device
     rows, _, C1 = tails.shape
     C = C1 - 1
@@ -57,16 +57,43 @@ def tail_index(tails, c0, Lc, B, T):
     rel = torch.where(valid, tails[..., 1:].long() - c0, Lc).clamp(0, Lc)
     b = (torch.arange(rows, device=dev) // T).view(rows, 1, 1)
     flags = torch.zeros(B * (Lc + 1), dtype=torch.bool, device=dev)
-    flags[(b * (Lc + 1) + rel).view(-1)] = True
-    return flags.view(B, Lc + 1)[:, :Lc].reshape(-1).nonzero().squeeze(1)
+    flags.index_fill_(0, (b * (Lc + 1) + rel).view(-1), True)
+    return flags.view(B, Lc + 1)[:, :Lc].reshape(-1)
 
 
-def compact_tails(tails):
+def compact(flags, n):
+    """The ascending indices of the n set flags (n known to the host), without a host synchronisation."""
+    dev = flags.device
+    pos = torch.cumsum(flags.long(), 0) - 1
+    out = torch.full((flags.numel() + 1,), -1, dtype=torch.int64, device=dev)
+    out.index_put_((torch.where(flags, pos, flags.numel()),), torch.arange(flags.numel(), device=dev))
+    return out[:n]
+
+
+def compact_cap(flags, cap):
+    """The ascending indices of the set flags in a (cap,) tensor padded with -1 (flags past cap are dropped: the
+    caller checks the count against cap on the device)."""
+    dev = flags.device
+    pos = torch.cumsum(flags.long(), 0) - 1
+    out = torch.full((max(flags.numel(), cap) + 1,), -1, dtype=torch.int64, device=dev)
+    tgt = torch.where(flags & (pos < cap), pos, out.numel() - 1)
+    out.index_put_((tgt,), torch.arange(flags.numel(), device=dev))
+    out[-1:].fill_(-1)
+    return out[:cap]
+
+
+def tail_index(tails, c0, Lc, B, T):
+    """Local flat indices b * Lc + (p - c0), ascending, of the positions p of this chunk in its bucket tails."""
+    return tail_flags(tails, c0, Lc, B, T).nonzero().squeeze(1)
+
+
+def compact_tails(tails, n=None):
     """The non-empty bucket tails of a chunk: flat indices row * 2^nb + bucket (int64) and their (count, positions)
     entries as raw bytes (n, (C + 1) * 4). In the heavy regime few buckets are used, so this is far smaller than the
-    dense (rows, 2^nb, C + 1) array the merge kernel reads."""
+    dense (rows, 2^nb, C + 1) array the merge kernel reads. n: their number if the host knows it (no synchronisation)."""
     flat = tails.reshape(-1, tails.shape[-1])
-    nz = (flat[:, 0] != 0).nonzero().squeeze(1)
+    ne = flat[:, 0] != 0
+    nz = ne.nonzero().squeeze(1) if n is None else compact(ne, n)
     return flat[nz].contiguous().view(torch.uint8), nz
 
 
@@ -74,12 +101,15 @@ def expand_tails(ent_all, idx_all, shape):
     """(world, m, bytes) entries and (world, m) indices (-1 = padding) -> dense (world,) + shape int32 tails, zeros
     (empty tails) elsewhere."""
     world = ent_all.shape[0]
-    dense = torch.zeros((world,) + tuple(shape), dtype=torch.int32, device=ent_all.device)
+    R = 1
+    for x in shape[:-1]:
+        R *= x
+    flat = torch.zeros(world * R + 1, shape[-1], dtype=torch.int32, device=ent_all.device)
     for q in range(world):
-        keep = idx_all[q] >= 0
-        rows = ent_all[q][keep].contiguous().view(torch.int32).view(-1, shape[-1])
-        dense[q].view(-1, shape[-1]).index_copy_(0, idx_all[q][keep], rows)
-    return dense
+        rows = ent_all[q].contiguous().view(torch.int32).view(-1, shape[-1])
+        dst = torch.where(idx_all[q] >= 0, q * R + idx_all[q], world * R)   # padding into the spare row
+        flat.index_copy_(0, dst, rows)
+    return flat[:world * R].view((world,) + tuple(shape))
 
 
 def _row_payload(loc, sel, Ea_next):
@@ -99,33 +129,33 @@ def _row_widths(loc, Ea_next):
 
 
 def _full_rows(loc, B, L, c0, c1, Ea_first_next):
-    """Zero-filled (B, L, .) feature tensors holding this chunk's own rows and, at c1, the next chunk's first value
-    row; the earlier chunks' rows are scattered in by _scatter_rows."""
+    """Zero-filled feature tensors of B * L rows (flat index b * L + p) plus one spare row at the end, holding this
+    chunk's own rows and, at c1, the next chunk's first value row; the earlier chunks' rows are scattered in by
+    _scatter_rows (padding entries land in the spare row, so no step needs the host)."""
     full = {}
     for k in _ROW_KEYS + ('Ea',):
         x = loc[k]
-        t = torch.zeros((B, L) + tuple(x.shape[2:]), dtype=x.dtype, device=x.device)
-        t[:, c0:c1] = x
+        t = torch.zeros((B * L + 1,) + tuple(x.shape[2:]), dtype=x.dtype, device=x.device)
+        t[:B * L].view((B, L) + tuple(x.shape[2:]))[:, c0:c1] = x
         full[k] = t
     if Ea_first_next is not None and c1 < L:
-        full['Ea'][:, c1] = Ea_first_next
+        full['Ea'][:B * L].view((B, L) + tuple(Ea_first_next.shape[1:]))[:, c1] = Ea_first_next
     return full
 
 
 def _scatter_rows(full, payload, gidx, widths, L):
     """Rows of another chunk (payload (n, bytes), global flat indices b * L + p, -1 = padding) into full: phi, Qc, Kc
     at p, the value row at p + 1 (where the scoring kernel reads the value of key p)."""
-    keep = gidx >= 0
-    gidx, payload = gidx[keep], payload[keep]
     off = 0
     for k, w in zip(_ROW_KEYS + ('Ea',), widths):
-        t = full[k]
+        t = full[k].view(-1, full[k].shape[-1])
+        spare = t.shape[0] - 1
         rows = payload[:, off:off + w].contiguous().view(t.dtype).view(-1, t.shape[-1])
-        dst = gidx + 1 if k == 'Ea' else gidx
         if k == 'Ea':                                   # the value row of the sequence's last position is unused
-            ok = (dst % L) != 0
-            dst, rows = dst[ok], rows[ok]
-        t.view(-1, t.shape[-1]).index_copy_(0, dst, rows)
+            dst = torch.where((gidx >= 0) & ((gidx + 1) % L != 0), gidx + 1, spare)
+        else:
+            dst = torch.where(gidx >= 0, gidx, spare)
+        t.index_copy_(0, dst, rows)                     # padding rows all land in the spare row
         off += w
 
 
@@ -150,7 +180,7 @@ def carry_violations(sums=None, maps=None, keys=None, tails=None, Lc=None, C=Non
     if keys is not None and keys.shape[-1] > 1:
         k = keys.view(torch.int64) if keys.dtype != torch.int64 else keys
         # order-preserving images of the fp64 keys are unsigned 64-bit: compare with the sign bit flipped
-        flip = torch.bitwise_xor(k, torch.tensor(-(1 << 63), dtype=torch.int64, device=k.device))
+        flip = torch.bitwise_xor(k, -(1 << 63))
         bad.append((flip[..., 1:] < flip[..., :-1]).sum())
     if tails is not None:
         world = tails.shape[0]
@@ -454,7 +484,16 @@ def exchange_first_rows(first, world, group=None):
     return flat
 
 
-def exchange_varlen_async(items, world, group=None):
+def exchange_counts(local, world, group=None):
+    """(k,) int64 device counts of this rank -> (world, k) list of lists on the host: the forward's one host
+    synchronisation (the padded sizes of the variable-length exchange must be known to allocate)."""
+    import torch.distributed as dist
+    counts = torch.empty(world, local.numel(), dtype=torch.int64, device=local.device)
+    dist.all_gather_into_tensor(counts.view(-1), local.contiguous(), group=group)
+    return counts.tolist()
+
+
+def exchange_varlen_async(items, world, group=None, counts=None, async_op=True):
     """Variable-length exchange of several items, each this rank's (n, bytes) uint8 payload and (n,) int64 indices:
     returns per item (payloads (world, m, bytes), indices (world, m)) padded to the largest n of any rank (index -1
     marks padding), and finish(), which makes the current stream wait for the collectives. The counts of all items go
@@ -462,10 +501,10 @@ def exchange_varlen_async(items, world, group=None):
     without waiting."""
     import torch.distributed as dist
     dev = items[0][0].device
-    n = torch.tensor([p.shape[0] for p, _ in items], dtype=torch.int64, device=dev)
-    counts = torch.empty(world, len(items), dtype=torch.int64, device=dev)
-    dist.all_gather_into_tensor(counts.view(-1), n, group=group)
-    ms = [max(1, int(m)) for m in counts.max(0).values.tolist()]
+    if counts is None:
+        counts = exchange_counts(torch.tensor([p.shape[0] for p, _ in items], dtype=torch.int64, device=dev), world,
+                                 group)
+    ms = [max(1, max(c[j] for c in counts)) for j in range(len(items))]
     out, works = [], []
     for (payload, gidx), m in zip(items, ms):
         pad = torch.zeros(m, payload.shape[1], dtype=torch.uint8, device=dev)
@@ -474,13 +513,14 @@ def exchange_varlen_async(items, world, group=None):
         idx[:gidx.shape[0]] = gidx
         pay_all = torch.empty(world, m, payload.shape[1], dtype=torch.uint8, device=dev)
         idx_all = torch.empty(world, m, dtype=torch.int64, device=dev)
-        works.append(dist.all_gather_into_tensor(pay_all.view(-1), pad.view(-1), group=group, async_op=True))
-        works.append(dist.all_gather_into_tensor(idx_all.view(-1), idx, group=group, async_op=True))
+        works.append(dist.all_gather_into_tensor(pay_all.view(-1), pad.view(-1), group=group, async_op=async_op))
+        works.append(dist.all_gather_into_tensor(idx_all.view(-1), idx, group=group, async_op=async_op))
         out.append((pay_all, idx_all))
 
     def finish():
         for w in works:
-            w.wait()
+            if w is not None:
+                w.wait()
     return out, finish
 
 
@@ -494,8 +534,9 @@ def exchange_rows_async(payload, gidx, world, group=None):
 def exchange_halo(last, world, rank, group=None):
     """(B, d) E of this chunk's last position -> E of the position before this chunk (zeros on rank 0)."""
     import torch.distributed as dist
-    lasts = [torch.empty_like(last) for _ in range(world)]
-    dist.all_gather(lasts, last.contiguous(), group=group)
+    x = last.contiguous()
+    lasts = torch.empty((world,) + tuple(x.shape), dtype=x.dtype, device=x.device)
+    dist.all_gather_into_tensor(lasts.view(-1), x.view(-1), group=group)
     return lasts[rank - 1] if rank > 0 else torch.zeros_like(last)
 
 
@@ -539,10 +580,23 @@ def exchange_racha_maps(rmap, world, group=None):
 def forward(layer, E, h, tokens=None, group=None):
     """One rank of the sharded forward under torch.distributed: E, h (B, Lc, d), tokens (B, Lc) are this rank's chunk
     of every sequence (chunks in rank order); returns h' (B, Lc, d) fp32 for the chunk. Every rank calls it with the
-    same shapes; the collectives are the same on every rank, in the same order."""
+    same shapes; the collectives are the same on every rank, in the same order. Eager, with one host synchronisation
+    (the sizes of the variable-length exchange); ShardedForward replays it as a CUDA graph instead."""
     import torch.distributed as dist
     _check(layer, E, h, tokens)
     _raise_reported(E.device, block=False)
+    if dist.get_world_size(group) == 1:
+        return layer(E.float().contiguous(), h.float().contiguous(), tokens)
+    out, status, _ = _forward(layer, E, h, tokens, group, None)
+    _defer_status(status)
+    return out
+
+
+def _forward(layer, E, h, tokens, group, caps):
+    """The sharded forward. caps None: the exchange is sized from the counts read by the host (one synchronisation);
+    caps = (tails, rows): fixed capacities, no host synchronisation (a count above its capacity is recorded in the
+    status word). Returns (h' of the chunk, device status word, device (tails, rows) counts of this rank)."""
+    import torch.distributed as dist
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
     half = compute_half('cuda')
@@ -550,32 +604,45 @@ def forward(layer, E, h, tokens=None, group=None):
     L = world * Lc
     c0, c1 = rank * Lc, (rank + 1) * Lc
     E, h = E.float().contiguous(), h.float().contiguous()
-    if world == 1:
-        return layer(E, h, tokens)
     # (1) halo rows: E of every chunk's last position
     halo = exchange_halo(E[:, -1], world, rank, group)
     loc = _phase1(layer, E, h, tokens, halo, half, c0)
     # (2) chunk sums of beta (= the last local clock value) -> clock offsets
     sums = exchange_chunk_sums(loc['Bt'][:, -1], world, group)
-    # (3) bucket tails, (4) the per-position scalars of every position, (5) the feature and value rows of the tail
-    # positions only (gathered while the n-gram memory sorts its chunk)
+    # (3) the per-position scalars of every position, the first value row of every chunk
     full = {k: _gather_seq(loc[k], world, group) for k in _SCALAR_KEYS}
     firsts = exchange_first_rows(loc['Ea'][:, 0], world, group)
+    _apply_clock_offsets(full['Bt'], sums, Lc)
+    # what this rank publishes: the positions in its tails and its non-empty tails (device-side counts)
+    flags = tail_flags(loc['tails'], c0, Lc, B, layer.n_tablas)
+    t_ne = loc['tails'][..., 0].reshape(-1) != 0
+    local_counts = torch.stack([t_ne.sum(), flags.sum()])
+    # (4) n-gram memory: the chunk's sort and per-group summaries (queued before the exchange of (5))
+    ng = ngram_sort(layer, full, c0, Lc, half)
     nxt = firsts[rank + 1].unsqueeze(1) if rank + 1 < world else torch.zeros_like(loc['Ea'][:, :1])
     Ea_next = torch.cat([loc['Ea'][:, 1:], nxt], 1)
-    sel = tail_index(loc['tails'], c0, Lc, B, layer.n_tablas)
-    payload = _row_payload(loc, sel, Ea_next)
-    gidx = (sel // Lc) * L + c0 + sel % Lc
     widths = _row_widths(loc, Ea_next)
-    t_ent, t_idx = compact_tails(loc['tails'])
-    ((ent_all, tidx_all), (pay_all, gidx_all)), finish = exchange_varlen_async([(t_ent, t_idx), (payload, gidx)],
-                                                                                world, group)
-    last_exchange.update(rows_sent=int(payload.shape[0]), rows_padded=int(pay_all.shape[1]), rows_chunk=B * Lc,
-                         row_bytes=int(payload.shape[1]), tails_sent=int(t_idx.shape[0]),
-                         tails_padded=int(tidx_all.shape[1]), tails_dense=int(loc['tails'][..., 0].numel()))
-    _apply_clock_offsets(full['Bt'], sums, Lc)
-    # (6) n-gram memory: per-group summaries of every chunk, then the streak maps
-    ng = ngram_sort(layer, full, c0, Lc, half)
+    # (5) the non-empty tails and the feature / value rows of the tail positions, padded to the largest rank's count
+    if caps is None:
+        counts = exchange_counts(local_counts, world, group)
+        n_tails, n_rows = counts[rank]
+        sel = compact(flags, n_rows)
+        t_ent, t_idx = compact_tails(loc['tails'], n_tails)
+        over = None
+    else:
+        n_tails, n_rows = caps
+        counts = [list(caps)] * world
+        sel = compact_cap(flags, n_rows)
+        flat = loc['tails'].reshape(-1, loc['tails'].shape[-1])
+        t_idx = compact_cap(t_ne, n_tails)
+        t_ent = flat[t_idx.clamp(min=0)].contiguous().view(torch.uint8)
+        over = (local_counts[0] > n_tails) | (local_counts[1] > n_rows)
+    payload = _row_payload(loc, sel.clamp(min=0), Ea_next)
+    gidx = torch.where(sel >= 0, (sel // Lc) * L + c0 + sel % Lc, -1)
+    ((ent_all, tidx_all), (pay_all, gidx_all)), finish = exchange_varlen_async(
+        [(t_ent, t_idx), (payload, gidx)], world, group, counts, async_op=caps is None)
+    last_exchange.update(rows_padded=int(pay_all.shape[1]), rows_chunk=B * Lc, row_bytes=int(payload.shape[1]),
+                         tails_padded=int(tidx_all.shape[1]), tails_dense=int(t_ne.numel()), counts=local_counts)
     full.update(_full_rows(loc, B, L, c0, c1, firsts[rank + 1] if rank + 1 < world else None))
     finish()
     for q in range(rank):
@@ -587,9 +654,57 @@ def forward(layer, E, h, tokens=None, group=None):
     _, rmap = racha_chunk(layer, vistos, loc['beta'], None, half, want_racha=False)
     maps = exchange_racha_maps(rmap, world, group)
     racha, _ = racha_chunk(layer, vistos, loc['beta'], racha_before(maps, rank), half)
-    status = carry_violations(sums=sums, maps=maps, keys=keys).clamp(max=1).to(torch.int32).mul(
-        _lib.ASRN_ERR_DATA).view(1)
-    out = _phase2(layer, loc, full, tails, (vistos, hawkes, racha), h, c0, c1, half,
-                  status)
-    _defer_status(status)
-    return out
+    bad = carry_violations(sums=sums, maps=maps, keys=keys).clamp(max=1)
+    if over is not None:
+        bad = torch.maximum(bad, over.to(bad.dtype))
+    status = bad.to(torch.int32).mul(_lib.ASRN_ERR_DATA).view(1)
+    out = _phase2(layer, loc, full, tails, (vistos, hawkes, racha), h, c0, c1, half, status)
+    return out, status, local_counts
+
+
+class ShardedForward:
+    """The sharded forward of one rank for fixed shapes, replayed as one CUDA graph (NCCL collectives included): no
+    host synchronisation and no per-op launch cost inside a step. The first (eager) pass measures how many tail rows
+    and tails each rank publishes; the exchange is then sized to the largest count of any rank times `margin` (plus
+    `extra`), and a later input whose counts exceed that is reported like inconsistent state (ShardExchangeError at
+    the next call or check_exchange): build a new ShardedForward for it. Every rank builds and calls it in the same
+    order; call close() (or drop it) before destroying the process group."""
+
+    def __init__(self, layer, E, h, tokens=None, group=None, margin=1.5, extra=64):
+        import torch.distributed as dist
+        _check(layer, E, h, tokens)
+        self.layer, self.group = layer, group
+        self.device = E.device
+        self.E = E.float().contiguous().clone()
+        self.h = h.float().contiguous().clone()
+        self.tokens = None if tokens is None else tokens.contiguous().clone()
+        world = dist.get_world_size(group)
+        with torch.no_grad():
+            _, _, cnt = _forward(layer, self.E, self.h, self.tokens, group, None)
+            counts = exchange_counts(cnt, world, group)
+        self.caps = tuple(int(max(c[j] for c in counts) * margin) + extra for j in range(2))
+        side = torch.cuda.Stream(self.device)
+        side.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(side), torch.no_grad():           # warm the capacity path (allocations, kernels)
+            _forward(layer, self.E, self.h, self.tokens, group, self.caps)
+        torch.cuda.current_stream(self.device).wait_stream(side)
+        torch.cuda.synchronize(self.device)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph), torch.no_grad():
+            self.out, self.status, _ = _forward(layer, self.E, self.h, self.tokens, group, self.caps)
+
+    def __call__(self, E, h, tokens=None):
+        """h' of this rank's chunk for new inputs of the captured shapes (the returned tensor is overwritten by the
+        next call)."""
+        _raise_reported(self.device, block=False)
+        self.E.copy_(E)
+        self.h.copy_(h)
+        if self.tokens is not None:
+            self.tokens.copy_(tokens)
+        self.graph.replay()
+        _defer_status(self.status)
+        return self.out
+
+    def close(self):
+        self.graph = None
+        self.out = self.status = None

@@ -710,13 +710,27 @@ def leg_cfg4(args, dev, rank, world):
                 return layer(Ed, hd, xd)
             return shard.forward(layer, Ed, hd, xd)
 
+    sf = None
+    if world > 1 and not args.eager:
+        # the sharded forward captured as one CUDA graph per rank (NCCL collectives inside)
+        with torch.no_grad(), torch.autocast('cuda', dtype=torch.bfloat16):
+            sf = shard.ShardedForward(layer, Ed, hd, xd)
+        step = lambda: sf(Ed, hd, xd)                      # noqa: E731
     warm = warm_up(step, args.warmup, world)
-    run, mode, graph = graph_or_eager(step, args.eager or world > 1)
+    if sf is not None:
+        run, mode, graph = step, 'cuda_graph', None
+    else:
+        run, mode, graph = graph_or_eager(step, args.eager or world > 1)
     if world > 1:
         import torch.distributed as dist
         dist.barrier()
     steps = max(5, args.steps // 2)
     ms, step_ms = timed(run, steps)
+    if sf is not None:
+        torch.cuda.synchronize()
+        shard.check_exchange(dev)
+        exch = {k: (v.tolist() if hasattr(v, 'tolist') else v) for k, v in shard.last_exchange.items()}
+        sf.close()
     del run, graph
     ms, = _max_over_ranks([ms], dev, world)
     cpu = None
@@ -742,9 +756,11 @@ def leg_cfg4(args, dev, rank, world):
            'ms_per_step': ms / steps, 'step_ms': spread(step_ms), 'higher_is_better': True, 'scaling': 'strong',
            'dtype': 'bf16', 'data': 'synthetic', 'launch': mode,
            'config': {'workload': 'cfg4 layer: ASRNLayer(512) forward, 1 x %d tokens, bf16 autocast, fp32 E/h' % L,
-                      'parallelism': ('sequence-sharded over %d GPUs (NCCL all-gathers of the halo, clock offsets, '
-                                      'bucket tails, per-position features, n-gram summaries and streak maps)'
+                      'parallelism': ('sequence-sharded over %d GPUs, each rank one CUDA graph (NCCL all-gathers of '
+                                      'the halo, clock offsets, per-position scalars, the non-empty bucket tails and '
+                                      'the feature rows of the tail positions, n-gram summaries and streak maps)'
                                       % world) if world > 1 else 'single GPU'},
+           'exchange': exch if world > 1 and sf is not None else None,
            'roofline': {'bound': 'hbm', 'kernel': 'whole layer forward (per GPU)', 'achieved': achieved, 'peak': hbm,
                         'peak_source': src, 'unit': 'GB/s', 'frac': achieved / hbm,
                         'algorithmic_bytes_per_token': CFG4_BYTES_PER_TOKEN}}

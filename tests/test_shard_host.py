@@ -268,14 +268,18 @@ def test_scattered_rows_land_at_the_key_and_the_value_after_it():
     sel = torch.tensor([1, 3])
     payload = shard._row_payload(loc, sel, Ea_next)
     widths = shard._row_widths(loc, Ea_next)
-    full = {k: torch.zeros((B, L) + tuple(loc[k].shape[2:]), dtype=torch.bfloat16) for k in ('phi', 'Qc', 'Kc', 'Ea')}
+    full = {k: torch.zeros((B * L + 1,) + tuple(loc[k].shape[2:]), dtype=torch.bfloat16)   # + the spare row
+            for k in ('phi', 'Qc', 'Kc', 'Ea')}
     padded = torch.cat([payload, torch.zeros_like(payload[:1])])          # a padding row, index -1
     shard._scatter_rows(full, padded, torch.tensor([1, 3, -1]), widths, L)
-    assert torch.equal(full['phi'][0, 1], loc['phi'][0, 1]) and torch.equal(full['phi'][0, 3], loc['phi'][0, 3])
-    assert torch.equal(full['Kc'][0, 3], loc['Kc'][0, 3]) and full['phi'][0, 2].abs().sum() == 0
-    assert torch.equal(full['Ea'][0, 2], loc['Ea'][0, 2]) and torch.equal(full['Ea'][0, 4], nxt[0, 0])
+    f = {k: v[:B * L].view((B, L) + tuple(v.shape[1:])) for k, v in full.items()}
+    assert torch.equal(f['phi'][0, 1], loc['phi'][0, 1]) and torch.equal(f['phi'][0, 3], loc['phi'][0, 3])
+    assert torch.equal(f['Kc'][0, 3], loc['Kc'][0, 3]) and f['phi'][0, 2].abs().sum() == 0
+    assert torch.equal(f['Ea'][0, 2], loc['Ea'][0, 2]) and torch.equal(f['Ea'][0, 4], nxt[0, 0])
+    assert f['phi'][0, L - 1].abs().sum() == 0                          # the padding row went to the spare row
+    before = full['Ea'].clone()
     shard._scatter_rows(full, payload[1:], torch.tensor([L - 1]), widths, L)   # last position: no value row
-    assert full['Ea'].shape == (B, L, d)
+    assert torch.equal(full['Ea'][:B * L], before[:B * L])
 
 
 def test_compact_tails_round_trip():
@@ -297,3 +301,19 @@ def test_compact_tails_round_trip():
         ent[q, :ix.numel()] = e
         idx[q, :ix.numel()] = ix
     assert torch.equal(shard.expand_tails(ent, idx, tails.shape[1:]), tails)
+
+
+def test_compact_equals_nonzero():
+    """The synchronisation-free compactions of set flags give nonzero()'s indices (padded with -1 up to a capacity,
+    or cut at it)."""
+    from asrn_b200 import shard
+    g = torch.Generator().manual_seed(3)
+    for n in (1, 17, 1000):
+        flags = torch.rand(n, generator=g) < 0.3
+        want = flags.nonzero().squeeze(1)
+        m = want.numel()
+        assert torch.equal(shard.compact(flags, m), want)
+        padded = shard.compact_cap(flags, m + 5)
+        assert torch.equal(padded[:m], want) and (padded[m:] == -1).all()
+        if m > 2:
+            assert torch.equal(shard.compact_cap(flags, m - 2), want[:m - 2])
