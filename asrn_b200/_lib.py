@@ -78,6 +78,7 @@ _SIGS = {
     'asrn_gen_ring_insert': (ctypes.c_int, [ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                             _P, _P, _P, _P, _P]),
     'asrn_gen_front': (ctypes.c_int, [_P] * 17),
+    'asrn_gen_front_residual': (ctypes.c_int, [_P] * 19),
     'asrn_local_in': (ctypes.c_int, [ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, _P, _P, _P, _P, _P,
                                      ctypes.c_float, _P, ctypes.c_int32, _P]),
     'asrn_local_mid': (ctypes.c_int, [ctypes.c_int64, ctypes.c_int32, _P, _P, _P, _P, _P, ctypes.c_float, _P,

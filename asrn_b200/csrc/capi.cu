@@ -638,10 +638,10 @@ int asrn_gen_ring_insert(int64_t B, int32_t T, int32_t nb, int32_t C, const int6
   return launch_ring_insert(B, T, nb, C, t_pos, ids_t, ring, count, as_stream(stream));
 }
 
-int asrn_gen_front(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared, const float* h,
-                   const float* e_t, const float* e_prev, const int64_t* tokens, void* Qc, void* Kc, double* beta,
-                   float* log_alfa, float* glogit, float* sig, void* phi, uint16_t* ids, float* scratch,
-                   void* stream) {
+static int gen_front(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared, const float* h,
+                     const void* y, float* h_sum, const float* e_t, const float* e_prev, const int64_t* tokens,
+                     void* Qc, void* Kc, double* beta, float* log_alfa, float* glogit, float* sig, void* phi,
+                     uint16_t* ids, float* scratch, void* stream) {
   int st = check_config(cfg);
   if (st) return st;
   if ((st = check_weights(w))) return st;
@@ -661,7 +661,26 @@ int asrn_gen_front(const asrn_layer_config* cfg, const asrn_layer_weights* w, co
   a.Qc = Qc; a.Kc = Kc; a.beta = beta; a.log_alfa = log_alfa; a.glogit = glogit; a.sig = sig; a.phi = phi; a.ids = ids;
   a.dots = scratch;
   a.status = reinterpret_cast<int*>(const_cast<char*>(prep) + pl.status);
+  a.y = y;
+  a.h_sum = h_sum;
   return launch_gen_front(a, cfg->half != 0, as_stream(stream));
+}
+
+int asrn_gen_front(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared, const float* h,
+                   const float* e_t, const float* e_prev, const int64_t* tokens, void* Qc, void* Kc, double* beta,
+                   float* log_alfa, float* glogit, float* sig, void* phi, uint16_t* ids, float* scratch,
+                   void* stream) {
+  return gen_front(cfg, w, prepared, h, nullptr, nullptr, e_t, e_prev, tokens, Qc, Kc, beta, log_alfa, glogit, sig,
+                   phi, ids, scratch, stream);
+}
+
+int asrn_gen_front_residual(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared,
+                            const float* h, const void* y, float* h_sum, const float* e_t, const float* e_prev,
+                            const int64_t* tokens, void* Qc, void* Kc, double* beta, float* log_alfa, float* glogit,
+                            float* sig, void* phi, uint16_t* ids, float* scratch, void* stream) {
+  if (cfg && cfg->B > 0 && (!y || !h_sum)) return ASRN_ERR_ARG;
+  return gen_front(cfg, w, prepared, h, y, h_sum, e_t, e_prev, tokens, Qc, Kc, beta, log_alfa, glogit, sig, phi, ids,
+                   scratch, stream);
 }
 
 int asrn_gen_gate(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared, const float* h,

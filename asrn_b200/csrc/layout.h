@@ -173,6 +173,8 @@ struct GenFrontArgs {
   uint16_t* ids;           // (B, T)
   float* dots;             // optional scratch (B, 2cf + 3 + 3m): the front split over more blocks
   int* status;             // device status word (bounded waits)
+  const void* y;           // optional act (B, d): the previous local block's MLP output, added to h first
+  float* h_sum;            // with y: (B, d) receives h + y (the gate's residual input)
 };
 
 // One generation step of one layer: B sequences, the new token at position t of caches of `cap` positions.

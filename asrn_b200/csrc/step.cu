@@ -112,9 +112,11 @@ __global__ void __launch_bounds__(kFrontThreads) k_gen_front(GenFrontArgs a) {
   float* s_red = s_phi + ((P + 3) & ~3);   // 32, then the weight double buffer (16-byte aligned)
 
   const float* hrow = a.h + b * d;
+  const AT* yrow = a.y ? reinterpret_cast<const AT*>(a.y) + b * d : nullptr;
   float s = 0.f;
   for (int j = tid; j < d; j += kFrontThreads) {
-    const float x = hrow[j];
+    const float x = yrow ? __fadd_rn(hrow[j], A::load(yrow + j)) : hrow[j];   // the residual h + y of the block
+    if (a.h_sum) a.h_sum[b * d + j] = x;
     s_h[j] = x;
     s += x;
     s_e[j] = act<Half>(a.e_t[b * d + j]);
@@ -300,9 +302,11 @@ __global__ void __launch_bounds__(kF1Threads) k_gen_front_dots(GenFrontArgs a) {
                    : "memory");
   }
   const float* hrow = a.h + b * d;
+  const AT* yrow = a.y ? reinterpret_cast<const AT*>(a.y) + b * d : nullptr;
   float s = 0.f;
   for (int j = tid; j < d; j += kF1Threads) {
-    const float x = hrow[j];
+    const float x = yrow ? __fadd_rn(hrow[j], Act<Half>::load(yrow + j)) : hrow[j];   // the residual h + y
+    if (a.h_sum && slice == 0) a.h_sum[b * d + j] = x;
     s_h[j] = x;
     s += x;
     s_e[j] = act<Half>(a.e_t[b * d + j]);

@@ -236,7 +236,7 @@ class Writer:
                 _lib.check(lib.asrn_local_gelu(f.numel(), _lib.ptr(f), half, s), 'asrn_local_gelu')
                 h, y = h1, F.linear(f, w2, b2)
                 if i in m.pos_largo:
-                    h = self._step_layer(self.layers[j], e_t, h + y, tok)
+                    h = self._step_layer(self.layers[j], e_t, h, y, tok)     # the layer's front adds y to h
                     y = None
                     j += 1
             _lib.check(lib.asrn_local_in(B, d, 1, _lib.ptr(h), _lib.ptr(y), None, _lib.ptr(m.ln_f.weight),
@@ -247,8 +247,9 @@ class Writer:
             self.t_dev += 1
         return lg
 
-    def _step_layer(self, st, e_t, h, tok):
-        """One ASRN layer for the new tokens: front (context + hash), n-gram memory, candidate attention, gate."""
+    def _step_layer(self, st, e_t, h_prev, y, tok):
+        """One ASRN layer for the new tokens: front (context + hash, on h = h_prev + y, formed in the front kernel),
+        n-gram memory, candidate attention, gate."""
         capa, half, B = st.capa, self.half, self.B
         dev = tok.device
         T, nb, C, n, cf, d = capa.n_tablas, capa.n_bits, capa.chunk, capa.vistos, capa.confirmar, capa.d
@@ -269,10 +270,12 @@ class Writer:
         nq = 2 * cf + 3 + 3 * cfg.hidden
         if self._front_scratch is None or self._front_scratch.numel() < B * nq:
             self._front_scratch = torch.empty(B * nq, dtype=torch.float32, device=dev)
-        _lib.check(lib.asrn_gen_front(cr, wr, pr, _lib.ptr(h), _lib.ptr(e_t), _lib.ptr(self.e_last), _lib.ptr(tok),
-                                      _lib.ptr(qc), _lib.ptr(kc), _lib.ptr(beta), _lib.ptr(la), _lib.ptr(glogit),
-                                      _lib.ptr(sig), _lib.ptr(phi), _lib.ptr(ids), _lib.ptr(self._front_scratch), s),
-                   'asrn_gen_front')
+        h = torch.empty(B, d, dtype=torch.float32, device=dev)
+        _lib.check(lib.asrn_gen_front_residual(cr, wr, pr, _lib.ptr(h_prev), _lib.ptr(y), _lib.ptr(h), _lib.ptr(e_t),
+                                               _lib.ptr(self.e_last), _lib.ptr(tok), _lib.ptr(qc), _lib.ptr(kc),
+                                               _lib.ptr(beta), _lib.ptr(la), _lib.ptr(glogit), _lib.ptr(sig),
+                                               _lib.ptr(phi), _lib.ptr(ids), _lib.ptr(self._front_scratch), s),
+                   'asrn_gen_front_residual')
         vistos = torch.empty(B, n, dtype=torch.uint8, device=dev)
         hawkes = torch.empty(B, n, dtype=torch.float32, device=dev)
         racha = torch.empty(B, dtype=torch.float32, device=dev)

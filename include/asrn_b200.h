@@ -332,6 +332,13 @@ int asrn_gen_front(const asrn_layer_config* cfg, const asrn_layer_weights* w, co
                    const float* e_t, const float* e_prev, const int64_t* tokens, void* Qc, void* Kc, double* beta,
                    float* log_alfa, float* glogit, float* sig, void* phi, uint16_t* ids, float* scratch,
                    void* stream);
+/* asrn_gen_front on h + y, where y (act, (B, d)) is the previous local block's MLP output that the model adds to the
+ * residual stream before the ASRN layer (asrn/nucleo.py:1816-1822): the sum is formed in the kernel that reads h and
+ * written to h_sum (float32 (B, d), the gate's residual input), so the step needs no separate add. */
+int asrn_gen_front_residual(const asrn_layer_config* cfg, const asrn_layer_weights* w, const void* prepared,
+                            const float* h, const void* y, float* h_sum, const float* e_t, const float* e_prev,
+                            const int64_t* tokens, void* Qc, void* Kc, double* beta, float* log_alfa, float* glogit,
+                            float* sig, void* phi, uint16_t* ids, float* scratch, void* stream);
 
 /* Gate of the new tokens (asrn_gate's semantics for cfg->B * cfg->L rows, no workspace): W_ov is spread over d / 32
  * blocks. cbuf / sigma (both or neither; bf16 mode): the operand and gate values asrn_gen_attend precomputed. */
