@@ -112,6 +112,12 @@ _SIGS = {
     'asrn_local_block': (ctypes.c_int, [ctypes.c_int64, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                         _P, _P, _P, _P, ctypes.c_float, _P, _P, _P, _P, ctypes.c_float, _P, _P, _P, _P,
                                         _P, ctypes.c_size_t, _P, _P]),
+    'asrn_bucket_attn_forward': (ctypes.c_int, [ctypes.c_int64, ctypes.c_int64] + [ctypes.c_int32] * 6 + [_P] * 12
+                                 + [ctypes.c_float, ctypes.c_float, ctypes.c_int32, _P, _P, _P]),
+    'asrn_bucket_attn_backward': (ctypes.c_int, [ctypes.c_int64, ctypes.c_int64] + [ctypes.c_int32] * 6 + [_P] * 12
+                                  + [ctypes.c_float, ctypes.c_float, ctypes.c_int32] + [_P] * 11),
+    'asrn_scan_forward': (ctypes.c_int, [ctypes.c_int64, ctypes.c_int64, _P, _P, _P, _P]),
+    'asrn_scan_backward': (ctypes.c_int, [ctypes.c_int64, ctypes.c_int64, _P, _P, _P, _P, _P, _P]),
     'asrn_sampler_seed_state': (ctypes.c_int, [ctypes.c_uint64, _P]),
     'asrn_sampler_jump_poly': (ctypes.c_int, [ctypes.c_uint64, _P]),
     'asrn_sampler_fill': (ctypes.c_int, [ctypes.c_int64, ctypes.c_int64, ctypes.c_int32, _P, _P, _P, _P, _P]),

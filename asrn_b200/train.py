@@ -1,0 +1,139 @@
+"""Training on the device: the bucket attention with its backward and the linear-recurrence scan with its backward,
+as autograd functions over the C-ABI kernels (asrn_bucket_attn_forward / _backward, asrn_scan_forward / _backward).
+
+BucketAttention.apply takes what the reference's fused attention takes (asrn/nucleo.py:461-515, called by
+asrn/estable.py:282-291): phi, V, Qc, Kc, the clock Bt, log_alfa, w_sufijo, gamma, the previous signatures Pf, the
+bucket order and sorted ids of every (sequence, table) row, T, C and the two score scales; it returns the attention
+output summed over the tables (B, L, d) and the per-table signals (B T, L, 3). Its backward recomputes the scores
+(nothing of (windows, C, 2C) is stored) and fills per-slot buffers without atomics, added here in a fixed order
+(asrn/nucleo.py:491-515). escaneo(a, b) is S_i = a_i S_{i-1} + b_i along the last dimension with the backward of
+asrn/nucleo.py:518-537. Both run on CUDA only and raise elsewhere."""
+import torch
+
+from . import _lib
+
+
+def _p(t):
+    return None if t is None else t.data_ptr()
+
+
+def _need_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError('asrn_b200.train runs on CUDA tensors only')
+
+
+def _clock_parts(Bt, Bt_bajo):
+    """The clock as fp32 high and low parts: high = Bt in fp32, low = the rest of a 64-bit clock (asrn/estable.py:
+    282-287), or the given low part, or zero for an fp32 clock."""
+    hi = Bt.detach().float().contiguous()
+    if Bt_bajo is not None:
+        lo = Bt_bajo.detach().float().contiguous()
+    elif Bt.dtype == torch.float64:
+        lo = (Bt.detach() - hi.double()).float().contiguous()
+    else:
+        lo = torch.zeros_like(hi)
+    return hi, lo
+
+
+class BucketAttention(torch.autograd.Function):
+    """Bucket attention of all tables, forward and backward on the device."""
+
+    @staticmethod
+    def forward(ctx, phi, V, Qc, Kc, Bt, log_alfa, w, gamma, Pf, orden, ids_o, T, C, escala_phi, escala_c,
+                Bt_bajo=None):
+        _need_cuda(phi, V, Qc, Kc, Bt, log_alfa, w, gamma, Pf, orden, ids_o)
+        B, L, P = phi.shape
+        D, CF, K = V.shape[-1], Qc.shape[-1], Pf.shape[-1]
+        half = phi.dtype == torch.bfloat16
+        act = torch.bfloat16 if half else torch.float32
+        if any(x.dtype != act for x in (phi, V, Qc, Kc)):
+            raise TypeError('phi, V, Qc and Kc must all be float32 or all bfloat16')
+        ent = [x.contiguous() for x in (phi, Qc, Kc, V)]
+        pf = Pf.detach().float().contiguous()
+        hi, lo = _clock_parts(Bt, Bt_bajo)
+        la = log_alfa.detach().float().contiguous()
+        orden32 = orden.to(torch.int32).contiguous()
+        ids32 = ids_o.to(torch.int32).contiguous()
+        w32, g32 = w.detach().float().contiguous(), gamma.detach().float().contiguous()
+        out = torch.empty(B * T, L, D, dtype=act, device=V.device)
+        sen = torch.empty(B * T, L, 3, dtype=torch.float32, device=V.device)
+        _lib.check(_lib.lib().asrn_bucket_attn_forward(
+            B, L, T, C, P, CF, K, D, *[_p(x) for x in ent], _p(pf), _p(hi), _p(lo), _p(la), _p(orden32), _p(ids32),
+            _p(w32), _p(g32), float(escala_phi), float(escala_c), int(half), _p(out), _p(sen),
+            _lib.stream_ptr(V.device)), 'asrn_bucket_attn_forward')
+        ctx.save_for_backward(*ent, pf, hi, lo, la, orden32, ids32, w32, g32)
+        ctx.datos = (B, L, P, D, CF, K, T, C, float(escala_phi), float(escala_c), half,
+                     [x.dtype for x in (phi, Qc, Kc, V, Bt, log_alfa)])
+        ctx.mark_non_differentiable(sen)
+        return out.view(B, T, L, D).sum(1), sen
+
+    @staticmethod
+    def backward(ctx, dsalida, _dsen):
+        phi, Qc, Kc, V, pf, hi, lo, la, orden32, ids32, w32, g32 = ctx.saved_tensors
+        B, L, P, D, CF, K, T, C, escala_phi, escala_c, half, tipos = ctx.datos
+        BT, dev = B * T, V.device
+        NB = (L + C - 1) // C
+        act = V.dtype
+        f32 = dict(dtype=torch.float32, device=dev)
+        G = dict(phi_q=torch.empty(BT, L, P, dtype=act, device=dev), qc=torch.empty(BT, L, CF, dtype=act, device=dev),
+                 b_q=torch.empty(BT, L, **f32), phi_k=torch.empty(2, BT, L, P, dtype=act, device=dev),
+                 kc=torch.empty(2, BT, L, CF, dtype=act, device=dev), v=torch.empty(2, BT, L, D, dtype=act, device=dev),
+                 la=torch.empty(2, BT, L, **f32), b_k=torch.empty(2, BT, L, **f32))
+        partes = torch.empty(BT, NB, K + 2, **f32)
+        dout = dsalida.to(act).contiguous()
+        _lib.check(_lib.lib().asrn_bucket_attn_backward(
+            B, L, T, C, P, CF, K, D, _p(phi), _p(Qc), _p(Kc), _p(V), _p(pf), _p(hi), _p(lo), _p(la), _p(orden32),
+            _p(ids32), _p(w32), _p(g32), escala_phi, escala_c, int(half), _p(dout), _p(G['phi_q']), _p(G['qc']),
+            _p(G['b_q']), _p(G['phi_k']), _p(G['kc']), _p(G['v']), _p(G['la']), _p(G['b_k']), _p(partes),
+            _lib.stream_ptr(dev)), 'asrn_bucket_attn_backward')
+
+        def sumar(q, k):               # the tables (and the two places of every key) -> (B, L, ...), in fp32
+            total = k.view(2, B, T, *k.shape[2:]).sum((0, 2), dtype=torch.float32)
+            return total if q is None else total + q.view(B, T, *q.shape[1:]).sum(1, dtype=torch.float32)
+        per_table = partes.view(B, T, NB, K + 2).sum((0, 2))                        # (T, K + 2)
+        tp, tq, tk, tv, tb, tl = tipos
+        return (sumar(G['phi_q'], G['phi_k']).to(tp), sumar(None, G['v']).to(tv),
+                G['qc'].view(B, T, L, CF).sum(1, dtype=torch.float32).to(tq), sumar(None, G['kc']).to(tk),
+                sumar(G['b_q'], G['b_k']).to(tb), sumar(None, G['la']).to(tl), per_table[:, 1:].sum(0),
+                per_table[:, 0] / C, None, None, None, None, None, None, None, None)
+
+
+class _Scan(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, a, b):
+        S = _scan(a, b)
+        ctx.save_for_backward(a, S)
+        return S
+
+    @staticmethod
+    def backward(ctx, g):
+        a, S = ctx.saved_tensors
+        rows, L = a.numel() // a.shape[-1], a.shape[-1]
+        g32 = g.float().contiguous()
+        ga = torch.empty_like(a) if ctx.needs_input_grad[0] else None
+        gb = torch.empty_like(a) if ctx.needs_input_grad[1] else None
+        _lib.check(_lib.lib().asrn_scan_backward(rows, L, _p(a), _p(S), _p(g32), _p(ga), _p(gb),
+                                                 _lib.stream_ptr(a.device)), 'asrn_scan_backward')
+        return ga, gb
+
+
+def _scan(a, b):
+    rows, L = a.numel() // a.shape[-1], a.shape[-1]
+    S = torch.empty_like(a)
+    _lib.check(_lib.lib().asrn_scan_forward(rows, L, _p(a), _p(b), _p(S), _lib.stream_ptr(a.device)),
+               'asrn_scan_forward')
+    return S
+
+
+def escaneo(a, b):
+    """S_i = a_i S_{i-1} + b_i over the last dimension (S_{-1} = 0), fp32, with a gradient when a or b needs one
+    (asrn/nucleo.py:188-197, 518-537)."""
+    _need_cuda(a, b)
+    a, b = torch.broadcast_tensors(a, b)
+    if a.dtype != torch.float32 or b.dtype != torch.float32:
+        raise TypeError('escaneo takes float32 tensors')
+    a, b = a.contiguous(), b.contiguous()
+    if torch.is_grad_enabled() and (a.requires_grad or b.requires_grad):
+        return _Scan.apply(a, b)
+    return _scan(a, b)

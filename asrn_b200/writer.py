@@ -456,7 +456,10 @@ def escribir(modelo, inicio, n_nuevos=200, temperatura=0.8, top_k=40, semilla=0,
                 break
             if k < n_nuevos - 1:
                 lg = w.paso(nxt[:, 0])
+        status = w.status()
         w.cerrar()
+        if any(status):
+            raise RuntimeError(f'generation step status words {status} (asrn_status_string names them)')
         x = text[:, :length]
         if not devolver_logits:
             return x.cpu(), None

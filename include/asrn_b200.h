@@ -199,6 +199,37 @@ int asrn_local_block(int64_t B, int64_t L, int32_t d, int32_t k, int32_t ff, con
                      const void* w2, const float* b2, void* workspace, size_t workspace_bytes, int* status,
                      void* stream);
 
+/* ---- training: bucket attention and scan, forward and backward ---------------------------------------------------
+ * The kernels the reference's training path calls (asrn/nucleo.py:461-537; asrn/estable.py:282-291 in its exact-mask,
+ * 64-bit-clock mode), for one table set: phi (B, L, P), Qc / Kc (B, L, CF), V (B, L, D) all fp32 (half = 0) or all
+ * bf16 (half = 1); Pf (B, L, K) the K previous signatures (NaN before the start); the clock as fp32 high and low
+ * parts Bt_hi, Bt_lo (B, L); log_alfa (B, L); orden / ids_o (B T, L) int32, the positions of each row sorted by
+ * bucket and their bucket ids; w_suf (K + 1), gamma (T) fp32. C <= 32, P <= 256, CF <= 32, K <= 8.
+ * asrn_bucket_attn_forward: out (B T, L, D) in V's type, per table row in text order (the caller sums the T tables);
+ * sen (B T, L, 3) = (any valid key, max valid score or 0, max weight).
+ * asrn_bucket_attn_backward: from dout (B, L, D) in V's type, with the scores recomputed, the per-slot gradient
+ * buffers of asrn/nucleo.py:491-515 (no atomics): g_phi_q (B T, L, P), g_qc (B T, L, CF), g_b_q (B T, L) fp32;
+ * g_phi_k (2, B T, L, P), g_kc (2, B T, L, CF), g_v (2, B T, L, D), g_la (2, B T, L), g_b_k (2, B T, L) fp32 (place
+ * 1: the key in its own block, place 0: in the next block's window); partes (B T, ceil(L / C), K + 2) fp32 = per
+ * program (sum dS dt, then sum dS per suffix length 0 .. K). Gradient types follow their inputs'. */
+int asrn_bucket_attn_forward(int64_t B, int64_t L, int32_t T, int32_t C, int32_t P, int32_t CF, int32_t K, int32_t D,
+                             const void* phi, const void* Qc, const void* Kc, const void* V, const float* Pf,
+                             const float* Bt_hi, const float* Bt_lo, const float* log_alfa, const int32_t* orden,
+                             const int32_t* ids_o, const float* w_suf, const float* gamma, float scale_phi,
+                             float scale_c, int32_t half, void* out, float* sen, void* stream);
+int asrn_bucket_attn_backward(int64_t B, int64_t L, int32_t T, int32_t C, int32_t P, int32_t CF, int32_t K, int32_t D,
+                              const void* phi, const void* Qc, const void* Kc, const void* V, const float* Pf,
+                              const float* Bt_hi, const float* Bt_lo, const float* log_alfa, const int32_t* orden,
+                              const int32_t* ids_o, const float* w_suf, const float* gamma, float scale_phi,
+                              float scale_c, int32_t half, const void* dout, void* g_phi_q, void* g_qc, float* g_b_q,
+                              void* g_phi_k, void* g_kc, void* g_v, float* g_la, float* g_b_k, float* partes,
+                              void* stream);
+/* S_i = a_i S_{i-1} + b_i along each of `rows` rows of L fp32 values (asrn/nucleo.py:188-197), and its backward from
+ * g = dL/dS: ga = dL/da, gb = dL/db (either may be NULL) (asrn/nucleo.py:518-537). */
+int asrn_scan_forward(int64_t rows, int64_t L, const float* a, const float* b, float* S, void* stream);
+int asrn_scan_backward(int64_t rows, int64_t L, const float* a, const float* S, const float* g, float* ga, float* gb,
+                       void* stream);
+
 /* ---- sequence-chunk sharding (one long sequence over several GPUs) --------------------------------------------------
  * Shard r of `world` owns positions [c0, c0 + Lc) of every sequence (L = world * Lc). Its sorted rows hold its own
  * slots and, before each bucket's local run, the up to C earlier-chunk slots some local query has as a candidate (the

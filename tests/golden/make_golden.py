@@ -16,6 +16,8 @@ The generation-state fixture runs the O(1) writer _Escritor(o1=True) (asrn/nucle
 overflow (chunk 4, 2 bits) and records, after the prompt and after every step, each layer's rings and counts
 (_anillo_desde / _anillo_meter, asrn/nucleo.py:1585-1618), the candidate positions of the step (_candidatos,
 asrn/nucleo.py:1621-1631) and the Hawkes state of every n-gram key (_MemoriaHawkes, asrn/nucleo.py:1634-1714).
+The gradient fixtures run the reference's own autograd through _acumular and escaneo (asrn/estable.py:204-263,
+asrn/nucleo.py:188-197, 518-537).
 The fixtures are read by the tests on any machine; this script is the only place that imports the reference.
 """
 import json
@@ -266,6 +268,70 @@ def init_case(name, V, d, n_capas, seed):
     print(f'{name}: {os.path.getsize(path) / 1024:.0f} KB')
 
 
+def grad_case(name, d, B, L, V, opts, seed=0):
+    """Gradients of the bucket attention and of the linear-recurrence scan, from the reference's own autograd on the
+    CPU: _acumular (asrn/estable.py:204-263, backward through torch.bmm, _softmax_valido, _TiempoRelativo,
+    _DesordenarSumar) with phi, V, Qc, Kc, Bt, log_alfa as leaves, loss = sum(salida * G); escaneo (asrn/nucleo.py:
+    188-197, backward _Escaneo, asrn/nucleo.py:518-537) with loss = sum(S * g)."""
+    import asrn
+    import asrn.nucleo as v89
+    torch.manual_seed(seed)
+    capa = asrn.ASRNLayer(d, **opts)
+    _move(capa, seed=seed + 1)
+    capa.eval()
+    x = synthetic.zipf_tokens(B, L, V, 1.1, seed)
+    x = torch.from_numpy(synthetic.plant_repeats(x, 0.25, 4, max(4, L // 4), seed=seed + 1))
+    g = torch.Generator().manual_seed(seed + 7)
+    E = torch.randn(V, d, generator=g)[x]
+    h = torch.randn(B, L, d, generator=g)
+    with torch.no_grad():
+        sig = asrn.firmas_de_piezas(x)
+        Qc, Kc, beta, log_alfa = capa._contexto(h)
+        Bt = beta.cumsum(1)
+        phi, Vv = capa._phi_y_valores(E)
+        ids = capa._ids(phi)
+    T = capa.n_tablas
+    ids_rows = ids.transpose(1, 2).reshape(B * T, L)
+    orden = ids_rows.argsort(dim=-1, stable=True)
+    leaves = {k: t.detach().clone().requires_grad_() for k, t in
+              dict(phi=phi, V=Vv, Qc=Qc, Kc=Kc, Bt=Bt, log_alfa=log_alfa).items()}
+    captured = {}
+    orig_senales = capa._senales
+
+    def grab(salida, senal):
+        captured['senal'] = senal.detach().clone()
+        return orig_senales(salida, senal)
+
+    capa._senales = grab
+    capa._phi_y_valores = lambda E_: (leaves['phi'], leaves['V'])
+    acc = capa._acumular(E, leaves['Qc'], leaves['Kc'], leaves['Bt'], leaves['log_alfa'], sig)
+    G = torch.randn(B, L, d, generator=g)
+    (acc['salida'] * G).sum().backward()
+    out = dict(sig=_np(sig), orden=orden.numpy().astype(np.int32),
+               ids_o=torch.gather(ids_rows, 1, orden).numpy().astype(np.int32), G=_np(G),
+               salida=_np(acc['salida']), senal=_np(captured['senal']), w_sufijo=_np(capa.w_sufijo),
+               gamma=_np(capa.gamma), grad_w_sufijo=_np(capa.w_sufijo.grad), grad_gamma=_np(capa.gamma.grad))
+    for k, t in leaves.items():
+        out[k] = _np(t)
+        out['grad_' + k] = _np(t.grad)
+    # the scan: a in [0, 1) with resets (a = 0), b and the upstream gradient g of normal draws, rows x L
+    a = torch.rand(3, 1000, generator=g, dtype=torch.float64).float()
+    a[:, ::97] = 0
+    a.requires_grad_()
+    b = torch.randn(3, 1000, generator=g).requires_grad_()
+    S = v89.escaneo(a, b)
+    gS = torch.randn(3, 1000, generator=g)
+    (S * gS).sum().backward()
+    out.update(scan_a=_np(a), scan_b=_np(b), scan_S=_np(S), scan_g=_np(gS), scan_grad_a=_np(a.grad),
+               scan_grad_b=_np(b.grad))
+    meta = dict(B=B, L=L, d=d, T=T, nb=capa.n_bits, C=capa.chunk, cf=capa.confirmar, K=capa.sufijo,
+                temperatura=float(capa.temperatura), opts=opts)
+    out['meta'] = np.frombuffer(json.dumps(meta).encode(), dtype=np.uint8)
+    path = os.path.join(HERE, name + '.npz')
+    np.savez_compressed(path, **out)
+    print(f'{name}: {os.path.getsize(path) / 1024:.0f} KB')
+
+
 def main(ref):
     sys.path.insert(0, ref)
     torch.set_num_threads(8)
@@ -282,6 +348,8 @@ def main(ref):
     gen_state_case('gen_state')
     checkpoint_case('ckpt_ref')
     gen_sampled_case('gen_sampled')
+    grad_case('grad_crowded', 64, 2, 300, 40, dict(chunk=16, n_bits=4))
+    grad_case('grad_default', 64, 2, 256, 64, {}, seed=3)
 
 
 if __name__ == '__main__':
@@ -293,6 +361,8 @@ if __name__ == '__main__':
         for case in sys.argv[2:]:
             {'gen_state': lambda: gen_state_case('gen_state'),
              'checkpoint': lambda: checkpoint_case('ckpt_ref'),
-             'gen_sampled': lambda: gen_sampled_case('gen_sampled')}[case]()
+             'gen_sampled': lambda: gen_sampled_case('gen_sampled'),
+             'grad': lambda: (grad_case('grad_crowded', 64, 2, 300, 40, dict(chunk=16, n_bits=4)),
+                              grad_case('grad_default', 64, 2, 256, 64, {}, seed=3))}[case]()
     else:
         main(sys.argv[1])

@@ -90,3 +90,25 @@ def test_synthetic_streams_are_seeded():
     assert np.array_equal(a, b) and a.max() < 50304 and a.min() >= 0
     x = synthetic.config_tokens('cfg2', B=1, L=4096)
     assert x.max() < 256
+
+
+def test_grad_fixture_scan_matches_the_recurrence():
+    """The reference's scan gradients in the gradient fixture follow l_i = g_i + a_{i+1} l_{i+1}, dL/da_i = l_i
+    S_{i-1} (asrn/nucleo.py:518-537), restated here in float64."""
+    import os
+    z = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), 'golden', 'grad_crowded.npz'))
+    a, b, g = (z[k].astype(np.float64) for k in ('scan_a', 'scan_b', 'scan_g'))
+    S = np.zeros_like(a)
+    x = np.zeros(a.shape[0])
+    for i in range(a.shape[1]):
+        x = a[:, i] * x + b[:, i]
+        S[:, i] = x
+    lam = np.zeros_like(a)
+    y = np.zeros(a.shape[0])
+    for i in range(a.shape[1] - 1, -1, -1):
+        y = g[:, i] + (a[:, i + 1] * y if i + 1 < a.shape[1] else 0)
+        lam[:, i] = y
+    assert np.abs(S - z['scan_S']).max() <= 1e-4 * np.abs(S).max()
+    assert np.abs(lam - z['scan_grad_b']).max() <= 1e-4 * np.abs(lam).max()
+    ga = lam * np.concatenate([np.zeros((a.shape[0], 1)), S[:, :-1]], 1)
+    assert np.abs(ga - z['scan_grad_a']).max() <= 1e-4 * np.abs(ga).max()
