@@ -597,6 +597,8 @@ def _forward(layer, E, h, tokens, group, caps):
     caps = (tails, rows): fixed capacities, no host synchronisation (a count above its capacity is recorded in the
     status word). Returns (h' of the chunk, device status word, device (tails, rows) counts of this rank)."""
     import torch.distributed as dist
+    if caps is not None:
+        return _forward_packed(layer, E, h, tokens, group, caps)
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
     half = compute_half('cuda')
@@ -659,6 +661,119 @@ def _forward(layer, E, h, tokens, group, caps):
         bad = torch.maximum(bad, over.to(bad.dtype))
     status = bad.to(torch.int32).mul(_lib.ASRN_ERR_DATA).view(1)
     out = _phase2(layer, loc, full, tails, (vistos, hawkes, racha), h, c0, c1, half, status)
+    return out, status, local_counts
+
+
+def _pack(parts):
+    """Tensors -> one uint8 buffer (each part padded to 8 bytes) and the (dtype, shape, offset) of each part."""
+    segs, meta, off = [], [], 0
+    for t in parts:
+        flat = torch.empty(t.numel(), dtype=t.dtype, device=t.device)     # stride 1 even for size-1 slices
+        b = flat.copy_(t.reshape(-1)).view(torch.uint8)
+        pad = (-b.numel()) % 8
+        if pad:
+            b = torch.cat([b, torch.zeros(pad, dtype=torch.uint8, device=b.device)])
+        segs.append(b)
+        meta.append((t.dtype, tuple(t.shape), off))
+        off += b.numel()
+    return torch.cat(segs), meta
+
+
+def _unpack(buf, meta, i):
+    """Part i of a packed buffer (world, bytes) -> (world,) + its shape, as views."""
+    dt, shape, off = meta[i]
+    n = 1
+    for x in shape:
+        n *= x
+    nb = n * torch.empty(0, dtype=dt).element_size()
+    return buf[:, off:off + nb].contiguous().view(dt).view((buf.shape[0],) + shape)
+
+
+def _all_gather_bytes(buf, world, group):
+    import torch.distributed as dist
+    out = torch.empty(world, buf.numel(), dtype=torch.uint8, device=buf.device)
+    dist.all_gather_into_tensor(out.view(-1), buf, group=group)
+    return out
+
+
+def _forward_packed(layer, E, h, tokens, group, caps):
+    """The sharded forward with fixed exchange capacities caps = (tails, rows) and no host synchronisation, its
+    exchanges packed into four all-gathers: (1) the halo row; (2) in one buffer, the chunk sums of beta, the
+    per-position scalars, the chunk's first bf16 E row, its non-empty bucket tails and the feature / value rows of
+    its tail positions (the value row of a chunk's last position is taken from the next chunk's first row on
+    arrival); (3) the n-gram keys and summaries; (4) the streak maps. The full-length feature buffers are zero-filled
+    first, as in the unpacked path: a masked key's value row still enters the value product with weight 0, so it must
+    hold numbers. A count above its capacity is recorded in the status word."""
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    half = compute_half('cuda')
+    B, Lc, d = E.shape
+    L = world * Lc
+    c0, c1 = rank * Lc, (rank + 1) * Lc
+    T, nb = layer.n_tablas, layer.n_bits
+    cap_t, cap_r = caps
+    E, h = E.float().contiguous(), h.float().contiguous()
+    halo = exchange_halo(E[:, -1], world, rank, group)
+    loc = _phase1(layer, E, h, tokens, halo, half, c0)
+    # what this chunk publishes: its non-empty tails (compacted), the positions in them, their rows
+    tails = loc['tails']
+    C1 = tails.shape[-1]
+    flat = tails.reshape(-1, C1)
+    t_ne = flat[:, 0] != 0
+    t_idx = compact_cap(t_ne, cap_t)
+    t_rows = flat[t_idx.clamp(min=0)]
+    cnt = t_rows[:, 0].long().clamp(0, C1 - 1)
+    used = (torch.arange(C1 - 1, device=E.device) < cnt.unsqueeze(1)) & (t_idx >= 0).unsqueeze(1)
+    b_of = (t_idx.clamp(min=0) // (1 << nb)) // T
+    rel = torch.where(used, t_rows[:, 1:].long() - c0, Lc).clamp(0, Lc)
+    flags = torch.zeros(B * (Lc + 1), dtype=torch.bool, device=E.device)
+    flags.index_fill_(0, (b_of.unsqueeze(1) * (Lc + 1) + rel).view(-1), True)
+    flags = flags.view(B, Lc + 1)[:, :Lc].reshape(-1)
+    sel = compact_cap(flags, cap_r)
+    Ea_next = torch.cat([loc['Ea'][:, 1:], torch.zeros_like(loc['Ea'][:, :1])], 1)   # last row: fixed on arrival
+    widths = _row_widths(loc, Ea_next)
+    payload = _row_payload(loc, sel.clamp(min=0), Ea_next)
+    gidx = torch.where(sel >= 0, (sel // Lc) * L + c0 + sel % Lc, -1)
+    local_counts = torch.stack([t_ne.sum(), flags.sum()])
+    over = (local_counts[0] > cap_t) | (local_counts[1] > cap_r)
+    buf, meta = _pack([loc['Bt'][:, -1], loc['Bt'], loc['beta'], loc['sig'], loc['log_alfa'], loc['Ea'][:, 0],
+                       t_rows, t_idx, payload, gidx])
+    got = _all_gather_bytes(buf, world, group)
+    sums = _unpack(got, meta, 0)                                          # (world, B)
+    full = {}
+    for i, k in ((1, 'Bt'), (2, 'beta'), (3, 'sig'), (4, 'log_alfa')):
+        full[k] = _unpack(got, meta, i).permute(1, 0, 2).reshape(B, L)    # (world, B, Lc) -> (B, L)
+    _apply_clock_offsets(full['Bt'], sums, Lc)
+    firsts = _unpack(got, meta, 5)                                        # (world, B, d)
+    ng = ngram_sort(layer, full, c0, Lc, half)
+    # the feature rows: this chunk's own, the earlier chunks' tail positions, every chunk start's value row
+    for k in _ROW_KEYS + ('Ea',):
+        x = loc[k]
+        t = torch.zeros((B * L + 1,) + tuple(x.shape[2:]), dtype=x.dtype, device=x.device)
+        t[:B * L].view((B, L) + tuple(x.shape[2:]))[:, c0:c1] = x
+        full[k] = t
+    pay_all, gidx_all = _unpack(got, meta, 8), _unpack(got, meta, 9)
+    for q in range(rank):
+        _scatter_rows(full, pay_all[q], gidx_all[q], widths, L)
+    ea = full['Ea'][:B * L].view(B, L, -1)
+    for q in range(1, min(rank + 2, world)):                             # chunk starts up to c1
+        ea[:, q * Lc] = firsts[q]
+    tails_prev = None
+    if rank > 0:
+        ent = _unpack(got, meta, 6)[:rank].contiguous().view(torch.uint8).view(rank, cap_t, -1)
+        tails_prev = expand_tails(ent, _unpack(got, meta, 7)[:rank], tails.shape)
+    keys, summ = exchange_ngram(ng['keys'], ng['summ'], world, group)
+    vistos, hawkes = ngram_finish(layer, full, ng, keys[:rank] if rank > 0 else None,
+                                  summ[:rank] if rank > 0 else None, c0, Lc, half)
+    _, rmap = racha_chunk(layer, vistos, loc['beta'], None, half, want_racha=False)
+    maps = exchange_racha_maps(rmap, world, group)
+    racha, _ = racha_chunk(layer, vistos, loc['beta'], racha_before(maps, rank), half)
+    bad = torch.maximum(carry_violations(sums=sums, maps=maps, keys=keys).clamp(max=1), over.to(torch.int64))
+    status = bad.to(torch.int32).mul(_lib.ASRN_ERR_DATA).view(1)
+    out = _phase2(layer, loc, full, tails_prev, (vistos, hawkes, racha), h, c0, c1, half, status)
+    last_exchange.update(rows_padded=cap_r, rows_chunk=B * Lc, row_bytes=int(payload.shape[1]), tails_padded=cap_t,
+                         tails_dense=int(t_ne.numel()), counts=local_counts, packed_bytes=int(buf.numel()))
     return out, status, local_counts
 
 

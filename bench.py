@@ -330,14 +330,20 @@ def graph_or_eager(step, eager):
         return step, 'eager (graph capture failed: %s)' % type(exc).__name__, None
 
 
-def timed(run, steps, clocks=None):
-    """K back-to-back steps between two CUDA events on the current stream: (total ms, per-step ms list)."""
+def timed(run, steps, clocks=None, barrier=False):
+    """K back-to-back steps between two CUDA events on the current stream: (total ms, per-step ms list). barrier:
+    every rank calls this, and the ranks meet at a barrier after the collector ran and the device went idle, so the
+    first step's collectives do not wait for a rank still collecting."""
     import torch
+    import torch.distributed as dist
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     marks = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     gc.collect()
     gc.disable()                  # no collector pause while the steps are enqueued
     torch.cuda.synchronize()
+    if barrier and dist.is_available() and dist.is_initialized() and dist.get_world_size() > 1:
+        dist.barrier()
+        torch.cuda.synchronize()
     w0 = time.time()
     t0.record()
     for i in range(steps):
@@ -588,7 +594,7 @@ def run_ours(args):
         kern, ours_k, names = count_graph_kernels(graph) if graph is not None else (None, None, None)
         if world > 1:
             dist.barrier()
-        ms, step_ms = timed(run, args.steps, clocks)
+        ms, step_ms = timed(run, args.steps, clocks, barrier=True)
         if world > 1:
             dist.barrier()
         clk = clocks.stop()
@@ -725,7 +731,7 @@ def leg_cfg4(args, dev, rank, world):
         import torch.distributed as dist
         dist.barrier()
     steps = max(5, args.steps // 2)
-    ms, step_ms = timed(run, steps)
+    ms, step_ms = timed(run, steps, barrier=True)
     if sf is not None:
         torch.cuda.synchronize()
         shard.check_exchange(dev)

@@ -317,3 +317,21 @@ def test_compact_equals_nonzero():
         assert torch.equal(padded[:m], want) and (padded[m:] == -1).all()
         if m > 2:
             assert torch.equal(shard.compact_cap(flags, m - 2), want[:m - 2])
+
+
+def test_pack_unpack_round_trip():
+    """The packed exchange buffer: parts of mixed types and shapes (a size-1 column slice included, whose stride is
+    not 1) come back unchanged from a (world, bytes) buffer."""
+    from asrn_b200.shard import _pack, _unpack
+    g = torch.Generator().manual_seed(0)
+    Bt = torch.randn(1, 4096, dtype=torch.float64, generator=g)
+    parts = [Bt[:, -1], Bt, torch.randint(0, 9, (3, 5), dtype=torch.int32, generator=g),
+             torch.randn(2, 3, generator=g).to(torch.bfloat16), torch.randint(0, 2, (7,), dtype=torch.uint8,
+                                                                               generator=g)]
+    buf, meta = _pack(parts)
+    assert buf.dtype == torch.uint8 and buf.numel() % 8 == 0
+    world = torch.stack([buf, buf])
+    for i, t in enumerate(parts):
+        got = _unpack(world, meta, i)
+        assert got.shape == (2,) + tuple(t.shape)
+        assert torch.equal(got[1], t) and got.dtype == t.dtype
