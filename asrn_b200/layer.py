@@ -50,7 +50,8 @@ def compute_half(device_type='cuda'):
 
 
 class _LayerForward(torch.autograd.Function):
-    """Forward through the C ABI; this build has no backward (the reference's training path is out of scope)."""
+    """The fused inference forward through the C ABI. It keeps no intermediates, so it has no backward: when a
+    gradient is wanted ASRNLayer.forward takes the training path (asrn_b200.train.layer_forward_train) instead."""
 
     @staticmethod
     def forward(ctx, layer, E, h, piezas, half, ngram):
@@ -58,7 +59,8 @@ class _LayerForward(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, *grads):
-        raise NotImplementedError('asrn_b200 implements the ASRN layer forward only (no backward kernels)')
+        raise NotImplementedError('the fused forward has no backward; ASRNLayer.forward uses the training path when '
+                                  'a gradient is wanted')
 
 
 class ASRNLayer(nn.Module):
@@ -112,13 +114,16 @@ class ASRNLayer(nn.Module):
 
     # ---- device-side weights -------------------------------------------------------------------------------------
 
-    def _check_supported(self):
+    def _check_protections(self):
         p = self.protecciones
         if not (p.mascara_exacta and p.reloj_64):
             raise NotImplementedError('asrn_b200 implements the default protections (exact mask, 64-bit clock); '
                                       'Protecciones.ninguna() is not available in this build')
+
+    def _check_supported(self):
+        self._check_protections()
         if self.training and self.drop.p > 0:
-            raise NotImplementedError('dropout at training time is not implemented (forward-only build)')
+            raise NotImplementedError('dropout at training time runs on the training path only (a gradient wanted)')
 
     def _weights(self, device):
         """LayerWeights of the current parameters (contiguous device copies, cast to the reference's dtypes)."""
@@ -159,7 +164,17 @@ class ASRNLayer(nn.Module):
     def forward(self, E, h, piezas=None, ngram=None):
         """E (B, L, d) token vectors, h (B, L, d) state, piezas (B, L) token ids (or None: signatures E . r_firma).
         Returns h' (B, L, d). ngram: the n-gram sort of piezas made by ngram_sort() (by this layer or another one with
-        the same vistos and c_vistos); the layer then skips its own sort (the result is the same)."""
+        the same vistos and c_vistos); the layer then skips its own sort (the result is the same).
+        When a gradient is wanted (grad enabled and E or h requiring one, or the layer training with parameters that
+        do), the differentiable training path runs (asrn_b200.train.layer_forward_train: the bucket attention and
+        scans on the training kernels, forward and backward); otherwise the fused inference forward."""
+        if torch.is_grad_enabled() and (E.requires_grad or h.requires_grad or
+                                        (self.training and any(q.requires_grad for q in self.parameters()))):
+            from .train import layer_forward_train
+            self._check_protections()
+            if not (E.is_cuda and h.is_cuda):
+                raise RuntimeError('asrn_b200.ASRNLayer runs on CUDA tensors only (there is no CPU implementation)')
+            return layer_forward_train(self, E, h, piezas)
         half = compute_half(h.device.type) if h.is_cuda else False
         return _LayerForward.apply(self, E, h, piezas, half, ngram)
 

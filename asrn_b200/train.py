@@ -8,6 +8,8 @@ output summed over the tables (B, L, d) and the per-table signals (B T, L, 3). I
 (nothing of (windows, C, 2C) is stored) and fills per-slot buffers without atomics, added here in a fixed order
 (asrn/nucleo.py:491-515). escaneo(a, b) is S_i = a_i S_{i-1} + b_i along the last dimension with the backward of
 asrn/nucleo.py:518-537. Both run on CUDA only and raise elsewhere."""
+import math
+
 import torch
 
 from . import _lib
@@ -137,3 +139,110 @@ def escaneo(a, b):
     if torch.is_grad_enabled() and (a.requires_grad or b.requires_grad):
         return _Scan.apply(a, b)
     return _scan(a, b)
+
+
+_FORBIDDEN = -1e9          # score of "not allowed" (asrn/nucleo.py:86)
+
+
+def layer_forward_train(layer, E, h, piezas=None):
+    """Differentiable forward of an ASRNLayer (the reference's asrn/estable.py:407-421 with its default protections),
+    used by ASRNLayer.forward when a gradient is wanted. The index work runs on this library's kernels without a
+    gradient (bucket ids and their stable sort, asrn_bucket_sort; the n-gram keys, their order and repeats,
+    asrn_repetition), the bucket attention and the two scans on the training kernels above (forward and backward),
+    and the dense projections, LayerNorm and gate as PyTorch ops, as in the reference:
+      context   LN(h); Qc, Kc = LN(h) W in the autocast type; the clock projection in fp32; beta = min(softplus, beta_max)
+                in fp64, log_alfa = max(logsigmoid + ln 2, log_alfa_min); Bt = cumsum(beta)     (asrn/estable.py:153-194)
+      hash      phi = [word MLP(E), context MLP([E, E_prev])], V = v(E) of the next position     (asrn/nucleo.py:644-659)
+      attention BucketAttention over the per-table bucket order, then the table signals          (asrn/estable.py:282-300)
+      memory    Hawkes intensities and the streak from the n-gram order (two scans)              (asrn/estable.py:304-321)
+      gate      h + sigmoid(logit) o(salida / tables with candidates)                            (asrn/estable.py:376-403)"""
+    import torch.nn.functional as F
+    from . import stages
+    _need_cuda(E, h)
+    p = layer.protecciones
+    B, L, d = E.shape
+    T, nb, C, cf, K, n = layer.n_tablas, layer.n_bits, layer.chunk, layer.confirmar, layer.sufijo, layer.vistos
+    dev = E.device
+    auto = torch.is_autocast_enabled('cuda')
+    act = torch.get_autocast_dtype('cuda') if auto else torch.float32
+    if auto and act != torch.bfloat16:
+        raise NotImplementedError('the training path supports fp32 and bf16 autocast')
+    with torch.autocast('cuda', enabled=False):
+        sig = piezas.to(torch.float32) if piezas is not None else E.float() @ layer.r_firma.float()
+    # context
+    hh32 = layer.ln_ctx(h)
+    hh = hh32.to(act)
+    y = F.linear(hh, torch.cat([layer.cq.weight, layer.ck.weight]))
+    with torch.autocast('cuda', enabled=False):
+        u = F.linear(hh32.float(), layer.w_reloj.float(), layer.b_reloj.float())
+    beta = F.softplus(u[..., 0])
+    log_alfa = F.logsigmoid(u[..., 1]) + math.log(2)
+    if p.beta_max is not None:
+        beta = beta.clamp(max=p.beta_max)
+    if p.log_alfa_min is not None:
+        log_alfa = log_alfa.clamp(min=p.log_alfa_min)
+    beta = beta.double()
+    Qc, Kc = y[..., :cf], y[..., cf:2 * cf]
+    Bt = beta.cumsum(1)
+    # hash and values
+    E16 = E.to(act)
+    pal = layer.afin_palabra
+    yv = F.linear(E16, torch.cat([pal[0].weight, layer.v.weight]), F.pad(pal[0].bias, (0, d)))
+    hp, vv = yv.split([pal[0].out_features, d], dim=-1)
+    llave = torch.cat([E16, F.pad(E16, (0, 0, 1, 0))[:, :L]], dim=-1)
+    phi = torch.cat([pal[2](pal[1](hp)), layer.afin_contexto(llave)], dim=-1)
+    V = F.pad(vv, (0, 0, 0, 1))[:, 1:]
+    phi, V, Qc, Kc = (t.to(act).contiguous() for t in (phi, V, Qc, Kc))
+    with torch.no_grad():
+        bits = (phi.detach().float().view(B, L, T, nb) > 0).to(torch.int32)
+        ids = (bits * layer.pot.to(torch.int32)).sum(-1, dtype=torch.int32)                 # (B, L, T)
+        ids_rows = ids.transpose(1, 2).reshape(B * T, L).to(torch.int16)
+        orden, ids_o = stages.bucket_sort(ids_rows, nb)
+        ids_o = ids_o.to(torch.int32) & 0xFFFF
+        pad = torch.full((B, K), float('nan'), device=dev)
+        prev = torch.cat([pad, sig.detach()], 1)
+        Pf = torch.stack([prev[:, K - 1 - k:K - 1 - k + L] for k in range(K)], -1)         # t-1, ..., t-K
+    salida, senal = BucketAttention.apply(phi, V, Qc, Kc, Bt, log_alfa, layer.w_sufijo, layer.gamma, Pf, orden,
+                                          ids_o, T, C, 1.0 / layer.temperatura, cf ** -0.5)
+    sen = senal.view(B, T, L, 3)
+    hay_t, mx_t, pico_t = sen[..., 0:1], sen[..., 1:2], sen[..., 2:3]
+    mejor = torch.where(hay_t > 0, mx_t, torch.full_like(mx_t, _FORBIDDEN)).amax(1).clamp(min=_FORBIDDEN)
+    pt = hay_t.sum(1)
+    pico = (pico_t * hay_t).sum(1)
+    peso_ctx = hay_t[:, T - layer.tablas_contexto:].sum(1)
+    # n-gram memory: Hawkes intensity per order and the streak
+    with torch.no_grad():
+        rep = stages.repetition(layer, sig.detach(), beta.detach(), Bt.detach(), log_alfa.detach(), debug=True)
+        orden_ng = rep['orden_ng'].long()                                                  # (B, n, L)
+        repetido = rep['repetido'].float()
+        vistos = rep['vistos'].float()                                                    # (B, L, n)
+    kappa, kappa_r = layer.log_kappa.exp(), layer.log_kappa_racha.exp()
+    if p.kappa_min is not None:
+        kappa, kappa_r = kappa.clamp(min=p.kappa_min), kappa_r.clamp(min=p.kappa_min)
+    B_o = torch.gather(Bt.unsqueeze(1).expand(-1, n, -1), -1, orden_ng)
+    alfa_o = torch.gather(log_alfa.exp().unsqueeze(1).expand(-1, n, -1), -1, orden_ng)
+    dB = F.pad((B_o[..., 1:] - B_o[..., :-1]).clamp(min=0), (1, 0)).float()
+    a = repetido * torch.exp(-kappa.float().unsqueeze(-1) * dB)
+    lam = escaneo(a, a * F.pad(alfa_o[..., :-1].float(), (1, 0)))
+    hawkes = torch.zeros_like(lam).scatter(-1, orden_ng, lam).transpose(1, 2)
+    r = vistos[..., -1]
+    racha = escaneo((r * torch.exp(-kappa_r.float() * beta.float())).contiguous(), r.contiguous())
+    # gate
+    pt_d = pt.detach()
+    sal = salida / pt.clamp(min=1)
+    mejor = torch.where(pt_d > 0, mejor, torch.zeros_like(pt_d))
+    if p.mejor_max is not None:
+        mejor = mejor.clamp(-p.mejor_max, p.mejor_max)
+    senales = torch.cat([pt_d / T, mejor, pico / pt_d.clamp(min=1), peso_ctx.detach() / layer.tablas_contexto], -1)
+    with torch.autocast('cuda', enabled=False):
+        logit = F.linear(h, layer.g.weight.to(h.dtype), layer.g.bias.to(h.dtype))
+    logit = logit + layer.g_conf(senales).to(logit.dtype)
+    logit = logit + (vistos.to(logit.dtype) * layer.w_vistos.to(logit.dtype)).sum(-1, keepdim=True)
+    logit = logit + (torch.log1p(hawkes).to(logit.dtype) * layer.u_hawkes.to(logit.dtype)).sum(-1, keepdim=True)
+    x = (torch.log1p(racha) / layer.racha_paso).clamp(max=layer.d_racha.shape[0] - 1)
+    i = torch.nan_to_num(x.detach(), nan=0.0).floor().long().clamp(0, layer.d_racha.shape[0] - 2)
+    logit = logit + (layer.u_racha[i] + (x - i) * layer.d_racha[1:][i]).unsqueeze(-1).to(logit.dtype)
+    if p.tope_puerta is not None:
+        logit = p.tope_puerta * torch.tanh(logit / p.tope_puerta)
+    aporte = layer.o(sal.to(act))
+    return h + torch.sigmoid(logit).to(aporte.dtype) * layer.drop(aporte)

@@ -17,7 +17,7 @@ overflow (chunk 4, 2 bits) and records, after the prompt and after every step, e
 (_anillo_desde / _anillo_meter, asrn/nucleo.py:1585-1618), the candidate positions of the step (_candidatos,
 asrn/nucleo.py:1621-1631) and the Hawkes state of every n-gram key (_MemoriaHawkes, asrn/nucleo.py:1634-1714).
 The gradient fixtures run the reference's own autograd through _acumular and escaneo (asrn/estable.py:204-263,
-asrn/nucleo.py:188-197, 518-537).
+asrn/nucleo.py:188-197, 518-537), and through the whole layer forward (asrn/estable.py:407-421).
 The fixtures are read by the tests on any machine; this script is the only place that imports the reference.
 """
 import json
@@ -332,6 +332,37 @@ def grad_case(name, d, B, L, V, opts, seed=0):
     print(f'{name}: {os.path.getsize(path) / 1024:.0f} KB')
 
 
+def layer_grad_case(name, d, B, L, V, opts, seed=0):
+    """The whole layer's gradients from the reference's autograd on the CPU (asrn/estable.py:407-421, fp32): E and h
+    as leaves, loss = sum(forward(E, h, tokens) * G); the output, the gradients of E and h and of every parameter."""
+    import asrn
+    torch.manual_seed(seed)
+    capa = asrn.ASRNLayer(d, **opts)
+    _move(capa, seed=seed + 1)
+    with torch.no_grad():                     # the streak response and the Hawkes weights off zero too
+        g0 = torch.Generator().manual_seed(seed + 5)
+        capa.d_racha.add_(torch.randn(capa.d_racha.shape, generator=g0) * 0.3)
+        capa.u_hawkes.add_(torch.randn(capa.u_hawkes.shape, generator=g0) * 0.5)
+    capa.train()
+    x = synthetic.zipf_tokens(B, L, V, 1.1, seed)
+    x = torch.from_numpy(synthetic.plant_repeats(x, 0.25, 4, max(4, L // 4), seed=seed + 1))
+    g = torch.Generator().manual_seed(seed + 7)
+    E = torch.randn(V, d, generator=g)[x].requires_grad_()
+    h = torch.randn(B, L, d, generator=g).requires_grad_()
+    y = capa(E, h, x)
+    G = torch.randn(B, L, d, generator=g)
+    (y * G).sum().backward()
+    out = dict(tokens=x.numpy(), E=_np(E), h=_np(h), G=_np(G), y=_np(y), grad_E=_np(E.grad), grad_h=_np(h.grad))
+    for k, t in capa.state_dict().items():
+        out['param.' + k] = _np(t)
+    for k, t in capa.named_parameters():
+        out['grad.' + k] = _np(t.grad) if t.grad is not None else np.zeros(tuple(t.shape), np.float32)
+    out['meta'] = np.frombuffer(json.dumps(dict(d=d, B=B, L=L, opts=opts)).encode(), dtype=np.uint8)
+    path = os.path.join(HERE, name + '.npz')
+    np.savez_compressed(path, **out)
+    print(f'{name}: {os.path.getsize(path) / 1024:.0f} KB')
+
+
 def main(ref):
     sys.path.insert(0, ref)
     torch.set_num_threads(8)
@@ -350,6 +381,8 @@ def main(ref):
     gen_sampled_case('gen_sampled')
     grad_case('grad_crowded', 64, 2, 300, 40, dict(chunk=16, n_bits=4))
     grad_case('grad_default', 64, 2, 256, 64, {}, seed=3)
+    layer_grad_case('layer_grad_crowded', 64, 2, 200, 40, dict(chunk=16, n_bits=4))
+    layer_grad_case('layer_grad_default', 64, 2, 160, 64, {}, seed=2)
 
 
 if __name__ == '__main__':
@@ -363,6 +396,8 @@ if __name__ == '__main__':
              'checkpoint': lambda: checkpoint_case('ckpt_ref'),
              'gen_sampled': lambda: gen_sampled_case('gen_sampled'),
              'grad': lambda: (grad_case('grad_crowded', 64, 2, 300, 40, dict(chunk=16, n_bits=4)),
-                              grad_case('grad_default', 64, 2, 256, 64, {}, seed=3))}[case]()
+                              grad_case('grad_default', 64, 2, 256, 64, {}, seed=3)),
+             'layer_grad': lambda: (layer_grad_case('layer_grad_crowded', 64, 2, 200, 40, dict(chunk=16, n_bits=4)),
+                                    layer_grad_case('layer_grad_default', 64, 2, 160, 64, {}, seed=2))}[case]()
     else:
         main(sys.argv[1])
