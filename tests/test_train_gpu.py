@@ -79,3 +79,25 @@ def test_a_training_step_lowers_the_loss(cuda):
         opt.step()
         losses.append(float(loss.detach()))
     assert losses[-1] < losses[0]
+
+
+def test_model_trains_end_to_end(cuda):
+    """create_model's whole forward is differentiable (local blocks as torch modules, ASRN layers on the training
+    path): three Adam steps of next-token cross-entropy on a fixed batch lower the loss, and every ASRN layer's
+    parameters get a gradient."""
+    import asrn_b200
+    m = asrn_b200.create_model(V=64, d=64, n_capas=4, semilla=1).to(cuda).train()
+    x = torch.from_numpy(np.random.default_rng(0).integers(0, 64, (2, 96))).to(cuda)
+    opt = torch.optim.Adam(m.parameters(), lr=3e-3)
+    losses = []
+    for _ in range(3):
+        opt.zero_grad()
+        lg = m(x[:, :-1])
+        loss = torch.nn.functional.cross_entropy(lg.float().reshape(-1, 64), x[:, 1:].reshape(-1))
+        loss.backward()
+        for layer in m.largos:
+            assert layer.v.weight.grad is not None and torch.isfinite(layer.v.weight.grad).all()
+            assert layer.gamma.grad is not None
+        opt.step()
+        losses.append(float(loss.detach()))
+    assert losses[-1] < losses[0]
