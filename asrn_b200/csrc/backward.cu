@@ -14,8 +14,10 @@
 // the clock and log_alfa. No atomics: every query slot is written once per table (its block), every key slot twice
 // -- as a current-block key (place 1) and as a previous-block key of the next block (place 0; the last block writes
 // zeros there) -- and the gamma / w_suf sums go to one row of partials per CTA; the caller adds them up in a fixed
-// order. Scores and sums in fp32 on CUDA cores; under bf16 the operands are bf16 and rounded where the reference's
-// kernel rounds (att and dS to the operand type before their products).
+// order. Scores and sums in fp32; under bf16 the operands are bf16 and rounded where the reference's kernel rounds
+// (att and dS to the operand type before their products), and the value-width products (att . V forward; dO . V^T
+// and att^T . dO backward: 64-column chunks of the values, 32 queries x 64 keys) run on mma.sync tiles from bf16
+// shared-memory tiles, fp32 accumulation. In fp32 every product stays on CUDA cores (exact fp32 sums).
 //
 // Scan. S_i = a_i S_{i-1} + b_i along each row (S_{-1} = 0); its backward is the same recurrence right to left:
 // l_i = g_i + a_{i+1} l_{i+1}, dL/db_i = l_i, dL/da_i = l_i S_{i-1}. One CTA per row: each thread composes the affine
@@ -31,6 +33,7 @@ namespace {
 constexpr int kBaThreads = 256;
 constexpr int kBaMaxC = 32;
 constexpr int kBaBd = 64;             // value columns per staged chunk
+constexpr int kBaLdb = 72;            // bf16 row stride of the tensor-core tiles (64 + 8: ldmatrix rows on distinct banks)
 
 template <bool Half>
 struct BaT {
@@ -54,6 +57,25 @@ __device__ __forceinline__ void ba_st(typename BaT<Half>::T* p, int64_t i, float
 template <bool Half>
 __device__ __forceinline__ float ba_round(float v) {
   return Half ? round_bf16(v) : v;
+}
+
+__device__ __forceinline__ void ba_ldsm_x4(const void* p, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"((uint32_t)__cvta_generic_to_shared(p)));
+}
+__device__ __forceinline__ void ba_ldsm_x4_t(const void* p, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"((uint32_t)__cvta_generic_to_shared(p)));
+}
+__device__ __forceinline__ void ba_mma(float* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                       uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
 struct BaArgs {
@@ -111,6 +133,10 @@ struct BaSmem {
   float* vs;       // 2C x (kBaBd + 1)
   float* os;       // C x (kBaBd + 1)
   float* red;      // 32
+  // bf16 tiles of the tensor-core products (bf16 operands), padded to 32 queries x 64 keys
+  __nv_bfloat16* attb;   // 32 x kBaLdb: att rounded to bf16 (zero outside C x 2C)
+  __nv_bfloat16* vb;     // 64 x kBaLdb: value rows of the chunk
+  __nv_bfloat16* ob;     // 32 x kBaLdb: output-gradient rows of the chunk
 };
 
 __host__ __device__ inline size_t ba_smem_bytes(int C, int P, int CF, int K) {
@@ -126,6 +152,7 @@ __host__ __device__ inline size_t ba_smem_bytes(int C, int P, int CF, int K) {
   n = (n + 15) / 16 * 16;
   n += (C2 + C) * (kBaBd + 1) * 4;
   n += 32 * 4;
+  n += 16 + (size_t)(32 + 64 + 32) * kBaLdb * 2;
   return n + 64;
 }
 
@@ -160,6 +187,10 @@ __device__ inline BaSmem ba_carve(unsigned char* base, int C, int P, int CF, int
   s.vs = reinterpret_cast<float*>(take((size_t)C2 * (kBaBd + 1) * 4));
   s.os = reinterpret_cast<float*>(take((size_t)C * (kBaBd + 1) * 4));
   s.red = reinterpret_cast<float*>(take(32 * 4));
+  p = base + ((p - base + 15) / 16 * 16);
+  s.attb = reinterpret_cast<__nv_bfloat16*>(take((size_t)32 * kBaLdb * 2));
+  s.vb = reinterpret_cast<__nv_bfloat16*>(take((size_t)64 * kBaLdb * 2));
+  s.ob = reinterpret_cast<__nv_bfloat16*>(take((size_t)32 * kBaLdb * 2));
   return s;
 }
 
@@ -284,6 +315,36 @@ __device__ void ba_scores(const BaArgs& a, const BaSmem& s, int64_t r, int j, fl
   __syncthreads();
 }
 
+// att (C x 2C fp32) -> attb (32 x 64 bf16, zero outside C x 2C)
+__device__ __forceinline__ void ba_fill_attb(const BaSmem& s, int C) {
+  const int C2 = 2 * C;
+  for (int e = threadIdx.x; e < 32 * 64; e += kBaThreads) {
+    const int q = e >> 6, k = e & 63;
+    s.attb[q * kBaLdb + k] = __float2bfloat16_rn(q < C && k < C2 ? s.att[q * (C2 + 1) + k] : 0.f);
+  }
+}
+
+// Rows of a bf16 (., D) tensor into a 64-column bf16 tile: tile[i][c] = src[row(i) * D + d0 + c] for c < bd and a
+// valid row, else 0; n rows.
+__device__ __forceinline__ void ba_fill_tile(__nv_bfloat16* tile, const __nv_bfloat16* src, const int64_t* rows,
+                                             const int* pos, int n_valid, int n, int D, int d0, int bd) {
+  const bool vec = (D % 8) == 0 && bd == kBaBd;
+  if (vec) {                                         // 16-byte loads: 8 columns per thread
+    for (int e = threadIdx.x; e < n * 8; e += kBaThreads) {
+      const int i = e >> 3, c = (e & 7) * 8;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (i < n_valid && pos[i] >= 0) v = *reinterpret_cast<const uint4*>(src + rows[i] * D + d0 + c);
+      *reinterpret_cast<uint4*>(tile + i * kBaLdb + c) = v;
+    }
+  } else {
+    for (int e = threadIdx.x; e < n * 64; e += kBaThreads) {
+      const int i = e >> 6, c = e & 63;
+      tile[i * kBaLdb + c] = (i < n_valid && pos[i] >= 0 && c < bd) ? src[rows[i] * D + d0 + c]
+                                                                   : __float2bfloat16_rn(0.f);
+    }
+  }
+}
+
 template <bool Half>
 __global__ void __launch_bounds__(kBaThreads) k_bucket_attn_fwd(const BaArgs a) {
   using T = typename BaT<Half>::T;
@@ -294,6 +355,42 @@ __global__ void __launch_bounds__(kBaThreads) k_bucket_attn_fwd(const BaArgs a) 
   ba_scores<Half>(a, s, r, j, a.sen);
   const T* V = reinterpret_cast<const T*>(a.v);
   T* out = reinterpret_cast<T*>(a.out);
+  if constexpr (Half) {
+    // out (32 x 64 per chunk) = attb (32 x 64 keys) . vb (64 keys x 64 columns) on mma.sync; warp: rows 16 (w % 2),
+    // columns 16 (w / 2)
+    const int lane = tid & 31, wid = tid >> 5, mt = wid & 1, nt = wid >> 1;
+    ba_fill_attb(s, C);
+    for (int d0 = 0; d0 < D; d0 += kBaBd) {
+      const int bd = min(kBaBd, D - d0);
+      ba_fill_tile(s.vb, V, s.filk, s.kpos, C2, 64, D, d0, bd);
+      __syncthreads();
+      float acc[2][4] = {};
+#pragma unroll
+      for (int kk = 0; kk < 64; kk += 16) {
+        uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
+        ba_ldsm_x4(s.attb + (16 * mt + (lane & 15)) * kBaLdb + kk + (lane >> 4) * 8, a0, a1, a2, a3);
+        const int i = lane >> 3;                     // matrix i: k half i % 2, n block i / 2
+        ba_ldsm_x4_t(s.vb + (kk + (i & 1) * 8 + (lane & 7)) * kBaLdb + 16 * nt + (i >> 1) * 8, b0, b1, b2, b3);
+        ba_mma(acc[0], a0, a1, a2, a3, b0, b1);
+        ba_mma(acc[1], a0, a1, a2, a3, b2, b3);
+      }
+      const int g = lane >> 2, t4 = lane & 3;
+#pragma unroll
+      for (int jn = 0; jn < 2; ++jn) {
+        const int c = 16 * nt + 8 * jn + 2 * t4;
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const int q = 16 * mt + g + 8 * hh;
+          if (q >= C || s.qpos[q] < 0 || c >= bd) continue;
+          const int64_t o = (r * a.L + s.qpos[q]) * D + d0 + c;
+          out[o] = __float2bfloat16_rn(acc[jn][2 * hh]);
+          if (c + 1 < bd) out[o + 1] = __float2bfloat16_rn(acc[jn][2 * hh + 1]);
+        }
+      }
+      __syncthreads();
+    }
+    return;
+  }
   for (int d0 = 0; d0 < D; d0 += kBaBd) {
     const int bd = min(kBaBd, D - d0);
     for (int e = tid; e < C2 * kBaBd; e += kBaThreads) {
@@ -333,6 +430,74 @@ __global__ void __launch_bounds__(kBaThreads) k_bucket_attn_bwd(const BaArgs a) 
   float dp[8];
 #pragma unroll
   for (int u = 0; u < 8; ++u) dp[u] = 0.f;
+  if constexpr (Half) {
+    // dP (32 x 64) += ob (32 x chunk) . vb^T and dV chunk (64 keys x 64) = attb^T . ob on mma.sync
+    const int g = lane >> 2, t4 = lane & 3, i4 = lane >> 3;
+    const int mt = wid & 1, nt = wid >> 1;        // dP tile of this warp: queries 16 mt .., keys 16 nt ..
+    const int mk = wid & 3, nh = wid >> 2;        // dV tile: keys 16 mk .., columns 32 nh ..
+    float pacc[2][4] = {};
+    ba_fill_attb(s, C);
+    for (int d0 = 0; d0 < D; d0 += kBaBd) {
+      const int bd = min(kBaBd, D - d0);
+      ba_fill_tile(s.vb, V, s.filk, s.kpos, C2, 64, D, d0, bd);
+      ba_fill_tile(s.ob, dO, s.filq, s.qpos, C, 32, D, d0, bd);
+      __syncthreads();
+#pragma unroll
+      for (int kk = 0; kk < 64; kk += 16) {       // K = the chunk's columns
+        uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
+        ba_ldsm_x4(s.ob + (16 * mt + (lane & 15)) * kBaLdb + kk + (lane >> 4) * 8, a0, a1, a2, a3);
+        ba_ldsm_x4(s.vb + (16 * nt + (i4 >> 1) * 8 + (lane & 7)) * kBaLdb + kk + (i4 & 1) * 8, b0, b1, b2, b3);
+        ba_mma(pacc[0], a0, a1, a2, a3, b0, b1);
+        ba_mma(pacc[1], a0, a1, a2, a3, b2, b3);
+      }
+      float vacc[4][4] = {};
+#pragma unroll
+      for (int kq = 0; kq < 32; kq += 16) {       // K = the queries
+        uint32_t a0, a1, a2, a3;
+        // A = att^T (keys x queries) from attb (queries x keys): matrix i = (key half i % 2, query half i / 2)
+        ba_ldsm_x4_t(s.attb + (kq + (i4 >> 1) * 8 + (lane & 7)) * kBaLdb + 16 * mk + (i4 & 1) * 8, a0, a1, a2, a3);
+#pragma unroll
+        for (int nb = 0; nb < 2; ++nb) {
+          uint32_t b0, b1, b2, b3;
+          ba_ldsm_x4_t(s.ob + (kq + (i4 & 1) * 8 + (lane & 7)) * kBaLdb + 32 * nh + 16 * nb + (i4 >> 1) * 8, b0, b1,
+                       b2, b3);
+          ba_mma(vacc[2 * nb], a0, a1, a2, a3, b0, b1);
+          ba_mma(vacc[2 * nb + 1], a0, a1, a2, a3, b2, b3);
+        }
+      }
+#pragma unroll
+      for (int jn = 0; jn < 4; ++jn) {
+        const int c = 32 * nh + 8 * jn + 2 * t4;
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const int k = 16 * mk + g + 8 * hh;
+          if (k >= C2 || s.kpos[k] < 0 || c >= bd) continue;
+          const int64_t lk = lugar_k(k) * D + d0 + c, zk = (r * L + s.kpos[k]) * D + d0 + c;
+          const bool zero = last_block && k >= C;
+          gv[lk] = __float2bfloat16_rn(vacc[jn][2 * hh]);
+          if (zero) gv[zk] = __float2bfloat16_rn(0.f);
+          if (c + 1 < bd) {
+            gv[lk + 1] = __float2bfloat16_rn(vacc[jn][2 * hh + 1]);
+            if (zero) gv[zk + 1] = __float2bfloat16_rn(0.f);
+          }
+        }
+      }
+      __syncthreads();
+    }
+#pragma unroll
+    for (int jn = 0; jn < 2; ++jn) {
+      const int k = 16 * nt + 8 * jn + 2 * t4;
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int q = 16 * mt + g + 8 * hh;
+        if (q < C) {
+          if (k < C2) s.ds[q * (C2 + 1) + k] = pacc[jn][2 * hh];
+          if (k + 1 < C2) s.ds[q * (C2 + 1) + k + 1] = pacc[jn][2 * hh + 1];
+        }
+      }
+    }
+    __syncthreads();
+  } else {
   for (int d0 = 0; d0 < D; d0 += kBaBd) {
     const int bd = min(kBaBd, D - d0);
     for (int e = tid; e < C2 * kBaBd; e += kBaThreads) {
@@ -374,6 +539,7 @@ __global__ void __launch_bounds__(kBaThreads) k_bucket_attn_bwd(const BaArgs a) 
     }
   }
   __syncthreads();
+  }
   // dS = att (dP - sum_k att dP), one warp per query row
   for (int q = wid; q < C; q += kBaThreads / 32) {
     const float* at = s.att + q * (C2 + 1);

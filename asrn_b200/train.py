@@ -144,6 +144,24 @@ def escaneo(a, b):
 _FORBIDDEN = -1e9          # score of "not allowed" (asrn/nucleo.py:86)
 
 
+class _Take(torch.autograd.Function):
+    """w[i] for a short w (the streak response's nodes) read at every position: the backward adds each entry's
+    positions by a one-hot reduction (deterministic; PyTorch's indexing backward sorts millions of indices into a
+    few entries). The reference does the same with a reduction per entry (asrn/nucleo.py:136-158)."""
+
+    @staticmethod
+    def forward(ctx, w, i):
+        ctx.save_for_backward(i)
+        ctx.n = w.shape[0]
+        return w[i]
+
+    @staticmethod
+    def backward(ctx, g):
+        (i,) = ctx.saved_tensors
+        one_hot = torch.nn.functional.one_hot(i.reshape(-1), ctx.n).to(torch.float32)
+        return (one_hot * g.reshape(-1, 1).float()).sum(0).to(g.dtype), None
+
+
 def layer_forward_train(layer, E, h, piezas=None):
     """Differentiable forward of an ASRNLayer (the reference's asrn/estable.py:407-421 with its default protections),
     used by ASRNLayer.forward when a gradient is wanted. The index work runs on this library's kernels without a
@@ -241,7 +259,8 @@ def layer_forward_train(layer, E, h, piezas=None):
     logit = logit + (torch.log1p(hawkes).to(logit.dtype) * layer.u_hawkes.to(logit.dtype)).sum(-1, keepdim=True)
     x = (torch.log1p(racha) / layer.racha_paso).clamp(max=layer.d_racha.shape[0] - 1)
     i = torch.nan_to_num(x.detach(), nan=0.0).floor().long().clamp(0, layer.d_racha.shape[0] - 2)
-    logit = logit + (layer.u_racha[i] + (x - i) * layer.d_racha[1:][i]).unsqueeze(-1).to(logit.dtype)
+    resp = _Take.apply(layer.u_racha, i) + (x - i) * _Take.apply(layer.d_racha[1:], i)
+    logit = logit + resp.unsqueeze(-1).to(logit.dtype)
     if p.tope_puerta is not None:
         logit = p.tope_puerta * torch.tanh(logit / p.tope_puerta)
     aporte = layer.o(sal.to(act))
