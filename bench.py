@@ -31,6 +31,9 @@ Legs in the same line (each with its own value, device timing and the reference'
              (NCCL exchanges of halo, clock offsets, bucket tails, features, n-gram summaries and streak maps).
   cfg2       ASRNLayer(256) forward in fp32, 16 x 4096 tokens (batch-sharded).
   cfg1       create_model(V=256, d=64, n_capas=4) forward on 8 x 256 bytes, then generate(top_k=1) of 200 tokens.
+  model      the configuration-3 model forward (shared n-gram sort, fused local blocks) on 4 x 8192 tokens.
+  train      ASRNLayer(768) forward + backward in training mode, bf16 autocast, 4 x 8192 tokens (rank 0), beside the
+             reference's forward + backward on the host cores.
 --impl reference: times the reference's CPU implementation of the headline workload (asrn.ASRNLayer from
 baseline/_ref, torch on the host cores, bf16 autocast, chunks of 4 sequences per step) and its O(1) writer.
 """
@@ -66,6 +69,7 @@ CFG4_BYTES_PER_TOKEN = 24968     # algorithmic HBM bytes per token of one layer 
 D2, B2, L2 = 256, 16, 4096
 CFG2_BYTES_PER_TOKEN = 25256     # d=256, fp32
 REF_CHUNK = 4                    # sequences per step of the reference's CPU timing (its V_o buffer is ~6.5 GB per 4)
+TRAIN_B = 4                      # sequences of the training leg (cfg3 shapes: ASRNLayer(768), 8192 tokens, bf16)
 
 
 def parse():
@@ -77,9 +81,9 @@ def parse():
     p.add_argument('--batch', type=int, default=B_PER_GPU, help='sequences per GPU')
     p.add_argument('--seq', type=int, default=L_SEQ)
     p.add_argument('--no-cpu-baseline', action='store_true')
-    p.add_argument('--workload', default='cfg3', choices=['cfg3', 'cfg4', 'gen', 'model', 'localblock'],
-                   help='cfg3: the batch-sharded layer metric (default); cfg4 / gen / model / localblock: only that '
-                        'leg (for profiling)')
+    p.add_argument('--workload', default='cfg3', choices=['cfg3', 'cfg4', 'gen', 'model', 'localblock', 'train'],
+                   help='cfg3: the batch-sharded layer metric (default); cfg4 / gen / model / localblock / train: '
+                        'only that leg (for profiling)')
     p.add_argument('--no-gen', action='store_true', help='skip the generation leg')
     p.add_argument('--no-legs', action='store_true', help='skip the cfg1 / cfg2 / cfg4 legs')
     p.add_argument('--eager', action='store_true', help='time the eager forward instead of its CUDA-graph replay')
@@ -666,6 +670,8 @@ def run_ours(args):
         legs['model'] = leg_model(args, dev, rank, world)
     if args.workload == 'localblock':
         legs['localblock'] = leg_localblock(args, dev, rank, world)
+    if args.workload == 'train':
+        legs['train'] = leg_train(args, dev, rank, world)
     if args.workload == 'cfg3':
         if not args.no_gen:
             legs['generation'] = leg_generation(args, dev, rank, world)
@@ -673,10 +679,11 @@ def run_ours(args):
             legs['cfg2'] = leg_cfg2(args, dev, rank, world)
             legs['cfg1'] = leg_cfg1(args, dev, rank, world)
             legs['model'] = leg_model(args, dev, rank, world)
+            legs['train'] = leg_train(args, dev, rank, world)
     if rank == 0:
         if out is None:                       # --workload cfg4 / gen: that leg is the line
             out = dict(legs.pop({'cfg4': 'cfg4', 'gen': 'generation', 'model': 'model',
-                                 'localblock': 'localblock'}[args.workload]))
+                                 'localblock': 'localblock', 'train': 'train'}[args.workload]))
         out.update({k: v for k, v in legs.items() if v is not None})
         print(json.dumps(out), flush=True)
     if world > 1:
@@ -820,6 +827,81 @@ def leg_cfg2(args, dev, rank, world):
            'roofline': {'bound': 'hbm', 'kernel': 'whole layer forward (per GPU)', 'achieved': achieved, 'peak': hbm,
                         'peak_source': src, 'unit': 'GB/s', 'frac': achieved / hbm,
                         'algorithmic_bytes_per_token': CFG2_BYTES_PER_TOKEN}}
+    if cpu is not None:
+        leg['cpu_baseline'] = cpu
+    return leg
+
+
+def ref_train_baseline(state, x, E, h, G, steps=2, warmup=1):
+    """The reference's ASRNLayer forward + backward of sum(h' * G) on the host cores (torch CPU, bf16 autocast), one
+    sequence per step: tokens/s."""
+    import torch
+    asrn = import_reference()
+    torch.set_num_threads(host_cores())
+    layer = asrn.ASRNLayer(E.shape[-1])
+    layer.load_state_dict(state)
+    layer.train()
+    xs, Gs = torch.from_numpy(x), torch.from_numpy(G)
+    secs = []
+    for i in range(warmup + steps):
+        Es = torch.from_numpy(E).requires_grad_()
+        hs = torch.from_numpy(h).requires_grad_()
+        t0 = time.perf_counter()
+        with torch.autocast('cpu', dtype=torch.bfloat16):
+            y = layer(Es, hs, xs)
+        (y.float() * Gs).sum().backward()
+        if i >= warmup:
+            secs.append(time.perf_counter() - t0)
+        layer.zero_grad(set_to_none=True)
+    tok = x.shape[0] * x.shape[1]
+    return {'value': tok * len(secs) / sum(secs), 'unit': 'tokens/s', 'cores': torch.get_num_threads(),
+            'kind': 'reference', 'ms_per_step': 1e3 * statistics.median(secs),
+            'sample': 'asrn.ASRNLayer of the reference (baseline/_ref), forward + backward on the host cores, torch '
+                      'CPU, bf16 autocast, %d step(s) of %d x %d tokens after %d warm-up' % (len(secs), x.shape[0],
+                                                                                            x.shape[1], warmup)}
+
+
+def leg_train(args, dev, rank, world):
+    """Training step of the layer on one GPU (rank 0; the other ranks skip it): ASRNLayer(768) in training mode, bf16
+    autocast, forward + backward of sum(h' * G) on TRAIN_B x 8192 tokens (cfg3 shapes): the differentiable path with
+    the bucket attention and the scans on the training kernels. Eager (the backward is autograd's)."""
+    import numpy as np
+    import torch
+    if rank != 0:
+        return None
+    layer = make_layer_params(d=D).to(dev).train()
+    x, E, h, _ = make_inputs(TRAIN_B, L_SEQ, 0)
+    G = np.random.default_rng(5).standard_normal(E.shape).astype(np.float32)
+    xd, Ed, hd, Gd = (torch.from_numpy(a).to(dev) for a in (x, E, h, G))
+    Ed.requires_grad_()
+    hd.requires_grad_()
+
+    def step():
+        with torch.autocast('cuda', dtype=torch.bfloat16):
+            y = layer(Ed, hd, xd)
+        (y.float() * Gd).sum().backward()
+        layer.zero_grad(set_to_none=True)
+        Ed.grad = None
+        hd.grad = None
+
+    warm_up(step, args.warmup, 1)
+    n = max(3, args.steps // 4)
+    ms, step_ms = timed(step, n)
+    cpu = None
+    if not args.no_cpu_baseline:
+        try:
+            state = {k: v.detach().cpu() for k, v in layer.state_dict().items()}
+            seg = 2048
+            cpu = ref_train_baseline(state, x[:1, :seg], E[:1, :seg], h[:1, :seg], G[:1, :seg])
+        except Exception as exc:
+            cpu = {'unavailable': '%s: %s' % (type(exc).__name__, exc)}
+    del layer, xd, Ed, hd, Gd
+    torch.cuda.empty_cache()
+    step_s = ms / n * 1e-3
+    leg = {'metric': 'asrn_layer_train_tokens_per_s', 'value': TRAIN_B * L_SEQ / step_s, 'unit': 'tokens/s',
+           'ms_per_step': ms / n, 'step_ms': spread(step_ms), 'dtype': 'bf16', 'launch': 'eager',
+           'config': {'workload': 'ASRNLayer(768) forward + backward of sum(h\' * G), training mode, bf16 autocast, '
+                                  '%d x %d tokens (cfg3 shapes)' % (TRAIN_B, L_SEQ)}}
     if cpu is not None:
         leg['cpu_baseline'] = cpu
     return leg
