@@ -15,9 +15,10 @@
 // -- as a current-block key (place 1) and as a previous-block key of the next block (place 0; the last block writes
 // zeros there) -- and the gamma / w_suf sums go to one row of partials per CTA; the caller adds them up in a fixed
 // order. Scores and sums in fp32; under bf16 the operands are bf16 and rounded where the reference's kernel rounds
-// (att and dS to the operand type before their products), and the value-width products (att . V forward; dO . V^T
-// and att^T . dO backward: 64-column chunks of the values, 32 queries x 64 keys) run on mma.sync tiles from bf16
-// shared-memory tiles, fp32 accumulation. In fp32 every product stays on CUDA cores (exact fp32 sums).
+// (att and dS to the operand type before their products), and every product runs on mma.sync tiles from bf16
+// shared-memory tiles with fp32 accumulation: the scores [phi | Qc] . [phi | Kc]^T, the value-width products (att . V
+// forward; dO . V^T and att^T . dO backward, in 64-column chunks of the values) and the feature gradients dS . [phi_k
+// | Kc] and dS^T . [phi_q | Qc]. In fp32 every product stays on CUDA cores (exact fp32 sums).
 //
 // Scan. S_i = a_i S_{i-1} + b_i along each row (S_{-1} = 0); its backward is the same recurrence right to left:
 // l_i = g_i + a_{i+1} l_{i+1}, dL/db_i = l_i, dL/da_i = l_i S_{i-1}. One CTA per row: each thread composes the affine
@@ -137,7 +138,12 @@ struct BaSmem {
   __nv_bfloat16* attb;   // 32 x kBaLdb: att rounded to bf16 (zero outside C x 2C)
   __nv_bfloat16* vb;     // 64 x kBaLdb: value rows of the chunk
   __nv_bfloat16* ob;     // 32 x kBaLdb: output-gradient rows of the chunk
+  __nv_bfloat16* fq;     // 32 x (Fp + 8): the queries' [phi | Qc] rows, each part zero-padded to a multiple of 16
+  __nv_bfloat16* fk;     // 64 x (Fp + 8): the keys' [phi | Kc] rows
 };
+
+__host__ __device__ inline int ba_pad16(int x) { return (x + 15) / 16 * 16; }
+__host__ __device__ inline int ba_fp(int P, int CF) { return ba_pad16(P) + ba_pad16(CF); }
 
 __host__ __device__ inline size_t ba_smem_bytes(int C, int P, int CF, int K) {
   const size_t C2 = 2 * (size_t)C;
@@ -153,6 +159,7 @@ __host__ __device__ inline size_t ba_smem_bytes(int C, int P, int CF, int K) {
   n += (C2 + C) * (kBaBd + 1) * 4;
   n += 32 * 4;
   n += 16 + (size_t)(32 + 64 + 32) * kBaLdb * 2;
+  n += 16 + (size_t)(32 + 64) * (ba_fp(P, CF) + 8) * 2;
   return n + 64;
 }
 
@@ -191,6 +198,9 @@ __device__ inline BaSmem ba_carve(unsigned char* base, int C, int P, int CF, int
   s.attb = reinterpret_cast<__nv_bfloat16*>(take((size_t)32 * kBaLdb * 2));
   s.vb = reinterpret_cast<__nv_bfloat16*>(take((size_t)64 * kBaLdb * 2));
   s.ob = reinterpret_cast<__nv_bfloat16*>(take((size_t)32 * kBaLdb * 2));
+  p = base + ((p - base + 15) / 16 * 16);
+  s.fq = reinterpret_cast<__nv_bfloat16*>(take((size_t)32 * (ba_fp(P, CF) + 8) * 2));
+  s.fk = reinterpret_cast<__nv_bfloat16*>(take((size_t)64 * (ba_fp(P, CF) + 8) * 2));
   return s;
 }
 
@@ -222,6 +232,39 @@ __device__ void ba_scores(const BaArgs& a, const BaSmem& s, int64_t r, int j, fl
   const T* phi = reinterpret_cast<const T*>(a.phi);
   const T* qc = reinterpret_cast<const T*>(a.qc);
   const T* kc = reinterpret_cast<const T*>(a.kc);
+  if constexpr (Half) {
+    // [phi | Qc] of the queries and [phi | Kc] of the keys as bf16 tiles (zero rows / columns outside)
+    const int Pp = ba_pad16(P), Fp = ba_fp(P, CF), ldf = Fp + 8;
+    if (P % 8 == 0 && CF % 8 == 0) {               // 16-byte pieces (8 features) when rows allow them
+      const int nc8 = Fp / 8;
+      for (int e = tid; e < 96 * nc8; e += kBaThreads) {
+        const int i = e / nc8, c = (e % nc8) * 8;
+        const bool is_q = i < 32;
+        const int row = is_q ? i : i - 32;
+        const bool ok = is_q ? (row < C && s.qpos[row] >= 0) : (row < C2 && s.kpos[row] >= 0);
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (ok) {
+          const int64_t fil = is_q ? s.filq[row] : s.filk[row];
+          if (c < P) v = *reinterpret_cast<const uint4*>(phi + fil * P + c);
+          else if (c >= Pp && c - Pp < CF) v = *reinterpret_cast<const uint4*>((is_q ? qc : kc) + fil * CF + (c - Pp));
+        }
+        *reinterpret_cast<uint4*>((is_q ? s.fq : s.fk) + row * ldf + c) = v;
+      }
+    } else
+    for (int e = tid; e < 96 * Fp; e += kBaThreads) {
+      const int i = e / Fp, c = e % Fp;
+      const bool is_q = i < 32;
+      const int row = is_q ? i : i - 32;
+      const bool ok = is_q ? (row < C && s.qpos[row] >= 0) : (row < C2 && s.kpos[row] >= 0);
+      __nv_bfloat16 v = __float2bfloat16_rn(0.f);
+      if (ok) {
+        const int64_t fil = is_q ? s.filq[row] : s.filk[row];
+        if (c < P) v = phi[fil * P + c];
+        else if (c >= Pp && c - Pp < CF) v = (is_q ? qc : kc)[fil * CF + (c - Pp)];
+      }
+      (is_q ? s.fq : s.fk)[row * ldf + c] = v;
+    }
+  } else {
   for (int e = tid; e < C * P; e += kBaThreads) {
     const int i = e / P, c = e % P;
     s.phq[i * (P + 1) + c] = s.qpos[i] >= 0 ? ba_ld<Half>(phi, s.filq[i] * P + c) : 0.f;
@@ -237,6 +280,7 @@ __device__ void ba_scores(const BaArgs& a, const BaSmem& s, int64_t r, int j, fl
   for (int e = tid; e < C2 * CF; e += kBaThreads) {
     const int i = e / CF, c = e % CF;
     s.kcs[i * (CF + 1) + c] = s.kpos[i] >= 0 ? ba_ld<Half>(kc, s.filk[i] * CF + c) : 0.f;
+  }
   }
   for (int e = tid; e < C * K; e += kBaThreads) {
     const int i = e / K, c = e % K;
@@ -258,6 +302,32 @@ __device__ void ba_scores(const BaArgs& a, const BaSmem& s, int64_t r, int j, fl
     s.lak[i] = ok ? a.la[s.filk[i]] : 0.f;
   }
   __syncthreads();
+  if constexpr (Half) {
+    // phi_q . phi_k and Qc . Kc (32 x 64 each) on mma.sync; the scaled sum goes to s.ds as scratch
+    const int lane = tid & 31, wid = tid >> 5, i4 = lane >> 3, g = lane >> 2, t4 = lane & 3;
+    const int mt = wid & 1, nt = wid >> 1, Pp = ba_pad16(P), Fp = ba_fp(P, CF), ldf = Fp + 8;
+    float a1[2][4] = {}, a2[2][4] = {};
+    auto tile_product = [&](float(&acc)[2][4], int k0, int k1) {
+      for (int kk = k0; kk < k1; kk += 16) {
+        uint32_t x0, x1, x2, x3, y0, y1, y2, y3;
+        ba_ldsm_x4(s.fq + (16 * mt + (lane & 15)) * ldf + kk + (lane >> 4) * 8, x0, x1, x2, x3);
+        ba_ldsm_x4(s.fk + (16 * nt + (i4 >> 1) * 8 + (lane & 7)) * ldf + kk + (i4 & 1) * 8, y0, y1, y2, y3);
+        ba_mma(acc[0], x0, x1, x2, x3, y0, y1);
+        ba_mma(acc[1], x0, x1, x2, x3, y2, y3);
+      }
+    };
+    tile_product(a1, 0, Pp);
+    tile_product(a2, Pp, Fp);
+#pragma unroll
+    for (int jn = 0; jn < 2; ++jn)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int q = 16 * mt + g + 8 * (e >> 1), k = 16 * nt + 8 * jn + 2 * t4 + (e & 1);
+        if (q < C && k < C2)
+          s.ds[q * (C2 + 1) + k] = __fadd_rn(__fmul_rn(a1[jn][e], a.scale_phi), __fmul_rn(a2[jn][e], a.scale_c));
+      }
+    __syncthreads();
+  }
   const float tasa = a.gamma[r % a.T] / (float)C;
   // thread -> query tid / 8, keys tid % 8 + 8 u
   const int iq = tid >> 3;
@@ -265,8 +335,10 @@ __device__ void ba_scores(const BaArgs& a, const BaSmem& s, int64_t r, int j, fl
     for (int ik = tid & 7; ik < C2; ik += 8) {
       const bool qm = s.qpos[iq] >= 0, km = s.kpos[ik] >= 0;
       float s1 = 0.f, s2 = 0.f;
-      for (int c = 0; c < P; ++c) s1 = fmaf(s.phq[iq * (P + 1) + c], s.phk[ik * (P + 1) + c], s1);
-      for (int c = 0; c < CF; ++c) s2 = fmaf(s.qcs[iq * (CF + 1) + c], s.kcs[ik * (CF + 1) + c], s2);
+      if constexpr (!Half) {
+        for (int c = 0; c < P; ++c) s1 = fmaf(s.phq[iq * (P + 1) + c], s.phk[ik * (P + 1) + c], s1);
+        for (int c = 0; c < CF; ++c) s2 = fmaf(s.qcs[iq * (CF + 1) + c], s.kcs[ik * (CF + 1) + c], s2);
+      }
       bool sigue = qm && km;
       int largo = 0;
       for (int c = 0; c < K; ++c) {
@@ -274,7 +346,7 @@ __device__ void ba_scores(const BaArgs& a, const BaSmem& s, int64_t r, int j, fl
         largo += sigue ? 1 : 0;
       }
       const float dt = __fadd_rn(__fsub_rn(s.bk[2 * ik], s.bq[2 * iq]), __fsub_rn(s.bk[2 * ik + 1], s.bq[2 * iq + 1]));
-      float sc = __fadd_rn(__fmul_rn(s1, a.scale_phi), __fmul_rn(s2, a.scale_c));
+      float sc = Half ? s.ds[iq * (C2 + 1) + ik] : __fadd_rn(__fmul_rn(s1, a.scale_phi), __fmul_rn(s2, a.scale_c));
       sc = __fadd_rn(__fadd_rn(__fadd_rn(sc, a.w_suf[largo]), s.lak[ik]), __fmul_rn(tasa, dt));
       const bool valido = ik >= iq && ik < C + iq && s.qid[iq] == s.kid[ik] && km && qm;
       s.att[iq * (C2 + 1) + ik] = valido ? sc : -INFINITY;       // -inf marks an invalid key (weight exactly 0)
@@ -555,6 +627,69 @@ __global__ void __launch_bounds__(kBaThreads) k_bucket_attn_bwd(const BaArgs a) 
   T* gpk = reinterpret_cast<T*>(a.g_phi_k);
   T* gqc = reinterpret_cast<T*>(a.g_qc);
   T* gkc = reinterpret_cast<T*>(a.g_kc);
+  if constexpr (Half) {
+    // dS rounded to bf16 into attb (free after the value products), then [dphi_q | dQc] = dS . [phi_k | Kc] and
+    // [dphi_k | dKc] = dS^T . [phi_q | Qc] on mma.sync, 16 x 16 output tiles round-robin over the warps
+    for (int e = tid; e < 32 * 64; e += kBaThreads) {
+      const int q = e >> 6, k = e & 63;
+      s.attb[q * kBaLdb + k] = __float2bfloat16_rn(q < C && k < C2 ? s.ds[q * (C2 + 1) + k] : 0.f);
+    }
+    __syncthreads();
+    const int g = lane >> 2, t4 = lane & 3, i4 = lane >> 3;
+    const int Pp = ba_pad16(P), Fp = ba_fp(P, CF), ldf = Fp + 8, nfb = Fp / 16;
+    // queries: 2 row tiles x nfb column blocks, K = the 64 keys
+    for (int tile = wid; tile < 2 * nfb; tile += kBaThreads / 32) {
+      const int mt = tile & 1, nb = tile >> 1;
+      float acc[2][4] = {};
+#pragma unroll
+      for (int kk = 0; kk < 64; kk += 16) {
+        uint32_t x0, x1, x2, x3, y0, y1, y2, y3;
+        ba_ldsm_x4(s.attb + (16 * mt + (lane & 15)) * kBaLdb + kk + (lane >> 4) * 8, x0, x1, x2, x3);
+        ba_ldsm_x4_t(s.fk + (kk + (i4 & 1) * 8 + (lane & 7)) * ldf + 16 * nb + (i4 >> 1) * 8, y0, y1, y2, y3);
+        ba_mma(acc[0], x0, x1, x2, x3, y0, y1);
+        ba_mma(acc[1], x0, x1, x2, x3, y2, y3);
+      }
+#pragma unroll
+      for (int jn = 0; jn < 2; ++jn)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int q = 16 * mt + g + 8 * (e >> 1), c = 16 * nb + 8 * jn + 2 * t4 + (e & 1);
+          if (q >= C || s.qpos[q] < 0) continue;
+          const int64_t lq = r * L + s.qpos[q];
+          if (c < P) gpq[lq * P + c] = __float2bfloat16_rn(acc[jn][e] * a.scale_phi);
+          else if (c >= Pp && c - Pp < CF) gqc[lq * CF + (c - Pp)] = __float2bfloat16_rn(acc[jn][e] * a.scale_c);
+        }
+    }
+    // keys: 4 row tiles x nfb column blocks, K = the 32 queries
+    for (int tile = wid; tile < 4 * nfb; tile += kBaThreads / 32) {
+      const int mk = tile & 3, nb = tile >> 2;
+      float acc[2][4] = {};
+#pragma unroll
+      for (int kq = 0; kq < 32; kq += 16) {
+        uint32_t x0, x1, x2, x3, y0, y1, y2, y3;
+        ba_ldsm_x4_t(s.attb + (kq + (i4 >> 1) * 8 + (lane & 7)) * kBaLdb + 16 * mk + (i4 & 1) * 8, x0, x1, x2, x3);
+        ba_ldsm_x4_t(s.fq + (kq + (i4 & 1) * 8 + (lane & 7)) * ldf + 16 * nb + (i4 >> 1) * 8, y0, y1, y2, y3);
+        ba_mma(acc[0], x0, x1, x2, x3, y0, y1);
+        ba_mma(acc[1], x0, x1, x2, x3, y2, y3);
+      }
+#pragma unroll
+      for (int jn = 0; jn < 2; ++jn)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int k = 16 * mk + g + 8 * (e >> 1), c = 16 * nb + 8 * jn + 2 * t4 + (e & 1);
+          if (k >= C2 || s.kpos[k] < 0) continue;
+          const int64_t lk = lugar_k(k), zk = r * L + s.kpos[k];
+          const bool zero = last_block && k >= C;
+          if (c < P) {
+            gpk[lk * P + c] = __float2bfloat16_rn(acc[jn][e] * a.scale_phi);
+            if (zero) gpk[zk * P + c] = __float2bfloat16_rn(0.f);
+          } else if (c >= Pp && c - Pp < CF) {
+            gkc[lk * CF + (c - Pp)] = __float2bfloat16_rn(acc[jn][e] * a.scale_c);
+            if (zero) gkc[zk * CF + (c - Pp)] = __float2bfloat16_rn(0.f);
+          }
+        }
+    }
+  } else {
   // query-side gradients: dphi_q = dS phi_k, dQc = dS Kc
   for (int e = tid; e < C * (P + CF); e += kBaThreads) {
     const int q = e / (P + CF), c = e % (P + CF);
@@ -587,6 +722,7 @@ __global__ void __launch_bounds__(kBaThreads) k_bucket_attn_bwd(const BaArgs a) 
       ba_st<Half>(gkc, lk * CF + cc, acc * a.scale_c);
       if (zero) ba_st<Half>(gkc, zk * CF + cc, 0.f);
     }
+  }
   }
   // per-key column sums (log_alfa, clock of the key), per-query row sums (clock of the query)
   for (int k = tid; k < C2; k += kBaThreads) {
