@@ -145,27 +145,29 @@ struct BaSmem {
 __host__ __device__ inline int ba_pad16(int x) { return (x + 15) / 16 * 16; }
 __host__ __device__ inline int ba_fp(int P, int CF) { return ba_pad16(P) + ba_pad16(CF); }
 
-__host__ __device__ inline size_t ba_smem_bytes(int C, int P, int CF, int K) {
-  const size_t C2 = 2 * (size_t)C;
+// half: the bf16 path, which reads its features and values from the bf16 tiles only (the fp32 copies get no space)
+__host__ __device__ inline size_t ba_smem_bytes(int C, int P, int CF, int K, bool half) {
+  const size_t C2 = 2 * (size_t)C, f32 = half ? 0 : 1;
   size_t n = 0;
   n += (C + C2) * 8;                                       // filq, filk
   n += (C + C2) * 4 * 2;                                   // qpos, kpos, qid, kid
-  n += (C + C2) * (P + 1) * 4 + (C + C2) * (CF + 1) * 4;
+  n += f32 * ((C + C2) * (P + 1) * 4 + (C + C2) * (CF + 1) * 4);
   n += (C + C2) * (K > 0 ? K : 1) * 4;
   n += (C + C2) * 2 * 4 + C2 * 4;
   n += 2 * (size_t)C * (C2 + 1) * 4;
   n += (size_t)C * C2;
   n = (n + 15) / 16 * 16;
-  n += (C2 + C) * (kBaBd + 1) * 4;
+  n += f32 * (C2 + C) * (kBaBd + 1) * 4;
   n += 32 * 4;
   n += 16 + (size_t)(32 + 64 + 32) * kBaLdb * 2;
   n += 16 + (size_t)(32 + 64) * (ba_fp(P, CF) + 8) * 2;
   return n + 64;
 }
 
-__device__ inline BaSmem ba_carve(unsigned char* base, int C, int P, int CF, int K) {
+__device__ inline BaSmem ba_carve(unsigned char* base, int C, int P, int CF, int K, bool half) {
   BaSmem s;
   const int C2 = 2 * C;
+  const size_t f32 = half ? 0 : 1;
   unsigned char* p = base;
   auto take = [&](size_t bytes) {
     unsigned char* q = p;
@@ -178,10 +180,10 @@ __device__ inline BaSmem ba_carve(unsigned char* base, int C, int P, int CF, int
   s.kpos = reinterpret_cast<int*>(take((size_t)C2 * 4));
   s.qid = reinterpret_cast<int*>(take((size_t)C * 4));
   s.kid = reinterpret_cast<int*>(take((size_t)C2 * 4));
-  s.phq = reinterpret_cast<float*>(take((size_t)C * (P + 1) * 4));
-  s.phk = reinterpret_cast<float*>(take((size_t)C2 * (P + 1) * 4));
-  s.qcs = reinterpret_cast<float*>(take((size_t)C * (CF + 1) * 4));
-  s.kcs = reinterpret_cast<float*>(take((size_t)C2 * (CF + 1) * 4));
+  s.phq = reinterpret_cast<float*>(take(f32 * C * (P + 1) * 4));
+  s.phk = reinterpret_cast<float*>(take(f32 * C2 * (P + 1) * 4));
+  s.qcs = reinterpret_cast<float*>(take(f32 * C * (CF + 1) * 4));
+  s.kcs = reinterpret_cast<float*>(take(f32 * C2 * (CF + 1) * 4));
   s.pfq = reinterpret_cast<float*>(take((size_t)C * (K > 0 ? K : 1) * 4));
   s.pfk = reinterpret_cast<float*>(take((size_t)C2 * (K > 0 ? K : 1) * 4));
   s.bq = reinterpret_cast<float*>(take((size_t)C * 2 * 4));
@@ -191,8 +193,8 @@ __device__ inline BaSmem ba_carve(unsigned char* base, int C, int P, int CF, int
   s.ds = reinterpret_cast<float*>(take((size_t)C * (C2 + 1) * 4));
   s.largo = take((size_t)C * C2);
   p = base + ((p - base + 15) / 16 * 16);
-  s.vs = reinterpret_cast<float*>(take((size_t)C2 * (kBaBd + 1) * 4));
-  s.os = reinterpret_cast<float*>(take((size_t)C * (kBaBd + 1) * 4));
+  s.vs = reinterpret_cast<float*>(take(f32 * C2 * (kBaBd + 1) * 4));
+  s.os = reinterpret_cast<float*>(take(f32 * C * (kBaBd + 1) * 4));
   s.red = reinterpret_cast<float*>(take(32 * 4));
   p = base + ((p - base + 15) / 16 * 16);
   s.attb = reinterpret_cast<__nv_bfloat16*>(take((size_t)32 * kBaLdb * 2));
@@ -421,7 +423,7 @@ template <bool Half>
 __global__ void __launch_bounds__(kBaThreads) k_bucket_attn_fwd(const BaArgs a) {
   using T = typename BaT<Half>::T;
   extern __shared__ __align__(16) unsigned char ba_smem[];
-  const BaSmem s = ba_carve(ba_smem, a.C, a.P, a.CF, a.K);
+  const BaSmem s = ba_carve(ba_smem, a.C, a.P, a.CF, a.K, Half);
   const int64_t r = blockIdx.x;
   const int j = blockIdx.y, C = a.C, C2 = 2 * C, D = a.D, tid = threadIdx.x;
   ba_scores<Half>(a, s, r, j, a.sen);
@@ -486,7 +488,7 @@ template <bool Half>
 __global__ void __launch_bounds__(kBaThreads) k_bucket_attn_bwd(const BaArgs a) {
   using T = typename BaT<Half>::T;
   extern __shared__ __align__(16) unsigned char ba_smem[];
-  const BaSmem s = ba_carve(ba_smem, a.C, a.P, a.CF, a.K);
+  const BaSmem s = ba_carve(ba_smem, a.C, a.P, a.CF, a.K, Half);
   const int64_t r = blockIdx.x, L = a.L, BT = a.B * a.T;
   const int j = blockIdx.y, C = a.C, C2 = 2 * C, D = a.D, P = a.P, CF = a.CF, K = a.K, tid = threadIdx.x;
   const int lane = tid & 31, wid = tid >> 5;
@@ -852,7 +854,7 @@ __global__ void __launch_bounds__(kScanThreads) k_scan_bwd(int64_t L, const floa
 int ba_check(int64_t B, int64_t L, int T, int C, int P, int CF, int K, int D) {
   if (B < 0 || L < 0 || T <= 0 || C <= 0 || P <= 0 || CF < 0 || K < 0 || D <= 0) return ASRN_ERR_ARG;
   if (C > kBaMaxC || P > kMaxPhi || CF > kMaxConfirm || K > kMaxSuffix) return ASRN_ERR_UNSUPPORTED;
-  if (ba_smem_bytes(C, P, CF, K) > 220 * 1024) return ASRN_ERR_UNSUPPORTED;
+  if (ba_smem_bytes(C, P, CF, K, false) > 220 * 1024) return ASRN_ERR_UNSUPPORTED;
   return ASRN_OK;
 }
 
@@ -908,7 +910,7 @@ int asrn_bucket_attn_forward(int64_t B, int64_t L, int32_t T, int32_t C, int32_t
                      scale_phi, scale_c);
   a.out = out;
   a.sen = sen;
-  const size_t smem = ba_smem_bytes(C, P, CF, K);
+  const size_t smem = ba_smem_bytes(C, P, CF, K, half != 0);
   const dim3 grid((unsigned)(B * T), (unsigned)a.NB);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (half) {
@@ -947,7 +949,7 @@ int asrn_bucket_attn_backward(int64_t B, int64_t L, int32_t T, int32_t C, int32_
   a.g_la = g_la;
   a.g_b_k = g_b_k;
   a.partes = partes;
-  const size_t smem = ba_smem_bytes(C, P, CF, K);
+  const size_t smem = ba_smem_bytes(C, P, CF, K, half != 0);
   const dim3 grid((unsigned)(B * T), (unsigned)a.NB);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (half) {
