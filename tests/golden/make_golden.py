@@ -383,6 +383,9 @@ def main(ref):
     grad_case('grad_default', 64, 2, 256, 64, {}, seed=3)
     layer_grad_case('layer_grad_crowded', 64, 2, 200, 40, dict(chunk=16, n_bits=4))
     layer_grad_case('layer_grad_default', 64, 2, 160, 64, {}, seed=2)
+    grad_case('grad_ragged', 48, 2, 203, 24, dict(chunk=8, n_bits=6, confirmar=20, sufijo=6, vistos=3), seed=4)
+    layer_grad_case('layer_grad_ragged', 48, 2, 203, 24, dict(chunk=8, n_bits=6, confirmar=20, sufijo=6, vistos=3),
+                    seed=4)
 
 
 if __name__ == '__main__':
@@ -398,6 +401,11 @@ if __name__ == '__main__':
              'grad': lambda: (grad_case('grad_crowded', 64, 2, 300, 40, dict(chunk=16, n_bits=4)),
                               grad_case('grad_default', 64, 2, 256, 64, {}, seed=3)),
              'layer_grad': lambda: (layer_grad_case('layer_grad_crowded', 64, 2, 200, 40, dict(chunk=16, n_bits=4)),
-                                    layer_grad_case('layer_grad_default', 64, 2, 160, 64, {}, seed=2))}[case]()
+                                    layer_grad_case('layer_grad_default', 64, 2, 160, 64, {}, seed=2)),
+             'grad_ragged': lambda: (
+                 grad_case('grad_ragged', 48, 2, 203, 24, dict(chunk=8, n_bits=6, confirmar=20, sufijo=6, vistos=3),
+                           seed=4),
+                 layer_grad_case('layer_grad_ragged', 48, 2, 203, 24,
+                                 dict(chunk=8, n_bits=6, confirmar=20, sufijo=6, vistos=3), seed=4))}[case]()
     else:
         main(sys.argv[1])

@@ -54,7 +54,7 @@ def _run(f, m, cuda, half):
     return salida, sen, grads
 
 
-@pytest.mark.parametrize('name', ['grad_crowded', 'grad_default'])
+@pytest.mark.parametrize('name', ['grad_crowded', 'grad_default', 'grad_ragged'])
 def test_bucket_attention_forward_and_gradients_match_reference(name, cuda):
     f, m = _fixture(name)
     salida, sen, grads = _run(f, m, cuda, False)
@@ -71,8 +71,9 @@ def test_bucket_attention_forward_and_gradients_match_reference(name, cuda):
         assert rel_err(grads[k].cpu().numpy(), f['grad_' + k]) <= 1e-4, k
 
 
-def test_bucket_attention_bf16_operands(cuda):
-    f, m = _fixture('grad_crowded')
+@pytest.mark.parametrize('name', ['grad_crowded', 'grad_ragged'])
+def test_bucket_attention_bf16_operands(name, cuda):
+    f, m = _fixture(name)
     salida, _, grads = _run(f, m, cuda, True)
     assert salida.dtype == torch.bfloat16
     assert rel_err(salida.detach().float().cpu().numpy(), f['salida']) <= 3e-2

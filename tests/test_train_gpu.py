@@ -30,7 +30,7 @@ def _case(name, cuda):
     return z, layer, E, h, x
 
 
-@pytest.mark.parametrize('name', ['layer_grad_crowded', 'layer_grad_default'])
+@pytest.mark.parametrize('name', ['layer_grad_crowded', 'layer_grad_default', 'layer_grad_ragged'])
 def test_layer_gradients_match_reference(name, cuda):
     z, layer, E, h, x = _case(name, cuda)
     y = layer(E, h, x)
