@@ -888,7 +888,7 @@ def leg_train(args, dev, rank, world):
     n = max(3, args.steps // 4)
     ms, step_ms = timed(step, n)
     cpu = None
-    if not args.no_cpu_baseline:
+    if world == 1 and not args.no_cpu_baseline:
         try:
             state = {k: v.detach().cpu() for k, v in layer.state_dict().items()}
             seg = 2048
