@@ -96,55 +96,62 @@ __global__ void __launch_bounds__(256) k_context(ContextArgs a) {
   }
 }
 
-// Inclusive fp64 prefix sum along L, one block per batch row, chunks of 1024 * 4 with a running carry.
+// Inclusive fp64 prefix sum along L (the clock B_t = cumsum(beta), asrn/estable.py:418). Block (c, b) owns chunk c
+// of row b (kClockChunk slots): it first sums every beta before its chunk itself (a block-wide fp64 reduction; the
+// reads of all blocks add up to about L^2 / (2 kClockChunk) values per row, a few tens of MB at L = 262,144), then
+// scans its chunk (4 slots per thread) on top of that sum. No block waits for another and no workspace is needed; a
+// long row is spread over L / kClockChunk blocks instead of one block walking the whole row.
+constexpr int kClockItems = 4;
+constexpr int kClockChunk = 1024 * kClockItems;
+
 __global__ void __launch_bounds__(1024) k_clock(const double* __restrict__ beta, double* __restrict__ Bt, int64_t L) {
-  const int64_t b = blockIdx.x;
+  const int64_t b = blockIdx.y, c0 = (int64_t)blockIdx.x * kClockChunk;
   const double* src = beta + b * L;
   double* dst = Bt + b * L;
   __shared__ double warp_tot[32];
-  __shared__ double carry_s;
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
-  if (tid == 0) carry_s = 0.0;
-  __syncthreads();
-  constexpr int kItems = 4;
-  for (int64_t base = 0; base < L; base += 1024 * kItems) {
-    double v[kItems];
-    double run = 0.0;
+  // the sum of the row before this chunk
+  double pre = 0.0;
+  for (int64_t i = tid; i < c0; i += 1024) pre += src[i];
 #pragma unroll
-    for (int k = 0; k < kItems; ++k) {
-      int64_t i = base + (int64_t)tid * kItems + k;
-      run += (i < L) ? src[i] : 0.0;
-      v[k] = run;
-    }
-    // warp inclusive scan of the thread totals
-    double t = run;
+  for (int o = 16; o > 0; o >>= 1) pre += __shfl_xor_sync(0xffffffffu, pre, o);
+  if (lane == 0) warp_tot[wid] = pre;
+  __syncthreads();
+  double carry = 0.0;
+  for (int w = 0; w < 32; ++w) carry += warp_tot[w];
+  __syncthreads();
+  // the chunk: per-thread runs, a warp scan of the run totals, a block scan of the warp totals
+  double v[kClockItems];
+  double run = 0.0;
+#pragma unroll
+  for (int k = 0; k < kClockItems; ++k) {
+    const int64_t i = c0 + (int64_t)tid * kClockItems + k;
+    run += (i < L) ? src[i] : 0.0;
+    v[k] = run;
+  }
+  double t = run;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const double y = __shfl_up_sync(0xffffffffu, t, o);
+    if (lane >= o) t += y;
+  }
+  if (lane == 31) warp_tot[wid] = t;
+  __syncthreads();
+  if (wid == 0) {
+    double w = warp_tot[lane];
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      double y = __shfl_up_sync(0xffffffffu, t, o);
-      if (lane >= o) t += y;
+      const double y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
     }
-    if (lane == 31) warp_tot[wid] = t;
-    __syncthreads();
-    if (wid == 0) {
-      double w = warp_tot[lane];
+    warp_tot[lane] = w;
+  }
+  __syncthreads();
+  const double excl = carry + (wid > 0 ? warp_tot[wid - 1] : 0.0) + (t - run);
 #pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        double y = __shfl_up_sync(0xffffffffu, w, o);
-        if (lane >= o) w += y;
-      }
-      warp_tot[lane] = w;
-    }
-    __syncthreads();
-    const double carry = carry_s;
-    const double excl = carry + (wid > 0 ? warp_tot[wid - 1] : 0.0) + (t - run);
-#pragma unroll
-    for (int k = 0; k < kItems; ++k) {
-      int64_t i = base + (int64_t)tid * kItems + k;
-      if (i < L) dst[i] = excl + v[k];
-    }
-    __syncthreads();
-    if (tid == 0) carry_s = carry + warp_tot[31];
-    __syncthreads();
+  for (int k = 0; k < kClockItems; ++k) {
+    const int64_t i = c0 + (int64_t)tid * kClockItems + k;
+    if (i < L) dst[i] = excl + v[k];
   }
 }
 
@@ -166,7 +173,10 @@ int launch_context(const ContextArgs& a, bool half, cudaStream_t s) {
 
 int launch_clock(const double* beta, double* Bt, int64_t B, int64_t L, cudaStream_t s) {
   if (B == 0 || L == 0) return ASRN_OK;
-  k_clock<<<(unsigned)B, 1024, 0, s>>>(beta, Bt, L);
+  for (int64_t b0 = 0; b0 < B; b0 += 65535) {          // grid.y holds at most 65535 rows
+    const dim3 grid((unsigned)((L + kClockChunk - 1) / kClockChunk), (unsigned)(B - b0 < 65535 ? B - b0 : 65535));
+    k_clock<<<grid, 1024, 0, s>>>(beta + b0 * L, Bt + b0 * L, L);
+  }
   return cudaGetLastError() == cudaSuccess ? ASRN_OK : ASRN_ERR_CUDA;
 }
 

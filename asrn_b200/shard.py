@@ -123,6 +123,21 @@ def _row_payload(loc, sel, Ea_next):
     return torch.cat(parts, 1)
 
 
+def _row_payload_next(loc, sel, Lc):
+    """As _row_payload, with the value rows taken straight from the chunk's own E rows: the value row of local
+    position p is E[p + 1]; a sequence's last local position gets a zero row (the receiver writes the next chunk's
+    first row there). Only the selected rows are read (no shifted copy of the chunk)."""
+    parts = []
+    for k in _ROW_KEYS:
+        x = loc[k]
+        parts.append(x.reshape(-1, x.shape[-1])[sel].contiguous().view(torch.uint8))
+    ea = loc['Ea'].reshape(-1, loc['Ea'].shape[-1])
+    rows = ea[(sel + 1).clamp(max=ea.shape[0] - 1)]
+    rows = rows.masked_fill(((sel % Lc) == Lc - 1).unsqueeze(1), 0)
+    parts.append(rows.contiguous().view(torch.uint8))
+    return torch.cat(parts, 1)
+
+
 def _row_widths(loc, Ea_next):
     return [loc[k].shape[-1] * loc[k].element_size() for k in _ROW_KEYS] + \
         [Ea_next.shape[-1] * Ea_next.element_size()]
@@ -237,12 +252,16 @@ def chunk_bounds(L, world, rank):
     return rank * Lc, (rank + 1) * Lc
 
 
-def _phase1(layer, E, h, tokens, E_halo, half, c0):
+def _phase1(layer, E, h, tokens, E_halo, half, c0, E_ext=None):
     """Local stages of one chunk starting at position c0. E, h (B, Lc, d) fp32, tokens (B, Lc) or None, E_halo (B, d):
-    E of the position before the chunk."""
+    E of the position before the chunk. E_ext: a (B, Lc + 1, d) buffer whose rows 1 .. Lc are E's own storage; the
+    halo goes to its row 0 (else the extended rows are a copy)."""
     ctx = stages.context(layer, h, tokens, E=None if tokens is not None else E, half=half)
     Bt = stages.clock(ctx['beta'])
-    E_ext = torch.cat([E_halo.unsqueeze(1).to(E.dtype), E], 1)
+    if E_ext is not None and E_ext.shape[1] == E.shape[1] + 1 and E_ext[:, 1:].data_ptr() == E.data_ptr():
+        E_ext[:, 0].copy_(E_halo)
+    else:
+        E_ext = torch.cat([E_halo.unsqueeze(1).to(E.dtype), E], 1)
     hs = stages.hash(layer, E_ext, half=half)
     B, Lc = E.shape[:2]
     T = layer.n_tablas
@@ -592,13 +611,13 @@ def forward(layer, E, h, tokens=None, group=None):
     return out
 
 
-def _forward(layer, E, h, tokens, group, caps):
+def _forward(layer, E, h, tokens, group, caps, bufs=None):
     """The sharded forward. caps None: the exchange is sized from the counts read by the host (one synchronisation);
     caps = (tails, rows): fixed capacities, no host synchronisation (a count above its capacity is recorded in the
     status word). Returns (h' of the chunk, device status word, device (tails, rows) counts of this rank)."""
     import torch.distributed as dist
     if caps is not None:
-        return _forward_packed(layer, E, h, tokens, group, caps)
+        return _forward_packed(layer, E, h, tokens, group, caps, bufs)
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
     half = compute_half('cuda')
@@ -696,14 +715,16 @@ def _all_gather_bytes(buf, world, group):
     return out
 
 
-def _forward_packed(layer, E, h, tokens, group, caps):
+def _forward_packed(layer, E, h, tokens, group, caps, bufs=None):
     """The sharded forward with fixed exchange capacities caps = (tails, rows) and no host synchronisation, its
     exchanges packed into four all-gathers: (1) the halo row; (2) in one buffer, the chunk sums of beta, the
-    per-position scalars, the chunk's first bf16 E row, its non-empty bucket tails and the feature / value rows of
-    its tail positions (the value row of a chunk's last position is taken from the next chunk's first row on
-    arrival); (3) the n-gram keys and summaries; (4) the streak maps. The full-length feature buffers are zero-filled
-    first, as in the unpacked path: a masked key's value row still enters the value product with weight 0, so it must
-    hold numbers. A count above its capacity is recorded in the status word."""
+    per-position signature, clock and log_alfa, the chunk's first bf16 E row, its non-empty bucket tails and the
+    feature / value rows of its tail positions (the value row of a chunk's last position is taken from the next
+    chunk's first row on arrival); (3) the n-gram keys and summaries; (4) the streak maps. The full-length feature buffers must hold numbers
+    in every row (a masked key's value row still enters the value product with weight 0): they come from `bufs` (a
+    dict kept by the caller, zero-filled on first use and reused, so a captured step does no memset; a reused row
+    holds the finite values of an earlier step) or are zero-filled here. A count above its capacity is recorded in
+    the status word."""
     import torch.distributed as dist
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
@@ -715,7 +736,7 @@ def _forward_packed(layer, E, h, tokens, group, caps):
     cap_t, cap_r = caps
     E, h = E.float().contiguous(), h.float().contiguous()
     halo = exchange_halo(E[:, -1], world, rank, group)
-    loc = _phase1(layer, E, h, tokens, halo, half, c0)
+    loc = _phase1(layer, E, h, tokens, halo, half, c0, None if bufs is None else bufs.get('_E_ext'))
     # what this chunk publishes: its non-empty tails (compacted), the positions in them, their rows
     tails = loc['tails']
     C1 = tails.shape[-1]
@@ -731,29 +752,34 @@ def _forward_packed(layer, E, h, tokens, group, caps):
     flags.index_fill_(0, (b_of.unsqueeze(1) * (Lc + 1) + rel).view(-1), True)
     flags = flags.view(B, Lc + 1)[:, :Lc].reshape(-1)
     sel = compact_cap(flags, cap_r)
-    Ea_next = torch.cat([loc['Ea'][:, 1:], torch.zeros_like(loc['Ea'][:, :1])], 1)   # last row: fixed on arrival
-    widths = _row_widths(loc, Ea_next)
-    payload = _row_payload(loc, sel.clamp(min=0), Ea_next)
+    widths = _row_widths(loc, loc['Ea'])
+    payload = _row_payload_next(loc, sel.clamp(min=0), Lc)      # a sequence's last row: fixed on arrival
     gidx = torch.where(sel >= 0, (sel // Lc) * L + c0 + sel % Lc, -1)
     local_counts = torch.stack([t_ne.sum(), flags.sum()])
     over = (local_counts[0] > cap_t) | (local_counts[1] > cap_r)
-    buf, meta = _pack([loc['Bt'][:, -1], loc['Bt'], loc['beta'], loc['sig'], loc['log_alfa'], loc['Ea'][:, 0],
+    # (beta is not sent: the sequence-wide steps read sig, the clock and log_alfa only)
+    buf, meta = _pack([loc['Bt'][:, -1], loc['Bt'], loc['sig'], loc['log_alfa'], loc['Ea'][:, 0],
                        t_rows, t_idx, payload, gidx])
     got = _all_gather_bytes(buf, world, group)
     sums = _unpack(got, meta, 0)                                          # (world, B)
     full = {}
-    for i, k in ((1, 'Bt'), (2, 'beta'), (3, 'sig'), (4, 'log_alfa')):
+    for i, k in ((1, 'Bt'), (2, 'sig'), (3, 'log_alfa')):
         full[k] = _unpack(got, meta, i).permute(1, 0, 2).reshape(B, L)    # (world, B, Lc) -> (B, L)
     _apply_clock_offsets(full['Bt'], sums, Lc)
-    firsts = _unpack(got, meta, 5)                                        # (world, B, d)
+    firsts = _unpack(got, meta, 4)                                        # (world, B, d)
     ng = ngram_sort(layer, full, c0, Lc, half)
     # the feature rows: this chunk's own, the earlier chunks' tail positions, every chunk start's value row
     for k in _ROW_KEYS + ('Ea',):
         x = loc[k]
-        t = torch.zeros((B * L + 1,) + tuple(x.shape[2:]), dtype=x.dtype, device=x.device)
+        shape = (B * L + 1,) + tuple(x.shape[2:])
+        t = None if bufs is None else bufs.get(k)
+        if t is None or tuple(t.shape) != shape or t.dtype != x.dtype:
+            t = torch.zeros(shape, dtype=x.dtype, device=x.device)
+            if bufs is not None:
+                bufs[k] = t
         t[:B * L].view((B, L) + tuple(x.shape[2:]))[:, c0:c1] = x
         full[k] = t
-    pay_all, gidx_all = _unpack(got, meta, 8), _unpack(got, meta, 9)
+    pay_all, gidx_all = _unpack(got, meta, 7), _unpack(got, meta, 8)
     for q in range(rank):
         _scatter_rows(full, pay_all[q], gidx_all[q], widths, L)
     ea = full['Ea'][:B * L].view(B, L, -1)
@@ -761,8 +787,8 @@ def _forward_packed(layer, E, h, tokens, group, caps):
         ea[:, q * Lc] = firsts[q]
     tails_prev = None
     if rank > 0:
-        ent = _unpack(got, meta, 6)[:rank].contiguous().view(torch.uint8).view(rank, cap_t, -1)
-        tails_prev = expand_tails(ent, _unpack(got, meta, 7)[:rank], tails.shape)
+        ent = _unpack(got, meta, 5)[:rank].contiguous().view(torch.uint8).view(rank, cap_t, -1)
+        tails_prev = expand_tails(ent, _unpack(got, meta, 6)[:rank], tails.shape)
     keys, summ = exchange_ngram(ng['keys'], ng['summ'], world, group)
     vistos, hawkes = ngram_finish(layer, full, ng, keys[:rank] if rank > 0 else None,
                                   summ[:rank] if rank > 0 else None, c0, Lc, half)
@@ -790,7 +816,12 @@ class ShardedForward:
         _check(layer, E, h, tokens)
         self.layer, self.group = layer, group
         self.device = E.device
-        self.E = E.float().contiguous().clone()
+        B, Lc, d = E.shape
+        # the input buffers of the graph: E lives in rows 1 .. Lc of a (B, Lc + 1, d) buffer whose row 0 receives the
+        # previous chunk's last row (so the hash reads the extended rows in place); for one sequence E is contiguous
+        self.E_ext = torch.empty(B, Lc + 1, d, dtype=torch.float32, device=E.device)
+        self.E = self.E_ext[:, 1:]
+        self.E.copy_(E)
         self.h = h.float().contiguous().clone()
         self.tokens = None if tokens is None else tokens.contiguous().clone()
         world = dist.get_world_size(group)
@@ -798,24 +829,25 @@ class ShardedForward:
             _, _, cnt = _forward(layer, self.E, self.h, self.tokens, group, None)
             counts = exchange_counts(cnt, world, group)
         self.caps = tuple(int(max(c[j] for c in counts) * margin) + extra for j in range(2))
+        self.bufs = {'_E_ext': self.E_ext}                      # full-length feature rows, zeroed once, reused
         side = torch.cuda.Stream(self.device)
         side.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(side), torch.no_grad():           # warm the capacity path (allocations, kernels)
-            _forward(layer, self.E, self.h, self.tokens, group, self.caps)
+            _forward(layer, self.E, self.h, self.tokens, group, self.caps, self.bufs)
         torch.cuda.current_stream(self.device).wait_stream(side)
         torch.cuda.synchronize(self.device)
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph), torch.no_grad():
-            self.out, self.status, _ = _forward(layer, self.E, self.h, self.tokens, group, self.caps)
+            self.out, self.status, _ = _forward(layer, self.E, self.h, self.tokens, group, self.caps, self.bufs)
 
-    def __call__(self, E, h, tokens=None):
+    def __call__(self, E=None, h=None, tokens=None):
         """h' of this rank's chunk for new inputs of the captured shapes (the returned tensor is overwritten by the
-        next call)."""
+        next call). The inputs are copied into the graph's input buffers (self.E, self.h, self.tokens); a caller that
+        writes its inputs there itself passes nothing (or those buffers) and no copy is made."""
         _raise_reported(self.device, block=False)
-        self.E.copy_(E)
-        self.h.copy_(h)
-        if self.tokens is not None:
-            self.tokens.copy_(tokens)
+        for dst, src in ((self.E, E), (self.h, h), (self.tokens, tokens)):
+            if dst is not None and src is not None and src.data_ptr() != dst.data_ptr():
+                dst.copy_(src)
         self.graph.replay()
         _defer_status(self.status)
         return self.out
@@ -823,3 +855,4 @@ class ShardedForward:
     def close(self):
         self.graph = None
         self.out = self.status = None
+        self.bufs = {}

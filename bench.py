@@ -728,7 +728,9 @@ def leg_cfg4(args, dev, rank, world):
         # the sharded forward captured as one CUDA graph per rank (NCCL collectives inside)
         with torch.no_grad(), torch.autocast('cuda', dtype=torch.bfloat16):
             sf = shard.ShardedForward(layer, Ed, hd, xd)
-        step = lambda: sf(Ed, hd, xd)                      # noqa: E731
+        # the chunk's inputs live in the graph's input buffers (copied there at construction), as with the one-GPU
+        # graph replay: a step is the replay alone
+        step = lambda: sf()                                # noqa: E731
     warm = warm_up(step, args.warmup, world)
     if sf is not None:
         run, mode, graph = step, 'cuda_graph', None
