@@ -105,10 +105,11 @@ def expand_tails(ent_all, idx_all, shape):
     for x in shape[:-1]:
         R *= x
     flat = torch.zeros(world * R + 1, shape[-1], dtype=torch.int32, device=ent_all.device)
-    for q in range(world):
-        rows = ent_all[q].contiguous().view(torch.int32).view(-1, shape[-1])
-        dst = torch.where(idx_all[q] >= 0, q * R + idx_all[q], world * R)   # padding into the spare row
-        flat.index_copy_(0, dst, rows)
+    # every rank's entries in one copy (the same launches whatever the number of ranks)
+    rows = ent_all.contiguous().view(torch.int32).view(-1, shape[-1])
+    base = torch.arange(world, device=idx_all.device).unsqueeze(1) * R
+    dst = torch.where(idx_all >= 0, base + idx_all, world * R).reshape(-1)   # padding into the spare row
+    flat.index_copy_(0, dst, rows)
     return flat[:world * R].view((world,) + tuple(shape))
 
 
@@ -780,11 +781,13 @@ def _forward_packed(layer, E, h, tokens, group, caps, bufs=None):
         t[:B * L].view((B, L) + tuple(x.shape[2:]))[:, c0:c1] = x
         full[k] = t
     pay_all, gidx_all = _unpack(got, meta, 7), _unpack(got, meta, 8)
-    for q in range(rank):
-        _scatter_rows(full, pay_all[q], gidx_all[q], widths, L)
+    if rank > 0:                                   # the earlier ranks' rows in one scatter
+        _scatter_rows(full, pay_all[:rank].reshape(-1, pay_all.shape[-1]), gidx_all[:rank].reshape(-1), widths, L)
     ea = full['Ea'][:B * L].view(B, L, -1)
-    for q in range(1, min(rank + 2, world)):                             # chunk starts up to c1
-        ea[:, q * Lc] = firsts[q]
+    q_hi = min(rank + 2, world)                    # chunk starts 1 .. q_hi - 1 (up to c1), in one indexed write
+    if q_hi > 1:
+        starts = torch.arange(1, q_hi, device=ea.device) * Lc
+        ea[:, starts] = firsts[1:q_hi].transpose(0, 1).to(ea.dtype)
     tails_prev = None
     if rank > 0:
         ent = _unpack(got, meta, 5)[:rank].contiguous().view(torch.uint8).view(rank, cap_t, -1)
