@@ -118,6 +118,7 @@ _SIGS = {
                                   + [ctypes.c_float, ctypes.c_float, ctypes.c_int32] + [_P] * 11),
     'asrn_scan_forward': (ctypes.c_int, [ctypes.c_int64, ctypes.c_int64, _P, _P, _P, _P]),
     'asrn_scan_backward': (ctypes.c_int, [ctypes.c_int64, ctypes.c_int64, _P, _P, _P, _P, _P, _P]),
+    'asrn_argmax_rows': (ctypes.c_int, [ctypes.c_int64, ctypes.c_int64, _P, ctypes.c_int32, _P, _P]),
     'asrn_sampler_seed_state': (ctypes.c_int, [ctypes.c_uint64, _P]),
     'asrn_sampler_jump_poly': (ctypes.c_int, [ctypes.c_uint64, _P]),
     'asrn_sampler_fill': (ctypes.c_int, [ctypes.c_int64, ctypes.c_int64, ctypes.c_int32, _P, _P, _P, _P, _P]),

@@ -307,10 +307,95 @@ __global__ void __launch_bounds__(kArgThreads) k_sample_argmax(int64_t V, const 
   }
 }
 
+// Plain argmax of each row with torch.argmax's rule (the greedy token of a step): T = float or bf16, rows of V values;
+// bf16 rows with V % 8 == 0 are read 16 bytes at a time.
+template <typename T>
+__global__ void __launch_bounds__(kArgThreads) k_argmax_rows(int64_t V, const T* __restrict__ x,
+                                                             int64_t* __restrict__ out) {
+  const int64_t row = blockIdx.x;
+  const T* xr = x + row * V;
+  float bv = -INFINITY;
+  int64_t bi = V;
+  if constexpr (sizeof(T) == 2) {
+    if (V % 8 == 0) {
+      const uint4* v8 = reinterpret_cast<const uint4*>(xr);
+      for (int64_t c = threadIdx.x; c < V / 8; c += kArgThreads) {
+        const uint4 u = __ldg(v8 + c);
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const float f = __uint_as_float((k & 1) ? (w[k >> 1] & 0xFFFF0000u) : (w[k >> 1] << 16));
+          if (better(f, 8 * c + k, bv, bi)) {
+            bv = f;
+            bi = 8 * c + k;
+          }
+        }
+      }
+    } else {
+      for (int64_t j = threadIdx.x; j < V; j += kArgThreads) {
+        const float f = __bfloat162float(xr[j]);
+        if (better(f, j, bv, bi)) {
+          bv = f;
+          bi = j;
+        }
+      }
+    }
+  } else {
+    for (int64_t j = threadIdx.x; j < V; j += kArgThreads) {
+      const float f = __ldg(reinterpret_cast<const float*>(xr) + j);
+      if (better(f, j, bv, bi)) {
+        bv = f;
+        bi = j;
+      }
+    }
+  }
+  for (int o = 16; o; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int64_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (better(ov, oi, bv, bi)) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  __shared__ float sv[kArgThreads / 32];
+  __shared__ int64_t si[kArgThreads / 32];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  if (lane == 0) {
+    sv[w] = bv;
+    si[w] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int i = 1; i < kArgThreads / 32; ++i)
+      if (better(sv[i], si[i], bv, bi)) {
+        bv = sv[i];
+        bi = si[i];
+      }
+    out[row] = bi < V ? bi : 0;
+  }
+}
+
 }  // namespace mt
 }  // namespace asrn
 
 extern "C" {
+
+int asrn_argmax_rows(int64_t rows, int64_t V, const void* x, int32_t dtype, int64_t* out, void* stream) {
+  using namespace asrn::mt;
+  if (rows < 0 || V <= 0 || rows > 0x7fffffff || (dtype != 0 && dtype != 1)) return ASRN_ERR_ARG;
+  if (rows == 0) return ASRN_OK;
+  if (!x || !out) return ASRN_ERR_ARG;
+  if (dtype == 1 && (reinterpret_cast<uintptr_t>(x) & 15)) return ASRN_ERR_ARG;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (dtype == 1)
+    k_argmax_rows<__nv_bfloat16><<<static_cast<unsigned>(rows), kArgThreads, 0, s>>>(
+        V, reinterpret_cast<const __nv_bfloat16*>(x), out);
+  else
+    k_argmax_rows<float><<<static_cast<unsigned>(rows), kArgThreads, 0, s>>>(V, reinterpret_cast<const float*>(x),
+                                                                            out);
+  return cudaGetLastError() == cudaSuccess ? ASRN_OK : ASRN_ERR_CUDA;
+}
+
 
 int asrn_sampler_seed_state(uint64_t seed, uint32_t* state) {
   if (!state) return ASRN_ERR_ARG;

@@ -378,6 +378,18 @@ def _keep_quote_mass(q, p, quote):
     return torch.where(ok, q * scale, q)
 
 
+def argmax_rows(x):
+    """argmax over the last dimension of a (rows, V) CUDA tensor (fp32 or bf16) with torch.argmax's rule (NaN wins,
+    ties keep the lower index), one block per row on the device (asrn_argmax_rows): the greedy token of a step."""
+    if not x.is_cuda or x.dim() != 2 or x.dtype not in (torch.float32, torch.bfloat16):
+        raise ValueError('argmax_rows takes a 2-D float32 or bfloat16 CUDA tensor')
+    x = x.contiguous()
+    out = torch.empty(x.shape[0], dtype=torch.int64, device=x.device)
+    _lib.check(_lib.lib().asrn_argmax_rows(x.shape[0], x.shape[1], _lib.ptr(x), int(x.dtype == torch.bfloat16),
+                                           _lib.ptr(out), _lib.stream_ptr(x.device)), 'asrn_argmax_rows')
+    return out
+
+
 def _sample(lg, temperature, top_k, sampler, top_p=1.0, quote=None):
     """Temperature, top-k, top-p and the multinomial draw (asrn/nucleo.py:1945-1962); the draw is the device replay of
     the reference's seeded CPU generator (asrn_b200.sampling.DeviceSampler)."""

@@ -25,7 +25,7 @@ Printed (rank 0, one JSON line):
   clocks     nvidia-smi samples inside the timed region.
 Legs in the same line (each with its own value, device timing and the reference's CPU time beside it):
   generation configuration 5: the configuration-3 model, 64 sequences split over the GPUs, 65,536-token Zipf+repeat
-             prompts, greedy steps of the O(1) writer (CUDA-graph step + device argmax); flatness at 4,096 and 16,384;
+             prompts, greedy steps of the O(1) writer (CUDA-graph step + asrn_argmax_rows); flatness at 4,096 and 16,384;
              the public generate() end to end; the reference's _Escritor(o1=True) at batch 4 on the host cores.
   cfg4       one 262,144-token sequence, ASRNLayer(512), bf16: one GPU, or sequence-sharded over the GPUs of the run
              (NCCL exchanges of halo, clock offsets, bucket tails, features, n-gram summaries and streak maps).
@@ -1053,6 +1053,7 @@ def leg_generation(args, dev, rank, world):
     import torch
     import asrn_b200
     from asrn_b200 import synthetic
+    from asrn_b200.writer import argmax_rows
     B = max(1, GEN_B // world)
     torch.manual_seed(0)
     m = asrn_b200.create_model(V=V, d=D, n_capas=12, semilla=0).to(dev).eval()
@@ -1067,15 +1068,15 @@ def leg_generation(args, dev, rank, world):
             p0.record()
             lg = w.inicio(x0, capacidad=L0 + args.gen_steps + 8)
             p1.record()
-            nxt = lg.argmax(-1)
+            nxt = argmax_rows(lg)
             for _ in range(3):
-                nxt = w.paso(nxt, copiar=False).argmax(-1)
+                nxt = argmax_rows(w.paso(nxt, copiar=False))
             torch.cuda.synchronize()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             torch.cuda.nvtx.range_push('gen_steps')          # lets a profiler select the timed steps' kernels
             e0.record()
             for _ in range(args.gen_steps):
-                nxt = w.paso(nxt, copiar=False).argmax(-1)
+                nxt = argmax_rows(w.paso(nxt, copiar=False))
             e1.record()
             torch.cuda.nvtx.range_pop()
             torch.cuda.synchronize()

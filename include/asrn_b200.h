@@ -427,6 +427,9 @@ int asrn_sampler_fill(int64_t draws, int64_t steps, int32_t levels, const uint32
                       float* q, uint32_t* end_state, void* stream);
 int asrn_sample_argmax(int64_t rows, int64_t V, const float* prob, const float* q, int64_t* out, int* status,
                        void* stream);
+/* out[r] = argmax_j x[r, j] (device), torch.argmax's rule (NaN wins; equal values keep the lower index): the greedy
+ * token of a generation step. x (rows, V) fp32 (dtype 0) or bf16 (dtype 1, 16-byte aligned). */
+int asrn_argmax_rows(int64_t rows, int64_t V, const void* x, int32_t dtype, int64_t* out, void* stream);
 
 /* ---- test hooks (no counterpart in the reference; the layer forward never calls them) ------------------------------
  * asrn_test_force_cuda_core: 1 routes the bfloat16 work of later calls to the CUDA-core kernels (the fp32 path's), so

@@ -105,3 +105,20 @@ def test_generate_sampling_matches_reference(i, cuda):
     x0 = torch.from_numpy(z['tokens'][:, :meta['L0']]).to(cuda)
     seqs, _ = asrn_b200.generate(m, x0, n_nuevos=meta['n_new'], devolver_logits=False, **settings[i])
     assert np.array_equal(seqs.numpy(), ref[f'seqs_{i}'])
+
+
+@pytest.mark.parametrize('dtype', [torch.float32, torch.bfloat16])
+def test_argmax_rows_matches_torch(dtype, cuda):
+    """asrn_argmax_rows against torch.argmax: random rows, rows of equal maxima (bf16 ties), a row with NaNs, a row of
+    -inf, a length that is not a multiple of 8."""
+    from asrn_b200.writer import argmax_rows
+    g = torch.Generator().manual_seed(3)
+    for V in (50304, 1001):
+        x = torch.randn(64, V, generator=g)
+        x[1] = torch.round(x[1])                     # many equal maxima
+        x[2, [7, 900]] = float('nan')
+        x[3] = -float('inf')
+        x[4, :] = 0.0
+        x[5, 500:] = x[5].max() + 1                  # the maximum first reached at 500
+        xd = x.to(cuda, dtype)
+        assert torch.equal(argmax_rows(xd).cpu(), xd.argmax(-1).cpu())
