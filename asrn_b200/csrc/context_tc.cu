@@ -134,7 +134,10 @@ k_context_tc(const __grid_constant__ CUtensorMap tmap_wctx, const __grid_constan
     const float4* p_w0 = reinterpret_cast<const float4*>(s_par + 2 * d);
     const float4* p_w1 = reinterpret_cast<const float4*>(s_par + 3 * d);
     const float4* p_g = reinterpret_cast<const float4*>(s_par + 4 * d);
-    const int ar = tid >> 1, ah = tid & 1;
+    // the two threads of a tile row sit in the two half-warps (lanes l and l + 16): a quarter-warp's 16-byte reads of
+    // the staged rows then cover eight different rows (eight distinct swizzled chunks, no bank conflict), where
+    // adjacent lanes on the two boxes of one row would read the same banks 16 KB apart
+    const int ar = (tid & 15) + 16 * (tid >> 5), ah = (tid >> 4) & 1;
     int q = 0, j = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++j) {
@@ -178,14 +181,14 @@ k_context_tc(const __grid_constant__ CUtensorMap tmap_wctx, const __grid_constan
       }
       if (!ok) break;
       {
-        const float cnt_o = __shfl_xor_sync(0xffffffffu, cnt, 1);
-        const float mean_o = __shfl_xor_sync(0xffffffffu, mean, 1);
-        const float m2_o = __shfl_xor_sync(0xffffffffu, m2, 1);
+        const float cnt_o = __shfl_xor_sync(0xffffffffu, cnt, 16);
+        const float mean_o = __shfl_xor_sync(0xffffffffu, mean, 16);
+        const float m2_o = __shfl_xor_sync(0xffffffffu, m2, 16);
         const float n = cnt + cnt_o;
         const float dl = mean_o - mean;
         mean = mean + dl * (cnt_o / n);
         m2 = m2 + m2_o + dl * dl * (cnt * cnt_o / n);
-        gl += __shfl_xor_sync(0xffffffffu, gl, 1);
+        gl += __shfl_xor_sync(0xffffffffu, gl, 16);
       }
       const float rstd = 1.f / sqrtf(m2 / (float)d + 1e-5f);
       // ---- normalise, clock projection in fp32, bf16 operand for Qc / Kc ------------------------------------------
@@ -230,8 +233,8 @@ k_context_tc(const __grid_constant__ CUtensorMap tmap_wctx, const __grid_constan
       }
       if (!ok) break;
       // scalar outputs (the partner threads of a row combine their halves)
-      u0 += __shfl_xor_sync(0xffffffffu, u0, 1);
-      u1 += __shfl_xor_sync(0xffffffffu, u1, 1);
+      u0 += __shfl_xor_sync(0xffffffffu, u0, 16);
+      u1 += __shfl_xor_sync(0xffffffffu, u1, 16);
       if (ah == 0 && row_ok) {
         u0 += a.b_reloj[0];
         u1 += a.b_reloj[1];
