@@ -684,34 +684,41 @@ def _forward(layer, E, h, tokens, group, caps, bufs=None):
     return out, status, local_counts
 
 
-def _pack(parts):
-    """Tensors -> one uint8 buffer (each part padded to 8 bytes) and the (dtype, shape, offset) of each part."""
-    segs, meta, off = [], [], 0
+def _pack(parts, cache=None):
+    """Tensors -> one uint8 buffer (each part at an 8-byte aligned offset, the padding zero) and the (dtype, shape,
+    offset) of each part: one copy per part into the buffer, which `cache` (a dict) keeps for the next call."""
+    meta, off = [], 0
     for t in parts:
-        flat = torch.empty(t.numel(), dtype=t.dtype, device=t.device)     # stride 1 even for size-1 slices
-        b = flat.copy_(t.reshape(-1)).view(torch.uint8)
-        pad = (-b.numel()) % 8
-        if pad:
-            b = torch.cat([b, torch.zeros(pad, dtype=torch.uint8, device=b.device)])
-        segs.append(b)
         meta.append((t.dtype, tuple(t.shape), off))
-        off += b.numel()
-    return torch.cat(segs), meta
+        off += (t.numel() * t.element_size() + 7) // 8 * 8
+    dev = parts[0].device
+    buf = None if cache is None else cache.get('_pack')
+    if buf is None or buf.numel() != off or buf.device != dev:
+        buf = torch.zeros(off, dtype=torch.uint8, device=dev)
+        if cache is not None:
+            cache['_pack'] = buf
+    for t, (dt, shape, o) in zip(parts, meta):
+        buf[o:o + t.numel() * t.element_size()].view(dt).view(shape).copy_(t)
+    return buf, meta
 
 
 def _unpack(buf, meta, i):
-    """Part i of a packed buffer (world, bytes) -> (world,) + its shape, as views."""
+    """Part i of a packed buffer (world, bytes) -> (world,) + its shape, a strided view (no copy)."""
     dt, shape, off = meta[i]
     n = 1
     for x in shape:
         n *= x
     nb = n * torch.empty(0, dtype=dt).element_size()
-    return buf[:, off:off + nb].contiguous().view(dt).view((buf.shape[0],) + shape)
+    return buf[:, off:off + nb].view(dt).view((buf.shape[0],) + shape)
 
 
-def _all_gather_bytes(buf, world, group):
+def _all_gather_bytes(buf, world, group, cache=None):
     import torch.distributed as dist
-    out = torch.empty(world, buf.numel(), dtype=torch.uint8, device=buf.device)
+    out = None if cache is None else cache.get('_gathered')
+    if out is None or tuple(out.shape) != (world, buf.numel()):
+        out = torch.empty(world, buf.numel(), dtype=torch.uint8, device=buf.device)
+        if cache is not None:
+            cache['_gathered'] = out
     dist.all_gather_into_tensor(out.view(-1), buf, group=group)
     return out
 
@@ -760,8 +767,8 @@ def _forward_packed(layer, E, h, tokens, group, caps, bufs=None):
     over = (local_counts[0] > cap_t) | (local_counts[1] > cap_r)
     # (beta is not sent: the sequence-wide steps read sig, the clock and log_alfa only)
     buf, meta = _pack([loc['Bt'][:, -1], loc['Bt'], loc['sig'], loc['log_alfa'], loc['Ea'][:, 0],
-                       t_rows, t_idx, payload, gidx])
-    got = _all_gather_bytes(buf, world, group)
+                       t_rows, t_idx, payload, gidx], bufs)
+    got = _all_gather_bytes(buf, world, group, bufs)
     sums = _unpack(got, meta, 0)                                          # (world, B)
     full = {}
     for i, k in ((1, 'Bt'), (2, 'sig'), (3, 'log_alfa')):
