@@ -384,3 +384,15 @@ def test_bounded_wait_gives_up_and_the_context_stays_usable(cuda):
     with torch.no_grad():
         y = layer(_t(z['E'], cuda), _t(z['h'], cuda), _t(z['tokens'], cuda)).cpu().numpy()
     assert rel_err(y, z['out']) <= TOL_F32
+
+
+@pytest.mark.parametrize('B,L', [(1, 262144), (3, 40961), (2, 4096), (5, 1), (1, 4097)])
+def test_clock_scan_long_and_ragged_rows(B, L, cuda):
+    """asrn_clock (B_t = cumsum(beta) in fp64; one block per 4096-slot chunk, which sums the chunks before it itself)
+    against numpy's fp64 cumsum: within 1e-12 of the row's largest value (the sums run in another order)."""
+    from asrn_b200 import stages
+    rng = np.random.default_rng(B * 7 + L)
+    beta = rng.gamma(1.5, 0.7, size=(B, L))
+    got = stages.clock(torch.from_numpy(beta).to(cuda)).cpu().numpy()
+    ref = np.cumsum(beta, axis=1)
+    assert np.abs(got - ref).max() <= 1e-12 * np.abs(ref).max()
