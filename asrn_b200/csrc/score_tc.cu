@@ -739,10 +739,11 @@ int launch_score_tc(const ScoreArgs& a, cudaStream_t s) {
       !make_tmap_rows_bf16(&tm_kc, a.Kc, (uint64_t)a.cf, rows, (uint64_t)a.cf * 2, 32, 64))
     return ASRN_ERR_CUDA;
   cudaFuncSetAttribute(k_score_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  // each block pays a prologue (the first window half and two sub-tiles of latency): spans of 1024 or 2048 slots
-  // while the grid keeps at least 8 blocks per SM
+  // each block pays a prologue of about 10 us (the first window half and two sub-tiles of latency): spans of 1024 or
+  // 2048 slots while the grid keeps at least 4 blocks per SM (32 x 8192 tokens: 2048 slots, 6.9 waves of one block
+  // per SM, 3.11 instead of 3.16 ms with the 8-per-SM rule's 1024)
   int span = kSpanTc;
-  while (span < 2048 && ((a.L + 2 * span - 1) / (2 * span)) * nds * a.B * a.T >= 8 * 148) span *= 2;
+  while (span < 2048 && ((a.L + 2 * span - 1) / (2 * span)) * nds * a.B * a.T >= 4 * 148) span *= 2;
   dim3 grid((unsigned)(((a.L + span - 1) / span) * nds), (unsigned)(a.B * a.T));
   k_score_tc<<<grid, kThreadsTc, smem, s>>>(tm_phi, tm_qc, tm_kc, a, nds, dpart, span);
   return cudaGetLastError() == cudaSuccess ? ASRN_OK : ASRN_ERR_CUDA;
