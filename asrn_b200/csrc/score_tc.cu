@@ -10,12 +10,13 @@
 // other rows keep finite contents (zeros) and meet zero weights.
 //
 // One block of 20 warps per (row, span of 512-2048 slots), three warp groups working on consecutive sub-tiles at once:
-// in iteration i group A (warps 0-7) scores sub-tile i + 1 (S products issued to the tensor cores by one thread, the
-// element epilogue by the four warps whose TMEM lanes hold the window's keys) and takes its softmax, while group B
-// (warps 8-15) has the value products of sub-tile i computed by the tensor cores (lane 0 of warp m issues M-tile m)
-// and reduces them into acc, and the load group (warps 16-19) issues the copies: the sorted entries of sub-tile i + 3 and the per-position
-// scalars of i + 2 by cp.async, the phi / Qc / Kc rows of i + 2 by tensor-map row gathers (four rows per instruction)
-// into a 4-sub-tile feature ring, the used value rows of i + 1 by 16-byte cp.async into a 3-sub-tile value ring kept
+// in iteration i group A (warps 0-7) scores sub-tile i + 1 (its S products were issued to the tensor cores an
+// iteration earlier; the element epilogue by the four warps whose TMEM lanes hold the window's keys) and takes its
+// softmax, while the load group's first thread issues the S products of i + 2; group B (warps 8-15) has the value products
+// of sub-tile i computed by the tensor cores (lane 0 of warp m issues M-tile m) and reduces them into acc, and the
+// load group (warps 16-19) issues the copies: the sorted entries of sub-tile i + 4 and the per-position scalars of
+// i + 3 by cp.async, the phi / Qc / Kc rows of i + 3 by tensor-map row gathers (four rows per instruction) into a
+// 4-sub-tile feature ring, the used value rows of i + 1 by 16-byte cp.async into a 3-sub-tile value ring kept
 // in the MMA's MN-major 128-byte-swizzled layout (one 12 KB region per 64 columns of d). The weights pass from A to B
 // through a double buffer in the MMA's K-major swizzled layout; one block barrier per iteration.
 // The value epilogue stages each warp's 32 rows of d x 16 queries in shared memory and reads them back transposed, so
@@ -33,7 +34,7 @@ namespace asrn {
 
 namespace {
 constexpr int kQ = 32;           // queries per sub-tile
-constexpr int kRF = 128;         // feature ring: 4 sub-tiles (score windows of i and i + 1, prefetch of i + 2)
+constexpr int kRF = 128;         // feature ring: 4 sub-tiles (iteration i: i, i + 1 scored, i + 2 in the MMAs, i + 3 loaded)
 constexpr int kRV = 96;          // value ring: 3 sub-tiles (window of i, prefetch of i + 1)
 constexpr int kSpanTc = 512;     // sorted slots per block: the shortest span (longer ones when the grid stays large)
 constexpr int kGroupWarps = 8;   // warps 0-7: scores (group A); 8-15: value products (group B)
@@ -295,11 +296,21 @@ __device__ __forceinline__ void tc_stage2_values(const ScoreArgs& a, const TcSme
   // the value of position p is row p + 1 of Ea
   const __nv_bfloat16* ea = reinterpret_cast<const __nv_bfloat16*>(a.Ea) + (k.b * a.Lf + 1) * (int64_t)a.d + k.dp0 +
                             lane * 8;
-  for (int i = wb; i < kQ; i += kLoadWarps) {
-    const int li = (t + 1) * kQ + i;
-    const int fr = frow(li), vr = vrow(li);
-    if (!S.used[fr]) continue;
-    const __nv_bfloat16* src = ea + (int64_t)S.pos[fr] * a.d;
+  // the warp's 8 rows' flags and positions first: read inside the copy loop, each row's shared-memory loads wait
+  // behind the previous row's copies (1.7 of a 4 us iteration)
+  constexpr int kRows = kQ / kLoadWarps;
+  int used[kRows], pos[kRows];
+#pragma unroll
+  for (int u = 0; u < kRows; ++u) {
+    const int fr = frow((t + 1) * kQ + wb + kLoadWarps * u);
+    used[u] = S.used[fr];
+    pos[u] = S.pos[fr];
+  }
+#pragma unroll
+  for (int u = 0; u < kRows; ++u) {
+    if (!used[u]) continue;
+    const int vr = vrow((t + 1) * kQ + wb + kLoadWarps * u);
+    const __nv_bfloat16* src = ea + (int64_t)pos[u] * a.d;
     const uint32_t x = (uint32_t)(vr & 7);
     const uint32_t dst = v_lane + (uint32_t)(vr >> 3) * 1024 + (x << 7) + (x_lane ^ (x << 4));
     if (c0) cp_async16_s(dst, src);
@@ -399,8 +410,7 @@ __device__ __forceinline__ void tc_issue_scores(const TcSmem& S, const TcBlock& 
 }
 
 template <bool kSuf4>
-__device__ __forceinline__ void tc_scores(const ScoreArgs& a, const TcSmem& S, const TcBlock& k, int t, uint32_t tmem,
-                                          bool issue_next) {
+__device__ __forceinline__ void tc_scores(const ScoreArgs& a, const TcSmem& S, const TcBlock& k, int t, uint32_t tmem) {
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const int C = a.C;
   const int64_t q0 = k.S0 + (int64_t)t * kQ;
@@ -500,11 +510,6 @@ __device__ __forceinline__ void tc_scores(const ScoreArgs& a, const TcSmem& S, c
     }
   }
   tc_softmax(a, S, k, t);
-  // the next sub-tile's score MMAs, one iteration ahead of their epilogue (its feature rows were copied meanwhile)
-  if (issue_next && wid == 0 && lane == 0) {
-    umma::mbar_wait(S.fbar + ((t + 2) & 3), (uint32_t)(((t + 2) >> 2) & 1), a.status);
-    tc_issue_scores(S, k, t + 1, tmem);
-  }
 }
 
 // Group B: out^T = V^T . att^T for sub-tile t on tcgen05, reduced into the bf16 accumulator. Lane 0 of warp mm issues
@@ -646,8 +651,9 @@ k_score_tc(const __grid_constant__ CUtensorMap tm_phi, const __grid_constant__ C
   };
   auto bar_load = []() { asm volatile("bar.sync 2, %0;" ::"n"(kLoadThreads) : "memory"); };
 
-  // prologue: the load group copies sub-tiles -1 (the first window half), 0 and 1 of the features, sub-tile 2's
-  // sorted entries and the value rows of -1 and 0; then group A scores sub-tile 0
+  // prologue: the load group copies sub-tiles -1 (the first window half), 0, 1 and 2 of the features, sub-tile 3's
+  // sorted entries and the value rows of -1 and 0; then group A issues the score MMAs of sub-tiles 0 and 1 and scores
+  // sub-tile 0
   umma::tc_fence_before();
   __syncthreads();
   umma::tc_fence_after();
@@ -668,7 +674,15 @@ k_score_tc(const __grid_constant__ CUtensorMap tm_phi, const __grid_constant__ C
     cp_async_commit();
     cp_async_wait_all();
     bar_load();
-    if (ntile > 2) tc_stage1(a, S, k, 2, pt);   // its buffer was read by sub-tile -1's feature stage above
+    if (ntile > 2) {
+      tc_stage1(a, S, k, 2, pt);                // its buffer was read by sub-tile -1's feature stage above
+      cp_async_commit();
+      cp_async_wait_all();
+      expect_features(2);
+      bar_load();
+      tc_stage2_features(a, S, k, 2, pt, &tm_phi, &tm_qc, &tm_kc);
+      if (ntile > 3) tc_stage1(a, S, k, 3, pt);  // its buffer was read by sub-tile 0's feature stage
+    }
     tc_stage2_values(a, S, k, -1, pt);
     tc_stage2_values(a, S, k, 0, pt);
     cp_async_commit();
@@ -681,29 +695,43 @@ k_score_tc(const __grid_constant__ CUtensorMap tm_phi, const __grid_constant__ C
       wait_features(-1);
       wait_features(0);
       tc_issue_scores(S, k, 0, tmem);
+      if (ntile > 1) {
+        wait_features(1);
+        tc_issue_scores(S, k, 1, tmem);
+      }
     }
-    if (suf4) tc_scores<true>(a, S, k, 0, tmem, ntile > 1);
-    else tc_scores<false>(a, S, k, 0, tmem, ntile > 1);
+    if (suf4) tc_scores<true>(a, S, k, 0, tmem);
+    else tc_scores<false>(a, S, k, 0, tmem);
   }
   __syncthreads();
 
   // iteration i: group A scores sub-tile i + 1, group B takes the value products of i; meanwhile the load group copies
-  // the value rows of i + 1, the features of i + 2 and the sorted entries of i + 3
+  // the value rows of i + 1, the features of i + 3 (into the ring stage of i - 1, which no score MMA or epilogue reads
+  // from here on) and the sorted entries of i + 4, and its first thread issues the score MMAs of i + 2 while its copies
+  // are in flight: their features arrived during the previous iteration, their TMEM buffer (sub-tile i's) was read by
+  // group A in the previous iteration. (Issued by group A at the end of its epilogue, the six MMAs held its iteration
+  // about 450 ns; issued at its start, where group B's value MMAs queue, about 1 us.)
   for (int i = 0; i < ntile; ++i) {
     if (loader) {
-      if (i + 2 < ntile) expect_features(i + 2);
-      if (i + 3 < ntile) tc_stage1(a, S, k, i + 3, pt);
-      if (i + 2 < ntile) {
+      if (i + 3 < ntile) expect_features(i + 3);
+      if (i + 4 < ntile) tc_stage1(a, S, k, i + 4, pt);
+      if (i + 3 < ntile) {
         bar_load();                             // the expect_tx precedes every copy of the stage
-        tc_stage2_features(a, S, k, i + 2, pt, &tm_phi, &tm_qc, &tm_kc);
+        tc_stage2_features(a, S, k, i + 3, pt, &tm_phi, &tm_qc, &tm_kc);
       }
       if (i + 1 < ntile) tc_stage2_values(a, S, k, i + 1, pt);
       cp_async_commit();
+      // the score MMAs of sub-tile i + 2 while the copies are in flight
+      if (i + 2 < ntile && pt == 0) {
+        wait_features(i + 2);
+        tc_issue_scores(S, k, i + 2, tmem);
+      }
+      __syncwarp();                             // the issuing warp converges before its next named barrier
       wait_copies();
     } else if (group_a) {
       if (i + 1 < ntile) {
-        if (suf4) tc_scores<true>(a, S, k, i + 1, tmem, i + 2 < ntile);
-        else tc_scores<false>(a, S, k, i + 1, tmem, i + 2 < ntile);
+        if (suf4) tc_scores<true>(a, S, k, i + 1, tmem);
+        else tc_scores<false>(a, S, k, i + 1, tmem);
       }
     } else {
       tc_values(a, S, k, i, wid - kGroupWarps, tmem);
