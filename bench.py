@@ -662,7 +662,7 @@ def run_ours(args):
                 out['cpu_baseline'] = cpu_info
         del layer
         torch.cuda.empty_cache()
-    if not args.no_legs and args.workload in ('cfg3', 'cfg4'):
+    if args.workload == 'cfg4' or (args.workload == 'cfg3' and not args.no_legs):   # --no-legs keeps the line's own
         legs['cfg4'] = leg_cfg4(args, dev, rank, world)
     if args.workload == 'gen':
         legs['generation'] = leg_generation(args, dev, rank, world)
