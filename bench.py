@@ -613,9 +613,12 @@ def run_ours(args):
                                         ctx['log_alfa'], hs['Ea'], half=True)
             for _ in range(2):
                 call()
-            score_ms, _ = timed(call, args.steps)
+            # replayed as a CUDA graph like the forward: an eager loop's host work (allocations, argument
+            # preparation) can fall behind the 1.8 ms launches when the host cores are busy and leave gaps on the device
+            srun, _, sgraph = graph_or_eager(call, args.eager)
+            score_ms, _ = timed(srun, args.steps)
             score_ms /= args.steps
-            del ctx, Bt, hs, orden, ids_o
+            del srun, sgraph, ctx, Bt, hs, orden, ids_o
 
         del run, graph
         torch.cuda.empty_cache()
@@ -653,6 +656,8 @@ def run_ours(args):
                                 'algorithmic_bytes_per_token': SCORE_BYTES_PER_TOKEN,
                                 'traffic': None if traffic_pt is None else traffic_pt * tokens,
                                 'kernel_ms': score_ms,
+                                'kernel_timing': 'CUDA-graph replays of the scoring call on its stream: the kernel and '
+                                                 'the zero fill of its bf16 accumulator',
                                 'layer_frac': LAYER_BYTES_PER_TOKEN * tokens / (ms / args.steps * 1e-3) / 1e9 / hbm},
                    'gpu_launches': (ours_k * args.steps) if ours_k else None,
                    'graph_kernels_per_step': {'all': kern, 'ours': ours_k, 'by_name': names},
