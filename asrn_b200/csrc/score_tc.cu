@@ -191,6 +191,7 @@ __device__ __forceinline__ void round2_bf16(float& a, float& b) {
   b = __uint_as_float(u & 0xFFFF0000u);
 }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_but_last() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 __device__ __forceinline__ void bar_group_a() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
 
@@ -706,28 +707,33 @@ k_score_tc(const __grid_constant__ CUtensorMap tm_phi, const __grid_constant__ C
   __syncthreads();
 
   // iteration i: group A scores sub-tile i + 1, group B takes the value products of i; meanwhile the load group copies
-  // the value rows of i + 1, the features of i + 3 (into the ring stage of i - 1, which no score MMA or epilogue reads
-  // from here on) and the sorted entries of i + 4, and its first thread issues the score MMAs of i + 2 while its copies
-  // are in flight: their features arrived during the previous iteration, their TMEM buffer (sub-tile i's) was read by
+  // the value rows of i + 1 and the sorted entries of i + 4 (waited for at the end of the iteration), then the features
+  // of i + 3 (into the ring stage of i - 1, which no score MMA or epilogue reads from here on; the scalar copies are
+  // waited for in the next iteration, the rows by the stage's mbarrier), and its first thread issues the score MMAs of
+  // i + 2 while its copies are in flight: their features arrived during the previous iteration, their TMEM buffer (sub-tile i's) was read by
   // group A in the previous iteration. (Issued by group A at the end of its epilogue, the six MMAs held its iteration
   // about 450 ns; issued at its start, where group B's value MMAs queue, about 1 us.)
   for (int i = 0; i < ntile; ++i) {
     if (loader) {
       if (i + 3 < ntile) expect_features(i + 3);
       if (i + 4 < ntile) tc_stage1(a, S, k, i + 4, pt);
+      if (i + 1 < ntile) tc_stage2_values(a, S, k, i + 1, pt);
+      cp_async_commit();                        // group 1: the value rows and sorted entries, used next iteration
       if (i + 3 < ntile) {
         bar_load();                             // the expect_tx precedes every copy of the stage
         tc_stage2_features(a, S, k, i + 3, pt, &tm_phi, &tm_qc, &tm_kc);
       }
-      if (i + 1 < ntile) tc_stage2_values(a, S, k, i + 1, pt);
-      cp_async_commit();
+      cp_async_commit();                        // group 2: the scalars of i + 3, first read in iteration i + 2
       // the score MMAs of sub-tile i + 2 while the copies are in flight
       if (i + 2 < ntile && pt == 0) {
         wait_features(i + 2);
         tc_issue_scores(S, k, i + 2, tmem);
       }
       __syncwarp();                             // the issuing warp converges before its next named barrier
-      wait_copies();
+      // group 1 and everything older (the previous iteration's group 2) complete; this iteration's scalars may land
+      // during the next one. Value rows: then made visible to the tensor cores.
+      cp_async_wait_but_last();
+      umma::fence_proxy_async();
     } else if (group_a) {
       if (i + 1 < ntile) {
         if (suf4) tc_scores<true>(a, S, k, i + 1, tmem);
